@@ -1,0 +1,339 @@
+#!/usr/bin/env python
+"""Routed tokens/s of one SPALMER micro-expert MoE layer forward on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config m100] [--impl ours|reference]
+
+One step = one full layer forward (router GEMM, exact top-k, dispatch, grouped
+expert SwiGLU, shared SwiGLU + combine, statistics, auxiliary loss) over the
+configuration's tokens.  Multi-GPU runs are data parallel (every rank owns its
+own tokens and a replica of the weights; no collective in the forward), so
+``value`` is weak-scaled: total tokens of all ranks / slowest rank's time.
+
+``value`` is timed on the device with CUDA events around each step, inputs
+resident in HBM, L2 flushed (256 MiB write) before every step.  ``e2e`` is the
+same metric through the public module API with host buffers: pinned H2D of the
+step's hidden states, the forward, and D2H of the update and auxiliary loss,
+all inside the timed region.  ``--impl reference`` times the CPU restatement
+of the reference path (``oracle/``, numpy + the standard-library top-k) on the
+host cores, on a bounded token sample per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    # 100M-preset shape (MXFP8 promotion lane pending: all experts BF16).
+    "m100": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
+                          active_experts=8), batch=64, seq=1024, cpu_sample=1024),
+    # 10M-preset shape.
+    "m10": dict(cfg=dict(d_model=256, num_experts=200, expert_inter_dim=64, shared_inter_dim=256,
+                         active_experts=8), batch=32, seq=512, cpu_sample=4096),
+    # CPU-runnable smoke layer.
+    "smoke": dict(cfg=dict(d_model=128, num_experts=200, expert_inter_dim=32, shared_inter_dim=128,
+                           active_experts=4), batch=2, seq=256, cpu_sample=512),
+}
+METRIC = "routed tokens/sec per MoE layer"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": data["hbm_gbs"], "bf16_tflops": data["bf16_tflops"],
+                "bf16_tflops_sustained": data.get("bf16_tflops_sustained"), "source": "measured"}
+    return dict(FALLBACK_PEAKS)
+
+
+def layer_flops(cfg: dict, tokens: int) -> dict:
+    d, E, I, k = cfg["d_model"], cfg["num_experts"], cfg["expert_inter_dim"], cfg["active_experts"]
+    S = cfg["shared_inter_dim"]
+    P = tokens * k
+    return {
+        "router_gemm": 2.0 * tokens * d * E,
+        "expert_gemm1_swiglu": 2.0 * P * d * 2 * I,
+        "expert_gemm2_scatter": 2.0 * P * I * d,
+        "shared_gemm1_swiglu": 2.0 * tokens * d * 2 * S,
+        "shared_gemm2_combine": 2.0 * tokens * S * d,
+    }
+
+
+def workload_config(name: str, world: int) -> dict:
+    spec = CONFIGS[name]
+    cfg = spec["cfg"]
+    return {
+        "workload": f"{name}: SPALMER micro-expert layer forward",
+        "tokens_per_gpu": spec["batch"] * spec["seq"],
+        "batch": spec["batch"], "seq_len": spec["seq"],
+        "d_model": cfg["d_model"], "num_experts": cfg["num_experts"],
+        "expert_inter_dim": cfg["expert_inter_dim"], "top_k": cfg["active_experts"],
+        "shared_inter_dim": cfg["shared_inter_dim"],
+        "expert_precision": "bf16 for all experts (MXFP8 promotion lane not implemented yet)",
+        "weights": "random init, torch.manual_seed(0), N(0,0.02)",
+        "l2": "flushed by a 256 MiB write before every timed step",
+        "parallelism": f"dp{world}",
+    }
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(device_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i] and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def init_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def run_reference_arm(args) -> None:
+    world, rank, _ = init_dist()
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle import mixer_ref as R
+    from spalmer_b200 import B200MicroExpertChannelMixer, MicroExpertsConfig
+    from tests.helpers import bf16_bits, oracle_params
+
+    spec = CONFIGS[args.config]
+    config = MicroExpertsConfig(**spec["cfg"])
+    torch.manual_seed(0)
+    mixer = B200MicroExpertChannelMixer(config).to(torch.bfloat16)
+    params = oracle_params(mixer)
+    sample = spec["cpu_sample"]
+    x = torch.randn(sample, config.d_model, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    x_bits = bf16_bits(x)
+    k = config.active_experts
+    for _ in range(args.warmup):
+        R.mixer_forward(params, x_bits, k)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        R.mixer_forward(params, x_bits, k)
+        times.append(time.perf_counter() - t0)
+    mean_s = sum(times) / len(times)
+    value = sample / mean_s
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean_s * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": workload_config(args.config, world),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{sample} tokens of the {args.config} workload per step"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(args, mixer, x_cpu) -> dict:
+    from oracle import mixer_ref as R
+    from tests.helpers import bf16_bits, oracle_params
+
+    spec = CONFIGS[args.config]
+    sample = spec["cpu_sample"]
+    params = oracle_params(mixer)
+    x_bits = bf16_bits(x_cpu.reshape(-1, x_cpu.shape[-1])[:sample])
+    k = mixer.config.active_experts
+    R.mixer_forward(params, x_bits, k)
+    times = []
+    t_end = time.perf_counter() + 15.0
+    while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 10):
+        t0 = time.perf_counter()
+        R.mixer_forward(params, x_bits, k)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": sample / med, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{sample} tokens of the {args.config} workload, median of {len(times)} runs "
+                      f"(numpy/OpenBLAS on all host threads)"}
+
+
+def run_ours(args) -> None:
+    world, rank, local = init_dist()
+    import torch.distributed as dist
+
+    from spalmer_b200 import B200MicroExpertChannelMixer, MicroExpertsConfig
+    from spalmer_b200 import _lib
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    spec = CONFIGS[args.config]
+    config = MicroExpertsConfig(**spec["cfg"])
+    batch, seq = spec["batch"], spec["seq"]
+    tokens = batch * seq
+    torch.manual_seed(0)
+    mixer = B200MicroExpertChannelMixer(config).to(torch.bfloat16).eval().to(device)
+    x_cpu = torch.randn(batch, seq, config.d_model, generator=torch.Generator().manual_seed(1 + rank))
+    x_cpu = x_cpu.to(torch.bfloat16)
+    x_host = x_cpu.pin_memory()
+    x = x_host.to(device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    K, W = args.steps, args.warmup
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    with torch.inference_mode():
+        for _ in range(W):
+            mixer(x)
+        torch.cuda.synchronize()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+        stage_sets = [[torch.cuda.Event(enable_timing=True) for _ in range(_lib.STAGE_EVENTS)] for _ in range(K)]
+        barrier()
+        torch.cuda.synchronize()
+        sampler = ClockSampler(local)
+        time.sleep(0.3)
+        for i in range(K):
+            flush.zero_()
+            mixer.record_stage_events(stage_sets[i])
+            starts[i].record()
+            out = mixer(x)
+            ends[i].record()
+        torch.cuda.synchronize()
+        barrier()
+        clocks = sampler.stop()
+        mixer.record_stage_events(None)
+        status = mixer.device_status()
+        step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+        total_ms = sum(step_ms)
+        stages = {}
+        for j, name in enumerate(_lib.STAGE_NAMES):
+            stages[name] = sum(st[j].elapsed_time(st[j + 1]) for st in stage_sets) / K
+
+        # e2e through the module API with host buffers
+        out_host = torch.empty(batch, seq, config.d_model, dtype=torch.bfloat16).pin_memory()
+        aux_host = torch.empty((), dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step():
+            xd = x_host.to(device, non_blocking=True)
+            o = mixer(xd)
+            out_host.copy_(o.update, non_blocking=True)
+            aux_host.copy_(o.auxiliary_loss, non_blocking=True)
+
+        for _ in range(W):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(K):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = e0.elapsed_time(e1)
+
+    # max over ranks
+    t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms = float(t[0]), float(t[1])
+    ms_per_step = total_ms / K
+    value = world * tokens / (ms_per_step / 1e3)
+    e2e_value = world * tokens / (e2e_ms / K / 1e3)
+
+    if rank == 0:
+        pk = peaks()
+        flops = layer_flops(spec["cfg"], tokens)
+        dom = "expert_gemm1_swiglu"
+        dom_ms = stages[dom]
+        achieved = flops[dom] / (dom_ms / 1e3) / 1e12
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,1) hidden states, seeded random-init weights)",
+            "config": workload_config(args.config, world),
+            "e2e": {"value": e2e_value, "unit": "tokens/s",
+                    "h2d_bytes_per_step": tokens * config.d_model * 2,
+                    "d2h_bytes_per_step": tokens * config.d_model * 2 + 2},
+            "gpu_launches": K * 10,
+            "roofline": {"bound": "tensor", "kernel": "gemm_kernel<kEpiSwiglu> (expert GEMM1, gathered rows)",
+                         "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": achieved / pk["bf16_tflops"], "traffic": None,
+                         "peak_source": f"{pk['source']} bf16 burst"},
+            "layer_tensor_tflops": sum(flops.values()) / (ms_per_step / 1e3) / 1e12,
+            "stages_ms": stages,
+            "device_status": status,
+        }
+        if clocks is not None:
+            line["clocks"] = clocks
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args, mixer, x_cpu)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="m100", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

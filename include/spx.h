@@ -1,0 +1,153 @@
+/*
+ * libspx — B200 (sm_100a) kernels for SPALMER's routed micro-expert channel
+ * mixer, behind a plain C ABI.
+ *
+ * All pointers are device pointers unless stated otherwise; BF16 tensors are
+ * passed as uint16_t bit patterns; every tensor is contiguous row-major and
+ * 16-byte aligned.  `stream` is a cudaStream_t (NULL = legacy default
+ * stream).  Every entry point returns SPX_OK (0) or a negative status; no C++
+ * exception crosses this boundary.  The caller owns all memory: weights,
+ * outputs and the workspace (size from spx_layer_sizes, zero-filled once
+ * before first use).  Calls on distinct streams with distinct workspaces are
+ * independent.
+ *
+ * Reference interfaces replaced (mESmaC/spalmer, paths under src/spalmer/):
+ *   spx_layer_forward  MicroExpertChannelMixer.forward   experts/mixer.py:145-241
+ *   spx_route          SurpriseRouter.forward (score transform, router.py:52-56)
+ *                      + select_least_surprised_experts  experts/router.py:59-95
+ *   spx_dispatch       _pair_counts / cumsum / argsort(stable=True)
+ *                                                        experts/bank.py:721-723
+ *   spx_pack_weights   derived cache of the state_dict layout
+ *                                                        experts/bank.py:52-54, nn/ffn.py:16-18
+ *   spx_softplus_table F.softplus on every BF16 input    experts/router.py:56
+ */
+#ifndef SPX_H_
+#define SPX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SPX_ABI_VERSION 1
+
+#define SPX_OK 0
+#define SPX_ERR_INVALID_ARG -1
+#define SPX_ERR_UNSUPPORTED -2
+#define SPX_ERR_CUDA -3
+#define SPX_ERR_DRIVER -4
+#define SPX_ERR_TIMEOUT -5
+#define SPX_ERR_ALIGNMENT -6
+#define SPX_ERR_WORKSPACE -7
+#define SPX_ERR_DEVICE -8
+
+/* Shape of one mixer layer (MicroExpertsConfig resolved values, experts/config.py:86-110,231-244). */
+typedef struct spx_layer_dims {
+  int64_t tokens;          /* T = batch * seq_len                               */
+  int32_t d_model;         /* d                                                  */
+  int32_t num_experts;     /* E (<= 1024)                                        */
+  int32_t inter_dim;       /* I, resolved_inter_dim                              */
+  int32_t shared_dim;      /* S, resolved_shared_inter_dim; 0 = no shared path   */
+  int32_t top_k;           /* k, active experts per token (1..20, <= E)          */
+  int32_t score_transform; /* 0 = softplus, 1 = identity (router_score_transform) */
+  int32_t execution_loop;  /* 1 = telemetry of expert_execution="loop"          */
+} spx_layer_dims;
+
+/* The reference state_dict tensors (BF16), unchanged layouts. */
+typedef struct spx_reference_weights {
+  const uint16_t* router_weight; /* router.proj.weight            [E, d]    */
+  const uint16_t* router_bias;   /* router.proj.bias              [E] | NULL */
+  const uint16_t* gate_proj;     /* experts.gate_proj             [E, d, I] */
+  const uint16_t* up_proj;       /* experts.up_proj               [E, d, I] */
+  const uint16_t* down_proj;     /* experts.down_proj             [E, I, d] */
+  const uint16_t* shared_gate;   /* shared.gate_projection.weight [S, d] | NULL */
+  const uint16_t* shared_up;     /* shared.up_projection.weight   [S, d] | NULL */
+  const uint16_t* shared_down;   /* shared.down_projection.weight [d, S] | NULL */
+} spx_reference_weights;
+
+/* Element counts (uint16_t) of the packed weight buffers. */
+typedef struct spx_packed_sizes {
+  size_t router_weight;
+  size_t expert_w1;
+  size_t expert_w2;
+  size_t shared_w1;
+  size_t shared_w2;
+} spx_packed_sizes;
+
+typedef struct spx_packed_weights {
+  const uint16_t* router_weight;  /* from spx_pack_weights                     */
+  const uint16_t* router_bias;    /* [E] | NULL                                */
+  const uint16_t* expert_w1;
+  const uint16_t* expert_w2;
+  const uint16_t* shared_w1;      /* NULL when shared_dim == 0                 */
+  const uint16_t* shared_w2;
+  const uint16_t* softplus_table; /* [65536]; required for score_transform 0   */
+  const uint8_t* resident_mask;   /* [E] (0/1) | NULL = full pool              */
+} spx_packed_weights;
+
+typedef struct spx_layer_outputs {
+  uint16_t* update;                /* [T, d]  routed + shared update (required) */
+  uint16_t* router_scores;         /* [T, E]  (required)                        */
+  int64_t* expert_ids;             /* [T, k]  (required)                        */
+  uint16_t* routing_weights;       /* [T, k]  (required)                        */
+  float* expert_utilization;       /* [E]     | NULL                            */
+  int64_t* group_stats;            /* [6] count, max_load, real, padded,
+                                      counterfactual padded, num_active | NULL  */
+  float* group_ratios;             /* [2] padding amplification,
+                                      counterfactual amplification | NULL       */
+  uint16_t* auxiliary_loss;        /* [1] BF16 load-balance loss | NULL         */
+  int32_t* dispatch_order;         /* [T*k] argsort(stable) | NULL              */
+  int32_t* expert_counts;          /* [E] | NULL                                */
+  const uint16_t* injected_logits; /* [T, E] use instead of the router GEMM | NULL */
+  uint16_t* router_logits;         /* [T, E] receives router GEMM output | NULL */
+  void* const* stage_events;       /* NULL, or SPX_STAGE_EVENTS cudaEvent_t handles recorded
+                                      on `stream` at the stage boundaries below            */
+} spx_layer_outputs;
+
+/* Stage boundaries recorded into spx_layer_outputs.stage_events:
+ * [0] start  [1] router GEMM done  [2] top-k done  [3] dispatch done
+ * [4] expert GEMM1+SwiGLU done  [5] expert GEMM2 done  [6] shared GEMM1 done
+ * [7] shared GEMM2 + combine done (end). */
+#define SPX_STAGE_EVENTS 8
+
+int spx_abi_version(void);
+const char* spx_status_string(int status);
+
+/* Workspace bytes and packed weight sizes for `dims`. Host-only, no GPU work. */
+int spx_layer_sizes(const spx_layer_dims* dims, size_t* workspace_bytes, spx_packed_sizes* packed);
+
+/* BF16 -> BF16 softplus table (beta 1, threshold 20) for all 65536 inputs. */
+int spx_softplus_table(uint16_t* table, void* stream);
+
+/* Repack the reference state_dict into the kernel layouts (outputs sized by spx_layer_sizes). */
+int spx_pack_weights(const spx_layer_dims* dims, const spx_reference_weights* src,
+                     uint16_t* router_weight, uint16_t* expert_w1, uint16_t* expert_w2,
+                     uint16_t* shared_w1, uint16_t* shared_w2, void* stream);
+
+/* Scores, top-k ids and routing weights from given BF16 router logits [T, E]. */
+int spx_route(const spx_layer_dims* dims, const uint16_t* logits, const uint16_t* softplus_table,
+              const uint8_t* resident_mask, uint16_t* router_scores, int64_t* expert_ids,
+              uint16_t* routing_weights, void* workspace, void* stream);
+
+/* Stable permutation of the T*k pairs by expert id, plus per-expert counts. */
+int spx_dispatch(const spx_layer_dims* dims, const int64_t* expert_ids, int32_t* order,
+                 int32_t* counts, void* workspace, void* stream);
+
+/* One full layer forward: router GEMM, selection, dispatch, grouped expert
+ * SwiGLU, shared SwiGLU and combine, routing statistics and auxiliary loss.
+ * No host synchronisation. */
+int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* weights,
+                      const uint16_t* hidden, const spx_layer_outputs* outputs, void* workspace,
+                      void* stream);
+
+/* Read (and clear when `clear` != 0) the device status word of a workspace.
+ * Synchronises `stream`.  *device_status == 0 means no kernel reported an error. */
+int spx_workspace_status(void* workspace, int* device_status, int clear, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPX_H_ */

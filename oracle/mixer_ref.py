@@ -1,0 +1,310 @@
+"""numpy restatement of the reference micro-expert channel mixer forward.
+
+TEST INFRASTRUCTURE ONLY (see ``oracle/__init__.py``).  Every function names
+the reference lines it restates (paths inside mESmaC/spalmer ``src/spalmer``).
+BF16 tensors are ``uint16`` bit patterns; each place where the reference's
+PyTorch CPU kernels materialise a BF16 tensor is an explicit RNE rounding here.
+GEMMs accumulate in float32 (numpy/OpenBLAS), as PyTorch's CPU BF16 GEMMs do,
+so results can differ from the reference in accumulation order only.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+
+from oracle.bf16 import bf16_bits_to_f32, f32_to_bf16_bits, f64_to_bf16_bits, round_bf16
+from oracle.topk import topk_least
+
+_SOFTPLUS_LUT: np.ndarray | None = None
+
+
+def softplus_lut() -> np.ndarray:
+    """BF16 -> BF16 table of ``F.softplus`` (beta=1, threshold=20).
+
+    Restates ``experts/router.py:56``.  PyTorch's CPU kernel evaluates
+    ``x > 20 ? x : log1p(exp(x))`` in float and rounds to BF16; over all 65536
+    BF16 inputs that equals the correctly rounded value, which is what this
+    table holds (pinned against torch in ``tests/test_oracle_golden.py``).
+    """
+
+    global _SOFTPLUS_LUT
+    if _SOFTPLUS_LUT is None:
+        bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+        x = bf16_bits_to_f32(bits).astype(np.float64)
+        with np.errstate(over="ignore", invalid="ignore"):
+            y = np.where(x > 20.0, x, np.log1p(np.exp(x)))
+        out = f64_to_bf16_bits(y)
+        keep = x > 20.0
+        out[keep] = bits[keep]
+        out[np.isnan(x)] = np.uint16(0x7FC0)
+        _SOFTPLUS_LUT = out
+    return _SOFTPLUS_LUT
+
+
+def bf16_matmul(a_bits: np.ndarray, b_f32: np.ndarray) -> np.ndarray:
+    """``a @ b`` with BF16 operands, float32 accumulation, BF16 result (bits)."""
+
+    return f32_to_bf16_bits(bf16_bits_to_f32(a_bits) @ b_f32)
+
+
+def router_logits(x_bits: np.ndarray, w_bits: np.ndarray, bias_bits: np.ndarray | None = None):
+    """``self.proj(hidden_states)`` of ``experts/router.py:51`` (nn.Linear, BF16)."""
+
+    acc = bf16_bits_to_f32(x_bits) @ bf16_bits_to_f32(w_bits).T
+    if bias_bits is not None:
+        acc = acc + bf16_bits_to_f32(bias_bits)[None, :]
+    return f32_to_bf16_bits(acc)
+
+
+def router_scores(logit_bits: np.ndarray, transform: str = "softplus") -> np.ndarray:
+    """``experts/router.py:52-56``: identity (legacy) or softplus, BF16 out."""
+
+    if transform == "identity":
+        return np.array(logit_bits, dtype=np.uint16, copy=True)
+    return softplus_lut()[logit_bits]
+
+
+def routing_softmax(selected_bits: np.ndarray) -> np.ndarray:
+    """``F.softmax(-selected_scores, dim=-1)`` of ``experts/router.py:94`` (BF16 out)."""
+
+    neg = -bf16_bits_to_f32(selected_bits).astype(np.float64)
+    m = neg.max(axis=-1, keepdims=True)
+    with np.errstate(invalid="ignore"):
+        e = np.exp(neg - m)
+        p = e / e.sum(axis=-1, keepdims=True)
+    return f64_to_bf16_bits(p)
+
+
+def select_least_surprised(score_bits: np.ndarray, k: int, resident_mask: np.ndarray | None = None):
+    """``select_least_surprised_experts`` of ``experts/router.py:59-95``.
+
+    Returns ``(expert_ids int64 [T,k], routing_weight_bits uint16 [T,k])``.
+    """
+
+    n = score_bits.shape[-1]
+    if not 1 <= k <= n:
+        raise ValueError(f"num_active must be in [1, {n}]; got {k}")
+    eligible = bf16_bits_to_f32(score_bits).reshape(-1, n).copy()
+    if resident_mask is not None:
+        eligible[:, ~np.asarray(resident_mask, dtype=bool)] = np.inf
+    ids = topk_least(eligible, k)
+    flat = score_bits.reshape(-1, n)
+    selected = np.take_along_axis(flat, ids, axis=1)
+    return ids.reshape(*score_bits.shape[:-1], k), routing_softmax(selected).reshape(
+        *score_bits.shape[:-1], k
+    )
+
+
+def expert_utilization(expert_ids: np.ndarray, num_experts: int) -> np.ndarray:
+    """``experts/losses.py:17-33``: pair fraction per expert (float32)."""
+
+    flat = expert_ids.reshape(-1)
+    counts = np.bincount(flat, minlength=num_experts).astype(np.float32)
+    return counts / np.float32(flat.size)
+
+
+def load_balance_loss(score_bits: np.ndarray, expert_ids: np.ndarray,
+                      resident_mask: np.ndarray | None = None) -> float:
+    """``experts/losses.py:36-70`` with its BF16 rounding points; returns the BF16 value."""
+
+    n = score_bits.shape[-1]
+    logits = -bf16_bits_to_f32(score_bits.reshape(-1, n)).astype(np.float64)
+    if resident_mask is not None:
+        mask = np.asarray(resident_mask, dtype=bool)
+        logits[:, ~mask] = -np.inf
+        eligible = float(mask.sum())
+    else:
+        eligible = float(n)
+    m = logits.max(axis=-1, keepdims=True)
+    e = np.exp(logits - m)
+    prob = bf16_bits_to_f32(f64_to_bf16_bits(e / e.sum(axis=-1, keepdims=True)))
+    mean_p = round_bf16((prob.astype(np.float64).sum(axis=0) / prob.shape[0]).astype(np.float32))
+    frac = round_bf16(expert_utilization(expert_ids, n))
+    prod = round_bf16(frac * mean_p)
+    total = round_bf16(np.float32(prod.astype(np.float64).sum()))
+    elig = round_bf16(np.float32(eligible))
+    return float(round_bf16(np.float32(elig * total)))
+
+
+def pair_counts(expert_index: np.ndarray, num_experts: int) -> np.ndarray:
+    """``_pair_counts`` of ``experts/bank.py:981-985``."""
+
+    return np.bincount(expert_index.reshape(-1), minlength=num_experts).astype(np.int64)
+
+
+def dispatch_order(expert_index: np.ndarray) -> np.ndarray:
+    """``torch.argsort(expert_index, stable=True)`` of ``experts/bank.py:723``."""
+
+    return np.argsort(expert_index.reshape(-1), kind="stable").astype(np.int64)
+
+
+def _silu_bf16(g_bits: np.ndarray) -> np.ndarray:
+    g = bf16_bits_to_f32(g_bits)
+    with np.errstate(over="ignore"):
+        return f32_to_bf16_bits(g / (np.float32(1.0) + np.exp(-g)))
+
+
+def _swiglu_rows(x_bits, gate_f32, up_f32, down_f32):
+    """``silu(x@G)*(x@U) @ D`` with the BF16 rounding of ``experts/bank.py:760-763``."""
+
+    g = bf16_matmul(x_bits, gate_f32)
+    u = bf16_matmul(x_bits, up_f32)
+    h = f32_to_bf16_bits(bf16_bits_to_f32(_silu_bf16(g)) * bf16_bits_to_f32(u))
+    return bf16_matmul(h, down_f32)
+
+
+def _next_pow2(n: np.ndarray) -> np.ndarray:
+    out = np.ones_like(n)
+    pos = n > 1
+    out[pos] = 1 << np.ceil(np.log2(n[pos])).astype(np.int64)
+    return out
+
+
+def grouped_experts(x_bits: np.ndarray, expert_ids: np.ndarray, weight_bits: np.ndarray,
+                    gate_bits: np.ndarray, up_bits: np.ndarray, down_bits: np.ndarray):
+    """``MicroExpertBank._execute_grouped`` (``experts/bank.py:705-779``).
+
+    ``x_bits [T,d]``, ``expert_ids [T,k]``, ``weight_bits [T,k]``; expert stacks
+    ``gate/up [E,d,I]``, ``down [E,I,d]`` (BF16 bits).  Returns the routed
+    update ``[T,d]`` (BF16 bits), reduced in the reference's ``index_add`` order
+    (buckets by padded capacity, then expert id, then sorted pair order) with a
+    BF16 rounding after every addition.
+    """
+
+    T, d = x_bits.shape
+    k = expert_ids.shape[-1]
+    E = gate_bits.shape[0]
+    ids = expert_ids.reshape(-1)
+    P = ids.size
+    counts = pair_counts(ids, E)
+    starts = np.cumsum(counts) - counts
+    order = dispatch_order(ids)
+    w_bf = bf16_bits_to_f32(weight_bits.reshape(-1))
+    weighted = np.zeros((P, d), dtype=np.float32)
+    for e in np.nonzero(counts)[0]:
+        rows = order[starts[e]: starts[e] + counts[e]]
+        tokens = rows // k
+        y = _swiglu_rows(
+            x_bits[tokens],
+            bf16_bits_to_f32(gate_bits[e]),
+            bf16_bits_to_f32(up_bits[e]),
+            bf16_bits_to_f32(down_bits[e]),
+        )
+        # _weighted_expert_updates (bank.py:970-978): bf16(out) * bf16(w)
+        weighted[rows] = round_bf16(bf16_bits_to_f32(y) * w_bf[rows][:, None])
+    # index_add order per token: key (capacity(e), e) over the token's k slots.
+    cap = _next_pow2(counts)
+    slot_e = ids.reshape(T, k)
+    key = cap[slot_e] * (E + 1) + slot_e
+    seq = np.argsort(key, axis=1, kind="stable")
+    contrib = weighted.reshape(T, k, d)
+    acc = np.zeros((T, d), dtype=np.float32)
+    for j in range(k):
+        step = np.take_along_axis(contrib, seq[:, j][:, None, None], axis=1)[:, 0, :]
+        acc = round_bf16(acc + step)
+    return f32_to_bf16_bits(acc), order, counts
+
+
+def shared_swiglu(x_bits, gate_w_bits, up_w_bits, down_w_bits):
+    """``SwiGLU.forward`` of ``nn/ffn.py:27-30`` (nn.Linear weights ``[out,in]``)."""
+
+    return _swiglu_rows(
+        x_bits,
+        bf16_bits_to_f32(gate_w_bits).T,
+        bf16_bits_to_f32(up_w_bits).T,
+        bf16_bits_to_f32(down_w_bits).T,
+    )
+
+
+def execution_metrics(expert_ids: np.ndarray, num_experts: int, execution: str = "grouped") -> dict:
+    """``_expert_execution_metrics`` of ``experts/mixer.py:244-297`` (host ints/floats)."""
+
+    counts = np.bincount(expert_ids.reshape(-1), minlength=num_experts).astype(np.int64)
+    active = counts > 0
+    groups = int(active.sum())
+    max_load = int(counts.max())
+    real = int(counts.sum())
+    if execution == "grouped":
+        padded = int(_next_pow2(counts[active]).sum())
+    elif execution == "loop":
+        padded = real
+    else:
+        raise ValueError(f"unsupported expert execution mode: {execution!r}")
+    cf = max_load * groups
+    return {
+        "expert_group_count": groups,
+        "expert_group_max_load": max_load,
+        "expert_group_real_pairs": real,
+        "expert_group_padded_pairs": padded,
+        "expert_group_padding_amplification": float(np.float32(padded) / np.float32(real)),
+        "expert_group_global_max_counterfactual_padded_pairs": cf,
+        "expert_group_global_max_counterfactual_padding_amplification": float(
+            np.float32(cf) / np.float32(real)
+        ),
+    }
+
+
+@dataclass
+class LayerParams:
+    """BF16 bit patterns of one mixer's state_dict (reference key names in comments)."""
+
+    router_w: np.ndarray            # router.proj.weight [E,d]
+    gate: np.ndarray                # experts.gate_proj [E,d,I]
+    up: np.ndarray                  # experts.up_proj [E,d,I]
+    down: np.ndarray                # experts.down_proj [E,I,d]
+    router_b: np.ndarray | None = None   # router.proj.bias [E]
+    shared_gate: np.ndarray | None = None  # shared.gate_projection.weight [S,d]
+    shared_up: np.ndarray | None = None    # shared.up_projection.weight [S,d]
+    shared_down: np.ndarray | None = None  # shared.down_projection.weight [d,S]
+
+
+def mixer_forward(params: LayerParams, x_bits: np.ndarray, k: int, *,
+                  resident_mask: np.ndarray | None = None, transform: str = "softplus",
+                  logit_bits: np.ndarray | None = None) -> dict:
+    """``MicroExpertChannelMixer.forward`` of ``experts/mixer.py:145-241``.
+
+    ``x_bits [T,d]``.  ``logit_bits`` injects router logits (the bit-exact
+    routing contract is stated "given identical logits").
+    """
+
+    T, d = x_bits.shape
+    E = params.router_w.shape[0]
+    if logit_bits is None:
+        logit_bits = router_logits(x_bits, params.router_w, params.router_b)
+    scores = router_scores(logit_bits, transform)
+    ids, weights = select_least_surprised(scores, k, resident_mask)
+    routed, order, counts = grouped_experts(x_bits, ids, weights, params.gate, params.up, params.down)
+    if params.shared_gate is not None:
+        shared = shared_swiglu(x_bits, params.shared_gate, params.shared_up, params.shared_down)
+        update = f32_to_bf16_bits(bf16_bits_to_f32(routed) + bf16_bits_to_f32(shared))
+    else:
+        shared = None
+        update = routed
+    util = expert_utilization(ids, E)
+    return {
+        "logits": logit_bits,
+        "router_scores": scores,
+        "expert_ids": ids,
+        "routing_weights": weights,
+        "order": order,
+        "counts": counts,
+        "routed": routed,
+        "shared": shared,
+        "update": update,
+        "auxiliary_loss": load_balance_loss(scores, ids, resident_mask),
+        "expert_utilization": util,
+        "num_active_experts": int((util > 0).sum()),
+        **execution_metrics(ids, E),
+    }
+
+
+def isclose_bf16(a_bits: np.ndarray, b_bits: np.ndarray, rtol: float = 2e-2, atol: float = 1e-2) -> bool:
+    a = bf16_bits_to_f32(a_bits).astype(np.float64)
+    b = bf16_bits_to_f32(b_bits).astype(np.float64)
+    return bool(np.all(np.abs(a - b) <= atol + rtol * np.abs(b)))
+
+
+__all__ = [name for name in dir() if not name.startswith("_") and name not in {"annotations", "math"}]

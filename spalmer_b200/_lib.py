@@ -1,0 +1,171 @@
+"""ctypes binding of libspx (the C ABI declared in ``include/spx.h``).
+
+The shared library is built in-tree by ``spalmer_b200.build`` and loaded from
+``spalmer_b200/libspx.so``.  There is no fallback: if the library is missing
+or fails to load, every GPU entry point raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libspx.so"
+
+SPX_OK = 0
+STATUS_NAMES = {
+    -1: "SPX_ERR_INVALID_ARG",
+    -2: "SPX_ERR_UNSUPPORTED",
+    -3: "SPX_ERR_CUDA",
+    -4: "SPX_ERR_DRIVER",
+    -5: "SPX_ERR_TIMEOUT",
+    -6: "SPX_ERR_ALIGNMENT",
+    -7: "SPX_ERR_WORKSPACE",
+    -8: "SPX_ERR_DEVICE",
+}
+
+# Every function exported by include/spx.h (checked by tests/test_abi_symbols.py).
+EXPORTED = (
+    "spx_abi_version",
+    "spx_status_string",
+    "spx_layer_sizes",
+    "spx_softplus_table",
+    "spx_pack_weights",
+    "spx_route",
+    "spx_dispatch",
+    "spx_layer_forward",
+    "spx_workspace_status",
+)
+
+_vp = ctypes.c_void_p
+
+
+class LayerDims(ctypes.Structure):
+    _fields_ = [
+        ("tokens", ctypes.c_int64),
+        ("d_model", ctypes.c_int32),
+        ("num_experts", ctypes.c_int32),
+        ("inter_dim", ctypes.c_int32),
+        ("shared_dim", ctypes.c_int32),
+        ("top_k", ctypes.c_int32),
+        ("score_transform", ctypes.c_int32),
+        ("execution_loop", ctypes.c_int32),
+    ]
+
+
+class ReferenceWeights(ctypes.Structure):
+    _fields_ = [
+        ("router_weight", _vp),
+        ("router_bias", _vp),
+        ("gate_proj", _vp),
+        ("up_proj", _vp),
+        ("down_proj", _vp),
+        ("shared_gate", _vp),
+        ("shared_up", _vp),
+        ("shared_down", _vp),
+    ]
+
+
+class PackedSizes(ctypes.Structure):
+    _fields_ = [
+        ("router_weight", ctypes.c_size_t),
+        ("expert_w1", ctypes.c_size_t),
+        ("expert_w2", ctypes.c_size_t),
+        ("shared_w1", ctypes.c_size_t),
+        ("shared_w2", ctypes.c_size_t),
+    ]
+
+
+class PackedWeights(ctypes.Structure):
+    _fields_ = [
+        ("router_weight", _vp),
+        ("router_bias", _vp),
+        ("expert_w1", _vp),
+        ("expert_w2", _vp),
+        ("shared_w1", _vp),
+        ("shared_w2", _vp),
+        ("softplus_table", _vp),
+        ("resident_mask", _vp),
+    ]
+
+
+class LayerOutputs(ctypes.Structure):
+    _fields_ = [
+        ("update", _vp),
+        ("router_scores", _vp),
+        ("expert_ids", _vp),
+        ("routing_weights", _vp),
+        ("expert_utilization", _vp),
+        ("group_stats", _vp),
+        ("group_ratios", _vp),
+        ("auxiliary_loss", _vp),
+        ("dispatch_order", _vp),
+        ("expert_counts", _vp),
+        ("injected_logits", _vp),
+        ("router_logits", _vp),
+        ("stage_events", _vp),
+    ]
+
+
+STAGE_EVENTS = 8
+STAGE_NAMES = ("router_gemm", "route_topk", "dispatch", "expert_gemm1_swiglu", "expert_gemm2_scatter",
+               "shared_gemm1_swiglu", "shared_gemm2_combine")
+
+
+_lib = None
+
+
+class SpxError(RuntimeError):
+    """A libspx entry point returned a non-zero status."""
+
+
+def load() -> ctypes.CDLL:
+    """Load libspx, raising if it is absent (no CPU fallback exists)."""
+
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise SpxError(
+            f"libspx is not built ({LIB_PATH} missing); run `python -m spalmer_b200.build`"
+        )
+    lib = ctypes.CDLL(str(LIB_PATH))
+    P = ctypes.POINTER
+    sig = {
+        "spx_abi_version": (ctypes.c_int, []),
+        "spx_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+        "spx_layer_sizes": (ctypes.c_int, [P(LayerDims), P(ctypes.c_size_t), P(PackedSizes)]),
+        "spx_softplus_table": (ctypes.c_int, [_vp, _vp]),
+        "spx_pack_weights": (
+            ctypes.c_int,
+            [P(LayerDims), P(ReferenceWeights), _vp, _vp, _vp, _vp, _vp, _vp],
+        ),
+        "spx_route": (ctypes.c_int, [P(LayerDims), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+        "spx_dispatch": (ctypes.c_int, [P(LayerDims), _vp, _vp, _vp, _vp, _vp]),
+        "spx_layer_forward": (
+            ctypes.c_int,
+            [P(LayerDims), P(PackedWeights), _vp, P(LayerOutputs), _vp, _vp],
+        ),
+        "spx_workspace_status": (ctypes.c_int, [_vp, P(ctypes.c_int), ctypes.c_int, _vp]),
+    }
+    for name, (restype, argtypes) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    if lib.spx_abi_version() != 1:
+        raise SpxError(f"libspx ABI version {lib.spx_abi_version()} != 1")
+    _lib = lib
+    return lib
+
+
+def check(status: int, what: str) -> None:
+    if status != SPX_OK:
+        lib = load()
+        text = lib.spx_status_string(status).decode()
+        raise SpxError(f"{what} failed: {STATUS_NAMES.get(status, status)} ({text})")
+
+
+def ptr(tensor) -> int | None:
+    """Device pointer of a tensor (None for None)."""
+
+    return None if tensor is None else tensor.data_ptr()

@@ -1,0 +1,432 @@
+// C ABI of libspx (declared in include/spx.h): shapes, workspace layout,
+// weight packing and the orchestration of one mixer layer forward.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace spx {
+namespace {
+
+constexpr size_t kAlign = 256;
+
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+int round_up_i(int v, int a) { return (v + a - 1) / a * a; }
+int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
+
+uint32_t pow2_at_least(uint32_t v) {
+  uint32_t p = 32;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+struct Shape {
+  int64_t T, P;
+  int d, E, I, S, k;
+  int kd;             // d padded to 64 (GEMM1 / router K)
+  int c, nc, kp;      // expert GEMM1 chunk, chunks, hidden width padded to 64
+  int cs, ncs, ksp;   // shared GEMM1 chunk, chunks, hidden width padded to 64
+  int bn_router, gn_router;
+  int bn_d, gn_d;
+  int lb_blocks, nchunks, max_tiles;
+};
+
+int make_shape(const spx_layer_dims* dm, Shape* s) {
+  if (dm == nullptr || s == nullptr) return SPX_ERR_INVALID_ARG;
+  s->T = dm->tokens;
+  s->d = dm->d_model;
+  s->E = dm->num_experts;
+  s->I = dm->inter_dim;
+  s->S = dm->shared_dim;
+  s->k = dm->top_k;
+  if (s->T < 1 || s->d < 1 || s->E < 1 || s->I < 1 || s->S < 0 || s->k < 1) return SPX_ERR_INVALID_ARG;
+  if (s->k > s->E || s->k > kMaxTopK || s->E > 1024 || s->E > 65535) return SPX_ERR_UNSUPPORTED;
+  if (s->T * s->k > (int64_t(1) << 31) - 1) return SPX_ERR_UNSUPPORTED;
+  s->P = s->T * s->k;
+  s->kd = round_up_i(s->d, 64);
+  s->c = std::min(round_up_i(s->I, 16), 128);
+  s->nc = ceil_div(s->I, s->c);
+  s->kp = round_up_i(s->nc * s->c, 64);
+  if (s->S > 0) {
+    s->cs = std::min(round_up_i(s->S, 16), 128);
+    s->ncs = ceil_div(s->S, s->cs);
+    s->ksp = round_up_i(s->ncs * s->cs, 64);
+  } else {
+    s->cs = s->ncs = s->ksp = 0;
+  }
+  s->bn_router = std::min(256, round_up_i(s->E, 16));
+  s->gn_router = ceil_div(s->E, s->bn_router);
+  s->bn_d = std::min(256, round_up_i(s->d, 16));
+  s->gn_d = ceil_div(s->d, s->bn_d);
+  s->lb_blocks = ceil_div(s->T, kRouteRows);
+  s->nchunks = ceil_div(s->P, kDispatchChunk);
+  s->max_tiles = ceil_div(s->P, kTileRows) + s->E;
+  return SPX_OK;
+}
+
+struct Layout {
+  size_t small, tie_rows, lb_partial, chunk_hist, counts, starts, tiles, order, src_row;
+  size_t hidden, y, shared_hidden, logits, x_pad, util, stats, ratios, aux, total;
+};
+
+Layout make_layout(const Shape& s) {
+  Layout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = round_up(off + bytes, kAlign);
+    return at;
+  };
+  L.small = take(64);
+  L.tie_rows = take(sizeof(int) * s.T);
+  L.lb_partial = take(sizeof(float) * static_cast<size_t>(s.lb_blocks) * s.E);
+  L.chunk_hist = take(sizeof(int) * static_cast<size_t>(s.nchunks) * s.E);
+  L.counts = take(sizeof(int) * s.E);
+  L.starts = take(sizeof(int) * s.E);
+  L.tiles = take(sizeof(int4) * static_cast<size_t>(s.max_tiles));
+  L.order = take(sizeof(int) * s.P);
+  L.src_row = take(sizeof(int) * s.P);
+  L.hidden = take(2 * static_cast<size_t>(s.P) * s.kp);
+  L.y = take(2 * static_cast<size_t>(s.P) * s.d);
+  L.shared_hidden = take(s.S > 0 ? 2 * static_cast<size_t>(s.T) * s.ksp : 0);
+  L.logits = take(2 * static_cast<size_t>(s.T) * s.E);
+  L.x_pad = take(s.kd != s.d ? 2 * static_cast<size_t>(s.T) * s.kd : 0);
+  L.util = take(sizeof(float) * s.E);
+  L.stats = take(sizeof(long long) * 6);
+  L.ratios = take(sizeof(float) * 2);
+  L.aux = take(sizeof(uint16_t) * 2);
+  L.total = off;
+  return L;
+}
+
+template <typename T>
+T* at(void* ws, size_t off) {
+  return reinterpret_cast<T*>(static_cast<uint8_t*>(ws) + off);
+}
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+GemmArgs base_args(int bn, int k_blocks, int* status) {
+  GemmArgs g{};
+  g.bn = bn;
+  g.k_blocks = k_blocks;
+  g.stages = gemm_pick_stages(bn, k_blocks);
+  g.tmem_cols = pow2_at_least(static_cast<uint32_t>(bn));
+  g.groups = 1;
+  g.status = status;
+  return g;
+}
+
+int run_route(const Shape& s, const uint16_t* logits, const uint16_t* lut, const uint8_t* resident,
+              uint16_t* scores, int64_t* ids, uint16_t* weights, void* ws, const Layout& L,
+              cudaStream_t st) {
+  int* small = at<int>(ws, L.small);
+  if (cudaMemsetAsync(small + 1, 0, sizeof(int), st) != cudaSuccess) return SPX_ERR_CUDA;
+  RouteArgs r{};
+  r.logits = logits;
+  r.lut = lut;
+  r.resident = resident;
+  r.scores = scores;
+  r.ids = ids;
+  r.weights = weights;
+  r.tie_count = small + 1;
+  r.tie_rows = at<int>(ws, L.tie_rows);
+  r.lb_partial = at<float>(ws, L.lb_partial);
+  r.tokens = s.T;
+  r.num_experts = s.E;
+  r.top_k = s.k;
+  r.sm_count = sm_count();
+  r.status = small;
+  return launch_route(r, st);
+}
+
+DispatchArgs dispatch_args(const Shape& s, const int64_t* ids, int* order, int* counts, void* ws,
+                           const Layout& L) {
+  DispatchArgs a{};
+  a.ids = ids;
+  a.pairs = s.P;
+  a.tokens = s.T;
+  a.num_experts = s.E;
+  a.top_k = s.k;
+  a.chunk_hist = at<int>(ws, L.chunk_hist);
+  a.counts = counts != nullptr ? counts : at<int>(ws, L.counts);
+  a.starts = at<int>(ws, L.starts);
+  a.tiles = at<int4>(ws, L.tiles);
+  a.num_tiles = at<int>(ws, L.small) + 2;
+  a.order = order != nullptr ? order : at<int>(ws, L.order);
+  a.src_row = at<int>(ws, L.src_row);
+  a.lb_partial = at<float>(ws, L.lb_partial);
+  a.lb_blocks = s.lb_blocks;
+  a.eligible_experts = s.E;
+  a.status = at<int>(ws, L.small);
+  return a;
+}
+
+}  // namespace
+}  // namespace spx
+
+using namespace spx;
+
+extern "C" {
+
+int spx_abi_version(void) { return SPX_ABI_VERSION; }
+
+const char* spx_status_string(int status) {
+  switch (status) {
+    case SPX_OK:
+      return "ok";
+    case SPX_ERR_INVALID_ARG:
+      return "invalid argument";
+    case SPX_ERR_UNSUPPORTED:
+      return "unsupported shape or configuration";
+    case SPX_ERR_CUDA:
+      return "CUDA runtime error";
+    case SPX_ERR_DRIVER:
+      return "CUDA driver entry point or tensor map error";
+    case SPX_ERR_TIMEOUT:
+      return "device wait timed out";
+    case SPX_ERR_ALIGNMENT:
+      return "pointer or stride not 16-byte aligned";
+    case SPX_ERR_WORKSPACE:
+      return "workspace missing or too small";
+    case SPX_ERR_DEVICE:
+      return "a kernel reported an error in the workspace status word";
+    default:
+      return "unknown status";
+  }
+}
+
+int spx_layer_sizes(const spx_layer_dims* dims, size_t* workspace_bytes, spx_packed_sizes* packed) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (workspace_bytes != nullptr) *workspace_bytes = make_layout(s).total;
+  if (packed != nullptr) {
+    packed->router_weight = static_cast<size_t>(s.E) * s.kd;
+    packed->expert_w1 = static_cast<size_t>(s.E) * s.nc * 2 * s.c * s.kd;
+    packed->expert_w2 = static_cast<size_t>(s.E) * s.d * s.kp;
+    packed->shared_w1 = s.S > 0 ? static_cast<size_t>(s.ncs) * 2 * s.cs * s.kd : 0;
+    packed->shared_w2 = s.S > 0 ? static_cast<size_t>(s.d) * s.ksp : 0;
+  }
+  return SPX_OK;
+}
+
+int spx_softplus_table(uint16_t* table, void* stream) {
+  if (table == nullptr) return SPX_ERR_INVALID_ARG;
+  return launch_softplus_table(table, static_cast<cudaStream_t>(stream));
+}
+
+int spx_pack_weights(const spx_layer_dims* dims, const spx_reference_weights* src, uint16_t* router_weight,
+                     uint16_t* expert_w1, uint16_t* expert_w2, uint16_t* shared_w1, uint16_t* shared_w2,
+                     void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (src == nullptr || src->router_weight == nullptr || src->gate_proj == nullptr || src->up_proj == nullptr ||
+      src->down_proj == nullptr || router_weight == nullptr || expert_w1 == nullptr || expert_w2 == nullptr)
+    return SPX_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = launch_pad_rows(src->router_weight, s.E, s.d, s.kd, router_weight, st);
+  if (rc == SPX_OK)
+    rc = launch_pack_chunked_w1(src->gate_proj, src->up_proj, s.E, s.d, s.I, s.kd, s.c, s.nc, 0, expert_w1, st);
+  if (rc == SPX_OK) rc = launch_pack_w2(src->down_proj, s.E, s.I, s.d, s.kp, 0, expert_w2, st);
+  if (rc == SPX_OK && s.S > 0) {
+    if (src->shared_gate == nullptr || src->shared_up == nullptr || src->shared_down == nullptr ||
+        shared_w1 == nullptr || shared_w2 == nullptr)
+      return SPX_ERR_INVALID_ARG;
+    rc = launch_pack_chunked_w1(src->shared_gate, src->shared_up, 1, s.d, s.S, s.kd, s.cs, s.ncs, 1, shared_w1, st);
+    if (rc == SPX_OK) rc = launch_pack_w2(src->shared_down, 1, s.S, s.d, s.ksp, 1, shared_w2, st);
+  }
+  return rc;
+}
+
+int spx_route(const spx_layer_dims* dims, const uint16_t* logits, const uint16_t* softplus_table,
+              const uint8_t* resident_mask, uint16_t* router_scores, int64_t* expert_ids, uint16_t* routing_weights,
+              void* workspace, void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (logits == nullptr || router_scores == nullptr || expert_ids == nullptr || routing_weights == nullptr)
+    return SPX_ERR_INVALID_ARG;
+  if (workspace == nullptr) return SPX_ERR_WORKSPACE;
+  if (dims->score_transform == 0 && softplus_table == nullptr) return SPX_ERR_INVALID_ARG;
+  const Layout L = make_layout(s);
+  return run_route(s, logits, dims->score_transform == 0 ? softplus_table : nullptr, resident_mask, router_scores,
+                   expert_ids, routing_weights, workspace, L, static_cast<cudaStream_t>(stream));
+}
+
+int spx_dispatch(const spx_layer_dims* dims, const int64_t* expert_ids, int32_t* order, int32_t* counts,
+                 void* workspace, void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (expert_ids == nullptr) return SPX_ERR_INVALID_ARG;
+  if (workspace == nullptr) return SPX_ERR_WORKSPACE;
+  const Layout L = make_layout(s);
+  DispatchArgs a = dispatch_args(s, expert_ids, order, counts, workspace, L);
+  a.lb_blocks = 0;  // no routing probabilities here: skip the auxiliary loss
+  a.execution_loop = dims->execution_loop;
+  return launch_dispatch(a, static_cast<cudaStream_t>(stream));
+}
+
+int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, const uint16_t* hidden,
+                      const spx_layer_outputs* out, void* workspace, void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (w == nullptr || out == nullptr || hidden == nullptr) return SPX_ERR_INVALID_ARG;
+  if (workspace == nullptr) return SPX_ERR_WORKSPACE;
+  if (out->update == nullptr || out->router_scores == nullptr || out->expert_ids == nullptr ||
+      out->routing_weights == nullptr)
+    return SPX_ERR_INVALID_ARG;
+  if (w->router_weight == nullptr || w->expert_w1 == nullptr || w->expert_w2 == nullptr) return SPX_ERR_INVALID_ARG;
+  if (s.S > 0 && (w->shared_w1 == nullptr || w->shared_w2 == nullptr)) return SPX_ERR_INVALID_ARG;
+  if (dims->score_transform == 0 && w->softplus_table == nullptr) return SPX_ERR_INVALID_ARG;
+  if (!aligned16(hidden) || !aligned16(out->update) || !aligned16(workspace)) return SPX_ERR_ALIGNMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const Layout L = make_layout(s);
+  int* status = at<int>(workspace, L.small);
+  int rc = SPX_OK;
+  auto mark = [&](int i) {
+    if (out->stage_events != nullptr && out->stage_events[i] != nullptr)
+      cudaEventRecord(static_cast<cudaEvent_t>(out->stage_events[i]), st);
+  };
+  mark(0);
+
+  // A operand source: the hidden states, zero-padded to a multiple of 64 columns if needed.
+  const uint16_t* xa = hidden;
+  if (s.kd != s.d) {
+    uint16_t* xp = at<uint16_t>(workspace, L.x_pad);
+    if ((rc = launch_pad_rows(hidden, s.T, s.d, s.kd, xp, st)) != SPX_OK) return rc;
+    xa = xp;
+  }
+
+  // ---- K1: router logits (tcgen05 GEMM) unless injected
+  const uint16_t* logits = out->injected_logits;
+  if (logits == nullptr) {
+    uint16_t* lg = out->router_logits != nullptr ? out->router_logits : at<uint16_t>(workspace, L.logits);
+    GemmArgs g = base_args(s.bn_router, s.kd / 64, status);
+    if ((rc = encode_2d(&g.tma_a, xa, s.T, s.kd, s.kd, kTileRows)) != SPX_OK) return rc;
+    if ((rc = encode_3d(&g.tma_b, w->router_weight, 1, s.E, s.kd, s.bn_router)) != SPX_OK) return rc;
+    g.m_rows = static_cast<int>(s.T);
+    g.n_valid = s.E;
+    g.out = lg;
+    g.ldo = s.E;
+    g.bias = w->router_bias;
+    if ((rc = launch_gemm(kEpiStore, g, ceil_div(s.T, kTileRows), s.gn_router, st)) != SPX_OK) return rc;
+    logits = lg;
+  }
+  mark(1);
+
+  // ---- K1: scores, top-k, weights, load-balance partials
+  rc = run_route(s, logits, dims->score_transform == 0 ? w->softplus_table : nullptr, w->resident_mask,
+                 out->router_scores, out->expert_ids, out->routing_weights, workspace, L, st);
+  if (rc != SPX_OK) return rc;
+  mark(2);
+
+  // ---- K2: dispatch + statistics
+  DispatchArgs da = dispatch_args(s, out->expert_ids, out->dispatch_order, out->expert_counts, workspace, L);
+  da.utilization = out->expert_utilization != nullptr ? out->expert_utilization : at<float>(workspace, L.util);
+  da.group_stats = out->group_stats != nullptr ? reinterpret_cast<long long*>(out->group_stats)
+                                               : at<long long>(workspace, L.stats);
+  da.group_ratios = out->group_ratios != nullptr ? out->group_ratios : at<float>(workspace, L.ratios);
+  da.aux_loss = out->auxiliary_loss != nullptr ? out->auxiliary_loss : at<uint16_t>(workspace, L.aux);
+  da.resident = w->resident_mask;
+  da.execution_loop = dims->execution_loop;
+  if ((rc = launch_dispatch(da, st)) != SPX_OK) return rc;
+  mark(3);
+
+  uint16_t* hid = at<uint16_t>(workspace, L.hidden);
+  uint16_t* y = at<uint16_t>(workspace, L.y);
+
+  // ---- K3a: expert GEMM1 (gathered rows) + SwiGLU
+  {
+    GemmArgs g = base_args(2 * s.c, s.kd / 64, status);
+    if ((rc = encode_2d(&g.tma_a, xa, s.T, s.kd, s.kd, 1)) != SPX_OK) return rc;
+    if ((rc = encode_3d(&g.tma_b, w->expert_w1, s.E, static_cast<int64_t>(s.nc) * 2 * s.c, s.kd, 2 * s.c)) != SPX_OK)
+      return rc;
+    g.groups = s.E;
+    g.gather = 1;
+    g.gather_idx = da.src_row;
+    g.tiles = da.tiles;
+    g.num_tiles = da.num_tiles;
+    g.chunk = s.c;
+    g.h_cols = s.kp;
+    g.out = hid;
+    g.ldo = s.kp;
+    if ((rc = launch_gemm(kEpiSwiglu, g, s.max_tiles, s.nc, st)) != SPX_OK) return rc;
+  }
+  mark(4);
+  // ---- K3b: expert GEMM2, scaled by the routing weight, scattered to pair order
+  {
+    GemmArgs g = base_args(s.bn_d, s.kp / 64, status);
+    if ((rc = encode_2d(&g.tma_a, hid, s.P, s.kp, s.kp, kTileRows)) != SPX_OK) return rc;
+    if ((rc = encode_3d(&g.tma_b, w->expert_w2, s.E, s.d, s.kp, s.bn_d)) != SPX_OK) return rc;
+    g.groups = s.E;
+    g.tiles = da.tiles;
+    g.num_tiles = da.num_tiles;
+    g.n_valid = s.d;
+    g.out = y;
+    g.ldo = s.d;
+    g.pos_to_pair = da.order;
+    g.pair_weight = out->routing_weights;
+    if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn_d, st)) != SPX_OK) return rc;
+  }
+  mark(5);
+  // ---- K4: shared SwiGLU with the combine fused into its down projection
+  if (s.S > 0) {
+    uint16_t* hs = at<uint16_t>(workspace, L.shared_hidden);
+    {
+      GemmArgs g = base_args(2 * s.cs, s.kd / 64, status);
+      if ((rc = encode_2d(&g.tma_a, xa, s.T, s.kd, s.kd, kTileRows)) != SPX_OK) return rc;
+      if ((rc = encode_3d(&g.tma_b, w->shared_w1, 1, static_cast<int64_t>(s.ncs) * 2 * s.cs, s.kd, 2 * s.cs)) !=
+          SPX_OK)
+        return rc;
+      g.m_rows = static_cast<int>(s.T);
+      g.chunk = s.cs;
+      g.h_cols = s.ksp;
+      g.out = hs;
+      g.ldo = s.ksp;
+      if ((rc = launch_gemm(kEpiSwiglu, g, ceil_div(s.T, kTileRows), s.ncs, st)) != SPX_OK) return rc;
+    }
+    mark(6);
+    {
+      GemmArgs g = base_args(s.bn_d, s.ksp / 64, status);
+      if ((rc = encode_2d(&g.tma_a, hs, s.T, s.ksp, s.ksp, kTileRows)) != SPX_OK) return rc;
+      if ((rc = encode_3d(&g.tma_b, w->shared_w2, 1, s.d, s.ksp, s.bn_d)) != SPX_OK) return rc;
+      g.m_rows = static_cast<int>(s.T);
+      g.n_valid = s.d;
+      g.out = out->update;
+      g.ldo = s.d;
+      g.y_pairs = y;
+      g.ld_y = s.d;
+      g.top_k = s.k;
+      if ((rc = launch_gemm(kEpiCombine, g, ceil_div(s.T, kTileRows), s.gn_d, st)) != SPX_OK) return rc;
+    }
+  } else {
+    mark(6);
+    if ((rc = launch_combine(y, s.T, s.d, s.k, out->update, st)) != SPX_OK) return rc;
+  }
+  mark(7);
+  return SPX_OK;
+}
+
+int spx_workspace_status(void* workspace, int* device_status, int clear, void* stream) {
+  if (workspace == nullptr || device_status == nullptr) return SPX_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  if (cudaMemcpyAsync(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess) return SPX_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return SPX_ERR_CUDA;
+  *device_status = v;
+  if (clear && v != 0) {
+    if (cudaMemsetAsync(workspace, 0, sizeof(int), st) != cudaSuccess) return SPX_ERR_CUDA;
+  }
+  return SPX_OK;
+}
+
+}  // extern "C"

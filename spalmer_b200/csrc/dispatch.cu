@@ -1,0 +1,216 @@
+// K2 dispatch: stable counting sort of routed pairs by expert id, the grouped
+// GEMM tile table, and the per-layer routing statistics.
+//
+// Reference: mESmaC/spalmer src/spalmer/experts/bank.py:721-736
+// (`_pair_counts`, `cumsum`, `argsort(expert_index, stable=True)`, group ids),
+// experts/losses.py:17-33 (utilization), losses.py:58-70 (load-balance loss)
+// and experts/mixer.py:244-297 (padding / load telemetry).  The reference
+// syncs with the host twice here; this path keeps everything on the device.
+//
+// Pairs are in the reference's order p = token * k + slot
+// (mixer.py:193-197).  The permutation equals argsort(stable=True): pairs of
+// one expert keep increasing p.
+//   dispatch_count_kernel   per-chunk expert histograms (chunk = 2048 pairs)
+//   dispatch_scan_kernel    one CTA: chunk offsets, counts, starts, tile table,
+//                           utilization, group statistics, auxiliary loss
+//   dispatch_scatter_kernel per-chunk stable placement (warp match_any ranks)
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace spx {
+
+__device__ __forceinline__ int64_t min_i64(int64_t a, int64_t b) { return a < b ? a : b; }
+
+__global__ void __launch_bounds__(kDispatchThreads) dispatch_count_kernel(const DispatchArgs a) {
+  extern __shared__ int hist[];
+  const int E = a.num_experts;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
+  const int64_t p0 = static_cast<int64_t>(blockIdx.x) * kDispatchChunk;
+  const int64_t p1 = min_i64(a.pairs, p0 + kDispatchChunk);
+  for (int64_t p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
+    const int64_t e = a.ids[p];
+    if (e < 0 || e >= E) {
+      record_error(a.status, SPX_DEV_BAD_EXPERT);
+      continue;
+    }
+    atomicAdd(&hist[e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    a.chunk_hist[static_cast<int64_t>(blockIdx.x) * E + e] = hist[e];
+}
+
+__device__ __forceinline__ int64_t next_pow2_i64(int64_t n) {
+  int64_t c = 1;
+  while (c < n) c <<= 1;
+  return c;
+}
+
+__global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs a) {
+  __shared__ int s_scan[1024];
+  __shared__ float s_red[1024];
+  __shared__ long long s_i64[4];
+  const int E = a.num_experts;
+  const int nchunks = static_cast<int>((a.pairs + kDispatchChunk - 1) / kDispatchChunk);
+  const int e = threadIdx.x;
+
+  // Exclusive scan over chunks for each expert (chunk offsets within expert).
+  int count = 0;
+  if (e < E) {
+    for (int c = 0; c < nchunks; ++c) {
+      int* slot = a.chunk_hist + static_cast<int64_t>(c) * E + e;
+      const int v = *slot;
+      *slot = count;
+      count += v;
+    }
+  }
+  // Block-wide exclusive scans: pair starts and tile starts.
+  const int tiles = (count + kTileRows - 1) / kTileRows;
+  s_scan[threadIdx.x] = (e < E) ? count : 0;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const int v = threadIdx.x >= off ? s_scan[threadIdx.x - off] : 0;
+    __syncthreads();
+    s_scan[threadIdx.x] += v;
+    __syncthreads();
+  }
+  const int start = s_scan[threadIdx.x] - ((e < E) ? count : 0);
+  __syncthreads();
+  s_scan[threadIdx.x] = (e < E) ? tiles : 0;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const int v = threadIdx.x >= off ? s_scan[threadIdx.x - off] : 0;
+    __syncthreads();
+    s_scan[threadIdx.x] += v;
+    __syncthreads();
+  }
+  const int tile_start = s_scan[threadIdx.x] - ((e < E) ? tiles : 0);
+  if (threadIdx.x == 1023) *a.num_tiles = s_scan[1023];
+  if (e < E) {
+    a.counts[e] = count;
+    a.starts[e] = start;
+    for (int t = 0; t < tiles; ++t) {
+      const int r0 = t * kTileRows;
+      a.tiles[tile_start + t] = make_int4(e, start + r0, min(kTileRows, count - r0), 0);
+    }
+  }
+
+  // Utilization (losses.py:28-33): count / P in float32.
+  const float util = (e < E) ? static_cast<float>(count) / static_cast<float>(a.pairs) : 0.0f;
+  if (e < E && a.utilization != nullptr) a.utilization[e] = util;
+
+  // Group statistics (mixer.py:257-297).
+  if (threadIdx.x < 4) s_i64[threadIdx.x] = 0;
+  __syncthreads();
+  if (e < E && a.resident != nullptr && a.resident[e] != 0)
+    atomicAdd(reinterpret_cast<unsigned long long*>(&s_i64[3]), 1ull);
+  if (e < E && count > 0) {
+    atomicAdd(reinterpret_cast<unsigned long long*>(&s_i64[0]), 1ull);
+    atomicMax(reinterpret_cast<unsigned long long*>(&s_i64[1]), static_cast<unsigned long long>(count));
+    atomicAdd(reinterpret_cast<unsigned long long*>(&s_i64[2]),
+              static_cast<unsigned long long>(a.execution_loop ? count : next_pow2_i64(count)));
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && a.group_stats != nullptr) {
+    const long long groups = s_i64[0], max_load = s_i64[1], padded = s_i64[2];
+    const long long real = a.pairs;
+    a.group_stats[0] = groups;             // expert_group_count
+    a.group_stats[1] = max_load;           // expert_group_max_load
+    a.group_stats[2] = real;               // expert_group_real_pairs
+    a.group_stats[3] = padded;             // expert_group_padded_pairs
+    a.group_stats[4] = max_load * groups;  // ..._global_max_counterfactual_padded_pairs
+    a.group_stats[5] = groups;             // num_active_experts ((utilization > 0).sum())
+    a.group_ratios[0] = static_cast<float>(padded) / static_cast<float>(real);
+    a.group_ratios[1] = static_cast<float>(max_load * groups) / static_cast<float>(real);
+  }
+
+  // Load-balance loss (losses.py:58-70) with its BF16 rounding points:
+  // mean_p = bf16(sum_t p / T), frac = bf16(util), prod = bf16(frac*mean_p),
+  // total = bf16(sum prod), loss = bf16(bf16(eligible) * total).
+  if (a.aux_loss != nullptr && a.lb_blocks > 0) {
+    float prod = 0.0f;
+    if (e < E) {
+      float s = 0.0f;
+      for (int b = 0; b < a.lb_blocks; ++b) s += a.lb_partial[static_cast<int64_t>(b) * E + e];
+      const float mean_p = round_bf16(s / static_cast<float>(a.tokens));
+      prod = round_bf16(round_bf16(util) * mean_p);
+    }
+    s_red[threadIdx.x] = prod;
+    __syncthreads();
+    for (int off = 512; off > 0; off >>= 1) {
+      if (threadIdx.x < off) s_red[threadIdx.x] += s_red[threadIdx.x + off];
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+      const float total = round_bf16(s_red[0]);
+      const long long n_eligible = a.resident != nullptr ? s_i64[3] : a.eligible_experts;
+      const float eligible = round_bf16(static_cast<float>(n_eligible));
+      a.aux_loss[0] = f32_to_bf16_rne(eligible * total);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kDispatchThreads) dispatch_scatter_kernel(const DispatchArgs a) {
+  extern __shared__ int warp_base[];  // [kDispatchWarps][E]
+  const int E = a.num_experts;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kSub = kDispatchChunk / kDispatchWarps;
+  for (int i = threadIdx.x; i < kDispatchWarps * E; i += blockDim.x) warp_base[i] = 0;
+  __syncthreads();
+  const int64_t p0 = static_cast<int64_t>(blockIdx.x) * kDispatchChunk + static_cast<int64_t>(warp) * kSub;
+  const int64_t p1 = min_i64(a.pairs, p0 + kSub);
+  // Pass 1: per-warp counts of this warp's sub-chunk.
+  for (int64_t p = p0 + lane; p < p1; p += 32) {
+    const int64_t e = a.ids[p];
+    if (e >= 0 && e < E) atomicAdd(&warp_base[warp * E + e], 1);
+  }
+  __syncthreads();
+  // Per expert: global base = start + chunk offset, then exclusive over warps.
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int base = a.starts[e] + a.chunk_hist[static_cast<int64_t>(blockIdx.x) * E + e];
+    for (int w = 0; w < kDispatchWarps; ++w) {
+      const int c = warp_base[w * E + e];
+      warp_base[w * E + e] = base;
+      base += c;
+    }
+  }
+  __syncthreads();
+  // Pass 2: stable placement, 32 consecutive pairs at a time.
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int64_t g = p0; g < p1; g += 32) {
+    const int64_t p = g + lane;
+    const bool valid = p < p1;
+    const int e = valid ? static_cast<int>(a.ids[p]) : -1;
+    const bool ok = valid && e >= 0 && e < E;
+    const unsigned peers = __match_any_sync(0xFFFFFFFFu, ok ? e : -1);
+    int base = 0;
+    if (ok) base = warp_base[warp * E + e];
+    __syncwarp();
+    if (ok) {
+      const int rank = __popc(peers & lt_mask);
+      const int pos = base + rank;
+      a.order[pos] = static_cast<int>(p);
+      a.src_row[pos] = static_cast<int>(p / a.top_k);
+      if ((peers & lt_mask) == 0) warp_base[warp * E + e] = base + __popc(peers);
+    }
+    __syncwarp();
+  }
+}
+
+int launch_dispatch(const DispatchArgs& a, cudaStream_t stream) {
+  if (a.pairs <= 0) return SPX_ERR_INVALID_ARG;
+  if (a.num_experts > 1024) return SPX_ERR_UNSUPPORTED;
+  const int nchunks = static_cast<int>((a.pairs + kDispatchChunk - 1) / kDispatchChunk);
+  dispatch_count_kernel<<<nchunks, kDispatchThreads, a.num_experts * sizeof(int), stream>>>(a);
+  if (cudaGetLastError() != cudaSuccess) return SPX_ERR_CUDA;
+  dispatch_scan_kernel<<<1, 1024, 0, stream>>>(a);
+  if (cudaGetLastError() != cudaSuccess) return SPX_ERR_CUDA;
+  dispatch_scatter_kernel<<<nchunks, kDispatchThreads, kDispatchWarps * a.num_experts * sizeof(int), stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+}  // namespace spx

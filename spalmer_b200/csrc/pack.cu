@@ -1,0 +1,147 @@
+// Weight repacking (a derived cache of the reference state_dict) and the
+// standalone combine used when the layer has no shared path.
+//
+// The reference stores expert projections as [E, d, I] / [E, I, d] ("x @ W",
+// experts/bank.py:52-54) and the shared SwiGLU as nn.Linear [out, in]
+// (nn/ffn.py:16-18).  The tensor-core kernels want every B operand K-major
+// ([N rows, K contiguous]) and GEMM1 wants gate and up side by side:
+//   W1[e] rows: for chunk c: [gate cols c*C .. c*C+C) ++ [up cols c*C .. c*C+C)
+//   W2[e] = down[e]^T  ([d rows, I contiguous], K zero-padded to a multiple of 64)
+// Rows or columns beyond the real sizes are zero, so padding contributes 0.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace spx {
+
+__global__ void pack_chunked_w1_kernel(const uint16_t* __restrict__ gate, const uint16_t* __restrict__ up,
+                                       int experts, int d, int inter, int kd, int chunk, int chunks,
+                                       int transposed_src, uint16_t* __restrict__ out) {
+  const int64_t rows_per_e = static_cast<int64_t>(chunks) * 2 * chunk;
+  const int64_t total = static_cast<int64_t>(experts) * rows_per_e * kd;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int kk = static_cast<int>(idx % kd);
+    const int64_t rowg = idx / kd;
+    const int row = static_cast<int>(rowg % rows_per_e);
+    const int e = static_cast<int>(rowg / rows_per_e);
+    const int ch = row / (2 * chunk);
+    const int within = row - ch * 2 * chunk;
+    const int half = within / chunk;
+    const int i = ch * chunk + (within - half * chunk);
+    uint16_t v = 0;
+    if (i < inter && kk < d) {
+      const uint16_t* src = half == 0 ? gate : up;
+      v = transposed_src ? src[static_cast<int64_t>(i) * d + kk]
+                         : src[(static_cast<int64_t>(e) * d + kk) * inter + i];
+    }
+    out[idx] = v;
+  }
+}
+
+__global__ void pack_w2_kernel(const uint16_t* __restrict__ down, int experts, int inter, int d, int kp,
+                               int transposed_src, uint16_t* __restrict__ out) {
+  const int64_t total = static_cast<int64_t>(experts) * d * kp;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(idx % kp);
+    const int64_t rest = idx / kp;
+    const int n = static_cast<int>(rest % d);
+    const int e = static_cast<int>(rest / d);
+    uint16_t v = 0;
+    if (i < inter) {
+      v = transposed_src ? down[static_cast<int64_t>(n) * inter + i]
+                         : down[(static_cast<int64_t>(e) * inter + i) * d + n];
+    }
+    out[idx] = v;
+  }
+}
+
+__global__ void pad_rows_kernel(const uint16_t* __restrict__ src, int64_t rows, int cols, int ld_out,
+                                uint16_t* __restrict__ out) {
+  const int64_t total = rows * ld_out;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(idx % ld_out);
+    const int64_t r = idx / ld_out;
+    out[idx] = c < cols ? src[r * cols + c] : static_cast<uint16_t>(0);
+  }
+}
+
+// update[t] = bf16(sum_j Y[t*k + j]) in FP32, 8 columns per thread.
+__global__ void combine_kernel(const uint16_t* __restrict__ y, int64_t tokens, int d, int k,
+                               uint16_t* __restrict__ out) {
+  const int vec = d / 8;
+  const int64_t total = tokens * vec;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = idx / vec;
+    const int c = static_cast<int>(idx - t * vec) * 8;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int j = 0; j < k; ++j) {
+      const uint4 q = *reinterpret_cast<const uint4*>(y + (t * k + j) * d + c);
+      const uint16_t* h = reinterpret_cast<const uint16_t*>(&q);
+#pragma unroll
+      for (int q8 = 0; q8 < 8; ++q8) acc[q8] += bf16_to_f32(h[q8]);
+    }
+    uint4 o;
+    uint16_t* oh = reinterpret_cast<uint16_t*>(&o);
+#pragma unroll
+    for (int q8 = 0; q8 < 8; ++q8) oh[q8] = f32_to_bf16_rne(acc[q8]);
+    *reinterpret_cast<uint4*>(out + t * d + c) = o;
+  }
+}
+
+__global__ void combine_scalar_kernel(const uint16_t* __restrict__ y, int64_t tokens, int d, int k,
+                                      uint16_t* __restrict__ out) {
+  const int64_t total = tokens * d;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = idx / d;
+    const int c = static_cast<int>(idx - t * d);
+    float acc = 0.0f;
+    for (int j = 0; j < k; ++j) acc += bf16_to_f32(y[(t * k + j) * d + c]);
+    out[idx] = f32_to_bf16_rne(acc);
+  }
+}
+
+static int grid_for(int64_t total) {
+  int64_t g = (total + 255) / 256;
+  if (g > 148 * 32) g = 148 * 32;
+  return static_cast<int>(g < 1 ? 1 : g);
+}
+
+int launch_pack_chunked_w1(const uint16_t* gate, const uint16_t* up, int experts, int d, int inter, int kd,
+                           int chunk, int chunks, int transposed_src, uint16_t* out, cudaStream_t stream) {
+  const int64_t total = static_cast<int64_t>(experts) * chunks * 2 * chunk * kd;
+  pack_chunked_w1_kernel<<<grid_for(total), 256, 0, stream>>>(gate, up, experts, d, inter, kd, chunk, chunks,
+                                                               transposed_src, out);
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+int launch_pack_w2(const uint16_t* down, int experts, int inter, int d, int kp, int transposed_src, uint16_t* out,
+                   cudaStream_t stream) {
+  const int64_t total = static_cast<int64_t>(experts) * d * kp;
+  pack_w2_kernel<<<grid_for(total), 256, 0, stream>>>(down, experts, inter, d, kp, transposed_src, out);
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+int launch_pad_rows(const uint16_t* src, int64_t rows, int cols, int ld_out, uint16_t* out, cudaStream_t stream) {
+  pad_rows_kernel<<<grid_for(rows * ld_out), 256, 0, stream>>>(src, rows, cols, ld_out, out);
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+int launch_combine(const uint16_t* y, int64_t tokens, int d, int k, uint16_t* out, cudaStream_t stream) {
+  const bool vec_ok = (d % 8) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0 &&
+                      (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+  if (vec_ok) {
+    combine_kernel<<<grid_for(tokens * (d / 8)), 256, 0, stream>>>(y, tokens, d, k, out);
+  } else {
+    combine_scalar_kernel<<<grid_for(tokens * d), 256, 0, stream>>>(y, tokens, d, k, out);
+  }
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+}  // namespace spx

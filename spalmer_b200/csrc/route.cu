@@ -1,0 +1,275 @@
+// K1 (selection half): surprise scores, least-surprise top-k, routing weights
+// and load-balance partial sums, from BF16 router logits.
+//
+// Reference: mESmaC/spalmer src/spalmer/experts/router.py:52-56 (softplus),
+// router.py:80-95 (masked bottom-k, gather, softmax of -scores) and
+// experts/losses.py:58-70 (softmax over all experts, mean over tokens).
+//
+// route_select_kernel: one CTA per 128 token rows, one thread per row.  The
+//   CTA stages its rows of logits into shared memory with 16-byte coalesced
+//   loads, maps them through the softplus table and writes router_scores.
+//   Each thread keeps the k+1 smallest (score, index) keys of its row in
+//   registers.  When those k+1 scores are pairwise distinct the CPU tie order
+//   cannot matter and the sorted k smallest are final; otherwise the row is
+//   appended to a tie list.  The same pass accumulates the per-expert sums of
+//   BF16-rounded softmax(-scores) probabilities for the load-balance loss.
+// route_ties_kernel: replays PyTorch's CPU top-k (topk_exact.cuh) for every
+//   listed row, one thread per row, the row staged in shared memory.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kernels.h"
+#include "sm100.cuh"
+#include "topk_exact.cuh"
+
+namespace spx {
+
+__device__ __forceinline__ int64_t min_i64(int64_t a, int64_t b) { return a < b ? a : b; }
+
+namespace {
+
+// Total order on BF16 bit patterns that agrees with the CPU comparator:
+// -0 == +0, NaN after +inf.
+__device__ __forceinline__ uint32_t order_key16(uint16_t b) {
+  if ((b & 0x7F80u) == 0x7F80u && (b & 0x007Fu) != 0u) return 0xFFFFu;  // NaN
+  if (b == 0x8000u) b = 0;                                               // -0 -> +0
+  return (b & 0x8000u) ? (~static_cast<uint32_t>(b) & 0xFFFFu) : (static_cast<uint32_t>(b) | 0x8000u);
+}
+
+// Softmax of the negated selected scores, computed in double and rounded to
+// BF16 through float (the conversion PyTorch applies).
+__device__ __forceinline__ void routing_softmax(const uint16_t* sel, int k, uint16_t* out) {
+  double m = -1.0e300;
+  for (int j = 0; j < k; ++j) m = fmax(m, -static_cast<double>(bf16_to_f32(sel[j])));
+  double sum = 0.0;
+  for (int j = 0; j < k; ++j) sum += exp(-static_cast<double>(bf16_to_f32(sel[j])) - m);
+  for (int j = 0; j < k; ++j) {
+    const double p = exp(-static_cast<double>(bf16_to_f32(sel[j])) - m) / sum;
+    out[j] = f32_to_bf16_rne(__double2float_rn(p));
+  }
+}
+
+}  // namespace
+
+__global__ void softplus_table_kernel(uint16_t* lut) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= 65536) return;
+  const uint16_t bits = static_cast<uint16_t>(b);
+  const float x = bf16_to_f32(bits);
+  uint16_t out;
+  if (x != x) {
+    out = 0x7FC0u;
+  } else if (x > 20.0f) {
+    out = bits;  // F.softplus threshold: returns the input unchanged
+  } else {
+    const double y = log1p(exp(static_cast<double>(x)));
+    out = f32_to_bf16_rne(__double2float_rn(y));
+  }
+  lut[b] = out;
+}
+
+template <int K1MAX>
+__global__ void __launch_bounds__(kRouteRows) route_select_kernel(const RouteArgs a) {
+  extern __shared__ uint32_t route_smem[];
+  const int E = a.num_experts;
+  const int k = a.top_k;
+  const int row_words = (((E + 1) / 2) | 1);  // odd stride -> conflict-free column reads
+  uint16_t* tile = reinterpret_cast<uint16_t*>(route_smem);
+  uint8_t* resident = reinterpret_cast<uint8_t*>(route_smem + kRouteRows * row_words);
+  float* warp_sums = reinterpret_cast<float*>(route_smem + kRouteRows * row_words + (E + 3) / 4);
+
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kRouteRows;
+  const int nrows = static_cast<int>(min_i64(kRouteRows, a.tokens - row0));
+  const uint16_t* src = a.logits + row0 * E;
+  uint16_t* dst = a.scores + row0 * E;
+  const int total = nrows * E;
+
+  for (int c = threadIdx.x; c < E; c += blockDim.x) resident[c] = a.resident ? a.resident[c] : 1;
+
+  // Stage logits -> scores (coalesced), keep a row-strided copy in smem.
+  if ((E & 7) == 0) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+    for (int i = threadIdx.x; i < total / 8; i += blockDim.x) {
+      uint4 v = s4[i];
+      uint16_t* h = reinterpret_cast<uint16_t*>(&v);
+      const int base = i * 8;
+      const int r = base / E;
+      const int c = base - r * E;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (a.lut != nullptr) h[q] = a.lut[h[q]];
+        tile[r * 2 * row_words + c + q] = h[q];
+      }
+      d4[i] = v;
+    }
+  } else {
+    for (int i = threadIdx.x; i < total; i += blockDim.x) {
+      uint16_t v = src[i];
+      if (a.lut != nullptr) v = a.lut[v];
+      const int r = i / E;
+      tile[r * 2 * row_words + (i - r * E)] = v;
+      dst[i] = v;
+    }
+  }
+  __syncthreads();
+
+  const int r = threadIdx.x;
+  const bool live = r < nrows;
+  const uint16_t* row = tile + r * 2 * row_words;
+
+  // ---- k+1 smallest keys (packed key16 << 16 | index), ascending.
+  uint32_t best[K1MAX];
+#pragma unroll
+  for (int j = 0; j < K1MAX; ++j) best[j] = 0xFFFFFFFFu;
+  if (live) {
+    for (int c = 0; c < E; ++c) {
+      const uint16_t s = resident[c] ? row[c] : static_cast<uint16_t>(0x7F80u);
+      const uint32_t w = (order_key16(s) << 16) | static_cast<uint32_t>(c);
+      if (w < best[K1MAX - 1]) {
+        best[K1MAX - 1] = w;
+#pragma unroll
+        for (int j = K1MAX - 1; j > 0; --j) {
+          const uint32_t lo = min(best[j - 1], best[j]);
+          const uint32_t hi = max(best[j - 1], best[j]);
+          best[j - 1] = lo;
+          best[j] = hi;
+        }
+      }
+    }
+    const int k1 = min(k + 1, E);
+    bool tie = false;
+#pragma unroll
+    for (int j = 0; j + 1 < K1MAX; ++j)
+      if (j + 1 < k1 && (best[j] >> 16) == (best[j + 1] >> 16)) tie = true;
+    const int64_t grow = row0 + r;
+    if (tie) {
+      const int slot = atomicAdd(a.tie_count, 1);
+      a.tie_rows[slot] = static_cast<int>(grow);
+    } else {
+      uint16_t sel[K1MAX];
+      uint16_t wts[K1MAX];
+#pragma unroll
+      for (int j = 0; j < K1MAX; ++j) {
+        if (j < k) {
+          const int id = static_cast<int>(best[j] & 0xFFFFu);
+          a.ids[grow * k + j] = id;
+          sel[j] = row[id];
+        }
+      }
+      routing_softmax(sel, k, wts);
+#pragma unroll
+      for (int j = 0; j < K1MAX; ++j)
+        if (j < k) a.weights[grow * k + j] = wts[j];
+    }
+  }
+
+  // ---- load-balance partials: sum over this CTA's rows of
+  // bf16(softmax(-scores)) per expert (non-resident experts get 0).
+  float mx = 0.0f, denom = 1.0f;
+  if (live) {
+    const uint32_t k0 = best[0] >> 16;  // smallest eligible key
+    // decode key back to the score value
+    const uint16_t b0 = (k0 & 0x8000u) ? static_cast<uint16_t>(k0 & 0x7FFFu) : static_cast<uint16_t>(~k0);
+    mx = -bf16_to_f32(b0);
+    float s = 0.0f;
+    for (int c = 0; c < E; ++c)
+      if (resident[c]) s += expf(-bf16_to_f32(row[c]) - mx);
+    denom = s;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int g0 = 0; g0 < E; g0 += 32) {
+    float v[32];
+#pragma unroll
+    for (int q = 0; q < 32; ++q) {
+      const int c = g0 + q;
+      float p = 0.0f;
+      if (live && c < E && resident[c]) p = round_bf16(expf(-bf16_to_f32(row[c]) - mx) / denom);
+      v[q] = p;
+    }
+    // Transpose-reduce: after 5 halving steps lane l holds column g0 + l.
+#pragma unroll
+    for (int width = 16; width >= 1; width >>= 1) {
+      const bool upper = (lane & width) != 0;
+#pragma unroll
+      for (int q = 0; q < width; ++q) {
+        const float keep = upper ? v[q + width] : v[q];
+        const float send = upper ? v[q] : v[q + width];
+        v[q] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, width);
+      }
+    }
+    if (g0 + lane < E) warp_sums[warp * E + g0 + lane] = v[0];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < E; c += blockDim.x) {
+    float s = 0.0f;
+    for (int w = 0; w < kRouteRows / 32; ++w) s += warp_sums[w * E + c];
+    a.lb_partial[static_cast<int64_t>(blockIdx.x) * E + c] = s;
+  }
+}
+
+__global__ void __launch_bounds__(kTieThreads) route_ties_kernel(const RouteArgs a) {
+  extern __shared__ uint32_t tie_smem[];
+  const int E = a.num_experts;
+  const int k = a.top_k;
+  const int stride = E | 1;
+  uint32_t* v = tie_smem + threadIdx.x * stride;
+  const int n_ties = *a.tie_count;
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n_ties; t += gridDim.x * blockDim.x) {
+    const int64_t row = a.tie_rows[t];
+    const uint16_t* s = a.scores + row * E;
+    for (int c = 0; c < E; ++c) {
+      const bool res = a.resident == nullptr || a.resident[c] != 0;
+      const uint16_t b = res ? s[c] : static_cast<uint16_t>(0x7F80u);
+      v[c] = (static_cast<uint32_t>(b) << 16) | static_cast<uint32_t>(c);
+    }
+    exact::topk_least_cpu_order(v, E, k);
+    uint16_t sel[kMaxTopK];
+    uint16_t wts[kMaxTopK];
+    for (int j = 0; j < k; ++j) {
+      const int id = static_cast<int>(v[j] & 0xFFFFu);
+      a.ids[row * k + j] = id;
+      sel[j] = s[id];
+    }
+    routing_softmax(sel, k, wts);
+    for (int j = 0; j < k; ++j) a.weights[row * k + j] = wts[j];
+  }
+}
+
+int launch_softplus_table(uint16_t* lut, cudaStream_t stream) {
+  softplus_table_kernel<<<256, 256, 0, stream>>>(lut);
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+size_t route_select_smem(int E) {
+  const int row_words = (((E + 1) / 2) | 1);
+  return static_cast<size_t>(kRouteRows) * row_words * 4 + ((E + 3) / 4) * 4 +
+         static_cast<size_t>(kRouteRows / 32) * E * 4;
+}
+
+int launch_route(const RouteArgs& a, cudaStream_t stream) {
+  if (a.tokens <= 0) return SPX_OK;
+  const int blocks = static_cast<int>((a.tokens + kRouteRows - 1) / kRouteRows);
+  const size_t smem = route_select_smem(a.num_experts);
+  cudaError_t err;
+  if (a.top_k + 1 <= 5) {
+    cudaFuncSetAttribute(route_select_kernel<5>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    route_select_kernel<5><<<blocks, kRouteRows, smem, stream>>>(a);
+  } else if (a.top_k + 1 <= 9) {
+    cudaFuncSetAttribute(route_select_kernel<9>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    route_select_kernel<9><<<blocks, kRouteRows, smem, stream>>>(a);
+  } else {
+    cudaFuncSetAttribute(route_select_kernel<kMaxTopK + 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    route_select_kernel<kMaxTopK + 1><<<blocks, kRouteRows, smem, stream>>>(a);
+  }
+  err = cudaGetLastError();
+  if (err != cudaSuccess) return SPX_ERR_CUDA;
+  const size_t tsmem = static_cast<size_t>(kTieThreads) * (a.num_experts | 1) * 4;
+  cudaFuncSetAttribute(route_ties_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tsmem));
+  int tie_blocks = static_cast<int>((a.tokens + kTieThreads - 1) / kTieThreads);
+  if (tie_blocks > a.sm_count * 8) tie_blocks = a.sm_count * 8;
+  route_ties_kernel<<<tie_blocks, kTieThreads, tsmem, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+}  // namespace spx

@@ -1,0 +1,613 @@
+"""B200 drop-in for SPALMER's routed micro-expert channel mixer.
+
+``B200MicroExpertChannelMixer`` (alias ``MicroExpertChannelMixer``) has the
+constructor and ``forward`` contract of the reference module
+(mESmaC/spalmer src/spalmer/experts/mixer.py:38-241) and the same
+``state_dict`` keys and layouts, and a model built under the same
+``torch.manual_seed`` holds bit-identical weights: the parameter-holding
+submodules below create their parameters in the reference's order
+(router ``nn.Linear`` + ``normal_``, bank ``randn`` x3, shared SwiGLU
+``nn.Linear`` x3 + ``normal_``).
+
+``forward`` runs one call of ``spx_layer_forward`` (libspx, sm_100a): router
+GEMM, exact least-surprise top-k, dispatch, grouped expert SwiGLU, shared
+SwiGLU fused with the combine, routing statistics and the load-balance loss,
+with no host synchronisation.  There is no CPU or PyTorch fallback: inputs
+must be BF16 CUDA tensors and the library must be built.  The backward pass is
+not implemented yet, so ``forward`` refuses to run when autograd would need it.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Any, Mapping
+from weakref import ref
+
+import torch
+from torch import Tensor, nn
+
+from spalmer_b200 import _lib
+from spalmer_b200.config import MicroExpertsConfig, coerce_config
+
+try:  # the reference shell's output type, when the reference package is importable
+    from spalmer.modeling import ChannelMixerOutput  # type: ignore
+except Exception:  # noqa: BLE001 - optional integration
+
+    @dataclass(slots=True)
+    class ChannelMixerOutput:  # same fields as spalmer.modeling.ChannelMixerOutput (modeling.py:27-31)
+        update: Tensor
+        state: Any = None
+        auxiliary_loss: Tensor | None = None
+        metrics: Mapping[str, Any] = field(default_factory=dict)
+
+
+class NativeExpertPrecisionError(RuntimeError):
+    """The requested expert precision has no B200 kernel (experts/native.py:30)."""
+
+
+# ---------------------------------------------------------------- parameter holders
+
+
+class SurpriseRouter(nn.Module):
+    """Router parameters and score transform (experts/router.py:19-56)."""
+
+    def __init__(self, config) -> None:
+        super().__init__()
+        config = coerce_config(config)
+        self.config = config
+        self.num_experts = config.num_experts
+        self.proj = nn.Linear(config.d_model, config.num_experts, bias=config.router_bias)
+        nn.init.normal_(self.proj.weight, mean=0.0, std=config.initializer_range)
+        if self.proj.bias is not None:
+            nn.init.zeros_(self.proj.bias)
+
+    @property
+    def num_features(self) -> int:
+        return self.config.d_model
+
+    def forward(self, hidden_states: Tensor) -> Tensor:
+        """Predicted surprise ``[..., experts]`` through the B200 router GEMM."""
+
+        if hidden_states.shape[-1] != self.config.d_model:
+            raise ValueError(
+                f"expected trailing dimension {self.config.d_model}, got {hidden_states.shape[-1]}"
+            )
+        raise NotImplementedError(
+            "the standalone router forward runs inside B200MicroExpertChannelMixer.forward"
+        )
+
+
+class MicroExpertBank(nn.Module):
+    """Stacked expert projections, reference layout (experts/bank.py:37-54)."""
+
+    def __init__(self, config) -> None:
+        super().__init__()
+        config = coerce_config(config)
+        self.config = config
+        e, d, i = config.num_experts, config.d_model, config.resolved_inter_dim
+        std = config.initializer_range
+        self.gate_proj = nn.Parameter(torch.randn(e, d, i) * std)
+        self.up_proj = nn.Parameter(torch.randn(e, d, i) * std)
+        self.down_proj = nn.Parameter(torch.randn(e, i, d) * std)
+
+    @property
+    def num_experts(self) -> int:
+        return self.config.num_experts
+
+    @property
+    def parameters_per_expert(self) -> int:
+        return self.gate_proj[0].numel() + self.up_proj[0].numel() + self.down_proj[0].numel()
+
+
+class SwiGLU(nn.Module):
+    """Shared gated MLP parameters (nn/ffn.py:9-25)."""
+
+    def __init__(self, d_model: int, hidden_size: int, *, initializer_range: float | None = None):
+        super().__init__()
+        if d_model <= 0 or hidden_size <= 0:
+            raise ValueError("d_model and hidden_size must be positive")
+        self.gate_projection = nn.Linear(d_model, hidden_size, bias=False)
+        self.up_projection = nn.Linear(d_model, hidden_size, bias=False)
+        self.down_projection = nn.Linear(hidden_size, d_model, bias=False)
+        if initializer_range is not None:
+            for linear in (self.gate_projection, self.up_projection, self.down_projection):
+                nn.init.normal_(linear.weight, mean=0.0, std=initializer_range)
+
+    @property
+    def parameter_count(self) -> int:
+        return sum(p.numel() for p in self.parameters())
+
+
+class ExpertPotentiationController(nn.Module):
+    """Checkpoint-visible promotion state (experts/potentiation.py:24-47).
+
+    The B200 layer consumes ``promoted_mask``; the EMA update policy of the
+    reference controller is outside this hot path.
+    """
+
+    def __init__(self, config) -> None:
+        super().__init__()
+        config = coerce_config(config)
+        self.config = config
+        shape = (config.num_experts,)
+        self.register_buffer("utilization_ema", torch.zeros(shape, dtype=torch.float32))
+        self.register_buffer("attributed_nll_ema", torch.zeros(shape, dtype=torch.float32))
+        self.register_buffer("quantization_error_ema", torch.zeros(shape, dtype=torch.float32))
+        self.register_buffer("promoted_mask", torch.zeros(shape, dtype=torch.bool))
+        self.register_buffer("observations", torch.zeros((), dtype=torch.long))
+        self.register_buffer("last_change", torch.zeros((), dtype=torch.long))
+
+    def _apply(self, fn, recurse: bool = True):
+        super()._apply(fn, recurse)
+        for name in ("utilization_ema", "attributed_nll_ema", "quantization_error_ema"):
+            self._buffers[name] = self._buffers[name].float()
+        return self
+
+
+class ExpertResidency(nn.Module):
+    """Resident expert set shared by all layers (experts/residency.py:59-215 subset)."""
+
+    def __init__(self, config) -> None:
+        super().__init__()
+        config = coerce_config(config)
+        self.config = config
+        self._ids: tuple[int, ...] = tuple(range(config.num_experts))
+        self._active_experts_override: int | None = None
+        self.register_buffer("resident_mask", torch.ones(config.num_experts, dtype=torch.bool), persistent=False)
+        self.register_buffer(
+            "resident_ids", torch.arange(config.num_experts, dtype=torch.long), persistent=False
+        )
+
+    @property
+    def num_experts(self) -> int:
+        return self.config.num_experts
+
+    @property
+    def ids(self) -> tuple[int, ...]:
+        return self._ids
+
+    @property
+    def size(self) -> int:
+        return len(self._ids)
+
+    @property
+    def is_full(self) -> bool:
+        return len(self._ids) == self.num_experts
+
+    @property
+    def active_experts(self) -> int:
+        if self._active_experts_override is not None:
+            return self._active_experts_override
+        return self.config.active_experts
+
+    @property
+    def active_experts_override(self) -> int | None:
+        return self._active_experts_override
+
+    @property
+    def max_active_experts(self) -> int:
+        return min(self.config.max_active_experts, self.num_experts)
+
+    def set_active_experts(self, count: int | None) -> None:
+        if count is not None and not self.config.min_active_experts <= count <= self.max_active_experts:
+            raise ValueError(
+                f"active_experts must be in [{self.config.min_active_experts}, {self.max_active_experts}]; "
+                f"got {count}"
+            )
+        effective = self.config.active_experts if count is None else count
+        if effective > self.size:
+            raise ValueError(f"per-token top-{effective} cannot be served by only {self.size} resident experts")
+        self._active_experts_override = count
+
+    def set(self, ids) -> tuple[int, ...]:
+        unique = tuple(sorted({int(e) for e in ids}))
+        if not unique:
+            raise ValueError("the resident set cannot be empty")
+        if unique[0] < 0 or unique[-1] >= self.num_experts:
+            raise ValueError(f"expert ids must be in [0, {self.num_experts})")
+        if len(unique) < self.active_experts:
+            raise ValueError(f"{len(unique)} resident experts cannot serve a per-token top-{self.active_experts}")
+        if len(unique) > self.config.resident_cap and len(unique) != self.num_experts:
+            raise ValueError(f"resident set of {len(unique)} exceeds the cap {self.config.resident_cap}")
+        self._ids = unique
+        mask = torch.zeros(self.num_experts, dtype=torch.bool, device=self.resident_mask.device)
+        mask[list(unique)] = True
+        self.resident_mask.copy_(mask)
+        self.resident_ids = torch.tensor(unique, dtype=torch.long, device=self.resident_mask.device)
+        return unique
+
+
+# ---------------------------------------------------------------- device caches
+
+_SOFTPLUS: dict[torch.device, Tensor] = {}
+
+
+def softplus_table(device: torch.device) -> Tensor:
+    """The BF16 softplus table of ``device`` (computed once by a libspx kernel)."""
+
+    table = _SOFTPLUS.get(device)
+    if table is None:
+        lib = _lib.load()
+        table = torch.empty(65536, dtype=torch.int16, device=device)
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(lib.spx_softplus_table(table.data_ptr(), stream), "spx_softplus_table")
+        _SOFTPLUS[device] = table
+    return table
+
+
+def layer_dims(config: MicroExpertsConfig, tokens: int, top_k: int) -> _lib.LayerDims:
+    return _lib.LayerDims(
+        tokens=tokens,
+        d_model=config.d_model,
+        num_experts=config.num_experts,
+        inter_dim=config.resolved_inter_dim,
+        shared_dim=config.resolved_shared_inter_dim,
+        top_k=top_k,
+        score_transform=0 if config.router_score_transform == "softplus" else 1,
+        execution_loop=1 if config.expert_execution == "loop" else 0,
+    )
+
+
+def _bits(t: Tensor) -> Tensor:
+    return t.detach().contiguous()
+
+
+class B200MicroExpertChannelMixer(nn.Module):
+    """Shared SwiGLU plus routed micro-experts on B200 (experts/mixer.py:38-241)."""
+
+    def __init__(self, config, *, router: SurpriseRouter | None = None,
+                 potentiation_controller: ExpertPotentiationController | None = None,
+                 residency: ExpertResidency | None = None) -> None:
+        super().__init__()
+        config = coerce_config(config)
+        if router is not None:
+            if router.num_experts != config.num_experts:
+                raise ValueError(
+                    f"shared router serves {router.num_experts} experts; this bank has {config.num_experts}"
+                )
+            if router.num_features != config.d_model:
+                raise ValueError(
+                    f"shared router expects width {router.num_features}; this layer has {config.d_model}"
+                )
+        self.config = config
+        self.router = router if router is not None else SurpriseRouter(config)
+        self.experts = MicroExpertBank(config)
+        width = config.resolved_shared_inter_dim
+        self.shared = SwiGLU(config.d_model, width, initializer_range=config.initializer_range) if width > 0 else None
+        if potentiation_controller is None:
+            self._owned_potentiation_controller = ExpertPotentiationController(config)
+            potentiation_controller = self._owned_potentiation_controller
+        elif coerce_config(potentiation_controller.config) != config:
+            raise ValueError("potentiation controller configuration does not match this bank")
+        if residency is None:
+            self._owned_residency = ExpertResidency(config)
+            residency = self._owned_residency
+        elif coerce_config(residency.config) != config:
+            raise ValueError("residency configuration does not match this bank")
+        object.__setattr__(self, "_potentiation_controller_ref", ref(potentiation_controller))
+        object.__setattr__(self, "_residency_ref", ref(residency))
+        object.__setattr__(self, "_pack_cache", None)
+        object.__setattr__(self, "_ws_cache", {})
+        object.__setattr__(self, "_stage_event_array", None)
+
+    def record_stage_events(self, events: list | None) -> None:
+        """Record ``SPX_STAGE_EVENTS`` torch CUDA events at the kernel-stage
+        boundaries of every following forward (``None`` switches it off)."""
+
+        if events is None:
+            object.__setattr__(self, "_stage_event_array", None)
+            return
+        if len(events) != _lib.STAGE_EVENTS:
+            raise ValueError(f"need {_lib.STAGE_EVENTS} events")
+        handles = []
+        for ev in events:
+            if ev.cuda_event == 0:  # torch creates the event lazily on first record
+                ev.record()
+            handles.append(ev.cuda_event)
+        array = (_lib.ctypes.c_void_p * len(handles))(*handles)
+        object.__setattr__(self, "_stage_event_array", array)
+
+    # ---- reference-compatible properties
+    @property
+    def potentiation_controller(self) -> ExpertPotentiationController:
+        controller = self._potentiation_controller_ref()
+        if controller is None:
+            raise RuntimeError("the shared potentiation controller no longer exists")
+        return controller
+
+    @property
+    def residency(self) -> ExpertResidency:
+        residency = self._residency_ref()
+        if residency is None:
+            raise RuntimeError("the shared expert residency no longer exists")
+        return residency
+
+    @property
+    def active_experts(self) -> int:
+        return self.residency.active_experts
+
+    @property
+    def active_experts_override(self) -> int | None:
+        return self.residency.active_experts_override
+
+    @property
+    def max_active_experts(self) -> int:
+        return self.residency.max_active_experts
+
+    def set_active_experts(self, count: int | None) -> None:
+        self.residency.set_active_experts(count)
+
+    @property
+    def has_shared_path(self) -> bool:
+        return self.shared is not None
+
+    # ---- derived caches
+    def _weight_tensors(self) -> dict[str, Tensor | None]:
+        s = self.shared
+        return {
+            "router_weight": self.router.proj.weight,
+            "router_bias": self.router.proj.bias,
+            "gate_proj": self.experts.gate_proj,
+            "up_proj": self.experts.up_proj,
+            "down_proj": self.experts.down_proj,
+            "shared_gate": None if s is None else s.gate_projection.weight,
+            "shared_up": None if s is None else s.up_projection.weight,
+            "shared_down": None if s is None else s.down_projection.weight,
+        }
+
+    def _packed(self, device: torch.device, tokens: int, top_k: int) -> dict[str, Tensor | None]:
+        tensors = self._weight_tensors()
+        key = (device,) + tuple(
+            (None if t is None else (t.data_ptr(), t._version, t.dtype)) for t in tensors.values()
+        )
+        cache = self._pack_cache
+        if cache is not None and cache[0] == key:
+            return cache[1]
+        for name, t in tensors.items():
+            if t is None:
+                continue
+            if t.device != device:
+                raise RuntimeError(f"parameter {name} is on {t.device}, hidden states on {device}")
+            if t.dtype != torch.bfloat16:
+                raise RuntimeError(
+                    f"the B200 layer executes BF16 weights; {name} is {t.dtype} (cast the module with .to(torch.bfloat16))"
+                )
+        lib = _lib.load()
+        dims = layer_dims(self.config, tokens, top_k)
+        sizes = _lib.PackedSizes()
+        _lib.check(lib.spx_layer_sizes(dims, None, sizes), "spx_layer_sizes")
+        bits = {n: (None if t is None else _bits(t)) for n, t in tensors.items()}
+        empty = lambda n: torch.empty(max(1, n), dtype=torch.int16, device=device)  # noqa: E731
+        packed = {
+            "router_weight": empty(sizes.router_weight),
+            "expert_w1": empty(sizes.expert_w1),
+            "expert_w2": empty(sizes.expert_w2),
+            "shared_w1": empty(sizes.shared_w1) if sizes.shared_w1 else None,
+            "shared_w2": empty(sizes.shared_w2) if sizes.shared_w2 else None,
+            "router_bias": bits["router_bias"],
+        }
+        src = _lib.ReferenceWeights(*(_lib.ptr(bits[n]) for n in (
+            "router_weight", "router_bias", "gate_proj", "up_proj", "down_proj",
+            "shared_gate", "shared_up", "shared_down")))
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(
+            lib.spx_pack_weights(
+                dims, src, _lib.ptr(packed["router_weight"]), _lib.ptr(packed["expert_w1"]),
+                _lib.ptr(packed["expert_w2"]), _lib.ptr(packed["shared_w1"]), _lib.ptr(packed["shared_w2"]),
+                stream,
+            ),
+            "spx_pack_weights",
+        )
+        packed["_keepalive"] = bits
+        object.__setattr__(self, "_pack_cache", (key, packed))
+        return packed
+
+    def _workspace(self, device: torch.device, dims: _lib.LayerDims) -> Tensor:
+        lib = _lib.load()
+        nbytes = _lib.ctypes.c_size_t()
+        _lib.check(lib.spx_layer_sizes(dims, nbytes, None), "spx_layer_sizes")
+        key = (device, nbytes.value)
+        ws = self._ws_cache.get(key)
+        if ws is None:
+            self._ws_cache.clear()
+            ws = torch.zeros(nbytes.value, dtype=torch.uint8, device=device)
+            self._ws_cache[key] = ws
+        return ws
+
+    def device_status(self, clear: bool = True) -> int:
+        """Device status word of the last workspace (synchronises); 0 means no kernel error."""
+
+        lib = _lib.load()
+        for (device, _), ws in self._ws_cache.items():
+            value = _lib.ctypes.c_int(0)
+            stream = torch.cuda.current_stream(device).cuda_stream
+            _lib.check(lib.spx_workspace_status(ws.data_ptr(), value, int(clear), stream), "spx_workspace_status")
+            return value.value
+        return 0
+
+    # ---- forward
+    def forward(self, hidden_states: Tensor, *, state: Any = None,
+                router_logits: Tensor | None = None) -> ChannelMixerOutput:
+        """Run the layer; see ``experts/mixer.py:145-241`` for the contract.
+
+        ``router_logits`` (optional, ``[batch, seq, experts]`` BF16) replaces
+        the router GEMM output; it exists to check the routing contract
+        "bit-exact given identical logits".
+        """
+
+        if hidden_states.ndim != 3:
+            raise ValueError(
+                f"hidden_states must have shape [batch, seq, d_model]; got {tuple(hidden_states.shape)}"
+            )
+        config = self.config
+        if hidden_states.shape[-1] != config.d_model:
+            raise ValueError(f"expected trailing dimension {config.d_model}; got {hidden_states.shape[-1]}")
+        if torch.is_grad_enabled() and (
+            hidden_states.requires_grad or any(p.requires_grad for p in self.parameters())
+        ):
+            raise NotImplementedError(
+                "the B200 micro-expert layer implements the forward pass only; call it under "
+                "torch.no_grad() or torch.inference_mode()"
+            )
+        if not hidden_states.is_cuda:
+            raise RuntimeError("the B200 micro-expert layer requires CUDA hidden states")
+        if hidden_states.dtype != torch.bfloat16:
+            raise RuntimeError(
+                f"bfloat16/bfloat16 expert execution requires torch.bfloat16 hidden states, got {hidden_states.dtype}"
+            )
+        if config.expert_weight_format != "bfloat16":
+            raise NativeExpertPrecisionError(
+                f"no B200 kernel for {config.expert_weight_format}/{config.expert_activation_format} experts yet"
+            )
+        batch, seq_len, d_model = hidden_states.shape
+        tokens = batch * seq_len
+        k = self.active_experts
+        residency = self.residency
+        full_pool = residency.is_full
+        if not full_pool and residency.size < k:
+            raise ValueError(f"{residency.size} resident experts cannot serve a per-token top-{k}")
+        device = hidden_states.device
+        E = config.num_experts
+        lib = _lib.load()
+        dims = layer_dims(config, tokens, k)
+        packed = self._packed(device, tokens, k)
+        ws = self._workspace(device, dims)
+        x = hidden_states.reshape(tokens, d_model).contiguous()
+        update = torch.empty(batch, seq_len, d_model, dtype=torch.bfloat16, device=device)
+        scores = torch.empty(batch, seq_len, E, dtype=torch.bfloat16, device=device)
+        ids = torch.empty(batch, seq_len, k, dtype=torch.long, device=device)
+        weights = torch.empty(batch, seq_len, k, dtype=torch.bfloat16, device=device)
+        util = torch.empty(E, dtype=torch.float32, device=device)
+        stats = torch.empty(6, dtype=torch.long, device=device)
+        ratios = torch.empty(2, dtype=torch.float32, device=device)
+        aux = torch.empty(1, dtype=torch.bfloat16, device=device)
+        injected = None
+        if router_logits is not None:
+            if router_logits.shape != (batch, seq_len, E) or router_logits.dtype != torch.bfloat16:
+                raise ValueError("router_logits must be [batch, seq, experts] bfloat16")
+            injected = router_logits.contiguous()
+        mask = None if full_pool else residency.resident_mask.to(device=device).contiguous()
+        lut = softplus_table(device) if config.router_score_transform == "softplus" else None
+        pw = _lib.PackedWeights(
+            router_weight=_lib.ptr(packed["router_weight"]),
+            router_bias=_lib.ptr(packed["router_bias"]),
+            expert_w1=_lib.ptr(packed["expert_w1"]),
+            expert_w2=_lib.ptr(packed["expert_w2"]),
+            shared_w1=_lib.ptr(packed["shared_w1"]),
+            shared_w2=_lib.ptr(packed["shared_w2"]),
+            softplus_table=_lib.ptr(lut),
+            resident_mask=_lib.ptr(mask),
+        )
+        events = self._stage_event_array
+        outs = _lib.LayerOutputs(
+            update=update.data_ptr(), router_scores=scores.data_ptr(), expert_ids=ids.data_ptr(),
+            routing_weights=weights.data_ptr(), expert_utilization=util.data_ptr(),
+            group_stats=stats.data_ptr(), group_ratios=ratios.data_ptr(), auxiliary_loss=aux.data_ptr(),
+            dispatch_order=None, expert_counts=None, injected_logits=_lib.ptr(injected), router_logits=None,
+            stage_events=None if events is None else _lib.ctypes.addressof(events),
+        )
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(lib.spx_layer_forward(dims, pw, x.data_ptr(), outs, ws.data_ptr(), stream), "spx_layer_forward")
+        controller = self.potentiation_controller
+        metrics: dict[str, Any] = {
+            "expert_ids": ids,
+            "routing_weights": weights,
+            "router_scores": scores,
+            "expert_utilization": util,
+            "expert_quantization_error": torch.zeros(E, dtype=torch.float32, device=device),
+            "promoted_experts": controller.promoted_mask.detach().clone(),
+            "resident_experts": residency.resident_mask.detach().clone(),
+            "expert_paging": False,
+            "routing_full_pool": full_pool,
+            "active_experts_per_token": k,
+            "num_active_experts": stats[5],
+            "expert_execution": config.expert_execution,
+            "expert_group_count": stats[0],
+            "expert_group_max_load": stats[1],
+            "expert_group_real_pairs": stats[2],
+            "expert_group_padded_pairs": stats[3],
+            "expert_group_padding_amplification": ratios[0],
+            "expert_group_global_max_counterfactual_padded_pairs": stats[4],
+            "expert_group_global_max_counterfactual_padding_amplification": ratios[1],
+        }
+        return ChannelMixerOutput(update=update, state=None, auxiliary_loss=aux[0], metrics=metrics)
+
+
+MicroExpertChannelMixer = B200MicroExpertChannelMixer
+
+
+def route(logits: Tensor, top_k: int, *, transform: str = "softplus",
+          resident_mask: Tensor | None = None) -> tuple[Tensor, Tensor, Tensor]:
+    """Scores, top-k ids and weights from BF16 logits ``[T, E]`` (spx_route).
+
+    Restates ``SurpriseRouter`` score transform + ``select_least_surprised_experts``
+    (experts/router.py:52-95) given logits.
+    """
+
+    if logits.ndim != 2 or logits.dtype != torch.bfloat16 or not logits.is_cuda:
+        raise ValueError("logits must be a [T, E] bfloat16 CUDA tensor")
+    T, E = logits.shape
+    lib = _lib.load()
+    device = logits.device
+    dims = _lib.LayerDims(tokens=T, d_model=64, num_experts=E, inter_dim=16, shared_dim=0, top_k=top_k,
+                          score_transform=0 if transform == "softplus" else 1, execution_loop=0)
+    nbytes = _lib.ctypes.c_size_t()
+    _lib.check(lib.spx_layer_sizes(dims, nbytes, None), "spx_layer_sizes")
+    ws = torch.zeros(nbytes.value, dtype=torch.uint8, device=device)
+    scores = torch.empty(T, E, dtype=torch.bfloat16, device=device)
+    ids = torch.empty(T, top_k, dtype=torch.long, device=device)
+    weights = torch.empty(T, top_k, dtype=torch.bfloat16, device=device)
+    lut = softplus_table(device) if transform == "softplus" else None
+    mask = None if resident_mask is None else resident_mask.to(device=device, dtype=torch.bool).contiguous()
+    stream = torch.cuda.current_stream(device).cuda_stream
+    _lib.check(
+        lib.spx_route(dims, logits.contiguous().data_ptr(), _lib.ptr(lut), _lib.ptr(mask), scores.data_ptr(),
+                      ids.data_ptr(), weights.data_ptr(), ws.data_ptr(), stream),
+        "spx_route",
+    )
+    return scores, ids, weights
+
+
+def dispatch(expert_ids: Tensor, num_experts: int) -> tuple[Tensor, Tensor]:
+    """Stable permutation of pairs by expert and per-expert counts (spx_dispatch).
+
+    Restates ``argsort(expert_index, stable=True)`` and ``_pair_counts``
+    (experts/bank.py:721-723, 981-985).
+    """
+
+    if expert_ids.ndim != 2 or expert_ids.dtype != torch.long or not expert_ids.is_cuda:
+        raise ValueError("expert_ids must be a [T, k] int64 CUDA tensor")
+    T, k = expert_ids.shape
+    lib = _lib.load()
+    device = expert_ids.device
+    dims = _lib.LayerDims(tokens=T, d_model=64, num_experts=num_experts, inter_dim=16, shared_dim=0,
+                          top_k=k, score_transform=1, execution_loop=0)
+    nbytes = _lib.ctypes.c_size_t()
+    _lib.check(lib.spx_layer_sizes(dims, nbytes, None), "spx_layer_sizes")
+    ws = torch.zeros(nbytes.value, dtype=torch.uint8, device=device)
+    order = torch.empty(T * k, dtype=torch.int32, device=device)
+    counts = torch.empty(num_experts, dtype=torch.int32, device=device)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    _lib.check(
+        lib.spx_dispatch(dims, expert_ids.contiguous().data_ptr(), order.data_ptr(), counts.data_ptr(),
+                         ws.data_ptr(), stream),
+        "spx_dispatch",
+    )
+    return order, counts
+
+
+__all__ = [
+    "B200MicroExpertChannelMixer",
+    "ChannelMixerOutput",
+    "ExpertPotentiationController",
+    "ExpertResidency",
+    "MicroExpertBank",
+    "MicroExpertChannelMixer",
+    "MicroExpertsConfig",
+    "NativeExpertPrecisionError",
+    "SurpriseRouter",
+    "SwiGLU",
+    "dispatch",
+    "route",
+    "softplus_table",
+]
