@@ -124,9 +124,9 @@ def load_balance_loss(score_bits: np.ndarray, expert_ids: np.ndarray,
     mean_p = round_bf16((prob.astype(np.float64).sum(axis=0) / prob.shape[0]).astype(np.float32))
     frac = round_bf16(expert_utilization(expert_ids, n))
     prod = round_bf16(frac * mean_p)
-    total = round_bf16(np.float32(prod.astype(np.float64).sum()))
-    elig = round_bf16(np.float32(eligible))
-    return float(round_bf16(np.float32(elig * total)))
+    total = round_bf16(np.array([prod.astype(np.float64).sum()], dtype=np.float32))[0]
+    elig = round_bf16(np.array([eligible], dtype=np.float32))[0]
+    return float(round_bf16(np.array([elig * total], dtype=np.float32))[0])
 
 
 def pair_counts(expert_index: np.ndarray, num_experts: int) -> np.ndarray:
