@@ -42,6 +42,7 @@ extern "C" {
 #define SPX_ERR_ALIGNMENT -6
 #define SPX_ERR_WORKSPACE -7
 #define SPX_ERR_DEVICE -8
+#define SPX_ERR_SCRATCH_LIMIT -9 /* problem larger than spx_dispatch_static's fixed scratch */
 
 /* Shape of one mixer layer (MicroExpertsConfig resolved values, experts/config.py:86-110,231-244). */
 typedef struct spx_layer_dims {
@@ -141,6 +142,21 @@ int spx_dispatch(const spx_layer_dims* dims, const int64_t* expert_ids, int32_t*
 int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* weights,
                       const uint16_t* hidden, const spx_layer_outputs* outputs, void* workspace,
                       void* stream);
+
+/* spx_dispatch without a workspace: same outputs, no device allocation by
+ * anyone.  No counterpart in the reference; it exists for callers that cannot
+ * allocate device memory (an FFI client holding only the buffers it was
+ * handed, or code where cudaMalloc is forbidden or would synchronise, such as
+ * global-mode stream capture).  Scratch is one file-scope device array of
+ * about 6.2 MiB that every GPU loading libspx keeps until exit.  Limits:
+ * tokens * top_k <= 1048576 and num_experts <= 1024, else
+ * SPX_ERR_SCRATCH_LIMIT.  The first call on a device (with it current) looks
+ * up the array's device address; make it before any stream capture.  Calls
+ * share the array: calls that overlap on the GPU race, so serialise them.
+ * Expert ids outside [0, num_experts) are skipped and their order slots are
+ * left unwritten. */
+int spx_dispatch_static(const spx_layer_dims* dims, const int64_t* expert_ids, int32_t* order,
+                        int32_t* counts, void* stream);
 
 /* Read (and clear when `clear` != 0) the device status word of a workspace.
  * Synchronises `stream`.  *device_status == 0 means no kernel reported an error. */

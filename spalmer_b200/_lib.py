@@ -22,6 +22,7 @@ STATUS_NAMES = {
     -6: "SPX_ERR_ALIGNMENT",
     -7: "SPX_ERR_WORKSPACE",
     -8: "SPX_ERR_DEVICE",
+    -9: "SPX_ERR_SCRATCH_LIMIT",
 }
 
 # Every function exported by include/spx.h (checked by tests/test_abi_symbols.py).
@@ -35,6 +36,7 @@ EXPORTED = (
     "spx_dispatch",
     "spx_layer_forward",
     "spx_workspace_status",
+    "spx_dispatch_static",
 )
 
 _vp = ctypes.c_void_p
@@ -147,6 +149,7 @@ def load() -> ctypes.CDLL:
             [P(LayerDims), P(PackedWeights), _vp, P(LayerOutputs), _vp, _vp],
         ),
         "spx_workspace_status": (ctypes.c_int, [_vp, P(ctypes.c_int), ctypes.c_int, _vp]),
+        "spx_dispatch_static": (ctypes.c_int, [P(LayerDims), _vp, _vp, _vp, _vp]),
     }
     for name, (restype, argtypes) in sig.items():
         fn = getattr(lib, name)

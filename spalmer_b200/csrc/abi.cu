@@ -201,6 +201,9 @@ const char* spx_status_string(int status) {
       return "workspace missing or too small";
     case SPX_ERR_DEVICE:
       return "a kernel reported an error in the workspace status word";
+    case SPX_ERR_SCRATCH_LIMIT:
+      return "problem exceeds the fixed scratch of spx_dispatch_static "
+             "(tokens * top_k <= 1048576, num_experts <= 1024)";
     default:
       return "unknown status";
   }
