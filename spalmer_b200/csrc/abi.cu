@@ -108,11 +108,7 @@ T* at(void* ws, size_t off) {
   return reinterpret_cast<T*>(static_cast<uint8_t*>(ws) + off);
 }
 
-int sm_count() {
-  int dev = 0, n = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n;
-}
+int sm_count() { return device_sm_count(); }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -40,8 +40,9 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_count_kernel(const 
     atomicAdd(&hist[e], 1);
   }
   __syncthreads();
+  // Expert-major layout [E][nchunks]: the scan reads each expert's chunks contiguously.
   for (int e = threadIdx.x; e < E; e += blockDim.x)
-    a.chunk_hist[static_cast<int64_t>(blockIdx.x) * E + e] = hist[e];
+    a.chunk_hist[static_cast<int64_t>(e) * gridDim.x + blockIdx.x] = hist[e];
 }
 
 __device__ __forceinline__ int64_t next_pow2_i64(int64_t n) {
@@ -54,20 +55,36 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs 
   __shared__ int s_scan[1024];
   __shared__ float s_red[1024];
   __shared__ long long s_i64[4];
+  __shared__ int s_count[1024];
   const int E = a.num_experts;
   const int nchunks = static_cast<int>((a.pairs + kDispatchChunk - 1) / kDispatchChunk);
   const int e = threadIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // Exclusive scan over chunks for each expert (chunk offsets within expert).
-  int count = 0;
-  if (e < E) {
-    for (int c = 0; c < nchunks; ++c) {
-      int* slot = a.chunk_hist + static_cast<int64_t>(c) * E + e;
-      const int v = *slot;
-      *slot = count;
-      count += v;
+  // Exclusive scan over chunks for each expert (chunk offsets within the
+  // expert), one warp per expert: each lane owns a contiguous run of chunks.
+  const int seg = (nchunks + 31) / 32;
+  for (int x = warp; x < E; x += 32) {
+    int* row = a.chunk_hist + static_cast<int64_t>(x) * nchunks;
+    const int c0 = min(nchunks, lane * seg), c1 = min(nchunks, c0 + seg);
+    int sum = 0;
+    for (int c = c0; c < c1; ++c) sum += row[c];
+    int incl = sum;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(0xFFFFFFFFu, incl, off);
+      if (lane >= off) incl += v;
     }
+    int run = incl - sum;
+    for (int c = c0; c < c1; ++c) {
+      const int v = row[c];
+      row[c] = run;
+      run += v;
+    }
+    if (lane == 31) s_count[x] = incl;
   }
+  __syncthreads();
+  const int count = (e < E) ? s_count[e] : 0;
   // Block-wide exclusive scans: pair starts and tile starts.
   const int tiles = (count + kTileRows - 1) / kTileRows;
   s_scan[threadIdx.x] = (e < E) ? count : 0;
@@ -171,7 +188,7 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_scatter_kernel(cons
   __syncthreads();
   // Per expert: global base = start + chunk offset, then exclusive over warps.
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    int base = a.starts[e] + a.chunk_hist[static_cast<int64_t>(blockIdx.x) * E + e];
+    int base = a.starts[e] + a.chunk_hist[static_cast<int64_t>(e) * gridDim.x + blockIdx.x];
     for (int w = 0; w < kDispatchWarps; ++w) {
       const int c = warp_base[w * E + e];
       warp_base[w * E + e] = base;

@@ -65,7 +65,7 @@ __device__ __forceinline__ void load_bf16x16_f32(const uint16_t* src, float (&f)
 
 template <int EPI>
 __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, int r, int row0, int rows,
-                                             int n0) {
+                                             int n0, int nt) {
   const bool live = r < rows;
   const int bn = a.bn;
   if constexpr (EPI == kEpiStore) {
@@ -90,7 +90,7 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
   } else if constexpr (EPI == kEpiSwiglu) {
     uint16_t* out = static_cast<uint16_t*>(a.out);
     const int c_half = a.chunk;
-    const int col0 = blockIdx.y * c_half;
+    const int col0 = nt * c_half;
     for (int c = 0; c < c_half; c += 16) {
       uint32_t g[16], u[16];
       tmem_ld16(taddr + c, g);
@@ -109,9 +109,9 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
       }
     }
     // Zero the K padding of the hidden matrix (columns [chunks*c, h_cols)).
-    if (live && blockIdx.y == gridDim.y - 1) {
+    if (live && nt == a.n_tiles - 1) {
       uint16_t* dst = out + static_cast<int64_t>(row0 + r) * a.ldo;
-      for (int col = gridDim.y * c_half; col < a.h_cols; ++col) dst[col] = 0;
+      for (int col = a.n_tiles * c_half; col < a.h_cols; ++col) dst[col] = 0;
     }
   } else if constexpr (EPI == kEpiScatter) {
     uint16_t* out = static_cast<uint16_t*>(a.out);
@@ -164,6 +164,28 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
 
 }  // namespace
 
+// Tile coordinates of linear tile `t` (N tiles fastest, so consecutive tiles
+// of one CTA share A rows in L2).  Returns false for a malformed table entry.
+__device__ __forceinline__ bool decode_tile(const GemmArgs& a, int t, int& group, int& row0, int& rows, int& nt) {
+  const int mt = t / a.n_tiles;
+  nt = t - mt * a.n_tiles;
+  if (a.tiles != nullptr) {
+    const int4 e = a.tiles[mt];
+    group = e.x;
+    row0 = e.y;
+    rows = e.z;
+    return rows > 0 && rows <= kTileRows && group >= 0 && group < a.groups;
+  }
+  group = 0;
+  row0 = mt * kTileRows;
+  rows = min(kTileRows, a.m_rows - row0);
+  return rows > 0;
+}
+
+// Persistent GEMM: each CTA walks tiles blockIdx.x, blockIdx.x + gridDim.x, ...
+// The TMA producer and the MMA issuer stream k-blocks through the stage ring
+// without stopping at tile boundaries; the accumulator is double-buffered in
+// TMEM so the epilogue of one tile overlaps the MMAs of the next.
 template <int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ GemmArgs a) {
   extern __shared__ uint8_t gemm_smem_raw[];
@@ -176,42 +198,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   uint8_t* sb = smem + S * a_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(sb + S * b_bytes);
   uint64_t* empty = full + S;
-  uint64_t* accum = empty + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* tfull = empty + S;   // [2] accumulator ready
+  uint64_t* tempty = tfull + 2;  // [2] accumulator drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  int group = 0, row0, rows;
-  if (a.tiles != nullptr) {
-    if (static_cast<int>(blockIdx.x) >= *a.num_tiles) return;
-    const int4 t = a.tiles[blockIdx.x];
-    group = t.x;
-    row0 = t.y;
-    rows = t.z;
-    if (rows <= 0 || rows > kTileRows || group < 0 || group >= a.groups) {
-      if (threadIdx.x == 0) record_error(a.status, SPX_DEV_BAD_TILE);
-      return;
-    }
-  } else {
-    row0 = blockIdx.x * kTileRows;
-    rows = min(kTileRows, a.m_rows - row0);
-    if (rows <= 0) return;
-  }
-  const int n0 = blockIdx.y * bn;
+  const int m_tiles = a.tiles != nullptr ? *a.num_tiles : (a.m_rows + kTileRows - 1) / kTileRows;
+  const int total = m_tiles * a.n_tiles;
+  if (static_cast<int>(blockIdx.x) >= total) return;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kGemmEpilogueWarps);
+    }
     fence_mbar_init();
     prefetch_tensormap(&a.tma_a);
     prefetch_tensormap(&a.tma_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, a.tmem_cols);
+    tmem_alloc(tmem_slot, 2 * a.tmem_cols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -221,70 +232,105 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
 
   if (warp == 0) {
     // ---------------- TMA producer
-    int gi0 = 0, gi1 = 0, gi2 = 0, gi3 = 0;
-    if (a.gather) {
-      const int r = lane * 4;
-      gi0 = a.gather_idx[row0 + (r + 0 < rows ? r + 0 : 0)];
-      gi1 = a.gather_idx[row0 + (r + 1 < rows ? r + 1 : 0)];
-      gi2 = a.gather_idx[row0 + (r + 2 < rows ? r + 2 : 0)];
-      gi3 = a.gather_idx[row0 + (r + 3 < rows ? r + 3 : 0)];
-    }
-    for (int kb = 0; kb < a.k_blocks; ++kb) {
-      const int s = kb % S;
-      const uint32_t ph = static_cast<uint32_t>(kb / S) & 1u;
-      int ok = 1;
-      if (lane == 0) {
-        ok = mbar_wait(&empty[s], ph ^ 1u, a.status, SPX_DEV_TIMEOUT_PRODUCER) ? 1 : 0;
-        if (ok) mbar_arrive_expect_tx(&full[s], a_bytes + b_bytes);
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+      int group, row0, rows, nt;
+      if (!decode_tile(a, t, group, row0, rows, nt)) {
+        if (lane == 0) record_error(a.status, SPX_DEV_BAD_TILE);
+        break;
       }
-      ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-      if (!ok) break;
+      int gi0 = 0, gi1 = 0, gi2 = 0, gi3 = 0;
       if (a.gather) {
-        tma_gather4(sa + s * a_bytes + lane * 512, &a.tma_a, &full[s], kb * 64, gi0, gi1, gi2, gi3);
-      } else if (lane == 0) {
-        tma_load_2d(sa + s * a_bytes, &a.tma_a, &full[s], kb * 64, row0);
+        const int r = lane * 4;
+        gi0 = a.gather_idx[row0 + (r + 0 < rows ? r + 0 : 0)];
+        gi1 = a.gather_idx[row0 + (r + 1 < rows ? r + 1 : 0)];
+        gi2 = a.gather_idx[row0 + (r + 2 < rows ? r + 2 : 0)];
+        gi3 = a.gather_idx[row0 + (r + 3 < rows ? r + 3 : 0)];
       }
-      if (lane == 0) tma_load_3d(sb + s * b_bytes, &a.tma_b, &full[s], kb * 64, n0, group);
-      __syncwarp();
+      const int n0 = nt * bn;
+      for (int kb = 0; kb < a.k_blocks; ++kb, ++it) {
+        const int s = static_cast<int>(it % S);
+        const uint32_t ph = (it / S) & 1u;
+        int go = 1;
+        if (lane == 0) {
+          go = mbar_wait(&empty[s], ph ^ 1u, a.status, SPX_DEV_TIMEOUT_PRODUCER) ? 1 : 0;
+          if (go) mbar_arrive_expect_tx(&full[s], a_bytes + b_bytes);
+        }
+        go = __shfl_sync(0xFFFFFFFFu, go, 0);
+        if (!go) {
+          ok = false;
+          break;
+        }
+        if (a.gather) {
+          tma_gather4(sa + s * a_bytes + lane * 512, &a.tma_a, &full[s], kb * 64, gi0, gi1, gi2, gi3);
+        } else if (lane == 0) {
+          tma_load_2d(sa + s * a_bytes, &a.tma_a, &full[s], kb * 64, row0);
+        }
+        if (lane == 0) tma_load_3d(sb + s * b_bytes, &a.tma_b, &full[s], kb * 64, n0, group);
+        __syncwarp();
+      }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(kTileRows, bn);
-      for (int kb = 0; kb < a.k_blocks; ++kb) {
-        const int s = kb % S;
-        const uint32_t ph = static_cast<uint32_t>(kb / S) & 1u;
-        if (!mbar_wait(&full[s], ph, a.status, SPX_DEV_TIMEOUT_MMA)) break;
+      uint32_t it = 0, lt = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++lt) {
+        const uint32_t b = lt & 1u;
+        const uint32_t tph = (lt >> 1) & 1u;
+        if (!mbar_wait(&tempty[b], tph ^ 1u, a.status, SPX_DEV_TIMEOUT_MMA)) break;
         tc_fence_after();
-        const uint32_t a_base = smem_u32(sa + s * a_bytes);
-        const uint32_t b_base = smem_u32(sb + s * b_bytes);
+        const uint32_t acc = tmem + b * a.tmem_cols;
+        for (int kb = 0; kb < a.k_blocks; ++kb, ++it) {
+          const int s = static_cast<int>(it % S);
+          const uint32_t ph = (it / S) & 1u;
+          if (!mbar_wait(&full[s], ph, a.status, SPX_DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sa + s * a_bytes);
+          const uint32_t b_base = smem_u32(sb + s * b_bytes);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          mma_bf16_ss(tmem, desc_kmajor_sw128(a_base + kk * 32), desc_kmajor_sw128(b_base + kk * 32), idesc,
-                      (kb | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) {
+            mma_bf16_ss(acc, desc_kmajor_sw128(a_base + kk * 32), desc_kmajor_sw128(b_base + kk * 32), idesc,
+                        (kb | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[s]);
         }
-        mma_commit(&empty[s]);
+        mma_commit(&tfull[b]);
       }
-      mma_commit(accum);
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue (warps 2..5)
+    // ---------------- epilogue (warps 2..5): warp w drains TMEM lanes 32*(w%4) .. +31
     const int quad = warp & 3;
-    int ok = 1;
-    if (lane == 0) ok = mbar_wait(accum, 0, a.status, SPX_DEV_TIMEOUT_EPILOGUE) ? 1 : 0;
-    ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-    tc_fence_after();
-    if (ok) {
-      const int r = quad * 32 + lane;
-      run_epilogue<EPI>(a, tmem + (static_cast<uint32_t>(quad * 32) << 16), r, row0, rows, n0);
+    const int r = quad * 32 + lane;
+    uint32_t lt = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++lt) {
+      int group, row0, rows, nt;
+      if (!decode_tile(a, t, group, row0, rows, nt)) break;
+      const uint32_t b = lt & 1u;
+      const uint32_t tph = (lt >> 1) & 1u;
+      int go = 1;
+      if (lane == 0) go = mbar_wait(&tfull[b], tph, a.status, SPX_DEV_TIMEOUT_EPILOGUE) ? 1 : 0;
+      go = __shfl_sync(0xFFFFFFFFu, go, 0);
+      if (!go) break;
+      tc_fence_after();
+      run_epilogue<EPI>(a, tmem + b * a.tmem_cols + (static_cast<uint32_t>(quad * 32) << 16), r, row0, rows,
+                        nt * bn, nt);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, a.tmem_cols);
+    tmem_dealloc(tmem, 2 * a.tmem_cols);
   }
 }
 
@@ -338,25 +384,30 @@ int encode_3d(CUtensorMap* map, const void* base, int64_t groups, int64_t rows, 
 
 size_t gemm_smem_bytes(int bn, int stages) {
   return 1024 + static_cast<size_t>(stages) * (kTileRows * 128 + static_cast<size_t>(bn) * 128) +
-         (2 * stages + 1) * 8 + 16;
+         (2 * stages + 4) * 8 + 16;
 }
 
+// As many stages as fit: the persistent producer keeps prefetching the next
+// tile's k-blocks, so stages beyond one tile's K still hide load latency.
 int gemm_pick_stages(int bn, int k_blocks) {
-  int stages = 1;
-  for (int s = 2; s <= 8; ++s)
+  (void)k_blocks;
+  int stages = 2;
+  for (int s = 3; s <= 8; ++s)
     if (gemm_smem_bytes(bn, s) <= kGemmSmemBudget) stages = s;
-  if (k_blocks >= 1 && stages > k_blocks) stages = k_blocks < 2 ? 2 : k_blocks;
   return stages;
 }
 
 template <int EPI>
 static int launch_gemm_t(const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream) {
   const size_t smem = gemm_smem_bytes(a.bn, a.stages);
-  cudaError_t e = cudaFuncSetAttribute(gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
-  if (e != cudaSuccess) return SPX_ERR_CUDA;
-  dim3 grid(grid_m, grid_n);
-  gemm_kernel<EPI><<<grid, kGemmThreads, smem, stream>>>(a);
+  if (int rc = ensure_max_dynamic_smem(reinterpret_cast<const void*>(gemm_kernel<EPI>)); rc != SPX_OK) return rc;
+  // Persistent grid: one CTA per SM, never more CTAs than (upper bound of) tiles.
+  const int sms = device_sm_count();
+  const int64_t tiles = static_cast<int64_t>(grid_m) * grid_n;
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  GemmArgs b = a;
+  b.n_tiles = grid_n;
+  gemm_kernel<EPI><<<grid, kGemmThreads, smem, stream>>>(b);
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 

@@ -11,6 +11,7 @@ namespace spx {
 
 constexpr int kTileRows = 128;         // M of every tcgen05 tile (cta_group::1)
 constexpr int kGemmThreads = 192;      // 6 warps: TMA, MMA, 4 x epilogue
+constexpr int kGemmEpilogueWarps = 4;
 constexpr size_t kGemmSmemBudget = 200 * 1024;
 constexpr int kRouteRows = 128;        // token rows per route_select CTA
 constexpr int kTieThreads = 64;        // rows replayed per route_ties CTA
@@ -71,7 +72,8 @@ struct GemmArgs {
   int k_blocks;              // K / 64
   int bn;                    // N per tile: multiple of 16, 16..256
   int stages;
-  uint32_t tmem_cols;        // power of two >= max(32, bn)
+  uint32_t tmem_cols;        // per accumulator buffer: power of two >= max(32, bn); two buffers
+  int n_tiles;               // N tiles per M tile (set by launch_gemm)
   int groups;                // B groups (bounds check of the tile table)
   int gather;                // 1: A rows gathered through gather_idx
   const int* gather_idx;
@@ -90,6 +92,12 @@ struct GemmArgs {
   int top_k;
   int* status;
 };
+
+// Host helpers (launch.cu): per-device caches so the hot path issues no
+// attribute or device queries after the first call on a device.
+int device_sm_count();
+// Raise `func`'s dynamic shared memory limit to the device maximum once per device.
+int ensure_max_dynamic_smem(const void* func);
 
 int launch_softplus_table(uint16_t* lut, cudaStream_t stream);
 size_t route_select_smem(int num_experts);

@@ -1,0 +1,56 @@
+// Host-side launch helpers shared by the kernels: cached per-device queries.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "kernels.h"
+
+namespace spx {
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int kMaxFuncs = 64;
+
+std::mutex g_mu;
+int g_sm_count[kMaxDevices] = {};
+const void* g_func[kMaxDevices][kMaxFuncs] = {};
+
+int current_device() {
+  int dev = 0;
+  return cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices ? dev : -1;
+}
+
+}  // namespace
+
+int device_sm_count() {
+  const int dev = current_device();
+  if (dev < 0) return 148;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_sm_count[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_sm_count[dev] = n;
+  }
+  return g_sm_count[dev];
+}
+
+int ensure_max_dynamic_smem(const void* func) {
+  const int dev = current_device();
+  if (dev < 0) return SPX_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_mu);
+  for (int i = 0; i < kMaxFuncs; ++i) {
+    if (g_func[dev][i] == func) return SPX_OK;
+    if (g_func[dev][i] == nullptr) {
+      int optin = 0;
+      if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+        return SPX_ERR_CUDA;
+      if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess)
+        return SPX_ERR_CUDA;
+      g_func[dev][i] = func;
+      return SPX_OK;
+    }
+  }
+  return SPX_ERR_UNSUPPORTED;
+}
+
+}  // namespace spx

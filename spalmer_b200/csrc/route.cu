@@ -174,8 +174,8 @@ __global__ void __launch_bounds__(kRouteRows) route_select_kernel(const RouteArg
     mx = -bf16_to_f32(b0);
     float s = 0.0f;
     for (int c = 0; c < E; ++c)
-      if (resident[c]) s += expf(-bf16_to_f32(row[c]) - mx);
-    denom = s;
+      if (resident[c]) s += __expf(-bf16_to_f32(row[c]) - mx);
+    denom = 1.0f / s;  // reciprocal: the probabilities below are rounded to BF16
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int g0 = 0; g0 < E; g0 += 32) {
@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(kRouteRows) route_select_kernel(const RouteArg
     for (int q = 0; q < 32; ++q) {
       const int c = g0 + q;
       float p = 0.0f;
-      if (live && c < E && resident[c]) p = round_bf16(expf(-bf16_to_f32(row[c]) - mx) / denom);
+      if (live && c < E && resident[c]) p = round_bf16(__expf(-bf16_to_f32(row[c]) - mx) * denom);
       v[q] = p;
     }
     // Transpose-reduce: after 5 halving steps lane l holds column g0 + l.
@@ -253,19 +253,19 @@ int launch_route(const RouteArgs& a, cudaStream_t stream) {
   const size_t smem = route_select_smem(a.num_experts);
   cudaError_t err;
   if (a.top_k + 1 <= 5) {
-    cudaFuncSetAttribute(route_select_kernel<5>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (ensure_max_dynamic_smem(reinterpret_cast<const void*>(route_select_kernel<5>)) != SPX_OK) return SPX_ERR_CUDA;
     route_select_kernel<5><<<blocks, kRouteRows, smem, stream>>>(a);
   } else if (a.top_k + 1 <= 9) {
-    cudaFuncSetAttribute(route_select_kernel<9>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (ensure_max_dynamic_smem(reinterpret_cast<const void*>(route_select_kernel<9>)) != SPX_OK) return SPX_ERR_CUDA;
     route_select_kernel<9><<<blocks, kRouteRows, smem, stream>>>(a);
   } else {
-    cudaFuncSetAttribute(route_select_kernel<kMaxTopK + 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (ensure_max_dynamic_smem(reinterpret_cast<const void*>(route_select_kernel<kMaxTopK + 1>)) != SPX_OK) return SPX_ERR_CUDA;
     route_select_kernel<kMaxTopK + 1><<<blocks, kRouteRows, smem, stream>>>(a);
   }
   err = cudaGetLastError();
   if (err != cudaSuccess) return SPX_ERR_CUDA;
   const size_t tsmem = static_cast<size_t>(kTieThreads) * (a.num_experts | 1) * 4;
-  cudaFuncSetAttribute(route_ties_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tsmem));
+  if (ensure_max_dynamic_smem(reinterpret_cast<const void*>(route_ties_kernel)) != SPX_OK) return SPX_ERR_CUDA;
   int tie_blocks = static_cast<int>((a.tokens + kTieThreads - 1) / kTieThreads);
   if (tie_blocks > a.sm_count * 8) tie_blocks = a.sm_count * 8;
   route_ties_kernel<<<tie_blocks, kTieThreads, tsmem, stream>>>(a);
