@@ -229,8 +229,12 @@ def run_ours(args) -> None:
             dist.barrier()
 
     with torch.inference_mode():
+        # Warm-up runs the timed loop's exact pattern (the previous step's outputs
+        # stay alive while the next step allocates), so the caching allocator
+        # holds both output sets before timing starts.
+        out = None
         for i in range(W):
-            mixer(x_bufs[i % 2])
+            out = mixer(x_bufs[i % 2])
         torch.cuda.synchronize()
         stage_sets = [[torch.cuda.Event(enable_timing=True) for _ in range(_lib.STAGE_EVENTS)] for _ in range(K)]
         for st in stage_sets:
@@ -257,26 +261,48 @@ def run_ours(args) -> None:
         for j, name in enumerate(_lib.STAGE_NAMES):
             stages[name] = sum(st[j].elapsed_time(st[j + 1]) for st in stage_sets) / K
 
-        # e2e through the module API with host buffers
-        out_host = torch.empty(batch, seq, config.d_model, dtype=torch.bfloat16).pin_memory()
-        aux_host = torch.empty((), dtype=torch.bfloat16).pin_memory()
+        # e2e through the module API with host buffers.  Every step copies its
+        # own hidden states in from pinned host memory and its update + aux
+        # loss back out; the copies run on their own streams (double-buffered)
+        # so step i's H2D/D2H overlap the neighbouring steps' compute.
+        main = torch.cuda.current_stream(device)
+        s_in = torch.cuda.Stream(device)
+        s_out = torch.cuda.Stream(device)
+        x_dev = [torch.empty_like(x_bufs[0]) for _ in range(2)]
+        out_host = [torch.empty(batch, seq, config.d_model, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        aux_host = [torch.empty((), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        freed = [torch.cuda.Event() for _ in range(2)]  # x_dev[b] consumed by its forward
+        for ev in freed:
+            ev.record(main)
 
-        def e2e_step():
-            xd = x_host.to(device, non_blocking=True)
-            o = mixer(xd)
-            out_host.copy_(o.update, non_blocking=True)
-            aux_host.copy_(o.auxiliary_loss, non_blocking=True)
+        def e2e_steps(n):
+            for i in range(n):
+                b = i % 2
+                with torch.cuda.stream(s_in):
+                    s_in.wait_event(freed[b])
+                    x_dev[b].copy_(x_host, non_blocking=True)
+                    loaded = torch.cuda.Event()
+                    loaded.record(s_in)
+                main.wait_event(loaded)
+                o = mixer(x_dev[b])
+                freed[b].record(main)
+                with torch.cuda.stream(s_out):
+                    s_out.wait_stream(main)
+                    o.update.record_stream(s_out)
+                    o.auxiliary_loss.record_stream(s_out)
+                    out_host[b].copy_(o.update, non_blocking=True)
+                    aux_host[b].copy_(o.auxiliary_loss, non_blocking=True)
 
-        for _ in range(W):
-            e2e_step()
+        e2e_steps(W)
         torch.cuda.synchronize()
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(K):
-            e2e_step()
-        e1.record()
+        e0.record(main)
+        s_in.wait_stream(main)
+        e2e_steps(K)
+        main.wait_stream(s_out)
+        e1.record(main)
         torch.cuda.synchronize()
         barrier()
         e2e_ms = e0.elapsed_time(e1)

@@ -69,7 +69,7 @@ int make_shape(const spx_layer_dims* dm, Shape* s) {
 }
 
 struct Layout {
-  size_t small, tie_rows, lb_partial, chunk_hist, counts, starts, tiles, order, src_row;
+  size_t small, tie_rows, lb_partial, chunk_hist, counts, starts, tiles, order, src_row, sorted_w;
   size_t hidden, y, shared_hidden, logits, x_pad, util, stats, ratios, aux, total;
 };
 
@@ -90,6 +90,7 @@ Layout make_layout(const Shape& s) {
   L.tiles = take(sizeof(int4) * static_cast<size_t>(s.max_tiles));
   L.order = take(sizeof(int) * s.P);
   L.src_row = take(sizeof(int) * s.P);
+  L.sorted_w = take(sizeof(uint16_t) * s.P);
   L.hidden = take(2 * static_cast<size_t>(s.P) * s.kp);
   L.y = take(2 * static_cast<size_t>(s.P) * s.d);
   L.shared_hidden = take(s.S > 0 ? 2 * static_cast<size_t>(s.T) * s.ksp : 0);
@@ -337,6 +338,8 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   da.aux_loss = out->auxiliary_loss != nullptr ? out->auxiliary_loss : at<uint16_t>(workspace, L.aux);
   da.resident = w->resident_mask;
   da.execution_loop = dims->execution_loop;
+  da.pair_weights = out->routing_weights;
+  da.sorted_weights = at<uint16_t>(workspace, L.sorted_w);
   if ((rc = launch_dispatch(da, st)) != SPX_OK) return rc;
   mark(3);
 
@@ -373,7 +376,7 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
     g.out = y;
     g.ldo = s.d;
     g.pos_to_pair = da.order;
-    g.pair_weight = out->routing_weights;
+    g.pos_weight = da.sorted_weights;
     if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn_d, st)) != SPX_OK) return rc;
   }
   mark(5);

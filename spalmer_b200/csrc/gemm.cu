@@ -21,6 +21,7 @@
 // experts/mixer.py:207); accumulation is FP32 throughout.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -35,129 +36,159 @@ __device__ __forceinline__ uint8_t* align_1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+// Epilogue arithmetic on BF16 pairs.  The hardware conversions round to
+// nearest even like the reference's CPU tensors (NaN payloads aside).
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+__device__ __forceinline__ float lo_f(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float hi_f(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+// silu(x) = x / (1 + e^-x); approximate exp/divide, the result is rounded to BF16.
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
-__device__ __forceinline__ void store_bf16x16(uint16_t* dst, const uint16_t (&h)[16], int valid) {
-  if (valid >= 16 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
-    const uint4* s = reinterpret_cast<const uint4*>(h);
-    reinterpret_cast<uint4*>(dst)[0] = s[0];
-    reinterpret_cast<uint4*>(dst)[1] = s[1];
+// Epilogue staging: each epilogue warp owns a 32-row x 64-column BF16 slice
+// buffer (4 KB).  Threads write their own row (TMEM lane = row), then the warp
+// writes 4 rows x 128 B per instruction, so global stores (and the combine's
+// loads of Y) move whole row segments.  16-byte chunk c of row i sits at chunk
+// position c ^ (i & 7): conflict-free for both access patterns.
+__device__ __forceinline__ uint32_t stage_off(int i, int chunk) {
+  return static_cast<uint32_t>(i * 128 + ((chunk ^ (i & 7)) << 4));
+}
+
+// 16 BF16 values (8 packed words) of row i starting at column col (multiple of 16).
+__device__ __forceinline__ void stage_put16(uint8_t* buf, int i, int col, const uint32_t* w) {
+  *reinterpret_cast<uint4*>(buf + stage_off(i, col >> 3)) = make_uint4(w[0], w[1], w[2], w[3]);
+  *reinterpret_cast<uint4*>(buf + stage_off(i, (col >> 3) + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+__device__ __forceinline__ void put8(uint16_t* dst, const uint4& v, int n) {
+  if (n >= 8 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+    *reinterpret_cast<uint4*>(dst) = v;
   } else {
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (j < valid) dst[j] = h[j];
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(&v);
+    for (int j = 0; j < n; ++j) dst[j] = h[j];
   }
 }
 
-__device__ __forceinline__ void load_bf16x16_f32(const uint16_t* src, float (&f)[16], int valid) {
-  if (valid >= 16 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
-    uint4 q[2];
-    q[0] = reinterpret_cast<const uint4*>(src)[0];
-    q[1] = reinterpret_cast<const uint4*>(src)[1];
-    const uint16_t* h = reinterpret_cast<const uint16_t*>(q);
+// Combine one staged 8-column chunk with the k weighted expert rows of token
+// `rowid`: all k loads are issued before any is consumed.
+__device__ __forceinline__ void combine8(uint4& v, const uint16_t* y, int k, int64_t ld_y, int n) {
+  float acc[8] = {lo_f(v.x), hi_f(v.x), lo_f(v.y), hi_f(v.y), lo_f(v.z), hi_f(v.z), lo_f(v.w), hi_f(v.w)};
+  if (n >= 8 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0 && ((ld_y * 2) & 15) == 0) {
+    // Slots in batches of 8: every load of a batch is in flight before any is used.
+    for (int s0 = 0; s0 < k; s0 += 8) {
+      uint4 t[8];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) f[j] = bf16_to_f32(h[j]);
+      for (int q = 0; q < 8; ++q)
+        if (s0 + q < k) t[q] = __ldg(reinterpret_cast<const uint4*>(y + (s0 + q) * ld_y));
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (s0 + q < k) {
+          acc[0] += lo_f(t[q].x);
+          acc[1] += hi_f(t[q].x);
+          acc[2] += lo_f(t[q].y);
+          acc[3] += hi_f(t[q].y);
+          acc[4] += lo_f(t[q].z);
+          acc[5] += hi_f(t[q].z);
+          acc[6] += lo_f(t[q].w);
+          acc[7] += hi_f(t[q].w);
+        }
+      }
+    }
   } else {
-#pragma unroll
-    for (int j = 0; j < 16; ++j) f[j] = j < valid ? bf16_to_f32(src[j]) : 0.0f;
+    for (int sl = 0; sl < k; ++sl)
+      for (int q = 0; q < n; ++q) acc[q] += bf16_to_f32(y[sl * ld_y + q]);
   }
+  v = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
+                 pack_bf16x2(acc[6], acc[7]));
 }
 
+// One epilogue warp: TMEM lane quadrant `quad` (32 tile rows), output column
+// slices half, half + 2, ... of the tile (two warps share a quadrant).
+// `my_row` is the output row of this thread's tile row (the pair index for
+// kEpiScatter) and `my_w` its routing weight; the caller loads both before it
+// waits for the accumulator so their latency overlaps the MMAs.
 template <int EPI>
-__device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, int r, int row0, int rows,
-                                             int n0, int nt) {
+__device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, uint8_t* stage, int quad, int half,
+                                             int lane, int row0, int rows, int n0, int nt, long long my_row,
+                                             float my_w) {
+  constexpr int W = (EPI == kEpiSwiglu) ? 32 : 64;  // output columns per slice
+  const int r = quad * 32 + lane;                   // tile row owned by this thread (its TMEM lane)
   const bool live = r < rows;
-  const int bn = a.bn;
-  if constexpr (EPI == kEpiStore) {
-    uint16_t* out = static_cast<uint16_t*>(a.out);
-    for (int c = 0; c < bn; c += 16) {
-      uint32_t v[16];
-      tmem_ld16(taddr + c, v);
+  const int wrows = rows - quad * 32;               // valid rows of this quadrant (may be <= 0)
+  uint16_t* out = static_cast<uint16_t*>(a.out);
+  const int out_cols = (EPI == kEpiSwiglu) ? a.chunk : a.bn;
+  const int col_base = (EPI == kEpiSwiglu) ? nt * a.chunk : n0;
+  for (int s0 = half * W; s0 < out_cols; s0 += 2 * W) {
+    const int w = min(W, out_cols - s0);
+    // 1) accumulator -> registers (one TMEM wait per slice) -> staged BF16 row slice
+    uint32_t hw[W / 2];
+    if constexpr (EPI == kEpiSwiglu) {
+      uint32_t g[32], u[32];
+      tmem_ld32(taddr + s0, g);
+      tmem_ld32(taddr + a.chunk + s0, u);
       tmem_wait_ld();
-      const int gcol = n0 + c;
-      const int valid = a.n_valid - gcol;
-      if (live && valid > 0) {
-        uint16_t h[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float f = __uint_as_float(v[j]);
-          if (a.bias != nullptr && j < valid) f += bf16_to_f32(a.bias[gcol + j]);
-          h[j] = f32_to_bf16_rne(f);
+      for (int j = 0; j < 32; j += 2) {
+        const float h0 = bfr(silu_fast(bfr(__uint_as_float(g[j])))) * bfr(__uint_as_float(u[j]));
+        const float h1 = bfr(silu_fast(bfr(__uint_as_float(g[j + 1])))) * bfr(__uint_as_float(u[j + 1]));
+        hw[j / 2] = pack_bf16x2(h0, h1);
+      }
+    } else {
+      uint32_t v[64];
+      tmem_ld32(taddr + s0, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      if (w > 32) tmem_ld32(taddr + s0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      tmem_wait_ld();
+      if constexpr (EPI == kEpiStore) {
+        const int gcol = col_base + s0;
+#pragma unroll
+        for (int j = 0; j < 64; j += 2) {
+          float f0 = __uint_as_float(v[j]), f1 = __uint_as_float(v[j + 1]);
+          if (a.bias != nullptr) {
+            if (j < w && gcol + j < a.n_valid) f0 += bf16_to_f32(a.bias[gcol + j]);
+            if (j + 1 < w && gcol + j + 1 < a.n_valid) f1 += bf16_to_f32(a.bias[gcol + j + 1]);
+          }
+          hw[j / 2] = pack_bf16x2(f0, f1);
         }
-        store_bf16x16(out + static_cast<int64_t>(row0 + r) * a.ldo + gcol, h, valid);
+      } else if constexpr (EPI == kEpiScatter) {
+#pragma unroll
+        for (int j = 0; j < 64; j += 2)
+          hw[j / 2] = pack_bf16x2(bfr(__uint_as_float(v[j])) * my_w, bfr(__uint_as_float(v[j + 1])) * my_w);
+      } else {  // kEpiCombine: the shared path's output, rounded to BF16
+#pragma unroll
+        for (int j = 0; j < 64; j += 2) hw[j / 2] = pack_bf16x2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
       }
     }
-  } else if constexpr (EPI == kEpiSwiglu) {
-    uint16_t* out = static_cast<uint16_t*>(a.out);
-    const int c_half = a.chunk;
-    const int col0 = nt * c_half;
-    for (int c = 0; c < c_half; c += 16) {
-      uint32_t g[16], u[16];
-      tmem_ld16(taddr + c, g);
-      tmem_ld16(taddr + c_half + c, u);
-      tmem_wait_ld();
-      if (live) {
-        uint16_t h[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float gb = round_bf16(__uint_as_float(g[j]));
-          const float ub = round_bf16(__uint_as_float(u[j]));
-          const float sb = round_bf16(silu_f(gb));
-          h[j] = f32_to_bf16_rne(sb * ub);
+    for (int c = 0; c < W; c += 16) stage_put16(stage, lane, c, &hw[c / 2]);
+    __syncwarp();
+    // 2) staged rows -> global: lane group (lane >> 3) takes one row, lane & 7 its 16-byte chunk
+    const int gcol0 = col_base + s0;
+    const int valid = (EPI == kEpiSwiglu) ? w : min(w, a.n_valid - gcol0);
+    const int j = lane & 7;
+#pragma unroll 2
+    for (int step = 0; step < 8; ++step) {
+      const int ri = step * 4 + (lane >> 3);
+      const long long rowid = __shfl_sync(0xFFFFFFFFu, my_row, ri);
+      const int n = min(8, valid - j * 8);
+      if (ri < wrows && n > 0) {
+        uint4 v = *reinterpret_cast<const uint4*>(stage + stage_off(ri, j));
+        if constexpr (EPI == kEpiCombine) {
+          const uint16_t* y = a.y_pairs + (rowid * a.top_k) * a.ld_y + gcol0 + j * 8;
+          combine8(v, y, a.top_k, a.ld_y, n);
         }
-        store_bf16x16(out + static_cast<int64_t>(row0 + r) * a.ldo + col0 + c, h, 16);
+        put8(out + rowid * a.ldo + gcol0 + j * 8, v, n);
       }
     }
+    __syncwarp();
+  }
+  if constexpr (EPI == kEpiSwiglu) {
     // Zero the K padding of the hidden matrix (columns [chunks*c, h_cols)).
-    if (live && nt == a.n_tiles - 1) {
+    if (half == 0 && live && nt == a.n_tiles - 1) {
       uint16_t* dst = out + static_cast<int64_t>(row0 + r) * a.ldo;
-      for (int col = a.n_tiles * c_half; col < a.h_cols; ++col) dst[col] = 0;
-    }
-  } else if constexpr (EPI == kEpiScatter) {
-    uint16_t* out = static_cast<uint16_t*>(a.out);
-    int64_t pair = 0;
-    float w = 0.0f;
-    if (live) {
-      pair = a.pos_to_pair[row0 + r];
-      w = bf16_to_f32(a.pair_weight[pair]);
-    }
-    for (int c = 0; c < bn; c += 16) {
-      uint32_t v[16];
-      tmem_ld16(taddr + c, v);
-      tmem_wait_ld();
-      const int gcol = n0 + c;
-      const int valid = a.n_valid - gcol;
-      if (live && valid > 0) {
-        uint16_t h[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) h[j] = f32_to_bf16_rne(round_bf16(__uint_as_float(v[j])) * w);
-        store_bf16x16(out + pair * a.ldo + gcol, h, valid);
-      }
-    }
-  } else {  // kEpiCombine
-    uint16_t* out = static_cast<uint16_t*>(a.out);
-    const int64_t t = static_cast<int64_t>(row0) + r;
-    for (int c = 0; c < bn; c += 16) {
-      uint32_t v[16];
-      tmem_ld16(taddr + c, v);
-      tmem_wait_ld();
-      const int gcol = n0 + c;
-      const int valid = a.n_valid - gcol;
-      if (live && valid > 0) {
-        float acc[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = round_bf16(__uint_as_float(v[j]));
-        for (int s = 0; s < a.top_k; ++s) {
-          float y[16];
-          load_bf16x16_f32(a.y_pairs + (t * a.top_k + s) * a.ld_y + gcol, y, valid);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) acc[j] += y[j];
-        }
-        uint16_t h[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) h[j] = f32_to_bf16_rne(acc[j]);
-        store_bf16x16(out + t * a.ldo + gcol, h, valid);
-      }
+      for (int col = a.n_tiles * a.chunk; col < a.h_cols; ++col) dst[col] = 0;
     }
   }
 }
@@ -196,7 +227,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   const uint32_t b_bytes = static_cast<uint32_t>(bn) * 128u;
   uint8_t* sa = smem;
   uint8_t* sb = smem + S * a_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sb + S * b_bytes);
+  uint8_t* stage_all = sb + S * b_bytes;  // kGemmEpilogueWarps x kStageBytesPerWarp
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_all + kGemmEpilogueWarps * kStageBytesPerWarp);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;   // [2] accumulator ready
   uint64_t* tempty = tfull + 2;  // [2] accumulator drained
@@ -305,22 +337,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue (warps 2..5): warp w drains TMEM lanes 32*(w%4) .. +31
+    // ---------------- epilogue (warps 2..9): warp w drains TMEM lanes 32*(w%4) .. +31,
+    // column slices (w-2)/4, +2, ...
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;
+    const int half = (warp - 2) >> 2;
     uint32_t lt = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++lt) {
       int group, row0, rows, nt;
       if (!decode_tile(a, t, group, row0, rows, nt)) break;
       const uint32_t b = lt & 1u;
       const uint32_t tph = (lt >> 1) & 1u;
+      const int r = quad * 32 + lane;
+      long long my_row = static_cast<long long>(row0) + r;
+      float my_w = 0.0f;
+      if constexpr (EPI == kEpiScatter) {
+        my_row = 0;
+        if (r < rows) {
+          my_row = a.pos_to_pair[row0 + r];
+          my_w = bf16_to_f32(a.pos_weight[row0 + r]);
+        }
+      }
       int go = 1;
       if (lane == 0) go = mbar_wait(&tfull[b], tph, a.status, SPX_DEV_TIMEOUT_EPILOGUE) ? 1 : 0;
       go = __shfl_sync(0xFFFFFFFFu, go, 0);
       if (!go) break;
       tc_fence_after();
-      run_epilogue<EPI>(a, tmem + b * a.tmem_cols + (static_cast<uint32_t>(quad * 32) << 16), r, row0, rows,
-                        nt * bn, nt);
+      run_epilogue<EPI>(a, tmem + b * a.tmem_cols + (static_cast<uint32_t>(quad * 32) << 16),
+                        stage_all + (warp - 2) * kStageBytesPerWarp, quad, half, lane, row0, rows, nt * bn, nt,
+                        my_row, my_w);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
@@ -384,7 +428,7 @@ int encode_3d(CUtensorMap* map, const void* base, int64_t groups, int64_t rows, 
 
 size_t gemm_smem_bytes(int bn, int stages) {
   return 1024 + static_cast<size_t>(stages) * (kTileRows * 128 + static_cast<size_t>(bn) * 128) +
-         (2 * stages + 4) * 8 + 16;
+         kGemmEpilogueWarps * kStageBytesPerWarp + (2 * stages + 4) * 8 + 16;
 }
 
 // As many stages as fit: the persistent producer keeps prefetching the next

@@ -10,9 +10,11 @@
 namespace spx {
 
 constexpr int kTileRows = 128;         // M of every tcgen05 tile (cta_group::1)
-constexpr int kGemmThreads = 192;      // 6 warps: TMA, MMA, 4 x epilogue
-constexpr int kGemmEpilogueWarps = 4;
-constexpr size_t kGemmSmemBudget = 200 * 1024;
+constexpr int kGemmThreads = 320;      // 10 warps: TMA, MMA, 8 x epilogue (2 per TMEM lane quadrant)
+constexpr int kGemmEpilogueWarps = 8;
+constexpr size_t kGemmSmemBudget = 227 * 1024;  // sm_100 opt-in maximum per CTA
+constexpr int kSliceCols = 64;                  // epilogue staging slice width
+constexpr int kStageBytesPerWarp = 32 * kSliceCols * 2;
 constexpr int kRouteRows = 128;        // token rows per route_select CTA
 constexpr int kTieThreads = 64;        // rows replayed per route_ties CTA
 constexpr int kMaxTopK = 20;           // MicroExpertsConfig.max_active_experts default
@@ -52,6 +54,8 @@ struct DispatchArgs {
   int* num_tiles;
   int* order;                // [P] argsort(stable) permutation
   int* src_row;              // [P] token row of each sorted position
+  const uint16_t* pair_weights;  // [P] routing weights in pair order, or null
+  uint16_t* sorted_weights;  // [P] the same weights in sorted (dispatch) order, or null
   // statistics (any may be null)
   float* utilization;        // [E]
   long long* group_stats;    // [6]
@@ -85,8 +89,8 @@ struct GemmArgs {
   void* out;
   int64_t ldo;
   const uint16_t* bias;      // kEpiStore
-  const int* pos_to_pair;    // kEpiScatter
-  const uint16_t* pair_weight;
+  const int* pos_to_pair;    // kEpiScatter: pair index of each sorted position
+  const uint16_t* pos_weight;  // kEpiScatter: routing weight of each sorted position
   const uint16_t* y_pairs;   // kEpiCombine
   int64_t ld_y;
   int top_k;
