@@ -349,12 +349,13 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   // ---- K3a: expert GEMM1 (gathered rows) + SwiGLU
   {
     GemmArgs g = base_args(2 * s.c, s.kd / 64, status);
-    if ((rc = encode_2d(&g.tma_a, xa, s.T, s.kd, s.kd, 1)) != SPX_OK) return rc;
     if ((rc = encode_3d(&g.tma_b, w->expert_w1, s.E, static_cast<int64_t>(s.nc) * 2 * s.c, s.kd, 2 * s.c)) != SPX_OK)
       return rc;
     g.groups = s.E;
     g.gather = 1;
     g.gather_idx = da.src_row;
+    g.a_base = xa;
+    g.lda = s.kd;
     g.tiles = da.tiles;
     g.num_tiles = da.num_tiles;
     g.chunk = s.c;

@@ -16,7 +16,7 @@ constexpr size_t kGemmSmemBudget = 227 * 1024;  // sm_100 opt-in maximum per CTA
 constexpr int kSliceCols = 64;                  // epilogue staging slice width
 constexpr int kStageBytesPerWarp = 32 * kSliceCols * 2;
 constexpr int kRouteRows = 128;        // token rows per route_select CTA
-constexpr int kTieThreads = 64;        // rows replayed per route_ties CTA
+constexpr int kTieWarps = 8;           // rows replayed at once per route_ties CTA (one warp each)
 constexpr int kMaxTopK = 20;           // MicroExpertsConfig.max_active_experts default
 constexpr int kDispatchChunk = 2048;   // pairs per dispatch CTA
 constexpr int kDispatchWarps = 4;
@@ -70,7 +70,7 @@ struct DispatchArgs {
 };
 
 struct GemmArgs {
-  CUtensorMap tma_a;         // A rows: box {64,128} (tiled) or {64,1} (gather4)
+  CUtensorMap tma_a;         // A rows: box {64,128} (unused when gather != 0)
   CUtensorMap tma_b;         // B [groups, N, K]: box {64, bn, 1}
   int m_rows;                // uniform tiling: rows of A
   int k_blocks;              // K / 64
@@ -79,8 +79,10 @@ struct GemmArgs {
   uint32_t tmem_cols;        // per accumulator buffer: power of two >= max(32, bn); two buffers
   int n_tiles;               // N tiles per M tile (set by launch_gemm)
   int groups;                // B groups (bounds check of the tile table)
-  int gather;                // 1: A rows gathered through gather_idx
+  int gather;                // 1: A rows gathered through gather_idx with cp.async (a_base/lda)
   const int* gather_idx;
+  const uint16_t* a_base;    // gather: A rows (row stride lda elements)
+  int64_t lda;
   const int4* tiles;         // grouped tiling, or null
   const int* num_tiles;
   int n_valid;               // valid output columns

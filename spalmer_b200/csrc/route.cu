@@ -14,7 +14,8 @@
 //   appended to a tie list.  The same pass accumulates the per-expert sums of
 //   BF16-rounded softmax(-scores) probabilities for the load-balance loss.
 // route_ties_kernel: replays PyTorch's CPU top-k (topk_exact.cuh) for every
-//   listed row, one thread per row, the row staged in shared memory.
+//   listed row, one warp per row (each partition step data-parallel over the
+//   warp), the row staged in shared memory.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -208,31 +209,116 @@ __global__ void __launch_bounds__(kRouteRows) route_select_kernel(const RouteArg
   }
 }
 
-__global__ void __launch_bounds__(kTieThreads) route_ties_kernel(const RouteArgs a) {
+// One Hoare partition step of v[lo, hi) by a whole warp: the data-parallel
+// form of exact::partition_by_lists (identical result, see topk_exact.cuh).
+__device__ int warp_partition(uint32_t* v, int lo, int hi, uint16_t* lpos, uint16_t* rpos, int lane) {
+  if (lane == 0) exact::median_to_slot(v, lo, lo + 1, lo + (hi - lo) / 2, hi - 1);
+  __syncwarp();
+  const uint32_t pivot = v[lo];
+  const unsigned lt = (1u << lane) - 1u;
+  int nl = 0, nr = 0;
+  for (int base = lo; base < hi; base += 32) {
+    const int p = base + lane;
+    const bool in = p < hi;
+    const uint32_t x = in ? v[p] : 0u;
+    const bool is_l = in && p > lo && !exact::before(x, pivot);
+    const bool is_r = in && !exact::before(pivot, x);
+    const unsigned bl = __ballot_sync(0xFFFFFFFFu, is_l);
+    const unsigned br = __ballot_sync(0xFFFFFFFFu, is_r);
+    if (is_l) lpos[nl + __popc(bl & lt)] = static_cast<uint16_t>(p);
+    if (is_r) rpos[nr + __popc(br & lt)] = static_cast<uint16_t>(p);
+    nl += __popc(bl);
+    nr += __popc(br);
+  }
+  __syncwarp();
+  // Swaps happen for the leading m with Lo[m] < Ro[m]; the condition is
+  // monotone in m, so each ballot is a run of low lanes.
+  int m = 0;
+  for (int m0 = 0;; m0 += 32) {
+    const int q = m0 + lane;
+    const bool c = q < nl && q < nr && lpos[q] < rpos[nr - 1 - q];
+    const int ones = __popc(__ballot_sync(0xFFFFFFFFu, c));
+    m += ones;
+    if (ones < 32) break;
+  }
+  for (int q = lane; q < m; q += 32) {
+    const int pl = lpos[q], pr = rpos[nr - 1 - q];
+    const uint32_t t = v[pl];
+    v[pl] = v[pr];
+    v[pr] = t;
+  }
+  __syncwarp();
+  if (m == 0) return lpos[0];
+  const int left = m < nl ? lpos[m] : hi;
+  const int right_prev = rpos[nr - m];
+  return left < right_prev ? left : right_prev;
+}
+
+// exact::topk_least_cpu_order with the partition steps spread over a warp;
+// the short sequential tails (<= 3 elements, the sort of the first k-1, heap
+// fallbacks) run on lane 0.
+__device__ void warp_topk_cpu_order(uint32_t* v, int n, int k, uint16_t* lpos, uint16_t* rpos, int lane) {
+  if (k * 64 <= n) {
+    if (lane == 0) exact::partial_sort_first(v, k, n);
+    __syncwarp();
+    return;
+  }
+  const int nth = k - 1;
+  int lo = 0, hi = n;
+  int depth = 2 * exact::floor_log2(n);
+  bool by_heap = false;
+  while (hi - lo > 3) {
+    if (depth == 0) {
+      if (lane == 0) {
+        exact::heap_select(v, lo, nth + 1, hi);
+        exact::swap_at(v, lo, nth);
+      }
+      by_heap = true;
+      break;
+    }
+    --depth;
+    const int cut = warp_partition(v, lo, hi, lpos, rpos, lane);
+    if (cut <= nth)
+      lo = cut;
+    else
+      hi = cut;
+  }
+  if (lane == 0) {
+    if (!by_heap) exact::insertion_sort(v, lo, hi);
+    exact::intro_sort(v, k - 1);
+  }
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(kTieWarps * 32) route_ties_kernel(const RouteArgs a) {
   extern __shared__ uint32_t tie_smem[];
   const int E = a.num_experts;
   const int k = a.top_k;
-  const int stride = E | 1;
-  uint32_t* v = tie_smem + threadIdx.x * stride;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half_words = (E + 1) / 2;
+  uint32_t* v = tie_smem + warp * (E + 2 * half_words);
+  uint16_t* lpos = reinterpret_cast<uint16_t*>(v + E);
+  uint16_t* rpos = reinterpret_cast<uint16_t*>(v + E + half_words);
   const int n_ties = *a.tie_count;
-  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n_ties; t += gridDim.x * blockDim.x) {
+  for (int t = blockIdx.x * kTieWarps + warp; t < n_ties; t += gridDim.x * kTieWarps) {
     const int64_t row = a.tie_rows[t];
     const uint16_t* s = a.scores + row * E;
-    for (int c = 0; c < E; ++c) {
+    for (int c = lane; c < E; c += 32) {
       const bool res = a.resident == nullptr || a.resident[c] != 0;
       const uint16_t b = res ? s[c] : static_cast<uint16_t>(0x7F80u);
       v[c] = (static_cast<uint32_t>(b) << 16) | static_cast<uint32_t>(c);
     }
-    exact::topk_least_cpu_order(v, E, k);
-    uint16_t sel[kMaxTopK];
-    uint16_t wts[kMaxTopK];
-    for (int j = 0; j < k; ++j) {
-      const int id = static_cast<int>(v[j] & 0xFFFFu);
-      a.ids[row * k + j] = id;
-      sel[j] = s[id];
+    __syncwarp();
+    warp_topk_cpu_order(v, E, k, lpos, rpos, lane);
+    if (lane < k) a.ids[row * k + lane] = static_cast<int64_t>(v[lane] & 0xFFFFu);
+    if (lane == 0) {
+      uint16_t sel[kMaxTopK];
+      uint16_t wts[kMaxTopK];
+      for (int j = 0; j < k; ++j) sel[j] = s[v[j] & 0xFFFFu];
+      routing_softmax(sel, k, wts);
+      for (int j = 0; j < k; ++j) a.weights[row * k + j] = wts[j];
     }
-    routing_softmax(sel, k, wts);
-    for (int j = 0; j < k; ++j) a.weights[row * k + j] = wts[j];
+    __syncwarp();
   }
 }
 
@@ -264,11 +350,11 @@ int launch_route(const RouteArgs& a, cudaStream_t stream) {
   }
   err = cudaGetLastError();
   if (err != cudaSuccess) return SPX_ERR_CUDA;
-  const size_t tsmem = static_cast<size_t>(kTieThreads) * (a.num_experts | 1) * 4;
+  const size_t tsmem = static_cast<size_t>(kTieWarps) * (a.num_experts + 2 * ((a.num_experts + 1) / 2)) * 4;
   if (ensure_max_dynamic_smem(reinterpret_cast<const void*>(route_ties_kernel)) != SPX_OK) return SPX_ERR_CUDA;
-  int tie_blocks = static_cast<int>((a.tokens + kTieThreads - 1) / kTieThreads);
+  int tie_blocks = static_cast<int>((a.tokens + kTieWarps - 1) / kTieWarps);
   if (tie_blocks > a.sm_count * 8) tie_blocks = a.sm_count * 8;
-  route_ties_kernel<<<tie_blocks, kTieThreads, tsmem, stream>>>(a);
+  route_ties_kernel<<<tie_blocks, kTieWarps * 32, tsmem, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 

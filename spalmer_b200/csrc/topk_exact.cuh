@@ -140,6 +140,35 @@ SPX_HD int partition_around_front(uint32_t* v, int lo, int hi) {
   }
 }
 
+// The same partition computed from two position lists instead of two moving
+// scanners, which makes it data-parallel (route.cu runs it with one warp per
+// row).  With the pivot at v[lo]:
+//   Lo = positions in (lo, hi) holding an element not before the pivot, ascending
+//   Ro = positions in [lo, hi) holding an element the pivot is not before, descending
+// Before any swap the scanners see original values only, and a swap at step m
+// exchanges v[Lo[m]] and v[Ro[m]] while Lo[m] < Ro[m].  The first m with
+// Lo[m] >= Ro[m] (Lo past its end counts as +inf, Ro past its end as -inf)
+// ends the loop, and the left scanner then rests at Lo[m], or at the swapped
+// slot Ro[m-1] if that comes first.  `lpos`/`rpos` are caller scratch of n
+// entries; Ro[m] is stored as rpos[nR-1-m] (ascending).
+SPX_HD int partition_by_lists(uint32_t* v, int lo, int hi, uint16_t* lpos, uint16_t* rpos) {
+  const int mid = lo + (hi - lo) / 2;
+  median_to_slot(v, lo, lo + 1, mid, hi - 1);
+  const uint32_t pivot = v[lo];
+  int nl = 0, nr = 0;
+  for (int p = lo; p < hi; ++p) {
+    if (p > lo && !before(v[p], pivot)) lpos[nl++] = static_cast<uint16_t>(p);
+    if (!before(pivot, v[p])) rpos[nr++] = static_cast<uint16_t>(p);
+  }
+  int m = 0;
+  while (m < nl && m < nr && lpos[m] < rpos[nr - 1 - m]) ++m;
+  for (int q = 0; q < m; ++q) swap_at(v, lpos[q], rpos[nr - 1 - q]);
+  if (m == 0) return lpos[0];
+  const int left = m < nl ? lpos[m] : hi;
+  const int right_prev = rpos[nr - m];
+  return left < right_prev ? left : right_prev;
+}
+
 // ---- binary max-heap on base[0, len) ordered by `before`.
 SPX_HD void heap_sift_up(uint32_t* base, int hole, int top, uint32_t x) {
   int parent = (hole - 1) / 2;

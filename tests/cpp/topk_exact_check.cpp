@@ -84,6 +84,36 @@ int main(int argc, char** argv) {
       }
     }
   }
-  std::printf("OK %ld\n", checked);
+  // The list form of the partition (parallelised on the device) must leave the
+  // array and the cut exactly as the two-scanner form does.
+  std::vector<uint32_t> a, b;
+  std::vector<uint16_t> lpos, rpos;
+  long parts = 0;
+  for (int n : ns) {
+    if (n < 4) continue;
+    for (long r = 0; r < rows * 4; ++r) {
+      const int levels = 1 + static_cast<int>(rng() % 8) * static_cast<int>(rng() % 20);
+      a.resize(n);
+      lpos.resize(n);
+      rpos.resize(n);
+      for (int j = 0; j < n; ++j) {
+        float x = 0.25f * static_cast<float>(rng() % static_cast<unsigned>(levels));
+        if (rng() % 211 == 0) x = NAN;
+        const uint16_t bits = std::isnan(x) ? uint16_t(0x7FC0) : bf16_bits(x);
+        a[j] = (static_cast<uint32_t>(bits) << 16) | static_cast<uint32_t>(j);
+      }
+      const int lo = static_cast<int>(rng() % static_cast<unsigned>(n - 3));
+      const int hi = lo + 4 + static_cast<int>(rng() % static_cast<unsigned>(n - lo - 3));
+      b = a;
+      const int c1 = spx::exact::partition_around_front(a.data(), lo, hi);
+      const int c2 = spx::exact::partition_by_lists(b.data(), lo, hi, lpos.data(), rpos.data());
+      if (c1 != c2 || a != b) {
+        std::printf("PARTITION MISMATCH n=%d lo=%d hi=%d cut %d vs %d\n", n, lo, hi, c1, c2);
+        return 1;
+      }
+      ++parts;
+    }
+  }
+  std::printf("OK %ld rows, %ld partitions\n", checked, parts);
   return 0;
 }
