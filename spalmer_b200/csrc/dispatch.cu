@@ -63,25 +63,35 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs 
 
   // Exclusive scan over chunks for each expert (chunk offsets within the
   // expert), one warp per expert: each lane owns a contiguous run of chunks.
-  const int seg = (nchunks + 31) / 32;
+  // Lanes take 16 consecutive chunks per pass; all 16 loads are issued before
+  // any is used (this kernel is latency bound, not bandwidth bound).
   for (int x = warp; x < E; x += 32) {
     int* row = a.chunk_hist + static_cast<int64_t>(x) * nchunks;
-    const int c0 = min(nchunks, lane * seg), c1 = min(nchunks, c0 + seg);
-    int sum = 0;
-    for (int c = c0; c < c1; ++c) sum += row[c];
-    int incl = sum;
+    int carry = 0;
+    for (int base = 0; base < nchunks; base += 32 * 16) {
+      const int c0 = base + lane * 16;
+      int vals[16];
+      int sum = 0;
 #pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int v = __shfl_up_sync(0xFFFFFFFFu, incl, off);
-      if (lane >= off) incl += v;
+      for (int q = 0; q < 16; ++q) {
+        vals[q] = (c0 + q < nchunks) ? row[c0 + q] : 0;
+        sum += vals[q];
+      }
+      int incl = sum;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int v = __shfl_up_sync(0xFFFFFFFFu, incl, off);
+        if (lane >= off) incl += v;
+      }
+      int run = carry + incl - sum;
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        if (c0 + q < nchunks) row[c0 + q] = run;
+        run += vals[q];
+      }
+      carry += __shfl_sync(0xFFFFFFFFu, incl, 31);
     }
-    int run = incl - sum;
-    for (int c = c0; c < c1; ++c) {
-      const int v = row[c];
-      row[c] = run;
-      run += v;
-    }
-    if (lane == 31) s_count[x] = incl;
+    if (lane == 0) s_count[x] = carry;
   }
   __syncthreads();
   const int count = (e < E) ? s_count[e] : 0;
@@ -121,17 +131,41 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs 
   if (e < E && a.utilization != nullptr) a.utilization[e] = util;
 
   // Group statistics (mixer.py:257-297).
-  if (threadIdx.x < 4) s_i64[threadIdx.x] = 0;
-  __syncthreads();
-  if (e < E && a.resident != nullptr && a.resident[e] != 0)
-    atomicAdd(reinterpret_cast<unsigned long long*>(&s_i64[3]), 1ull);
-  if (e < E && count > 0) {
-    atomicAdd(reinterpret_cast<unsigned long long*>(&s_i64[0]), 1ull);
-    atomicMax(reinterpret_cast<unsigned long long*>(&s_i64[1]), static_cast<unsigned long long>(count));
-    atomicAdd(reinterpret_cast<unsigned long long*>(&s_i64[2]),
-              static_cast<unsigned long long>(a.execution_loop ? count : next_pow2_i64(count)));
+  // Warp reductions, then one thread folds the 32 warp results (no contended atomics).
+  __syncthreads();  // every thread has read its tile_start out of s_scan
+  {
+    const bool act = e < E && count > 0;
+    int groups_w = __popc(__ballot_sync(0xFFFFFFFFu, act));
+    int resid_w = __popc(__ballot_sync(0xFFFFFFFFu, e < E && a.resident != nullptr && a.resident[e] != 0));
+    int max_w = act ? count : 0;
+    long long pad_w = act ? (a.execution_loop ? count : next_pow2_i64(count)) : 0;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      max_w = max(max_w, __shfl_xor_sync(0xFFFFFFFFu, max_w, off));
+      pad_w += __shfl_xor_sync(0xFFFFFFFFu, pad_w, off);
+    }
+    if (lane == 0) {
+      s_scan[warp] = groups_w;
+      s_scan[32 + warp] = resid_w;
+      s_scan[64 + warp] = max_w;
+      s_count[warp] = static_cast<int>(pad_w);  // s_count is no longer needed: reuse it
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      long long g = 0, rsd = 0, mx = 0, pad = 0;
+      for (int w = 0; w < 32; ++w) {
+        g += s_scan[w];
+        rsd += s_scan[32 + w];
+        mx = max(mx, static_cast<long long>(s_scan[64 + w]));
+        pad += s_count[w];
+      }
+      s_i64[0] = g;
+      s_i64[1] = mx;
+      s_i64[2] = pad;
+      s_i64[3] = rsd;
+    }
+    __syncthreads();
   }
-  __syncthreads();
   if (threadIdx.x == 0 && a.group_stats != nullptr) {
     const long long groups = s_i64[0], max_load = s_i64[1], padded = s_i64[2];
     const long long real = a.pairs;
@@ -149,10 +183,28 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs 
   // mean_p = bf16(sum_t p / T), frac = bf16(util), prod = bf16(frac*mean_p),
   // total = bf16(sum prod), loss = bf16(bf16(eligible) * total).
   if (a.aux_loss != nullptr && a.lb_blocks > 0) {
+    // Sum of the route blocks' probability partials per expert: one warp per
+    // expert, fixed lane striding and a fixed shuffle tree (deterministic).
+    for (int x = warp; x < E; x += 32) {
+      float part = 0.0f;
+      for (int b0 = 0; b0 < a.lb_blocks; b0 += 32 * 8) {
+        float v[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int b = b0 + q * 32 + lane;
+          v[q] = b < a.lb_blocks ? a.lb_partial[static_cast<int64_t>(b) * E + x] : 0.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) part += v[q];
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xFFFFFFFFu, part, off);
+      if (lane == 0) s_red[x] = part;
+    }
+    __syncthreads();
     float prod = 0.0f;
     if (e < E) {
-      float s = 0.0f;
-      for (int b = 0; b < a.lb_blocks; ++b) s += a.lb_partial[static_cast<int64_t>(b) * E + e];
+      const float s = s_red[e];
       const float mean_p = round_bf16(s / static_cast<float>(a.tokens));
       prod = round_bf16(round_bf16(util) * mean_p);
     }

@@ -301,9 +301,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   uint8_t* stage_all = sb + S * b_bytes;  // kGemmEpilogueWarps x kStageBytesPerWarp
   uint64_t* full = reinterpret_cast<uint64_t*>(stage_all + kGemmEpilogueWarps * kStageBytesPerWarp);
   uint64_t* empty = full + S;
-  uint64_t* tfull = empty + S;   // [2] accumulator ready
-  uint64_t* tempty = tfull + 2;  // [2] accumulator drained
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* tfull = empty + S;                 // [kMaxAccBufs] accumulator ready
+  uint64_t* tempty = tfull + kMaxAccBufs;      // [kMaxAccBufs] accumulator drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + kMaxAccBufs);
+  // As many accumulators as fit in the 512 TMEM columns (2 for 256-column tiles).
+  const uint32_t nacc = min(static_cast<uint32_t>(kMaxAccBufs), 512u / a.tmem_cols);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -316,7 +318,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       mbar_init(&full[s], a.gather ? 2 : 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kMaxAccBufs; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kGemmEpilogueWarps);
     }
@@ -325,7 +327,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     prefetch_tensormap(&a.tma_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 2 * a.tmem_cols);
+    tmem_alloc(tmem_slot, nacc * a.tmem_cols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -371,8 +373,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       uint32_t it = 0, lt = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++lt) {
-        const uint32_t b = lt & 1u;
-        const uint32_t tph = (lt >> 1) & 1u;
+        const uint32_t b = lt % nacc;
+        const uint32_t tph = (lt / nacc) & 1u;
         if (!mbar_wait(&tempty[b], tph ^ 1u, a.status, SPX_DEV_TIMEOUT_MMA)) break;
         tc_fence_after();
         const uint32_t acc = tmem + b * a.tmem_cols;
@@ -406,8 +408,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++lt) {
       int group, row0, rows, nt;
       if (!decode_tile(a, t, group, row0, rows, nt)) break;
-      const uint32_t b = lt & 1u;
-      const uint32_t tph = (lt >> 1) & 1u;
+      const uint32_t b = lt % nacc;
+      const uint32_t tph = (lt / nacc) & 1u;
       const int r = quad * 32 + lane;
       long long my_row = static_cast<long long>(row0) + r;
       float my_w = 0.0f;
@@ -435,7 +437,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * a.tmem_cols);
+    tmem_dealloc(tmem, nacc * a.tmem_cols);
   }
 }
 
@@ -489,7 +491,7 @@ int encode_3d(CUtensorMap* map, const void* base, int64_t groups, int64_t rows, 
 
 size_t gemm_smem_bytes(int bn, int stages) {
   return 1024 + static_cast<size_t>(stages) * (kTileRows * 128 + static_cast<size_t>(bn) * 128) +
-         kGemmEpilogueWarps * kStageBytesPerWarp + (2 * stages + 4) * 8 + 16;
+         kGemmEpilogueWarps * kStageBytesPerWarp + (2 * stages + 2 * kMaxAccBufs) * 8 + 16;
 }
 
 // As many stages as fit: the persistent producer keeps prefetching the next

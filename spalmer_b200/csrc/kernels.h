@@ -12,6 +12,7 @@ namespace spx {
 constexpr int kTileRows = 128;         // M of every tcgen05 tile (cta_group::1)
 constexpr int kGemmThreads = 320;      // 10 warps: TMA, MMA, 8 x epilogue (2 per TMEM lane quadrant)
 constexpr int kGemmEpilogueWarps = 8;
+constexpr int kMaxAccBufs = 4;         // TMEM accumulator buffers per CTA (as many as fit in 512 columns)
 constexpr size_t kGemmSmemBudget = 227 * 1024;  // sm_100 opt-in maximum per CTA
 constexpr int kSliceCols = 64;                  // epilogue staging slice width
 constexpr int kStageBytesPerWarp = 32 * kSliceCols * 2;
@@ -76,7 +77,7 @@ struct GemmArgs {
   int k_blocks;              // K / 64
   int bn;                    // N per tile: multiple of 16, 16..256
   int stages;
-  uint32_t tmem_cols;        // per accumulator buffer: power of two >= max(32, bn); two buffers
+  uint32_t tmem_cols;        // per accumulator buffer: power of two >= max(32, bn)
   int n_tiles;               // N tiles per M tile (set by launch_gemm)
   int groups;                // B groups (bounds check of the tile table)
   int gather;                // 1: A rows gathered through gather_idx with cp.async (a_base/lda)

@@ -147,22 +147,26 @@ __global__ void __launch_bounds__(kRouteRows) route_select_kernel(const RouteArg
     if (tie) {
       const int slot = atomicAdd(a.tie_count, 1);
       a.tie_rows[slot] = static_cast<int>(grow);
-    } else {
-      uint16_t sel[K1MAX];
-      uint16_t wts[K1MAX];
-#pragma unroll
-      for (int j = 0; j < K1MAX; ++j) {
-        if (j < k) {
-          const int id = static_cast<int>(best[j] & 0xFFFFu);
-          a.ids[grow * k + j] = id;
-          sel[j] = row[id];
-        }
-      }
-      routing_softmax(sel, k, wts);
-#pragma unroll
-      for (int j = 0; j < K1MAX; ++j)
-        if (j < k) a.weights[grow * k + j] = wts[j];
     }
+    // The weights depend only on the selected scores in ascending order, which
+    // a tie does not change (only which of several equal-score experts is
+    // chosen), so they are final for tie rows too.  With a resident mask a
+    // selected non-resident expert would carry its unmasked score; the tie
+    // replay recomputes the weights in that configuration.
+    uint16_t sel[K1MAX];
+    uint16_t wts[K1MAX];
+#pragma unroll
+    for (int j = 0; j < K1MAX; ++j) {
+      if (j < k) {
+        const int id = static_cast<int>(best[j] & 0xFFFFu);
+        if (!tie) a.ids[grow * k + j] = id;
+        sel[j] = row[id];
+      }
+    }
+    routing_softmax(sel, k, wts);
+#pragma unroll
+    for (int j = 0; j < K1MAX; ++j)
+      if (j < k) a.weights[grow * k + j] = wts[j];
   }
 
   // ---- load-balance partials: sum over this CTA's rows of
@@ -283,9 +287,25 @@ __device__ void warp_topk_cpu_order(uint32_t* v, int n, int k, uint16_t* lpos, u
     else
       hi = cut;
   }
-  if (lane == 0) {
-    if (!by_heap) exact::insertion_sort(v, lo, hi);
-    exact::intro_sort(v, k - 1);
+  if (lane == 0 && !by_heap) exact::insertion_sort(v, lo, hi);
+  __syncwarp();
+  const int m = k - 1;
+  if (m <= 16) {
+    // std::sort of at most 16 elements is a plain insertion sort, i.e. a
+    // stable sort: every lane ranks one element (earlier equal ones first).
+    uint32_t x = 0;
+    int rank = 0;
+    if (lane < m) {
+      x = v[lane];
+      for (int i = 0; i < m; ++i) {
+        const uint32_t y = v[i];
+        rank += (exact::before(y, x) || (i < lane && !exact::before(x, y))) ? 1 : 0;
+      }
+    }
+    __syncwarp();
+    if (lane < m) v[rank] = x;
+  } else if (lane == 0) {
+    exact::intro_sort(v, m);
   }
   __syncwarp();
 }
@@ -311,7 +331,7 @@ __global__ void __launch_bounds__(kTieWarps * 32) route_ties_kernel(const RouteA
     __syncwarp();
     warp_topk_cpu_order(v, E, k, lpos, rpos, lane);
     if (lane < k) a.ids[row * k + lane] = static_cast<int64_t>(v[lane] & 0xFFFFu);
-    if (lane == 0) {
+    if (lane == 0 && a.resident != nullptr) {  // otherwise route_select's weights are exact
       uint16_t sel[kMaxTopK];
       uint16_t wts[kMaxTopK];
       for (int j = 0; j < k; ++j) sel[j] = s[v[j] & 0xFFFFu];
