@@ -20,6 +20,12 @@
  *   spx_pack_weights   derived cache of the state_dict layout
  *                                                        experts/bank.py:52-54, nn/ffn.py:16-18
  *   spx_softplus_table F.softplus on every BF16 input    experts/router.py:56
+ *   spx_pack_weights_mxfp8  MXFP8 packing of the expert masters (the weight side
+ *                      of _mxfp8_mm_nt)                  experts/native.py:113-140
+ *   spx_mxfp8_quantize_rows _mx_quantize_rows (MXTensor.to_mx, E4M3, block 32,
+ *                      RCEIL)                            experts/native.py:91-110
+ *   spx_mxfp8_mm_nt    _mxfp8_mm_nt (left @ right_rows.T, both MXFP8, BF16 out)
+ *                                                        experts/native.py:113-140
  */
 #ifndef SPX_H_
 #define SPX_H_
@@ -31,7 +37,7 @@
 extern "C" {
 #endif
 
-#define SPX_ABI_VERSION 1
+#define SPX_ABI_VERSION 2
 
 #define SPX_OK 0
 #define SPX_ERR_INVALID_ARG -1
@@ -54,6 +60,8 @@ typedef struct spx_layer_dims {
   int32_t top_k;           /* k, active experts per token (1..20, <= E)          */
   int32_t score_transform; /* 0 = softplus, 1 = identity (router_score_transform) */
   int32_t execution_loop;  /* 1 = telemetry of expert_execution="loop"          */
+  int32_t mxfp8_lane;      /* 1 = some experts may run the MXFP8 lane: the workspace
+                              then holds quantised activations (I % 32 == 0)  */
 } spx_layer_dims;
 
 /* The reference state_dict tensors (BF16), unchanged layouts. */
@@ -68,13 +76,18 @@ typedef struct spx_reference_weights {
   const uint16_t* shared_down;   /* shared.down_projection.weight [d, S] | NULL */
 } spx_reference_weights;
 
-/* Element counts (uint16_t) of the packed weight buffers. */
+/* Element counts (uint16_t) of the packed weight buffers; the *_mx fields
+ * are BYTES of the MXFP8 copies (zero unless dims->mxfp8_lane). */
 typedef struct spx_packed_sizes {
   size_t router_weight;
   size_t expert_w1;
   size_t expert_w2;
   size_t shared_w1;
   size_t shared_w2;
+  size_t expert_w1_mx;        /* E4M3 [E, 2I, round_up(d, 128)]                  */
+  size_t expert_w1_mx_scales; /* E8M0 scale atoms of expert_w1_mx                */
+  size_t expert_w2_mx;        /* E4M3 [E, d, round_up(I, 128)]                   */
+  size_t expert_w2_mx_scales; /* E8M0 scale atoms of expert_w2_mx                */
 } spx_packed_sizes;
 
 typedef struct spx_packed_weights {
@@ -86,6 +99,14 @@ typedef struct spx_packed_weights {
   const uint16_t* shared_w2;
   const uint16_t* softplus_table; /* [65536]; required for score_transform 0   */
   const uint8_t* resident_mask;   /* [E] (0/1) | NULL = full pool              */
+  /* MXFP8 lane (dims->mxfp8_lane): per-expert kernel lane and the copies made
+   * by spx_pack_weights_mxfp8.  expert_lane_mxfp8[e] = 1 runs expert e as
+   * ("mxfp8", "mxfp8") -- MicroExpertBank._execution_pair, experts/bank.py:462-475. */
+  const uint8_t* expert_lane_mxfp8; /* [E] (0/1) | NULL = every expert BF16 */
+  const uint8_t* expert_w1_mx;
+  const uint8_t* expert_w1_mx_scales;
+  const uint8_t* expert_w2_mx;
+  const uint8_t* expert_w2_mx_scales;
 } spx_packed_weights;
 
 typedef struct spx_layer_outputs {
@@ -126,6 +147,29 @@ int spx_softplus_table(uint16_t* table, void* stream);
 int spx_pack_weights(const spx_layer_dims* dims, const spx_reference_weights* src,
                      uint16_t* router_weight, uint16_t* expert_w1, uint16_t* expert_w2,
                      uint16_t* shared_w1, uint16_t* shared_w2, void* stream);
+
+/* Quantise the expert masters for the MXFP8 lane (dims->mxfp8_lane = 1):
+ * gate/up/down from the reference layouts into E4M3 copies with E8M0 scale
+ * atoms (sizes from spx_layer_sizes).  Returns SPX_ERR_UNSUPPORTED when
+ * inter_dim % 32 != 0. */
+int spx_pack_weights_mxfp8(const spx_layer_dims* dims, const spx_reference_weights* src, uint8_t* expert_w1_mx,
+                           uint8_t* expert_w1_mx_scales, uint8_t* expert_w2_mx, uint8_t* expert_w2_mx_scales,
+                           void* stream);
+
+/* MXFP8 quantisation of BF16 rows [rows, cols] along cols (cols % 32 == 0):
+ * values[rows, cols] E4M3, scales[rows, cols / 32] E8M0 (RCEIL: byte =
+ * clamp(ceil(log2(amax / 448)), -127, 127) + 127, multiplier 1 for byte 0). */
+int spx_mxfp8_quantize_rows(const uint16_t* src, int64_t rows, int32_t cols, uint8_t* values, uint8_t* scales,
+                            void* stream);
+
+/* Workspace bytes of spx_mxfp8_mm_nt for the given shape. Host-only. */
+size_t spx_mxfp8_mm_workspace(int64_t m, int64_t n, int64_t k);
+
+/* out[m, n] = bf16(mx(left[m, k]) @ mx(right_rows[n, k]).T), FP32 accumulation
+ * on the block-scaled tensor cores; K is zero-padded to a multiple of 128 as
+ * in the reference.  BF16 inputs row-major, output row-major [m, n]. */
+int spx_mxfp8_mm_nt(const uint16_t* left, const uint16_t* right_rows, int64_t m, int64_t n, int64_t k,
+                    uint16_t* out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Scores, top-k ids and routing weights from given BF16 router logits [T, E]. */
 int spx_route(const spx_layer_dims* dims, const uint16_t* logits, const uint16_t* softplus_table,

@@ -156,6 +156,21 @@ def _swiglu_rows(x_bits, gate_f32, up_f32, down_f32):
     return bf16_matmul(h, down_f32)
 
 
+def _swiglu_rows_mxfp8(x_bits, gate_io_bits, up_io_bits, down_io_bits):
+    """``MicroExpertBank.expert_forward`` for the ("mxfp8", "mxfp8") pair (experts/bank.py:408-461).
+
+    Each projection is ``native_expert_matmul(v, W)`` = ``_mxfp8_mm_nt(v, W.T)``
+    (experts/native.py:113-140, 305-350): both operands quantised row-wise along K.
+    """
+
+    from oracle.mxfp8 import mxfp8_matmul_bits
+
+    g = mxfp8_matmul_bits(x_bits, np.ascontiguousarray(gate_io_bits.T))
+    u = mxfp8_matmul_bits(x_bits, np.ascontiguousarray(up_io_bits.T))
+    h = f32_to_bf16_bits(bf16_bits_to_f32(_silu_bf16(g)) * bf16_bits_to_f32(u))
+    return mxfp8_matmul_bits(h, np.ascontiguousarray(down_io_bits.T))
+
+
 def _next_pow2(n: np.ndarray) -> np.ndarray:
     out = np.ones_like(n)
     pos = n > 1
@@ -164,14 +179,17 @@ def _next_pow2(n: np.ndarray) -> np.ndarray:
 
 
 def grouped_experts(x_bits: np.ndarray, expert_ids: np.ndarray, weight_bits: np.ndarray,
-                    gate_bits: np.ndarray, up_bits: np.ndarray, down_bits: np.ndarray):
+                    gate_bits: np.ndarray, up_bits: np.ndarray, down_bits: np.ndarray,
+                    lane_mx: np.ndarray | None = None, execution: str = "grouped"):
     """``MicroExpertBank._execute_grouped`` (``experts/bank.py:705-779``).
 
     ``x_bits [T,d]``, ``expert_ids [T,k]``, ``weight_bits [T,k]``; expert stacks
     ``gate/up [E,d,I]``, ``down [E,I,d]`` (BF16 bits).  Returns the routed
     update ``[T,d]`` (BF16 bits), reduced in the reference's ``index_add`` order
-    (buckets by padded capacity, then expert id, then sorted pair order) with a
-    BF16 rounding after every addition.
+    (buckets by padded capacity, then expert id, then sorted pair order; or
+    ascending expert id for ``execution="loop"``, bank.py:674-701) with a BF16
+    rounding after every addition.  ``lane_mx[e]`` selects the MXFP8 pair for
+    expert e (``_execution_pair``, bank.py:462-475).
     """
 
     T, d = x_bits.shape
@@ -187,16 +205,19 @@ def grouped_experts(x_bits: np.ndarray, expert_ids: np.ndarray, weight_bits: np.
     for e in np.nonzero(counts)[0]:
         rows = order[starts[e]: starts[e] + counts[e]]
         tokens = rows // k
-        y = _swiglu_rows(
-            x_bits[tokens],
-            bf16_bits_to_f32(gate_bits[e]),
-            bf16_bits_to_f32(up_bits[e]),
-            bf16_bits_to_f32(down_bits[e]),
-        )
+        if lane_mx is not None and lane_mx[e]:
+            y = _swiglu_rows_mxfp8(x_bits[tokens], gate_bits[e], up_bits[e], down_bits[e])
+        else:
+            y = _swiglu_rows(
+                x_bits[tokens],
+                bf16_bits_to_f32(gate_bits[e]),
+                bf16_bits_to_f32(up_bits[e]),
+                bf16_bits_to_f32(down_bits[e]),
+            )
         # _weighted_expert_updates (bank.py:970-978): bf16(out) * bf16(w)
         weighted[rows] = round_bf16(bf16_bits_to_f32(y) * w_bf[rows][:, None])
     # index_add order per token: key (capacity(e), e) over the token's k slots.
-    cap = _next_pow2(counts)
+    cap = _next_pow2(counts) if execution == "grouped" else np.zeros_like(counts)
     slot_e = ids.reshape(T, k)
     key = cap[slot_e] * (E + 1) + slot_e
     seq = np.argsort(key, axis=1, kind="stable")
@@ -263,11 +284,13 @@ class LayerParams:
 
 def mixer_forward(params: LayerParams, x_bits: np.ndarray, k: int, *,
                   resident_mask: np.ndarray | None = None, transform: str = "softplus",
-                  logit_bits: np.ndarray | None = None) -> dict:
+                  logit_bits: np.ndarray | None = None, lane_mx: np.ndarray | None = None,
+                  execution: str = "grouped") -> dict:
     """``MicroExpertChannelMixer.forward`` of ``experts/mixer.py:145-241``.
 
     ``x_bits [T,d]``.  ``logit_bits`` injects router logits (the bit-exact
-    routing contract is stated "given identical logits").
+    routing contract is stated "given identical logits").  ``lane_mx [E]``
+    marks experts executed in MXFP8.
     """
 
     T, d = x_bits.shape
@@ -276,7 +299,8 @@ def mixer_forward(params: LayerParams, x_bits: np.ndarray, k: int, *,
         logit_bits = router_logits(x_bits, params.router_w, params.router_b)
     scores = router_scores(logit_bits, transform)
     ids, weights = select_least_surprised(scores, k, resident_mask)
-    routed, order, counts = grouped_experts(x_bits, ids, weights, params.gate, params.up, params.down)
+    routed, order, counts = grouped_experts(x_bits, ids, weights, params.gate, params.up, params.down,
+                                            lane_mx=lane_mx, execution=execution)
     if params.shared_gate is not None:
         shared = shared_swiglu(x_bits, params.shared_gate, params.shared_up, params.shared_down)
         update = f32_to_bf16_bits(bf16_bits_to_f32(routed) + bf16_bits_to_f32(shared))
@@ -297,7 +321,7 @@ def mixer_forward(params: LayerParams, x_bits: np.ndarray, k: int, *,
         "auxiliary_loss": load_balance_loss(scores, ids, resident_mask),
         "expert_utilization": util,
         "num_active_experts": int((util > 0).sum()),
-        **execution_metrics(ids, E),
+        **execution_metrics(ids, E, execution),
     }
 
 

@@ -37,7 +37,13 @@ EXPORTED = (
     "spx_layer_forward",
     "spx_workspace_status",
     "spx_dispatch_static",
+    "spx_pack_weights_mxfp8",
+    "spx_mxfp8_quantize_rows",
+    "spx_mxfp8_mm_workspace",
+    "spx_mxfp8_mm_nt",
 )
+
+ABI_VERSION = 2
 
 _vp = ctypes.c_void_p
 
@@ -52,6 +58,7 @@ class LayerDims(ctypes.Structure):
         ("top_k", ctypes.c_int32),
         ("score_transform", ctypes.c_int32),
         ("execution_loop", ctypes.c_int32),
+        ("mxfp8_lane", ctypes.c_int32),
     ]
 
 
@@ -75,6 +82,10 @@ class PackedSizes(ctypes.Structure):
         ("expert_w2", ctypes.c_size_t),
         ("shared_w1", ctypes.c_size_t),
         ("shared_w2", ctypes.c_size_t),
+        ("expert_w1_mx", ctypes.c_size_t),
+        ("expert_w1_mx_scales", ctypes.c_size_t),
+        ("expert_w2_mx", ctypes.c_size_t),
+        ("expert_w2_mx_scales", ctypes.c_size_t),
     ]
 
 
@@ -88,6 +99,11 @@ class PackedWeights(ctypes.Structure):
         ("shared_w2", _vp),
         ("softplus_table", _vp),
         ("resident_mask", _vp),
+        ("expert_lane_mxfp8", _vp),
+        ("expert_w1_mx", _vp),
+        ("expert_w1_mx_scales", _vp),
+        ("expert_w2_mx", _vp),
+        ("expert_w2_mx_scales", _vp),
     ]
 
 
@@ -150,13 +166,20 @@ def load() -> ctypes.CDLL:
         ),
         "spx_workspace_status": (ctypes.c_int, [_vp, P(ctypes.c_int), ctypes.c_int, _vp]),
         "spx_dispatch_static": (ctypes.c_int, [P(LayerDims), _vp, _vp, _vp, _vp]),
+        "spx_pack_weights_mxfp8": (ctypes.c_int, [P(LayerDims), P(ReferenceWeights), _vp, _vp, _vp, _vp, _vp]),
+        "spx_mxfp8_quantize_rows": (ctypes.c_int, [_vp, ctypes.c_int64, ctypes.c_int32, _vp, _vp, _vp]),
+        "spx_mxfp8_mm_workspace": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]),
+        "spx_mxfp8_mm_nt": (
+            ctypes.c_int,
+            [_vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp, _vp, ctypes.c_size_t, _vp],
+        ),
     }
     for name, (restype, argtypes) in sig.items():
         fn = getattr(lib, name)
         fn.restype = restype
         fn.argtypes = argtypes
-    if lib.spx_abi_version() != 1:
-        raise SpxError(f"libspx ABI version {lib.spx_abi_version()} != 1")
+    if lib.spx_abi_version() != ABI_VERSION:
+        raise SpxError(f"libspx ABI version {lib.spx_abi_version()} != {ABI_VERSION}")
     _lib = lib
     return lib
 

@@ -33,6 +33,12 @@ struct Shape {
   int bn_router, gn_router;
   int bn_d, gn_d;
   int lb_blocks, nchunks, max_tiles;
+  // MXFP8 lane
+  bool mx;
+  int kx;             // GEMM1 K in bytes (d padded to 128)
+  int cm, ncm;        // GEMM1 chunk (N tile = 2*cm) and chunks
+  int kh;             // hidden width in bytes (I padded to 128) = GEMM2 K
+  int bn2m, gn2m;     // GEMM2 N tile and tiles
 };
 
 int make_shape(const spx_layer_dims* dm, Shape* s) {
@@ -65,12 +71,42 @@ int make_shape(const spx_layer_dims* dm, Shape* s) {
   s->lb_blocks = ceil_div(s->T, kRouteRows);
   s->nchunks = ceil_div(s->P, kDispatchChunk);
   s->max_tiles = ceil_div(s->P, kTileRows) + s->E;
+  s->mx = dm->mxfp8_lane != 0;
+  if (s->mx) {
+    if (s->I % kMxBlock != 0) return SPX_ERR_UNSUPPORTED;
+    s->kx = round_up_i(s->d, 128);
+    s->cm = (s->I % 64 == 0) ? 64 : 32;
+    s->ncm = s->I / s->cm;
+    s->kh = round_up_i(s->I, 128);
+    s->bn2m = std::min(kMxMaxBn, round_up_i(s->d, 16));
+    s->gn2m = ceil_div(s->d, s->bn2m);
+  } else {
+    s->kx = s->cm = s->ncm = s->kh = s->bn2m = s->gn2m = 0;
+  }
   return SPX_OK;
+}
+
+// Byte sizes of the MXFP8 weight copies.
+struct MxPackSizes {
+  size_t w1, w1_sf, w2, w2_sf;
+};
+
+MxPackSizes mx_pack_sizes(const Shape& s) {
+  MxPackSizes z{};
+  if (!s.mx) return z;
+  const int rows1 = s.ncm * 2 * s.cm;
+  z.w1 = static_cast<size_t>(s.E) * rows1 * s.kx;
+  z.w1_sf = mx_atoms_bytes(s.E, rows1, s.kx, 2 * s.cm);
+  z.w2 = static_cast<size_t>(s.E) * s.d * s.kh;
+  z.w2_sf = mx_atoms_bytes(s.E, s.d, s.kh, s.bn2m);
+  return z;
 }
 
 struct Layout {
   size_t small, tie_rows, lb_partial, chunk_hist, counts, starts, tiles, order, src_row, sorted_w;
-  size_t hidden, y, shared_hidden, logits, x_pad, util, stats, ratios, aux, total;
+  size_t hidden, y, shared_hidden, logits, x_pad, util, stats, ratios, aux;
+  size_t x_q, x_sf, h_q, h_sf, tiles_mx;  // MXFP8 lane (empty otherwise)
+  size_t total;
 };
 
 Layout make_layout(const Shape& s) {
@@ -100,6 +136,11 @@ Layout make_layout(const Shape& s) {
   L.stats = take(sizeof(long long) * 6);
   L.ratios = take(sizeof(float) * 2);
   L.aux = take(sizeof(uint16_t) * 2);
+  L.x_q = take(s.mx ? static_cast<size_t>(s.T) * s.kx : 0);
+  L.x_sf = take(s.mx ? static_cast<size_t>(s.T) * (s.kx / kMxBlock) : 0);
+  L.h_q = take(s.mx ? static_cast<size_t>(s.P) * s.kh : 0);
+  L.h_sf = take(s.mx ? static_cast<size_t>(s.P) * (s.kh / kMxBlock) : 0);
+  L.tiles_mx = take(s.mx ? sizeof(int4) * static_cast<size_t>(s.max_tiles) : 0);
   L.total = off;
   return L;
 }
@@ -113,11 +154,11 @@ int sm_count() { return device_sm_count(); }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-GemmArgs base_args(int bn, int k_blocks, int* status) {
+GemmArgs base_args(int bn, int k_blocks, int* status, bool mx = false) {
   GemmArgs g{};
   g.bn = bn;
   g.k_blocks = k_blocks;
-  g.stages = gemm_pick_stages(bn, k_blocks);
+  g.stages = gemm_pick_stages(bn, k_blocks, mx);
   g.tmem_cols = pow2_at_least(static_cast<uint32_t>(bn));
   g.groups = 1;
   g.status = status;
@@ -211,6 +252,11 @@ int spx_layer_sizes(const spx_layer_dims* dims, size_t* workspace_bytes, spx_pac
   if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
   if (workspace_bytes != nullptr) *workspace_bytes = make_layout(s).total;
   if (packed != nullptr) {
+    const MxPackSizes z = mx_pack_sizes(s);
+    packed->expert_w1_mx = z.w1;
+    packed->expert_w1_mx_scales = z.w1_sf;
+    packed->expert_w2_mx = z.w2;
+    packed->expert_w2_mx_scales = z.w2_sf;
     packed->router_weight = static_cast<size_t>(s.E) * s.kd;
     packed->expert_w1 = static_cast<size_t>(s.E) * s.nc * 2 * s.c * s.kd;
     packed->expert_w2 = static_cast<size_t>(s.E) * s.d * s.kp;
@@ -246,6 +292,106 @@ int spx_pack_weights(const spx_layer_dims* dims, const spx_reference_weights* sr
     if (rc == SPX_OK) rc = launch_pack_w2(src->shared_down, 1, s.S, s.d, s.ksp, 1, shared_w2, st);
   }
   return rc;
+}
+
+int spx_pack_weights_mxfp8(const spx_layer_dims* dims, const spx_reference_weights* src, uint8_t* expert_w1_mx,
+                           uint8_t* expert_w1_mx_scales, uint8_t* expert_w2_mx, uint8_t* expert_w2_mx_scales,
+                           void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (!s.mx) return SPX_ERR_INVALID_ARG;
+  if (src == nullptr || src->gate_proj == nullptr || src->up_proj == nullptr || src->down_proj == nullptr ||
+      expert_w1_mx == nullptr || expert_w1_mx_scales == nullptr || expert_w2_mx == nullptr ||
+      expert_w2_mx_scales == nullptr)
+    return SPX_ERR_INVALID_ARG;
+  if (!aligned16(expert_w1_mx) || !aligned16(expert_w2_mx) || !aligned16(expert_w1_mx_scales) ||
+      !aligned16(expert_w2_mx_scales))
+    return SPX_ERR_ALIGNMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int rows1 = s.ncm * 2 * s.cm;
+  int rc = launch_mx_quantize_b(kMxSrcW1, src->gate_proj, src->up_proj, s.E, rows1, rows1, s.d, s.kx, 2 * s.cm, s.d,
+                                s.I, s.cm, 0, expert_w1_mx, expert_w1_mx_scales, st);
+  if (rc == SPX_OK)
+    rc = launch_mx_quantize_b(kMxSrcW2, src->down_proj, nullptr, s.E, s.d, s.d, s.I, s.kh, s.bn2m, s.d, s.I, 0, 0,
+                              expert_w2_mx, expert_w2_mx_scales, st);
+  return rc;
+}
+
+int spx_mxfp8_quantize_rows(const uint16_t* src, int64_t rows, int32_t cols, uint8_t* values, uint8_t* scales,
+                            void* stream) {
+  if (rows < 0 || cols <= 0 || cols % kMxBlock != 0) return SPX_ERR_INVALID_ARG;
+  if (rows == 0) return SPX_OK;
+  if (src == nullptr || values == nullptr || scales == nullptr) return SPX_ERR_INVALID_ARG;
+  return launch_mx_quantize_rows(src, rows, cols, cols, cols, values, cols, scales, cols / kMxBlock,
+                                 static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+struct MmLayout {
+  int64_t kp;
+  int bn;
+  size_t status, lq, lsf, rq, rsf, total;
+};
+
+MmLayout mm_layout(int64_t m, int64_t n, int64_t k) {
+  MmLayout L{};
+  L.kp = static_cast<int64_t>(round_up(static_cast<size_t>(k > 0 ? k : 1), 128));
+  L.bn = static_cast<int>(std::min<int64_t>(kMxMaxBn, static_cast<int64_t>(round_up(static_cast<size_t>(n), 16))));
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = round_up(off + bytes, kAlign);
+    return at;
+  };
+  L.status = take(64);
+  L.lq = take(static_cast<size_t>(m) * L.kp);
+  L.lsf = take(static_cast<size_t>(m) * (L.kp / kMxBlock));
+  L.rq = take(static_cast<size_t>(n) * L.kp);
+  L.rsf = take(mx_atoms_bytes(1, static_cast<int>(n), static_cast<int>(L.kp), L.bn));
+  L.total = off;
+  return L;
+}
+}  // namespace
+
+size_t spx_mxfp8_mm_workspace(int64_t m, int64_t n, int64_t k) {
+  if (m < 0 || n < 0 || k < 0) return 0;
+  return mm_layout(m, n, k).total;
+}
+
+int spx_mxfp8_mm_nt(const uint16_t* left, const uint16_t* right_rows, int64_t m, int64_t n, int64_t k,
+                    uint16_t* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (m < 0 || n < 0 || k < 0) return SPX_ERR_INVALID_ARG;
+  if (m == 0 || n == 0) return SPX_OK;
+  if (out == nullptr) return SPX_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (k == 0)  // empty contraction: zeros, as the reference's new_zeros
+    return cudaMemsetAsync(out, 0, static_cast<size_t>(m) * n * 2, st) == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+  if (left == nullptr || right_rows == nullptr) return SPX_ERR_INVALID_ARG;
+  if (m > (int64_t(1) << 31) - 1 || n > (int64_t(1) << 31) - 1 || k > (int64_t(1) << 30)) return SPX_ERR_UNSUPPORTED;
+  const MmLayout L = mm_layout(m, n, k);
+  if (workspace == nullptr || workspace_bytes < L.total) return SPX_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return SPX_ERR_ALIGNMENT;
+  uint8_t* lq = at<uint8_t>(workspace, L.lq);
+  uint8_t* lsf = at<uint8_t>(workspace, L.lsf);
+  uint8_t* rq = at<uint8_t>(workspace, L.rq);
+  uint8_t* rsf = at<uint8_t>(workspace, L.rsf);
+  const int kp = static_cast<int>(L.kp);
+  int rc = launch_mx_quantize_rows(left, m, static_cast<int>(k), k, kp, lq, kp, lsf, kp / kMxBlock, st);
+  if (rc == SPX_OK)
+    rc = launch_mx_quantize_b(kMxSrcRows, right_rows, nullptr, 1, static_cast<int>(n), static_cast<int>(n),
+                              static_cast<int>(k), kp, L.bn, 0, 0, 0, k, rq, rsf, st);
+  if (rc != SPX_OK) return rc;
+  GemmArgs g = base_args(L.bn, kp / 128, at<int>(workspace, L.status), true);
+  if ((rc = encode_2d(&g.tma_a, lq, m, kp, kp, kTileRows, 1)) != SPX_OK) return rc;
+  if ((rc = encode_3d(&g.tma_b, rq, 1, n, kp, L.bn, 1)) != SPX_OK) return rc;
+  g.m_rows = static_cast<int>(m);
+  g.n_valid = static_cast<int>(n);
+  g.out = out;
+  g.ldo = n;
+  g.sfa = lsf;
+  g.ld_sfa = kp / kMxBlock;
+  g.sfb = rsf;
+  return launch_gemm(kEpiStore, g, ceil_div(m, kTileRows), ceil_div(n, L.bn), st, true);
 }
 
 int spx_route(const spx_layer_dims* dims, const uint16_t* logits, const uint16_t* softplus_table,
@@ -287,6 +433,12 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   if (w->router_weight == nullptr || w->expert_w1 == nullptr || w->expert_w2 == nullptr) return SPX_ERR_INVALID_ARG;
   if (s.S > 0 && (w->shared_w1 == nullptr || w->shared_w2 == nullptr)) return SPX_ERR_INVALID_ARG;
   if (dims->score_transform == 0 && w->softplus_table == nullptr) return SPX_ERR_INVALID_ARG;
+  if (w->expert_lane_mxfp8 != nullptr) {
+    if (!s.mx) return SPX_ERR_INVALID_ARG;  // the workspace has no MXFP8 regions
+    if (w->expert_w1_mx == nullptr || w->expert_w1_mx_scales == nullptr || w->expert_w2_mx == nullptr ||
+        w->expert_w2_mx_scales == nullptr)
+      return SPX_ERR_INVALID_ARG;
+  }
   if (!aligned16(hidden) || !aligned16(out->update) || !aligned16(workspace)) return SPX_ERR_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const Layout L = make_layout(s);
@@ -340,8 +492,24 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   da.execution_loop = dims->execution_loop;
   da.pair_weights = out->routing_weights;
   da.sorted_weights = at<uint16_t>(workspace, L.sorted_w);
+  const bool mx = s.mx && w->expert_lane_mxfp8 != nullptr;
+  if (mx) {
+    da.lane_mx = w->expert_lane_mxfp8;
+    da.tiles_mx = at<int4>(workspace, L.tiles_mx);
+    da.num_tiles_mx = at<int>(workspace, L.small) + 3;
+  }
   if ((rc = launch_dispatch(da, st)) != SPX_OK) return rc;
   mark(3);
+  uint8_t* xq = at<uint8_t>(workspace, L.x_q);
+  uint8_t* xsf = at<uint8_t>(workspace, L.x_sf);
+  uint8_t* hq = at<uint8_t>(workspace, L.h_q);
+  uint8_t* hsf = at<uint8_t>(workspace, L.h_sf);
+  if (mx) {
+    // Hidden states of the MXFP8 lane: E4M3 rows with their block scales
+    // (per token, so every expert's gathered rows share them).
+    if ((rc = launch_mx_quantize_rows(hidden, s.T, s.d, s.d, s.kx, xq, s.kx, xsf, s.kx / kMxBlock, st)) != SPX_OK)
+      return rc;
+  }
 
   uint16_t* hid = at<uint16_t>(workspace, L.hidden);
   uint16_t* y = at<uint16_t>(workspace, L.y);
@@ -354,8 +522,8 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
     g.groups = s.E;
     g.gather = 1;
     g.gather_idx = da.src_row;
-    g.a_base = xa;
-    g.lda = s.kd;
+    g.a_base = reinterpret_cast<const uint8_t*>(xa);
+    g.lda = 2 * static_cast<int64_t>(s.kd);
     g.tiles = da.tiles;
     g.num_tiles = da.num_tiles;
     g.chunk = s.c;
@@ -363,6 +531,30 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
     g.out = hid;
     g.ldo = s.kp;
     if ((rc = launch_gemm(kEpiSwiglu, g, s.max_tiles, s.nc, st)) != SPX_OK) return rc;
+  }
+  if (mx) {
+    // MXFP8-lane experts: block-scaled GEMM1, hidden written quantised.
+    GemmArgs g = base_args(2 * s.cm, s.kx / 128, status, true);
+    if ((rc = encode_3d(&g.tma_b, w->expert_w1_mx, s.E, static_cast<int64_t>(s.ncm) * 2 * s.cm, s.kx, 2 * s.cm,
+                        1)) != SPX_OK)
+      return rc;
+    g.groups = s.E;
+    g.gather = 1;
+    g.gather_idx = da.src_row;
+    g.a_base = xq;
+    g.lda = s.kx;
+    g.sfa = xsf;
+    g.ld_sfa = s.kx / kMxBlock;
+    g.sfb = w->expert_w1_mx_scales;
+    g.tiles = da.tiles_mx;
+    g.num_tiles = da.num_tiles_mx;
+    g.chunk = s.cm;
+    g.h_cols = s.kh;
+    g.out = hq;
+    g.ldo = s.kh;
+    g.out_sf = hsf;
+    g.ld_out_sf = s.kh / kMxBlock;
+    if ((rc = launch_gemm(kEpiSwiglu, g, s.max_tiles, s.ncm, st, true)) != SPX_OK) return rc;
   }
   mark(4);
   // ---- K3b: expert GEMM2, scaled by the routing weight, scattered to pair order
@@ -379,6 +571,23 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
     g.pos_to_pair = da.order;
     g.pos_weight = da.sorted_weights;
     if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn_d, st)) != SPX_OK) return rc;
+  }
+  if (mx) {
+    GemmArgs g = base_args(s.bn2m, s.kh / 128, status, true);
+    if ((rc = encode_2d(&g.tma_a, hq, s.P, s.kh, s.kh, kTileRows, 1)) != SPX_OK) return rc;
+    if ((rc = encode_3d(&g.tma_b, w->expert_w2_mx, s.E, s.d, s.kh, s.bn2m, 1)) != SPX_OK) return rc;
+    g.groups = s.E;
+    g.tiles = da.tiles_mx;
+    g.num_tiles = da.num_tiles_mx;
+    g.sfa = hsf;
+    g.ld_sfa = s.kh / kMxBlock;
+    g.sfb = w->expert_w2_mx_scales;
+    g.n_valid = s.d;
+    g.out = y;
+    g.ldo = s.d;
+    g.pos_to_pair = da.order;
+    g.pos_weight = da.sorted_weights;
+    if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn2m, st, true)) != SPX_OK) return rc;
   }
   mark(5);
   // ---- K4: shared SwiGLU with the combine fused into its down projection

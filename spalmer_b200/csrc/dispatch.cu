@@ -53,6 +53,7 @@ __device__ __forceinline__ int64_t next_pow2_i64(int64_t n) {
 
 __global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs a) {
   __shared__ int s_scan[1024];
+  __shared__ unsigned long long s_scan64[1024];
   __shared__ float s_red[1024];
   __shared__ long long s_i64[4];
   __shared__ int s_count[1024];
@@ -107,22 +108,32 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs 
   }
   const int start = s_scan[threadIdx.x] - ((e < E) ? count : 0);
   __syncthreads();
-  s_scan[threadIdx.x] = (e < E) ? tiles : 0;
+  // Tile starts of the two lanes in one scan: BF16-lane tiles in the low
+  // 32 bits, MXFP8-lane tiles in the high 32 bits.
+  const bool mx = (e < E) && a.lane_mx != nullptr && a.lane_mx[e] != 0;
+  const unsigned long long mine =
+      (e < E) ? (mx ? (static_cast<unsigned long long>(tiles) << 32) : static_cast<unsigned long long>(tiles)) : 0ull;
+  s_scan64[threadIdx.x] = mine;
   __syncthreads();
   for (int off = 1; off < 1024; off <<= 1) {
-    const int v = threadIdx.x >= off ? s_scan[threadIdx.x - off] : 0;
+    const unsigned long long v = threadIdx.x >= off ? s_scan64[threadIdx.x - off] : 0ull;
     __syncthreads();
-    s_scan[threadIdx.x] += v;
+    s_scan64[threadIdx.x] += v;
     __syncthreads();
   }
-  const int tile_start = s_scan[threadIdx.x] - ((e < E) ? tiles : 0);
-  if (threadIdx.x == 1023) *a.num_tiles = s_scan[1023];
+  const unsigned long long excl = s_scan64[threadIdx.x] - mine;
+  const int tile_start = mx ? static_cast<int>(excl >> 32) : static_cast<int>(excl & 0xFFFFFFFFull);
+  if (threadIdx.x == 1023) {
+    *a.num_tiles = static_cast<int>(s_scan64[1023] & 0xFFFFFFFFull);
+    if (a.num_tiles_mx != nullptr) *a.num_tiles_mx = static_cast<int>(s_scan64[1023] >> 32);
+  }
   if (e < E) {
     a.counts[e] = count;
     a.starts[e] = start;
+    int4* table = mx ? a.tiles_mx : a.tiles;
     for (int t = 0; t < tiles; ++t) {
       const int r0 = t * kTileRows;
-      a.tiles[tile_start + t] = make_int4(e, start + r0, min(kTileRows, count - r0), 0);
+      table[tile_start + t] = make_int4(e, start + r0, min(kTileRows, count - r0), 0);
     }
   }
 

@@ -21,6 +21,16 @@
 // The BF16 rounding points follow the reference's tensor boundaries
 // (mESmaC/spalmer experts/bank.py:760-763, bank.py:970-978, nn/ffn.py:27-30,
 // experts/mixer.py:207); accumulation is FP32 throughout.
+//
+// MXFP8 lane (template flag MX): E4M3 operands (128 elements = 128 B of K per
+// stage) with E8M0 scales per 32 elements.  The producer also copies one
+// 512-byte scale atom for A (gathered 4-byte words, one per row) and one for
+// B (pre-packed) per stage; the MMA warp moves them to tensor memory with
+// tcgen05.cp and issues kind::mxf8f6f4.block_scale MMAs (K = 32).  TMEM holds
+// three 128-column accumulators and rotating scale slots from column 384.
+// The SwiGLU epilogue of this lane writes the hidden rows already quantised
+// (the reference quantises `silu(g) * u` row-wise before the down
+// projection, experts/native.py:113-140 via bank.py:440-461).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
@@ -28,6 +38,7 @@
 #include <stdint.h>
 
 #include "kernels.h"
+#include "mx.cuh"
 #include "sm100.cuh"
 
 namespace spx {
@@ -195,6 +206,42 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
   }
 }
 
+// MXFP8-lane SwiGLU epilogue: each thread holds 32 hidden values of its row
+// (one scale block) and writes them as E4M3 bytes plus the block's scale byte.
+__device__ __forceinline__ void run_epilogue_swiglu_mx(const GemmArgs& a, uint32_t taddr, int quad, int half,
+                                                       int lane, int row0, int rows, int nt) {
+  const int r = quad * 32 + lane;
+  const bool live = r < rows;
+  uint8_t* hq = static_cast<uint8_t*>(a.out);
+  const int64_t row = static_cast<int64_t>(row0) + r;
+  for (int s0 = half * 32; s0 < a.chunk; s0 += 64) {
+    uint32_t g[32], u[32];
+    tmem_ld32(taddr + s0, g);
+    tmem_ld32(taddr + a.chunk + s0, u);
+    tmem_wait_ld();
+    float h[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      h[j] = bfr(bfr(silu_fast(bfr(__uint_as_float(g[j])))) * bfr(__uint_as_float(u[j])));
+    uint32_t q[8];
+    const uint32_t sb = mx_quantize32(h, q);
+    if (live) {
+      const int col = nt * a.chunk + s0;
+      uint4* dst = reinterpret_cast<uint4*>(hq + row * a.ldo + col);
+      dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
+      dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+      a.out_sf[row * a.ld_out_sf + col / kMxBlock] = static_cast<uint8_t>(sb);
+    }
+  }
+  // Zero the K padding of the quantised hidden row (values and scales).
+  if (half == 0 && live && nt == a.n_tiles - 1) {
+    const int c0 = a.n_tiles * a.chunk;
+    for (int col = c0; col < a.h_cols; col += 16)
+      *reinterpret_cast<uint4*>(hq + row * a.ldo + col) = make_uint4(0u, 0u, 0u, 0u);
+    for (int b = c0 / kMxBlock; b < a.h_cols / kMxBlock; ++b) a.out_sf[row * a.ld_out_sf + b] = 0;
+  }
+}
+
 }  // namespace
 
 // Tile coordinates of linear tile `t` (N tiles fastest, so consecutive tiles
@@ -215,18 +262,24 @@ __device__ __forceinline__ bool decode_tile(const GemmArgs& a, int t, int& group
   return rows > 0;
 }
 
-constexpr int kGatherLag = 2;  // cp.async producer: A stages kept in flight beyond the newest
+constexpr int kGatherLag = 2;  // cp.async producer: stages kept in flight beyond the newest
 
-// Producer warp that gathers A rows with cp.async (each instruction moves 4
-// rows x 128 B, fully coalesced) and loads B with TMA.  full[s] expects two
-// arrivals: lane 0's arrive.expect_tx for B, and lane 0's arrive once the
-// warp's cp.async group for stage s has landed (kGatherLag stages later,
-// after wait_group + fence.proxy.async so the MMA's async-proxy reads see it).
-__device__ __forceinline__ void produce_gather_cp_async(const GemmArgs& a, uint8_t* sa, uint8_t* sb, uint64_t* full,
-                                                        uint64_t* empty, int S, uint32_t a_bytes, uint32_t b_bytes,
-                                                        int total, int lane) {
+// Producer warp for the stages that need the load/store unit: A rows gathered
+// through `gather_idx` (each cp.async instruction moves 4 rows x 128 B, fully
+// coalesced) and, in the MXFP8 lane, the two scale atoms of every stage.  B
+// (and an ungathered A) come by TMA.  full[s] expects two arrivals: lane 0's
+// arrive.expect_tx for the TMA bytes, and lane 0's arrive once the warp's
+// cp.async group for stage s has landed (kGatherLag stages later, after
+// wait_group + fence.proxy.async so the async proxy -- tcgen05.mma and
+// tcgen05.cp -- sees it).
+template <bool MX>
+__device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa, uint8_t* sb, uint8_t* ssf,
+                                                 uint64_t* full, uint64_t* empty, int S, uint32_t a_bytes,
+                                                 uint32_t b_bytes, int total, int lane) {
   const int bn = a.bn;
   const int chunk = lane & 7;
+  const bool gather = a.gather != 0;
+  const uint32_t tx_bytes = b_bytes + (gather ? 0u : a_bytes);
   uint32_t it = 0;
   bool ok = true;
   for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
@@ -236,10 +289,21 @@ __device__ __forceinline__ void produce_gather_cp_async(const GemmArgs& a, uint8
       break;
     }
     int src[32];  // source row of tile row 4*i + (lane >> 3)
+    if (gather) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int rr = 4 * i + (lane >> 3);
-      src[i] = a.gather_idx[row0 + (rr < rows ? rr : 0)];
+      for (int i = 0; i < 32; ++i) {
+        const int rr = 4 * i + (lane >> 3);
+        src[i] = a.gather_idx[row0 + (rr < rows ? rr : 0)];
+      }
+    }
+    int sfr[4];  // MX: source row of tile row lane + 32*j (scale words)
+    if constexpr (MX) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int rr = lane + 32 * j;
+        const int rc = rr < rows ? rr : 0;
+        sfr[j] = gather ? a.gather_idx[row0 + rc] : row0 + rc;
+      }
     }
     const int n0 = nt * bn;
     for (int kb = 0; kb < a.k_blocks; ++kb, ++it) {
@@ -249,8 +313,9 @@ __device__ __forceinline__ void produce_gather_cp_async(const GemmArgs& a, uint8
       if (lane == 0) {
         go = mbar_wait(&empty[s], ph ^ 1u, a.status, SPX_DEV_TIMEOUT_PRODUCER) ? 1 : 0;
         if (go) {
-          mbar_arrive_expect_tx(&full[s], b_bytes);
-          tma_load_3d(sb + s * b_bytes, &a.tma_b, &full[s], kb * 64, n0, group);
+          mbar_arrive_expect_tx(&full[s], tx_bytes);
+          tma_load_3d(sb + s * b_bytes, &a.tma_b, &full[s], kb * 64 * (MX ? 2 : 1), n0, group);
+          if (!gather) tma_load_2d(sa + s * a_bytes, &a.tma_a, &full[s], kb * 64 * (MX ? 2 : 1), row0);
         }
       }
       go = __shfl_sync(0xFFFFFFFFu, go, 0);
@@ -258,13 +323,22 @@ __device__ __forceinline__ void produce_gather_cp_async(const GemmArgs& a, uint8
         ok = false;
         break;
       }
-      const uint32_t dst0 = smem_u32(sa + s * a_bytes);
-      const uint16_t* col = a.a_base + kb * 64 + chunk * 8;
+      if (gather) {
+        const uint32_t dst0 = smem_u32(sa + s * a_bytes);
+        const uint8_t* col = a.a_base + kb * 128 + chunk * 16;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int rr = 4 * i + (lane >> 3);
-        const uint32_t dst = dst0 + (rr >> 3) * 1024 + (rr & 7) * 128 + ((chunk ^ (rr & 7)) << 4);
-        cp_async16(dst, col + static_cast<int64_t>(src[i]) * a.lda);
+        for (int i = 0; i < 32; ++i) {
+          const int rr = 4 * i + (lane >> 3);
+          const uint32_t dst = dst0 + (rr >> 3) * 1024 + (rr & 7) * 128 + ((chunk ^ (rr & 7)) << 4);
+          cp_async16(dst, col + static_cast<int64_t>(src[i]) * a.lda);
+        }
+      }
+      if constexpr (MX) {
+        const uint32_t sf = smem_u32(ssf + s * kMxStageSfBytes);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) cp_async4(sf + lane * 16 + j * 4, a.sfa + sfr[j] * a.ld_sfa + kb * 4);
+        const int64_t atom = (static_cast<int64_t>(group) * a.n_tiles + nt) * a.k_blocks + kb;
+        cp_async16(sf + kMxAtomBytes + lane * 16, a.sfb + atom * kMxAtomBytes + lane * 16);
       }
       cp_async_commit();
       if (it >= static_cast<uint32_t>(kGatherLag)) {
@@ -286,9 +360,9 @@ __device__ __forceinline__ void produce_gather_cp_async(const GemmArgs& a, uint8
 
 // Persistent GEMM: each CTA walks tiles blockIdx.x, blockIdx.x + gridDim.x, ...
 // The TMA producer and the MMA issuer stream k-blocks through the stage ring
-// without stopping at tile boundaries; the accumulator is double-buffered in
+// without stopping at tile boundaries; the accumulator is multi-buffered in
 // TMEM so the epilogue of one tile overlaps the MMAs of the next.
-template <int EPI>
+template <int EPI, bool MX>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ GemmArgs a) {
   extern __shared__ uint8_t gemm_smem_raw[];
   uint8_t* smem = align_1024(gemm_smem_raw);
@@ -298,24 +372,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   const uint32_t b_bytes = static_cast<uint32_t>(bn) * 128u;
   uint8_t* sa = smem;
   uint8_t* sb = smem + S * a_bytes;
-  uint8_t* stage_all = sb + S * b_bytes;  // kGemmEpilogueWarps x kStageBytesPerWarp
+  uint8_t* ssf = sb + S * b_bytes;                           // MX: [S][SFA atom | SFB atom]
+  uint8_t* stage_all = ssf + (MX ? S * kMxStageSfBytes : 0u);  // kGemmEpilogueWarps x kStageBytesPerWarp
   uint64_t* full = reinterpret_cast<uint64_t*>(stage_all + kGemmEpilogueWarps * kStageBytesPerWarp);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;                 // [kMaxAccBufs] accumulator ready
   uint64_t* tempty = tfull + kMaxAccBufs;      // [kMaxAccBufs] accumulator drained
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + kMaxAccBufs);
-  // As many accumulators as fit in the 512 TMEM columns (2 for 256-column tiles).
-  const uint32_t nacc = min(static_cast<uint32_t>(kMaxAccBufs), 512u / a.tmem_cols);
+  // As many accumulators as fit in the 512 TMEM columns (2 for 256-column
+  // tiles); the MXFP8 lane keeps columns 384.. for scale factors.
+  const uint32_t acc_limit = MX ? kMxSfColumn : 512u;
+  const uint32_t nacc = min(static_cast<uint32_t>(kMaxAccBufs), acc_limit / a.tmem_cols);
+  const uint32_t tmem_alloc_cols = MX ? 512u : nacc * a.tmem_cols;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int m_tiles = a.tiles != nullptr ? *a.num_tiles : (a.m_rows + kTileRows - 1) / kTileRows;
   const int total = m_tiles * a.n_tiles;
   if (static_cast<int>(blockIdx.x) >= total) return;
+  const bool ldst_producer = MX || a.gather != 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], a.gather ? 2 : 1);
+      mbar_init(&full[s], ldst_producer ? 2 : 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < kMaxAccBufs; ++b) {
@@ -327,7 +406,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     prefetch_tensormap(&a.tma_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, nacc * a.tmem_cols);
+    tmem_alloc(tmem_slot, tmem_alloc_cols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -335,8 +414,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && a.gather) {
-    produce_gather_cp_async(a, sa, sb, full, empty, S, a_bytes, b_bytes, total, lane);
+  if (warp == 0 && ldst_producer) {
+    produce_cp_async<MX>(a, sa, sb, ssf, full, empty, S, a_bytes, b_bytes, total, lane);
   } else if (warp == 0) {
     // ---------------- TMA producer
     uint32_t it = 0;
@@ -388,10 +467,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
           tc_fence_after();
           const uint32_t a_base = smem_u32(sa + s * a_bytes);
           const uint32_t b_base = smem_u32(sb + s * b_bytes);
+          if constexpr (MX) {
+            // Scales of this stage -> a rotating TMEM slot (tcgen05.cp and the
+            // MMAs that read it are issued in order by this thread).
+            const uint32_t sfa_t = tmem + kMxSfColumn + (it % kMxSfSlots) * 8u;
+            const uint32_t sfb_t = sfa_t + 4u;
+            const uint32_t sf_smem = smem_u32(ssf + s * kMxStageSfBytes);
+            tmem_cp_32x128b_x4(sfa_t, desc_sf_atom(sf_smem));
+            tmem_cp_32x128b_x4(sfb_t, desc_sf_atom(sf_smem + kMxAtomBytes));
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            mma_bf16_ss(acc, desc_kmajor_sw128(a_base + kk * 32), desc_kmajor_sw128(b_base + kk * 32), idesc,
-                        (kb | kk) != 0 ? 1u : 0u);
+            for (uint32_t kk = 0; kk < 4; ++kk) {
+              mma_mxf8_ss(acc, desc_kmajor_sw128(a_base + kk * 32), desc_kmajor_sw128(b_base + kk * 32),
+                          idesc_mxf8(kTileRows, bn, kk, kk), sfa_t | (kk << 30), sfb_t | (kk << 30),
+                          (kb != 0 || kk != 0) ? 1u : 0u);
+            }
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              mma_bf16_ss(acc, desc_kmajor_sw128(a_base + kk * 32), desc_kmajor_sw128(b_base + kk * 32), idesc,
+                          (kb | kk) != 0 ? 1u : 0u);
+            }
           }
           mma_commit(&empty[s]);
         }
@@ -425,9 +520,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       go = __shfl_sync(0xFFFFFFFFu, go, 0);
       if (!go) break;
       tc_fence_after();
-      run_epilogue<EPI>(a, tmem + b * a.tmem_cols + (static_cast<uint32_t>(quad * 32) << 16),
-                        stage_all + (warp - 2) * kStageBytesPerWarp, quad, half, lane, row0, rows, nt * bn, nt,
-                        my_row, my_w);
+      const uint32_t taddr = tmem + b * a.tmem_cols + (static_cast<uint32_t>(quad * 32) << 16);
+      if constexpr (MX && EPI == kEpiSwiglu) {
+        run_epilogue_swiglu_mx(a, taddr, quad, half, lane, row0, rows, nt);
+      } else {
+        run_epilogue<EPI>(a, taddr, stage_all + (warp - 2) * kStageBytesPerWarp, quad, half, lane, row0, rows,
+                          nt * bn, nt, my_row, my_w);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
@@ -437,7 +536,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, nacc * a.tmem_cols);
+    tmem_dealloc(tmem, tmem_alloc_cols);
   }
 }
 
@@ -460,76 +559,101 @@ int get_encoder() {
 
 }  // namespace
 
-// 2-D BF16 tensor [rows, cols] (row pitch `ld` elements), box {64, box_rows}, 128B swizzle.
-int encode_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+// 2-D tensor [rows, cols] (row pitch `ld` elements), box {128 bytes, box_rows}, 128B swizzle.
+int encode_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+              int elem_bytes) {
   if (int rc = get_encoder(); rc != SPX_OK) return rc;
-  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (ld * 2) % 16 != 0) return SPX_ERR_ALIGNMENT;
+  if (elem_bytes != 1 && elem_bytes != 2) return SPX_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (ld * elem_bytes) % 16 != 0) return SPX_ERR_ALIGNMENT;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
-  cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * elem_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / elem_bytes), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1u, 1u};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  const CUtensorMapDataType dt = elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? SPX_OK : SPX_ERR_DRIVER;
 }
 
-// 3-D BF16 tensor [groups, rows, cols], box {64, box_rows, 1}, 128B swizzle.
-int encode_3d(CUtensorMap* map, const void* base, int64_t groups, int64_t rows, int64_t cols, int box_rows) {
+// 3-D tensor [groups, rows, cols], box {128 bytes, box_rows, 1}, 128B swizzle.
+int encode_3d(CUtensorMap* map, const void* base, int64_t groups, int64_t rows, int64_t cols, int box_rows,
+              int elem_bytes) {
   if (int rc = get_encoder(); rc != SPX_OK) return rc;
-  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (cols * 2) % 16 != 0) return SPX_ERR_ALIGNMENT;
+  if (elem_bytes != 1 && elem_bytes != 2) return SPX_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (cols * elem_bytes) % 16 != 0) return SPX_ERR_ALIGNMENT;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
                         static_cast<cuuint64_t>(groups)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols * 2), static_cast<cuuint64_t>(rows * cols * 2)};
-  cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(box_rows), 1u};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols * elem_bytes),
+                           static_cast<cuuint64_t>(rows * cols * elem_bytes)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / elem_bytes), static_cast<cuuint32_t>(box_rows), 1u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+  const CUtensorMapDataType dt = elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  CUresult r = g_encode(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? SPX_OK : SPX_ERR_DRIVER;
 }
 
-size_t gemm_smem_bytes(int bn, int stages) {
-  return 1024 + static_cast<size_t>(stages) * (kTileRows * 128 + static_cast<size_t>(bn) * 128) +
-         kGemmEpilogueWarps * kStageBytesPerWarp + (2 * stages + 2 * kMaxAccBufs) * 8 + 16;
+size_t gemm_smem_bytes(int bn, int stages, bool mx) {
+  const size_t per_stage = kTileRows * 128 + static_cast<size_t>(bn) * 128 + (mx ? kMxStageSfBytes : 0);
+  return 1024 + static_cast<size_t>(stages) * per_stage + kGemmEpilogueWarps * kStageBytesPerWarp +
+         (2 * stages + 2 * kMaxAccBufs) * 8 + 16;
 }
 
 // As many stages as fit: the persistent producer keeps prefetching the next
 // tile's k-blocks, so stages beyond one tile's K still hide load latency.
-int gemm_pick_stages(int bn, int k_blocks) {
+int gemm_pick_stages(int bn, int k_blocks, bool mx) {
   (void)k_blocks;
   int stages = 2;
   for (int s = 3; s <= 8; ++s)
-    if (gemm_smem_bytes(bn, s) <= kGemmSmemBudget) stages = s;
+    if (gemm_smem_bytes(bn, s, mx) <= kGemmSmemBudget) stages = s;
   return stages;
 }
 
-template <int EPI>
+template <int EPI, bool MX>
 static int launch_gemm_t(const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream) {
-  const size_t smem = gemm_smem_bytes(a.bn, a.stages);
-  if (int rc = ensure_max_dynamic_smem(reinterpret_cast<const void*>(gemm_kernel<EPI>)); rc != SPX_OK) return rc;
+  const size_t smem = gemm_smem_bytes(a.bn, a.stages, MX);
+  if (int rc = ensure_max_dynamic_smem(reinterpret_cast<const void*>(gemm_kernel<EPI, MX>)); rc != SPX_OK) return rc;
   // Persistent grid: one CTA per SM, never more CTAs than (upper bound of) tiles.
   const int sms = device_sm_count();
   const int64_t tiles = static_cast<int64_t>(grid_m) * grid_n;
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);
   GemmArgs b = a;
   b.n_tiles = grid_n;
-  gemm_kernel<EPI><<<grid, kGemmThreads, smem, stream>>>(b);
+  gemm_kernel<EPI, MX><<<grid, kGemmThreads, smem, stream>>>(b);
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 
-int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream) {
+int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream, bool mx) {
   if (grid_m <= 0 || grid_n <= 0) return SPX_OK;
   if (a.bn < 16 || a.bn > 256 || (a.bn % 16) != 0) return SPX_ERR_UNSUPPORTED;
+  if (mx) {
+    // Block-scaled lane: one scale atom per 128 B rows of N, accumulators of 128 columns at most.
+    if (a.bn > kMxMaxBn || a.tmem_cols > kMxMaxBn || a.sfa == nullptr || a.sfb == nullptr || (a.ld_sfa % 4) != 0)
+      return SPX_ERR_INVALID_ARG;
+    if (epi == kEpiSwiglu && (a.out_sf == nullptr || (a.chunk % kMxBlock) != 0 || (a.ldo % 16) != 0))
+      return SPX_ERR_INVALID_ARG;
+    switch (epi) {
+      case kEpiStore:
+        return launch_gemm_t<kEpiStore, true>(a, grid_m, grid_n, stream);
+      case kEpiSwiglu:
+        return launch_gemm_t<kEpiSwiglu, true>(a, grid_m, grid_n, stream);
+      case kEpiScatter:
+        return launch_gemm_t<kEpiScatter, true>(a, grid_m, grid_n, stream);
+      default:
+        return SPX_ERR_INVALID_ARG;
+    }
+  }
   switch (epi) {
     case kEpiStore:
-      return launch_gemm_t<kEpiStore>(a, grid_m, grid_n, stream);
+      return launch_gemm_t<kEpiStore, false>(a, grid_m, grid_n, stream);
     case kEpiSwiglu:
-      return launch_gemm_t<kEpiSwiglu>(a, grid_m, grid_n, stream);
+      return launch_gemm_t<kEpiSwiglu, false>(a, grid_m, grid_n, stream);
     case kEpiScatter:
-      return launch_gemm_t<kEpiScatter>(a, grid_m, grid_n, stream);
+      return launch_gemm_t<kEpiScatter, false>(a, grid_m, grid_n, stream);
     case kEpiCombine:
-      return launch_gemm_t<kEpiCombine>(a, grid_m, grid_n, stream);
+      return launch_gemm_t<kEpiCombine, false>(a, grid_m, grid_n, stream);
     default:
       return SPX_ERR_INVALID_ARG;
   }

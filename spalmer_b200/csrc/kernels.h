@@ -25,6 +25,17 @@ constexpr int kDispatchThreads = 32 * kDispatchWarps;
 
 enum Epi : int { kEpiStore = 0, kEpiSwiglu = 1, kEpiScatter = 2, kEpiCombine = 3 };
 
+// MXFP8 lane: B-operand sources of the pack-time quantiser, and the tensor
+// memory plan of the block-scaled GEMM (three 128-column accumulators, then
+// eight rotating 8-column scale-factor slots: SFA in the first 4, SFB next).
+enum MxSource : int { kMxSrcW1 = 0, kMxSrcW2 = 1, kMxSrcRows = 2 };
+constexpr int kMxBlock = 32;        // elements per E8M0 scale
+constexpr int kMxAtomBytes = 512;   // scale atom: 128 rows x 4 scales (one 128-element K block)
+constexpr int kMxMaxBn = 128;
+constexpr uint32_t kMxSfColumn = 384;
+constexpr int kMxSfSlots = 8;
+constexpr uint32_t kMxStageSfBytes = 1024;  // SFA atom + SFB atom per stage
+
 struct RouteArgs {
   const uint16_t* logits;    // [T, E] bf16
   const uint16_t* lut;       // softplus table [65536] or null (identity transform)
@@ -51,8 +62,11 @@ struct DispatchArgs {
   int* chunk_hist;           // [ceil(P/2048), E]
   int* counts;               // [E]
   int* starts;               // [E]
-  int4* tiles;               // [ceil(P/128) + E] {expert, row0, rows, 0}
+  int4* tiles;               // [ceil(P/128) + E] {expert, row0, rows, 0}: BF16-lane experts
   int* num_tiles;
+  const uint8_t* lane_mx;    // [E] 1 = expert runs the MXFP8 lane, or null (all BF16)
+  int4* tiles_mx;            // [ceil(P/128) + E] tiles of MXFP8-lane experts (when lane_mx)
+  int* num_tiles_mx;
   int* order;                // [P] argsort(stable) permutation
   int* src_row;              // [P] token row of each sorted position
   const uint16_t* pair_weights;  // [P] routing weights in pair order, or null
@@ -82,8 +96,14 @@ struct GemmArgs {
   int groups;                // B groups (bounds check of the tile table)
   int gather;                // 1: A rows gathered through gather_idx with cp.async (a_base/lda)
   const int* gather_idx;
-  const uint16_t* a_base;    // gather: A rows (row stride lda elements)
+  const uint8_t* a_base;     // gather: A rows (row stride lda bytes)
   int64_t lda;
+  // MXFP8 lane (block-scaled kernel only)
+  const uint8_t* sfa;        // A scale bytes [A rows, ld_sfa] row-major (row = gathered source row)
+  int64_t ld_sfa;            // bytes per row, multiple of 4
+  const uint8_t* sfb;        // B scale atoms [groups][n_tiles][k_blocks][512]
+  uint8_t* out_sf;           // kEpiSwiglu: hidden scale bytes [rows, ld_out_sf]
+  int64_t ld_out_sf;
   const int4* tiles;         // grouped tiling, or null
   const int* num_tiles;
   int n_valid;               // valid output columns
@@ -111,11 +131,24 @@ size_t route_select_smem(int num_experts);
 int launch_route(const RouteArgs& a, cudaStream_t stream);
 int launch_dispatch(const DispatchArgs& a, cudaStream_t stream);
 
-int encode_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows);
-int encode_3d(CUtensorMap* map, const void* base, int64_t groups, int64_t rows, int64_t cols, int box_rows);
-size_t gemm_smem_bytes(int bn, int stages);
-int gemm_pick_stages(int bn, int k_blocks);
-int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream);
+// Tensor maps with 128-byte rows per box (64 BF16 or 128 bytes of E4M3), 128B swizzle.
+// `elem_bytes` 2 = BF16, 1 = bytes; `ld` / `cols` in elements.
+int encode_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+              int elem_bytes = 2);
+int encode_3d(CUtensorMap* map, const void* base, int64_t groups, int64_t rows, int64_t cols, int box_rows,
+              int elem_bytes = 2);
+size_t gemm_smem_bytes(int bn, int stages, bool mx = false);
+int gemm_pick_stages(int bn, int k_blocks, bool mx = false);
+// `mx` selects the block-scaled MXFP8 kernel (bn <= 128, k_blocks of 128 elements).
+int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream, bool mx = false);
+
+// MXFP8 quantisers (mxfp8.cu).
+int launch_mx_quantize_rows(const uint16_t* src, int64_t rows, int cols, int64_t ld_src, int kp, uint8_t* q,
+                            int64_t ld_q, uint8_t* sf, int64_t ld_sf, cudaStream_t stream);
+size_t mx_atoms_bytes(int groups, int rows_per_group, int kp, int tile_rows);
+int launch_mx_quantize_b(int mode, const uint16_t* a, const uint16_t* b, int groups, int rows_per_group,
+                         int rows_real, int k_real, int kp, int tile_rows, int d, int inter, int chunk, int64_t ld,
+                         uint8_t* q, uint8_t* atoms, cudaStream_t stream);
 
 int launch_combine(const uint16_t* y, int64_t tokens, int d, int k, uint16_t* out, cudaStream_t stream);
 

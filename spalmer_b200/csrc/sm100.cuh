@@ -106,6 +106,11 @@ __device__ __forceinline__ void cp_async16(uint32_t dst_smem, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst_smem), "l"(src) : "memory");
 }
 
+// 4-byte copy (scale bytes); both addresses 4-byte aligned.
+__device__ __forceinline__ void cp_async4(uint32_t dst_smem, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst_smem), "l"(src) : "memory");
+}
+
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 
 template <int N>
@@ -153,6 +158,26 @@ __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, ui
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// Block-scaled MXFP8 MMA: D[tmem] (+)= (A * SFA) * (B * SFB)^T with E4M3
+// operands in shared memory and E8M0 scales in tensor memory (K = 32 per
+// instruction).  The scale addresses carry the byte selector in bits 30-31,
+// matching the sf_id fields of `idesc`.
+__device__ __forceinline__ void mma_mxf8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// Shared memory -> tensor memory: 32 rows x 16 bytes, replicated to the four
+// 32-lane quadrants (the scale-factor layout of the block-scaled MMA).
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t src_desc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(src_desc) : "memory");
 }
 
 // Arrive once on `bar` when all previously issued tcgen05.mma of this thread complete.
@@ -203,6 +228,29 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t smem_addr) {
   d |= static_cast<uint64_t>(1u) << 46;
   d |= static_cast<uint64_t>(2u) << 61;
   return d;
+}
+
+// Descriptor of a 512-byte scale atom for tcgen05.cp: no swizzle, K-major,
+// 8-row core matrices of 16-byte rows (SBO 128 B between them).
+__device__ __forceinline__ uint64_t desc_sf_atom(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1u) << 16;           // LBO 16 B (one core-matrix column; unused)
+  d |= static_cast<uint64_t>(128u >> 4) << 32;    // SBO 128 B
+  d |= static_cast<uint64_t>(1u) << 46;           // version
+  return d;                                        // layout 0 = no swizzle
+}
+
+// Instruction descriptor, kind::mxf8f6f4 block_scale: E4M3 A and B (K-major),
+// FP32 D, E8M0 scales, M x N; scale byte selectors a_sf (bits 29-30) and
+// b_sf (bits 4-5).
+__host__ __device__ __forceinline__ uint32_t idesc_mxf8(int m, int n, uint32_t a_sf, uint32_t b_sf) {
+  return (b_sf << 4)                                // B scale factor id
+         | (0u << 7) | (0u << 10)                   // A, B format: E4M3
+         | (static_cast<uint32_t>(n >> 3) << 17)    // N >> 3
+         | (1u << 23)                               // scale format: E8M0
+         | (static_cast<uint32_t>(m >> 4) << 24)    // M >> 4
+         | (a_sf << 29);                            // A scale factor id
 }
 
 // Instruction descriptor, kind::f16: BF16 A and B (K-major), FP32 D, M x N.

@@ -28,6 +28,7 @@ from torch import Tensor, nn
 
 from spalmer_b200 import _lib
 from spalmer_b200.config import MicroExpertsConfig, coerce_config
+from spalmer_b200.native import NativeExpertPrecisionError
 
 try:  # the reference shell's output type, when the reference package is importable
     from spalmer.modeling import ChannelMixerOutput  # type: ignore
@@ -39,10 +40,6 @@ except Exception:  # noqa: BLE001 - optional integration
         state: Any = None
         auxiliary_loss: Tensor | None = None
         metrics: Mapping[str, Any] = field(default_factory=dict)
-
-
-class NativeExpertPrecisionError(RuntimeError):
-    """The requested expert precision has no B200 kernel (experts/native.py:30)."""
 
 
 # ---------------------------------------------------------------- parameter holders
@@ -245,7 +242,39 @@ def layer_dims(config: MicroExpertsConfig, tokens: int, top_k: int) -> _lib.Laye
         top_k=top_k,
         score_transform=0 if config.router_score_transform == "softplus" else 1,
         execution_loop=1 if config.expert_execution == "loop" else 0,
+        mxfp8_lane=1 if uses_mxfp8_lane(config) else 0,
     )
+
+
+# Precision pairs with a B200 kernel lane: 0 = BF16 grouped GEMM, 1 = MXFP8 block-scaled grouped GEMM.
+_LANES = {("bfloat16", "bfloat16"): 0, ("mxfp8", "mxfp8"): 1}
+
+
+def execution_pair(config: MicroExpertsConfig, promoted: bool) -> tuple[str, str]:
+    """``MicroExpertBank._execution_pair`` (experts/bank.py:462-475)."""
+
+    if not promoted:
+        return config.expert_weight_format, config.expert_activation_format
+    fmt = config.expert_promotion_format
+    if fmt in {"bfloat16", "mxfp8", "float32"}:
+        return fmt, fmt
+    raise RuntimeError(f"no native promotion kernel for {fmt!r}")
+
+
+def _lane_of(config: MicroExpertsConfig, promoted: bool) -> int:
+    pair = execution_pair(config, promoted)
+    lane = _LANES.get(pair)
+    if lane is None:
+        raise NativeExpertPrecisionError(
+            f"no B200 kernel for {pair[0]}/{pair[1]} experts; emulation is prohibited"
+        )
+    return lane
+
+
+def uses_mxfp8_lane(config: MicroExpertsConfig) -> bool:
+    """True when some expert can execute the ("mxfp8", "mxfp8") pair."""
+
+    return 1 in (_lane_of(config, False), _lane_of(config, True))
 
 
 def _bits(t: Tensor) -> Tensor:
@@ -287,6 +316,7 @@ class B200MicroExpertChannelMixer(nn.Module):
         object.__setattr__(self, "_potentiation_controller_ref", ref(potentiation_controller))
         object.__setattr__(self, "_residency_ref", ref(residency))
         object.__setattr__(self, "_pack_cache", None)
+        object.__setattr__(self, "_lane_cache", None)
         object.__setattr__(self, "_ws_cache", {})
         object.__setattr__(self, "_stage_event_array", None)
 
@@ -398,9 +428,43 @@ class B200MicroExpertChannelMixer(nn.Module):
             ),
             "spx_pack_weights",
         )
+        if dims.mxfp8_lane:
+            mx_bytes = lambda n: torch.empty(max(16, n), dtype=torch.uint8, device=device)  # noqa: E731
+            for name in ("expert_w1_mx", "expert_w1_mx_scales", "expert_w2_mx", "expert_w2_mx_scales"):
+                packed[name] = mx_bytes(getattr(sizes, name))
+            _lib.check(
+                lib.spx_pack_weights_mxfp8(
+                    dims, src, _lib.ptr(packed["expert_w1_mx"]), _lib.ptr(packed["expert_w1_mx_scales"]),
+                    _lib.ptr(packed["expert_w2_mx"]), _lib.ptr(packed["expert_w2_mx_scales"]), stream,
+                ),
+                "spx_pack_weights_mxfp8",
+            )
         packed["_keepalive"] = bits
         object.__setattr__(self, "_pack_cache", (key, packed))
         return packed
+
+    def _lanes(self, device: torch.device) -> Tensor | None:
+        """Per-expert kernel lane (uint8 [E], 1 = MXFP8) from the promotion mask.
+
+        ``MicroExpertBank._execution_pair`` (experts/bank.py:462-475) decides each
+        expert's precision pair from ``promoted_mask``; the lane tensor is built on
+        the device (no host read of the mask) and cached on the mask's version.
+        None when every expert runs BF16.
+        """
+
+        config = self.config
+        unpromoted, promoted = _lane_of(config, False), _lane_of(config, True)
+        if unpromoted == 0 and promoted == 0:
+            return None
+        mask = self.potentiation_controller.promoted_mask
+        key = (device, mask.data_ptr(), mask._version)
+        cached = self._lane_cache
+        if cached is not None and cached[0] == key:
+            return cached[1]
+        m = mask.detach().to(device=device, dtype=torch.bool)
+        lanes = torch.where(m, promoted, unpromoted).to(torch.uint8).contiguous()
+        object.__setattr__(self, "_lane_cache", (key, lanes))
+        return lanes
 
     def _workspace(self, device: torch.device, dims: _lib.LayerDims) -> Tensor:
         lib = _lib.load()
@@ -453,12 +517,10 @@ class B200MicroExpertChannelMixer(nn.Module):
             raise RuntimeError("the B200 micro-expert layer requires CUDA hidden states")
         if hidden_states.dtype != torch.bfloat16:
             raise RuntimeError(
-                f"bfloat16/bfloat16 expert execution requires torch.bfloat16 hidden states, got {hidden_states.dtype}"
+                f"{config.expert_weight_format}/{config.expert_activation_format} expert execution requires "
+                f"torch.bfloat16 hidden states, got {hidden_states.dtype}"
             )
-        if config.expert_weight_format != "bfloat16":
-            raise NativeExpertPrecisionError(
-                f"no B200 kernel for {config.expert_weight_format}/{config.expert_activation_format} experts yet"
-            )
+        lanes = self._lanes(hidden_states.device)
         batch, seq_len, d_model = hidden_states.shape
         tokens = batch * seq_len
         k = self.active_experts
@@ -497,6 +559,11 @@ class B200MicroExpertChannelMixer(nn.Module):
             shared_w2=_lib.ptr(packed["shared_w2"]),
             softplus_table=_lib.ptr(lut),
             resident_mask=_lib.ptr(mask),
+            expert_lane_mxfp8=_lib.ptr(lanes),
+            expert_w1_mx=_lib.ptr(packed.get("expert_w1_mx")),
+            expert_w1_mx_scales=_lib.ptr(packed.get("expert_w1_mx_scales")),
+            expert_w2_mx=_lib.ptr(packed.get("expert_w2_mx")),
+            expert_w2_mx_scales=_lib.ptr(packed.get("expert_w2_mx_scales")),
         )
         events = self._stage_event_array
         outs = _lib.LayerOutputs(

@@ -66,3 +66,32 @@ def resident_mask(meta: dict) -> np.ndarray | None:
     mask = np.zeros(meta["config"]["num_experts"], dtype=bool)
     mask[meta["resident"]] = True
     return mask
+
+
+def mxfp8_experts(num_experts: int, fraction: float, seed: int = 2) -> np.ndarray:
+    """Seeded MXFP8 expert set: the first ceil(fraction * E) of randperm(E, seed)."""
+
+    import math
+
+    gen = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(num_experts, generator=gen).numpy()
+    lane = np.zeros(num_experts, dtype=bool)
+    lane[perm[: math.ceil(fraction * num_experts)]] = True
+    return lane
+
+
+def mxfp8_config(**kw) -> MicroExpertsConfig:
+    """MXFP8 expert weights whose promoted experts run BF16 (experts/bank.py:462-475)."""
+
+    kw.setdefault("expert_weight_format", "mxfp8")
+    kw.setdefault("expert_activation_format", "mxfp8")
+    kw.setdefault("expert_promotion_format", "bfloat16")
+    return MicroExpertsConfig(**kw)
+
+
+def set_mxfp8_lanes(mixer, lane_mx: np.ndarray) -> None:
+    """Run exactly the experts in `lane_mx` as MXFP8: promote (to BF16) all the others."""
+
+    with torch.no_grad():
+        mask = mixer.potentiation_controller.promoted_mask
+        mask.copy_(torch.from_numpy(~lane_mx).to(mask.device))
