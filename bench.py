@@ -36,9 +36,12 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 CONFIGS = {
-    # 100M-preset shape (MXFP8 promotion lane pending: all experts BF16).
+    # 100M-preset shape, a seeded 25% of the experts in MXFP8, the rest BF16.
     "m100": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
-                          active_experts=8), batch=64, seq=1024, cpu_sample=1024),
+                          active_experts=8), batch=64, seq=1024, cpu_sample=1024, mxfp8_fraction=0.25),
+    # The same shape with every expert in BF16.
+    "m100_bf16": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
+                               active_experts=8), batch=64, seq=1024, cpu_sample=1024),
     # 10M-preset shape.
     "m10": dict(cfg=dict(d_model=256, num_experts=200, expert_inter_dim=64, shared_inter_dim=256,
                          active_experts=8), batch=32, seq=512, cpu_sample=4096),
@@ -47,6 +50,8 @@ CONFIGS = {
                            active_experts=4), batch=2, seq=256, cpu_sample=512),
 }
 METRIC = "routed tokens/sec per MoE layer"
+CPU_ALL_BF16_NOTE = ("; all experts BF16: the reference has no CPU MXFP8 path and rejects BF16 experts "
+                     "mixed with MXFP8 (experts/config.py:140-161)")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
@@ -57,6 +62,45 @@ def peaks() -> dict:
         return {"hbm_gbs": data["hbm_gbs"], "bf16_tflops": data["bf16_tflops"],
                 "bf16_tflops_sustained": data.get("bf16_tflops_sustained"), "source": "measured"}
     return dict(FALLBACK_PEAKS)
+
+
+def mxfp8_experts(num_experts: int, fraction: float):
+    """Seeded MXFP8 expert set: the first ceil(fraction * E) of randperm(E, seed 2)."""
+
+    import math
+
+    perm = torch.randperm(num_experts, generator=torch.Generator().manual_seed(2))
+    lane = torch.zeros(num_experts, dtype=torch.bool)
+    lane[perm[: math.ceil(fraction * num_experts)]] = True
+    return lane
+
+
+def build_mixer(spec: dict, device=None):
+    """The bench layer: seed-0 random init; MXFP8 configs run their seeded expert set in MXFP8.
+
+    The reference expresses a mixed layer as MXFP8 expert weights whose promoted
+    experts run BF16 (experts/bank.py:462-475, experts/config.py:140-161), so
+    every expert outside the MXFP8 set is marked promoted.
+    """
+
+    from spalmer_b200 import B200MicroExpertChannelMixer, MicroExpertsConfig
+
+    fraction = spec.get("mxfp8_fraction", 0.0)
+    cfg = dict(spec["cfg"])
+    if fraction > 0:
+        cfg.update(expert_weight_format="mxfp8", expert_activation_format="mxfp8",
+                   expert_promotion_format="bfloat16")
+    config = MicroExpertsConfig(**cfg)
+    torch.manual_seed(0)
+    mixer = B200MicroExpertChannelMixer(config).to(torch.bfloat16).eval()
+    lane = None
+    if fraction > 0:
+        lane = mxfp8_experts(config.num_experts, fraction)
+        with torch.no_grad():
+            mixer.potentiation_controller.promoted_mask.copy_(~lane)
+    if device is not None:
+        mixer = mixer.to(device)
+    return mixer, lane
 
 
 def layer_flops(cfg: dict, tokens: int) -> dict:
@@ -82,7 +126,9 @@ def workload_config(name: str, world: int) -> dict:
         "d_model": cfg["d_model"], "num_experts": cfg["num_experts"],
         "expert_inter_dim": cfg["expert_inter_dim"], "top_k": cfg["active_experts"],
         "shared_inter_dim": cfg["shared_inter_dim"],
-        "expert_precision": "bf16 for all experts (MXFP8 promotion lane not implemented yet)",
+        "expert_precision": (f"MXFP8 (E4M3, E8M0 per 1x32 along K) for a seeded {spec['mxfp8_fraction']:.0%} "
+                             "of the experts (randperm seed 2), BF16 for the rest"
+                             if spec.get("mxfp8_fraction") else "BF16 for all experts"),
         "weights": "random init, torch.manual_seed(0), N(0,0.02)",
         "l2": "inputs larger than L2: two 100.7 MB hidden-state batches alternated + 121.6 MB weights; steps timed back to back",
         "parallelism": f"dp{world}",
@@ -140,13 +186,11 @@ def run_reference_arm(args) -> None:
     import numpy as np
 
     from oracle import mixer_ref as R
-    from spalmer_b200 import B200MicroExpertChannelMixer, MicroExpertsConfig
     from tests.helpers import bf16_bits, oracle_params
 
     spec = CONFIGS[args.config]
-    config = MicroExpertsConfig(**spec["cfg"])
-    torch.manual_seed(0)
-    mixer = B200MicroExpertChannelMixer(config).to(torch.bfloat16)
+    mixer, _ = build_mixer(spec)
+    config = mixer.config
     params = oracle_params(mixer)
     sample = spec["cpu_sample"]
     x = torch.randn(sample, config.d_model, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
@@ -168,7 +212,8 @@ def run_reference_arm(args) -> None:
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": workload_config(args.config, world),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{sample} tokens of the {args.config} workload per step"},
+                         "sample": f"{sample} tokens of the {args.config} workload per step"
+                                   + CPU_ALL_BF16_NOTE * bool(spec.get("mxfp8_fraction"))},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -193,14 +238,14 @@ def cpu_baseline(args, mixer, x_cpu) -> dict:
     med = statistics.median(times)
     return {"value": sample / med, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
             "sample": f"{sample} tokens of the {args.config} workload, median of {len(times)} runs "
-                      f"(numpy/OpenBLAS on all host threads)"}
+                      f"(numpy/OpenBLAS on all host threads)"
+                      + CPU_ALL_BF16_NOTE * bool(spec.get("mxfp8_fraction"))}
 
 
 def run_ours(args) -> None:
     world, rank, local = init_dist()
     import torch.distributed as dist
 
-    from spalmer_b200 import B200MicroExpertChannelMixer, MicroExpertsConfig
     from spalmer_b200 import _lib
 
     torch.cuda.set_device(local)
@@ -210,11 +255,10 @@ def run_ours(args) -> None:
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     spec = CONFIGS[args.config]
-    config = MicroExpertsConfig(**spec["cfg"])
     batch, seq = spec["batch"], spec["seq"]
     tokens = batch * seq
-    torch.manual_seed(0)
-    mixer = B200MicroExpertChannelMixer(config).to(torch.bfloat16).eval().to(device)
+    mixer, lane = build_mixer(spec, device)
+    config = mixer.config
     x_cpu = torch.randn(batch, seq, config.d_model, generator=torch.Generator().manual_seed(1 + rank))
     x_cpu = x_cpu.to(torch.bfloat16)
     x_host = x_cpu.pin_memory()
@@ -322,6 +366,13 @@ def run_ours(args) -> None:
         dom = "expert_gemm1_swiglu"
         dom_ms = stages[dom]
         achieved = flops[dom] / (dom_ms / 1e3) / 1e12
+        # MXFP8 pairs run at twice the BF16 tensor rate: the roofline peak of the
+        # stage is the FLOP-weighted blend of the two lanes' peaks.
+        mx_share = 0.0
+        if lane is not None:
+            util = out.metrics["expert_utilization"].float().cpu()
+            mx_share = float(util[lane].sum())
+        peak = pk["bf16_tflops"] / ((1.0 - mx_share) + mx_share / 2.0)
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -330,11 +381,13 @@ def run_ours(args) -> None:
             "e2e": {"value": e2e_value, "unit": "tokens/s",
                     "h2d_bytes_per_step": tokens * config.d_model * 2,
                     "d2h_bytes_per_step": tokens * config.d_model * 2 + 2},
-            "gpu_launches": K * 10,
-            "roofline": {"bound": "tensor", "kernel": "gemm_kernel<kEpiSwiglu> (expert GEMM1, gathered rows)",
-                         "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                         "frac": achieved / pk["bf16_tflops"], "traffic": None,
-                         "peak_source": f"{pk['source']} bf16 burst"},
+            "gpu_launches": K * (13 if lane is not None else 10),
+            "roofline": {"bound": "tensor",
+                         "kernel": "gemm_kernel<kEpiSwiglu> (expert GEMM1, gathered rows; BF16 and MXFP8 lanes)",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "mxfp8_pair_share": mx_share,
+                         "peak_source": f"{pk['source']} bf16 burst; MXFP8 share at 2x"},
             "layer_tensor_tflops": sum(flops.values()) / (ms_per_step / 1e3) / 1e12,
             "stages_ms": stages,
             "device_status": status,

@@ -36,7 +36,7 @@ struct Shape {
   // MXFP8 lane
   bool mx;
   int kx;             // GEMM1 K in bytes (d padded to 128)
-  int cm, ncm;        // GEMM1 chunk (N tile = 2*cm) and chunks
+  int cm, ncm;        // GEMM1 chunk (N tile = 2*cm, up to 256) and chunks
   int kh;             // hidden width in bytes (I padded to 128) = GEMM2 K
   int bn2m, gn2m;     // GEMM2 N tile and tiles
 };
@@ -75,10 +75,10 @@ int make_shape(const spx_layer_dims* dm, Shape* s) {
   if (s->mx) {
     if (s->I % kMxBlock != 0) return SPX_ERR_UNSUPPORTED;
     s->kx = round_up_i(s->d, 128);
-    s->cm = (s->I % 64 == 0) ? 64 : 32;
+    s->cm = (s->I % 128 == 0) ? 128 : (s->I % 64 == 0) ? 64 : 32;
     s->ncm = s->I / s->cm;
     s->kh = round_up_i(s->I, 128);
-    s->bn2m = std::min(kMxMaxBn, round_up_i(s->d, 16));
+    s->bn2m = std::min(kMxDenseBn, round_up_i(s->d, 16));
     s->gn2m = ceil_div(s->d, s->bn2m);
   } else {
     s->kx = s->cm = s->ncm = s->kh = s->bn2m = s->gn2m = 0;
@@ -336,7 +336,7 @@ struct MmLayout {
 MmLayout mm_layout(int64_t m, int64_t n, int64_t k) {
   MmLayout L{};
   L.kp = static_cast<int64_t>(round_up(static_cast<size_t>(k > 0 ? k : 1), 128));
-  L.bn = static_cast<int>(std::min<int64_t>(kMxMaxBn, static_cast<int64_t>(round_up(static_cast<size_t>(n), 16))));
+  L.bn = static_cast<int>(std::min<int64_t>(kMxDenseBn, static_cast<int64_t>(round_up(static_cast<size_t>(n), 16))));
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t at = off;

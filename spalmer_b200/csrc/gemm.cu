@@ -207,22 +207,50 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
 }
 
 // MXFP8-lane SwiGLU epilogue: each thread holds 32 hidden values of its row
-// (one scale block) and writes them as E4M3 bytes plus the block's scale byte.
+// per slice (one scale block) and writes them as E4M3 bytes plus the block's
+// scale byte.  The accumulator is released as soon as the thread's slices are
+// in registers (at most two slices of gate and up: 128 values), so a single
+// 256-column TMEM accumulator still lets the next tile's MMAs overlap this
+// tile's arithmetic and stores.
 __device__ __forceinline__ void run_epilogue_swiglu_mx(const GemmArgs& a, uint32_t taddr, int quad, int half,
-                                                       int lane, int row0, int rows, int nt) {
+                                                       int lane, int row0, int rows, int nt, uint64_t* release) {
   const int r = quad * 32 + lane;
   const bool live = r < rows;
   uint8_t* hq = static_cast<uint8_t*>(a.out);
   const int64_t row = static_cast<int64_t>(row0) + r;
-  for (int s0 = half * 32; s0 < a.chunk; s0 += 64) {
-    uint32_t g[32], u[32];
-    tmem_ld32(taddr + s0, g);
-    tmem_ld32(taddr + a.chunk + s0, u);
-    tmem_wait_ld();
+  // gate and up rounded to BF16 right away (the reference's tensor boundary),
+  // two values per register: 64 registers hold both slices.
+  uint32_t gp[2][16], up[2][16];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int s0 = half * 32 + 64 * j;
+    if (s0 < a.chunk) {
+      uint32_t g[32], u[32];
+      tmem_ld32(taddr + s0, g);
+      tmem_ld32(taddr + a.chunk + s0, u);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        gp[j][c] = pack_bf16x2(__uint_as_float(g[2 * c]), __uint_as_float(g[2 * c + 1]));
+        up[j][c] = pack_bf16x2(__uint_as_float(u[2 * c]), __uint_as_float(u[2 * c + 1]));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(release);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int s0 = half * 32 + 64 * j;
+    if (s0 >= a.chunk) break;
     float h[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      h[j] = bfr(bfr(silu_fast(bfr(__uint_as_float(g[j])))) * bfr(__uint_as_float(u[j])));
+    for (int c = 0; c < 16; ++c) {
+      h[2 * c] = bfr(silu_fast(lo_f(gp[j][c]))) * lo_f(up[j][c]);
+      h[2 * c + 1] = bfr(silu_fast(hi_f(gp[j][c]))) * hi_f(up[j][c]);
+    }
+#pragma unroll
+    for (int c = 0; c < 32; ++c) h[c] = bfr(h[c]);
     uint32_t q[8];
     const uint32_t sb = mx_quantize32(h, q);
     if (live) {
@@ -262,16 +290,16 @@ __device__ __forceinline__ bool decode_tile(const GemmArgs& a, int t, int& group
   return rows > 0;
 }
 
-constexpr int kGatherLag = 2;  // cp.async producer: stages kept in flight beyond the newest
-
 // Producer warp for the stages that need the load/store unit: A rows gathered
 // through `gather_idx` (each cp.async instruction moves 4 rows x 128 B, fully
 // coalesced) and, in the MXFP8 lane, the two scale atoms of every stage.  B
-// (and an ungathered A) come by TMA.  full[s] expects two arrivals: lane 0's
-// arrive.expect_tx for the TMA bytes, and lane 0's arrive once the warp's
-// cp.async group for stage s has landed (kGatherLag stages later, after
-// wait_group + fence.proxy.async so the async proxy -- tcgen05.mma and
-// tcgen05.cp -- sees it).
+// (and an ungathered A) come by TMA.  full[s] expects 1 + 32 arrivals: lane
+// 0's arrive.expect_tx for the TMA bytes, and one cp.async-tracked arrival per
+// lane (cp.async.mbarrier.arrive.noinc), which fires when that lane's copies
+// for the stage have landed.  The warp never waits for its own copies, so
+// every stage of the ring can be in flight at once.
+constexpr uint32_t kCpAsyncArrivals = 32;
+
 template <bool MX>
 __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa, uint8_t* sb, uint8_t* ssf,
                                                  uint64_t* full, uint64_t* empty, int S, uint32_t a_bytes,
@@ -337,25 +365,15 @@ __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa,
         const uint32_t sf = smem_u32(ssf + s * kMxStageSfBytes);
 #pragma unroll
         for (int j = 0; j < 4; ++j) cp_async4(sf + lane * 16 + j * 4, a.sfa + sfr[j] * a.ld_sfa + kb * 4);
-        const int64_t atom = (static_cast<int64_t>(group) * a.n_tiles + nt) * a.k_blocks + kb;
-        cp_async16(sf + kMxAtomBytes + lane * 16, a.sfb + atom * kMxAtomBytes + lane * 16);
+        const int sfb_atoms = (bn + 127) / 128;
+        const int64_t atom = ((static_cast<int64_t>(group) * a.n_tiles + nt) * a.k_blocks + kb) * sfb_atoms;
+        for (int q = 0; q < sfb_atoms; ++q)
+          cp_async16(sf + (1 + q) * kMxAtomBytes + lane * 16, a.sfb + (atom + q) * kMxAtomBytes + lane * 16);
       }
-      cp_async_commit();
-      if (it >= static_cast<uint32_t>(kGatherLag)) {
-        cp_async_wait<kGatherLag>();
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&full[(it - kGatherLag) % S]);
-      }
+      cp_async_mbar_arrive_noinc(&full[s]);
     }
   }
-  cp_async_wait<0>();
-  fence_proxy_async_smem();
-  __syncwarp();
-  if (lane == 0) {
-    const uint32_t first = it > static_cast<uint32_t>(kGatherLag) ? it - kGatherLag : 0u;
-    for (uint32_t j = first; j < it; ++j) mbar_arrive(&full[j % S]);
-  }
+  cp_async_wait_all();  // no copy outlives the producer (error paths included)
 }
 
 // Persistent GEMM: each CTA walks tiles blockIdx.x, blockIdx.x + gridDim.x, ...
@@ -394,7 +412,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], ldst_producer ? 2 : 1);
+      mbar_init(&full[s], ldst_producer ? 1 + kCpAsyncArrivals : 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < kMaxAccBufs; ++b) {
@@ -470,11 +488,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
           if constexpr (MX) {
             // Scales of this stage -> a rotating TMEM slot (tcgen05.cp and the
             // MMAs that read it are issued in order by this thread).
-            const uint32_t sfa_t = tmem + kMxSfColumn + (it % kMxSfSlots) * 8u;
+            const uint32_t sfa_t = tmem + kMxSfColumn + (it % kMxSfSlots) * kMxSfSlotCols;
             const uint32_t sfb_t = sfa_t + 4u;
             const uint32_t sf_smem = smem_u32(ssf + s * kMxStageSfBytes);
             tmem_cp_32x128b_x4(sfa_t, desc_sf_atom(sf_smem));
             tmem_cp_32x128b_x4(sfb_t, desc_sf_atom(sf_smem + kMxAtomBytes));
+            if (bn > 128) tmem_cp_32x128b_x4(sfb_t + 4u, desc_sf_atom(sf_smem + 2 * kMxAtomBytes));
 #pragma unroll
             for (uint32_t kk = 0; kk < 4; ++kk) {
               mma_mxf8_ss(acc, desc_kmajor_sw128(a_base + kk * 32), desc_kmajor_sw128(b_base + kk * 32),
@@ -522,14 +541,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       tc_fence_after();
       const uint32_t taddr = tmem + b * a.tmem_cols + (static_cast<uint32_t>(quad * 32) << 16);
       if constexpr (MX && EPI == kEpiSwiglu) {
-        run_epilogue_swiglu_mx(a, taddr, quad, half, lane, row0, rows, nt);
+        run_epilogue_swiglu_mx(a, taddr, quad, half, lane, row0, rows, nt, &tempty[b]);  // releases early
       } else {
         run_epilogue<EPI>(a, taddr, stage_all + (warp - 2) * kStageBytesPerWarp, quad, half, lane, row0, rows,
                           nt * bn, nt, my_row, my_w);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[b]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[b]);
     }
   }
   tc_fence_before();
@@ -632,7 +651,8 @@ int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t
     // Block-scaled lane: one scale atom per 128 B rows of N, accumulators of 128 columns at most.
     if (a.bn > kMxMaxBn || a.tmem_cols > kMxMaxBn || a.sfa == nullptr || a.sfb == nullptr || (a.ld_sfa % 4) != 0)
       return SPX_ERR_INVALID_ARG;
-    if (epi == kEpiSwiglu && (a.out_sf == nullptr || (a.chunk % kMxBlock) != 0 || (a.ldo % 16) != 0))
+    if (epi == kEpiSwiglu &&
+        (a.out_sf == nullptr || (a.chunk % kMxBlock) != 0 || a.chunk > 128 || (a.ldo % 16) != 0))
       return SPX_ERR_INVALID_ARG;
     switch (epi) {
       case kEpiStore:

@@ -26,15 +26,19 @@ constexpr int kDispatchThreads = 32 * kDispatchWarps;
 enum Epi : int { kEpiStore = 0, kEpiSwiglu = 1, kEpiScatter = 2, kEpiCombine = 3 };
 
 // MXFP8 lane: B-operand sources of the pack-time quantiser, and the tensor
-// memory plan of the block-scaled GEMM (three 128-column accumulators, then
-// eight rotating 8-column scale-factor slots: SFA in the first 4, SFB next).
+// memory plan of the block-scaled GEMM: accumulators in columns [0, 384)
+// (three of 128 columns, or one of 256), then eight rotating 16-column
+// scale-factor slots (SFA in the first 4 columns, SFB -- up to 256 rows,
+// 2 atoms -- in the next 8).
 enum MxSource : int { kMxSrcW1 = 0, kMxSrcW2 = 1, kMxSrcRows = 2 };
 constexpr int kMxBlock = 32;        // elements per E8M0 scale
 constexpr int kMxAtomBytes = 512;   // scale atom: 128 rows x 4 scales (one 128-element K block)
-constexpr int kMxMaxBn = 128;
+constexpr int kMxMaxBn = 256;
+constexpr int kMxDenseBn = 128;              // N tile of the dense MXFP8 matmul
 constexpr uint32_t kMxSfColumn = 384;
 constexpr int kMxSfSlots = 8;
-constexpr uint32_t kMxStageSfBytes = 1024;  // SFA atom + SFB atom per stage
+constexpr uint32_t kMxSfSlotCols = 16;
+constexpr uint32_t kMxStageSfBytes = 3 * kMxAtomBytes;  // SFA atom + up to two SFB atoms per stage
 
 struct RouteArgs {
   const uint16_t* logits;    // [T, E] bf16

@@ -7,7 +7,7 @@
 //           operands of `left @ right_rows.T` row-wise along K).
 //  * B operands (weights, pack time): E4M3 [groups, rows, kp] and the scales
 //           rearranged into the 512-byte atoms the GEMM copies into tensor
-//           memory, [groups][row tiles][kp/128][512].  Rows come from the
+//           memory, [groups][row tiles][kp/128][ceil(tile rows/128)][512].  Rows come from the
 //           reference layouts directly: expert gate/up [E, d, I] (row = output
 //           channel i, K = d, rows in the chunked [gate | up] order of the
 //           GEMM1 tiles), expert down [E, I, d] (row = output column n, K = I),
@@ -125,8 +125,9 @@ __global__ void mx_quantize_b_kernel(MxBSource s, int groups, int rows_per_group
     const uint32_t sb = mx_quantize32(v, qw);
     store32(q + (static_cast<int64_t>(g) * rows_per_group + row) * kp + blk * kMxBlock, qw);
     const int tile = row / tile_rows, r = row - tile * tile_rows;
-    const int64_t atom = (static_cast<int64_t>(g) * tiles + tile) * kblocks + (blk >> 2);
-    atoms[atom * kMxAtomBytes + mx_atom_offset(r, blk & 3)] = static_cast<uint8_t>(sb);
+    const int per_tile = (tile_rows + 127) / 128;
+    const int64_t atom = ((static_cast<int64_t>(g) * tiles + tile) * kblocks + (blk >> 2)) * per_tile + (r >> 7);
+    atoms[atom * kMxAtomBytes + mx_atom_offset(r & 127, blk & 3)] = static_cast<uint8_t>(sb);
   }
 }
 
@@ -141,14 +142,15 @@ int launch_mx_quantize_rows(const uint16_t* src, int64_t rows, int cols, int64_t
 
 size_t mx_atoms_bytes(int groups, int rows_per_group, int kp, int tile_rows) {
   const int tiles = (rows_per_group + tile_rows - 1) / tile_rows;
-  return static_cast<size_t>(groups) * tiles * (kp / 128) * kMxAtomBytes;
+  const int per_tile = (tile_rows + 127) / 128;
+  return static_cast<size_t>(groups) * tiles * (kp / 128) * per_tile * kMxAtomBytes;
 }
 
 int launch_mx_quantize_b(int mode, const uint16_t* a, const uint16_t* b, int groups, int rows_per_group,
                          int rows_real, int k_real, int kp, int tile_rows, int d, int inter, int chunk, int64_t ld,
                          uint8_t* q, uint8_t* atoms, cudaStream_t stream) {
   if (groups <= 0 || rows_per_group <= 0) return SPX_OK;
-  if (kp % 128 != 0 || tile_rows < 16 || tile_rows > 128) return SPX_ERR_INVALID_ARG;
+  if (kp % 128 != 0 || tile_rows < 16 || tile_rows > kMxMaxBn) return SPX_ERR_INVALID_ARG;
   if (cudaMemsetAsync(atoms, 0, mx_atoms_bytes(groups, rows_per_group, kp, tile_rows), stream) != cudaSuccess)
     return SPX_ERR_CUDA;
   MxBSource s{};

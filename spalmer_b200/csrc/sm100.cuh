@@ -118,6 +118,14 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Arrive on `bar` once every cp.async this thread issued so far has landed.
+// .noinc: the arrival is one of the barrier's expected arrivals.
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Make this thread's completed generic-proxy shared-memory writes visible to
 // the async proxy (tcgen05.mma operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
