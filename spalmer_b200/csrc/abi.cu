@@ -103,7 +103,7 @@ MxPackSizes mx_pack_sizes(const Shape& s) {
 }
 
 struct Layout {
-  size_t small, tie_rows, lb_partial, chunk_hist, counts, starts, tiles, order, src_row, sorted_w;
+  size_t small, tie_rows, lb_partial, chunk_hist, counts, starts, tiles, order, src_row, rank, sorted_w;
   size_t hidden, y, shared_hidden, logits, x_pad, util, stats, ratios, aux;
   size_t x_q, x_sf, h_q, h_sf, tiles_mx;  // MXFP8 lane (empty otherwise)
   size_t total;
@@ -126,6 +126,7 @@ Layout make_layout(const Shape& s) {
   L.tiles = take(sizeof(int4) * static_cast<size_t>(s.max_tiles));
   L.order = take(sizeof(int) * s.P);
   L.src_row = take(sizeof(int) * s.P);
+  L.rank = take(sizeof(int) * s.P);
   L.sorted_w = take(sizeof(uint16_t) * s.P);
   L.hidden = take(2 * static_cast<size_t>(s.P) * s.kp);
   L.y = take(2 * static_cast<size_t>(s.P) * s.d);
@@ -154,11 +155,11 @@ int sm_count() { return device_sm_count(); }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-GemmArgs base_args(int bn, int k_blocks, int* status, bool mx = false) {
+GemmArgs base_args(int epi, int bn, int k_blocks, int* status, bool mx = false) {
   GemmArgs g{};
   g.bn = bn;
   g.k_blocks = k_blocks;
-  g.stages = gemm_pick_stages(bn, k_blocks, mx);
+  g.stages = gemm_pick_stages(bn, k_blocks, mx, epi);
   g.tmem_cols = pow2_at_least(static_cast<uint32_t>(bn));
   g.groups = 1;
   g.status = status;
@@ -203,6 +204,7 @@ DispatchArgs dispatch_args(const Shape& s, const int64_t* ids, int* order, int* 
   a.num_tiles = at<int>(ws, L.small) + 2;
   a.order = order != nullptr ? order : at<int>(ws, L.order);
   a.src_row = at<int>(ws, L.src_row);
+  a.rank = at<int>(ws, L.rank);
   a.lb_partial = at<float>(ws, L.lb_partial);
   a.lb_blocks = s.lb_blocks;
   a.eligible_experts = s.E;
@@ -381,7 +383,7 @@ int spx_mxfp8_mm_nt(const uint16_t* left, const uint16_t* right_rows, int64_t m,
     rc = launch_mx_quantize_b(kMxSrcRows, right_rows, nullptr, 1, static_cast<int>(n), static_cast<int>(n),
                               static_cast<int>(k), kp, L.bn, 0, 0, 0, k, rq, rsf, st);
   if (rc != SPX_OK) return rc;
-  GemmArgs g = base_args(L.bn, kp / 128, at<int>(workspace, L.status), true);
+  GemmArgs g = base_args(kEpiStore, L.bn, kp / 128, at<int>(workspace, L.status), true);
   if ((rc = encode_2d(&g.tma_a, lq, m, kp, kp, kTileRows, 1)) != SPX_OK) return rc;
   if ((rc = encode_3d(&g.tma_b, rq, 1, n, kp, L.bn, 1)) != SPX_OK) return rc;
   g.m_rows = static_cast<int>(m);
@@ -462,7 +464,7 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   const uint16_t* logits = out->injected_logits;
   if (logits == nullptr) {
     uint16_t* lg = out->router_logits != nullptr ? out->router_logits : at<uint16_t>(workspace, L.logits);
-    GemmArgs g = base_args(s.bn_router, s.kd / 64, status);
+    GemmArgs g = base_args(kEpiStore, s.bn_router, s.kd / 64, status);
     if ((rc = encode_2d(&g.tma_a, xa, s.T, s.kd, s.kd, kTileRows)) != SPX_OK) return rc;
     if ((rc = encode_3d(&g.tma_b, w->router_weight, 1, s.E, s.kd, s.bn_router)) != SPX_OK) return rc;
     g.m_rows = static_cast<int>(s.T);
@@ -516,7 +518,7 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
 
   // ---- K3a: expert GEMM1 (gathered rows) + SwiGLU
   {
-    GemmArgs g = base_args(2 * s.c, s.kd / 64, status);
+    GemmArgs g = base_args(kEpiSwiglu, 2 * s.c, s.kd / 64, status);
     if ((rc = encode_3d(&g.tma_b, w->expert_w1, s.E, static_cast<int64_t>(s.nc) * 2 * s.c, s.kd, 2 * s.c)) != SPX_OK)
       return rc;
     g.groups = s.E;
@@ -534,7 +536,7 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   }
   if (mx) {
     // MXFP8-lane experts: block-scaled GEMM1, hidden written quantised.
-    GemmArgs g = base_args(2 * s.cm, s.kx / 128, status, true);
+    GemmArgs g = base_args(kEpiSwiglu, 2 * s.cm, s.kx / 128, status, true);
     if ((rc = encode_3d(&g.tma_b, w->expert_w1_mx, s.E, static_cast<int64_t>(s.ncm) * 2 * s.cm, s.kx, 2 * s.cm,
                         1)) != SPX_OK)
       return rc;
@@ -559,7 +561,7 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   mark(4);
   // ---- K3b: expert GEMM2, scaled by the routing weight, scattered to pair order
   {
-    GemmArgs g = base_args(s.bn_d, s.kp / 64, status);
+    GemmArgs g = base_args(kEpiScatter, s.bn_d, s.kp / 64, status);
     if ((rc = encode_2d(&g.tma_a, hid, s.P, s.kp, s.kp, kTileRows)) != SPX_OK) return rc;
     if ((rc = encode_3d(&g.tma_b, w->expert_w2, s.E, s.d, s.kp, s.bn_d)) != SPX_OK) return rc;
     g.groups = s.E;
@@ -568,12 +570,13 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
     g.n_valid = s.d;
     g.out = y;
     g.ldo = s.d;
-    g.pos_to_pair = da.order;
+    g.tma_store = (s.d % 64) == 0;  // whole 64-column boxes; other widths use plain stores
+    if (g.tma_store && (rc = encode_2d(&g.tma_out, y, s.P, s.d, s.d, 32)) != SPX_OK) return rc;
     g.pos_weight = da.sorted_weights;
     if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn_d, st)) != SPX_OK) return rc;
   }
   if (mx) {
-    GemmArgs g = base_args(s.bn2m, s.kh / 128, status, true);
+    GemmArgs g = base_args(kEpiScatter, s.bn2m, s.kh / 128, status, true);
     if ((rc = encode_2d(&g.tma_a, hq, s.P, s.kh, s.kh, kTileRows, 1)) != SPX_OK) return rc;
     if ((rc = encode_3d(&g.tma_b, w->expert_w2_mx, s.E, s.d, s.kh, s.bn2m, 1)) != SPX_OK) return rc;
     g.groups = s.E;
@@ -585,7 +588,8 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
     g.n_valid = s.d;
     g.out = y;
     g.ldo = s.d;
-    g.pos_to_pair = da.order;
+    g.tma_store = (s.d % 64) == 0;  // whole 64-column boxes; other widths use plain stores
+    if (g.tma_store && (rc = encode_2d(&g.tma_out, y, s.P, s.d, s.d, 32)) != SPX_OK) return rc;
     g.pos_weight = da.sorted_weights;
     if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn2m, st, true)) != SPX_OK) return rc;
   }
@@ -594,7 +598,7 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   if (s.S > 0) {
     uint16_t* hs = at<uint16_t>(workspace, L.shared_hidden);
     {
-      GemmArgs g = base_args(2 * s.cs, s.kd / 64, status);
+      GemmArgs g = base_args(kEpiSwiglu, 2 * s.cs, s.kd / 64, status);
       if ((rc = encode_2d(&g.tma_a, xa, s.T, s.kd, s.kd, kTileRows)) != SPX_OK) return rc;
       if ((rc = encode_3d(&g.tma_b, w->shared_w1, 1, static_cast<int64_t>(s.ncs) * 2 * s.cs, s.kd, 2 * s.cs)) !=
           SPX_OK)
@@ -608,21 +612,22 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
     }
     mark(6);
     {
-      GemmArgs g = base_args(s.bn_d, s.ksp / 64, status);
+      GemmArgs g = base_args(kEpiCombine, s.bn_d, s.ksp / 64, status);
       if ((rc = encode_2d(&g.tma_a, hs, s.T, s.ksp, s.ksp, kTileRows)) != SPX_OK) return rc;
       if ((rc = encode_3d(&g.tma_b, w->shared_w2, 1, s.d, s.ksp, s.bn_d)) != SPX_OK) return rc;
       g.m_rows = static_cast<int>(s.T);
       g.n_valid = s.d;
       g.out = out->update;
       g.ldo = s.d;
-      g.y_pairs = y;
+      g.y_rows = y;
+      g.y_rank = da.rank;
       g.ld_y = s.d;
       g.top_k = s.k;
       if ((rc = launch_gemm(kEpiCombine, g, ceil_div(s.T, kTileRows), s.gn_d, st)) != SPX_OK) return rc;
     }
   } else {
     mark(6);
-    if ((rc = launch_combine(y, s.T, s.d, s.k, out->update, st)) != SPX_OK) return rc;
+    if ((rc = launch_combine(y, da.rank, s.T, s.d, s.k, out->update, st)) != SPX_OK) return rc;
   }
   mark(7);
   return SPX_OK;

@@ -275,6 +275,7 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_scatter_kernel(cons
       const int pos = base + rank;
       a.order[pos] = static_cast<int>(p);
       a.src_row[pos] = static_cast<int>(p / a.top_k);
+      if (a.rank != nullptr) a.rank[p] = pos;
       if (a.sorted_weights != nullptr) a.sorted_weights[pos] = a.pair_weights[p];
       if ((peers & lt_mask) == 0) warp_base[warp * E + e] = base + __popc(peers);
     }

@@ -16,8 +16,9 @@
 //     kEpiStore    bf16(acc [+ bias])                   router logits
 //     kEpiSwiglu   bf16(bf16(silu(bf16(g))) * bf16(u))  expert / shared GEMM1,
 //                  B rows hold [gate chunk | up chunk]
-//     kEpiScatter  bf16(bf16(acc) * w_pair) -> Y[pair]  expert GEMM2
-//     kEpiCombine  bf16(bf16(acc) + sum_j Y[t*k+j])     shared GEMM2 + combine
+//     kEpiScatter  bf16(bf16(acc) * w_pos) -> Y[pos]    expert GEMM2: rows in sorted
+//                  (dispatch) order, written by TMA tile stores
+//     kEpiCombine  bf16(bf16(acc) + sum_j Y[rank[t*k+j]])  shared GEMM2 + combine
 // The BF16 rounding points follow the reference's tensor boundaries
 // (mESmaC/spalmer experts/bank.py:760-763, bank.py:970-978, nn/ffn.py:27-30,
 // experts/mixer.py:207); accumulation is FP32 throughout.
@@ -85,17 +86,21 @@ __device__ __forceinline__ void put8(uint16_t* dst, const uint4& v, int n) {
   }
 }
 
-// Combine one staged 8-column chunk with the k weighted expert rows of token
-// `rowid`: all k loads are issued before any is consumed.
-__device__ __forceinline__ void combine8(uint4& v, const uint16_t* y, int k, int64_t ld_y, int n) {
+// Combine one staged 8-column chunk with the k weighted expert rows of one
+// token (slot order, FP32): row q of the token is Y[rank[q]], `col` its
+// column.  All loads of a batch are in flight before any is used.
+__device__ __forceinline__ void combine8(uint4& v, const uint16_t* y, const int* rank, int k, int64_t ld_y,
+                                         int col, int n) {
   float acc[8] = {lo_f(v.x), hi_f(v.x), lo_f(v.y), hi_f(v.y), lo_f(v.z), hi_f(v.z), lo_f(v.w), hi_f(v.w)};
-  if (n >= 8 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0 && ((ld_y * 2) & 15) == 0) {
-    // Slots in batches of 8: every load of a batch is in flight before any is used.
+  if (n >= 8 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0 && ((ld_y * 2) & 15) == 0 && (col & 7) == 0) {
     for (int s0 = 0; s0 < k; s0 += 8) {
+      int r[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) r[q] = (s0 + q < k) ? __ldg(rank + s0 + q) : 0;
       uint4 t[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q)
-        if (s0 + q < k) t[q] = __ldg(reinterpret_cast<const uint4*>(y + (s0 + q) * ld_y));
+        if (s0 + q < k) t[q] = __ldg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(r[q]) * ld_y + col));
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         if (s0 + q < k) {
@@ -111,8 +116,10 @@ __device__ __forceinline__ void combine8(uint4& v, const uint16_t* y, int k, int
       }
     }
   } else {
-    for (int sl = 0; sl < k; ++sl)
-      for (int q = 0; q < n; ++q) acc[q] += bf16_to_f32(y[sl * ld_y + q]);
+    for (int sl = 0; sl < k; ++sl) {
+      const uint16_t* row = y + static_cast<int64_t>(rank[sl]) * ld_y + col;
+      for (int q = 0; q < n; ++q) acc[q] += bf16_to_f32(row[q]);
+    }
   }
   v = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
                  pack_bf16x2(acc[6], acc[7]));
@@ -120,13 +127,10 @@ __device__ __forceinline__ void combine8(uint4& v, const uint16_t* y, int k, int
 
 // One epilogue warp: TMEM lane quadrant `quad` (32 tile rows), output column
 // slices half, half + 2, ... of the tile (two warps share a quadrant).
-// `my_row` is the output row of this thread's tile row (the pair index for
-// kEpiScatter) and `my_w` its routing weight; the caller loads both before it
-// waits for the accumulator so their latency overlaps the MMAs.
+// `my_row` is the output row of this thread's tile row.
 template <int EPI>
 __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, uint8_t* stage, int quad, int half,
-                                             int lane, int row0, int rows, int n0, int nt, long long my_row,
-                                             float my_w) {
+                                             int lane, int row0, int rows, int n0, int nt, long long my_row) {
   constexpr int W = (EPI == kEpiSwiglu) ? 32 : 64;  // output columns per slice
   const int r = quad * 32 + lane;                   // tile row owned by this thread (its TMEM lane)
   const bool live = r < rows;
@@ -165,10 +169,6 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
           }
           hw[j / 2] = pack_bf16x2(f0, f1);
         }
-      } else if constexpr (EPI == kEpiScatter) {
-#pragma unroll
-        for (int j = 0; j < 64; j += 2)
-          hw[j / 2] = pack_bf16x2(bfr(__uint_as_float(v[j])) * my_w, bfr(__uint_as_float(v[j + 1])) * my_w);
       } else {  // kEpiCombine: the shared path's output, rounded to BF16
 #pragma unroll
         for (int j = 0; j < 64; j += 2) hw[j / 2] = pack_bf16x2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
@@ -188,10 +188,8 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
       const int n = min(8, valid - j * 8);
       if (ri < wrows && n > 0) {
         uint4 v = *reinterpret_cast<const uint4*>(stage + stage_off(ri, j));
-        if constexpr (EPI == kEpiCombine) {
-          const uint16_t* y = a.y_pairs + (rowid * a.top_k) * a.ld_y + gcol0 + j * 8;
-          combine8(v, y, a.top_k, a.ld_y, n);
-        }
+        if constexpr (EPI == kEpiCombine)
+          combine8(v, a.y_rows, a.y_rank + rowid * a.top_k, a.top_k, a.ld_y, gcol0 + j * 8, n);
         put8(out + rowid * a.ldo + gcol0 + j * 8, v, n);
       }
     }
@@ -203,6 +201,71 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
       uint16_t* dst = out + static_cast<int64_t>(row0 + r) * a.ldo;
       for (int col = a.n_tiles * a.chunk; col < a.h_cols; ++col) dst[col] = 0;
     }
+  }
+}
+
+// Expert GEMM2 epilogue: bf16(bf16(acc) * w) rows written in sorted order.
+// Each 32-row x 64-column slice is staged in one of the warp's two 4 KB
+// buffers (the 128B-swizzled layout of the output tensor map's box) and sent
+// with one TMA tile store, so the warp moves on while the copy drains.  A
+// warp whose 32 rows are not all inside the tile (the last tile of an expert)
+// stores its valid rows with plain stores instead: a box would spill into the
+// next expert's rows.  `slices` counts this warp's slices across tiles (it
+// picks the buffer); `committed` remembers whether the previous slice left a
+// bulk group behind.
+__device__ __forceinline__ void run_epilogue_rows(const GemmArgs& a, uint32_t taddr, uint8_t* stage, int quad,
+                                                  int half, int lane, int row0, int rows, int n0, float my_w,
+                                                  uint32_t& slices, bool& committed) {
+  const int wrows = rows - quad * 32;  // valid rows of this quadrant
+  if (wrows <= 0) return;
+  uint16_t* out = static_cast<uint16_t*>(a.out);
+  for (int s0 = half * 64; s0 < a.bn; s0 += 128) {
+    uint8_t* buf = stage + (slices & 1u) * kStageBytesPerWarp;
+    ++slices;
+    // The bulk store that last read `buf` (two slices ago) must be done reading.
+    if (lane == 0) {
+      if (committed)
+        bulk_wait_read<1>();
+      else
+        bulk_wait_read<0>();
+    }
+    __syncwarp();
+    const int w = min(64, a.bn - s0);
+    uint32_t v[64];
+    tmem_ld32(taddr + s0, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+    if (w > 32) tmem_ld32(taddr + s0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+    tmem_wait_ld();
+    uint32_t hw[32];
+#pragma unroll
+    for (int j = 0; j < 64; j += 2)
+      hw[j / 2] = pack_bf16x2(bfr(__uint_as_float(v[j])) * my_w, bfr(__uint_as_float(v[j + 1])) * my_w);
+#pragma unroll
+    for (int c = 0; c < 64; c += 16) stage_put16(buf, lane, c, &hw[c / 2]);
+    const int gcol0 = n0 + s0;
+    if (wrows >= 32 && a.tma_store) {
+      fence_proxy_async_smem();  // generic-proxy staging writes -> TMA reads
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&a.tma_out, buf, gcol0, row0 + quad * 32);
+        bulk_commit();
+      }
+      committed = true;
+    } else {
+      __syncwarp();
+      const int valid = min(w, a.n_valid - gcol0);
+      const int j = lane & 7;
+#pragma unroll 2
+      for (int step = 0; step < 8; ++step) {
+        const int ri = step * 4 + (lane >> 3);
+        const int n = min(8, valid - j * 8);
+        if (ri < wrows && n > 0) {
+          const uint4 val = *reinterpret_cast<const uint4*>(buf + stage_off(ri, j));
+          put8(out + static_cast<int64_t>(row0 + quad * 32 + ri) * a.ldo + gcol0 + j * 8, val, n);
+        }
+      }
+      committed = false;
+    }
+    __syncwarp();
   }
 }
 
@@ -391,8 +454,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   uint8_t* sa = smem;
   uint8_t* sb = smem + S * a_bytes;
   uint8_t* ssf = sb + S * b_bytes;                           // MX: [S][SFA atom | SFB atom]
-  uint8_t* stage_all = ssf + (MX ? S * kMxStageSfBytes : 0u);  // kGemmEpilogueWarps x kStageBytesPerWarp
-  uint64_t* full = reinterpret_cast<uint64_t*>(stage_all + kGemmEpilogueWarps * kStageBytesPerWarp);
+  // Epilogue staging: one 4 KB buffer per epilogue warp, two for the TMA-store epilogue.
+  constexpr int kStageBufs = (EPI == kEpiScatter) ? 2 : 1;
+  // 1024-byte aligned: the TMA store reads the buffers with the 128B swizzle.
+  uint8_t* stage_all = align_1024(ssf + (MX ? S * kMxStageSfBytes : 0u));
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_all + kGemmEpilogueWarps * kStageBufs * kStageBytesPerWarp);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;                 // [kMaxAccBufs] accumulator ready
   uint64_t* tempty = tfull + kMaxAccBufs;      // [kMaxAccBufs] accumulator drained
@@ -422,6 +488,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     fence_mbar_init();
     if (!a.gather) prefetch_tensormap(&a.tma_a);  // gathered A has no tensor map
     prefetch_tensormap(&a.tma_b);
+    if constexpr (EPI == kEpiScatter) {
+      if (a.tma_store) prefetch_tensormap(&a.tma_out);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, tmem_alloc_cols);
@@ -518,6 +587,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     // column slices (w-2)/4, +2, ...
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
+    uint8_t* my_stage = stage_all + (warp - 2) * kStageBufs * kStageBytesPerWarp;
+    uint32_t slices = 0;
+    bool committed = false;
     uint32_t lt = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++lt) {
       int group, row0, rows, nt;
@@ -528,11 +600,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       long long my_row = static_cast<long long>(row0) + r;
       float my_w = 0.0f;
       if constexpr (EPI == kEpiScatter) {
-        my_row = 0;
-        if (r < rows) {
-          my_row = a.pos_to_pair[row0 + r];
-          my_w = bf16_to_f32(a.pos_weight[row0 + r]);
-        }
+        if (r < rows) my_w = bf16_to_f32(a.pos_weight[row0 + r]);
       }
       int go = 1;
       if (lane == 0) go = mbar_wait(&tfull[b], tph, a.status, SPX_DEV_TIMEOUT_EPILOGUE) ? 1 : 0;
@@ -543,12 +611,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       if constexpr (MX && EPI == kEpiSwiglu) {
         run_epilogue_swiglu_mx(a, taddr, quad, half, lane, row0, rows, nt, &tempty[b]);  // releases early
       } else {
-        run_epilogue<EPI>(a, taddr, stage_all + (warp - 2) * kStageBytesPerWarp, quad, half, lane, row0, rows,
-                          nt * bn, nt, my_row, my_w);
+        if constexpr (EPI == kEpiScatter)
+          run_epilogue_rows(a, taddr, my_stage, quad, half, lane, row0, rows, nt * bn, my_w, slices, committed);
+        else
+          run_epilogue<EPI>(a, taddr, my_stage, quad, half, lane, row0, rows, nt * bn, nt, my_row);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[b]);
       }
+    }
+    if constexpr (EPI == kEpiScatter) {
+      if (lane == 0) bulk_wait_all();  // stores complete before the CTA (and its smem) goes away
+      __syncwarp();
     }
   }
   tc_fence_before();
@@ -614,25 +688,26 @@ int encode_3d(CUtensorMap* map, const void* base, int64_t groups, int64_t rows, 
   return r == CUDA_SUCCESS ? SPX_OK : SPX_ERR_DRIVER;
 }
 
-size_t gemm_smem_bytes(int bn, int stages, bool mx) {
+size_t gemm_smem_bytes(int bn, int stages, bool mx, int epi) {
   const size_t per_stage = kTileRows * 128 + static_cast<size_t>(bn) * 128 + (mx ? kMxStageSfBytes : 0);
-  return 1024 + static_cast<size_t>(stages) * per_stage + kGemmEpilogueWarps * kStageBytesPerWarp +
-         (2 * stages + 2 * kMaxAccBufs) * 8 + 16;
+  const size_t staging = static_cast<size_t>(kGemmEpilogueWarps) * kStageBytesPerWarp * (epi == kEpiScatter ? 2 : 1);
+  return 2048 + static_cast<size_t>(stages) * per_stage + staging + (2 * stages + 2 * kMaxAccBufs) * 8 + 16;
 }
 
 // As many stages as fit: the persistent producer keeps prefetching the next
 // tile's k-blocks, so stages beyond one tile's K still hide load latency.
-int gemm_pick_stages(int bn, int k_blocks, bool mx) {
+int gemm_pick_stages(int bn, int k_blocks, bool mx, int epi) {
   (void)k_blocks;
   int stages = 2;
   for (int s = 3; s <= 8; ++s)
-    if (gemm_smem_bytes(bn, s, mx) <= kGemmSmemBudget) stages = s;
+    if (gemm_smem_bytes(bn, s, mx, epi) <= kGemmSmemBudget) stages = s;
   return stages;
 }
 
 template <int EPI, bool MX>
 static int launch_gemm_t(const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream) {
-  const size_t smem = gemm_smem_bytes(a.bn, a.stages, MX);
+  const size_t smem = gemm_smem_bytes(a.bn, a.stages, MX, EPI);
+  if (smem > kGemmSmemBudget) return SPX_ERR_INVALID_ARG;
   if (int rc = ensure_max_dynamic_smem(reinterpret_cast<const void*>(gemm_kernel<EPI, MX>)); rc != SPX_OK) return rc;
   // Persistent grid: one CTA per SM, never more CTAs than (upper bound of) tiles.
   const int sms = device_sm_count();

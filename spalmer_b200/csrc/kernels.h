@@ -23,6 +23,8 @@ constexpr int kDispatchChunk = 2048;   // pairs per dispatch CTA
 constexpr int kDispatchWarps = 4;
 constexpr int kDispatchThreads = 32 * kDispatchWarps;
 
+// kEpiScatter writes the weighted expert rows in sorted (dispatch) order; the
+// combine gathers each token's k rows through the rank array.
 enum Epi : int { kEpiStore = 0, kEpiSwiglu = 1, kEpiScatter = 2, kEpiCombine = 3 };
 
 // MXFP8 lane: B-operand sources of the pack-time quantiser, and the tensor
@@ -73,6 +75,7 @@ struct DispatchArgs {
   int* num_tiles_mx;
   int* order;                // [P] argsort(stable) permutation
   int* src_row;              // [P] token row of each sorted position
+  int* rank;                 // [P] sorted position of each pair (inverse of order), or null
   const uint16_t* pair_weights;  // [P] routing weights in pair order, or null
   uint16_t* sorted_weights;  // [P] the same weights in sorted (dispatch) order, or null
   // statistics (any may be null)
@@ -116,9 +119,11 @@ struct GemmArgs {
   void* out;
   int64_t ldo;
   const uint16_t* bias;      // kEpiStore
-  const int* pos_to_pair;    // kEpiScatter: pair index of each sorted position
   const uint16_t* pos_weight;  // kEpiScatter: routing weight of each sorted position
-  const uint16_t* y_pairs;   // kEpiCombine
+  CUtensorMap tma_out;       // kEpiScatter: Y [P sorted rows, d] BF16, box {64, 32}, 128B swizzle
+  int tma_store;             // kEpiScatter: 1 = tma_out is valid (d % 64 == 0)
+  const uint16_t* y_rows;    // kEpiCombine: Y in sorted order
+  const int* y_rank;         // kEpiCombine: sorted position of each pair (t*k + slot)
   int64_t ld_y;
   int top_k;
   int* status;
@@ -141,8 +146,8 @@ int encode_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, in
               int elem_bytes = 2);
 int encode_3d(CUtensorMap* map, const void* base, int64_t groups, int64_t rows, int64_t cols, int box_rows,
               int elem_bytes = 2);
-size_t gemm_smem_bytes(int bn, int stages, bool mx = false);
-int gemm_pick_stages(int bn, int k_blocks, bool mx = false);
+size_t gemm_smem_bytes(int bn, int stages, bool mx, int epi);
+int gemm_pick_stages(int bn, int k_blocks, bool mx, int epi);
 // `mx` selects the block-scaled MXFP8 kernel (bn <= 128, k_blocks of 128 elements).
 int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream, bool mx = false);
 
@@ -154,7 +159,9 @@ int launch_mx_quantize_b(int mode, const uint16_t* a, const uint16_t* b, int gro
                          int rows_real, int k_real, int kp, int tile_rows, int d, int inter, int chunk, int64_t ld,
                          uint8_t* q, uint8_t* atoms, cudaStream_t stream);
 
-int launch_combine(const uint16_t* y, int64_t tokens, int d, int k, uint16_t* out, cudaStream_t stream);
+// update[t] = bf16(sum_j Y[rank[t*k + j]]): the routed-only combine (no shared path).
+int launch_combine(const uint16_t* y, const int* rank, int64_t tokens, int d, int k, uint16_t* out,
+                   cudaStream_t stream);
 
 int launch_pack_chunked_w1(const uint16_t* gate, const uint16_t* up, int experts, int d, int inter, int kd,
                            int chunk, int chunks, int transposed_src, uint16_t* out, cudaStream_t stream);

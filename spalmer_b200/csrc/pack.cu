@@ -1,5 +1,6 @@
 // Weight repacking (a derived cache of the reference state_dict) and the
-// standalone combine used when the layer has no shared path.
+// standalone combine used when the layer has no shared path (expert rows Y in
+// sorted order, gathered per token through the pair -> position rank).
 //
 // The reference stores expert projections as [E, d, I] / [E, I, d] ("x @ W",
 // experts/bank.py:52-54) and the shared SwiGLU as nn.Linear [out, in]
@@ -70,9 +71,9 @@ __global__ void pad_rows_kernel(const uint16_t* __restrict__ src, int64_t rows, 
   }
 }
 
-// update[t] = bf16(sum_j Y[t*k + j]) in FP32, 8 columns per thread.
-__global__ void combine_kernel(const uint16_t* __restrict__ y, int64_t tokens, int d, int k,
-                               uint16_t* __restrict__ out) {
+// update[t] = bf16(sum_j Y[rank[t*k + j]]) in FP32 (slot order), 8 columns per thread.
+__global__ void combine_kernel(const uint16_t* __restrict__ y, const int* __restrict__ rank, int64_t tokens, int d,
+                               int k, uint16_t* __restrict__ out) {
   const int vec = d / 8;
   const int64_t total = tokens * vec;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
@@ -81,7 +82,8 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, int64_t tokens, i
     const int c = static_cast<int>(idx - t * vec) * 8;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int j = 0; j < k; ++j) {
-      const uint4 q = *reinterpret_cast<const uint4*>(y + (t * k + j) * d + c);
+      const int64_t r = rank[t * k + j];
+      const uint4 q = *reinterpret_cast<const uint4*>(y + r * d + c);
       const uint16_t* h = reinterpret_cast<const uint16_t*>(&q);
 #pragma unroll
       for (int q8 = 0; q8 < 8; ++q8) acc[q8] += bf16_to_f32(h[q8]);
@@ -94,15 +96,15 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, int64_t tokens, i
   }
 }
 
-__global__ void combine_scalar_kernel(const uint16_t* __restrict__ y, int64_t tokens, int d, int k,
-                                      uint16_t* __restrict__ out) {
+__global__ void combine_scalar_kernel(const uint16_t* __restrict__ y, const int* __restrict__ rank, int64_t tokens,
+                                      int d, int k, uint16_t* __restrict__ out) {
   const int64_t total = tokens * d;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t t = idx / d;
     const int c = static_cast<int>(idx - t * d);
     float acc = 0.0f;
-    for (int j = 0; j < k; ++j) acc += bf16_to_f32(y[(t * k + j) * d + c]);
+    for (int j = 0; j < k; ++j) acc += bf16_to_f32(y[static_cast<int64_t>(rank[t * k + j]) * d + c]);
     out[idx] = f32_to_bf16_rne(acc);
   }
 }
@@ -133,13 +135,14 @@ int launch_pad_rows(const uint16_t* src, int64_t rows, int cols, int ld_out, uin
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 
-int launch_combine(const uint16_t* y, int64_t tokens, int d, int k, uint16_t* out, cudaStream_t stream) {
+int launch_combine(const uint16_t* y, const int* rank, int64_t tokens, int d, int k, uint16_t* out,
+                   cudaStream_t stream) {
   const bool vec_ok = (d % 8) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0 &&
                       (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
   if (vec_ok) {
-    combine_kernel<<<grid_for(tokens * (d / 8)), 256, 0, stream>>>(y, tokens, d, k, out);
+    combine_kernel<<<grid_for(tokens * (d / 8)), 256, 0, stream>>>(y, rank, tokens, d, k, out);
   } else {
-    combine_scalar_kernel<<<grid_for(tokens * d), 256, 0, stream>>>(y, tokens, d, k, out);
+    combine_scalar_kernel<<<grid_for(tokens * d), 256, 0, stream>>>(y, rank, tokens, d, k, out);
   }
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
