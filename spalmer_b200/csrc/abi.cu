@@ -104,7 +104,7 @@ MxPackSizes mx_pack_sizes(const Shape& s) {
 
 struct Layout {
   size_t small, tie_rows, lb_partial, chunk_hist, counts, starts, tiles, order, src_row, rank, sorted_w;
-  size_t hidden, y, shared_hidden, logits, x_pad, util, stats, ratios, aux;
+  size_t hidden, y, shared_hidden, shared_out, logits, x_pad, util, stats, ratios, aux;
   size_t x_q, x_sf, h_q, h_sf, tiles_mx;  // MXFP8 lane (empty otherwise)
   size_t total;
 };
@@ -131,6 +131,7 @@ Layout make_layout(const Shape& s) {
   L.hidden = take(2 * static_cast<size_t>(s.P) * s.kp);
   L.y = take(2 * static_cast<size_t>(s.P) * s.d);
   L.shared_hidden = take(s.S > 0 ? 2 * static_cast<size_t>(s.T) * s.ksp : 0);
+  L.shared_out = take(s.S > 0 ? 2 * static_cast<size_t>(s.T) * s.d : 0);
   L.logits = take(2 * static_cast<size_t>(s.T) * s.E);
   L.x_pad = take(s.kd != s.d ? 2 * static_cast<size_t>(s.T) * s.kd : 0);
   L.util = take(sizeof(float) * s.E);
@@ -611,23 +612,22 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
       if ((rc = launch_gemm(kEpiSwiglu, g, ceil_div(s.T, kTileRows), s.ncs, st)) != SPX_OK) return rc;
     }
     mark(6);
+    uint16_t* so = at<uint16_t>(workspace, L.shared_out);
     {
-      GemmArgs g = base_args(kEpiCombine, s.bn_d, s.ksp / 64, status);
+      GemmArgs g = base_args(kEpiStore, s.bn_d, s.ksp / 64, status);
       if ((rc = encode_2d(&g.tma_a, hs, s.T, s.ksp, s.ksp, kTileRows)) != SPX_OK) return rc;
       if ((rc = encode_3d(&g.tma_b, w->shared_w2, 1, s.d, s.ksp, s.bn_d)) != SPX_OK) return rc;
       g.m_rows = static_cast<int>(s.T);
       g.n_valid = s.d;
-      g.out = out->update;
+      g.out = so;
       g.ldo = s.d;
-      g.y_rows = y;
-      g.y_rank = da.rank;
-      g.ld_y = s.d;
-      g.top_k = s.k;
-      if ((rc = launch_gemm(kEpiCombine, g, ceil_div(s.T, kTileRows), s.gn_d, st)) != SPX_OK) return rc;
+      if ((rc = launch_gemm(kEpiStore, g, ceil_div(s.T, kTileRows), s.gn_d, st)) != SPX_OK) return rc;
     }
+    // update = bf16(shared + sum of the token's k expert rows), streamed.
+    if ((rc = launch_combine(y, da.rank, so, s.T, s.d, s.k, out->update, st)) != SPX_OK) return rc;
   } else {
     mark(6);
-    if ((rc = launch_combine(y, da.rank, s.T, s.d, s.k, out->update, st)) != SPX_OK) return rc;
+    if ((rc = launch_combine(y, da.rank, nullptr, s.T, s.d, s.k, out->update, st)) != SPX_OK) return rc;
   }
   mark(7);
   return SPX_OK;

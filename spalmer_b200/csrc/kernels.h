@@ -159,9 +159,9 @@ int launch_mx_quantize_b(int mode, const uint16_t* a, const uint16_t* b, int gro
                          int rows_real, int k_real, int kp, int tile_rows, int d, int inter, int chunk, int64_t ld,
                          uint8_t* q, uint8_t* atoms, cudaStream_t stream);
 
-// update[t] = bf16(sum_j Y[rank[t*k + j]]): the routed-only combine (no shared path).
-int launch_combine(const uint16_t* y, const int* rank, int64_t tokens, int d, int k, uint16_t* out,
-                   cudaStream_t stream);
+// update[t] = bf16(base[t] + sum_j Y[rank[t*k + j]]) (base: shared SwiGLU output or null).
+int launch_combine(const uint16_t* y, const int* rank, const uint16_t* base, int64_t tokens, int d, int k,
+                   uint16_t* out, cudaStream_t stream);
 
 int launch_pack_chunked_w1(const uint16_t* gate, const uint16_t* up, int experts, int d, int inter, int kd,
                            int chunk, int chunks, int transposed_src, uint16_t* out, cudaStream_t stream);

@@ -71,9 +71,15 @@ __global__ void pad_rows_kernel(const uint16_t* __restrict__ src, int64_t rows, 
   }
 }
 
-// update[t] = bf16(sum_j Y[rank[t*k + j]]) in FP32 (slot order), 8 columns per thread.
-__global__ void combine_kernel(const uint16_t* __restrict__ y, const int* __restrict__ rank, int64_t tokens, int d,
-                               int k, uint16_t* __restrict__ out) {
+// update[t] = bf16(base[t] + sum_j Y[rank[t*k + j]]) in FP32 (base first, then
+// slots in order), 8 columns per thread; base is the shared SwiGLU output
+// (BF16) or absent.  Consecutive threads take consecutive 16-byte chunks of
+// one token, so every slot's row is read in whole 128-byte lines; a thread
+// issues all k row loads before it adds any.
+template <int KMAX>
+__global__ void combine_kernel(const uint16_t* __restrict__ y, const int* __restrict__ rank,
+                               const uint16_t* __restrict__ base, int64_t tokens, int d, int k,
+                               uint16_t* __restrict__ out) {
   const int vec = d / 8;
   const int64_t total = tokens * vec;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
@@ -81,12 +87,32 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, const int* __rest
     const int64_t t = idx / vec;
     const int c = static_cast<int>(idx - t * vec) * 8;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int j = 0; j < k; ++j) {
-      const int64_t r = rank[t * k + j];
-      const uint4 q = *reinterpret_cast<const uint4*>(y + r * d + c);
-      const uint16_t* h = reinterpret_cast<const uint16_t*>(&q);
+    if (base != nullptr) {
+      const uint4 b = __ldg(reinterpret_cast<const uint4*>(base + t * d + c));
+      const uint32_t w[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-      for (int q8 = 0; q8 < 8; ++q8) acc[q8] += bf16_to_f32(h[q8]);
+      for (int q = 0; q < 4; ++q) {
+        acc[2 * q] = __uint_as_float(w[q] << 16);
+        acc[2 * q + 1] = __uint_as_float(w[q] & 0xFFFF0000u);
+      }
+    }
+    int r[KMAX];
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) r[j] = j < k ? __ldg(rank + t * k + j) : 0;
+    uint4 v[KMAX];
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j)
+      if (j < k) v[j] = __ldg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(r[j]) * d + c));
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) {
+      if (j < k) {
+        const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc[2 * q] += __uint_as_float(w[q] << 16);
+          acc[2 * q + 1] += __uint_as_float(w[q] & 0xFFFF0000u);
+        }
+      }
     }
     uint4 o;
     uint16_t* oh = reinterpret_cast<uint16_t*>(&o);
@@ -96,14 +122,15 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, const int* __rest
   }
 }
 
-__global__ void combine_scalar_kernel(const uint16_t* __restrict__ y, const int* __restrict__ rank, int64_t tokens,
-                                      int d, int k, uint16_t* __restrict__ out) {
+__global__ void combine_scalar_kernel(const uint16_t* __restrict__ y, const int* __restrict__ rank,
+                                      const uint16_t* __restrict__ base, int64_t tokens, int d, int k,
+                                      uint16_t* __restrict__ out) {
   const int64_t total = tokens * d;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t t = idx / d;
     const int c = static_cast<int>(idx - t * d);
-    float acc = 0.0f;
+    float acc = base != nullptr ? bf16_to_f32(base[idx]) : 0.0f;
     for (int j = 0; j < k; ++j) acc += bf16_to_f32(y[static_cast<int64_t>(rank[t * k + j]) * d + c]);
     out[idx] = f32_to_bf16_rne(acc);
   }
@@ -135,14 +162,22 @@ int launch_pad_rows(const uint16_t* src, int64_t rows, int cols, int ld_out, uin
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 
-int launch_combine(const uint16_t* y, const int* rank, int64_t tokens, int d, int k, uint16_t* out,
-                   cudaStream_t stream) {
+int launch_combine(const uint16_t* y, const int* rank, const uint16_t* base, int64_t tokens, int d, int k,
+                   uint16_t* out, cudaStream_t stream) {
   const bool vec_ok = (d % 8) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0 &&
-                      (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+                      (reinterpret_cast<uintptr_t>(out) & 15u) == 0 &&
+                      (base == nullptr || (reinterpret_cast<uintptr_t>(base) & 15u) == 0);
   if (vec_ok) {
-    combine_kernel<<<grid_for(tokens * (d / 8)), 256, 0, stream>>>(y, rank, tokens, d, k, out);
+    const int64_t total = tokens * (d / 8);
+    int64_t g = (total + 255) / 256;
+    if (g > 148 * 64) g = 148 * 64;
+    const int grid = static_cast<int>(g < 1 ? 1 : g);
+    if (k <= 8)
+      combine_kernel<8><<<grid, 256, 0, stream>>>(y, rank, base, tokens, d, k, out);
+    else
+      combine_kernel<kMaxTopK><<<grid, 256, 0, stream>>>(y, rank, base, tokens, d, k, out);
   } else {
-    combine_scalar_kernel<<<grid_for(tokens * d), 256, 0, stream>>>(y, rank, tokens, d, k, out);
+    combine_scalar_kernel<<<grid_for(tokens * d), 256, 0, stream>>>(y, rank, base, tokens, d, k, out);
   }
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
