@@ -16,9 +16,9 @@
 //     kEpiStore    bf16(acc [+ bias])                   router logits
 //     kEpiSwiglu   bf16(bf16(silu(bf16(g))) * bf16(u))  expert / shared GEMM1,
 //                  B rows hold [gate chunk | up chunk]
+//     kEpiStore    (also) shared down projection -> shared output
 //     kEpiScatter  bf16(bf16(acc) * w_pos) -> Y[pos]    expert GEMM2: rows in sorted
 //                  (dispatch) order, written by TMA tile stores
-//     kEpiCombine  bf16(bf16(acc) + sum_j Y[rank[t*k+j]])  shared GEMM2 + combine
 // The BF16 rounding points follow the reference's tensor boundaries
 // (mESmaC/spalmer experts/bank.py:760-763, bank.py:970-978, nn/ffn.py:27-30,
 // experts/mixer.py:207); accumulation is FP32 throughout.
@@ -86,45 +86,6 @@ __device__ __forceinline__ void put8(uint16_t* dst, const uint4& v, int n) {
   }
 }
 
-// Combine one staged 8-column chunk with the k weighted expert rows of one
-// token (slot order, FP32): row q of the token is Y[rank[q]], `col` its
-// column.  All loads of a batch are in flight before any is used.
-__device__ __forceinline__ void combine8(uint4& v, const uint16_t* y, const int* rank, int k, int64_t ld_y,
-                                         int col, int n) {
-  float acc[8] = {lo_f(v.x), hi_f(v.x), lo_f(v.y), hi_f(v.y), lo_f(v.z), hi_f(v.z), lo_f(v.w), hi_f(v.w)};
-  if (n >= 8 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0 && ((ld_y * 2) & 15) == 0 && (col & 7) == 0) {
-    for (int s0 = 0; s0 < k; s0 += 8) {
-      int r[8];
-#pragma unroll
-      for (int q = 0; q < 8; ++q) r[q] = (s0 + q < k) ? __ldg(rank + s0 + q) : 0;
-      uint4 t[8];
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (s0 + q < k) t[q] = __ldg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(r[q]) * ld_y + col));
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        if (s0 + q < k) {
-          acc[0] += lo_f(t[q].x);
-          acc[1] += hi_f(t[q].x);
-          acc[2] += lo_f(t[q].y);
-          acc[3] += hi_f(t[q].y);
-          acc[4] += lo_f(t[q].z);
-          acc[5] += hi_f(t[q].z);
-          acc[6] += lo_f(t[q].w);
-          acc[7] += hi_f(t[q].w);
-        }
-      }
-    }
-  } else {
-    for (int sl = 0; sl < k; ++sl) {
-      const uint16_t* row = y + static_cast<int64_t>(rank[sl]) * ld_y + col;
-      for (int q = 0; q < n; ++q) acc[q] += bf16_to_f32(row[q]);
-    }
-  }
-  v = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
-                 pack_bf16x2(acc[6], acc[7]));
-}
-
 // One epilogue warp: TMEM lane quadrant `quad` (32 tile rows), output column
 // slices half, half + 2, ... of the tile (two warps share a quadrant).
 // `my_row` is the output row of this thread's tile row.
@@ -169,9 +130,6 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
           }
           hw[j / 2] = pack_bf16x2(f0, f1);
         }
-      } else {  // kEpiCombine: the shared path's output, rounded to BF16
-#pragma unroll
-        for (int j = 0; j < 64; j += 2) hw[j / 2] = pack_bf16x2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
       }
     }
 #pragma unroll
@@ -188,8 +146,6 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
       const int n = min(8, valid - j * 8);
       if (ri < wrows && n > 0) {
         uint4 v = *reinterpret_cast<const uint4*>(stage + stage_off(ri, j));
-        if constexpr (EPI == kEpiCombine)
-          combine8(v, a.y_rows, a.y_rank + rowid * a.top_k, a.top_k, a.ld_y, gcol0 + j * 8, n);
         put8(out + rowid * a.ldo + gcol0 + j * 8, v, n);
       }
     }
@@ -747,8 +703,6 @@ int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t
       return launch_gemm_t<kEpiSwiglu, false>(a, grid_m, grid_n, stream);
     case kEpiScatter:
       return launch_gemm_t<kEpiScatter, false>(a, grid_m, grid_n, stream);
-    case kEpiCombine:
-      return launch_gemm_t<kEpiCombine, false>(a, grid_m, grid_n, stream);
     default:
       return SPX_ERR_INVALID_ARG;
   }

@@ -24,8 +24,8 @@ constexpr int kDispatchWarps = 4;
 constexpr int kDispatchThreads = 32 * kDispatchWarps;
 
 // kEpiScatter writes the weighted expert rows in sorted (dispatch) order; the
-// combine gathers each token's k rows through the rank array.
-enum Epi : int { kEpiStore = 0, kEpiSwiglu = 1, kEpiScatter = 2, kEpiCombine = 3 };
+// combine (pack.cu) gathers each token's k rows through the rank array.
+enum Epi : int { kEpiStore = 0, kEpiSwiglu = 1, kEpiScatter = 2 };
 
 // MXFP8 lane: B-operand sources of the pack-time quantiser, and the tensor
 // memory plan of the block-scaled GEMM: accumulators in columns [0, 384)
@@ -122,10 +122,6 @@ struct GemmArgs {
   const uint16_t* pos_weight;  // kEpiScatter: routing weight of each sorted position
   CUtensorMap tma_out;       // kEpiScatter: Y [P sorted rows, d] BF16, box {64, 32}, 128B swizzle
   int tma_store;             // kEpiScatter: 1 = tma_out is valid (d % 64 == 0)
-  const uint16_t* y_rows;    // kEpiCombine: Y in sorted order
-  const int* y_rank;         // kEpiCombine: sorted position of each pair (t*k + slot)
-  int64_t ld_y;
-  int top_k;
   int* status;
 };
 
