@@ -50,6 +50,11 @@ CONFIGS = {
                            active_experts=4), batch=2, seq=256, cpu_sample=512),
 }
 METRIC = "routed tokens/sec per MoE layer"
+# DRAM bytes (read + write) of the roofline stage's launches in one forward,
+# from an ncu capture of the same workload (dram__bytes_read.sum +
+# dram__bytes_write.sum over the stage's launches): hidden-state quantiser +
+# both expert GEMM1 lanes for m100.
+STAGE_TRAFFIC_BYTES = {"m100": 624.8e6}
 CPU_ALL_BF16_NOTE = ("; all experts BF16: the reference has no CPU MXFP8 path and rejects BF16 experts "
                      "mixed with MXFP8 (experts/config.py:140-161)")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
@@ -381,11 +386,12 @@ def run_ours(args) -> None:
             "e2e": {"value": e2e_value, "unit": "tokens/s",
                     "h2d_bytes_per_step": tokens * config.d_model * 2,
                     "d2h_bytes_per_step": tokens * config.d_model * 2 + 2},
-            "gpu_launches": K * (13 if lane is not None else 10),
+            "gpu_launches": K * (14 if lane is not None else 11),
             "roofline": {"bound": "tensor",
                          "kernel": "gemm_kernel<kEpiSwiglu> (expert GEMM1, gathered rows; BF16 and MXFP8 lanes)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak, "traffic": STAGE_TRAFFIC_BYTES.get(args.config),
+                         "traffic_unit": "bytes per forward (ncu dram read+write of the stage's launches)",
                          "mxfp8_pair_share": mx_share,
                          "peak_source": f"{pk['source']} bf16 burst; MXFP8 share at 2x"},
             "layer_tensor_tflops": sum(flops.values()) / (ms_per_step / 1e3) / 1e12,
