@@ -42,6 +42,11 @@ CONFIGS = {
     # The same shape with every expert in BF16.
     "m100_bf16": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
                                active_experts=8), batch=64, seq=1024, cpu_sample=1024),
+    # skewed expert parallel (Zipf(1.1) router bias), 131072 tokens in total,
+    # experts sharded E/N per GPU with NCCL all-to-all (strong scaling).  S = 2*d (reference default).
+    "ep_skew": dict(cfg=dict(d_model=1024, num_experts=200, expert_inter_dim=256, shared_inter_dim=2048,
+                             active_experts=8, router_bias=True), batch=128, seq=1024, cpu_sample=256,
+                    zipf=True, expert_parallel=True),
     # 10M-preset shape.
     "m10": dict(cfg=dict(d_model=256, num_experts=200, expert_inter_dim=64, shared_inter_dim=256,
                          active_experts=8), batch=32, seq=512, cpu_sample=4096),
@@ -91,6 +96,7 @@ def build_mixer(spec: dict, device=None):
     from spalmer_b200 import B200MicroExpertChannelMixer, MicroExpertsConfig
 
     fraction = spec.get("mxfp8_fraction", 0.0)
+    zipf = spec.get("zipf", False)
     cfg = dict(spec["cfg"])
     if fraction > 0:
         cfg.update(expert_weight_format="mxfp8", expert_activation_format="mxfp8",
@@ -103,6 +109,14 @@ def build_mixer(spec: dict, device=None):
         lane = mxfp8_experts(config.num_experts, fraction)
         with torch.no_grad():
             mixer.potentiation_controller.promoted_mask.copy_(~lane)
+    if zipf:
+        # b_e = alpha * ln(rank_e) over randperm(E, seed 3); alpha fitted for Zipf(1.1) popularity
+        alpha = json.loads((ROOT / "tests" / "golden" / "zipf_ep_skew.json").read_text())["alpha"]
+        perm = torch.randperm(config.num_experts, generator=torch.Generator().manual_seed(3))
+        rank = torch.empty(config.num_experts)
+        rank[perm] = torch.arange(1, config.num_experts + 1, dtype=torch.float32)
+        with torch.no_grad():
+            mixer.router.proj.bias.copy_(alpha * torch.log(rank))
     if device is not None:
         mixer = mixer.to(device)
     return mixer, lane
@@ -124,9 +138,16 @@ def layer_flops(cfg: dict, tokens: int) -> dict:
 def workload_config(name: str, world: int) -> dict:
     spec = CONFIGS[name]
     cfg = spec["cfg"]
+    ep = spec.get("expert_parallel", False)
+    extra = {}
+    if ep:
+        extra = {"total_tokens": spec["batch"] * spec["seq"], "experts_per_gpu": cfg["num_experts"] // world,
+                 "router_bias": "Zipf(1.1) popularity: b_e = alpha*ln(rank_e), alpha from tests/golden/zipf_ep_skew.json",
+                 "exchange": "NCCL all_to_all_single (counts, rows out, rows back); one host read of the counts"}
     return {
-        "workload": f"{name}: SPALMER micro-expert layer forward",
-        "tokens_per_gpu": spec["batch"] * spec["seq"],
+        "workload": f"{name}: SPALMER micro-expert layer forward" + (" (expert parallel)" if ep and world > 1 else ""),
+        **extra,
+        "tokens_per_gpu": spec["batch"] * spec["seq"] // (world if ep else 1),
         "batch": spec["batch"], "seq_len": spec["seq"],
         "d_model": cfg["d_model"], "num_experts": cfg["num_experts"],
         "expert_inter_dim": cfg["expert_inter_dim"], "top_k": cfg["active_experts"],
@@ -136,7 +157,7 @@ def workload_config(name: str, world: int) -> dict:
                              if spec.get("mxfp8_fraction") else "BF16 for all experts"),
         "weights": "random init, torch.manual_seed(0), N(0,0.02)",
         "l2": "inputs larger than L2: two 100.7 MB hidden-state batches alternated + 121.6 MB weights; steps timed back to back",
-        "parallelism": f"dp{world}",
+        "parallelism": f"ep{world}" if ep and world > 1 else f"dp{world}",
     }
 
 
@@ -407,6 +428,121 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+def run_ep(args) -> None:
+    """Strong-scaled expert-parallel forward: the configuration's tokens split
+    over the ranks, experts sharded E/N per GPU, rows exchanged over NCCL."""
+
+    world, rank, local = init_dist()
+    import torch.distributed as dist
+
+    from spalmer_b200.ep import ExpertParallelMixer
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    spec = CONFIGS[args.config]
+    total = spec["batch"] * spec["seq"]
+    batch = spec["batch"] // world
+    seq = spec["seq"]
+    tokens = batch * seq
+    mixer, _ = build_mixer(spec, device)
+    config = mixer.config
+    layer = ExpertParallelMixer(mixer) if world > 1 else None
+    x_cpu = torch.randn(spec["batch"], seq, config.d_model, generator=torch.Generator().manual_seed(1))
+    x_cpu = x_cpu.to(torch.bfloat16)[rank * batch:(rank + 1) * batch].contiguous()
+    x_host = x_cpu.pin_memory()
+    x_bufs = [x_host.to(device), x_host.roll(1, dims=0).to(device)]
+    K, W = args.steps, args.warmup
+
+    def step(x):
+        if layer is not None:
+            return layer(x)["update"]
+        return mixer(x).update
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    with torch.inference_mode():
+        for i in range(W):
+            out = step(x_bufs[i % 2])
+        torch.cuda.synchronize()
+        barrier()
+        sampler = ClockSampler(local)
+        time.sleep(0.3)
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for i in range(K):
+            out = step(x_bufs[i % 2])
+        t1.record()
+        torch.cuda.synchronize()
+        barrier()
+        clocks = sampler.stop()
+        total_ms = t0.elapsed_time(t1)
+        loads = None
+        if layer is not None:
+            r = layer(x_bufs[0])
+            loads = r["recv_rows"]
+        # e2e: pinned H2D of this rank's tokens, forward, D2H of the update, per step
+        out_host = torch.empty(batch, seq, config.d_model, dtype=torch.bfloat16).pin_memory()
+        xd = torch.empty_like(x_bufs[0])
+        for _ in range(W):
+            xd.copy_(x_host, non_blocking=True)
+            out_host.copy_(step(xd), non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(K):
+            xd.copy_(x_host, non_blocking=True)
+            out_host.copy_(step(xd), non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = e0.elapsed_time(e1)
+    t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
+    recv = torch.tensor([float(sum(loads)) if loads else float(tokens * config.active_experts)],
+                        dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        all_recv = [torch.zeros_like(recv) for _ in range(world)]
+        dist.all_gather(all_recv, recv)
+        recv_loads = [float(v) for v in all_recv]
+    else:
+        recv_loads = [float(recv)]
+    total_ms, e2e_ms = float(t[0]), float(t[1])
+    ms_per_step = total_ms / K
+    if rank == 0:
+        pk = peaks()
+        flops = sum(layer_flops(spec["cfg"], total).values()) / world
+        line = {
+            "metric": METRIC, "value": total / (ms_per_step / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) hidden states, seeded random-init weights, Zipf router bias)",
+            "config": workload_config(args.config, world),
+            "e2e": {"value": total / (e2e_ms / K / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": tokens * config.d_model * 2, "d2h_bytes_per_step": tokens * config.d_model * 2},
+            "gpu_launches": K * (13 if world > 1 else 11),
+            "roofline": {"bound": "tensor", "kernel": "whole layer per GPU (expert-parallel stages)",
+                         "achieved": flops / (ms_per_step / 1e3) / 1e12, "peak": pk["bf16_tflops_sustained"] or pk["bf16_tflops"],
+                         "unit": "TFLOP/s", "traffic": None, "peak_source": f"{pk['source']} bf16 sustained"},
+            "expert_rows_per_gpu": recv_loads,
+            "max_over_mean_expert_load": max(recv_loads) / (sum(recv_loads) / len(recv_loads)),
+        }
+        line["roofline"]["frac"] = line["roofline"]["achieved"] / line["roofline"]["peak"]
+        if clocks is not None:
+            line["clocks"] = clocks
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -420,6 +556,8 @@ def main() -> None:
         args.warmup = 3
     if args.impl == "reference":
         run_reference_arm(args)
+    elif CONFIGS[args.config].get("expert_parallel"):
+        run_ep(args)
     else:
         run_ours(args)
 

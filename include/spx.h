@@ -26,6 +26,18 @@
  *                      RCEIL)                            experts/native.py:91-110
  *   spx_mxfp8_mm_nt    _mxfp8_mm_nt (left @ right_rows.T, both MXFP8, BF16 out)
  *                                                        experts/native.py:113-140
+ *
+ * Stage entry points (expert parallelism: the caller moves rows between GPUs
+ * with NCCL all-to-all between them; on one GPU they compose to
+ * spx_layer_forward):
+ *   spx_layer_route    router + selection + dispatch     experts/mixer.py:176-199,
+ *                                                        bank.py:721-736
+ *   spx_gather_rows    hidden_states[token_index] in dispatch order   bank.py:751
+ *   spx_experts_forward grouped expert SwiGLU of rows with given expert ids
+ *                      (unweighted)                      bank.py:740-763
+ *   spx_shared_forward SwiGLU.forward                    nn/ffn.py:27-30
+ *   spx_combine        _weighted_expert_updates + index_add + shared add
+ *                                                        bank.py:764-778, mixer.py:207
  */
 #ifndef SPX_H_
 #define SPX_H_
@@ -37,7 +49,7 @@
 extern "C" {
 #endif
 
-#define SPX_ABI_VERSION 2
+#define SPX_ABI_VERSION 3
 
 #define SPX_OK 0
 #define SPX_ERR_INVALID_ARG -1
@@ -126,6 +138,8 @@ typedef struct spx_layer_outputs {
   uint16_t* router_logits;         /* [T, E] receives router GEMM output | NULL */
   void* const* stage_events;       /* NULL, or SPX_STAGE_EVENTS cudaEvent_t handles recorded
                                       on `stream` at the stage boundaries below            */
+  int32_t* pair_rank;              /* [T*k] sorted position of each pair (inverse of
+                                      dispatch_order) | NULL; required by spx_layer_route  */
 } spx_layer_outputs;
 
 /* Stage boundaries recorded into spx_layer_outputs.stage_events:
@@ -143,7 +157,9 @@ int spx_layer_sizes(const spx_layer_dims* dims, size_t* workspace_bytes, spx_pac
 /* BF16 -> BF16 softplus table (beta 1, threshold 20) for all 65536 inputs. */
 int spx_softplus_table(uint16_t* table, void* stream);
 
-/* Repack the reference state_dict into the kernel layouts (outputs sized by spx_layer_sizes). */
+/* Repack the reference state_dict into the kernel layouts (outputs sized by spx_layer_sizes).
+ * expert_w1/expert_w2 may be NULL (with gate/up/down) to pack only the router
+ * and shared weights. */
 int spx_pack_weights(const spx_layer_dims* dims, const spx_reference_weights* src,
                      uint16_t* router_weight, uint16_t* expert_w1, uint16_t* expert_w2,
                      uint16_t* shared_w1, uint16_t* shared_w2, void* stream);
@@ -186,6 +202,34 @@ int spx_dispatch(const spx_layer_dims* dims, const int64_t* expert_ids, int32_t*
 int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* weights,
                       const uint16_t* hidden, const spx_layer_outputs* outputs, void* workspace,
                       void* stream);
+
+/* Router GEMM (or dims' injected logits), selection and dispatch of `hidden`
+ * [T, d]: fills router_scores, expert_ids, routing_weights, the statistics,
+ * dispatch_order, expert_counts and pair_rank (all required but the
+ * statistics).  No expert or shared work. */
+int spx_layer_route(const spx_layer_dims* dims, const spx_packed_weights* weights, const uint16_t* hidden,
+                    const spx_layer_outputs* outputs, void* workspace, void* stream);
+
+/* out[i, :] = src[index[i] / index_div, :] for BF16 rows of d elements. */
+int spx_gather_rows(const uint16_t* src, int64_t ld_src, const int32_t* index, int32_t index_div, int64_t rows,
+                    int32_t d, uint16_t* out, int64_t ld_out, void* stream);
+
+/* Grouped SwiGLU experts of `rows` [R, d], row i through expert row_expert[i]
+ * (0..num_experts-1 of `weights`): out_rows[i] = bf16(down(silu(gate x) *
+ * up x)), unweighted, in input row order.  dims: tokens = R, top_k = 1,
+ * num_experts = the local experts, shared_dim = 0. */
+int spx_experts_forward(const spx_layer_dims* dims, const spx_packed_weights* weights, const uint16_t* rows,
+                        const int64_t* row_expert, uint16_t* out_rows, void* workspace, void* stream);
+
+/* Shared SwiGLU of `hidden` [T, d] into shared_out [T, d] (dims->shared_dim > 0). */
+int spx_shared_forward(const spx_layer_dims* dims, const spx_packed_weights* weights, const uint16_t* hidden,
+                       uint16_t* shared_out, void* workspace, void* stream);
+
+/* update[t] = bf16(shared[t] + sum_j bf16(expert_rows[pair_rank[t*k+j]] * w[t*k+j]))
+ * in FP32, slots in order; pair_weights NULL = rows already weighted, shared
+ * NULL = no shared path. */
+int spx_combine(const uint16_t* expert_rows, const int32_t* pair_rank, const uint16_t* pair_weights,
+                const uint16_t* shared, int64_t tokens, int32_t d, int32_t top_k, uint16_t* update, void* stream);
 
 /* spx_dispatch without a workspace: same outputs, no device allocation by
  * anyone.  No counterpart in the reference; it exists for callers that cannot

@@ -41,9 +41,14 @@ EXPORTED = (
     "spx_mxfp8_quantize_rows",
     "spx_mxfp8_mm_workspace",
     "spx_mxfp8_mm_nt",
+    "spx_layer_route",
+    "spx_gather_rows",
+    "spx_experts_forward",
+    "spx_shared_forward",
+    "spx_combine",
 )
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 _vp = ctypes.c_void_p
 
@@ -122,6 +127,7 @@ class LayerOutputs(ctypes.Structure):
         ("injected_logits", _vp),
         ("router_logits", _vp),
         ("stage_events", _vp),
+        ("pair_rank", _vp),
     ]
 
 
@@ -169,6 +175,17 @@ def load() -> ctypes.CDLL:
         "spx_pack_weights_mxfp8": (ctypes.c_int, [P(LayerDims), P(ReferenceWeights), _vp, _vp, _vp, _vp, _vp]),
         "spx_mxfp8_quantize_rows": (ctypes.c_int, [_vp, ctypes.c_int64, ctypes.c_int32, _vp, _vp, _vp]),
         "spx_mxfp8_mm_workspace": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]),
+        "spx_layer_route": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, P(LayerOutputs), _vp, _vp]),
+        "spx_gather_rows": (
+            ctypes.c_int,
+            [_vp, ctypes.c_int64, _vp, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, _vp, ctypes.c_int64, _vp],
+        ),
+        "spx_experts_forward": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, _vp, _vp, _vp, _vp]),
+        "spx_shared_forward": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, _vp, _vp, _vp]),
+        "spx_combine": (
+            ctypes.c_int,
+            [_vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, _vp, _vp],
+        ),
         "spx_mxfp8_mm_nt": (
             ctypes.c_int,
             [_vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp, _vp, ctypes.c_size_t, _vp],

@@ -213,6 +213,215 @@ DispatchArgs dispatch_args(const Shape& s, const int64_t* ids, int* order, int* 
   return a;
 }
 
+// One layer's launch context: shape, workspace layout, stream, status word
+// and (full layer only) the stage events.
+struct Ctx {
+  const Shape& s;
+  const Layout& L;
+  void* ws;
+  cudaStream_t st;
+  int* status;
+  void* const* events;
+  void mark(int i) const {
+    if (events != nullptr && events[i] != nullptr) cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st);
+  }
+};
+
+// A operand source: the hidden states, zero-padded to a multiple of 64 columns if needed.
+int stage_pad(const Ctx& c, const uint16_t* hidden, const uint16_t** xa) {
+  *xa = hidden;
+  if (c.s.kd == c.s.d) return SPX_OK;
+  uint16_t* xp = at<uint16_t>(c.ws, c.L.x_pad);
+  if (int rc = launch_pad_rows(hidden, c.s.T, c.s.d, c.s.kd, xp, c.st); rc != SPX_OK) return rc;
+  *xa = xp;
+  return SPX_OK;
+}
+
+// K1: router logits (tcgen05 GEMM, bias fused) into `lg`.
+int stage_router(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, uint16_t* lg) {
+  const Shape& s = c.s;
+  GemmArgs g = base_args(kEpiStore, s.bn_router, s.kd / 64, c.status);
+  if (int rc = encode_2d(&g.tma_a, xa, s.T, s.kd, s.kd, kTileRows); rc != SPX_OK) return rc;
+  if (int rc = encode_3d(&g.tma_b, w->router_weight, 1, s.E, s.kd, s.bn_router); rc != SPX_OK) return rc;
+  g.m_rows = static_cast<int>(s.T);
+  g.n_valid = s.E;
+  g.out = lg;
+  g.ldo = s.E;
+  g.bias = w->router_bias;
+  return launch_gemm(kEpiStore, g, ceil_div(s.T, kTileRows), s.gn_router, c.st);
+}
+
+// K2 arguments for the layer's dispatch: statistics into the caller's outputs
+// (or workspace dummies), sorted weights, ranks, the MXFP8 tile table.
+DispatchArgs layer_dispatch_args(const Ctx& c, const spx_layer_dims* dims, const spx_packed_weights* w,
+                                 const spx_layer_outputs* out) {
+  const Shape& s = c.s;
+  void* ws = c.ws;
+  const Layout& L = c.L;
+  DispatchArgs da = dispatch_args(s, out->expert_ids, out->dispatch_order, out->expert_counts, ws, L);
+  da.utilization = out->expert_utilization != nullptr ? out->expert_utilization : at<float>(ws, L.util);
+  da.group_stats = out->group_stats != nullptr ? reinterpret_cast<long long*>(out->group_stats)
+                                               : at<long long>(ws, L.stats);
+  da.group_ratios = out->group_ratios != nullptr ? out->group_ratios : at<float>(ws, L.ratios);
+  da.aux_loss = out->auxiliary_loss != nullptr ? out->auxiliary_loss : at<uint16_t>(ws, L.aux);
+  da.resident = w->resident_mask;
+  da.execution_loop = dims->execution_loop;
+  da.pair_weights = out->routing_weights;
+  da.sorted_weights = at<uint16_t>(ws, L.sorted_w);
+  if (out->pair_rank != nullptr) da.rank = out->pair_rank;
+  if (s.mx && w->expert_lane_mxfp8 != nullptr) {
+    da.lane_mx = w->expert_lane_mxfp8;
+    da.tiles_mx = at<int4>(ws, L.tiles_mx);
+    da.num_tiles_mx = at<int>(ws, L.small) + 3;
+  }
+  return da;
+}
+
+// K3: expert GEMM1 (+SwiGLU) and GEMM2 over the dispatched rows of `hidden`
+// (`xa` = hidden padded), both lanes; weighted rows land in Y (sorted order).
+int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hidden, const uint16_t* xa,
+                  const DispatchArgs& da) {
+  const Shape& s = c.s;
+  void* ws = c.ws;
+  const Layout& L = c.L;
+  int rc = SPX_OK;
+  const bool mx = da.lane_mx != nullptr;
+  uint8_t* xq = at<uint8_t>(ws, L.x_q);
+  uint8_t* xsf = at<uint8_t>(ws, L.x_sf);
+  uint8_t* hq = at<uint8_t>(ws, L.h_q);
+  uint8_t* hsf = at<uint8_t>(ws, L.h_sf);
+  if (mx) {
+    // Hidden states of the MXFP8 lane: E4M3 rows with their block scales
+    // (per token, so every expert's gathered rows share them).
+    if ((rc = launch_mx_quantize_rows(hidden, s.T, s.d, s.d, s.kx, xq, s.kx, xsf, s.kx / kMxBlock, c.st)) != SPX_OK)
+      return rc;
+  }
+  uint16_t* hid = at<uint16_t>(ws, L.hidden);
+  uint16_t* y = at<uint16_t>(ws, L.y);
+  {
+    GemmArgs g = base_args(kEpiSwiglu, 2 * s.c, s.kd / 64, c.status);
+    if ((rc = encode_3d(&g.tma_b, w->expert_w1, s.E, static_cast<int64_t>(s.nc) * 2 * s.c, s.kd, 2 * s.c)) != SPX_OK)
+      return rc;
+    g.groups = s.E;
+    g.gather = 1;
+    g.gather_idx = da.src_row;
+    g.a_base = reinterpret_cast<const uint8_t*>(xa);
+    g.lda = 2 * static_cast<int64_t>(s.kd);
+    g.tiles = da.tiles;
+    g.num_tiles = da.num_tiles;
+    g.chunk = s.c;
+    g.h_cols = s.kp;
+    g.out = hid;
+    g.ldo = s.kp;
+    if ((rc = launch_gemm(kEpiSwiglu, g, s.max_tiles, s.nc, c.st)) != SPX_OK) return rc;
+  }
+  if (mx) {
+    // MXFP8-lane experts: block-scaled GEMM1, hidden written quantised.
+    GemmArgs g = base_args(kEpiSwiglu, 2 * s.cm, s.kx / 128, c.status, true);
+    if ((rc = encode_3d(&g.tma_b, w->expert_w1_mx, s.E, static_cast<int64_t>(s.ncm) * 2 * s.cm, s.kx, 2 * s.cm,
+                        1)) != SPX_OK)
+      return rc;
+    g.groups = s.E;
+    g.gather = 1;
+    g.gather_idx = da.src_row;
+    g.a_base = xq;
+    g.lda = s.kx;
+    g.sfa = xsf;
+    g.ld_sfa = s.kx / kMxBlock;
+    g.sfb = w->expert_w1_mx_scales;
+    g.tiles = da.tiles_mx;
+    g.num_tiles = da.num_tiles_mx;
+    g.chunk = s.cm;
+    g.h_cols = s.kh;
+    g.out = hq;
+    g.ldo = s.kh;
+    g.out_sf = hsf;
+    g.ld_out_sf = s.kh / kMxBlock;
+    if ((rc = launch_gemm(kEpiSwiglu, g, s.max_tiles, s.ncm, c.st, true)) != SPX_OK) return rc;
+  }
+  c.mark(4);
+  {
+    GemmArgs g = base_args(kEpiScatter, s.bn_d, s.kp / 64, c.status);
+    if ((rc = encode_2d(&g.tma_a, hid, s.P, s.kp, s.kp, kTileRows)) != SPX_OK) return rc;
+    if ((rc = encode_3d(&g.tma_b, w->expert_w2, s.E, s.d, s.kp, s.bn_d)) != SPX_OK) return rc;
+    g.groups = s.E;
+    g.tiles = da.tiles;
+    g.num_tiles = da.num_tiles;
+    g.n_valid = s.d;
+    g.out = y;
+    g.ldo = s.d;
+    g.tma_store = (s.d % 64) == 0;  // whole 64-column boxes; other widths use plain stores
+    if (g.tma_store && (rc = encode_2d(&g.tma_out, y, s.P, s.d, s.d, 32)) != SPX_OK) return rc;
+    g.pos_weight = da.sorted_weights;
+    if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn_d, c.st)) != SPX_OK) return rc;
+  }
+  if (mx) {
+    GemmArgs g = base_args(kEpiScatter, s.bn2m, s.kh / 128, c.status, true);
+    if ((rc = encode_2d(&g.tma_a, hq, s.P, s.kh, s.kh, kTileRows, 1)) != SPX_OK) return rc;
+    if ((rc = encode_3d(&g.tma_b, w->expert_w2_mx, s.E, s.d, s.kh, s.bn2m, 1)) != SPX_OK) return rc;
+    g.groups = s.E;
+    g.tiles = da.tiles_mx;
+    g.num_tiles = da.num_tiles_mx;
+    g.sfa = hsf;
+    g.ld_sfa = s.kh / kMxBlock;
+    g.sfb = w->expert_w2_mx_scales;
+    g.n_valid = s.d;
+    g.out = y;
+    g.ldo = s.d;
+    g.tma_store = (s.d % 64) == 0;
+    if (g.tma_store && (rc = encode_2d(&g.tma_out, y, s.P, s.d, s.d, 32)) != SPX_OK) return rc;
+    g.pos_weight = da.sorted_weights;
+    if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn2m, c.st, true)) != SPX_OK) return rc;
+  }
+  c.mark(5);
+  return SPX_OK;
+}
+
+// K4 (shared half): shared SwiGLU of every token into `shared_out` [T, d].
+int stage_shared(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, uint16_t* shared_out) {
+  const Shape& s = c.s;
+  int rc = SPX_OK;
+  uint16_t* hs = at<uint16_t>(c.ws, c.L.shared_hidden);
+  {
+    GemmArgs g = base_args(kEpiSwiglu, 2 * s.cs, s.kd / 64, c.status);
+    if ((rc = encode_2d(&g.tma_a, xa, s.T, s.kd, s.kd, kTileRows)) != SPX_OK) return rc;
+    if ((rc = encode_3d(&g.tma_b, w->shared_w1, 1, static_cast<int64_t>(s.ncs) * 2 * s.cs, s.kd, 2 * s.cs)) !=
+        SPX_OK)
+      return rc;
+    g.m_rows = static_cast<int>(s.T);
+    g.chunk = s.cs;
+    g.h_cols = s.ksp;
+    g.out = hs;
+    g.ldo = s.ksp;
+    if ((rc = launch_gemm(kEpiSwiglu, g, ceil_div(s.T, kTileRows), s.ncs, c.st)) != SPX_OK) return rc;
+  }
+  c.mark(6);
+  GemmArgs g = base_args(kEpiStore, s.bn_d, s.ksp / 64, c.status);
+  if ((rc = encode_2d(&g.tma_a, hs, s.T, s.ksp, s.ksp, kTileRows)) != SPX_OK) return rc;
+  if ((rc = encode_3d(&g.tma_b, w->shared_w2, 1, s.d, s.ksp, s.bn_d)) != SPX_OK) return rc;
+  g.m_rows = static_cast<int>(s.T);
+  g.n_valid = s.d;
+  g.out = shared_out;
+  g.ldo = s.d;
+  return launch_gemm(kEpiStore, g, ceil_div(s.T, kTileRows), s.gn_d, c.st);
+}
+
+int check_layer_weights(const Shape& s, const spx_layer_dims* dims, const spx_packed_weights* w, bool router,
+                        bool experts, bool shared) {
+  if (w == nullptr) return SPX_ERR_INVALID_ARG;
+  if (router && w->router_weight == nullptr) return SPX_ERR_INVALID_ARG;
+  if (router && dims->score_transform == 0 && w->softplus_table == nullptr) return SPX_ERR_INVALID_ARG;
+  if (experts && (w->expert_w1 == nullptr || w->expert_w2 == nullptr)) return SPX_ERR_INVALID_ARG;
+  if (shared && s.S > 0 && (w->shared_w1 == nullptr || w->shared_w2 == nullptr)) return SPX_ERR_INVALID_ARG;
+  if (experts && w->expert_lane_mxfp8 != nullptr) {
+    if (!s.mx) return SPX_ERR_INVALID_ARG;  // the workspace has no MXFP8 regions
+    if (w->expert_w1_mx == nullptr || w->expert_w1_mx_scales == nullptr || w->expert_w2_mx == nullptr ||
+        w->expert_w2_mx_scales == nullptr)
+      return SPX_ERR_INVALID_ARG;
+  }
+  return SPX_OK;
+}
+
 }  // namespace
 }  // namespace spx
 
@@ -279,14 +488,16 @@ int spx_pack_weights(const spx_layer_dims* dims, const spx_reference_weights* sr
                      void* stream) {
   Shape s;
   if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
-  if (src == nullptr || src->router_weight == nullptr || src->gate_proj == nullptr || src->up_proj == nullptr ||
-      src->down_proj == nullptr || router_weight == nullptr || expert_w1 == nullptr || expert_w2 == nullptr)
+  if (src == nullptr || src->router_weight == nullptr || router_weight == nullptr) return SPX_ERR_INVALID_ARG;
+  const bool experts = expert_w1 != nullptr || expert_w2 != nullptr;
+  if (experts && (expert_w1 == nullptr || expert_w2 == nullptr || src->gate_proj == nullptr ||
+                  src->up_proj == nullptr || src->down_proj == nullptr))
     return SPX_ERR_INVALID_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc = launch_pad_rows(src->router_weight, s.E, s.d, s.kd, router_weight, st);
-  if (rc == SPX_OK)
+  if (rc == SPX_OK && experts)
     rc = launch_pack_chunked_w1(src->gate_proj, src->up_proj, s.E, s.d, s.I, s.kd, s.c, s.nc, 0, expert_w1, st);
-  if (rc == SPX_OK) rc = launch_pack_w2(src->down_proj, s.E, s.I, s.d, s.kp, 0, expert_w2, st);
+  if (rc == SPX_OK && experts) rc = launch_pack_w2(src->down_proj, s.E, s.I, s.d, s.kp, 0, expert_w2, st);
   if (rc == SPX_OK && s.S > 0) {
     if (src->shared_gate == nullptr || src->shared_up == nullptr || src->shared_down == nullptr ||
         shared_w1 == nullptr || shared_w2 == nullptr)
@@ -428,209 +639,145 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
                       const spx_layer_outputs* out, void* workspace, void* stream) {
   Shape s;
   if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
-  if (w == nullptr || out == nullptr || hidden == nullptr) return SPX_ERR_INVALID_ARG;
+  if (out == nullptr || hidden == nullptr) return SPX_ERR_INVALID_ARG;
   if (workspace == nullptr) return SPX_ERR_WORKSPACE;
   if (out->update == nullptr || out->router_scores == nullptr || out->expert_ids == nullptr ||
       out->routing_weights == nullptr)
     return SPX_ERR_INVALID_ARG;
-  if (w->router_weight == nullptr || w->expert_w1 == nullptr || w->expert_w2 == nullptr) return SPX_ERR_INVALID_ARG;
-  if (s.S > 0 && (w->shared_w1 == nullptr || w->shared_w2 == nullptr)) return SPX_ERR_INVALID_ARG;
-  if (dims->score_transform == 0 && w->softplus_table == nullptr) return SPX_ERR_INVALID_ARG;
-  if (w->expert_lane_mxfp8 != nullptr) {
-    if (!s.mx) return SPX_ERR_INVALID_ARG;  // the workspace has no MXFP8 regions
-    if (w->expert_w1_mx == nullptr || w->expert_w1_mx_scales == nullptr || w->expert_w2_mx == nullptr ||
-        w->expert_w2_mx_scales == nullptr)
-      return SPX_ERR_INVALID_ARG;
-  }
+  if (int rc = check_layer_weights(s, dims, w, true, true, true); rc != SPX_OK) return rc;
   if (!aligned16(hidden) || !aligned16(out->update) || !aligned16(workspace)) return SPX_ERR_ALIGNMENT;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   const Layout L = make_layout(s);
-  int* status = at<int>(workspace, L.small);
+  const Ctx c{s, L, workspace, static_cast<cudaStream_t>(stream), at<int>(workspace, L.small), out->stage_events};
   int rc = SPX_OK;
-  auto mark = [&](int i) {
-    if (out->stage_events != nullptr && out->stage_events[i] != nullptr)
-      cudaEventRecord(static_cast<cudaEvent_t>(out->stage_events[i]), st);
-  };
-  mark(0);
-
-  // A operand source: the hidden states, zero-padded to a multiple of 64 columns if needed.
-  const uint16_t* xa = hidden;
-  if (s.kd != s.d) {
-    uint16_t* xp = at<uint16_t>(workspace, L.x_pad);
-    if ((rc = launch_pad_rows(hidden, s.T, s.d, s.kd, xp, st)) != SPX_OK) return rc;
-    xa = xp;
-  }
-
+  c.mark(0);
+  const uint16_t* xa = nullptr;
+  if ((rc = stage_pad(c, hidden, &xa)) != SPX_OK) return rc;
   // ---- K1: router logits (tcgen05 GEMM) unless injected
   const uint16_t* logits = out->injected_logits;
   if (logits == nullptr) {
     uint16_t* lg = out->router_logits != nullptr ? out->router_logits : at<uint16_t>(workspace, L.logits);
-    GemmArgs g = base_args(kEpiStore, s.bn_router, s.kd / 64, status);
-    if ((rc = encode_2d(&g.tma_a, xa, s.T, s.kd, s.kd, kTileRows)) != SPX_OK) return rc;
-    if ((rc = encode_3d(&g.tma_b, w->router_weight, 1, s.E, s.kd, s.bn_router)) != SPX_OK) return rc;
-    g.m_rows = static_cast<int>(s.T);
-    g.n_valid = s.E;
-    g.out = lg;
-    g.ldo = s.E;
-    g.bias = w->router_bias;
-    if ((rc = launch_gemm(kEpiStore, g, ceil_div(s.T, kTileRows), s.gn_router, st)) != SPX_OK) return rc;
+    if ((rc = stage_router(c, w, xa, lg)) != SPX_OK) return rc;
     logits = lg;
   }
-  mark(1);
-
+  c.mark(1);
   // ---- K1: scores, top-k, weights, load-balance partials
   rc = run_route(s, logits, dims->score_transform == 0 ? w->softplus_table : nullptr, w->resident_mask,
-                 out->router_scores, out->expert_ids, out->routing_weights, workspace, L, st);
+                 out->router_scores, out->expert_ids, out->routing_weights, workspace, L, c.st);
   if (rc != SPX_OK) return rc;
-  mark(2);
-
+  c.mark(2);
   // ---- K2: dispatch + statistics
-  DispatchArgs da = dispatch_args(s, out->expert_ids, out->dispatch_order, out->expert_counts, workspace, L);
-  da.utilization = out->expert_utilization != nullptr ? out->expert_utilization : at<float>(workspace, L.util);
-  da.group_stats = out->group_stats != nullptr ? reinterpret_cast<long long*>(out->group_stats)
-                                               : at<long long>(workspace, L.stats);
-  da.group_ratios = out->group_ratios != nullptr ? out->group_ratios : at<float>(workspace, L.ratios);
-  da.aux_loss = out->auxiliary_loss != nullptr ? out->auxiliary_loss : at<uint16_t>(workspace, L.aux);
-  da.resident = w->resident_mask;
-  da.execution_loop = dims->execution_loop;
-  da.pair_weights = out->routing_weights;
-  da.sorted_weights = at<uint16_t>(workspace, L.sorted_w);
-  const bool mx = s.mx && w->expert_lane_mxfp8 != nullptr;
-  if (mx) {
+  const DispatchArgs da = layer_dispatch_args(c, dims, w, out);
+  if ((rc = launch_dispatch(da, c.st)) != SPX_OK) return rc;
+  c.mark(3);
+  // ---- K3: grouped experts (both lanes)
+  if ((rc = stage_experts(c, w, hidden, xa, da)) != SPX_OK) return rc;
+  // ---- K4: shared SwiGLU, then update = shared + the token's k weighted expert rows
+  uint16_t* y = at<uint16_t>(workspace, L.y);
+  uint16_t* so = nullptr;
+  if (s.S > 0) {
+    so = at<uint16_t>(workspace, L.shared_out);
+    if ((rc = stage_shared(c, w, xa, so)) != SPX_OK) return rc;
+  } else {
+    c.mark(6);
+  }
+  if ((rc = launch_combine(y, da.rank, nullptr, so, s.T, s.d, s.k, out->update, c.st)) != SPX_OK) return rc;
+  c.mark(7);
+  return SPX_OK;
+}
+
+int spx_layer_route(const spx_layer_dims* dims, const spx_packed_weights* w, const uint16_t* hidden,
+                    const spx_layer_outputs* out, void* workspace, void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (out == nullptr || hidden == nullptr) return SPX_ERR_INVALID_ARG;
+  if (workspace == nullptr) return SPX_ERR_WORKSPACE;
+  if (out->router_scores == nullptr || out->expert_ids == nullptr || out->routing_weights == nullptr ||
+      out->dispatch_order == nullptr || out->expert_counts == nullptr || out->pair_rank == nullptr)
+    return SPX_ERR_INVALID_ARG;
+  if (int rc = check_layer_weights(s, dims, w, true, false, false); rc != SPX_OK) return rc;
+  if (!aligned16(hidden) || !aligned16(workspace)) return SPX_ERR_ALIGNMENT;
+  const Layout L = make_layout(s);
+  const Ctx c{s, L, workspace, static_cast<cudaStream_t>(stream), at<int>(workspace, L.small), nullptr};
+  int rc = SPX_OK;
+  const uint16_t* xa = nullptr;
+  if ((rc = stage_pad(c, hidden, &xa)) != SPX_OK) return rc;
+  const uint16_t* logits = out->injected_logits;
+  if (logits == nullptr) {
+    uint16_t* lg = out->router_logits != nullptr ? out->router_logits : at<uint16_t>(workspace, L.logits);
+    if ((rc = stage_router(c, w, xa, lg)) != SPX_OK) return rc;
+    logits = lg;
+  }
+  rc = run_route(s, logits, dims->score_transform == 0 ? w->softplus_table : nullptr, w->resident_mask,
+                 out->router_scores, out->expert_ids, out->routing_weights, workspace, L, c.st);
+  if (rc != SPX_OK) return rc;
+  DispatchArgs da = layer_dispatch_args(c, dims, w, out);
+  da.lane_mx = nullptr;  // the experts run elsewhere
+  return launch_dispatch(da, c.st);
+}
+
+int spx_experts_forward(const spx_layer_dims* dims, const spx_packed_weights* w, const uint16_t* rows,
+                        const int64_t* row_expert, uint16_t* out_rows, void* workspace, void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (dims->top_k != 1) return SPX_ERR_INVALID_ARG;  // one expert per row
+  if (rows == nullptr || row_expert == nullptr || out_rows == nullptr) return SPX_ERR_INVALID_ARG;
+  if (workspace == nullptr) return SPX_ERR_WORKSPACE;
+  if (int rc = check_layer_weights(s, dims, w, false, true, false); rc != SPX_OK) return rc;
+  if (!aligned16(rows) || !aligned16(out_rows) || !aligned16(workspace)) return SPX_ERR_ALIGNMENT;
+  const Layout L = make_layout(s);
+  const Ctx c{s, L, workspace, static_cast<cudaStream_t>(stream), at<int>(workspace, L.small), nullptr};
+  int rc = SPX_OK;
+  const uint16_t* xa = nullptr;
+  if ((rc = stage_pad(c, rows, &xa)) != SPX_OK) return rc;
+  DispatchArgs da = dispatch_args(s, row_expert, nullptr, nullptr, workspace, L);
+  da.lb_blocks = 0;  // no routing probabilities here
+  da.utilization = at<float>(workspace, L.util);
+  da.group_stats = at<long long>(workspace, L.stats);
+  da.group_ratios = at<float>(workspace, L.ratios);
+  da.pair_weights = nullptr;  // unit weights: the caller applies the routing weights
+  da.sorted_weights = nullptr;
+  if (s.mx && w->expert_lane_mxfp8 != nullptr) {
     da.lane_mx = w->expert_lane_mxfp8;
     da.tiles_mx = at<int4>(workspace, L.tiles_mx);
     da.num_tiles_mx = at<int>(workspace, L.small) + 3;
   }
-  if ((rc = launch_dispatch(da, st)) != SPX_OK) return rc;
-  mark(3);
-  uint8_t* xq = at<uint8_t>(workspace, L.x_q);
-  uint8_t* xsf = at<uint8_t>(workspace, L.x_sf);
-  uint8_t* hq = at<uint8_t>(workspace, L.h_q);
-  uint8_t* hsf = at<uint8_t>(workspace, L.h_sf);
-  if (mx) {
-    // Hidden states of the MXFP8 lane: E4M3 rows with their block scales
-    // (per token, so every expert's gathered rows share them).
-    if ((rc = launch_mx_quantize_rows(hidden, s.T, s.d, s.d, s.kx, xq, s.kx, xsf, s.kx / kMxBlock, st)) != SPX_OK)
-      return rc;
-  }
+  if ((rc = launch_dispatch(da, c.st)) != SPX_OK) return rc;
+  if ((rc = stage_experts(c, w, rows, xa, da)) != SPX_OK) return rc;
+  // back to the input row order (one "slot" per row)
+  return launch_combine(at<uint16_t>(workspace, L.y), da.rank, nullptr, nullptr, s.T, s.d, 1, out_rows, c.st);
+}
 
-  uint16_t* hid = at<uint16_t>(workspace, L.hidden);
-  uint16_t* y = at<uint16_t>(workspace, L.y);
+int spx_shared_forward(const spx_layer_dims* dims, const spx_packed_weights* w, const uint16_t* hidden,
+                       uint16_t* shared_out, void* workspace, void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (hidden == nullptr || shared_out == nullptr) return SPX_ERR_INVALID_ARG;
+  if (s.S == 0) return SPX_ERR_INVALID_ARG;
+  if (workspace == nullptr) return SPX_ERR_WORKSPACE;
+  if (int rc = check_layer_weights(s, dims, w, false, false, true); rc != SPX_OK) return rc;
+  if (!aligned16(hidden) || !aligned16(shared_out) || !aligned16(workspace)) return SPX_ERR_ALIGNMENT;
+  const Layout L = make_layout(s);
+  const Ctx c{s, L, workspace, static_cast<cudaStream_t>(stream), at<int>(workspace, L.small), nullptr};
+  const uint16_t* xa = nullptr;
+  if (int rc = stage_pad(c, hidden, &xa); rc != SPX_OK) return rc;
+  return stage_shared(c, w, xa, shared_out);
+}
 
-  // ---- K3a: expert GEMM1 (gathered rows) + SwiGLU
-  {
-    GemmArgs g = base_args(kEpiSwiglu, 2 * s.c, s.kd / 64, status);
-    if ((rc = encode_3d(&g.tma_b, w->expert_w1, s.E, static_cast<int64_t>(s.nc) * 2 * s.c, s.kd, 2 * s.c)) != SPX_OK)
-      return rc;
-    g.groups = s.E;
-    g.gather = 1;
-    g.gather_idx = da.src_row;
-    g.a_base = reinterpret_cast<const uint8_t*>(xa);
-    g.lda = 2 * static_cast<int64_t>(s.kd);
-    g.tiles = da.tiles;
-    g.num_tiles = da.num_tiles;
-    g.chunk = s.c;
-    g.h_cols = s.kp;
-    g.out = hid;
-    g.ldo = s.kp;
-    if ((rc = launch_gemm(kEpiSwiglu, g, s.max_tiles, s.nc, st)) != SPX_OK) return rc;
-  }
-  if (mx) {
-    // MXFP8-lane experts: block-scaled GEMM1, hidden written quantised.
-    GemmArgs g = base_args(kEpiSwiglu, 2 * s.cm, s.kx / 128, status, true);
-    if ((rc = encode_3d(&g.tma_b, w->expert_w1_mx, s.E, static_cast<int64_t>(s.ncm) * 2 * s.cm, s.kx, 2 * s.cm,
-                        1)) != SPX_OK)
-      return rc;
-    g.groups = s.E;
-    g.gather = 1;
-    g.gather_idx = da.src_row;
-    g.a_base = xq;
-    g.lda = s.kx;
-    g.sfa = xsf;
-    g.ld_sfa = s.kx / kMxBlock;
-    g.sfb = w->expert_w1_mx_scales;
-    g.tiles = da.tiles_mx;
-    g.num_tiles = da.num_tiles_mx;
-    g.chunk = s.cm;
-    g.h_cols = s.kh;
-    g.out = hq;
-    g.ldo = s.kh;
-    g.out_sf = hsf;
-    g.ld_out_sf = s.kh / kMxBlock;
-    if ((rc = launch_gemm(kEpiSwiglu, g, s.max_tiles, s.ncm, st, true)) != SPX_OK) return rc;
-  }
-  mark(4);
-  // ---- K3b: expert GEMM2, scaled by the routing weight, scattered to pair order
-  {
-    GemmArgs g = base_args(kEpiScatter, s.bn_d, s.kp / 64, status);
-    if ((rc = encode_2d(&g.tma_a, hid, s.P, s.kp, s.kp, kTileRows)) != SPX_OK) return rc;
-    if ((rc = encode_3d(&g.tma_b, w->expert_w2, s.E, s.d, s.kp, s.bn_d)) != SPX_OK) return rc;
-    g.groups = s.E;
-    g.tiles = da.tiles;
-    g.num_tiles = da.num_tiles;
-    g.n_valid = s.d;
-    g.out = y;
-    g.ldo = s.d;
-    g.tma_store = (s.d % 64) == 0;  // whole 64-column boxes; other widths use plain stores
-    if (g.tma_store && (rc = encode_2d(&g.tma_out, y, s.P, s.d, s.d, 32)) != SPX_OK) return rc;
-    g.pos_weight = da.sorted_weights;
-    if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn_d, st)) != SPX_OK) return rc;
-  }
-  if (mx) {
-    GemmArgs g = base_args(kEpiScatter, s.bn2m, s.kh / 128, status, true);
-    if ((rc = encode_2d(&g.tma_a, hq, s.P, s.kh, s.kh, kTileRows, 1)) != SPX_OK) return rc;
-    if ((rc = encode_3d(&g.tma_b, w->expert_w2_mx, s.E, s.d, s.kh, s.bn2m, 1)) != SPX_OK) return rc;
-    g.groups = s.E;
-    g.tiles = da.tiles_mx;
-    g.num_tiles = da.num_tiles_mx;
-    g.sfa = hsf;
-    g.ld_sfa = s.kh / kMxBlock;
-    g.sfb = w->expert_w2_mx_scales;
-    g.n_valid = s.d;
-    g.out = y;
-    g.ldo = s.d;
-    g.tma_store = (s.d % 64) == 0;  // whole 64-column boxes; other widths use plain stores
-    if (g.tma_store && (rc = encode_2d(&g.tma_out, y, s.P, s.d, s.d, 32)) != SPX_OK) return rc;
-    g.pos_weight = da.sorted_weights;
-    if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn2m, st, true)) != SPX_OK) return rc;
-  }
-  mark(5);
-  // ---- K4: shared SwiGLU with the combine fused into its down projection
-  if (s.S > 0) {
-    uint16_t* hs = at<uint16_t>(workspace, L.shared_hidden);
-    {
-      GemmArgs g = base_args(kEpiSwiglu, 2 * s.cs, s.kd / 64, status);
-      if ((rc = encode_2d(&g.tma_a, xa, s.T, s.kd, s.kd, kTileRows)) != SPX_OK) return rc;
-      if ((rc = encode_3d(&g.tma_b, w->shared_w1, 1, static_cast<int64_t>(s.ncs) * 2 * s.cs, s.kd, 2 * s.cs)) !=
-          SPX_OK)
-        return rc;
-      g.m_rows = static_cast<int>(s.T);
-      g.chunk = s.cs;
-      g.h_cols = s.ksp;
-      g.out = hs;
-      g.ldo = s.ksp;
-      if ((rc = launch_gemm(kEpiSwiglu, g, ceil_div(s.T, kTileRows), s.ncs, st)) != SPX_OK) return rc;
-    }
-    mark(6);
-    uint16_t* so = at<uint16_t>(workspace, L.shared_out);
-    {
-      GemmArgs g = base_args(kEpiStore, s.bn_d, s.ksp / 64, status);
-      if ((rc = encode_2d(&g.tma_a, hs, s.T, s.ksp, s.ksp, kTileRows)) != SPX_OK) return rc;
-      if ((rc = encode_3d(&g.tma_b, w->shared_w2, 1, s.d, s.ksp, s.bn_d)) != SPX_OK) return rc;
-      g.m_rows = static_cast<int>(s.T);
-      g.n_valid = s.d;
-      g.out = so;
-      g.ldo = s.d;
-      if ((rc = launch_gemm(kEpiStore, g, ceil_div(s.T, kTileRows), s.gn_d, st)) != SPX_OK) return rc;
-    }
-    // update = bf16(shared + sum of the token's k expert rows), streamed.
-    if ((rc = launch_combine(y, da.rank, so, s.T, s.d, s.k, out->update, st)) != SPX_OK) return rc;
-  } else {
-    mark(6);
-    if ((rc = launch_combine(y, da.rank, nullptr, s.T, s.d, s.k, out->update, st)) != SPX_OK) return rc;
-  }
-  mark(7);
-  return SPX_OK;
+int spx_combine(const uint16_t* expert_rows, const int32_t* pair_rank, const uint16_t* pair_weights,
+                const uint16_t* shared, int64_t tokens, int32_t d, int32_t top_k, uint16_t* update, void* stream) {
+  if (tokens < 0 || d < 1 || top_k < 1 || top_k > kMaxTopK) return SPX_ERR_INVALID_ARG;
+  if (tokens == 0) return SPX_OK;
+  if (expert_rows == nullptr || pair_rank == nullptr || update == nullptr) return SPX_ERR_INVALID_ARG;
+  return launch_combine(expert_rows, pair_rank, pair_weights, shared, tokens, d, top_k, update,
+                        static_cast<cudaStream_t>(stream));
+}
+
+int spx_gather_rows(const uint16_t* src, int64_t ld_src, const int32_t* index, int32_t index_div, int64_t rows,
+                    int32_t d, uint16_t* out, int64_t ld_out, void* stream) {
+  if (rows < 0 || d < 1 || index_div < 1 || ld_src < d || ld_out < d) return SPX_ERR_INVALID_ARG;
+  if (rows == 0) return SPX_OK;
+  if (src == nullptr || index == nullptr || out == nullptr) return SPX_ERR_INVALID_ARG;
+  return launch_gather_rows(src, ld_src, index, index_div, rows, d, out, ld_out, static_cast<cudaStream_t>(stream));
 }
 
 int spx_workspace_status(void* workspace, int* device_status, int clear, void* stream) {

@@ -556,7 +556,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       long long my_row = static_cast<long long>(row0) + r;
       float my_w = 0.0f;
       if constexpr (EPI == kEpiScatter) {
-        if (r < rows) my_w = bf16_to_f32(a.pos_weight[row0 + r]);
+        my_w = 1.0f;  // no weights: unweighted rows (the caller applies the routing weights)
+        if (r < rows && a.pos_weight != nullptr) my_w = bf16_to_f32(a.pos_weight[row0 + r]);
       }
       int go = 1;
       if (lane == 0) go = mbar_wait(&tfull[b], tph, a.status, SPX_DEV_TIMEOUT_EPILOGUE) ? 1 : 0;

@@ -155,9 +155,14 @@ int launch_mx_quantize_b(int mode, const uint16_t* a, const uint16_t* b, int gro
                          int rows_real, int k_real, int kp, int tile_rows, int d, int inter, int chunk, int64_t ld,
                          uint8_t* q, uint8_t* atoms, cudaStream_t stream);
 
-// update[t] = bf16(base[t] + sum_j Y[rank[t*k + j]]) (base: shared SwiGLU output or null).
-int launch_combine(const uint16_t* y, const int* rank, const uint16_t* base, int64_t tokens, int d, int k,
-                   uint16_t* out, cudaStream_t stream);
+// update[t] = bf16(base[t] + sum_j rows_j) with rows_j = Y[rank[t*k + j]], or
+// bf16(Y[rank[t*k + j]] * w[t*k + j]) when pair weights are given (base: the
+// shared SwiGLU output or null).
+int launch_combine(const uint16_t* y, const int* rank, const uint16_t* weights, const uint16_t* base, int64_t tokens,
+                   int d, int k, uint16_t* out, cudaStream_t stream);
+// out[i] = src[index[i] / index_div] (BF16 rows of d elements).
+int launch_gather_rows(const uint16_t* src, int64_t ld_src, const int* index, int index_div, int64_t rows, int d,
+                       uint16_t* out, int64_t ld_out, cudaStream_t stream);
 
 int launch_pack_chunked_w1(const uint16_t* gate, const uint16_t* up, int experts, int d, int inter, int kd,
                            int chunk, int chunks, int transposed_src, uint16_t* out, cudaStream_t stream);

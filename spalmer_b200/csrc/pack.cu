@@ -71,49 +71,54 @@ __global__ void pad_rows_kernel(const uint16_t* __restrict__ src, int64_t rows, 
   }
 }
 
-// update[t] = bf16(base[t] + sum_j Y[rank[t*k + j]]) in FP32 (base first, then
-// slots in order), 8 columns per thread; base is the shared SwiGLU output
-// (BF16) or absent.  Consecutive threads take consecutive 16-byte chunks of
-// one token, so every slot's row is read in whole 128-byte lines; a thread
-// issues all k row loads before it adds any.
+// update[t] = bf16(base[t] + sum_j row_j) in FP32 (base first, then slots in
+// order), row_j = Y[rank[t*k + j]] -- or bf16(Y[rank[t*k + j]] * w[t*k + j])
+// when pair weights are given (expert rows computed elsewhere, unweighted).
+// base is the shared SwiGLU output (BF16) or absent.  8 columns per thread;
+// consecutive threads take consecutive 16-byte chunks of one token, so every
+// slot's row is read in whole 128-byte lines, and a thread issues all k row
+// loads before it adds any.
+__device__ __forceinline__ void add_row8(float (&acc)[8], const uint4& v, float w, bool weighted) {
+  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float lo = __uint_as_float(u[q] << 16), hi = __uint_as_float(u[q] & 0xFFFF0000u);
+    if (weighted) {
+      lo = round_bf16(lo * w);
+      hi = round_bf16(hi * w);
+    }
+    acc[2 * q] += lo;
+    acc[2 * q + 1] += hi;
+  }
+}
+
 template <int KMAX>
 __global__ void combine_kernel(const uint16_t* __restrict__ y, const int* __restrict__ rank,
-                               const uint16_t* __restrict__ base, int64_t tokens, int d, int k,
-                               uint16_t* __restrict__ out) {
+                               const uint16_t* __restrict__ weights, const uint16_t* __restrict__ base,
+                               int64_t tokens, int d, int k, uint16_t* __restrict__ out) {
   const int vec = d / 8;
   const int64_t total = tokens * vec;
+  const bool weighted = weights != nullptr;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t t = idx / vec;
     const int c = static_cast<int>(idx - t * vec) * 8;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (base != nullptr) {
-      const uint4 b = __ldg(reinterpret_cast<const uint4*>(base + t * d + c));
-      const uint32_t w[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        acc[2 * q] = __uint_as_float(w[q] << 16);
-        acc[2 * q + 1] = __uint_as_float(w[q] & 0xFFFF0000u);
-      }
-    }
+    if (base != nullptr) add_row8(acc, __ldg(reinterpret_cast<const uint4*>(base + t * d + c)), 1.0f, false);
     int r[KMAX];
+    float w[KMAX];
 #pragma unroll
-    for (int j = 0; j < KMAX; ++j) r[j] = j < k ? __ldg(rank + t * k + j) : 0;
+    for (int j = 0; j < KMAX; ++j) {
+      r[j] = j < k ? __ldg(rank + t * k + j) : 0;
+      w[j] = (weighted && j < k) ? bf16_to_f32(__ldg(weights + t * k + j)) : 1.0f;
+    }
     uint4 v[KMAX];
 #pragma unroll
     for (int j = 0; j < KMAX; ++j)
       if (j < k) v[j] = __ldg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(r[j]) * d + c));
 #pragma unroll
-    for (int j = 0; j < KMAX; ++j) {
-      if (j < k) {
-        const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          acc[2 * q] += __uint_as_float(w[q] << 16);
-          acc[2 * q + 1] += __uint_as_float(w[q] & 0xFFFF0000u);
-        }
-      }
-    }
+    for (int j = 0; j < KMAX; ++j)
+      if (j < k) add_row8(acc, v[j], w[j], weighted);
     uint4 o;
     uint16_t* oh = reinterpret_cast<uint16_t*>(&o);
 #pragma unroll
@@ -123,16 +128,38 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, const int* __rest
 }
 
 __global__ void combine_scalar_kernel(const uint16_t* __restrict__ y, const int* __restrict__ rank,
-                                      const uint16_t* __restrict__ base, int64_t tokens, int d, int k,
-                                      uint16_t* __restrict__ out) {
+                                      const uint16_t* __restrict__ weights, const uint16_t* __restrict__ base,
+                                      int64_t tokens, int d, int k, uint16_t* __restrict__ out) {
   const int64_t total = tokens * d;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t t = idx / d;
     const int c = static_cast<int>(idx - t * d);
     float acc = base != nullptr ? bf16_to_f32(base[idx]) : 0.0f;
-    for (int j = 0; j < k; ++j) acc += bf16_to_f32(y[static_cast<int64_t>(rank[t * k + j]) * d + c]);
+    for (int j = 0; j < k; ++j) {
+      float v = bf16_to_f32(y[static_cast<int64_t>(rank[t * k + j]) * d + c]);
+      if (weights != nullptr) v = round_bf16(v * bf16_to_f32(weights[t * k + j]));
+      acc += v;
+    }
     out[idx] = f32_to_bf16_rne(acc);
+  }
+}
+
+// out[i] = src[index[i] / div], 16 bytes per thread when aligned.
+__global__ void gather_rows_kernel(const uint16_t* __restrict__ src, int64_t ld_src, const int* __restrict__ index,
+                                   int div, int64_t rows, int d, uint16_t* __restrict__ out, int64_t ld_out,
+                                   bool vec) {
+  const int per_row = vec ? d / 8 : d;
+  const int64_t total = rows * per_row;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t i = idx / per_row;
+    const int c = static_cast<int>(idx - i * per_row);
+    const int64_t r = __ldg(index + i) / div;
+    if (vec)
+      *reinterpret_cast<uint4*>(out + i * ld_out + 8 * c) = __ldg(reinterpret_cast<const uint4*>(src + r * ld_src + 8 * c));
+    else
+      out[i * ld_out + c] = src[r * ld_src + c];
   }
 }
 
@@ -162,8 +189,8 @@ int launch_pad_rows(const uint16_t* src, int64_t rows, int cols, int ld_out, uin
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 
-int launch_combine(const uint16_t* y, const int* rank, const uint16_t* base, int64_t tokens, int d, int k,
-                   uint16_t* out, cudaStream_t stream) {
+int launch_combine(const uint16_t* y, const int* rank, const uint16_t* weights, const uint16_t* base, int64_t tokens,
+                   int d, int k, uint16_t* out, cudaStream_t stream) {
   const bool vec_ok = (d % 8) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0 &&
                       (reinterpret_cast<uintptr_t>(out) & 15u) == 0 &&
                       (base == nullptr || (reinterpret_cast<uintptr_t>(base) & 15u) == 0);
@@ -173,12 +200,21 @@ int launch_combine(const uint16_t* y, const int* rank, const uint16_t* base, int
     if (g > 148 * 64) g = 148 * 64;
     const int grid = static_cast<int>(g < 1 ? 1 : g);
     if (k <= 8)
-      combine_kernel<8><<<grid, 256, 0, stream>>>(y, rank, base, tokens, d, k, out);
+      combine_kernel<8><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out);
     else
-      combine_kernel<kMaxTopK><<<grid, 256, 0, stream>>>(y, rank, base, tokens, d, k, out);
+      combine_kernel<kMaxTopK><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out);
   } else {
-    combine_scalar_kernel<<<grid_for(tokens * d), 256, 0, stream>>>(y, rank, base, tokens, d, k, out);
+    combine_scalar_kernel<<<grid_for(tokens * d), 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out);
   }
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+int launch_gather_rows(const uint16_t* src, int64_t ld_src, const int* index, int index_div, int64_t rows, int d,
+                       uint16_t* out, int64_t ld_out, cudaStream_t stream) {
+  const bool vec = (d % 8) == 0 && (ld_src % 8) == 0 && (ld_out % 8) == 0 &&
+                   (reinterpret_cast<uintptr_t>(src) & 15u) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+  const int64_t total = rows * (vec ? d / 8 : d);
+  gather_rows_kernel<<<grid_for(total), 256, 0, stream>>>(src, ld_src, index, index_div, rows, d, out, ld_out, vec);
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 

@@ -1,0 +1,334 @@
+"""Expert parallelism for the micro-expert layer: experts sharded over GPUs,
+token rows exchanged with NCCL all-to-all.
+
+The reference runs every expert on every rank (its multi-GPU paths are data
+parallel); this module adds the expert-parallel layout its survey plans for
+the skewed 8-GPU configuration: rank r of G owns experts
+[r*E/G, (r+1)*E/G) and its own T_r tokens.  One forward:
+
+1. route (``spx_layer_route``): router GEMM, selection, dispatch of the local
+   tokens.  Pairs sorted by expert id are also sorted by owning rank.
+2. all-to-all of the per-expert pair counts (E/G int32 per peer), read on the
+   host to size the row exchange (the one host synchronisation).
+3. ``spx_gather_rows`` packs the hidden-state row of every pair in dispatch
+   order; all-to-all-v sends each peer the rows of its experts.
+4. ``spx_experts_forward`` runs the received rows through the local experts
+   (grouped tcgen05 GEMMs, both precision lanes), unweighted, in receive
+   order.
+5. all-to-all-v returns the rows; they arrive in the sender's dispatch order.
+6. ``spx_combine`` adds bf16(row * routing weight) of each token's k pairs in
+   slot order to the shared SwiGLU output (``spx_shared_forward``, computed
+   on a side stream while the rows travel).
+
+Every per-row result is computed by the same kernels as the single-GPU layer
+on the same operands, so the update is bit-identical to ``spx_layer_forward``
+on the same tokens.  The exchange logic (`exchange_plan`, `ExpertParallelMixer`)
+is backend-agnostic: `CudaOps` runs libspx; the CPU tests drive the same
+exchange with an oracle backend over gloo.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Any
+
+import numpy as np
+import torch
+import torch.distributed as dist
+from torch import Tensor
+
+from spalmer_b200 import _lib
+
+
+def experts_per_rank(num_experts: int, world: int) -> int:
+    if num_experts % world:
+        raise ValueError(f"{num_experts} experts do not shard evenly over {world} ranks")
+    return num_experts // world
+
+
+@dataclass
+class ExchangePlan:
+    """Row counts of one all-to-all round (host integers)."""
+
+    send_rows: list[int]        # rows this rank sends to each peer (its pairs on the peer's experts)
+    recv_rows: list[int]        # rows this rank receives from each peer
+    recv_expert_counts: np.ndarray  # [G, E_local] rows per (source, local expert), receive order
+
+
+def exchange_plan(local_counts: np.ndarray, recv_counts: np.ndarray, world: int) -> ExchangePlan:
+    """Split sizes from this rank's per-expert pair counts [E] and the counts
+    received from every peer for this rank's experts [G * E_local]."""
+
+    local_counts = np.asarray(local_counts, dtype=np.int64).reshape(world, -1)
+    recv = np.asarray(recv_counts, dtype=np.int64).reshape(world, -1)
+    return ExchangePlan(send_rows=[int(v) for v in local_counts.sum(axis=1)],
+                        recv_rows=[int(v) for v in recv.sum(axis=1)],
+                        recv_expert_counts=recv)
+
+
+def receive_expert_ids(plan: ExchangePlan, device: torch.device) -> Tensor:
+    """Local expert id of every received row: from each source, its rows for
+    local expert 0, then 1, ... (the sender's dispatch order)."""
+
+    counts = torch.from_numpy(plan.recv_expert_counts.reshape(-1)).to(device)
+    world, e_local = plan.recv_expert_counts.shape
+    ids = torch.arange(e_local, dtype=torch.int64, device=device).repeat(world)
+    return torch.repeat_interleave(ids, counts)
+
+
+class CudaOps:
+    """libspx stages for one rank (weights of all experts are kept by the
+    module; only this rank's experts are packed)."""
+
+    def __init__(self, mixer: Any, rank: int, world: int, device: torch.device):
+        from spalmer_b200.experts import layer_dims, softplus_table
+
+        self.mixer = mixer
+        self.config = mixer.config
+        self.device = device
+        cfg = self.config
+        self.E = cfg.num_experts
+        self.e_local = experts_per_rank(self.E, world)
+        self.e0 = rank * self.e_local
+        self.k = mixer.active_experts
+        self.d = cfg.d_model
+        self._layer_dims = layer_dims
+        self.lut = softplus_table(device) if cfg.router_score_transform == "softplus" else None
+        self._ws: dict[tuple, Tensor] = {}
+        self._pack()
+
+    # ---- packing
+    def _local_dims(self, rows: int) -> _lib.LayerDims:
+        dims = self._layer_dims(self.config, max(rows, 1), 1)
+        dims.num_experts = self.e_local
+        dims.shared_dim = 0
+        return dims
+
+    def _pack(self) -> None:
+        lib = _lib.load()
+        m = self.mixer
+        dev = self.device
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        full = self._layer_dims(self.config, 1, self.k)
+        sizes = _lib.PackedSizes()
+        _lib.check(lib.spx_layer_sizes(full, None, sizes), "spx_layer_sizes")
+        s = m.shared
+        t = lambda x: None if x is None else x.detach().contiguous()  # noqa: E731
+        keep = {
+            "router_weight": t(m.router.proj.weight), "router_bias": t(m.router.proj.bias),
+            "shared_gate": None if s is None else t(s.gate_projection.weight),
+            "shared_up": None if s is None else t(s.up_projection.weight),
+            "shared_down": None if s is None else t(s.down_projection.weight),
+        }
+        empty = lambda n: torch.empty(max(1, n), dtype=torch.int16, device=dev)  # noqa: E731
+        self.router_w = empty(sizes.router_weight)
+        self.shared_w1 = empty(sizes.shared_w1) if sizes.shared_w1 else None
+        self.shared_w2 = empty(sizes.shared_w2) if sizes.shared_w2 else None
+        src = _lib.ReferenceWeights(router_weight=_lib.ptr(keep["router_weight"]), router_bias=_lib.ptr(keep["router_bias"]),
+                                    shared_gate=_lib.ptr(keep["shared_gate"]), shared_up=_lib.ptr(keep["shared_up"]),
+                                    shared_down=_lib.ptr(keep["shared_down"]))
+        _lib.check(lib.spx_pack_weights(full, src, self.router_w.data_ptr(), None, None, _lib.ptr(self.shared_w1),
+                                        _lib.ptr(self.shared_w2), stream), "spx_pack_weights (router/shared)")
+        # this rank's experts
+        sl = slice(self.e0, self.e0 + self.e_local)
+        gate = m.experts.gate_proj.detach()[sl].contiguous()
+        up = m.experts.up_proj.detach()[sl].contiguous()
+        down = m.experts.down_proj.detach()[sl].contiguous()
+        local = self._local_dims(1)
+        lsizes = _lib.PackedSizes()
+        _lib.check(lib.spx_layer_sizes(local, None, lsizes), "spx_layer_sizes")
+        self.w1 = empty(lsizes.expert_w1)
+        self.w2 = empty(lsizes.expert_w2)
+        dummy_router = torch.zeros(self.e_local, self.d, dtype=torch.bfloat16, device=dev)
+        esrc = _lib.ReferenceWeights(router_weight=dummy_router.data_ptr(), gate_proj=gate.data_ptr(),
+                                     up_proj=up.data_ptr(), down_proj=down.data_ptr())
+        scratch_router = empty(lsizes.router_weight)
+        _lib.check(lib.spx_pack_weights(local, esrc, scratch_router.data_ptr(), self.w1.data_ptr(),
+                                        self.w2.data_ptr(), None, None, stream), "spx_pack_weights (experts)")
+        self.mx = {}
+        if local.mxfp8_lane:
+            for name in ("expert_w1_mx", "expert_w1_mx_scales", "expert_w2_mx", "expert_w2_mx_scales"):
+                self.mx[name] = torch.empty(max(16, getattr(lsizes, name)), dtype=torch.uint8, device=dev)
+            _lib.check(lib.spx_pack_weights_mxfp8(local, esrc, *(self.mx[n].data_ptr() for n in (
+                "expert_w1_mx", "expert_w1_mx_scales", "expert_w2_mx", "expert_w2_mx_scales")), stream),
+                "spx_pack_weights_mxfp8")
+        self._keep = (keep, gate, up, down, dummy_router, scratch_router)
+
+    def _weights(self, lanes: Tensor | None = None) -> _lib.PackedWeights:
+        return _lib.PackedWeights(
+            router_weight=self.router_w.data_ptr(), router_bias=_lib.ptr(self._keep[0]["router_bias"]),
+            expert_w1=self.w1.data_ptr(), expert_w2=self.w2.data_ptr(),
+            shared_w1=_lib.ptr(self.shared_w1), shared_w2=_lib.ptr(self.shared_w2),
+            softplus_table=_lib.ptr(self.lut), resident_mask=None,
+            expert_lane_mxfp8=_lib.ptr(lanes),
+            expert_w1_mx=_lib.ptr(self.mx.get("expert_w1_mx")),
+            expert_w1_mx_scales=_lib.ptr(self.mx.get("expert_w1_mx_scales")),
+            expert_w2_mx=_lib.ptr(self.mx.get("expert_w2_mx")),
+            expert_w2_mx_scales=_lib.ptr(self.mx.get("expert_w2_mx_scales")),
+        )
+
+    def _workspace(self, dims: _lib.LayerDims, tag: str) -> Tensor:
+        lib = _lib.load()
+        n = _lib.ctypes.c_size_t()
+        _lib.check(lib.spx_layer_sizes(dims, n, None), "spx_layer_sizes")
+        ws = self._ws.get(tag)
+        if ws is None or ws.numel() < n.value:
+            ws = torch.zeros(n.value, dtype=torch.uint8, device=self.device)
+            self._ws[tag] = ws
+        return ws
+
+    # ---- stages
+    def route(self, x: Tensor, router_logits: Tensor | None = None) -> dict[str, Tensor]:
+        lib = _lib.load()
+        T = x.shape[0]
+        E, k, dev = self.E, self.k, self.device
+        dims = self._layer_dims(self.config, T, k)
+        ws = self._workspace(dims, "route")
+        r = {
+            "router_scores": torch.empty(T, E, dtype=torch.bfloat16, device=dev),
+            "expert_ids": torch.empty(T, k, dtype=torch.long, device=dev),
+            "routing_weights": torch.empty(T, k, dtype=torch.bfloat16, device=dev),
+            "expert_utilization": torch.empty(E, dtype=torch.float32, device=dev),
+            "group_stats": torch.empty(6, dtype=torch.long, device=dev),
+            "group_ratios": torch.empty(2, dtype=torch.float32, device=dev),
+            "auxiliary_loss": torch.empty(1, dtype=torch.bfloat16, device=dev),
+            "order": torch.empty(T * k, dtype=torch.int32, device=dev),
+            "counts": torch.empty(E, dtype=torch.int32, device=dev),
+            "rank": torch.empty(T * k, dtype=torch.int32, device=dev),
+        }
+        outs = _lib.LayerOutputs(
+            router_scores=r["router_scores"].data_ptr(), expert_ids=r["expert_ids"].data_ptr(),
+            routing_weights=r["routing_weights"].data_ptr(), expert_utilization=r["expert_utilization"].data_ptr(),
+            group_stats=r["group_stats"].data_ptr(), group_ratios=r["group_ratios"].data_ptr(),
+            auxiliary_loss=r["auxiliary_loss"].data_ptr(), dispatch_order=r["order"].data_ptr(),
+            expert_counts=r["counts"].data_ptr(), injected_logits=_lib.ptr(router_logits),
+            pair_rank=r["rank"].data_ptr(),
+        )
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        _lib.check(lib.spx_layer_route(dims, self._weights(), x.data_ptr(), outs, ws.data_ptr(), stream),
+                   "spx_layer_route")
+        return r
+
+    def gather(self, x: Tensor, order: Tensor, div: int) -> Tensor:
+        lib = _lib.load()
+        out = torch.empty(order.numel(), x.shape[1], dtype=x.dtype, device=x.device)
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        _lib.check(lib.spx_gather_rows(x.data_ptr(), x.stride(0), order.data_ptr(), div, order.numel(), x.shape[1],
+                                       out.data_ptr(), out.stride(0), stream), "spx_gather_rows")
+        return out
+
+    def experts(self, rows: Tensor, row_expert: Tensor, lanes: Tensor | None) -> Tensor:
+        out = torch.empty_like(rows)
+        R = rows.shape[0]
+        if R == 0:
+            return out
+        lib = _lib.load()
+        dims = self._local_dims(R)
+        ws = self._workspace(dims, "experts")
+        stream = torch.cuda.current_stream(rows.device).cuda_stream
+        _lib.check(lib.spx_experts_forward(dims, self._weights(lanes), rows.data_ptr(), row_expert.data_ptr(),
+                                           out.data_ptr(), ws.data_ptr(), stream), "spx_experts_forward")
+        return out
+
+    def shared(self, x: Tensor) -> Tensor | None:
+        if self.shared_w1 is None:
+            return None
+        lib = _lib.load()
+        dims = self._layer_dims(self.config, x.shape[0], self.k)
+        ws = self._workspace(dims, "shared")
+        out = torch.empty_like(x)
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        _lib.check(lib.spx_shared_forward(dims, self._weights(), x.data_ptr(), out.data_ptr(), ws.data_ptr(), stream),
+                   "spx_shared_forward")
+        return out
+
+    def combine(self, rows: Tensor, rank: Tensor, weights: Tensor, shared: Tensor | None) -> Tensor:
+        lib = _lib.load()
+        T = weights.shape[0]
+        out = torch.empty(T, self.d, dtype=torch.bfloat16, device=rows.device)
+        stream = torch.cuda.current_stream(rows.device).cuda_stream
+        _lib.check(lib.spx_combine(rows.data_ptr(), rank.data_ptr(), weights.data_ptr(), _lib.ptr(shared), T, self.d,
+                                   self.k, out.data_ptr(), stream), "spx_combine")
+        return out
+
+
+class ExpertParallelMixer:
+    """Expert-parallel forward of a `B200MicroExpertChannelMixer` (same
+    parameters on every rank; rank r executes experts [r*E/G, (r+1)*E/G)).
+
+    ``forward(hidden [B, S, d])`` takes this rank's tokens and returns their
+    update and this rank's routing metrics (statistics over the local tokens).
+    """
+
+    def __init__(self, mixer: Any, group: Any = None, ops: Any = None):
+        self.mixer = mixer
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.e_local = experts_per_rank(mixer.config.num_experts, self.world)
+        if ops is None:
+            device = next(mixer.parameters()).device
+            ops = CudaOps(mixer, self.rank, self.world, device)
+        self.ops = ops
+        self.side = torch.cuda.Stream(ops.device) if isinstance(ops, CudaOps) else None
+
+    def _local_lanes(self) -> Tensor | None:
+        lanes = self.mixer._lanes(self.ops.device) if isinstance(self.ops, CudaOps) else None
+        if lanes is None:
+            return None
+        return lanes[self.rank * self.e_local:(self.rank + 1) * self.e_local].contiguous()
+
+    def forward(self, hidden: Tensor, *, router_logits: Tensor | None = None) -> dict[str, Any]:
+        B, S, d = hidden.shape
+        T = B * S
+        x = hidden.reshape(T, d).contiguous()
+        ops = self.ops
+        k = self.mixer.active_experts
+        shared = None
+        if self.side is not None:
+            # the shared SwiGLU needs only x: run it while the rows travel
+            self.side.wait_stream(torch.cuda.current_stream(ops.device))
+            with torch.cuda.stream(self.side):
+                shared = ops.shared(x)
+        else:
+            shared = ops.shared(x)
+        logits = None if router_logits is None else router_logits.reshape(T, -1).contiguous()
+        r = ops.route(x, logits)
+        # 2. counts exchange; the only host read of the forward
+        recv_counts = torch.empty(self.world * self.e_local, dtype=torch.int32, device=r["counts"].device)
+        dist.all_to_all_single(recv_counts, r["counts"], group=self.group)
+        plan = exchange_plan(r["counts"].cpu().numpy(), recv_counts.cpu().numpy(), self.world)
+        # 3. rows to their experts' ranks
+        send = ops.gather(x, r["order"], k)
+        recv = send.new_empty(sum(plan.recv_rows), d)
+        dist.all_to_all_single(recv, send, output_split_sizes=plan.recv_rows, input_split_sizes=plan.send_rows,
+                               group=self.group)
+        # 4. local experts, unweighted
+        row_expert = receive_expert_ids(plan, recv.device)
+        out_rows = ops.experts(recv, row_expert, self._local_lanes())
+        # 5. back to the senders (in their dispatch order)
+        back = send.new_empty(T * k, d)
+        dist.all_to_all_single(back, out_rows, output_split_sizes=plan.send_rows, input_split_sizes=plan.recv_rows,
+                               group=self.group)
+        # 6. combine with the routing weights and the shared output
+        if self.side is not None:
+            torch.cuda.current_stream(ops.device).wait_stream(self.side)
+            if shared is not None:
+                shared.record_stream(torch.cuda.current_stream(ops.device))
+        update = ops.combine(back, r["rank"], r["routing_weights"], shared)
+        return {
+            "update": update.reshape(B, S, d),
+            "auxiliary_loss": r["auxiliary_loss"][0],
+            "expert_ids": r["expert_ids"].reshape(B, S, k),
+            "routing_weights": r["routing_weights"].reshape(B, S, k),
+            "router_scores": r["router_scores"].reshape(B, S, -1),
+            "expert_utilization": r["expert_utilization"],
+            "send_rows": plan.send_rows,
+            "recv_rows": plan.recv_rows,
+        }
+
+    __call__ = forward
+
+
+__all__ = ["CudaOps", "ExchangePlan", "ExpertParallelMixer", "exchange_plan", "experts_per_rank",
+           "receive_expert_ids"]
