@@ -156,7 +156,8 @@ def workload_config(name: str, world: int) -> dict:
                              "of the experts (randperm seed 2), BF16 for the rest"
                              if spec.get("mxfp8_fraction") else "BF16 for all experts"),
         "weights": "random init, torch.manual_seed(0), N(0,0.02)",
-        "l2": "inputs larger than L2: two 100.7 MB hidden-state batches alternated + 121.6 MB weights; steps timed back to back",
+        "l2": (f"inputs larger than L2: two {spec['batch'] * spec['seq'] * cfg['d_model'] * 2 / 1e6 / (world if ep else 1):.1f} MB "
+               "hidden-state batches alternated, plus the weights; steps timed back to back"),
         "parallelism": f"ep{world}" if ep and world > 1 else f"dp{world}",
     }
 
