@@ -47,6 +47,11 @@ CONFIGS = {
     "ep_skew": dict(cfg=dict(d_model=1024, num_experts=200, expert_inter_dim=256, shared_inter_dim=2048,
                              active_experts=8, router_bias=True), batch=128, seq=1024, cpu_sample=256,
                     zipf=True, expert_parallel=True),
+    # decode-shaped steps through a 16-layer stack (independent seeded weights per
+    # layer, 10% of each layer's experts in MXFP8); the forward of the stack is one CUDA graph.
+    "decode": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
+                            active_experts=8), batch=1, seq=64, cpu_sample=64, mxfp8_fraction=0.10,
+                   decode_layers=16, decode_tokens=(1, 8, 64)),
     # 10M-preset shape.
     "m10": dict(cfg=dict(d_model=256, num_experts=200, expert_inter_dim=64, shared_inter_dim=256,
                          active_experts=8), batch=32, seq=512, cpu_sample=4096),
@@ -85,7 +90,7 @@ def mxfp8_experts(num_experts: int, fraction: float):
     return lane
 
 
-def build_mixer(spec: dict, device=None):
+def build_mixer(spec: dict, device=None, seed: int = 0):
     """The bench layer: seed-0 random init; MXFP8 configs run their seeded expert set in MXFP8.
 
     The reference expresses a mixed layer as MXFP8 expert weights whose promoted
@@ -102,7 +107,7 @@ def build_mixer(spec: dict, device=None):
         cfg.update(expert_weight_format="mxfp8", expert_activation_format="mxfp8",
                    expert_promotion_format="bfloat16")
     config = MicroExpertsConfig(**cfg)
-    torch.manual_seed(0)
+    torch.manual_seed(seed)
     mixer = B200MicroExpertChannelMixer(config).to(torch.bfloat16).eval()
     lane = None
     if fraction > 0:
@@ -544,6 +549,116 @@ def run_ep(args) -> None:
         dist.destroy_process_group()
 
 
+def run_decode(args) -> None:
+    """Decode-shaped steps: T tokens (T = 1, 8, 64) through a 16-layer stack
+    of MoE layers with residual adds, captured once as a CUDA graph per T and
+    replayed.  value = routed tokens/s per layer at the largest T; the other
+    token counts are reported beside it.  Data parallel replicas for N > 1."""
+
+    world, rank, local = init_dist()
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    spec = CONFIGS[args.config]
+    L = spec["decode_layers"]
+    layers = [build_mixer(spec, device, seed=l)[0] for l in range(L)]
+    config = layers[0].config
+    K, W = max(args.steps, 10), args.warmup
+    per_t = {}
+    clocks = None
+    e2e = {}
+    with torch.inference_mode():
+        for T in spec["decode_tokens"]:
+            x_host = torch.randn(1, T, config.d_model, generator=torch.Generator().manual_seed(1 + rank))
+            x_host = x_host.to(torch.bfloat16).pin_memory()
+            x_static = x_host.to(device)
+
+            def stack(x):
+                for m in layers:
+                    x = x + m(x).update
+                return x
+
+            for _ in range(W):  # eager warm-up: packs weights, sizes workspaces, caches launch attributes
+                out = stack(x_static)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                out_static = stack(x_static)
+            for _ in range(W):
+                graph.replay()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            sampler = ClockSampler(local) if T == spec["decode_tokens"][-1] else None
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record()
+            for _ in range(K):
+                graph.replay()
+            t1.record()
+            torch.cuda.synchronize()
+            if sampler is not None:
+                clocks = sampler.stop()
+            ms = t0.elapsed_time(t1) / K
+            # e2e: pinned H2D of the step's tokens, the graph, D2H of the output
+            out_host = torch.empty(1, T, config.d_model, dtype=torch.bfloat16).pin_memory()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(K):
+                x_static.copy_(x_host, non_blocking=True)
+                graph.replay()
+                out_host.copy_(out_static, non_blocking=True)
+            e1.record()
+            torch.cuda.synchronize()
+            t = torch.tensor([ms, e0.elapsed_time(e1) / K], dtype=torch.float64, device=device)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            per_t[T] = (float(t[0]), float(t[1]))
+            del graph
+    T = spec["decode_tokens"][-1]
+    ms, e2e_ms = per_t[T]
+    if rank == 0:
+        pk = peaks()
+        # weight bytes a step must read per layer: distinct experts (expected 200(1-(1-k/E)^T)) x their
+        # BF16/MXFP8 bytes, plus shared and router weights
+        E, d, I, k, S = config.num_experts, config.d_model, config.resolved_inter_dim, config.active_experts, 768
+        frac = spec["mxfp8_fraction"]
+        per_expert = (1 - frac) * 3 * d * I * 2 + frac * (3 * d * I + 3 * d * I // 32)
+        distinct = E * (1 - (1 - k / E) ** T)
+        bytes_layer = distinct * per_expert + 3 * d * S * 2 + E * d * 2
+        line = {
+            "metric": METRIC, "value": world * T * L / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) tokens, seeded random-init layers)",
+            "config": {"workload": f"decode: {T} tokens x {L}-layer MoE stack per step (CUDA graph)",
+                       "layers": L, "tokens_per_step": T, "d_model": d, "num_experts": E, "expert_inter_dim": I,
+                       "top_k": k, "shared_inter_dim": S,
+                       "expert_precision": f"MXFP8 for a seeded {frac:.0%} of each layer's experts, BF16 rest",
+                       "l2": "each layer's weights (~122 MB) are read once per step; 16 layers exceed L2",
+                       "parallelism": f"dp{world} replicas"},
+            "per_token_count": {str(tt): {"ms_per_step": v[0], "tokens_per_s_per_layer": world * tt * L / (v[0] / 1e3),
+                                          "e2e_ms_per_step": v[1]} for tt, v in per_t.items()},
+            "e2e": {"value": world * T * L / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": T * d * 2, "d2h_bytes_per_step": T * d * 2},
+            "gpu_launches": K * L * 15,
+            "roofline": {"bound": "hbm", "kernel": "whole stack (weight bytes of the routed experts)",
+                         "achieved": bytes_layer * L / (ms / 1e3) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "traffic": None, "peak_source": pk["source"]},
+        }
+        line["roofline"]["frac"] = line["roofline"]["achieved"] / line["roofline"]["peak"]
+        if clocks is not None:
+            line["clocks"] = clocks
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -559,6 +674,8 @@ def main() -> None:
         run_reference_arm(args)
     elif CONFIGS[args.config].get("expert_parallel"):
         run_ep(args)
+    elif CONFIGS[args.config].get("decode_layers"):
+        run_decode(args)
     else:
         run_ours(args)
 

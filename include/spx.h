@@ -38,6 +38,8 @@
  *   spx_shared_forward SwiGLU.forward                    nn/ffn.py:27-30
  *   spx_combine        _weighted_expert_updates + index_add + shared add
  *                                                        bank.py:764-778, mixer.py:207
+ *   spx_surprise_calibration  _attach_surprise_telemetry + _attribute_nll_to_experts
+ *                                                        modeling.py:1468-1534
  */
 #ifndef SPX_H_
 #define SPX_H_
@@ -230,6 +232,20 @@ int spx_shared_forward(const spx_layer_dims* dims, const spx_packed_weights* wei
  * NULL = no shared path. */
 int spx_combine(const uint16_t* expert_rows, const int32_t* pair_rank, const uint16_t* pair_weights,
                 const uint16_t* shared, int64_t tokens, int32_t d, int32_t top_k, uint16_t* update, void* stream);
+
+/* Router calibration loss term and per-expert NLL attribution of one layer
+ * (the reference's _attach_surprise_telemetry / _attribute_nll_to_experts,
+ * modeling.py:1468-1534).  Inputs: the layer's router_scores [B, S, E],
+ * expert_ids [B, S, k] and routing_weights [B, S, k], the next-token NLL
+ * [B, S-1] (float) and its validity mask [B, S-1] (0/1 bytes).  Outputs
+ * (any may be NULL): the mean smooth-L1 calibration loss over valid
+ * positions (float scalar; NaN when none is valid), expert_attributed_nll [E]
+ * and potentiation_utilization [E] (float).  Deterministic. */
+size_t spx_calibration_workspace(int64_t batch, int64_t seq, int32_t num_experts);
+int spx_surprise_calibration(const uint16_t* router_scores, const int64_t* expert_ids, const uint16_t* routing_weights,
+                             const float* token_nll, const uint8_t* valid, int64_t batch, int64_t seq,
+                             int32_t num_experts, int32_t top_k, float* calibration, float* attributed_nll,
+                             float* utilization, void* workspace, size_t workspace_bytes, void* stream);
 
 /* spx_dispatch without a workspace: same outputs, no device allocation by
  * anyone.  No counterpart in the reference; it exists for callers that cannot

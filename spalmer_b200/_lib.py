@@ -46,6 +46,8 @@ EXPORTED = (
     "spx_experts_forward",
     "spx_shared_forward",
     "spx_combine",
+    "spx_calibration_workspace",
+    "spx_surprise_calibration",
 )
 
 ABI_VERSION = 3
@@ -182,6 +184,12 @@ def load() -> ctypes.CDLL:
         ),
         "spx_experts_forward": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, _vp, _vp, _vp, _vp]),
         "spx_shared_forward": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, _vp, _vp, _vp]),
+        "spx_calibration_workspace": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32]),
+        "spx_surprise_calibration": (
+            ctypes.c_int,
+            [_vp, _vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, _vp, _vp, _vp,
+             _vp, ctypes.c_size_t, _vp],
+        ),
         "spx_combine": (
             ctypes.c_int,
             [_vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, _vp, _vp],

@@ -780,6 +780,28 @@ int spx_gather_rows(const uint16_t* src, int64_t ld_src, const int32_t* index, i
   return launch_gather_rows(src, ld_src, index, index_div, rows, d, out, ld_out, static_cast<cudaStream_t>(stream));
 }
 
+size_t spx_calibration_workspace(int64_t batch, int64_t seq, int32_t num_experts) {
+  if (batch < 1 || seq < 2 || num_experts < 1) return 0;
+  return calibration_workspace_bytes(batch, seq, num_experts);
+}
+
+int spx_surprise_calibration(const uint16_t* router_scores, const int64_t* expert_ids, const uint16_t* routing_weights,
+                             const float* token_nll, const uint8_t* valid, int64_t batch, int64_t seq,
+                             int32_t num_experts, int32_t top_k, float* calibration, float* attributed_nll,
+                             float* utilization, void* workspace, size_t workspace_bytes, void* stream) {
+  if (batch < 1 || seq < 2 || num_experts < 1 || num_experts > 4096 || top_k < 1 || top_k > 32)
+    return SPX_ERR_INVALID_ARG;
+  if (router_scores == nullptr || expert_ids == nullptr || routing_weights == nullptr || token_nll == nullptr ||
+      valid == nullptr)
+    return SPX_ERR_INVALID_ARG;
+  if (workspace == nullptr || workspace_bytes < calibration_workspace_bytes(batch, seq, num_experts))
+    return SPX_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return SPX_ERR_ALIGNMENT;
+  return launch_calibration(router_scores, expert_ids, routing_weights, token_nll, valid, batch, seq, num_experts,
+                            top_k, calibration, attributed_nll, utilization, workspace,
+                            static_cast<cudaStream_t>(stream));
+}
+
 int spx_workspace_status(void* workspace, int* device_status, int clear, void* stream) {
   if (workspace == nullptr || device_status == nullptr) return SPX_ERR_INVALID_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

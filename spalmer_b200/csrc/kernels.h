@@ -147,6 +147,12 @@ int gemm_pick_stages(int bn, int k_blocks, bool mx, int epi);
 // `mx` selects the block-scaled MXFP8 kernel (bn <= 128, k_blocks of 128 elements).
 int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream, bool mx = false);
 
+// Router calibration loss term and NLL attribution (calibration.cu).
+size_t calibration_workspace_bytes(int64_t B, int64_t S, int E);
+int launch_calibration(const uint16_t* scores, const int64_t* ids, const uint16_t* weights, const float* nll,
+                       const uint8_t* valid, int64_t B, int64_t S, int E, int k, float* calibration,
+                       float* attributed, float* utilization, void* workspace, cudaStream_t stream);
+
 // MXFP8 quantisers (mxfp8.cu).
 int launch_mx_quantize_rows(const uint16_t* src, int64_t rows, int cols, int64_t ld_src, int kp, uint8_t* q,
                             int64_t ld_q, uint8_t* sf, int64_t ld_sf, cudaStream_t stream);
