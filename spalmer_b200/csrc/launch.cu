@@ -42,10 +42,18 @@ int ensure_max_dynamic_smem(const void* func) {
     if (g_func[dev][i] == func) return SPX_OK;
     if (g_func[dev][i] == nullptr) {
       int optin = 0;
-      if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+      cudaFuncAttributes attr{};
+      if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+          cudaFuncGetAttributes(&attr, func) != cudaSuccess) {
+        cudaGetLastError();  // clear, so later launch checks do not see it
         return SPX_ERR_CUDA;
-      if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess)
+      }
+      // The opt-in limit covers static and dynamic shared memory together.
+      const int dyn = optin - static_cast<int>(attr.sharedSizeBytes);
+      if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) != cudaSuccess) {
+        cudaGetLastError();
         return SPX_ERR_CUDA;
+      }
       g_func[dev][i] = func;
       return SPX_OK;
     }
