@@ -91,7 +91,10 @@ typedef struct spx_reference_weights {
 } spx_reference_weights;
 
 /* Element counts (uint16_t) of the packed weight buffers; the *_mx fields
- * are BYTES of the MXFP8 copies (zero unless dims->mxfp8_lane). */
+ * are BYTES of the MXFP8 copies (zero unless dims->mxfp8_lane).  Packed
+ * layouts depend on the batch class of dims->tokens (<= 256 tokens: decode
+ * tiles; more: throughput tiles): pack with a dims of the same class as the
+ * forward that uses the weights. */
 typedef struct spx_packed_sizes {
   size_t router_weight;
   size_t expert_w1;

@@ -54,31 +54,36 @@ int make_shape(const spx_layer_dims* dm, Shape* s) {
   if (s->T * s->k > (int64_t(1) << 31) - 1) return SPX_ERR_UNSUPPORTED;
   s->P = s->T * s->k;
   s->kd = round_up_i(s->d, 64);
-  s->c = std::min(round_up_i(s->I, 16), 128);
+  // Decode-sized batches (few rows per expert) read weights far more than they
+  // compute: narrow N tiles spread each weight matrix over more CTAs.  The
+  // packed GEMM1 layouts follow the chunk width, so they depend on this class.
+  const bool small = s->T <= kSmallBatchTokens;
+  const int wide = small ? 32 : 128;
+  s->c = std::min(round_up_i(s->I, 16), wide);
   s->nc = ceil_div(s->I, s->c);
   s->kp = round_up_i(s->nc * s->c, 64);
   if (s->S > 0) {
-    s->cs = std::min(round_up_i(s->S, 16), 128);
+    s->cs = std::min(round_up_i(s->S, 16), wide);
     s->ncs = ceil_div(s->S, s->cs);
     s->ksp = round_up_i(s->ncs * s->cs, 64);
   } else {
     s->cs = s->ncs = s->ksp = 0;
   }
-  s->bn_router = std::min(256, round_up_i(s->E, 16));
+  s->bn_router = std::min(small ? 32 : 256, round_up_i(s->E, 16));
   s->gn_router = ceil_div(s->E, s->bn_router);
-  s->bn_d = std::min(256, round_up_i(s->d, 16));
+  s->bn_d = std::min(small ? 64 : 256, round_up_i(s->d, 16));
   s->gn_d = ceil_div(s->d, s->bn_d);
-  s->lb_blocks = ceil_div(s->T, kRouteRows);
+  s->lb_blocks = route_lb_blocks(s->T);
   s->nchunks = ceil_div(s->P, kDispatchChunk);
   s->max_tiles = ceil_div(s->P, kTileRows) + s->E;
   s->mx = dm->mxfp8_lane != 0;
   if (s->mx) {
     if (s->I % kMxBlock != 0) return SPX_ERR_UNSUPPORTED;
     s->kx = round_up_i(s->d, 128);
-    s->cm = (s->I % 128 == 0) ? 128 : (s->I % 64 == 0) ? 64 : 32;
+    s->cm = small ? 32 : (s->I % 128 == 0) ? 128 : (s->I % 64 == 0) ? 64 : 32;
     s->ncm = s->I / s->cm;
     s->kh = round_up_i(s->I, 128);
-    s->bn2m = std::min(kMxDenseBn, round_up_i(s->d, 16));
+    s->bn2m = std::min(small ? 64 : kMxDenseBn, round_up_i(s->d, 16));
     s->gn2m = ceil_div(s->d, s->bn2m);
   } else {
     s->kx = s->cm = s->ncm = s->kh = s->bn2m = s->gn2m = 0;

@@ -18,6 +18,9 @@ constexpr int kSliceCols = 64;                  // epilogue staging slice width
 constexpr int kStageBytesPerWarp = 32 * kSliceCols * 2;
 constexpr int kRouteRows = 128;        // token rows per route_select CTA
 constexpr int kTieWarps = 8;           // rows replayed at once per route_ties CTA (one warp each)
+constexpr int kRouteWarps = 8;         // warps per small-T route CTA (one token row per warp)
+constexpr int kRouteRowsMaxTokens = 4096;  // up to this many rows the warp-per-row route kernel runs
+constexpr int kSmallBatchTokens = 256;     // decode-sized batches: narrow GEMM tiles (see make_shape)
 constexpr int kMaxTopK = 20;           // MicroExpertsConfig.max_active_experts default
 constexpr int kDispatchChunk = 2048;   // pairs per dispatch CTA
 constexpr int kDispatchWarps = 4;
@@ -134,6 +137,7 @@ int ensure_max_dynamic_smem(const void* func);
 int launch_softplus_table(uint16_t* lut, cudaStream_t stream);
 size_t route_select_smem(int num_experts);
 int launch_route(const RouteArgs& a, cudaStream_t stream);
+int route_lb_blocks(int64_t tokens);  // rows of the route kernel's load-balance partials
 int launch_dispatch(const DispatchArgs& a, cudaStream_t stream);
 
 // Tensor maps with 128-byte rows per box (64 BF16 or 128 bytes of E4M3), 128B swizzle.

@@ -16,6 +16,9 @@
 // route_ties_kernel: replays PyTorch's CPU top-k (topk_exact.cuh) for every
 //   listed row, one warp per row (each partition step data-parallel over the
 //   warp), the row staged in shared memory.
+// route_rows_kernel: the same results for small batches (<= 4096 rows), one
+//   warp per row end to end (tie replay inline), so a handful of rows still
+//   spreads over many warps.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -310,6 +313,193 @@ __device__ void warp_topk_cpu_order(uint32_t* v, int n, int k, uint16_t* lpos, u
   __syncwarp();
 }
 
+__device__ __forceinline__ uint16_t key16_to_bits(uint32_t key) {
+  return (key & 0x8000u) ? static_cast<uint16_t>(key & 0x7FFFu) : static_cast<uint16_t>(~key & 0xFFFFu);
+}
+
+// Column of lane `lane`'s slot q (8 slots per 256-column chunk).
+__device__ __forceinline__ int route_col(int q, int lane, bool vec) {
+  return vec ? 8 * (32 * (q >> 3) + lane) + (q & 7) : lane + 32 * q;
+}
+
+// Small-T route: one warp per token row (rows strided over all warps).  Lane l
+// owns 8 consecutive columns per 256-column chunk (one 16-byte load), maps
+// them through the softplus table and writes router_scores; the k+1 smallest
+// (score, index) keys come out of k+1 rounds of a warp min-reduction
+// (redux.sync).  Rows whose k+1 scores are distinct are final; otherwise the
+// same warp replays PyTorch's CPU top-k (warp_topk_cpu_order).  Lanes keep
+// per-column load-balance sums; a CTA reduces its warps' sums into one
+// partial row.  Used when the rows are too few to fill the GPU one thread
+// per row (decode-sized batches).
+template <int NCH, int K1MAX>
+__global__ void __launch_bounds__(kRouteWarps * 32) route_rows_kernel(const RouteArgs a) {
+  constexpr int NQ = 8 * NCH;  // columns per lane
+  extern __shared__ uint32_t route_smem[];
+  const int E = a.num_experts;
+  const int k = a.top_k;
+  const int k1 = min(k + 1, E);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half_words = (E + 1) / 2;
+  float* lb = reinterpret_cast<float*>(route_smem);                               // [warps][E]
+  uint8_t* resident = reinterpret_cast<uint8_t*>(lb + kRouteWarps * E);            // [E]
+  uint32_t* v = route_smem + kRouteWarps * E + (E + 3) / 4 + warp * (E + 2 * half_words);
+  uint16_t* lpos = reinterpret_cast<uint16_t*>(v + E);
+  uint16_t* rpos = reinterpret_cast<uint16_t*>(v + E + half_words);
+  for (int c = threadIdx.x; c < E; c += blockDim.x) resident[c] = a.resident ? a.resident[c] : 1;
+  __syncthreads();
+
+  const bool vec = (E & 7) == 0 && (reinterpret_cast<uintptr_t>(a.logits) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.scores) & 15u) == 0;
+  float acc[NQ];
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) acc[q] = 0.0f;
+
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kRouteWarps;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kRouteWarps + warp; row < a.tokens; row += nwarps) {
+    const uint16_t* src = a.logits + row * E;
+    uint16_t* dst = a.scores + row * E;
+    // ---- scores of this lane's columns (raw BF16 bits)
+    uint16_t sc[NQ];
+    if (vec) {
+#pragma unroll
+      for (int m = 0; m < NCH; ++m) {
+        const int c0 = 8 * (32 * m + lane);
+        if (c0 < E) {
+          uint4 u = __ldg(reinterpret_cast<const uint4*>(src + c0));
+          uint16_t* h = reinterpret_cast<uint16_t*>(&u);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (a.lut != nullptr) h[j] = __ldg(a.lut + h[j]);
+            sc[8 * m + j] = h[j];
+          }
+          *reinterpret_cast<uint4*>(dst + c0) = u;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) sc[8 * m + j] = 0;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        const int c = lane + 32 * q;
+        uint16_t b = 0;
+        if (c < E) {
+          b = src[c];
+          if (a.lut != nullptr) b = __ldg(a.lut + b);
+          dst[c] = b;
+        }
+        sc[q] = b;
+      }
+    }
+    // ---- k+1 smallest keys (order_key16 << 16 | column), ascending
+    uint32_t key[NQ];
+    uint32_t lane_min = 0xFFFFFFFFu;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      const int c = route_col(q, lane, vec);
+      uint32_t w = 0xFFFFFFFFu;
+      if (c < E) w = (order_key16(resident[c] ? sc[q] : static_cast<uint16_t>(0x7F80u)) << 16) | static_cast<uint32_t>(c);
+      key[q] = w;
+      lane_min = min(lane_min, w);
+    }
+    uint32_t best[K1MAX];
+#pragma unroll
+    for (int j = 0; j < K1MAX; ++j) {
+      best[j] = 0xFFFFFFFFu;
+      if (j < k1) {
+        const uint32_t m = __reduce_min_sync(0xFFFFFFFFu, lane_min);
+        best[j] = m;
+        if (lane_min == m) {
+          uint32_t nm = 0xFFFFFFFFu;
+#pragma unroll
+          for (int q = 0; q < NQ; ++q) {
+            if (key[q] == m) key[q] = 0xFFFFFFFFu;
+            nm = min(nm, key[q]);
+          }
+          lane_min = nm;
+        }
+      }
+    }
+    bool tie = false;
+#pragma unroll
+    for (int j = 0; j + 1 < K1MAX; ++j)
+      if (j + 1 < k1 && (best[j] >> 16) == (best[j + 1] >> 16)) tie = true;
+
+    // ---- routing weights: softmax(-selected scores) in double, summed in slot order.
+    // They depend only on the selected scores in ascending order, which a tie
+    // does not change; with a resident mask a tie row is recomputed below.
+    uint32_t mine = 0;
+#pragma unroll
+    for (int j = 0; j < K1MAX; ++j)
+      if (j == lane) mine = best[j];
+    const double x0 = -static_cast<double>(bf16_to_f32(key16_to_bits(best[0] >> 16)));
+    double e = 0.0;
+    if (lane < k) e = exp(-static_cast<double>(bf16_to_f32(key16_to_bits(mine >> 16))) - x0);
+    double sum = 0.0;
+    for (int j = 0; j < k; ++j) sum += __shfl_sync(0xFFFFFFFFu, e, j);
+    if (lane < k) a.weights[row * k + lane] = f32_to_bf16_rne(__double2float_rn(e / sum));
+
+    if (!tie) {
+      if (lane < k) a.ids[row * k + lane] = static_cast<int64_t>(mine & 0xFFFFu);
+    } else {
+      // Exact CPU order: stage (raw bits << 16 | column) and replay nth_element + sort.
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        const int c = route_col(q, lane, vec);
+        if (c < E) {
+          const uint16_t b = resident[c] ? sc[q] : static_cast<uint16_t>(0x7F80u);
+          v[c] = (static_cast<uint32_t>(b) << 16) | static_cast<uint32_t>(c);
+        }
+      }
+      __syncwarp();
+      warp_topk_cpu_order(v, E, k, lpos, rpos, lane);
+      if (lane < k) a.ids[row * k + lane] = static_cast<int64_t>(v[lane] & 0xFFFFu);
+      if (a.resident != nullptr) {
+        // A selected non-resident expert carries its unmasked score (router.py:91).
+        __syncwarp();
+        if (lane == 0) {
+          uint16_t sel[kMaxTopK];
+          uint16_t wts[kMaxTopK];
+          for (int j = 0; j < k; ++j) sel[j] = dst[v[j] & 0xFFFFu];
+          routing_softmax(sel, k, wts);
+          for (int j = 0; j < k; ++j) a.weights[row * k + j] = wts[j];
+        }
+      }
+      __syncwarp();
+    }
+
+    // ---- load-balance partials: bf16(softmax(-scores)) over eligible experts
+    const float mx = -bf16_to_f32(key16_to_bits(best[0] >> 16));  // max of -score
+    float ex[NQ];
+    float part = 0.0f;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      const int c = route_col(q, lane, vec);
+      ex[q] = 0.0f;
+      if (c < E && resident[c]) ex[q] = __expf(-bf16_to_f32(sc[q]) - mx);
+      part += ex[q];
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xFFFFFFFFu, part, off);
+    const float denom = 1.0f / part;  // reciprocal: the probabilities are rounded to BF16
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) acc[q] += round_bf16(ex[q] * denom);
+  }
+
+  // ---- CTA reduction of the per-column sums (fixed order: deterministic)
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) {
+    const int c = route_col(q, lane, vec);
+    if (c < E) lb[warp * E + c] = acc[q];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < E; c += blockDim.x) {
+    float t = 0.0f;
+    for (int w = 0; w < kRouteWarps; ++w) t += lb[w * E + c];
+    a.lb_partial[static_cast<int64_t>(blockIdx.x) * E + c] = t;
+  }
+}
+
 __global__ void __launch_bounds__(kTieWarps * 32) route_ties_kernel(const RouteArgs a) {
   extern __shared__ uint32_t tie_smem[];
   const int E = a.num_experts;
@@ -353,8 +543,41 @@ size_t route_select_smem(int E) {
          static_cast<size_t>(kRouteRows / 32) * E * 4;
 }
 
+int route_lb_blocks(int64_t tokens) {
+  if (tokens <= kRouteRowsMaxTokens) return static_cast<int>((tokens + kRouteWarps - 1) / kRouteWarps);
+  return static_cast<int>((tokens + kRouteRows - 1) / kRouteRows);
+}
+
+static size_t route_rows_smem(int E) {
+  const int half_words = (E + 1) / 2;
+  return static_cast<size_t>(kRouteWarps) * E * 4 + ((E + 3) / 4) * 4 +
+         static_cast<size_t>(kRouteWarps) * (E + 2 * half_words) * 4;
+}
+
+template <int NCH, int K1MAX>
+static int launch_route_rows_t(const RouteArgs& a, cudaStream_t stream) {
+  const void* fn = reinterpret_cast<const void*>(route_rows_kernel<NCH, K1MAX>);
+  if (ensure_max_dynamic_smem(fn) != SPX_OK) return SPX_ERR_CUDA;
+  route_rows_kernel<NCH, K1MAX><<<route_lb_blocks(a.tokens), kRouteWarps * 32, route_rows_smem(a.num_experts),
+                                  stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+template <int NCH>
+static int launch_route_rows_k(const RouteArgs& a, cudaStream_t stream) {
+  if (a.top_k + 1 <= 5) return launch_route_rows_t<NCH, 5>(a, stream);
+  if (a.top_k + 1 <= 9) return launch_route_rows_t<NCH, 9>(a, stream);
+  return launch_route_rows_t<NCH, kMaxTopK + 1>(a, stream);
+}
+
 int launch_route(const RouteArgs& a, cudaStream_t stream) {
   if (a.tokens <= 0) return SPX_OK;
+  if (a.tokens <= kRouteRowsMaxTokens) {
+    const int nch = (a.num_experts + 255) / 256;
+    if (nch <= 1) return launch_route_rows_k<1>(a, stream);
+    if (nch <= 2) return launch_route_rows_k<2>(a, stream);
+    return launch_route_rows_k<4>(a, stream);
+  }
   const int blocks = static_cast<int>((a.tokens + kRouteRows - 1) / kRouteRows);
   const size_t smem = route_select_smem(a.num_experts);
   cudaError_t err;

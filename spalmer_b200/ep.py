@@ -95,21 +95,27 @@ class CudaOps:
         self._layer_dims = layer_dims
         self.lut = softplus_table(device) if cfg.router_score_transform == "softplus" else None
         self._ws: dict[tuple, Tensor] = {}
-        self._pack()
+        self._router_packs: dict[bool, dict] = {}
+        self._expert_packs: dict[bool, dict] = {}
 
-    # ---- packing
+    # ---- packing (kernel layouts depend on the batch class of the call, so
+    # router/shared and expert copies are cached per class)
     def _local_dims(self, rows: int) -> _lib.LayerDims:
         dims = self._layer_dims(self.config, max(rows, 1), 1)
         dims.num_experts = self.e_local
         dims.shared_dim = 0
         return dims
 
-    def _pack(self) -> None:
+    def _pack_router_shared(self, tokens: int) -> dict:
+        from spalmer_b200.experts import SMALL_BATCH_TOKENS
+
+        cls = tokens <= SMALL_BATCH_TOKENS
+        if cls in self._router_packs:
+            return self._router_packs[cls]
         lib = _lib.load()
-        m = self.mixer
-        dev = self.device
+        m, dev = self.mixer, self.device
         stream = torch.cuda.current_stream(dev).cuda_stream
-        full = self._layer_dims(self.config, 1, self.k)
+        full = self._layer_dims(self.config, tokens, self.k)
         sizes = _lib.PackedSizes()
         _lib.check(lib.spx_layer_sizes(full, None, sizes), "spx_layer_sizes")
         s = m.shared
@@ -121,50 +127,65 @@ class CudaOps:
             "shared_down": None if s is None else t(s.down_projection.weight),
         }
         empty = lambda n: torch.empty(max(1, n), dtype=torch.int16, device=dev)  # noqa: E731
-        self.router_w = empty(sizes.router_weight)
-        self.shared_w1 = empty(sizes.shared_w1) if sizes.shared_w1 else None
-        self.shared_w2 = empty(sizes.shared_w2) if sizes.shared_w2 else None
+        pk = {"keep": keep, "router_w": empty(sizes.router_weight),
+              "shared_w1": empty(sizes.shared_w1) if sizes.shared_w1 else None,
+              "shared_w2": empty(sizes.shared_w2) if sizes.shared_w2 else None}
         src = _lib.ReferenceWeights(router_weight=_lib.ptr(keep["router_weight"]), router_bias=_lib.ptr(keep["router_bias"]),
                                     shared_gate=_lib.ptr(keep["shared_gate"]), shared_up=_lib.ptr(keep["shared_up"]),
                                     shared_down=_lib.ptr(keep["shared_down"]))
-        _lib.check(lib.spx_pack_weights(full, src, self.router_w.data_ptr(), None, None, _lib.ptr(self.shared_w1),
-                                        _lib.ptr(self.shared_w2), stream), "spx_pack_weights (router/shared)")
-        # this rank's experts
+        _lib.check(lib.spx_pack_weights(full, src, pk["router_w"].data_ptr(), None, None, _lib.ptr(pk["shared_w1"]),
+                                        _lib.ptr(pk["shared_w2"]), stream), "spx_pack_weights (router/shared)")
+        self._router_packs[cls] = pk
+        return pk
+
+    def _pack_experts(self, rows: int) -> dict:
+        from spalmer_b200.experts import SMALL_BATCH_TOKENS
+
+        cls = rows <= SMALL_BATCH_TOKENS
+        if cls in self._expert_packs:
+            return self._expert_packs[cls]
+        lib = _lib.load()
+        m, dev = self.mixer, self.device
+        stream = torch.cuda.current_stream(dev).cuda_stream
         sl = slice(self.e0, self.e0 + self.e_local)
         gate = m.experts.gate_proj.detach()[sl].contiguous()
         up = m.experts.up_proj.detach()[sl].contiguous()
         down = m.experts.down_proj.detach()[sl].contiguous()
-        local = self._local_dims(1)
+        local = self._local_dims(rows)
         lsizes = _lib.PackedSizes()
         _lib.check(lib.spx_layer_sizes(local, None, lsizes), "spx_layer_sizes")
-        self.w1 = empty(lsizes.expert_w1)
-        self.w2 = empty(lsizes.expert_w2)
+        empty = lambda n: torch.empty(max(1, n), dtype=torch.int16, device=dev)  # noqa: E731
+        pk = {"w1": empty(lsizes.expert_w1), "w2": empty(lsizes.expert_w2), "mx": {}}
         dummy_router = torch.zeros(self.e_local, self.d, dtype=torch.bfloat16, device=dev)
         esrc = _lib.ReferenceWeights(router_weight=dummy_router.data_ptr(), gate_proj=gate.data_ptr(),
                                      up_proj=up.data_ptr(), down_proj=down.data_ptr())
         scratch_router = empty(lsizes.router_weight)
-        _lib.check(lib.spx_pack_weights(local, esrc, scratch_router.data_ptr(), self.w1.data_ptr(),
-                                        self.w2.data_ptr(), None, None, stream), "spx_pack_weights (experts)")
-        self.mx = {}
+        _lib.check(lib.spx_pack_weights(local, esrc, scratch_router.data_ptr(), pk["w1"].data_ptr(),
+                                        pk["w2"].data_ptr(), None, None, stream), "spx_pack_weights (experts)")
         if local.mxfp8_lane:
-            for name in ("expert_w1_mx", "expert_w1_mx_scales", "expert_w2_mx", "expert_w2_mx_scales"):
-                self.mx[name] = torch.empty(max(16, getattr(lsizes, name)), dtype=torch.uint8, device=dev)
-            _lib.check(lib.spx_pack_weights_mxfp8(local, esrc, *(self.mx[n].data_ptr() for n in (
-                "expert_w1_mx", "expert_w1_mx_scales", "expert_w2_mx", "expert_w2_mx_scales")), stream),
-                "spx_pack_weights_mxfp8")
-        self._keep = (keep, gate, up, down, dummy_router, scratch_router)
+            names = ("expert_w1_mx", "expert_w1_mx_scales", "expert_w2_mx", "expert_w2_mx_scales")
+            for name in names:
+                pk["mx"][name] = torch.empty(max(16, getattr(lsizes, name)), dtype=torch.uint8, device=dev)
+            _lib.check(lib.spx_pack_weights_mxfp8(local, esrc, *(pk["mx"][n].data_ptr() for n in names), stream),
+                       "spx_pack_weights_mxfp8")
+        pk["keep"] = (gate, up, down, dummy_router, scratch_router)
+        self._expert_packs[cls] = pk
+        return pk
 
-    def _weights(self, lanes: Tensor | None = None) -> _lib.PackedWeights:
+    def _weights(self, tokens: int, rows: int, lanes: Tensor | None = None) -> _lib.PackedWeights:
+        rs = self._pack_router_shared(tokens)
+        ex = self._pack_experts(rows)
+        mx = ex["mx"]
         return _lib.PackedWeights(
-            router_weight=self.router_w.data_ptr(), router_bias=_lib.ptr(self._keep[0]["router_bias"]),
-            expert_w1=self.w1.data_ptr(), expert_w2=self.w2.data_ptr(),
-            shared_w1=_lib.ptr(self.shared_w1), shared_w2=_lib.ptr(self.shared_w2),
+            router_weight=rs["router_w"].data_ptr(), router_bias=_lib.ptr(rs["keep"]["router_bias"]),
+            expert_w1=ex["w1"].data_ptr(), expert_w2=ex["w2"].data_ptr(),
+            shared_w1=_lib.ptr(rs["shared_w1"]), shared_w2=_lib.ptr(rs["shared_w2"]),
             softplus_table=_lib.ptr(self.lut), resident_mask=None,
             expert_lane_mxfp8=_lib.ptr(lanes),
-            expert_w1_mx=_lib.ptr(self.mx.get("expert_w1_mx")),
-            expert_w1_mx_scales=_lib.ptr(self.mx.get("expert_w1_mx_scales")),
-            expert_w2_mx=_lib.ptr(self.mx.get("expert_w2_mx")),
-            expert_w2_mx_scales=_lib.ptr(self.mx.get("expert_w2_mx_scales")),
+            expert_w1_mx=_lib.ptr(mx.get("expert_w1_mx")),
+            expert_w1_mx_scales=_lib.ptr(mx.get("expert_w1_mx_scales")),
+            expert_w2_mx=_lib.ptr(mx.get("expert_w2_mx")),
+            expert_w2_mx_scales=_lib.ptr(mx.get("expert_w2_mx_scales")),
         )
 
     def _workspace(self, dims: _lib.LayerDims, tag: str) -> Tensor:
@@ -205,7 +226,7 @@ class CudaOps:
             pair_rank=r["rank"].data_ptr(),
         )
         stream = torch.cuda.current_stream(dev).cuda_stream
-        _lib.check(lib.spx_layer_route(dims, self._weights(), x.data_ptr(), outs, ws.data_ptr(), stream),
+        _lib.check(lib.spx_layer_route(dims, self._weights(T, 1), x.data_ptr(), outs, ws.data_ptr(), stream),
                    "spx_layer_route")
         return r
 
@@ -226,7 +247,7 @@ class CudaOps:
         dims = self._local_dims(R)
         ws = self._workspace(dims, "experts")
         stream = torch.cuda.current_stream(rows.device).cuda_stream
-        _lib.check(lib.spx_experts_forward(dims, self._weights(lanes), rows.data_ptr(), row_expert.data_ptr(),
+        _lib.check(lib.spx_experts_forward(dims, self._weights(R, R, lanes), rows.data_ptr(), row_expert.data_ptr(),
                                            out.data_ptr(), ws.data_ptr(), stream), "spx_experts_forward")
         return out
 
@@ -238,7 +259,8 @@ class CudaOps:
         ws = self._workspace(dims, "shared")
         out = torch.empty_like(x)
         stream = torch.cuda.current_stream(x.device).cuda_stream
-        _lib.check(lib.spx_shared_forward(dims, self._weights(), x.data_ptr(), out.data_ptr(), ws.data_ptr(), stream),
+        _lib.check(lib.spx_shared_forward(dims, self._weights(x.shape[0], 1), x.data_ptr(), out.data_ptr(),
+                                          ws.data_ptr(), stream),
                    "spx_shared_forward")
         return out
 

@@ -232,6 +232,10 @@ def softplus_table(device: torch.device) -> Tensor:
     return table
 
 
+# Batches of at most this many tokens use the decode tile shapes (kSmallBatchTokens in libspx).
+SMALL_BATCH_TOKENS = 256
+
+
 def layer_dims(config: MicroExpertsConfig, tokens: int, top_k: int) -> _lib.LayerDims:
     return _lib.LayerDims(
         tokens=tokens,
@@ -315,7 +319,7 @@ class B200MicroExpertChannelMixer(nn.Module):
             raise ValueError("residency configuration does not match this bank")
         object.__setattr__(self, "_potentiation_controller_ref", ref(potentiation_controller))
         object.__setattr__(self, "_residency_ref", ref(residency))
-        object.__setattr__(self, "_pack_cache", None)
+        object.__setattr__(self, "_pack_cache", {})
         object.__setattr__(self, "_lane_cache", None)
         object.__setattr__(self, "_ws_cache", {})
         object.__setattr__(self, "_stage_event_array", None)
@@ -386,11 +390,15 @@ class B200MicroExpertChannelMixer(nn.Module):
         }
 
     def _packed(self, device: torch.device, tokens: int, top_k: int) -> dict[str, Tensor | None]:
+        """Kernel layouts of the weights, one cache entry per batch class
+        (decode-sized batches of <= 256 tokens use narrower GEMM1 chunks)."""
+
         tensors = self._weight_tensors()
         key = (device,) + tuple(
             (None if t is None else (t.data_ptr(), t._version, t.dtype)) for t in tensors.values()
         )
-        cache = self._pack_cache
+        batch_class = tokens <= SMALL_BATCH_TOKENS
+        cache = self._pack_cache.get(batch_class)
         if cache is not None and cache[0] == key:
             return cache[1]
         for name, t in tensors.items():
@@ -440,7 +448,7 @@ class B200MicroExpertChannelMixer(nn.Module):
                 "spx_pack_weights_mxfp8",
             )
         packed["_keepalive"] = bits
-        object.__setattr__(self, "_pack_cache", (key, packed))
+        self._pack_cache[batch_class] = (key, packed)
         return packed
 
     def _lanes(self, device: torch.device) -> Tensor | None:

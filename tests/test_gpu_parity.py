@@ -58,15 +58,20 @@ def test_route_from_reference_logits_is_bit_exact(name):
     assert np.array_equal(bf16_bits(weights), arrays["routing_weights"])
 
 
+@pytest.mark.parametrize("tiled", [False, True], ids=["rows_kernel", "select_ties_kernels"])
 @pytest.mark.parametrize("case", TOPK_CASES, ids=[c["name"] for c in TOPK_CASES])
-def test_route_tie_order_matches_reference_topk(case, golden_topk):
+def test_route_tie_order_matches_reference_topk(case, golden_topk, tiled):
+    """Small batches take the warp-per-row route kernel; batches above 4096
+    rows (the fixture tiled) take route_select + route_ties."""
+
     scores_bits, mask = generate_scores(case)
-    logits = from_bits(scores_bits, DEV)  # identity transform: logits are the scores
+    reps = -(-4097 // scores_bits.shape[0]) if tiled else 1
+    logits = from_bits(np.tile(scores_bits, (reps, 1)), DEV)  # identity transform: logits are the scores
     for k in case["ks"]:
         _, ids, _ = route(logits, k, transform="identity",
                           resident_mask=None if mask is None else torch.from_numpy(mask))
         got = ids.cpu().numpy()
-        want = golden_topk[f"{case['name']}__k{k}"].astype(np.int64)
+        want = np.tile(golden_topk[f"{case['name']}__k{k}"].astype(np.int64), (reps, 1))
         rows = np.nonzero((got != want).any(axis=1))[0]
         assert rows.size == 0, f"k={k}: {rows.size} rows differ, first {rows[:5]}"
 
