@@ -31,7 +31,8 @@ struct Shape {
   int c, nc, kp;      // expert GEMM1 chunk, chunks, hidden width padded to 64
   int cs, ncs, ksp;   // shared GEMM1 chunk, chunks, hidden width padded to 64
   int bn_router, gn_router;
-  int bn_d, gn_d;
+  int bn_d, gn_d;     // expert down projection N tile
+  int bn_sd, gn_sd;   // shared down projection N tile
   int lb_blocks, nchunks, max_tiles;
   // MXFP8 lane
   bool mx;
@@ -54,12 +55,13 @@ int make_shape(const spx_layer_dims* dm, Shape* s) {
   if (s->T * s->k > (int64_t(1) << 31) - 1) return SPX_ERR_UNSUPPORTED;
   s->P = s->T * s->k;
   s->kd = round_up_i(s->d, 64);
-  // Decode-sized batches (few rows per expert) read weights far more than they
-  // compute: narrow N tiles spread each weight matrix over more CTAs.  The
-  // packed GEMM1 layouts follow the chunk width, so they depend on this class.
+  // Decode-sized batches read weights far more than they compute: the router
+  // and shared GEMMs (one M tile) take narrow N tiles so each weight matrix
+  // spreads over more CTAs.  The packed shared GEMM1 layout follows its chunk
+  // width, so it depends on this class.
   const bool small = s->T <= kSmallBatchTokens;
   const int wide = small ? 32 : 128;
-  s->c = std::min(round_up_i(s->I, 16), wide);
+  s->c = std::min(round_up_i(s->I, 16), 128);
   s->nc = ceil_div(s->I, s->c);
   s->kp = round_up_i(s->nc * s->c, 64);
   if (s->S > 0) {
@@ -71,8 +73,10 @@ int make_shape(const spx_layer_dims* dm, Shape* s) {
   }
   s->bn_router = std::min(small ? 32 : 256, round_up_i(s->E, 16));
   s->gn_router = ceil_div(s->E, s->bn_router);
-  s->bn_d = std::min(small ? 64 : 256, round_up_i(s->d, 16));
+  s->bn_d = std::min(256, round_up_i(s->d, 16));
   s->gn_d = ceil_div(s->d, s->bn_d);
+  s->bn_sd = std::min(small ? 64 : 256, round_up_i(s->d, 16));
+  s->gn_sd = ceil_div(s->d, s->bn_sd);
   s->lb_blocks = route_lb_blocks(s->T);
   s->nchunks = ceil_div(s->P, kDispatchChunk);
   s->max_tiles = ceil_div(s->P, kTileRows) + s->E;
@@ -80,10 +84,10 @@ int make_shape(const spx_layer_dims* dm, Shape* s) {
   if (s->mx) {
     if (s->I % kMxBlock != 0) return SPX_ERR_UNSUPPORTED;
     s->kx = round_up_i(s->d, 128);
-    s->cm = small ? 32 : (s->I % 128 == 0) ? 128 : (s->I % 64 == 0) ? 64 : 32;
+    s->cm = (s->I % 128 == 0) ? 128 : (s->I % 64 == 0) ? 64 : 32;
     s->ncm = s->I / s->cm;
     s->kh = round_up_i(s->I, 128);
-    s->bn2m = std::min(small ? 64 : kMxDenseBn, round_up_i(s->d, 16));
+    s->bn2m = std::min(kMxDenseBn, round_up_i(s->d, 16));
     s->gn2m = ceil_div(s->d, s->bn2m);
   } else {
     s->kx = s->cm = s->ncm = s->kh = s->bn2m = s->gn2m = 0;
@@ -108,7 +112,7 @@ MxPackSizes mx_pack_sizes(const Shape& s) {
 }
 
 struct Layout {
-  size_t small, tie_rows, lb_partial, chunk_hist, counts, starts, tiles, order, src_row, rank, sorted_w;
+  size_t small, tie_rows, lb_partial, lb_sum, chunk_hist, counts, starts, tiles, order, src_row, rank, sorted_w;
   size_t hidden, y, shared_hidden, shared_out, logits, x_pad, util, stats, ratios, aux;
   size_t x_q, x_sf, h_q, h_sf, tiles_mx;  // MXFP8 lane (empty otherwise)
   size_t total;
@@ -125,6 +129,7 @@ Layout make_layout(const Shape& s) {
   L.small = take(64);
   L.tie_rows = take(sizeof(int) * s.T);
   L.lb_partial = take(sizeof(float) * static_cast<size_t>(s.lb_blocks) * s.E);
+  L.lb_sum = take(sizeof(float) * s.E);
   L.chunk_hist = take(sizeof(int) * static_cast<size_t>(s.nchunks) * s.E);
   L.counts = take(sizeof(int) * s.E);
   L.starts = take(sizeof(int) * s.E);
@@ -212,6 +217,7 @@ DispatchArgs dispatch_args(const Shape& s, const int64_t* ids, int* order, int* 
   a.src_row = at<int>(ws, L.src_row);
   a.rank = at<int>(ws, L.rank);
   a.lb_partial = at<float>(ws, L.lb_partial);
+  a.lb_sum = at<float>(ws, L.lb_sum);
   a.lb_blocks = s.lb_blocks;
   a.eligible_experts = s.E;
   a.status = at<int>(ws, L.small);
@@ -401,14 +407,14 @@ int stage_shared(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, 
     if ((rc = launch_gemm(kEpiSwiglu, g, ceil_div(s.T, kTileRows), s.ncs, c.st)) != SPX_OK) return rc;
   }
   c.mark(6);
-  GemmArgs g = base_args(kEpiStore, s.bn_d, s.ksp / 64, c.status);
+  GemmArgs g = base_args(kEpiStore, s.bn_sd, s.ksp / 64, c.status);
   if ((rc = encode_2d(&g.tma_a, hs, s.T, s.ksp, s.ksp, kTileRows)) != SPX_OK) return rc;
-  if ((rc = encode_3d(&g.tma_b, w->shared_w2, 1, s.d, s.ksp, s.bn_d)) != SPX_OK) return rc;
+  if ((rc = encode_3d(&g.tma_b, w->shared_w2, 1, s.d, s.ksp, s.bn_sd)) != SPX_OK) return rc;
   g.m_rows = static_cast<int>(s.T);
   g.n_valid = s.d;
   g.out = shared_out;
   g.ldo = s.d;
-  return launch_gemm(kEpiStore, g, ceil_div(s.T, kTileRows), s.gn_d, c.st);
+  return launch_gemm(kEpiStore, g, ceil_div(s.T, kTileRows), s.gn_sd, c.st);
 }
 
 int check_layer_weights(const Shape& s, const spx_layer_dims* dims, const spx_packed_weights* w, bool router,

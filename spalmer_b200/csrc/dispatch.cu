@@ -11,8 +11,9 @@
 // (mixer.py:193-197).  The permutation equals argsort(stable=True): pairs of
 // one expert keep increasing p.
 //   dispatch_count_kernel   per-chunk expert histograms (chunk = 2048 pairs)
-//   dispatch_scan_kernel    one CTA: chunk offsets, counts, starts, tile table,
-//                           utilization, group statistics, auxiliary loss
+//   dispatch_prefix_kernel  per expert: chunk offsets and totals; load-balance sums
+//   dispatch_scan_kernel    one CTA: starts, tile tables, utilization, group
+//                           statistics, auxiliary loss
 //   dispatch_scatter_kernel per-chunk stable placement (warp match_any ranks)
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -51,22 +52,20 @@ __device__ __forceinline__ int64_t next_pow2_i64(int64_t n) {
   return c;
 }
 
-__global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs a) {
-  __shared__ int s_scan[1024];
-  __shared__ unsigned long long s_scan64[1024];
-  __shared__ float s_red[1024];
-  __shared__ long long s_i64[4];
-  __shared__ int s_count[1024];
+// Parallel prefix work ahead of the single-CTA scan (it was the scan's
+// critical path when done by 32 warps serially):
+//   blocks [0, E)        one expert each: exclusive scan of its per-chunk counts
+//                        in place (chunk offsets within the expert) and its total
+//                        into counts[e];
+//   blocks [E, E + E/32) the load-balance sums: 32 experts per block, the route
+//                        partial rows summed in a fixed order into lb_sum[e].
+__global__ void __launch_bounds__(256) dispatch_prefix_kernel(const DispatchArgs a) {
   const int E = a.num_experts;
   const int nchunks = static_cast<int>((a.pairs + kDispatchChunk - 1) / kDispatchChunk);
-  const int e = threadIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  // Exclusive scan over chunks for each expert (chunk offsets within the
-  // expert), one warp per expert: each lane owns a contiguous run of chunks.
-  // Lanes take 16 consecutive chunks per pass; all 16 loads are issued before
-  // any is used (this kernel is latency bound, not bandwidth bound).
-  for (int x = warp; x < E; x += 32) {
+  if (static_cast<int>(blockIdx.x) < E) {
+    if (warp != 0) return;
+    const int x = blockIdx.x;
     int* row = a.chunk_hist + static_cast<int64_t>(x) * nchunks;
     int carry = 0;
     for (int base = 0; base < nchunks; base += 32 * 16) {
@@ -92,8 +91,47 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs 
       }
       carry += __shfl_sync(0xFFFFFFFFu, incl, 31);
     }
-    if (lane == 0) s_count[x] = carry;
+    if (lane == 0) a.counts[x] = carry;
+    return;
   }
+  // load-balance sums: lane -> expert, warp -> every 8th partial row, then the
+  // 8 warps folded in order (deterministic)
+  __shared__ float part[8][32];
+  const int x = (blockIdx.x - E) * 32 + lane;
+  float acc = 0.0f;
+  if (x < E) {
+    for (int b0 = warp; b0 < a.lb_blocks; b0 += 8 * 8) {
+      float v[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int b = b0 + q * 8;
+        v[q] = b < a.lb_blocks ? a.lb_partial[static_cast<int64_t>(b) * E + x] : 0.0f;
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc += v[q];
+    }
+  }
+  part[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && x < E) {
+    float t = 0.0f;
+    for (int w = 0; w < 8; ++w) t += part[w][lane];
+    a.lb_sum[x] = t;
+  }
+}
+
+__global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs a) {
+  __shared__ int s_scan[1024];
+  __shared__ unsigned long long s_scan64[1024];
+  __shared__ float s_red[1024];
+  __shared__ long long s_i64[4];
+  __shared__ int s_count[1024];
+  const int E = a.num_experts;
+  const int e = threadIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // Chunk offsets and per-expert totals come from dispatch_prefix_kernel.
+  if (e < E) s_count[e] = a.counts[e];
   __syncthreads();
   const int count = (e < E) ? s_count[e] : 0;
   // Block-wide exclusive scans: pair starts and tile starts.
@@ -194,28 +232,10 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs 
   // mean_p = bf16(sum_t p / T), frac = bf16(util), prod = bf16(frac*mean_p),
   // total = bf16(sum prod), loss = bf16(bf16(eligible) * total).
   if (a.aux_loss != nullptr && a.lb_blocks > 0) {
-    // Sum of the route blocks' probability partials per expert: one warp per
-    // expert, fixed lane striding and a fixed shuffle tree (deterministic).
-    for (int x = warp; x < E; x += 32) {
-      float part = 0.0f;
-      for (int b0 = 0; b0 < a.lb_blocks; b0 += 32 * 8) {
-        float v[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int b = b0 + q * 32 + lane;
-          v[q] = b < a.lb_blocks ? a.lb_partial[static_cast<int64_t>(b) * E + x] : 0.0f;
-        }
-#pragma unroll
-        for (int q = 0; q < 8; ++q) part += v[q];
-      }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xFFFFFFFFu, part, off);
-      if (lane == 0) s_red[x] = part;
-    }
-    __syncthreads();
+    // Per-expert sums of the route blocks' probability partials (dispatch_prefix_kernel).
     float prod = 0.0f;
     if (e < E) {
-      const float s = s_red[e];
+      const float s = a.lb_sum[e];
       const float mean_p = round_bf16(s / static_cast<float>(a.tokens));
       prod = round_bf16(round_bf16(util) * mean_p);
     }
@@ -288,6 +308,11 @@ int launch_dispatch(const DispatchArgs& a, cudaStream_t stream) {
   if (a.num_experts > 1024) return SPX_ERR_UNSUPPORTED;
   const int nchunks = static_cast<int>((a.pairs + kDispatchChunk - 1) / kDispatchChunk);
   dispatch_count_kernel<<<nchunks, kDispatchThreads, a.num_experts * sizeof(int), stream>>>(a);
+  if (cudaGetLastError() != cudaSuccess) return SPX_ERR_CUDA;
+  const bool lb = a.aux_loss != nullptr && a.lb_blocks > 0;
+  if (lb && a.lb_sum == nullptr) return SPX_ERR_INVALID_ARG;
+  const int prefix_blocks = a.num_experts + (lb ? (a.num_experts + 31) / 32 : 0);
+  dispatch_prefix_kernel<<<prefix_blocks, 256, 0, stream>>>(a);
   if (cudaGetLastError() != cudaSuccess) return SPX_ERR_CUDA;
   dispatch_scan_kernel<<<1, 1024, 0, stream>>>(a);
   if (cudaGetLastError() != cudaSuccess) return SPX_ERR_CUDA;

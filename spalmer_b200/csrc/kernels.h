@@ -88,6 +88,7 @@ struct DispatchArgs {
   uint16_t* aux_loss;        // [1] bf16
   const float* lb_partial;   // [lb_blocks, E]
   int lb_blocks;
+  float* lb_sum;             // [E] workspace: lb_partial summed over blocks (needed with aux_loss)
   int eligible_experts;        // used when resident == null
   const uint8_t* resident;   // [E] resident mask or null
   int execution_loop;        // 1: reference expert_execution == "loop" telemetry
