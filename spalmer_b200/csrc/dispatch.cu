@@ -59,7 +59,9 @@ __device__ __forceinline__ int64_t next_pow2_i64(int64_t n) {
 //                        into counts[e];
 //   blocks [E, E + E/32) the load-balance sums: 32 experts per block, the route
 //                        partial rows summed in a fixed order into lb_sum[e].
-__global__ void __launch_bounds__(256) dispatch_prefix_kernel(const DispatchArgs a) {
+constexpr int kPrefixWarps = 32;
+
+__global__ void __launch_bounds__(kPrefixWarps * 32) dispatch_prefix_kernel(const DispatchArgs a) {
   const int E = a.num_experts;
   const int nchunks = static_cast<int>((a.pairs + kDispatchChunk - 1) / kDispatchChunk);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -94,17 +96,17 @@ __global__ void __launch_bounds__(256) dispatch_prefix_kernel(const DispatchArgs
     if (lane == 0) a.counts[x] = carry;
     return;
   }
-  // load-balance sums: lane -> expert, warp -> every 8th partial row, then the
-  // 8 warps folded in order (deterministic)
-  __shared__ float part[8][32];
+  // load-balance sums: lane -> expert, warp -> every 32nd partial row, then the
+  // warps folded in order (deterministic)
+  __shared__ float part[kPrefixWarps][32];
   const int x = (blockIdx.x - E) * 32 + lane;
   float acc = 0.0f;
   if (x < E) {
-    for (int b0 = warp; b0 < a.lb_blocks; b0 += 8 * 8) {
+    for (int b0 = warp; b0 < a.lb_blocks; b0 += kPrefixWarps * 8) {
       float v[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        const int b = b0 + q * 8;
+        const int b = b0 + q * kPrefixWarps;
         v[q] = b < a.lb_blocks ? a.lb_partial[static_cast<int64_t>(b) * E + x] : 0.0f;
       }
 #pragma unroll
@@ -115,7 +117,7 @@ __global__ void __launch_bounds__(256) dispatch_prefix_kernel(const DispatchArgs
   __syncthreads();
   if (warp == 0 && x < E) {
     float t = 0.0f;
-    for (int w = 0; w < 8; ++w) t += part[w][lane];
+    for (int w = 0; w < kPrefixWarps; ++w) t += part[w][lane];
     a.lb_sum[x] = t;
   }
 }
@@ -312,7 +314,7 @@ int launch_dispatch(const DispatchArgs& a, cudaStream_t stream) {
   const bool lb = a.aux_loss != nullptr && a.lb_blocks > 0;
   if (lb && a.lb_sum == nullptr) return SPX_ERR_INVALID_ARG;
   const int prefix_blocks = a.num_experts + (lb ? (a.num_experts + 31) / 32 : 0);
-  dispatch_prefix_kernel<<<prefix_blocks, 256, 0, stream>>>(a);
+  dispatch_prefix_kernel<<<prefix_blocks, kPrefixWarps * 32, 0, stream>>>(a);
   if (cudaGetLastError() != cudaSuccess) return SPX_ERR_CUDA;
   dispatch_scan_kernel<<<1, 1024, 0, stream>>>(a);
   if (cudaGetLastError() != cudaSuccess) return SPX_ERR_CUDA;

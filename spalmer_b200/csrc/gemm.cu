@@ -96,7 +96,6 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
   const int r = quad * 32 + lane;                   // tile row owned by this thread (its TMEM lane)
   const bool live = r < rows;
   const int wrows = rows - quad * 32;               // valid rows of this quadrant (may be <= 0)
-  if (wrows <= 0) return;                           // nothing of this quadrant is stored
   uint16_t* out = static_cast<uint16_t*>(a.out);
   const int out_cols = (EPI == kEpiSwiglu) ? a.chunk : a.bn;
   const int col_base = (EPI == kEpiSwiglu) ? nt * a.chunk : n0;
@@ -378,14 +377,13 @@ __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa,
         break;
       }
       if (gather) {
-        // Rows past the tile's end are not copied: their accumulator rows are never stored.
         const uint32_t dst0 = smem_u32(sa + s * a_bytes);
         const uint8_t* col = a.a_base + kb * 128 + chunk * 16;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int rr = 4 * i + (lane >> 3);
           const uint32_t dst = dst0 + (rr >> 3) * 1024 + (rr & 7) * 128 + ((chunk ^ (rr & 7)) << 4);
-          if (rr < rows) cp_async16(dst, col + static_cast<int64_t>(src[i]) * a.lda);
+          cp_async16(dst, col + static_cast<int64_t>(src[i]) * a.lda);
         }
       }
       if constexpr (MX) {

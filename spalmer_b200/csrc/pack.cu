@@ -78,12 +78,13 @@ __global__ void pad_rows_kernel(const uint16_t* __restrict__ src, int64_t rows, 
 // consecutive threads take consecutive 16-byte chunks of one token, so every
 // slot's row is read in whole 128-byte lines, and a thread issues all k row
 // loads before it adds any.
-__device__ __forceinline__ void add_row8(float (&acc)[8], const uint4& v, float w, bool weighted) {
+template <bool WEIGHTED>
+__device__ __forceinline__ void add_row8(float (&acc)[8], const uint4& v, float w) {
   const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     float lo = __uint_as_float(u[q] << 16), hi = __uint_as_float(u[q] & 0xFFFF0000u);
-    if (weighted) {
+    if constexpr (WEIGHTED) {
       lo = round_bf16(lo * w);
       hi = round_bf16(hi * w);
     }
@@ -92,33 +93,32 @@ __device__ __forceinline__ void add_row8(float (&acc)[8], const uint4& v, float 
   }
 }
 
-template <int KMAX>
+template <int KMAX, bool WEIGHTED>
 __global__ void combine_kernel(const uint16_t* __restrict__ y, const int* __restrict__ rank,
                                const uint16_t* __restrict__ weights, const uint16_t* __restrict__ base,
                                int64_t tokens, int d, int k, uint16_t* __restrict__ out) {
   const int vec = d / 8;
   const int64_t total = tokens * vec;
-  const bool weighted = weights != nullptr;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t t = idx / vec;
     const int c = static_cast<int>(idx - t * vec) * 8;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (base != nullptr) add_row8(acc, __ldg(reinterpret_cast<const uint4*>(base + t * d + c)), 1.0f, false);
+    if (base != nullptr) add_row8<false>(acc, __ldg(reinterpret_cast<const uint4*>(base + t * d + c)), 1.0f);
     int r[KMAX];
-    float w[KMAX];
 #pragma unroll
-    for (int j = 0; j < KMAX; ++j) {
-      r[j] = j < k ? __ldg(rank + t * k + j) : 0;
-      w[j] = (weighted && j < k) ? bf16_to_f32(__ldg(weights + t * k + j)) : 1.0f;
-    }
+    for (int j = 0; j < KMAX; ++j) r[j] = j < k ? __ldg(rank + t * k + j) : 0;
     uint4 v[KMAX];
 #pragma unroll
     for (int j = 0; j < KMAX; ++j)
       if (j < k) v[j] = __ldg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(r[j]) * d + c));
 #pragma unroll
-    for (int j = 0; j < KMAX; ++j)
-      if (j < k) add_row8(acc, v[j], w[j], weighted);
+    for (int j = 0; j < KMAX; ++j) {
+      if (j < k) {
+        const float w = WEIGHTED ? bf16_to_f32(__ldg(weights + t * k + j)) : 1.0f;
+        add_row8<WEIGHTED>(acc, v[j], w);
+      }
+    }
     uint4 o;
     uint16_t* oh = reinterpret_cast<uint16_t*>(&o);
 #pragma unroll
@@ -199,10 +199,14 @@ int launch_combine(const uint16_t* y, const int* rank, const uint16_t* weights, 
     int64_t g = (total + 255) / 256;
     if (g > 148 * 64) g = 148 * 64;
     const int grid = static_cast<int>(g < 1 ? 1 : g);
-    if (k <= 8)
-      combine_kernel<8><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out);
+    if (weights == nullptr && k <= 8)
+      combine_kernel<8, false><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out);
+    else if (weights == nullptr)
+      combine_kernel<kMaxTopK, false><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out);
+    else if (k <= 8)
+      combine_kernel<8, true><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out);
     else
-      combine_kernel<kMaxTopK><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out);
+      combine_kernel<kMaxTopK, true><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out);
   } else {
     combine_scalar_kernel<<<grid_for(tokens * d), 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out);
   }
