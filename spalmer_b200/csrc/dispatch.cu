@@ -15,6 +15,7 @@
 //   dispatch_scan_kernel    one CTA: starts, tile tables, utilization, group
 //                           statistics, auxiliary loss
 //   dispatch_scatter_kernel per-chunk stable placement (warp match_any ranks)
+//   dispatch_small_kernel   all of the above in one CTA for <= 4096 pairs
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -122,20 +123,27 @@ __global__ void __launch_bounds__(kPrefixWarps * 32) dispatch_prefix_kernel(cons
   }
 }
 
-__global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs a) {
-  __shared__ int s_scan[1024];
-  __shared__ unsigned long long s_scan64[1024];
-  __shared__ float s_red[1024];
-  __shared__ long long s_i64[4];
-  __shared__ int s_count[1024];
+// Shared by the scan kernels: from each expert's pair count (thread e holds
+// expert e's), the pair starts, both lanes' tile tables, utilization, group
+// statistics and the auxiliary loss (lb_e = expert e's load-balance sum).
+// One CTA of 1024 threads; E <= 1024.
+struct ScanShared {
+  int scan[1024];
+  unsigned long long scan64[1024];
+  float red[1024];
+  long long i64[4];
+  int count[1024];
+};
+
+__device__ __forceinline__ void finish_dispatch(const DispatchArgs& a, int count, float lb_e, ScanShared& sh) {
+  int* s_scan = sh.scan;
+  unsigned long long* s_scan64 = sh.scan64;
+  float* s_red = sh.red;
+  long long* s_i64 = sh.i64;
+  int* s_count = sh.count;
   const int E = a.num_experts;
   const int e = threadIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  // Chunk offsets and per-expert totals come from dispatch_prefix_kernel.
-  if (e < E) s_count[e] = a.counts[e];
-  __syncthreads();
-  const int count = (e < E) ? s_count[e] : 0;
   // Block-wide exclusive scans: pair starts and tile starts.
   const int tiles = (count + kTileRows - 1) / kTileRows;
   s_scan[threadIdx.x] = (e < E) ? count : 0;
@@ -237,7 +245,7 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs 
     // Per-expert sums of the route blocks' probability partials (dispatch_prefix_kernel).
     float prod = 0.0f;
     if (e < E) {
-      const float s = a.lb_sum[e];
+      const float s = lb_e;
       const float mean_p = round_bf16(s / static_cast<float>(a.tokens));
       prod = round_bf16(round_bf16(util) * mean_p);
     }
@@ -253,6 +261,70 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs 
       const float eligible = round_bf16(static_cast<float>(n_eligible));
       a.aux_loss[0] = f32_to_bf16_rne(eligible * total);
     }
+  }
+}
+
+__global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs a) {
+  __shared__ ScanShared sh;
+  const int E = a.num_experts;
+  const int e = threadIdx.x;
+  // Chunk offsets, per-expert totals and load-balance sums come from dispatch_prefix_kernel.
+  const int count = (e < E) ? a.counts[e] : 0;
+  const float lb_e = (e < E && a.aux_loss != nullptr && a.lb_blocks > 0) ? a.lb_sum[e] : 0.0f;
+  finish_dispatch(a, count, lb_e, sh);
+}
+
+// Small batches (pairs <= kDispatchSmallPairs): the whole dispatch in one CTA
+// -- counts, the scan work above, then stable placement by warp 0, 32 pairs
+// at a time in pair order (match_any ranks within the 32).
+__global__ void __launch_bounds__(1024) dispatch_small_kernel(const DispatchArgs a) {
+  __shared__ ScanShared sh;
+  __shared__ int s_base[1024];
+  __shared__ short s_ids[kDispatchSmallPairs];
+  const int E = a.num_experts;
+  const int e = threadIdx.x;
+  const int P = static_cast<int>(a.pairs);
+  if (e < 1024) s_base[e] = 0;
+  __syncthreads();
+  for (int p = threadIdx.x; p < P; p += blockDim.x) {
+    const int64_t x = a.ids[p];
+    const bool ok = x >= 0 && x < E;
+    if (!ok) record_error(a.status, SPX_DEV_BAD_EXPERT);
+    s_ids[p] = ok ? static_cast<short>(x) : static_cast<short>(-1);
+    if (ok) atomicAdd(&s_base[x], 1);
+  }
+  __syncthreads();
+  const int count = (e < E) ? s_base[e] : 0;
+  float lb_e = 0.0f;
+  if (e < E && a.aux_loss != nullptr && a.lb_blocks > 0) {
+#pragma unroll 8
+    for (int b = 0; b < a.lb_blocks; ++b) lb_e += a.lb_partial[static_cast<int64_t>(b) * E + e];
+  }
+  __syncthreads();
+  finish_dispatch(a, count, lb_e, sh);
+  __syncthreads();
+  if (e < E) s_base[e] = a.starts[e];
+  __syncthreads();
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int g = 0; g < P; g += 32) {
+    const int p = g + lane;
+    const int x = p < P ? s_ids[p] : -1;
+    const bool ok = x >= 0;
+    const unsigned peers = __match_any_sync(0xFFFFFFFFu, x);
+    int base = 0;
+    if (ok) base = s_base[x];
+    __syncwarp();
+    if (ok) {
+      const int pos = base + __popc(peers & lt_mask);
+      a.order[pos] = p;
+      a.src_row[pos] = p / a.top_k;
+      if (a.rank != nullptr) a.rank[p] = pos;
+      if (a.sorted_weights != nullptr) a.sorted_weights[pos] = a.pair_weights[p];
+      if ((peers & lt_mask) == 0) s_base[x] = base + __popc(peers);
+    }
+    __syncwarp();
   }
 }
 
@@ -308,6 +380,10 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_scatter_kernel(cons
 int launch_dispatch(const DispatchArgs& a, cudaStream_t stream) {
   if (a.pairs <= 0) return SPX_ERR_INVALID_ARG;
   if (a.num_experts > 1024) return SPX_ERR_UNSUPPORTED;
+  if (a.pairs <= kDispatchSmallPairs) {
+    dispatch_small_kernel<<<1, 1024, 0, stream>>>(a);
+    return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+  }
   const int nchunks = static_cast<int>((a.pairs + kDispatchChunk - 1) / kDispatchChunk);
   dispatch_count_kernel<<<nchunks, kDispatchThreads, a.num_experts * sizeof(int), stream>>>(a);
   if (cudaGetLastError() != cudaSuccess) return SPX_ERR_CUDA;

@@ -24,6 +24,7 @@ constexpr int kSmallBatchTokens = 256;     // decode-sized batches: narrow GEMM 
 constexpr int kMaxTopK = 20;           // MicroExpertsConfig.max_active_experts default
 constexpr int kDispatchChunk = 2048;   // pairs per dispatch CTA
 constexpr int kDispatchWarps = 4;
+constexpr int kDispatchSmallPairs = 4096;  // up to this many pairs one CTA runs the whole dispatch
 constexpr int kDispatchThreads = 32 * kDispatchWarps;
 
 // kEpiScatter writes the weighted expert rows in sorted (dispatch) order; the
