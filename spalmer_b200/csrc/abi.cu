@@ -389,7 +389,11 @@ int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hid
 }
 
 // K4 (shared half): shared SwiGLU of every token into `shared_out` [T, d].
-int stage_shared(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, uint16_t* shared_out) {
+// Shared SwiGLU.  With `y` given, the down projection's epilogue also does
+// the combine: out = bf16(shared + the token's k expert rows of y), written
+// to `out` (the layer update); otherwise `out` receives the shared output.
+int stage_shared(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, uint16_t* out,
+                 const uint16_t* y = nullptr, const int* rank = nullptr) {
   const Shape& s = c.s;
   int rc = SPX_OK;
   uint16_t* hs = at<uint16_t>(c.ws, c.L.shared_hidden);
@@ -407,14 +411,24 @@ int stage_shared(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, 
     if ((rc = launch_gemm(kEpiSwiglu, g, ceil_div(s.T, kTileRows), s.ncs, c.st)) != SPX_OK) return rc;
   }
   c.mark(6);
-  GemmArgs g = base_args(kEpiStore, s.bn_sd, s.ksp / 64, c.status);
+  const int epi = y != nullptr ? kEpiCombine : kEpiStore;
+  GemmArgs g = base_args(epi, s.bn_sd, s.ksp / 64, c.status);
   if ((rc = encode_2d(&g.tma_a, hs, s.T, s.ksp, s.ksp, kTileRows)) != SPX_OK) return rc;
   if ((rc = encode_3d(&g.tma_b, w->shared_w2, 1, s.d, s.ksp, s.bn_sd)) != SPX_OK) return rc;
   g.m_rows = static_cast<int>(s.T);
   g.n_valid = s.d;
-  g.out = shared_out;
+  g.out = out;
   g.ldo = s.d;
-  return launch_gemm(kEpiStore, g, ceil_div(s.T, kTileRows), s.gn_sd, c.st);
+  g.comb_y = y;
+  g.comb_rank = rank;
+  g.comb_k = s.k;
+  g.ldy = s.d;
+  return launch_gemm(epi, g, ceil_div(s.T, kTileRows), s.gn_sd, c.st);
+}
+
+// The combine can ride on the shared down projection's epilogue.
+bool fused_combine_ok(const Shape& s) {
+  return s.S > 0 && s.k <= kCombineMaxK && (s.d % 64) == 0 && (s.bn_sd % 64) == 0;
 }
 
 int check_layer_weights(const Shape& s, const spx_layer_dims* dims, const spx_packed_weights* w, bool router,
@@ -684,14 +698,18 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   if ((rc = stage_experts(c, w, hidden, xa, da)) != SPX_OK) return rc;
   // ---- K4: shared SwiGLU, then update = shared + the token's k weighted expert rows
   uint16_t* y = at<uint16_t>(workspace, L.y);
-  uint16_t* so = nullptr;
-  if (s.S > 0) {
-    so = at<uint16_t>(workspace, L.shared_out);
-    if ((rc = stage_shared(c, w, xa, so)) != SPX_OK) return rc;
+  if (fused_combine_ok(s)) {
+    if ((rc = stage_shared(c, w, xa, out->update, y, da.rank)) != SPX_OK) return rc;
   } else {
-    c.mark(6);
+    uint16_t* so = nullptr;
+    if (s.S > 0) {
+      so = at<uint16_t>(workspace, L.shared_out);
+      if ((rc = stage_shared(c, w, xa, so)) != SPX_OK) return rc;
+    } else {
+      c.mark(6);
+    }
+    if ((rc = launch_combine(y, da.rank, nullptr, so, s.T, s.d, s.k, out->update, c.st)) != SPX_OK) return rc;
   }
-  if ((rc = launch_combine(y, da.rank, nullptr, so, s.T, s.d, s.k, out->update, c.st)) != SPX_OK) return rc;
   c.mark(7);
   return SPX_OK;
 }

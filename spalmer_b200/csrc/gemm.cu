@@ -225,6 +225,111 @@ __device__ __forceinline__ void run_epilogue_rows(const GemmArgs& a, uint32_t ta
   }
 }
 
+// Shared down projection fused with the combine (kEpiCombine):
+//   update[t] = bf16(bf16(acc_t) + sum_j Y[rank[t*k + j]])
+// in FP32, base first and then the slots in order -- the combine kernel's
+// arithmetic, so the result is the same bit for bit.  The warp stages its
+// accumulator slices (BF16, at most two of 64 columns) in its two 4 KB
+// buffers and releases the accumulator.  It then walks its 32 tokens 4 at a
+// time: each 8-lane group reads one token's k expert rows in whole 128-byte
+// segments for both slices (2k loads in flight per lane) and stores the
+// finished segments.  The expert rows are too few per SM to cover HBM
+// latency with loads alone, so every token's rows are prefetched into L2
+// (by the token's own thread, which holds its ranks) kPrefetchSteps steps
+// before they are read.  Requires n_valid % 64 == 0 and bn % 64 == 0.
+__device__ __forceinline__ void run_epilogue_combine(const GemmArgs& a, uint32_t taddr, uint8_t* stage, int quad,
+                                                     int half, int lane, int rows, int n0, long long my_row,
+                                                     uint64_t* release) {
+  constexpr int kPrefetchSteps = 3;
+  const int r = quad * 32 + lane;
+  const int wrows = rows - quad * 32;
+  const int k = a.comb_k;
+  int rk[kCombineMaxK];
+#pragma unroll
+  for (int j = 0; j < kCombineMaxK; ++j)
+    rk[j] = (j < k && r < rows) ? __ldg(a.comb_rank + my_row * k + j) : 0;
+  const int cb = n0 + half * 64;  // first column of slice 0; slice 1 is 128 columns on
+  const bool ok0 = cb < a.bn + n0 && cb < a.n_valid;
+  const bool ok1 = cb + 128 < a.bn + n0 && cb + 128 < a.n_valid;
+  // Rows of step s belong to lanes 4s .. 4s+3.
+  auto prefetch_step = [&](int s) {
+    if ((lane >> 2) == s && lane < wrows) {
+#pragma unroll
+      for (int j = 0; j < kCombineMaxK; ++j) {
+        if (j < k) {
+          const uint16_t* src = a.comb_y + static_cast<int64_t>(rk[j]) * a.ldy + cb;
+          if (ok0) prefetch_l2(src);
+          if (ok1) prefetch_l2(src + 128);
+        }
+      }
+    }
+  };
+  if (wrows > 0) {
+    for (int s = 0; s < kPrefetchSteps; ++s) prefetch_step(s);
+  }
+  // 1) accumulator -> BF16 staging
+#pragma unroll
+  for (int sl = 0; sl < 2; ++sl) {
+    const int s0 = half * 64 + sl * 128;
+    if (s0 < a.bn) {
+      uint32_t v[64];
+      tmem_ld32(taddr + s0, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      tmem_ld32(taddr + s0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      tmem_wait_ld();
+      uint32_t hw[32];
+#pragma unroll
+      for (int j = 0; j < 64; j += 2) hw[j / 2] = pack_bf16x2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+      uint8_t* buf = stage + sl * kStageBytesPerWarp;
+#pragma unroll
+      for (int c = 0; c < 64; c += 16) stage_put16(buf, lane, c, &hw[c / 2]);
+    }
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(release);
+  if (wrows <= 0) return;
+  // 2) gather the expert rows, add, store
+  const int g = lane >> 3, j8 = lane & 7;
+  uint16_t* out = static_cast<uint16_t*>(a.out);
+#pragma unroll 1
+  for (int step = 0; step < 8; ++step) {
+    if (step + kPrefetchSteps < 8) prefetch_step(step + kPrefetchSteps);
+    const int ri = step * 4 + g;
+    int pr[kCombineMaxK];
+#pragma unroll
+    for (int j = 0; j < kCombineMaxK; ++j) pr[j] = __shfl_sync(0xFFFFFFFFu, rk[j], ri);
+    const long long t = __shfl_sync(0xFFFFFFFFu, my_row, ri);
+    if (ri < wrows) {
+      uint4 y0[kCombineMaxK], y1[kCombineMaxK];
+#pragma unroll
+      for (int j = 0; j < kCombineMaxK; ++j) {
+        if (j < k) {
+          const uint16_t* src = a.comb_y + static_cast<int64_t>(pr[j]) * a.ldy + cb + j8 * 8;
+          if (ok0) y0[j] = __ldg(reinterpret_cast<const uint4*>(src));
+          if (ok1) y1[j] = __ldg(reinterpret_cast<const uint4*>(src + 128));
+        }
+      }
+#pragma unroll
+      for (int sl = 0; sl < 2; ++sl) {
+        if (sl == 0 ? ok0 : ok1) {
+          float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+          add_row8<false>(acc, *reinterpret_cast<const uint4*>(stage + sl * kStageBytesPerWarp + stage_off(ri, j8)),
+                          1.0f);
+#pragma unroll
+          for (int j = 0; j < kCombineMaxK; ++j)
+            if (j < k) add_row8<false>(acc, sl == 0 ? y0[j] : y1[j], 1.0f);
+          uint4 o;
+          o.x = pack_bf16x2(acc[0], acc[1]);
+          o.y = pack_bf16x2(acc[2], acc[3]);
+          o.z = pack_bf16x2(acc[4], acc[5]);
+          o.w = pack_bf16x2(acc[6], acc[7]);
+          *reinterpret_cast<uint4*>(out + t * a.ldo + cb + sl * 128 + j8 * 8) = o;
+        }
+      }
+    }
+  }
+}
+
 // MXFP8-lane SwiGLU epilogue: each thread holds 32 hidden values of its row
 // per slice (one scale block) and writes them as E4M3 bytes plus the block's
 // scale byte.  The accumulator is released as soon as the thread's slices are
@@ -417,7 +522,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   uint8_t* sb = smem + S * a_bytes;
   uint8_t* ssf = sb + S * b_bytes;                           // MX: [S][SFA atom | SFB atom]
   // Epilogue staging: one 4 KB buffer per epilogue warp, two for the TMA-store epilogue.
-  constexpr int kStageBufs = (EPI == kEpiScatter) ? 2 : 1;
+  constexpr int kStageBufs = (EPI == kEpiScatter || EPI == kEpiCombine) ? 2 : 1;
   // 1024-byte aligned: the TMA store reads the buffers with the 128B swizzle.
   uint8_t* stage_all = align_1024(ssf + (MX ? S * kMxStageSfBytes : 0u));
   uint64_t* full = reinterpret_cast<uint64_t*>(stage_all + kGemmEpilogueWarps * kStageBufs * kStageBytesPerWarp);
@@ -573,6 +678,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       const uint32_t taddr = tmem + b * a.tmem_cols + (static_cast<uint32_t>(quad * 32) << 16);
       if constexpr (MX && EPI == kEpiSwiglu) {
         run_epilogue_swiglu_mx(a, taddr, quad, half, lane, row0, rows, nt, &tempty[b]);  // releases early
+      } else if constexpr (EPI == kEpiCombine) {
+        run_epilogue_combine(a, taddr, my_stage, quad, half, lane, rows, nt * bn, my_row, &tempty[b]);  // releases early
       } else {
         if constexpr (EPI == kEpiScatter)
           run_epilogue_rows(a, taddr, my_stage, quad, half, lane, row0, rows, nt * bn, my_w, slices, committed);
@@ -653,7 +760,8 @@ int encode_3d(CUtensorMap* map, const void* base, int64_t groups, int64_t rows, 
 
 size_t gemm_smem_bytes(int bn, int stages, bool mx, int epi) {
   const size_t per_stage = kTileRows * 128 + static_cast<size_t>(bn) * 128 + (mx ? kMxStageSfBytes : 0);
-  const size_t staging = static_cast<size_t>(kGemmEpilogueWarps) * kStageBytesPerWarp * (epi == kEpiScatter ? 2 : 1);
+  const size_t staging =
+      static_cast<size_t>(kGemmEpilogueWarps) * kStageBytesPerWarp * (epi == kEpiScatter || epi == kEpiCombine ? 2 : 1);
   return 2048 + static_cast<size_t>(stages) * per_stage + staging + (2 * stages + 2 * kMaxAccBufs) * 8 + 16;
 }
 
@@ -710,6 +818,12 @@ int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t
       return launch_gemm_t<kEpiSwiglu, false>(a, grid_m, grid_n, stream);
     case kEpiScatter:
       return launch_gemm_t<kEpiScatter, false>(a, grid_m, grid_n, stream);
+    case kEpiCombine:
+      if (a.comb_y == nullptr || a.comb_rank == nullptr || a.comb_k < 1 || a.comb_k > kCombineMaxK ||
+          (a.n_valid % 64) != 0 || (a.bn % 64) != 0 || (a.ldy % 8) != 0 || (a.ldo % 8) != 0 ||
+          (reinterpret_cast<uintptr_t>(a.comb_y) & 15u) != 0 || (reinterpret_cast<uintptr_t>(a.out) & 15u) != 0)
+        return SPX_ERR_INVALID_ARG;
+      return launch_gemm_t<kEpiCombine, false>(a, grid_m, grid_n, stream);
     default:
       return SPX_ERR_INVALID_ARG;
   }

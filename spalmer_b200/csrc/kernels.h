@@ -28,8 +28,10 @@ constexpr int kDispatchSmallPairs = 4096;  // up to this many pairs one CTA runs
 constexpr int kDispatchThreads = 32 * kDispatchWarps;
 
 // kEpiScatter writes the weighted expert rows in sorted (dispatch) order; the
-// combine (pack.cu) gathers each token's k rows through the rank array.
-enum Epi : int { kEpiStore = 0, kEpiSwiglu = 1, kEpiScatter = 2 };
+// combine (pack.cu, or kEpiCombine: the shared down projection's epilogue)
+// gathers each token's k rows through the rank array.
+enum Epi : int { kEpiStore = 0, kEpiSwiglu = 1, kEpiScatter = 2, kEpiCombine = 3 };
+constexpr int kCombineMaxK = 8;  // kEpiCombine: top-k up to this (larger k: separate combine kernel)
 
 // MXFP8 lane: B-operand sources of the pack-time quantiser, and the tensor
 // memory plan of the block-scaled GEMM: accumulators in columns [0, 384)
@@ -127,6 +129,10 @@ struct GemmArgs {
   const uint16_t* pos_weight;  // kEpiScatter: routing weight of each sorted position
   CUtensorMap tma_out;       // kEpiScatter: Y [P sorted rows, d] BF16, box {64, 32}, 128B swizzle
   int tma_store;             // kEpiScatter: 1 = tma_out is valid (d % 64 == 0)
+  const uint16_t* comb_y;    // kEpiCombine: expert rows Y [P, ldy] in sorted order (weights applied)
+  const int* comb_rank;      // kEpiCombine: sorted position of pair t*k+j
+  int comb_k;                // kEpiCombine: pairs per token (<= kCombineMaxK)
+  int64_t ldy;
   int* status;
 };
 

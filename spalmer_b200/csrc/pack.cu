@@ -78,21 +78,6 @@ __global__ void pad_rows_kernel(const uint16_t* __restrict__ src, int64_t rows, 
 // consecutive threads take consecutive 16-byte chunks of one token, so every
 // slot's row is read in whole 128-byte lines, and a thread issues all k row
 // loads before it adds any.
-template <bool WEIGHTED>
-__device__ __forceinline__ void add_row8(float (&acc)[8], const uint4& v, float w) {
-  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    float lo = __uint_as_float(u[q] << 16), hi = __uint_as_float(u[q] & 0xFFFF0000u);
-    if constexpr (WEIGHTED) {
-      lo = round_bf16(lo * w);
-      hi = round_bf16(hi * w);
-    }
-    acc[2 * q] += lo;
-    acc[2 * q + 1] += hi;
-  }
-}
-
 template <int KMAX, bool WEIGHTED>
 __global__ void combine_kernel(const uint16_t* __restrict__ y, const int* __restrict__ rank,
                                const uint16_t* __restrict__ weights, const uint16_t* __restrict__ base,

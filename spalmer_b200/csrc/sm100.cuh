@@ -117,6 +117,11 @@ __device__ __forceinline__ void bulk_wait_read() {
 // Wait until every bulk group of this thread has completed (writes performed).
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Bring the cache line holding p into L2 (no registers, no completion).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -315,5 +320,23 @@ __host__ __device__ __forceinline__ float bf16_to_f32(uint16_t b) {
 }
 
 __host__ __device__ __forceinline__ float round_bf16(float f) { return bf16_to_f32(f32_to_bf16_rne(f)); }
+
+// acc[i] += the 8 BF16 values of v (optionally bf16(value * w) first), in
+// FP32: one step of a combine, shared by the combine kernel and the fused
+// shared-projection epilogue so both sum identically.
+template <bool WEIGHTED>
+__device__ __forceinline__ void add_row8(float (&acc)[8], const uint4& v, float w) {
+  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float lo = __uint_as_float(u[q] << 16), hi = __uint_as_float(u[q] & 0xFFFF0000u);
+    if constexpr (WEIGHTED) {
+      lo = round_bf16(lo * w);
+      hi = round_bf16(hi * w);
+    }
+    acc[2 * q] += lo;
+    acc[2 * q + 1] += hi;
+  }
+}
 
 }  // namespace spx
