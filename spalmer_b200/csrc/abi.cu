@@ -113,7 +113,7 @@ MxPackSizes mx_pack_sizes(const Shape& s) {
 
 struct Layout {
   size_t small, tie_rows, lb_partial, lb_sum, chunk_hist, counts, starts, tiles, order, src_row, rank, sorted_w;
-  size_t hidden, y, shared_hidden, shared_out, logits, x_pad, util, stats, ratios, aux;
+  size_t hidden, y, shared_hidden, shared_out, x_pad, util, stats, ratios, aux;
   size_t x_q, x_sf, h_q, h_sf, tiles_mx;  // MXFP8 lane (empty otherwise)
   size_t total;
 };
@@ -142,7 +142,6 @@ Layout make_layout(const Shape& s) {
   L.y = take(2 * static_cast<size_t>(s.P) * s.d);
   L.shared_hidden = take(s.S > 0 ? 2 * static_cast<size_t>(s.T) * s.ksp : 0);
   L.shared_out = take(s.S > 0 ? 2 * static_cast<size_t>(s.T) * s.d : 0);
-  L.logits = take(2 * static_cast<size_t>(s.T) * s.E);
   L.x_pad = take(s.kd != s.d ? 2 * static_cast<size_t>(s.T) * s.kd : 0);
   L.util = take(sizeof(float) * s.E);
   L.stats = take(sizeof(long long) * 6);
@@ -260,6 +259,26 @@ int stage_router(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, 
   g.ldo = s.E;
   g.bias = w->router_bias;
   return launch_gemm(kEpiStore, g, ceil_div(s.T, kTileRows), s.gn_router, c.st);
+}
+
+// K1 of a layer: router GEMM, then scores / top-k / weights / load-balance
+// partials.  Unless the caller injects logits or asks for them, the GEMM
+// writes the logits into router_scores and the route maps them to scores in
+// place (each route CTA reads its rows before it writes them).
+int stage_router_route(const Ctx& c, const spx_layer_dims* dims, const spx_packed_weights* w, const uint16_t* xa,
+                       const spx_layer_outputs* out) {
+  const Shape& s = c.s;
+  const uint16_t* lut = dims->score_transform == 0 ? w->softplus_table : nullptr;
+  int rc = SPX_OK;
+  const uint16_t* logits = out->injected_logits;
+  if (logits == nullptr) {
+    uint16_t* lg = out->router_logits != nullptr ? out->router_logits : out->router_scores;
+    if ((rc = stage_router(c, w, xa, lg)) != SPX_OK) return rc;
+    logits = lg;
+  }
+  c.mark(1);
+  return run_route(s, logits, lut, w->resident_mask, out->router_scores, out->expert_ids, out->routing_weights,
+                   c.ws, c.L, c.st);
 }
 
 // K2 arguments for the layer's dispatch: statistics into the caller's outputs
@@ -426,9 +445,12 @@ int stage_shared(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, 
   return launch_gemm(epi, g, ceil_div(s.T, kTileRows), s.gn_sd, c.st);
 }
 
-// The combine can ride on the shared down projection's epilogue.
+// The combine can ride on the shared down projection's epilogue.  Not for
+// decode-sized batches: there the few epilogue warps would walk their rows'
+// expert rows one latency at a time, where the combine kernel spreads them
+// over the whole GPU.
 bool fused_combine_ok(const Shape& s) {
-  return s.S > 0 && s.k <= kCombineMaxK && (s.d % 64) == 0 && (s.bn_sd % 64) == 0;
+  return s.S > 0 && s.T > kSmallBatchTokens && s.k <= kCombineMaxK && (s.d % 64) == 0 && (s.bn_sd % 64) == 0;
 }
 
 int check_layer_weights(const Shape& s, const spx_layer_dims* dims, const spx_packed_weights* w, bool router,
@@ -677,18 +699,9 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   c.mark(0);
   const uint16_t* xa = nullptr;
   if ((rc = stage_pad(c, hidden, &xa)) != SPX_OK) return rc;
-  // ---- K1: router logits (tcgen05 GEMM) unless injected
-  const uint16_t* logits = out->injected_logits;
-  if (logits == nullptr) {
-    uint16_t* lg = out->router_logits != nullptr ? out->router_logits : at<uint16_t>(workspace, L.logits);
-    if ((rc = stage_router(c, w, xa, lg)) != SPX_OK) return rc;
-    logits = lg;
-  }
-  c.mark(1);
-  // ---- K1: scores, top-k, weights, load-balance partials
-  rc = run_route(s, logits, dims->score_transform == 0 ? w->softplus_table : nullptr, w->resident_mask,
-                 out->router_scores, out->expert_ids, out->routing_weights, workspace, L, c.st);
-  if (rc != SPX_OK) return rc;
+  // ---- K1: router GEMM (unless logits are injected), scores, top-k, weights,
+  // load-balance partials
+  if ((rc = stage_router_route(c, dims, w, xa, out)) != SPX_OK) return rc;
   c.mark(2);
   // ---- K2: dispatch + statistics
   const DispatchArgs da = layer_dispatch_args(c, dims, w, out);
@@ -730,15 +743,7 @@ int spx_layer_route(const spx_layer_dims* dims, const spx_packed_weights* w, con
   int rc = SPX_OK;
   const uint16_t* xa = nullptr;
   if ((rc = stage_pad(c, hidden, &xa)) != SPX_OK) return rc;
-  const uint16_t* logits = out->injected_logits;
-  if (logits == nullptr) {
-    uint16_t* lg = out->router_logits != nullptr ? out->router_logits : at<uint16_t>(workspace, L.logits);
-    if ((rc = stage_router(c, w, xa, lg)) != SPX_OK) return rc;
-    logits = lg;
-  }
-  rc = run_route(s, logits, dims->score_transform == 0 ? w->softplus_table : nullptr, w->resident_mask,
-                 out->router_scores, out->expert_ids, out->routing_weights, workspace, L, c.st);
-  if (rc != SPX_OK) return rc;
+  if ((rc = stage_router_route(c, dims, w, xa, out)) != SPX_OK) return rc;
   DispatchArgs da = layer_dispatch_args(c, dims, w, out);
   da.lane_mx = nullptr;  // the experts run elsewhere
   return launch_dispatch(da, c.st);

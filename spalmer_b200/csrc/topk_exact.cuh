@@ -25,13 +25,15 @@
 // against std::nth_element / std::partial_sort / std::sort on millions of
 // tie-heavy rows.
 //
-// Elements are 32-bit words: bits [31:16] hold the BF16 score, bits [15:0]
-// the expert index.  Only the score takes part in comparisons.
+// Elements are 32-bit words: bits [31:16] hold the BF16 score as an order
+// key (order_key16), bits [15:0] the expert index.  Only the key takes part in
+// comparisons, as one unsigned compare: the key maps the comparator "NaN
+// last, otherwise value <" onto integer order (-0 and +0 share a key, every
+// NaN gets the largest key, so NaNs compare equal to each other, as they do
+// under that comparator).
 #pragma once
 
 #include <stdint.h>
-
-#include <cstring>
 
 #if defined(__CUDACC__)
 #define SPX_HD __host__ __device__ __forceinline__
@@ -42,24 +44,22 @@
 namespace spx {
 namespace exact {
 
-SPX_HD float key_of(uint32_t w) {
-  uint32_t u = w & 0xFFFF0000u;
-#if defined(__CUDA_ARCH__)
-  return __uint_as_float(u);
-#else
-  float f;
-  std::memcpy(&f, &u, 4);
-  return f;
-#endif
+SPX_HD uint32_t order_key16(uint16_t b) {
+  if ((b & 0x7F80u) == 0x7F80u && (b & 0x007Fu) != 0u) return 0xFFFFu;  // NaN
+  if (b == 0x8000u) b = 0;                                               // -0 -> +0
+  return (b & 0x8000u) ? (~static_cast<uint32_t>(b) & 0xFFFFu) : (static_cast<uint32_t>(b) | 0x8000u);
 }
 
-SPX_HD bool is_nan_key(float f) { return f != f; }
-
-// "a before b": NaN last, otherwise strict less-than on the value.
-SPX_HD bool before(uint32_t a, uint32_t b) {
-  const float x = key_of(a), y = key_of(b);
-  return (!is_nan_key(x) && is_nan_key(y)) || (x < y);
+// BF16 bits back from an order key (+0 for the zero key, a NaN for the NaN key).
+SPX_HD uint16_t key16_to_bits(uint32_t key) {
+  return (key & 0x8000u) ? static_cast<uint16_t>(key & 0x7FFFu) : static_cast<uint16_t>(~key & 0xFFFFu);
 }
+
+// The element of score bits `b` at index `idx`.
+SPX_HD uint32_t make_elem(uint16_t b, uint32_t idx) { return (order_key16(b) << 16) | idx; }
+
+// "a before b": a's score comes strictly first.
+SPX_HD bool before(uint32_t a, uint32_t b) { return (a >> 16) < (b >> 16); }
 
 SPX_HD void swap_at(uint32_t* v, int i, int j) {
   const uint32_t t = v[i];

@@ -51,20 +51,22 @@ int main(int argc, char** argv) {
     for (int k = 1; k <= std::min(n, 20); ++k) {
       for (long r = 0; r < rows; ++r) {
         // Mix of value distributions: few levels (heavy ties), many levels,
-        // occasional +inf (masked experts), NaN and signed zeros.
+        // negative values, occasional +inf (masked experts), NaN and signed
+        // zeros.  Elements carry the order key of their BF16 bits.
         const int mode = static_cast<int>(rng() % 6);
         const int levels = mode == 0 ? 1 : mode == 1 ? 2 : mode == 2 ? 4 : mode == 3 ? 16 : 128;
         q.resize(n);
         v.resize(n);
         for (int j = 0; j < n; ++j) {
           float x = 0.25f * static_cast<float>(rng() % levels);
+          if (mode == 4) x -= 16.0f;  // negative scores too (identity score transform)
           const unsigned sp = static_cast<unsigned>(rng() % 97);
           if (mode == 5 && sp == 0) x = NAN;
           if (mode == 5 && sp == 1) x = INFINITY;
           if (mode == 5 && sp == 2) x = -0.0f;
           const uint16_t b = std::isnan(x) ? uint16_t(0x7FC0) : bf16_bits(x);
           q[j] = Elem(from_bits(b), j);
-          v[j] = (static_cast<uint32_t>(b) << 16) | static_cast<uint32_t>(j);
+          v[j] = spx::exact::make_elem(b, static_cast<uint32_t>(j));
         }
         if (k * 64 <= n) {
           std::partial_sort(q.begin(), q.begin() + k, q.end(), least_first);
@@ -100,7 +102,7 @@ int main(int argc, char** argv) {
         float x = 0.25f * static_cast<float>(rng() % static_cast<unsigned>(levels));
         if (rng() % 211 == 0) x = NAN;
         const uint16_t bits = std::isnan(x) ? uint16_t(0x7FC0) : bf16_bits(x);
-        a[j] = (static_cast<uint32_t>(bits) << 16) | static_cast<uint32_t>(j);
+        a[j] = spx::exact::make_elem(bits, static_cast<uint32_t>(j));
       }
       const int lo = static_cast<int>(rng() % static_cast<unsigned>(n - 3));
       const int hi = lo + 4 + static_cast<int>(rng() % static_cast<unsigned>(n - lo - 3));
