@@ -30,6 +30,7 @@ struct Shape {
   int kd;             // d padded to 64 (GEMM1 / router K)
   int c, nc, kp;      // expert GEMM1 chunk, chunks, hidden width padded to 64
   int cs, ncs, ksp;   // shared GEMM1 chunk, chunks, hidden width padded to 64
+  bool small;         // decode-sized batch (narrow tiles, single CTAs)
   int bn_router, gn_router;
   int bn_d, gn_d;     // expert down projection N tile
   int bn_sd, gn_sd;   // shared down projection N tile
@@ -60,6 +61,7 @@ int make_shape(const spx_layer_dims* dm, Shape* s) {
   // spreads over more CTAs.  The packed shared GEMM1 layout follows its chunk
   // width, so it depends on this class.
   const bool small = s->T <= kSmallBatchTokens;
+  s->small = small;
   const int wide = small ? 32 : 128;
   s->c = std::min(round_up_i(s->I, 16), 128);
   s->nc = ceil_div(s->I, s->c);
@@ -417,17 +419,23 @@ int stage_shared(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, 
   int rc = SPX_OK;
   uint16_t* hs = at<uint16_t>(c.ws, c.L.shared_hidden);
   {
+    // Large batches: CTA pairs (256-row tiles; each CTA loads one of the
+    // [gate | up] halves of the B tile).
+    const bool pair = !s.small && (2 * s.cs) % 32 == 0;
     GemmArgs g = base_args(kEpiSwiglu, 2 * s.cs, s.kd / 64, c.status);
+    if (pair) g.stages = gemm_pair_pick_stages(2 * s.cs);
     if ((rc = encode_2d(&g.tma_a, xa, s.T, s.kd, s.kd, kTileRows)) != SPX_OK) return rc;
-    if ((rc = encode_3d(&g.tma_b, w->shared_w1, 1, static_cast<int64_t>(s.ncs) * 2 * s.cs, s.kd, 2 * s.cs)) !=
-        SPX_OK)
+    if ((rc = encode_3d(&g.tma_b, w->shared_w1, 1, static_cast<int64_t>(s.ncs) * 2 * s.cs, s.kd,
+                        pair ? s.cs : 2 * s.cs)) != SPX_OK)
       return rc;
     g.m_rows = static_cast<int>(s.T);
     g.chunk = s.cs;
     g.h_cols = s.ksp;
     g.out = hs;
     g.ldo = s.ksp;
-    if ((rc = launch_gemm(kEpiSwiglu, g, ceil_div(s.T, kTileRows), s.ncs, c.st)) != SPX_OK) return rc;
+    rc = pair ? launch_gemm_pair(kEpiSwiglu, g, ceil_div(s.T, 2 * kTileRows), s.ncs, c.st)
+              : launch_gemm(kEpiSwiglu, g, ceil_div(s.T, kTileRows), s.ncs, c.st);
+    if (rc != SPX_OK) return rc;
   }
   c.mark(6);
   const int epi = y != nullptr ? kEpiCombine : kEpiStore;

@@ -703,6 +703,173 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   }
 }
 
+// CTA-pair GEMM (cluster of two CTAs, tcgen05 cta_group::2): one 256-row
+// tile of A (TMA, uniform tiling) x bn columns per pair.  Each CTA loads its
+// 128 rows of A and half of the B rows into its own shared memory; the TMA
+// loads of both CTAs complete on the leader's full barrier, for which the
+// leader alone expects the bytes of both.  The leader's lane 0 issues the
+// M = 256 MMAs and commits stage releases and accumulator-ready signals to
+// both CTAs at once; each CTA's epilogue drains its own 128 accumulator rows
+// exactly as the single-CTA kernel does.  The peer's epilogue warps arrive on
+// a local barrier and one peer thread forwards each completed release to the
+// leader (a cluster-scope release from the epilogue warps themselves would
+// wait for their global stores).  Per SM this halves the B bytes of every
+// tile.  Every wait is bounded; both CTAs always reach the final cluster
+// barrier, so a pipeline that gives up still tears down in step.
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ GemmArgs a) {
+  extern __shared__ uint8_t gemm_smem_raw[];
+  uint8_t* smem = align_1024(gemm_smem_raw);
+  const int bn = a.bn;  // the pair's N; each CTA holds bn / 2 rows of B
+  const int S = a.stages;
+  const uint32_t a_bytes = kTileRows * 128u;
+  const uint32_t b_bytes = static_cast<uint32_t>(bn / 2) * 128u;
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + S * a_bytes;
+  uint8_t* stage_all = align_1024(sb + S * b_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_all + kGemmEpilogueWarps * kStageBytesPerWarp);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + kMaxAccBufs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + kMaxAccBufs);
+  const uint32_t nacc = min(static_cast<uint32_t>(kMaxAccBufs), 512u / a.tmem_cols);
+  const uint32_t tmem_alloc_cols = nacc * a.tmem_cols;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int npairs = static_cast<int>(gridDim.x >> 1);
+  const int m_tiles = (a.m_rows + 2 * kTileRows - 1) / (2 * kTileRows);
+  const int total = m_tiles * a.n_tiles;
+  if (pair >= total) return;  // both CTAs of a pair share `pair`: they leave together
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);   // the leader's expect_tx arrival (+ both CTAs' bytes)
+      mbar_init(&empty[s], 1);  // one multicast commit
+    }
+    for (int b = 0; b < kMaxAccBufs; ++b) {
+      mbar_init(&tfull[b], 1);  // one multicast commit
+      // Local epilogue warps; on the leader also the peer's forwarded release.
+      mbar_init(&tempty[b], kGemmEpilogueWarps + (rank == 0 ? 1 : 0));
+    }
+    fence_mbar_init();
+    prefetch_tensormap(&a.tma_a);
+    prefetch_tensormap(&a.tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, tmem_alloc_cols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs)
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < total; t += npairs) {
+        const int mt = t / a.n_tiles;
+        const int nt = t - mt * a.n_tiles;
+        const int row0 = mt * 2 * kTileRows + static_cast<int>(rank) * kTileRows;
+        const int n0 = nt * bn + static_cast<int>(rank) * (bn / 2);
+        for (int kb = 0; kb < a.k_blocks; ++kb, ++it) {
+          const int s = static_cast<int>(it % S);
+          const uint32_t ph = (it / S) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, a.status, SPX_DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_leader = mapa_shared(smem_u32(&full[s]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (a_bytes + b_bytes));
+          tma_load_2d_pair(sa + s * a_bytes, &a.tma_a, full_leader, kb * 64, row0);
+          tma_load_3d_pair(sb + s * b_bytes, &a.tma_b, full_leader, kb * 64, n0, 0);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (rank != 0 && lane == 0) {
+      // ---------------- peer: forward the epilogue's releases to the leader
+      uint32_t lt = 0;
+      for (int t = pair; t < total; t += npairs, ++lt) {
+        const uint32_t b = lt % nacc;
+        if (!mbar_wait(&tempty[b], (lt / nacc) & 1u, a.status, SPX_DEV_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[b]), 0));
+      }
+    } else if (rank == 0 && lane == 0) {
+      // ---------------- leader: MMA issuer
+      const uint32_t idesc = idesc_bf16_f32(2 * kTileRows, bn);
+      uint32_t it = 0, lt = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < total; t += npairs, ++lt) {
+        const uint32_t b = lt % nacc;
+        const uint32_t tph = (lt / nacc) & 1u;
+        if (!mbar_wait(&tempty[b], tph ^ 1u, a.status, SPX_DEV_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + b * a.tmem_cols;
+        for (int kb = 0; kb < a.k_blocks; ++kb, ++it) {
+          const int s = static_cast<int>(it % S);
+          const uint32_t ph = (it / S) & 1u;
+          if (!mbar_wait(&full[s], ph, a.status, SPX_DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sa + s * a_bytes);
+          const uint32_t b_base = smem_u32(sb + s * b_bytes);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16_pair(acc, desc_kmajor_sw128(a_base + kk * 32), desc_kmajor_sw128(b_base + kk * 32), idesc,
+                          (kb | kk) != 0 ? 1u : 0u);
+          mma_commit_pair(&empty[s], 0x3);
+        }
+        if (!ok) break;
+        mma_commit_pair(&tfull[b], 0x3);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (both CTAs): this CTA's 128 accumulator rows
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    uint8_t* my_stage = stage_all + (warp - 2) * kStageBytesPerWarp;
+    uint32_t lt = 0;
+    for (int t = pair; t < total; t += npairs, ++lt) {
+      const int mt = t / a.n_tiles;
+      const int nt = t - mt * a.n_tiles;
+      const int row0 = mt * 2 * kTileRows + static_cast<int>(rank) * kTileRows;
+      const int rows = max(0, min(kTileRows, a.m_rows - row0));
+      const uint32_t b = lt % nacc;
+      const uint32_t tph = (lt / nacc) & 1u;
+      int go = 1;
+      if (lane == 0) go = mbar_wait(&tfull[b], tph, a.status, SPX_DEV_TIMEOUT_EPILOGUE) ? 1 : 0;
+      go = __shfl_sync(0xFFFFFFFFu, go, 0);
+      if (!go) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem + b * a.tmem_cols + (static_cast<uint32_t>(quad * 32) << 16);
+      const long long my_row = static_cast<long long>(row0) + quad * 32 + lane;
+      run_epilogue<EPI>(a, taddr, my_stage, quad, half, lane, row0, rows, nt * bn, nt, my_row);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its pair may still touch its shared or tensor memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, tmem_alloc_cols);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 
 namespace {
@@ -765,6 +932,19 @@ size_t gemm_smem_bytes(int bn, int stages, bool mx, int epi) {
   return 2048 + static_cast<size_t>(stages) * per_stage + staging + (2 * stages + 2 * kMaxAccBufs) * 8 + 16;
 }
 
+size_t gemm_pair_smem_bytes(int bn, int stages) {
+  const size_t per_stage = kTileRows * 128 + static_cast<size_t>(bn / 2) * 128;
+  const size_t staging = static_cast<size_t>(kGemmEpilogueWarps) * kStageBytesPerWarp;
+  return 2048 + static_cast<size_t>(stages) * per_stage + staging + (2 * stages + 2 * kMaxAccBufs) * 8 + 16;
+}
+
+int gemm_pair_pick_stages(int bn) {
+  int stages = 2;
+  for (int s = 3; s <= 8; ++s)
+    if (gemm_pair_smem_bytes(bn, s) <= kGemmSmemBudget) stages = s;
+  return stages;
+}
+
 // As many stages as fit: the persistent producer keeps prefetching the next
 // tile's k-blocks, so stages beyond one tile's K still hide load latency.
 int gemm_pick_stages(int bn, int k_blocks, bool mx, int epi) {
@@ -788,6 +968,39 @@ static int launch_gemm_t(const GemmArgs& a, int grid_m, int grid_n, cudaStream_t
   b.n_tiles = grid_n;
   gemm_kernel<EPI, MX><<<grid, kGemmThreads, smem, stream>>>(b);
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+template <int EPI>
+static int launch_gemm_pair_t(const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream) {
+  const size_t smem = gemm_pair_smem_bytes(a.bn, a.stages);
+  if (smem > kGemmSmemBudget) return SPX_ERR_INVALID_ARG;
+  const void* fn = reinterpret_cast<const void*>(gemm_pair_kernel<EPI>);
+  if (int rc = ensure_max_dynamic_smem(fn); rc != SPX_OK) return rc;
+  // Persistent grid of CTA pairs: no more pairs than tiles, nor than fit on
+  // the device at once.
+  const int pairs_max = device_max_pairs(fn, smem);
+  const int64_t tiles = static_cast<int64_t>(grid_m) * grid_n;
+  const int pairs = static_cast<int>(tiles < pairs_max ? tiles : pairs_max);
+  GemmArgs b = a;
+  b.n_tiles = grid_n;
+  gemm_pair_kernel<EPI><<<2 * pairs, kGemmThreads, smem, stream>>>(b);
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+// CTA-pair GEMM over 256-row tiles of a TMA-loaded A (grid_m counts 256-row
+// tiles).  bn: 32..256, a multiple of 32 (each CTA holds bn / 2 rows of B).
+int launch_gemm_pair(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream) {
+  if (grid_m <= 0 || grid_n <= 0) return SPX_OK;
+  if (a.bn < 32 || a.bn > 256 || (a.bn % 32) != 0 || a.gather != 0 || a.tiles != nullptr)
+    return SPX_ERR_UNSUPPORTED;
+  switch (epi) {
+    case kEpiStore:
+      return launch_gemm_pair_t<kEpiStore>(a, grid_m, grid_n, stream);
+    case kEpiSwiglu:
+      return launch_gemm_pair_t<kEpiSwiglu>(a, grid_m, grid_n, stream);
+    default:
+      return SPX_ERR_UNSUPPORTED;
+  }
 }
 
 int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream, bool mx) {

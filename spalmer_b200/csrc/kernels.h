@@ -141,6 +141,8 @@ struct GemmArgs {
 int device_sm_count();
 // Raise `func`'s dynamic shared memory limit to the device maximum once per device.
 int ensure_max_dynamic_smem(const void* func);
+// How many 2-CTA clusters of `func` (with `smem` dynamic bytes) fit on the device at once.
+int device_max_pairs(const void* func, size_t smem);
 
 int launch_softplus_table(uint16_t* lut, cudaStream_t stream);
 size_t route_select_smem(int num_experts);
@@ -158,6 +160,10 @@ size_t gemm_smem_bytes(int bn, int stages, bool mx, int epi);
 int gemm_pick_stages(int bn, int k_blocks, bool mx, int epi);
 // `mx` selects the block-scaled MXFP8 kernel (bn <= 128, k_blocks of 128 elements).
 int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream, bool mx = false);
+// CTA-pair (cluster of 2, cta_group::2) GEMM: 256-row tiles of a TMA-loaded A.
+size_t gemm_pair_smem_bytes(int bn, int stages);
+int gemm_pair_pick_stages(int bn);
+int launch_gemm_pair(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream);
 
 // Router calibration loss term and NLL attribution (calibration.cu).
 size_t calibration_workspace_bytes(int64_t B, int64_t S, int E);

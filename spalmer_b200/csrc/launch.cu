@@ -61,4 +61,44 @@ int ensure_max_dynamic_smem(const void* func) {
   return SPX_ERR_UNSUPPORTED;
 }
 
+int device_max_pairs(const void* func, size_t smem) {
+  const int fallback = device_sm_count() / 2;
+  const int dev = current_device();
+  if (dev < 0) return fallback;
+  static const void* cached_func[kMaxDevices][kMaxFuncs] = {};
+  static size_t cached_smem[kMaxDevices][kMaxFuncs] = {};
+  static int cached_pairs[kMaxDevices][kMaxFuncs] = {};
+  std::lock_guard<std::mutex> lock(g_mu);
+  int slot = -1;
+  for (int i = 0; i < kMaxFuncs; ++i) {
+    if (cached_func[dev][i] == func && cached_smem[dev][i] == smem) return cached_pairs[dev][i];
+    if (cached_func[dev][i] == nullptr) {
+      slot = i;
+      break;
+    }
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * static_cast<unsigned>(fallback > 0 ? fallback : 1), 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, func, &cfg) != cudaSuccess || clusters <= 0) {
+    cudaGetLastError();
+    clusters = fallback;
+  }
+  if (slot >= 0) {
+    cached_func[dev][slot] = func;
+    cached_smem[dev][slot] = smem;
+    cached_pairs[dev][slot] = clusters;
+  }
+  return clusters;
+}
+
 }  // namespace spx
