@@ -51,7 +51,7 @@
 extern "C" {
 #endif
 
-#define SPX_ABI_VERSION 3
+#define SPX_ABI_VERSION 4
 
 #define SPX_OK 0
 #define SPX_ERR_INVALID_ARG -1
@@ -249,6 +249,44 @@ int spx_surprise_calibration(const uint16_t* router_scores, const int64_t* exper
                              const float* token_nll, const uint8_t* valid, int64_t batch, int64_t seq,
                              int32_t num_experts, int32_t top_k, float* calibration, float* attributed_nll,
                              float* utilization, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- backward of the routed experts and the router scores
+ * Reference: autograd through MicroExpertChannelMixer.forward
+ * (experts/mixer.py:185-241: router.py:51-95, bank.py:705-779, 970-978,
+ * losses.py:36-70), as training/engine.py:470 runs it.  Loss gradients in:
+ * d_update (the update), d_aux (the auxiliary loss, optional) and d_scores
+ * (router_scores, optional).  Out: the routed experts' part of dL/dx
+ * (d_hidden_experts; the router's part is d_logits @ W_router and the shared
+ * SwiGLU's is the caller's), dL/d logits, and the sorted-pair operands of the
+ * expert weight gradients: with offsets from expert_counts,
+ *   d gate_e | d up_e = x_sorted[e]^T @ dgu_sorted[e]   ([d, I] each, the up
+ *                                                       half from column kI)
+ *   d down_e          = h_sorted[e]^T @ dy_sorted[e]    ([I, d]).
+ * BF16 experts only (SPX_ERR_UNSUPPORTED with an MXFP8 lane); d_model must be
+ * a multiple of 64.  The dispatch is recomputed from expert_ids, so the
+ * forward's workspace need not survive until the backward. */
+typedef struct spx_layer_grads {
+  const int64_t* expert_ids;        /* [T, k]  from the forward                  */
+  const uint16_t* routing_weights;  /* [T, k]  from the forward (BF16)          */
+  const uint16_t* router_scores;    /* [T, E]  from the forward (BF16)          */
+  const uint16_t* gate_proj;        /* [E, d, I] reference layout (BF16)        */
+  const uint16_t* up_proj;          /* [E, d, I]                                */
+  const uint16_t* down_proj;        /* [E, I, d]                                */
+  const uint16_t* d_update;         /* [T, d]  dL/d update                      */
+  const uint16_t* d_scores;         /* [T, E]  dL/d router_scores | NULL        */
+  const uint16_t* d_aux;            /* device BF16 scalar dL/d aux | NULL       */
+  uint16_t* d_hidden_experts;       /* [T, d]  out                              */
+  uint16_t* d_logits;               /* [T, E]  out                              */
+  uint16_t* x_sorted;               /* [T*k, d]   out                           */
+  uint16_t* h_sorted;               /* [T*k, I]   out                           */
+  uint16_t* dy_sorted;              /* [T*k, d]   out                           */
+  uint16_t* dgu_sorted;             /* [T*k, 2*kI] out, kI = round_up(I, 64)    */
+  int32_t* expert_counts;           /* [E]     out                              */
+} spx_layer_grads;
+
+int spx_layer_backward_sizes(const spx_layer_dims* dims, size_t* workspace_bytes);
+int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* weights, const uint16_t* hidden,
+                       const spx_layer_grads* grads, void* workspace, void* stream);
 
 /* spx_dispatch without a workspace: same outputs, no device allocation by
  * anyone.  No counterpart in the reference; it exists for callers that cannot

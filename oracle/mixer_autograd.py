@@ -41,11 +41,15 @@ PARAM_NAMES = (
 
 
 def forward(params: dict[str, torch.Tensor], x: torch.Tensor, top_k: int, *,
-            identity_scores: bool = False, resident: torch.Tensor | None = None):
+            identity_scores: bool = False, resident: torch.Tensor | None = None,
+            ids: torch.Tensor | None = None):
     """Return ``(update, aux_loss, scores, ids, weights)`` for ``x`` [T, d] (BF16).
 
     ``params`` maps reference state_dict names to BF16 tensors (leaves that may
-    require grad); absent names (no bias, no shared path) are skipped.
+    require grad); absent names (no bias, no shared path) are skipped.  ``ids``
+    ([T, k], optional) replaces the top-k selection -- for comparing gradients
+    with an implementation whose router GEMM rounded a logit differently and
+    so routed a token elsewhere; everything downstream follows the given ids.
     """
 
     num_tokens, d_model = x.shape
@@ -56,7 +60,8 @@ def forward(params: dict[str, torch.Tensor], x: torch.Tensor, top_k: int, *,
     eligible = scores
     if resident is not None:
         eligible = scores.masked_fill(~resident, torch.inf)
-    ids = eligible.topk(top_k, dim=-1, largest=False).indices
+    if ids is None:
+        ids = eligible.topk(top_k, dim=-1, largest=False).indices
     weights = F.softmax(-scores.gather(-1, ids), dim=-1)
 
     token_index = torch.arange(num_tokens).repeat_interleave(top_k)
@@ -99,13 +104,18 @@ def forward(params: dict[str, torch.Tensor], x: torch.Tensor, top_k: int, *,
 
 
 def gradients(params: dict[str, torch.Tensor], x: torch.Tensor, top_k: int, d_update: torch.Tensor,
-              d_aux: float, **kw) -> dict[str, torch.Tensor]:
-    """Gradients of ``sum(update * d_update) + d_aux * aux`` w.r.t. x and params."""
+              d_aux: float, d_scores: torch.Tensor | None = None, **kw) -> dict[str, torch.Tensor]:
+    """Gradients of ``sum(update * d_update) + d_aux * aux [+ sum(scores * d_scores)]``
+    w.r.t. x and params."""
 
     leaves = {k: v.detach().clone().requires_grad_(True) for k, v in params.items()}
     xg = x.detach().clone().requires_grad_(True)
-    update, aux, *_ = forward(leaves, xg, top_k, **kw)
-    torch.autograd.backward([update, aux], [d_update, torch.tensor(d_aux, dtype=aux.dtype)])
+    update, aux, scores, *_ = forward(leaves, xg, top_k, **kw)
+    outs, grads = [update, aux], [d_update, torch.tensor(d_aux, dtype=aux.dtype)]
+    if d_scores is not None:
+        outs.append(scores)
+        grads.append(d_scores)
+    torch.autograd.backward(outs, grads)
     out = {"x": xg.grad}
     for k, v in leaves.items():
         out[k] = v.grad if v.grad is not None else torch.zeros_like(v)

@@ -48,9 +48,11 @@ EXPORTED = (
     "spx_combine",
     "spx_calibration_workspace",
     "spx_surprise_calibration",
+    "spx_layer_backward_sizes",
+    "spx_layer_backward",
 )
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 _vp = ctypes.c_void_p
 
@@ -133,6 +135,27 @@ class LayerOutputs(ctypes.Structure):
     ]
 
 
+class LayerGrads(ctypes.Structure):
+    _fields_ = [
+        ("expert_ids", _vp),
+        ("routing_weights", _vp),
+        ("router_scores", _vp),
+        ("gate_proj", _vp),
+        ("up_proj", _vp),
+        ("down_proj", _vp),
+        ("d_update", _vp),
+        ("d_scores", _vp),
+        ("d_aux", _vp),
+        ("d_hidden_experts", _vp),
+        ("d_logits", _vp),
+        ("x_sorted", _vp),
+        ("h_sorted", _vp),
+        ("dy_sorted", _vp),
+        ("dgu_sorted", _vp),
+        ("expert_counts", _vp),
+    ]
+
+
 STAGE_EVENTS = 8
 STAGE_NAMES = ("router_gemm", "route_topk", "dispatch", "expert_gemm1_swiglu", "expert_gemm2_scatter",
                "shared_gemm1_swiglu", "shared_gemm2_combine")
@@ -194,6 +217,8 @@ def load() -> ctypes.CDLL:
             ctypes.c_int,
             [_vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, _vp, _vp],
         ),
+        "spx_layer_backward_sizes": (ctypes.c_int, [P(LayerDims), P(ctypes.c_size_t)]),
+        "spx_layer_backward": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, P(LayerGrads), _vp, _vp]),
         "spx_mxfp8_mm_nt": (
             ctypes.c_int,
             [_vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp, _vp, ctypes.c_size_t, _vp],

@@ -757,6 +757,177 @@ int spx_layer_route(const spx_layer_dims* dims, const spx_packed_weights* w, con
   return launch_dispatch(da, c.st);
 }
 
+// ---------------------------------------------------------------- backward
+}  // extern "C"
+
+namespace spx {
+namespace {
+
+// Backward workspace: the forward's layout (dispatch scratch, sorted weights,
+// ranks, tile table; y holds the sorted input-gradient rows) and then:
+struct BwdLayout {
+  size_t gu;      // [P, nc * 2c] recomputed gate | up pre-activations (chunk layout)
+  size_t dhp;     // [P, ldh]     bf16(dY_t @ D_e^T)
+  size_t w1cat;   // [E, d, 2 kI] [gate_e | up_e] along K
+  size_t logits;  // [T, E]       recomputed router logits (softplus scores only)
+  size_t dw;      // [P] float    routing-weight gradients in pair order
+  size_t total;
+};
+
+int bwd_ldh(const Shape& s) { return round_up_i(s.I, 16); }
+int bwd_ki(const Shape& s) { return round_up_i(s.I, 64); }
+
+BwdLayout make_bwd_layout(const Shape& s, size_t base) {
+  BwdLayout B{};
+  size_t off = round_up(base, kAlign);
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = round_up(off + bytes, kAlign);
+    return at;
+  };
+  B.gu = take(2 * static_cast<size_t>(s.P) * s.nc * 2 * s.c);
+  B.dhp = take(2 * static_cast<size_t>(s.P) * bwd_ldh(s));
+  B.w1cat = take(2 * static_cast<size_t>(s.E) * s.d * 2 * bwd_ki(s));
+  B.logits = take(2 * static_cast<size_t>(s.T) * s.E);
+  B.dw = take(sizeof(float) * static_cast<size_t>(s.P));
+  B.total = off;
+  return B;
+}
+
+}  // namespace
+}  // namespace spx
+
+extern "C" {
+
+int spx_layer_backward_sizes(const spx_layer_dims* dims, size_t* workspace_bytes) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (workspace_bytes == nullptr) return SPX_ERR_INVALID_ARG;
+  *workspace_bytes = make_bwd_layout(s, make_layout(s).total).total;
+  return SPX_OK;
+}
+
+int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, const uint16_t* hidden,
+                       const spx_layer_grads* gr, void* workspace, void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (gr == nullptr || hidden == nullptr || w == nullptr) return SPX_ERR_INVALID_ARG;
+  if (workspace == nullptr) return SPX_ERR_WORKSPACE;
+  if (s.mx || w->expert_lane_mxfp8 != nullptr) return SPX_ERR_UNSUPPORTED;  // BF16 experts only
+  if (s.kd != s.d) return SPX_ERR_UNSUPPORTED;                              // d_model % 64 == 0
+  if (gr->expert_ids == nullptr || gr->routing_weights == nullptr || gr->router_scores == nullptr ||
+      gr->gate_proj == nullptr || gr->up_proj == nullptr || gr->down_proj == nullptr || gr->d_update == nullptr ||
+      gr->d_hidden_experts == nullptr || gr->d_logits == nullptr || gr->x_sorted == nullptr ||
+      gr->h_sorted == nullptr || gr->dy_sorted == nullptr || gr->dgu_sorted == nullptr ||
+      gr->expert_counts == nullptr)
+    return SPX_ERR_INVALID_ARG;
+  if (int rc = check_layer_weights(s, dims, w, true, true, false); rc != SPX_OK) return rc;
+  if (!aligned16(hidden) || !aligned16(gr->d_update) || !aligned16(workspace) || !aligned16(gr->dgu_sorted) ||
+      !aligned16(gr->x_sorted) || !aligned16(gr->dy_sorted) || !aligned16(gr->d_hidden_experts) ||
+      !aligned16(gr->gate_proj) || !aligned16(gr->up_proj) || !aligned16(gr->down_proj))
+    return SPX_ERR_ALIGNMENT;
+  const Layout L = make_layout(s);
+  const BwdLayout B = make_bwd_layout(s, L.total);
+  const Ctx c{s, L, workspace, static_cast<cudaStream_t>(stream), at<int>(workspace, L.small), nullptr};
+  const cudaStream_t st = c.st;
+  int rc = SPX_OK;
+  const int ki = bwd_ki(s), ldh = bwd_ldh(s);
+  uint16_t* gu = at<uint16_t>(workspace, B.gu);
+  uint16_t* dhp = at<uint16_t>(workspace, B.dhp);
+  uint16_t* w1cat = at<uint16_t>(workspace, B.w1cat);
+  float* dw = at<float>(workspace, B.dw);
+  uint16_t* dxs = at<uint16_t>(workspace, L.y);
+
+  // ---- router logits again (the forward kept only the scores)
+  const bool softplus = dims->score_transform == 0;
+  uint16_t* logits = softplus ? at<uint16_t>(workspace, B.logits) : nullptr;
+  if (softplus && (rc = stage_router(c, w, hidden, logits)) != SPX_OK) return rc;
+
+  // ---- dispatch again, from the forward's expert ids (all experts in the BF16 table)
+  DispatchArgs da = dispatch_args(s, gr->expert_ids, nullptr, gr->expert_counts, workspace, L);
+  da.lb_blocks = 0;
+  da.pair_weights = gr->routing_weights;
+  da.sorted_weights = at<uint16_t>(workspace, L.sorted_w);
+  da.utilization = at<float>(workspace, L.util);
+  da.resident = w->resident_mask;
+  if ((rc = launch_dispatch(da, st)) != SPX_OK) return rc;
+
+  // ---- gate | up pre-activations again: GEMM1 (gathered rows) with a plain epilogue
+  {
+    GemmArgs g = base_args(kEpiStore, 2 * s.c, s.kd / 64, c.status);
+    if ((rc = encode_3d(&g.tma_b, w->expert_w1, s.E, static_cast<int64_t>(s.nc) * 2 * s.c, s.kd, 2 * s.c)) != SPX_OK)
+      return rc;
+    g.groups = s.E;
+    g.gather = 1;
+    g.gather_idx = da.src_row;
+    g.a_base = reinterpret_cast<const uint8_t*>(hidden);
+    g.lda = 2 * static_cast<int64_t>(s.kd);
+    g.tiles = da.tiles;
+    g.num_tiles = da.num_tiles;
+    g.n_valid = s.nc * 2 * s.c;
+    g.out = gu;
+    g.ldo = s.nc * 2 * s.c;
+    if ((rc = launch_gemm(kEpiStore, g, s.max_tiles, s.nc, st)) != SPX_OK) return rc;
+  }
+  // ---- dh' = dU_t @ D_e^T (gathered rows of the upstream gradient)
+  {
+    const int bn = std::min(256, ldh);
+    GemmArgs g = base_args(kEpiStore, bn, s.kd / 64, c.status);
+    if ((rc = encode_3d(&g.tma_b, gr->down_proj, s.E, s.I, s.d, bn)) != SPX_OK) return rc;
+    g.groups = s.E;
+    g.gather = 1;
+    g.gather_idx = da.src_row;
+    g.a_base = reinterpret_cast<const uint8_t*>(gr->d_update);
+    g.lda = 2 * static_cast<int64_t>(s.d);
+    g.tiles = da.tiles;
+    g.num_tiles = da.num_tiles;
+    g.n_valid = s.I;
+    g.out = dhp;
+    g.ldo = ldh;
+    if ((rc = launch_gemm(kEpiStore, g, s.max_tiles, ceil_div(s.I, bn), st)) != SPX_OK) return rc;
+  }
+  // ---- SwiGLU backward: h, [d gate | d up], routing-weight gradients
+  if ((rc = launch_bwd_swiglu(gu, s.nc * 2 * s.c, s.c, dhp, ldh, da.sorted_weights, da.order, s.P, s.I, ki,
+                              gr->h_sorted, gr->dgu_sorted, dw, st)) != SPX_OK)
+    return rc;
+  // ---- input gradient of the experts: dx_p = [d gate | d up] @ [G_e | U_e]^T, then per token
+  if ((rc = launch_bwd_pack_w1cat(gr->gate_proj, gr->up_proj, s.E, s.d, s.I, ki, w1cat, st)) != SPX_OK) return rc;
+  {
+    GemmArgs g = base_args(kEpiStore, s.bn_d, 2 * ki / 64, c.status);
+    if ((rc = encode_2d(&g.tma_a, gr->dgu_sorted, s.P, 2 * ki, 2 * ki, kTileRows)) != SPX_OK) return rc;
+    if ((rc = encode_3d(&g.tma_b, w1cat, s.E, s.d, 2 * ki, s.bn_d)) != SPX_OK) return rc;
+    g.groups = s.E;
+    g.tiles = da.tiles;
+    g.num_tiles = da.num_tiles;
+    g.n_valid = s.d;
+    g.out = dxs;
+    g.ldo = s.d;
+    if ((rc = launch_gemm(kEpiStore, g, s.max_tiles, s.gn_d, st)) != SPX_OK) return rc;
+  }
+  if ((rc = launch_combine(dxs, da.rank, nullptr, nullptr, s.T, s.d, s.k, gr->d_hidden_experts, st)) != SPX_OK)
+    return rc;
+  // ---- sorted operands of the expert weight gradients
+  if ((rc = launch_bwd_gather(hidden, gr->d_update, da.src_row, da.sorted_weights, s.P, s.d, gr->x_sorted,
+                              gr->dy_sorted, st)) != SPX_OK)
+    return rc;
+  // ---- router: selection and load-balance softmaxes, softplus
+  BwdRouterArgs ra{};
+  ra.scores = gr->router_scores;
+  ra.logits = logits;
+  ra.ids = gr->expert_ids;
+  ra.weights = gr->routing_weights;
+  ra.dw = dw;
+  ra.fractions = da.utilization;
+  ra.resident = w->resident_mask;
+  ra.d_aux = gr->d_aux;
+  ra.d_scores = gr->d_scores;
+  ra.d_logits = gr->d_logits;
+  ra.tokens = s.T;
+  ra.num_experts = s.E;
+  ra.top_k = s.k;
+  return launch_bwd_router(ra, st);
+}
+
 int spx_experts_forward(const spx_layer_dims* dims, const spx_packed_weights* w, const uint16_t* rows,
                         const int64_t* row_expert, uint16_t* out_rows, void* workspace, void* stream) {
   Shape s;

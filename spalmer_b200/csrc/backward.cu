@@ -1,0 +1,267 @@
+// Backward pass of the routed micro-expert layer: the elementwise and
+// per-row kernels between the grouped GEMMs (abi.cu spx_layer_backward runs
+// the GEMMs on the tcgen05 engine of gemm.cu).
+//
+// The steps mirror what PyTorch autograd does through the reference forward
+// in BF16 (mESmaC/spalmer src/spalmer): every tensor the reference holds in
+// BF16 is rounded to BF16 here at the same point, arithmetic in between is
+// FP32.  The gradient formulas:
+//   experts (experts/bank.py:760-778, bank.py:970-978):
+//     sg = bf16(silu(g)), h = bf16(sg * u)                    (forward values)
+//     dh = bf16(dh' * w), dh' = bf16(dY_t @ D_e^T)            (dh' from the GEMM)
+//     d_sg = bf16(dh * u), d_u = bf16(dh * sg)
+//     d_g = bf16(d_sg * sigmoid(g) * (1 + g * (1 - sigmoid(g))))
+//     d_w = sum_i dh'_i * h_i      (= sum over d of dY_t * y, y = h @ D_e)
+//   selection (experts/router.py:92-94): w = softmax(-s_sel)
+//     d_s_sel = -bf16(w * (d_w - sum_j w_j d_w_j))
+//   load balance (experts/losses.py:58-70), aux = m * sum_e f_e * mean_t p_te:
+//     d_p_te = bf16(bf16(bf16(d_aux * m) * f_e) / T)
+//     d_s_te = -bf16(p_te * (d_p_te - sum_e p_te d_p_te)),  p = bf16(softmax(-s))
+//   softplus (experts/router.py:56): d_logit = bf16(d_s * sigmoid(logit)),
+//     or d_s itself past the threshold 20.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace spx {
+
+namespace {
+
+__device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+__device__ __forceinline__ uint16_t bfbits(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+int grid_for(int64_t items, int per_block) {
+  int64_t g = (items + per_block - 1) / per_block;
+  if (g > 148 * 32) g = 148 * 32;
+  return static_cast<int>(g < 1 ? 1 : g);
+}
+
+}  // namespace
+
+// Sorted-order rows for the weight gradients: x_sorted[p] = x[t_p] and
+// dy_sorted[p] = bf16(dU[t_p] * w_p) (the reference's d(outputs) of the
+// weighted update, bank.py:978).  8 columns per thread.
+__global__ void bwd_gather_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ du,
+                                  const int* __restrict__ src_row, const uint16_t* __restrict__ sorted_w, int64_t P,
+                                  int d, uint16_t* __restrict__ x_sorted, uint16_t* __restrict__ dy_sorted) {
+  const int vec = d / 8;
+  const int64_t total = P * vec;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t p = idx / vec;
+    const int c = static_cast<int>(idx - p * vec) * 8;
+    const int64_t t = __ldg(src_row + p);
+    const float w = bf16_to_f32(__ldg(sorted_w + p));
+    const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + t * d + c));
+    const uint4 dv = __ldg(reinterpret_cast<const uint4*>(du + t * d + c));
+    *reinterpret_cast<uint4*>(x_sorted + p * d + c) = xv;
+    const uint32_t in[4] = {dv.x, dv.y, dv.z, dv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float lo = __uint_as_float(in[q] << 16) * w, hi = __uint_as_float(in[q] & 0xFFFF0000u) * w;
+      o[q] = static_cast<uint32_t>(bfbits(lo)) | (static_cast<uint32_t>(bfbits(hi)) << 16);
+    }
+    *reinterpret_cast<uint4*>(dy_sorted + p * d + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// SwiGLU backward, one warp per sorted pair row p.  gu holds the recomputed
+// pre-activations in the forward GEMM1's chunk layout (chunk n: c gate
+// columns, then c up columns), dhp = bf16(dY_t @ D_e^T).  Writes h (forward
+// hidden row), [d_gate | d_up] with the up half at column kI (zero padded to
+// 2 kI), and d_w of the pair in pair order (order[p]).
+__global__ void bwd_swiglu_kernel(const uint16_t* __restrict__ gu, int ld_gu, int c, const uint16_t* __restrict__ dhp,
+                                  int ld_dhp, const uint16_t* __restrict__ sorted_w, const int* __restrict__ order,
+                                  int64_t P, int I, int kI, uint16_t* __restrict__ h_sorted,
+                                  uint16_t* __restrict__ dgu, float* __restrict__ dw_pair) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); p < P; p += nwarps) {
+    const float w = bf16_to_f32(sorted_w[p]);
+    const uint16_t* grow = gu + p * ld_gu;
+    float part = 0.0f;
+    for (int i = lane; i < 2 * kI; i += 32) {
+      if (i < I) {
+        const int chunk = i / c, j = i - chunk * c;
+        const float g = bf16_to_f32(grow[chunk * 2 * c + j]);
+        const float u = bf16_to_f32(grow[chunk * 2 * c + c + j]);
+        const float dh1 = bf16_to_f32(dhp[p * ld_dhp + i]);
+        const float sgm = sigmoidf_(g);
+        const float sg = bfr(g / (1.0f + expf(-g)));  // silu as the reference evaluates it
+        const float h = bfr(sg * u);
+        part += dh1 * h;
+        const float dh = bfr(dh1 * w);
+        const float dsg = bfr(dh * u);
+        const float du = bfr(dh * sg);
+        const float dg = bfr(dsg * (sgm * (1.0f + g * (1.0f - sgm))));
+        h_sorted[p * I + i] = bfbits(h);
+        dgu[p * 2 * kI + i] = bfbits(dg);
+        dgu[p * 2 * kI + kI + i] = bfbits(du);
+      } else if (i < kI || i >= kI + I) {
+        dgu[p * 2 * kI + i] = 0;  // K padding of both halves
+      }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xFFFFFFFFu, part, off);
+    if (lane == 0) dw_pair[order[p]] = part;
+  }
+}
+
+// [gate_e | up_e] concatenated along K for the input-gradient GEMM:
+// out[e][n][k] = gate[e][n][k] (k < I), up[e][n][k - kI] (kI <= k < kI + I),
+// 0 otherwise; gate/up in the reference layout [E, d, I].
+__global__ void bwd_pack_w1cat_kernel(const uint16_t* __restrict__ gate, const uint16_t* __restrict__ up, int E,
+                                      int d, int I, int kI, uint16_t* __restrict__ out) {
+  const int64_t total = static_cast<int64_t>(E) * d * 2 * kI;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int k = static_cast<int>(idx % (2 * kI));
+    const int64_t row = idx / (2 * kI);  // e * d + n
+    uint16_t v = 0;
+    if (k < I)
+      v = gate[row * I + k];
+    else if (k >= kI && k < kI + I)
+      v = up[row * I + (k - kI)];
+    out[idx] = v;
+  }
+}
+
+// Router backward, one warp per token row: selection softmax, load-balance
+// softmax, optional upstream score gradient, softplus.  Lanes own columns
+// lane, lane + 32, ...; the row's k selected experts are distinct.
+template <int NQ>
+__global__ void bwd_router_kernel(const BwdRouterArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int E = a.num_experts, k = a.top_k;
+  // eligible expert count m (resident experts, or E)
+  int m = E;
+  if (a.resident != nullptr) {
+    int cnt = 0;
+    for (int c = lane; c < E; c += 32) cnt += a.resident[c] ? 1 : 0;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) cnt += __shfl_xor_sync(0xFFFFFFFFu, cnt, off);
+    m = cnt;
+  }
+  const float g_aux = a.d_aux != nullptr ? bf16_to_f32(*a.d_aux) : 0.0f;
+  const float gs = bfr(g_aux * bfr(static_cast<float>(m)));  // d(sum) = d_aux * eligible
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); t < a.tokens;
+       t += nwarps) {
+    const uint16_t* srow = a.scores + t * E;
+    float s[NQ], acc[NQ];
+    bool ok[NQ];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      const int c = lane + 32 * q;
+      ok[q] = c < E && (a.resident == nullptr || a.resident[c] != 0);
+      s[q] = c < E ? bf16_to_f32(srow[c]) : 0.0f;
+      acc[q] = 0.0f;
+      if (ok[q]) mx = fmaxf(mx, -s[q]);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+    // ---- load balance: p = bf16(softmax(-s)), d_p = bf16(bf16(gs * f_e) / T)
+    if (a.d_aux != nullptr) {
+      float e[NQ], sum = 0.0f;
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        e[q] = ok[q] ? expf(-s[q] - mx) : 0.0f;
+        sum += e[q];
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, off);
+      float p[NQ], dp[NQ], dot = 0.0f;
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        const int c = lane + 32 * q;
+        p[q] = ok[q] ? bfr(e[q] / sum) : 0.0f;
+        const float f = c < E ? bfr(a.fractions[c]) : 0.0f;
+        dp[q] = ok[q] ? bfr(bfr(gs * f) / static_cast<float>(a.tokens)) : 0.0f;
+        dot += p[q] * dp[q];
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) dot += __shfl_xor_sync(0xFFFFFFFFu, dot, off);
+#pragma unroll
+      for (int q = 0; q < NQ; ++q)
+        if (ok[q]) acc[q] -= bfr(p[q] * (dp[q] - dot));
+    }
+    // ---- selection softmax: w = softmax(-s_sel), d_w from the experts
+    float w = 0.0f, dw = 0.0f;
+    int id = -1;
+    if (lane < k) {
+      id = static_cast<int>(a.ids[t * k + lane]);
+      w = bf16_to_f32(a.weights[t * k + lane]);
+      dw = bfr(a.dw[t * k + lane]);
+    }
+    float wdw = w * dw;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) wdw += __shfl_xor_sync(0xFFFFFFFFu, wdw, off);
+    const float dsel = lane < k ? -bfr(w * (dw - wdw)) : 0.0f;
+    for (int j = 0; j < k; ++j) {
+      const int cj = __shfl_sync(0xFFFFFFFFu, id, j);
+      const float vj = __shfl_sync(0xFFFFFFFFu, dsel, j);
+#pragma unroll
+      for (int q = 0; q < NQ; ++q)
+        if (lane + 32 * q == cj) acc[q] += vj;
+    }
+    // ---- upstream score gradient, softplus, store
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      const int c = lane + 32 * q;
+      if (c < E) {
+        float ds = acc[q];
+        if (a.d_scores != nullptr) ds += bf16_to_f32(a.d_scores[t * E + c]);
+        ds = bfr(ds);
+        float dl = ds;
+        if (a.logits != nullptr) {
+          const float x = bf16_to_f32(a.logits[t * E + c]);
+          if (!(x > 20.0f)) dl = ds * sigmoidf_(x);
+        }
+        a.d_logits[t * E + c] = bfbits(dl);
+      }
+    }
+  }
+}
+
+int launch_bwd_gather(const uint16_t* x, const uint16_t* du, const int* src_row, const uint16_t* sorted_w, int64_t P,
+                      int d, uint16_t* x_sorted, uint16_t* dy_sorted, cudaStream_t stream) {
+  if (d % 8 != 0) return SPX_ERR_UNSUPPORTED;
+  bwd_gather_kernel<<<grid_for(P * (d / 8), 256), 256, 0, stream>>>(x, du, src_row, sorted_w, P, d, x_sorted,
+                                                                    dy_sorted);
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+int launch_bwd_swiglu(const uint16_t* gu, int ld_gu, int c, const uint16_t* dhp, int ld_dhp,
+                      const uint16_t* sorted_w, const int* order, int64_t P, int I, int kI, uint16_t* h_sorted,
+                      uint16_t* dgu, float* dw_pair, cudaStream_t stream) {
+  bwd_swiglu_kernel<<<grid_for(P, 8), 256, 0, stream>>>(gu, ld_gu, c, dhp, ld_dhp, sorted_w, order, P, I, kI,
+                                                        h_sorted, dgu, dw_pair);
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+int launch_bwd_pack_w1cat(const uint16_t* gate, const uint16_t* up, int E, int d, int I, int kI, uint16_t* out,
+                          cudaStream_t stream) {
+  const int64_t total = static_cast<int64_t>(E) * d * 2 * kI;
+  bwd_pack_w1cat_kernel<<<grid_for(total, 256), 256, 0, stream>>>(gate, up, E, d, I, kI, out);
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+int launch_bwd_router(const BwdRouterArgs& a, cudaStream_t stream) {
+  if (a.tokens <= 0) return SPX_OK;
+  if (a.top_k > 32 || a.num_experts > 1024) return SPX_ERR_UNSUPPORTED;
+  const int grid = grid_for(a.tokens, 8);
+  const int nq = (a.num_experts + 31) / 32;
+  if (nq <= 8)
+    bwd_router_kernel<8><<<grid, 256, 0, stream>>>(a);
+  else
+    bwd_router_kernel<32><<<grid, 256, 0, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+}  // namespace spx

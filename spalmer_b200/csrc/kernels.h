@@ -194,4 +194,29 @@ int launch_pack_w2(const uint16_t* down, int experts, int inter, int d, int kp, 
                    cudaStream_t stream);
 int launch_pad_rows(const uint16_t* src, int64_t rows, int cols, int ld_out, uint16_t* out, cudaStream_t stream);
 
+// Backward (backward.cu).
+struct BwdRouterArgs {
+  const uint16_t* scores;     // [T, E] router scores (BF16)
+  const uint16_t* logits;     // [T, E] router logits, or null (identity score transform)
+  const int64_t* ids;         // [T, k]
+  const uint16_t* weights;    // [T, k] routing weights (BF16)
+  const float* dw;            // [T, k] gradient of the routing weights
+  const float* fractions;     // [E] expert utilization (pairs / P)
+  const uint8_t* resident;    // [E] or null
+  const uint16_t* d_aux;      // device BF16 scalar, or null (no load-balance gradient)
+  const uint16_t* d_scores;   // [T, E] upstream gradient of router_scores, or null
+  uint16_t* d_logits;         // [T, E] out
+  int64_t tokens;
+  int num_experts;
+  int top_k;
+};
+int launch_bwd_gather(const uint16_t* x, const uint16_t* du, const int* src_row, const uint16_t* sorted_w, int64_t P,
+                      int d, uint16_t* x_sorted, uint16_t* dy_sorted, cudaStream_t stream);
+int launch_bwd_swiglu(const uint16_t* gu, int ld_gu, int c, const uint16_t* dhp, int ld_dhp,
+                      const uint16_t* sorted_w, const int* order, int64_t P, int I, int kI, uint16_t* h_sorted,
+                      uint16_t* dgu, float* dw_pair, cudaStream_t stream);
+int launch_bwd_pack_w1cat(const uint16_t* gate, const uint16_t* up, int E, int d, int I, int kI, uint16_t* out,
+                          cudaStream_t stream);
+int launch_bwd_router(const BwdRouterArgs& a, cudaStream_t stream);
+
 }  // namespace spx

@@ -517,10 +517,13 @@ class B200MicroExpertChannelMixer(nn.Module):
         if torch.is_grad_enabled() and (
             hidden_states.requires_grad or any(p.requires_grad for p in self.parameters())
         ):
-            raise NotImplementedError(
-                "the B200 micro-expert layer implements the forward pass only; call it under "
-                "torch.no_grad() or torch.inference_mode()"
-            )
+            if router_logits is not None:
+                raise ValueError("router_logits injection checks the forward only; run it without gradients")
+            return self._forward_autograd(hidden_states)
+        return self._forward_native(hidden_states, router_logits)
+
+    def _forward_native(self, hidden_states: Tensor, router_logits: Tensor | None) -> ChannelMixerOutput:
+        config = self.config
         if not hidden_states.is_cuda:
             raise RuntimeError("the B200 micro-expert layer requires CUDA hidden states")
         if hidden_states.dtype != torch.bfloat16:
@@ -606,6 +609,165 @@ class B200MicroExpertChannelMixer(nn.Module):
             "expert_group_global_max_counterfactual_padding_amplification": ratios[1],
         }
         return ChannelMixerOutput(update=update, state=None, auxiliary_loss=aux[0], metrics=metrics)
+
+
+    # ---- training: forward through the native kernels, backward through spx_layer_backward
+    def _trainable(self) -> list[tuple[str, Tensor]]:
+        named = dict(self.named_parameters())
+        keys = ["router.proj.weight", "router.proj.bias", "experts.gate_proj", "experts.up_proj",
+                "experts.down_proj", "shared.gate_projection.weight", "shared.up_projection.weight",
+                "shared.down_projection.weight"]
+        return [(k, named[k]) for k in keys if k in named]
+
+    def _forward_autograd(self, hidden_states: Tensor) -> ChannelMixerOutput:
+        if not hidden_states.is_cuda:
+            raise RuntimeError("the B200 micro-expert layer requires CUDA hidden states")
+        lanes = self._lanes(hidden_states.device)
+        if lanes is not None and bool(lanes.any()):
+            raise NativeExpertPrecisionError(
+                "provider spx_sm100_grouped has no backward for mxfp8 experts; train with BF16 experts"
+            )
+        named = self._trainable()
+        holder: dict[str, Any] = {}
+        update, aux, scores = _LayerFunction.apply(self, holder, [k for k, _ in named], hidden_states,
+                                                   *[p for _, p in named])
+        metrics = dict(holder["metrics"])
+        metrics["router_scores"] = scores
+        return ChannelMixerOutput(update=update, state=None, auxiliary_loss=aux, metrics=metrics)
+
+    def _backward_native(self, x: Tensor, ids: Tensor, weights: Tensor, scores: Tensor, d_update: Tensor,
+                         d_aux: Tensor | None, d_scores: Tensor | None) -> dict[str, Tensor]:
+        """Gradients of x and of every parameter (``spx_layer_backward`` for the
+        routed experts and the router scores; library GEMMs for the router's
+        and the experts' weight gradients and for the shared SwiGLU)."""
+
+        import torch.nn.functional as F
+
+        config = self.config
+        device = x.device
+        T, d = x.shape
+        k = ids.shape[-1]
+        E, I = config.num_experts, config.resolved_inter_dim
+        P = T * k
+        kI = -(-I // 64) * 64
+        lib = _lib.load()
+        dims = layer_dims(config, T, k)
+        packed = self._packed(device, T, k)
+        nbytes = _lib.ctypes.c_size_t()
+        _lib.check(lib.spx_layer_backward_sizes(dims, nbytes), "spx_layer_backward_sizes")
+        ws = torch.empty(nbytes.value, dtype=torch.uint8, device=device)
+        d_hidden = torch.empty(T, d, dtype=torch.bfloat16, device=device)
+        d_logits = torch.empty(T, E, dtype=torch.bfloat16, device=device)
+        x_sorted = torch.empty(P, d, dtype=torch.bfloat16, device=device)
+        h_sorted = torch.empty(P, I, dtype=torch.bfloat16, device=device)
+        dy_sorted = torch.empty(P, d, dtype=torch.bfloat16, device=device)
+        dgu = torch.empty(P, 2 * kI, dtype=torch.bfloat16, device=device)
+        counts = torch.empty(E, dtype=torch.int32, device=device)
+        residency = self.residency
+        mask = None if residency.is_full else residency.resident_mask.to(device=device).contiguous()
+        lut = softplus_table(device) if config.router_score_transform == "softplus" else None
+        pw = _lib.PackedWeights(
+            router_weight=_lib.ptr(packed["router_weight"]),
+            router_bias=_lib.ptr(packed["router_bias"]),
+            expert_w1=_lib.ptr(packed["expert_w1"]),
+            expert_w2=_lib.ptr(packed["expert_w2"]),
+            shared_w1=_lib.ptr(packed["shared_w1"]),
+            shared_w2=_lib.ptr(packed["shared_w2"]),
+            softplus_table=_lib.ptr(lut),
+            resident_mask=_lib.ptr(mask),
+        )
+        gate = self.experts.gate_proj.detach().contiguous()
+        up = self.experts.up_proj.detach().contiguous()
+        down = self.experts.down_proj.detach().contiguous()
+        du = d_update.reshape(T, d).to(torch.bfloat16).contiguous()
+        dsc = None if d_scores is None else d_scores.reshape(T, E).to(torch.bfloat16).contiguous()
+        dax = None if d_aux is None else d_aux.reshape(1).to(torch.bfloat16).contiguous()
+        gr = _lib.LayerGrads(
+            expert_ids=ids.data_ptr(), routing_weights=weights.data_ptr(), router_scores=scores.data_ptr(),
+            gate_proj=gate.data_ptr(), up_proj=up.data_ptr(), down_proj=down.data_ptr(),
+            d_update=du.data_ptr(), d_scores=_lib.ptr(dsc), d_aux=_lib.ptr(dax),
+            d_hidden_experts=d_hidden.data_ptr(), d_logits=d_logits.data_ptr(), x_sorted=x_sorted.data_ptr(),
+            h_sorted=h_sorted.data_ptr(), dy_sorted=dy_sorted.data_ptr(), dgu_sorted=dgu.data_ptr(),
+            expert_counts=counts.data_ptr(),
+        )
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(lib.spx_layer_backward(dims, pw, x.data_ptr(), gr, ws.data_ptr(), stream), "spx_layer_backward")
+
+        grads: dict[str, Tensor] = {}
+        w_router = self.router.proj.weight
+        grads["router.proj.weight"] = d_logits.t() @ x
+        if self.router.proj.bias is not None:
+            grads["router.proj.bias"] = d_logits.float().sum(0).to(torch.bfloat16)
+        dx = d_hidden.float() + (d_logits @ w_router.detach()).float()
+        offs = torch.cumsum(counts, 0, dtype=torch.int32)
+        d_w1 = _grouped_wgrad(x_sorted, dgu, counts, offs)
+        grads["experts.gate_proj"] = d_w1[:, :, :I].contiguous()
+        grads["experts.up_proj"] = d_w1[:, :, kI:kI + I].contiguous()
+        grads["experts.down_proj"] = _grouped_wgrad(h_sorted, dy_sorted, counts, offs)
+        if self.shared is not None:
+            sh = self.shared
+            ws_ = [sh.gate_projection.weight, sh.up_projection.weight, sh.down_projection.weight]
+            with torch.enable_grad():
+                xs = x.detach().requires_grad_(True)
+                leaves = [w.detach().requires_grad_(True) for w in ws_]
+                out = F.linear(F.silu(F.linear(xs, leaves[0])) * F.linear(xs, leaves[1]), leaves[2])
+                g = torch.autograd.grad(out, [xs] + leaves, du)
+            dx = dx + g[0].float()
+            grads["shared.gate_projection.weight"] = g[1]
+            grads["shared.up_projection.weight"] = g[2]
+            grads["shared.down_projection.weight"] = g[3]
+        grads["x"] = dx.to(torch.bfloat16)
+        return grads
+
+
+def _grouped_wgrad(a_sorted: Tensor, b_sorted: Tensor, counts: Tensor, offs: Tensor) -> Tensor:
+    """Per expert ``a_e^T @ b_e`` over the expert's sorted rows ([E, a_cols, b_cols], BF16).
+
+    One grouped library GEMM (``torch._grouped_mm``, groups along K) when the
+    installed PyTorch provides it for this device, else one GEMM per expert.
+    """
+
+    E = counts.numel()
+    if hasattr(torch, "_grouped_mm"):
+        try:
+            return torch._grouped_mm(a_sorted.t(), b_sorted, offs=offs)
+        except (RuntimeError, TypeError, NotImplementedError):
+            pass
+    out = torch.zeros(E, a_sorted.shape[1], b_sorted.shape[1], dtype=a_sorted.dtype, device=a_sorted.device)
+    ends = offs.tolist()
+    start = 0
+    for e, end in enumerate(ends):
+        if end > start:
+            out[e] = a_sorted[start:end].t() @ b_sorted[start:end]
+        start = end
+    return out
+
+
+class _LayerFunction(torch.autograd.Function):
+    """Autograd node of one layer: native forward, native backward."""
+
+    @staticmethod
+    def forward(ctx, mixer, holder, names, hidden_states, *params):
+        out = mixer._forward_native(hidden_states, None)
+        m = out.metrics
+        holder["metrics"] = m
+        ctx.mixer = mixer
+        ctx.names = names
+        ctx.shape = hidden_states.shape
+        x = hidden_states.reshape(-1, hidden_states.shape[-1]).contiguous()
+        k = m["expert_ids"].shape[-1]
+        ctx.save_for_backward(x, m["expert_ids"].reshape(-1, k), m["routing_weights"].reshape(-1, k),
+                              m["router_scores"].reshape(x.shape[0], -1))
+        ctx.mark_non_differentiable(m["expert_ids"], m["routing_weights"])
+        return out.update, out.auxiliary_loss, m["router_scores"]
+
+    @staticmethod
+    def backward(ctx, d_update, d_aux, d_scores):
+        x, ids, weights, scores = ctx.saved_tensors
+        if d_update is None:
+            d_update = torch.zeros(ctx.shape, dtype=torch.bfloat16, device=x.device)
+        grads = ctx.mixer._backward_native(x, ids, weights, scores, d_update, d_aux, d_scores)
+        return (None, None, None, grads["x"].reshape(ctx.shape), *[grads[n] for n in ctx.names])
 
 
 MicroExpertChannelMixer = B200MicroExpertChannelMixer

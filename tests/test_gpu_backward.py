@@ -1,0 +1,103 @@
+"""Training through the layer: gradients of the native backward (spx_layer_backward
+plus library GEMMs for the weight gradients) against the reference's own
+gradients (golden fixtures) and against the autograd oracle on the same
+routing, at both batch classes."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import mixer_autograd as MA
+from spalmer_b200 import B200MicroExpertChannelMixer, MicroExpertsConfig
+from tests.helpers import build_mixer, from_bits
+from tests.test_backward_oracle import CASES, load_backward_case, relnorm
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+# BF16 gradients summed in different orders (and, where a router logit rounds
+# differently on the GPU, a token routed elsewhere): relative L2 error bound.
+GRAD_RTOL = 3e-2
+
+
+def train_step(mixer, x: torch.Tensor, d_update: torch.Tensor, d_aux: float, d_scores=None):
+    mixer.zero_grad(set_to_none=True)
+    xg = x.detach().clone().requires_grad_(True)
+    out = mixer(xg)
+    outs = [out.update, out.auxiliary_loss]
+    grads = [d_update, torch.tensor(d_aux, dtype=torch.bfloat16, device=x.device)]
+    if d_scores is not None:
+        outs.append(out.metrics["router_scores"])
+        grads.append(d_scores)
+    torch.autograd.backward(outs, grads)
+    got = {"x": xg.grad}
+    for name, p in mixer.named_parameters():
+        if p.grad is not None:
+            got[name] = p.grad
+    return out, got
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_gradients_match_reference(name):
+    arrays, meta = load_backward_case(name)
+    mixer = build_mixer(meta, DEV).train()
+    batch, seq = meta["shape"]
+    d = meta["config"]["d_model"]
+    x = from_bits(arrays["x"], DEV).reshape(batch, seq, d)
+    d_update = from_bits(arrays["d_update"], DEV).reshape(batch, seq, d)
+    out, got = train_step(mixer, x, d_update, meta["d_aux"])
+    ids = out.metrics["expert_ids"].reshape(-1, meta["config"]["active_experts"]).cpu().numpy()
+    assert (ids == arrays["expert_ids"]).all(axis=1).mean() > 0.98  # routing as the reference's, bar rounding
+    assert set(meta["grads"]) <= set(got)
+    for key in meta["grads"]:
+        want = from_bits(arrays["grad__" + key])
+        assert relnorm(got[key].cpu(), want) < GRAD_RTOL, (key, relnorm(got[key].cpu(), want))
+    assert relnorm(got["x"].reshape(-1, d).cpu(), from_bits(arrays["grad_x"])) < GRAD_RTOL
+
+
+@pytest.mark.parametrize(
+    "cfg,shape",
+    [
+        (dict(d_model=256, num_experts=200, expert_inter_dim=64, shared_inter_dim=256, active_experts=8), (2, 1024)),
+        (dict(d_model=128, num_experts=200, expert_inter_dim=32, shared_inter_dim=0, active_experts=4), (1, 192)),
+        (dict(d_model=64, num_experts=24, expert_inter_dim=80, shared_inter_dim=64, active_experts=3,
+              router_score_transform="identity"), (2, 300)),
+    ],
+    ids=["m10_shape", "decode_no_shared", "identity_odd_inter"],
+)
+def test_gradients_match_oracle_on_same_routing(cfg, shape):
+    config = MicroExpertsConfig(**cfg)
+    torch.manual_seed(0)
+    mixer = B200MicroExpertChannelMixer(config).to(torch.bfloat16).to(DEV).train()
+    batch, seq = shape
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(batch, seq, config.d_model, generator=g).to(torch.bfloat16)
+    d_update = (0.05 * torch.randn(batch, seq, config.d_model, generator=g)).to(torch.bfloat16)
+    d_scores = (0.01 * torch.randn(batch, seq, config.num_experts, generator=g)).to(torch.bfloat16)
+    out, got = train_step(mixer, x.to(DEV), d_update.to(DEV), 0.5, d_scores.to(DEV))
+    k = config.active_experts
+    ids = out.metrics["expert_ids"].reshape(-1, k).cpu()
+    sd = {name: p.detach().cpu() for name, p in mixer.named_parameters()}
+    params = {name: sd[name] for name in MA.PARAM_NAMES if name in sd}
+    want = MA.gradients(params, x.reshape(-1, config.d_model), k, d_update.reshape(-1, config.d_model), 0.5,
+                        d_scores=d_scores.reshape(-1, config.num_experts), ids=ids,
+                        identity_scores=config.router_score_transform == "identity")
+    for key, w in want.items():
+        gk = got[key].reshape(w.shape).cpu()
+        assert relnorm(gk, w) < GRAD_RTOL, (key, relnorm(gk, w))
+
+
+def test_training_refuses_mxfp8_experts():
+    from spalmer_b200.native import NativeExpertPrecisionError
+    from tests.helpers import mxfp8_config, mxfp8_experts, set_mxfp8_lanes
+
+    config = mxfp8_config(d_model=128, num_experts=32, expert_inter_dim=64, active_experts=4)
+    torch.manual_seed(0)
+    mixer = B200MicroExpertChannelMixer(config).to(torch.bfloat16).to(DEV).train()
+    set_mxfp8_lanes(mixer, mxfp8_experts(config.num_experts, 0.25))
+    x = torch.randn(1, 64, 128, device=DEV).to(torch.bfloat16)
+    with pytest.raises(NativeExpertPrecisionError):
+        mixer(x)
+    with torch.no_grad():
+        mixer(x)  # inference still runs both lanes

@@ -38,11 +38,13 @@ def test_shared_router_validation_mirrors_reference():
     assert layer1.router is layer2.router and layer1.experts is not layer2.experts
 
 
-def test_forward_fails_loudly_off_gpu_and_under_autograd():
+def test_forward_fails_loudly_off_gpu_with_and_without_autograd():
     mixer = B200MicroExpertChannelMixer(small_config()).to(torch.bfloat16)
     x = torch.randn(1, 4, 64, dtype=torch.bfloat16)
-    with pytest.raises(NotImplementedError):
-        mixer(x)  # parameters require grad: no backward implementation
+    with pytest.raises(RuntimeError, match="CUDA"):
+        mixer(x)  # the training path has no CPU fallback either
+    with pytest.raises(ValueError, match="router_logits"):
+        mixer(x, router_logits=torch.zeros(1, 4, 16, dtype=torch.bfloat16))
     with torch.no_grad(), pytest.raises(RuntimeError, match="CUDA"):
         mixer(x)
     with torch.no_grad(), pytest.raises(ValueError):
