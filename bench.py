@@ -52,6 +52,10 @@ CONFIGS = {
     "decode": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
                             active_experts=8), batch=1, seq=64, cpu_sample=64, mxfp8_fraction=0.10,
                    decode_layers=16, decode_tokens=(1, 8, 64)),
+    # Training step (forward + backward) of the 100M-shape layer, BF16 experts
+    # (the MXFP8 lane has no backward); loss = sum(update * dU) + aux.
+    "m100_train": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
+                                active_experts=8), batch=64, seq=1024, cpu_sample=256, train=True),
     # 10M-preset shape.
     "m10": dict(cfg=dict(d_model=256, num_experts=200, expert_inter_dim=64, shared_inter_dim=256,
                          active_experts=8), batch=32, seq=512, cpu_sample=4096),
@@ -659,6 +663,137 @@ def run_decode(args) -> None:
         dist.destroy_process_group()
 
 
+def run_train(args) -> None:
+    """One training step of the layer per timed step: forward (native kernels),
+    then backward (spx_layer_backward for the routed experts and router
+    scores; library GEMMs for the weight gradients, the router's input
+    gradient and the shared SwiGLU).  value = tokens / step time; data-parallel
+    replicas for N > 1 (no gradient all-reduce: the layer's own work only)."""
+
+    world, rank, local = init_dist()
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    spec = CONFIGS[args.config]
+    batch, seq = spec["batch"], spec["seq"]
+    tokens = batch * seq
+    mixer, _ = build_mixer(spec, device)
+    mixer.train()
+    config = mixer.config
+    d = config.d_model
+    gen = torch.Generator().manual_seed(1 + rank)
+    x_host = torch.randn(batch, seq, d, generator=gen).to(torch.bfloat16).pin_memory()
+    du_host = (0.05 * torch.randn(batch, seq, d, generator=gen)).to(torch.bfloat16).pin_memory()
+    x_bufs = [x_host.to(device), x_host.roll(1, dims=0).to(device)]
+    du = du_host.to(device)
+    one = torch.ones((), dtype=torch.bfloat16, device=device)
+
+    def step(x):
+        mixer.zero_grad(set_to_none=True)
+        xg = x.detach().requires_grad_(True)
+        out = mixer(xg)
+        torch.autograd.backward([out.update, out.auxiliary_loss], [du, one])
+        return xg.grad
+
+    for i in range(args.warmup):
+        step(x_bufs[i % 2])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    K = args.steps
+    sampler = ClockSampler(local)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(K):
+        step(x_bufs[i % 2])
+    t1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = t0.elapsed_time(t1) / K
+    # forward alone, same inputs, for the split
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    with torch.no_grad():
+        f0.record()
+        for i in range(K):
+            mixer(x_bufs[i % 2])
+        f1.record()
+    torch.cuda.synchronize()
+    fwd_ms = f0.elapsed_time(f1) / K
+    # e2e: pinned H2D of the step's tokens and upstream gradient, the step, D2H of the input gradient
+    gx_host = torch.empty(batch, seq, d, dtype=torch.bfloat16).pin_memory()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(K):
+        x_bufs[0].copy_(x_host, non_blocking=True)
+        du.copy_(du_host, non_blocking=True)
+        gx = step(x_bufs[0])
+        gx_host.copy_(gx, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([ms, fwd_ms, e0.elapsed_time(e1) / K], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, fwd_ms, e2e_ms = (float(v) for v in t)
+    if rank == 0:
+        pk = peaks()
+        fl = layer_flops(spec["cfg"], tokens)
+        step_flops = 3.0 * sum(fl.values())  # forward + backward (input and weight gradients)
+        line = {
+            "metric": METRIC + " (training step: forward + backward)", "value": world * tokens / (ms / 1e3),
+            "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) hidden states and upstream gradients, seeded random-init weights)",
+            "config": {**workload_config(args.config, world),
+                       "workload": "m100_train: SPALMER micro-expert layer forward + backward"},
+            "forward_ms": fwd_ms, "backward_ms": ms - fwd_ms,
+            "e2e": {"value": world * tokens / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 2 * tokens * d * 2, "d2h_bytes_per_step": tokens * d * 2},
+            "gpu_launches": K * (14 + 11),
+            "roofline": {"bound": "tensor", "kernel": "whole step (3x the forward's GEMM FLOPs)",
+                         "achieved": step_flops / (ms / 1e3) / 1e12, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "traffic": None, "peak_source": pk["source"]},
+            "clocks": clocks,
+        }
+        line["roofline"]["frac"] = line["roofline"]["achieved"] / line["roofline"]["peak"]
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_train_baseline(spec, mixer)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def cpu_train_baseline(spec: dict, mixer) -> dict:
+    """The reference's training step restated in PyTorch autograd on the host
+    cores (oracle/mixer_autograd.py), on a bounded token sample."""
+
+    from oracle import mixer_autograd as MA
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    sample = spec["cpu_sample"]
+    d = spec["cfg"]["d_model"]
+    sd = {n: p.detach().cpu() for n, p in mixer.named_parameters()}
+    params = {n: sd[n] for n in MA.PARAM_NAMES if n in sd}
+    gen = torch.Generator().manual_seed(7)
+    x = torch.randn(sample, d, generator=gen).to(torch.bfloat16)
+    du = (0.05 * torch.randn(sample, d, generator=gen)).to(torch.bfloat16)
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        MA.gradients(params, x, spec["cfg"]["active_experts"], du, 1.0)
+        times.append(time.perf_counter() - t0)
+    sec = sorted(times)[1]
+    return {"value": sample / sec, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{sample} tokens, forward + backward through PyTorch CPU autograd, median of 3"}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -676,6 +811,8 @@ def main() -> None:
         run_ep(args)
     elif CONFIGS[args.config].get("decode_layers"):
         run_decode(args)
+    elif CONFIGS[args.config].get("train"):
+        run_train(args)
     else:
         run_ours(args)
 

@@ -70,64 +70,104 @@ __global__ void bwd_gather_kernel(const uint16_t* __restrict__ x, const uint16_t
   }
 }
 
-// SwiGLU backward, one warp per sorted pair row p.  gu holds the recomputed
-// pre-activations in the forward GEMM1's chunk layout (chunk n: c gate
-// columns, then c up columns), dhp = bf16(dY_t @ D_e^T).  Writes h (forward
-// hidden row), [d_gate | d_up] with the up half at column kI (zero padded to
-// 2 kI), and d_w of the pair in pair order (order[p]).
+// SwiGLU backward.  gu holds the recomputed pre-activations in the forward
+// GEMM1's chunk layout (chunk n: c gate columns, then c up columns), dhp =
+// bf16(dY_t @ D_e^T).  Writes h (forward hidden row), [d_gate | d_up] with
+// the up half at column kI (zero padded to 2 kI), and d_w of the pair in pair
+// order (order[p]).  A row is handled by `lanes` consecutive threads of a
+// warp, 8 hidden columns (16-byte loads and stores) each; needs c % 8 == 0.
+__device__ __forceinline__ void swiglu_bwd8(const uint4& gv, const uint4& uv, const uint4& dv, float w,
+                                            uint4& hv, uint4& dgv, uint4& duv, float& part) {
+  const uint32_t G[4] = {gv.x, gv.y, gv.z, gv.w}, U[4] = {uv.x, uv.y, uv.z, uv.w}, D[4] = {dv.x, dv.y, dv.z, dv.w};
+  uint32_t H[4], DG[4], DU[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t hw = 0, dgw = 0, duw = 0;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const float g = half ? __uint_as_float(G[q] & 0xFFFF0000u) : __uint_as_float(G[q] << 16);
+      const float u = half ? __uint_as_float(U[q] & 0xFFFF0000u) : __uint_as_float(U[q] << 16);
+      const float dh1 = half ? __uint_as_float(D[q] & 0xFFFF0000u) : __uint_as_float(D[q] << 16);
+      const float sgm = sigmoidf_(g);
+      const float sg = bfr(g / (1.0f + expf(-g)));  // silu as the reference evaluates it
+      const float h = bfr(sg * u);
+      part += dh1 * h;
+      const float dh = bfr(dh1 * w);
+      const float dsg = bfr(dh * u);
+      const float du = bfr(dh * sg);
+      const float dg = bfr(dsg * (sgm * (1.0f + g * (1.0f - sgm))));
+      hw |= static_cast<uint32_t>(bfbits(h)) << (16 * half);
+      dgw |= static_cast<uint32_t>(bfbits(dg)) << (16 * half);
+      duw |= static_cast<uint32_t>(bfbits(du)) << (16 * half);
+    }
+    H[q] = hw;
+    DG[q] = dgw;
+    DU[q] = duw;
+  }
+  hv = make_uint4(H[0], H[1], H[2], H[3]);
+  dgv = make_uint4(DG[0], DG[1], DG[2], DG[3]);
+  duv = make_uint4(DU[0], DU[1], DU[2], DU[3]);
+}
+
 __global__ void bwd_swiglu_kernel(const uint16_t* __restrict__ gu, int ld_gu, int c, const uint16_t* __restrict__ dhp,
                                   int ld_dhp, const uint16_t* __restrict__ sorted_w, const int* __restrict__ order,
-                                  int64_t P, int I, int kI, uint16_t* __restrict__ h_sorted,
+                                  int64_t P, int I, int kI, int lanes, uint16_t* __restrict__ h_sorted,
                                   uint16_t* __restrict__ dgu, float* __restrict__ dw_pair) {
   const int lane = threadIdx.x & 31;
-  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); p < P; p += nwarps) {
-    const float w = bf16_to_f32(sorted_w[p]);
-    const uint16_t* grow = gu + p * ld_gu;
+  const int sub = lane % lanes;            // position within the row group
+  const int group = lane / lanes;          // row group within the warp
+  const int groups = 32 / lanes;
+  const unsigned gmask = (lanes == 32) ? 0xFFFFFFFFu : (((1u << lanes) - 1u) << (group * lanes));
+  const int64_t nslots = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5) * groups;
+  const int64_t slot0 = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * groups + group;
+  const int64_t iters = (P + nslots - 1) / nslots;  // uniform over the warp: every lane runs the shuffles
+  for (int64_t it = 0; it < iters; ++it) {
+    const int64_t p = slot0 + it * nslots;
+    const bool live = p < P;
     float part = 0.0f;
-    for (int i = lane; i < 2 * kI; i += 32) {
-      if (i < I) {
-        const int chunk = i / c, j = i - chunk * c;
-        const float g = bf16_to_f32(grow[chunk * 2 * c + j]);
-        const float u = bf16_to_f32(grow[chunk * 2 * c + c + j]);
-        const float dh1 = bf16_to_f32(dhp[p * ld_dhp + i]);
-        const float sgm = sigmoidf_(g);
-        const float sg = bfr(g / (1.0f + expf(-g)));  // silu as the reference evaluates it
-        const float h = bfr(sg * u);
-        part += dh1 * h;
-        const float dh = bfr(dh1 * w);
-        const float dsg = bfr(dh * u);
-        const float du = bfr(dh * sg);
-        const float dg = bfr(dsg * (sgm * (1.0f + g * (1.0f - sgm))));
-        h_sorted[p * I + i] = bfbits(h);
-        dgu[p * 2 * kI + i] = bfbits(dg);
-        dgu[p * 2 * kI + kI + i] = bfbits(du);
-      } else if (i < kI || i >= kI + I) {
-        dgu[p * 2 * kI + i] = 0;  // K padding of both halves
+    if (live) {
+      const float w = bf16_to_f32(sorted_w[p]);
+      const uint16_t* grow = gu + p * ld_gu;
+      for (int i = 8 * sub; i < 2 * kI; i += 8 * lanes) {
+        if (i < I) {
+          const int chunk = i / c, j = i - chunk * c;
+          const uint4 gv = *reinterpret_cast<const uint4*>(grow + chunk * 2 * c + j);
+          const uint4 uv = *reinterpret_cast<const uint4*>(grow + chunk * 2 * c + c + j);
+          const uint4 dv = *reinterpret_cast<const uint4*>(dhp + p * ld_dhp + i);
+          uint4 hv, dgv, duv;
+          swiglu_bwd8(gv, uv, dv, w, hv, dgv, duv, part);
+          *reinterpret_cast<uint4*>(h_sorted + p * I + i) = hv;
+          *reinterpret_cast<uint4*>(dgu + p * 2 * kI + i) = dgv;
+          *reinterpret_cast<uint4*>(dgu + p * 2 * kI + kI + i) = duv;
+        } else if (i < kI) {
+          // K padding of both halves
+          *reinterpret_cast<uint4*>(dgu + p * 2 * kI + i) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(dgu + p * 2 * kI + kI + i) = make_uint4(0, 0, 0, 0);
+        }
       }
     }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xFFFFFFFFu, part, off);
-    if (lane == 0) dw_pair[order[p]] = part;
+    for (int off = lanes / 2; off >= 1; off >>= 1) part += __shfl_xor_sync(gmask, part, off);
+    if (live && sub == 0) dw_pair[order[p]] = part;
   }
 }
 
 // [gate_e | up_e] concatenated along K for the input-gradient GEMM:
 // out[e][n][k] = gate[e][n][k] (k < I), up[e][n][k - kI] (kI <= k < kI + I),
-// 0 otherwise; gate/up in the reference layout [E, d, I].
+// 0 otherwise; gate/up in the reference layout [E, d, I] (I % 8 == 0: 16-byte moves).
 __global__ void bwd_pack_w1cat_kernel(const uint16_t* __restrict__ gate, const uint16_t* __restrict__ up, int E,
                                       int d, int I, int kI, uint16_t* __restrict__ out) {
-  const int64_t total = static_cast<int64_t>(E) * d * 2 * kI;
+  const int per_row = 2 * kI / 8;
+  const int64_t total = static_cast<int64_t>(E) * d * per_row;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int k = static_cast<int>(idx % (2 * kI));
-    const int64_t row = idx / (2 * kI);  // e * d + n
-    uint16_t v = 0;
+    const int k = static_cast<int>(idx % per_row) * 8;
+    const int64_t row = idx / per_row;  // e * d + n
+    uint4 v = make_uint4(0, 0, 0, 0);
     if (k < I)
-      v = gate[row * I + k];
+      v = __ldg(reinterpret_cast<const uint4*>(gate + row * I + k));
     else if (k >= kI && k < kI + I)
-      v = up[row * I + (k - kI)];
-    out[idx] = v;
+      v = __ldg(reinterpret_cast<const uint4*>(up + row * I + (k - kI)));
+    *reinterpret_cast<uint4*>(out + row * 2 * kI + k) = v;
   }
 }
 
@@ -240,14 +280,19 @@ int launch_bwd_gather(const uint16_t* x, const uint16_t* du, const int* src_row,
 int launch_bwd_swiglu(const uint16_t* gu, int ld_gu, int c, const uint16_t* dhp, int ld_dhp,
                       const uint16_t* sorted_w, const int* order, int64_t P, int I, int kI, uint16_t* h_sorted,
                       uint16_t* dgu, float* dw_pair, cudaStream_t stream) {
-  bwd_swiglu_kernel<<<grid_for(P, 8), 256, 0, stream>>>(gu, ld_gu, c, dhp, ld_dhp, sorted_w, order, P, I, kI,
-                                                        h_sorted, dgu, dw_pair);
+  if (c % 8 != 0 || I % 8 != 0 || ld_gu % 8 != 0 || ld_dhp % 8 != 0) return SPX_ERR_UNSUPPORTED;
+  int lanes = 1;  // threads per row: enough for 8 columns each, a power of two <= 32
+  while (lanes < 32 && 8 * lanes < kI) lanes <<= 1;
+  const int rows_per_block = 8 * (32 / lanes);
+  bwd_swiglu_kernel<<<grid_for(P, rows_per_block), 256, 0, stream>>>(gu, ld_gu, c, dhp, ld_dhp, sorted_w, order, P,
+                                                                     I, kI, lanes, h_sorted, dgu, dw_pair);
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 
 int launch_bwd_pack_w1cat(const uint16_t* gate, const uint16_t* up, int E, int d, int I, int kI, uint16_t* out,
                           cudaStream_t stream) {
-  const int64_t total = static_cast<int64_t>(E) * d * 2 * kI;
+  if (I % 8 != 0) return SPX_ERR_UNSUPPORTED;
+  const int64_t total = static_cast<int64_t>(E) * d * (2 * kI / 8);
   bwd_pack_w1cat_kernel<<<grid_for(total, 256), 256, 0, stream>>>(gate, up, E, d, I, kI, out);
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }

@@ -698,11 +698,10 @@ class B200MicroExpertChannelMixer(nn.Module):
         grads["router.proj.weight"] = d_logits.t() @ x
         if self.router.proj.bias is not None:
             grads["router.proj.bias"] = d_logits.float().sum(0).to(torch.bfloat16)
-        dx = d_hidden.float() + (d_logits @ w_router.detach()).float()
+        dx = torch.addmm(d_hidden, d_logits, w_router.detach())  # one rounding: d_hidden + d_logits @ W
         offs = torch.cumsum(counts, 0, dtype=torch.int32)
-        d_w1 = _grouped_wgrad(x_sorted, dgu, counts, offs)
-        grads["experts.gate_proj"] = d_w1[:, :, :I].contiguous()
-        grads["experts.up_proj"] = d_w1[:, :, kI:kI + I].contiguous()
+        grads["experts.gate_proj"] = _grouped_wgrad(x_sorted, dgu[:, :I], counts, offs)
+        grads["experts.up_proj"] = _grouped_wgrad(x_sorted, dgu[:, kI:kI + I], counts, offs)
         grads["experts.down_proj"] = _grouped_wgrad(h_sorted, dy_sorted, counts, offs)
         if self.shared is not None:
             sh = self.shared
@@ -712,11 +711,11 @@ class B200MicroExpertChannelMixer(nn.Module):
                 leaves = [w.detach().requires_grad_(True) for w in ws_]
                 out = F.linear(F.silu(F.linear(xs, leaves[0])) * F.linear(xs, leaves[1]), leaves[2])
                 g = torch.autograd.grad(out, [xs] + leaves, du)
-            dx = dx + g[0].float()
+            dx = dx + g[0]
             grads["shared.gate_projection.weight"] = g[1]
             grads["shared.up_projection.weight"] = g[2]
             grads["shared.down_projection.weight"] = g[3]
-        grads["x"] = dx.to(torch.bfloat16)
+        grads["x"] = dx
         return grads
 
 
@@ -732,7 +731,11 @@ def _grouped_wgrad(a_sorted: Tensor, b_sorted: Tensor, counts: Tensor, offs: Ten
         try:
             return torch._grouped_mm(a_sorted.t(), b_sorted, offs=offs)
         except (RuntimeError, TypeError, NotImplementedError):
-            pass
+            if not b_sorted.is_contiguous():  # a column slice: the grouped GEMM may want it dense
+                try:
+                    return torch._grouped_mm(a_sorted.t(), b_sorted.contiguous(), offs=offs)
+                except (RuntimeError, TypeError, NotImplementedError):
+                    pass
     out = torch.zeros(E, a_sorted.shape[1], b_sorted.shape[1], dtype=a_sorted.dtype, device=a_sorted.device)
     ends = offs.tolist()
     start = 0
