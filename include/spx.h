@@ -51,7 +51,7 @@
 extern "C" {
 #endif
 
-#define SPX_ABI_VERSION 4
+#define SPX_ABI_VERSION 5
 
 #define SPX_OK 0
 #define SPX_ERR_INVALID_ARG -1
@@ -249,6 +249,18 @@ int spx_surprise_calibration(const uint16_t* router_scores, const int64_t* exper
                              const float* token_nll, const uint8_t* valid, int64_t batch, int64_t seq,
                              int32_t num_experts, int32_t top_k, float* calibration, float* attributed_nll,
                              float* utilization, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The channel half of a block: h_out = h + update, update = the layer
+ * applied to channel_norm(h) (mESmaC/spalmer modeling.py:283-302 with
+ * nn/norm.py:28-31 RMSNorm).  The RMSNorm is one pass writing the normalised
+ * rows that every GEMM reads; the residual add runs in the combine.  Inputs
+ * as spx_layer_forward plus the norm weight [d] (BF16) and eps; `hidden` is
+ * the residual stream h; outputs as spx_layer_forward except that
+ * outputs->update may be NULL (then only hidden_out = bf16(h + update) is
+ * written) and injected logits are not accepted.  Same workspace. */
+int spx_block_channel_forward(const spx_layer_dims* dims, const spx_packed_weights* weights,
+                              const uint16_t* norm_weight, float eps, const uint16_t* hidden,
+                              const spx_layer_outputs* outputs, uint16_t* hidden_out, void* workspace, void* stream);
 
 /* ---- backward of the routed experts and the router scores
  * Reference: autograd through MicroExpertChannelMixer.forward

@@ -332,3 +332,23 @@ def isclose_bf16(a_bits: np.ndarray, b_bits: np.ndarray, rtol: float = 2e-2, ato
 
 
 __all__ = [name for name in dir() if not name.startswith("_") and name not in {"annotations", "math"}]
+
+
+def rms_norm(h_bits: np.ndarray, w_bits: np.ndarray, eps: float) -> np.ndarray:
+    """``RMSNorm.forward`` of ``nn/norm.py:28-31`` on BF16 rows (bits in, bits out):
+    variance in float32, ``rsqrt(variance + eps)`` cast to BF16, then the two
+    BF16 products ``h * r`` and ``* weight``.  The float32 sum runs in numpy's
+    pairwise order (the reference's order differs: ``r`` can move by one BF16
+    ulp when the variance lands within a float ulp of a rounding boundary)."""
+
+    h = bf16_bits_to_f32(h_bits)
+    var = np.square(h, dtype=np.float32).mean(axis=-1, keepdims=True, dtype=np.float32)
+    r = bf16_bits_to_f32(f32_to_bf16_bits((np.float32(1.0) / np.sqrt(var + np.float32(eps))).astype(np.float32)))
+    x = f32_to_bf16_bits((h * r).astype(np.float32))
+    return f32_to_bf16_bits((bf16_bits_to_f32(x) * bf16_bits_to_f32(w_bits)).astype(np.float32))
+
+
+def block_channel_forward(h_bits: np.ndarray, norm_w_bits: np.ndarray, eps: float, update_bits: np.ndarray):
+    """``hidden_states + channel_update`` of ``modeling.py:302`` in BF16 (bits)."""
+
+    return f32_to_bf16_bits((bf16_bits_to_f32(h_bits) + bf16_bits_to_f32(update_bits)).astype(np.float32))

@@ -7,6 +7,7 @@ kernels in ``libspx`` (``include/spx.h``).
 
 from spalmer_b200.config import MicroExpertsConfig
 from spalmer_b200.experts import (
+    B200ChannelBlock,
     B200MicroExpertChannelMixer,
     ChannelMixerOutput,
     ExpertPotentiationController,
@@ -14,6 +15,7 @@ from spalmer_b200.experts import (
     MicroExpertBank,
     MicroExpertChannelMixer,
     NativeExpertPrecisionError,
+    RMSNorm,
     SurpriseRouter,
     SwiGLU,
     dispatch,
@@ -21,6 +23,7 @@ from spalmer_b200.experts import (
 )
 
 __all__ = [
+    "B200ChannelBlock",
     "B200MicroExpertChannelMixer",
     "ChannelMixerOutput",
     "ExpertPotentiationController",
@@ -29,6 +32,7 @@ __all__ = [
     "MicroExpertChannelMixer",
     "MicroExpertsConfig",
     "NativeExpertPrecisionError",
+    "RMSNorm",
     "SurpriseRouter",
     "SwiGLU",
     "dispatch",

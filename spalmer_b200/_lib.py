@@ -50,9 +50,10 @@ EXPORTED = (
     "spx_surprise_calibration",
     "spx_layer_backward_sizes",
     "spx_layer_backward",
+    "spx_block_channel_forward",
 )
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 _vp = ctypes.c_void_p
 
@@ -219,6 +220,10 @@ def load() -> ctypes.CDLL:
         ),
         "spx_layer_backward_sizes": (ctypes.c_int, [P(LayerDims), P(ctypes.c_size_t)]),
         "spx_layer_backward": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, P(LayerGrads), _vp, _vp]),
+        "spx_block_channel_forward": (
+            ctypes.c_int,
+            [P(LayerDims), P(PackedWeights), _vp, ctypes.c_float, _vp, P(LayerOutputs), _vp, _vp, _vp],
+        ),
         "spx_mxfp8_mm_nt": (
             ctypes.c_int,
             [_vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp, _vp, ctypes.c_size_t, _vp],

@@ -115,7 +115,7 @@ MxPackSizes mx_pack_sizes(const Shape& s) {
 
 struct Layout {
   size_t small, tie_rows, lb_partial, lb_sum, chunk_hist, counts, starts, tiles, order, src_row, rank, sorted_w;
-  size_t hidden, y, shared_hidden, shared_out, x_pad, util, stats, ratios, aux;
+  size_t hidden, y, shared_hidden, shared_out, x_pad, x_norm, util, stats, ratios, aux;
   size_t x_q, x_sf, h_q, h_sf, tiles_mx;  // MXFP8 lane (empty otherwise)
   size_t total;
 };
@@ -145,6 +145,7 @@ Layout make_layout(const Shape& s) {
   L.shared_hidden = take(s.S > 0 ? 2 * static_cast<size_t>(s.T) * s.ksp : 0);
   L.shared_out = take(s.S > 0 ? 2 * static_cast<size_t>(s.T) * s.d : 0);
   L.x_pad = take(s.kd != s.d ? 2 * static_cast<size_t>(s.T) * s.kd : 0);
+  L.x_norm = take(2 * static_cast<size_t>(s.T) * s.kd);
   L.util = take(sizeof(float) * s.E);
   L.stats = take(sizeof(long long) * 6);
   L.ratios = take(sizeof(float) * 2);
@@ -312,7 +313,7 @@ DispatchArgs layer_dispatch_args(const Ctx& c, const spx_layer_dims* dims, const
 // K3: expert GEMM1 (+SwiGLU) and GEMM2 over the dispatched rows of `hidden`
 // (`xa` = hidden padded), both lanes; weighted rows land in Y (sorted order).
 int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hidden, const uint16_t* xa,
-                  const DispatchArgs& da) {
+                  const DispatchArgs& da, int64_t ld_hidden = 0) {
   const Shape& s = c.s;
   void* ws = c.ws;
   const Layout& L = c.L;
@@ -325,7 +326,8 @@ int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hid
   if (mx) {
     // Hidden states of the MXFP8 lane: E4M3 rows with their block scales
     // (per token, so every expert's gathered rows share them).
-    if ((rc = launch_mx_quantize_rows(hidden, s.T, s.d, s.d, s.kx, xq, s.kx, xsf, s.kx / kMxBlock, c.st)) != SPX_OK)
+    if ((rc = launch_mx_quantize_rows(hidden, s.T, s.d, ld_hidden > 0 ? ld_hidden : s.d, s.kx, xq, s.kx, xsf,
+                                      s.kx / kMxBlock, c.st)) != SPX_OK)
       return rc;
   }
   uint16_t* hid = at<uint16_t>(ws, L.hidden);
@@ -414,7 +416,8 @@ int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hid
 // the combine: out = bf16(shared + the token's k expert rows of y), written
 // to `out` (the layer update); otherwise `out` receives the shared output.
 int stage_shared(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, uint16_t* out,
-                 const uint16_t* y = nullptr, const int* rank = nullptr) {
+                 const uint16_t* y = nullptr, const int* rank = nullptr, const uint16_t* residual = nullptr,
+                 uint16_t* residual_out = nullptr) {
   const Shape& s = c.s;
   int rc = SPX_OK;
   uint16_t* hs = at<uint16_t>(c.ws, c.L.shared_hidden);
@@ -450,6 +453,8 @@ int stage_shared(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, 
   g.comb_rank = rank;
   g.comb_k = s.k;
   g.ldy = s.d;
+  g.comb_res = residual;
+  g.comb_res_out = residual_out;
   return launch_gemm(epi, g, ceil_div(s.T, kTileRows), s.gn_sd, c.st);
 }
 
@@ -730,6 +735,54 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
       c.mark(6);
     }
     if ((rc = launch_combine(y, da.rank, nullptr, so, s.T, s.d, s.k, out->update, c.st)) != SPX_OK) return rc;
+  }
+  c.mark(7);
+  return SPX_OK;
+}
+
+int spx_block_channel_forward(const spx_layer_dims* dims, const spx_packed_weights* w, const uint16_t* norm_weight,
+                              float eps, const uint16_t* hidden, const spx_layer_outputs* out, uint16_t* hidden_out,
+                              void* workspace, void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (out == nullptr || hidden == nullptr || hidden_out == nullptr || norm_weight == nullptr)
+    return SPX_ERR_INVALID_ARG;
+  if (workspace == nullptr) return SPX_ERR_WORKSPACE;
+  if (out->router_scores == nullptr || out->expert_ids == nullptr || out->routing_weights == nullptr)
+    return SPX_ERR_INVALID_ARG;
+  if (out->injected_logits != nullptr) return SPX_ERR_INVALID_ARG;  // the logits come from the normalised rows
+  if (int rc = check_layer_weights(s, dims, w, true, true, true); rc != SPX_OK) return rc;
+  if (!aligned16(hidden) || !aligned16(hidden_out) || !aligned16(norm_weight) || !aligned16(workspace) ||
+      (out->update != nullptr && !aligned16(out->update)))
+    return SPX_ERR_ALIGNMENT;
+  const Layout L = make_layout(s);
+  const Ctx c{s, L, workspace, static_cast<cudaStream_t>(stream), at<int>(workspace, L.small), out->stage_events};
+  int rc = SPX_OK;
+  c.mark(0);
+  // ---- channel_norm(h): the normalised rows, K-padded, feed every GEMM and the MXFP8 quantiser
+  uint16_t* xn = at<uint16_t>(workspace, L.x_norm);
+  if ((rc = launch_rmsnorm_rows(hidden, norm_weight, eps, s.T, s.d, xn, s.kd, c.st)) != SPX_OK) return rc;
+  if ((rc = stage_router_route(c, dims, w, xn, out)) != SPX_OK) return rc;
+  c.mark(2);
+  const DispatchArgs da = layer_dispatch_args(c, dims, w, out);
+  if ((rc = launch_dispatch(da, c.st)) != SPX_OK) return rc;
+  c.mark(3);
+  if ((rc = stage_experts(c, w, xn, xn, da, s.kd)) != SPX_OK) return rc;
+  // ---- update and the residual add h + update in the combine
+  uint16_t* y = at<uint16_t>(workspace, L.y);
+  if (fused_combine_ok(s)) {
+    if ((rc = stage_shared(c, w, xn, out->update, y, da.rank, hidden, hidden_out)) != SPX_OK) return rc;
+  } else {
+    uint16_t* so = nullptr;
+    if (s.S > 0) {
+      so = at<uint16_t>(workspace, L.shared_out);
+      if ((rc = stage_shared(c, w, xn, so)) != SPX_OK) return rc;
+    } else {
+      c.mark(6);
+    }
+    if ((rc = launch_combine_residual(y, da.rank, nullptr, so, hidden, s.T, s.d, s.k, out->update, hidden_out,
+                                      c.st)) != SPX_OK)
+      return rc;
   }
   c.mark(7);
   return SPX_OK;

@@ -300,7 +300,7 @@ __device__ __forceinline__ void run_epilogue_combine(const GemmArgs& a, uint32_t
     for (int j = 0; j < kCombineMaxK; ++j) pr[j] = __shfl_sync(0xFFFFFFFFu, rk[j], ri);
     const long long t = __shfl_sync(0xFFFFFFFFu, my_row, ri);
     if (ri < wrows) {
-      uint4 y0[kCombineMaxK], y1[kCombineMaxK];
+      uint4 y0[kCombineMaxK], y1[kCombineMaxK], r0, r1;
 #pragma unroll
       for (int j = 0; j < kCombineMaxK; ++j) {
         if (j < k) {
@@ -308,6 +308,11 @@ __device__ __forceinline__ void run_epilogue_combine(const GemmArgs& a, uint32_t
           if (ok0) y0[j] = __ldg(reinterpret_cast<const uint4*>(src));
           if (ok1) y1[j] = __ldg(reinterpret_cast<const uint4*>(src + 128));
         }
+      }
+      if (a.comb_res != nullptr) {
+        const uint16_t* res = a.comb_res + t * a.ldo + cb + j8 * 8;
+        if (ok0) r0 = __ldg(reinterpret_cast<const uint4*>(res));
+        if (ok1) r1 = __ldg(reinterpret_cast<const uint4*>(res + 128));
       }
 #pragma unroll
       for (int sl = 0; sl < 2; ++sl) {
@@ -323,7 +328,20 @@ __device__ __forceinline__ void run_epilogue_combine(const GemmArgs& a, uint32_t
           o.y = pack_bf16x2(acc[2], acc[3]);
           o.z = pack_bf16x2(acc[4], acc[5]);
           o.w = pack_bf16x2(acc[6], acc[7]);
-          *reinterpret_cast<uint4*>(out + t * a.ldo + cb + sl * 128 + j8 * 8) = o;
+          const int64_t at = t * a.ldo + cb + sl * 128 + j8 * 8;
+          if (out != nullptr) *reinterpret_cast<uint4*>(out + at) = o;
+          if (a.comb_res != nullptr) {
+            // the block's residual add: bf16(h + update), update already BF16
+            float hs[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            add_row8<false>(hs, sl == 0 ? r0 : r1, 1.0f);
+            add_row8<false>(hs, o, 1.0f);
+            uint4 ro;
+            ro.x = pack_bf16x2(hs[0], hs[1]);
+            ro.y = pack_bf16x2(hs[2], hs[3]);
+            ro.z = pack_bf16x2(hs[4], hs[5]);
+            ro.w = pack_bf16x2(hs[6], hs[7]);
+            *reinterpret_cast<uint4*>(a.comb_res_out + at) = ro;
+          }
         }
       }
     }
@@ -1034,7 +1052,10 @@ int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t
     case kEpiCombine:
       if (a.comb_y == nullptr || a.comb_rank == nullptr || a.comb_k < 1 || a.comb_k > kCombineMaxK ||
           (a.n_valid % 64) != 0 || (a.bn % 64) != 0 || (a.ldy % 8) != 0 || (a.ldo % 8) != 0 ||
-          (reinterpret_cast<uintptr_t>(a.comb_y) & 15u) != 0 || (reinterpret_cast<uintptr_t>(a.out) & 15u) != 0)
+          (reinterpret_cast<uintptr_t>(a.comb_y) & 15u) != 0 || (reinterpret_cast<uintptr_t>(a.out) & 15u) != 0 ||
+          (a.out == nullptr && a.comb_res == nullptr) ||
+          (a.comb_res != nullptr && (a.comb_res_out == nullptr || (reinterpret_cast<uintptr_t>(a.comb_res) & 15u) != 0 ||
+                                     (reinterpret_cast<uintptr_t>(a.comb_res_out) & 15u) != 0)))
         return SPX_ERR_INVALID_ARG;
       return launch_gemm_t<kEpiCombine, false>(a, grid_m, grid_n, stream);
     default:

@@ -132,6 +132,8 @@ struct GemmArgs {
   const uint16_t* comb_y;    // kEpiCombine: expert rows Y [P, ldy] in sorted order (weights applied)
   const int* comb_rank;      // kEpiCombine: sorted position of pair t*k+j
   int comb_k;                // kEpiCombine: pairs per token (<= kCombineMaxK)
+  const uint16_t* comb_res;  // kEpiCombine: residual stream [rows, ldo] or null; with it
+  uint16_t* comb_res_out;    //   comb_res_out = bf16(residual + update) (out may then be null)
   int64_t ldy;
   int* status;
 };
@@ -182,6 +184,15 @@ int launch_mx_quantize_b(int mode, const uint16_t* a, const uint16_t* b, int gro
 // update[t] = bf16(base[t] + sum_j rows_j) with rows_j = Y[rank[t*k + j]], or
 // bf16(Y[rank[t*k + j]] * w[t*k + j]) when pair weights are given (base: the
 // shared SwiGLU output or null).
+// combine with a residual add: update (if not null) = bf16(base + sum_j rows_j),
+// residual_out = bf16(residual + update).
+int launch_combine_residual(const uint16_t* y, const int* rank, const uint16_t* weights, const uint16_t* base,
+                            const uint16_t* residual, int64_t tokens, int d, int k, uint16_t* out,
+                            uint16_t* residual_out, cudaStream_t stream);
+// Channel RMSNorm of the block (nn/norm.py:28-31): x = bf16(bf16(h * bf16(rsqrt(mean(h^2) + eps))) * w),
+// rows of x written with stride ld_out (columns [d, ld_out) zeroed).
+int launch_rmsnorm_rows(const uint16_t* h, const uint16_t* w, float eps, int64_t rows, int d, uint16_t* out,
+                        int ld_out, cudaStream_t stream);
 int launch_combine(const uint16_t* y, const int* rank, const uint16_t* weights, const uint16_t* base, int64_t tokens,
                    int d, int k, uint16_t* out, cudaStream_t stream);
 // out[i] = src[index[i] / index_div] (BF16 rows of d elements).

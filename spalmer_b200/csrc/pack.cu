@@ -81,7 +81,8 @@ __global__ void pad_rows_kernel(const uint16_t* __restrict__ src, int64_t rows, 
 template <int KMAX, bool WEIGHTED>
 __global__ void combine_kernel(const uint16_t* __restrict__ y, const int* __restrict__ rank,
                                const uint16_t* __restrict__ weights, const uint16_t* __restrict__ base,
-                               int64_t tokens, int d, int k, uint16_t* __restrict__ out) {
+                               int64_t tokens, int d, int k, uint16_t* __restrict__ out,
+                               const uint16_t* __restrict__ residual, uint16_t* __restrict__ residual_out) {
   const int vec = d / 8;
   const int64_t total = tokens * vec;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
@@ -108,13 +109,22 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, const int* __rest
     uint16_t* oh = reinterpret_cast<uint16_t*>(&o);
 #pragma unroll
     for (int q8 = 0; q8 < 8; ++q8) oh[q8] = f32_to_bf16_rne(acc[q8]);
-    *reinterpret_cast<uint4*>(out + t * d + c) = o;
+    if (out != nullptr) *reinterpret_cast<uint4*>(out + t * d + c) = o;
+    if (residual != nullptr) {  // the block's residual add: bf16(h + update)
+      float hs[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      add_row8<false>(hs, __ldg(reinterpret_cast<const uint4*>(residual + t * d + c)), 1.0f);
+      add_row8<false>(hs, o, 1.0f);
+#pragma unroll
+      for (int q8 = 0; q8 < 8; ++q8) oh[q8] = f32_to_bf16_rne(hs[q8]);
+      *reinterpret_cast<uint4*>(residual_out + t * d + c) = o;
+    }
   }
 }
 
 __global__ void combine_scalar_kernel(const uint16_t* __restrict__ y, const int* __restrict__ rank,
                                       const uint16_t* __restrict__ weights, const uint16_t* __restrict__ base,
-                                      int64_t tokens, int d, int k, uint16_t* __restrict__ out) {
+                                      int64_t tokens, int d, int k, uint16_t* __restrict__ out,
+                                      const uint16_t* __restrict__ residual, uint16_t* __restrict__ residual_out) {
   const int64_t total = tokens * d;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -126,7 +136,9 @@ __global__ void combine_scalar_kernel(const uint16_t* __restrict__ y, const int*
       if (weights != nullptr) v = round_bf16(v * bf16_to_f32(weights[t * k + j]));
       acc += v;
     }
-    out[idx] = f32_to_bf16_rne(acc);
+    const uint16_t u = f32_to_bf16_rne(acc);
+    if (out != nullptr) out[idx] = u;
+    if (residual != nullptr) residual_out[idx] = f32_to_bf16_rne(bf16_to_f32(residual[idx]) + bf16_to_f32(u));
   }
 }
 
@@ -174,28 +186,40 @@ int launch_pad_rows(const uint16_t* src, int64_t rows, int cols, int ld_out, uin
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 
-int launch_combine(const uint16_t* y, const int* rank, const uint16_t* weights, const uint16_t* base, int64_t tokens,
-                   int d, int k, uint16_t* out, cudaStream_t stream) {
-  const bool vec_ok = (d % 8) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0 &&
-                      (reinterpret_cast<uintptr_t>(out) & 15u) == 0 &&
-                      (base == nullptr || (reinterpret_cast<uintptr_t>(base) & 15u) == 0);
+int launch_combine_residual(const uint16_t* y, const int* rank, const uint16_t* weights, const uint16_t* base,
+                            const uint16_t* residual, int64_t tokens, int d, int k, uint16_t* out,
+                            uint16_t* residual_out, cudaStream_t stream) {
+  if (out == nullptr && residual == nullptr) return SPX_ERR_INVALID_ARG;
+  if (residual != nullptr && residual_out == nullptr) return SPX_ERR_INVALID_ARG;
+  auto a16 = [](const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const bool vec_ok = (d % 8) == 0 && a16(y) && a16(out) && a16(base) && a16(residual) && a16(residual_out);
   if (vec_ok) {
     const int64_t total = tokens * (d / 8);
     int64_t g = (total + 255) / 256;
     if (g > 148 * 64) g = 148 * 64;
     const int grid = static_cast<int>(g < 1 ? 1 : g);
     if (weights == nullptr && k <= 8)
-      combine_kernel<8, false><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out);
+      combine_kernel<8, false><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out, residual,
+                                                        residual_out);
     else if (weights == nullptr)
-      combine_kernel<kMaxTopK, false><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out);
+      combine_kernel<kMaxTopK, false><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out, residual,
+                                                                residual_out);
     else if (k <= 8)
-      combine_kernel<8, true><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out);
+      combine_kernel<8, true><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out, residual,
+                                                       residual_out);
     else
-      combine_kernel<kMaxTopK, true><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out);
+      combine_kernel<kMaxTopK, true><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out, residual,
+                                                               residual_out);
   } else {
-    combine_scalar_kernel<<<grid_for(tokens * d), 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out);
+    combine_scalar_kernel<<<grid_for(tokens * d), 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out,
+                                                                    residual, residual_out);
   }
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+int launch_combine(const uint16_t* y, const int* rank, const uint16_t* weights, const uint16_t* base, int64_t tokens,
+                   int d, int k, uint16_t* out, cudaStream_t stream) {
+  return launch_combine_residual(y, rank, weights, base, nullptr, tokens, d, k, out, nullptr, stream);
 }
 
 int launch_gather_rows(const uint16_t* src, int64_t ld_src, const int* index, int index_div, int64_t rows, int d,

@@ -522,7 +522,8 @@ class B200MicroExpertChannelMixer(nn.Module):
             return self._forward_autograd(hidden_states)
         return self._forward_native(hidden_states, router_logits)
 
-    def _forward_native(self, hidden_states: Tensor, router_logits: Tensor | None) -> ChannelMixerOutput:
+    def _forward_native(self, hidden_states: Tensor, router_logits: Tensor | None,
+                        block: tuple[Tensor, float, Tensor] | None = None) -> ChannelMixerOutput:
         config = self.config
         if not hidden_states.is_cuda:
             raise RuntimeError("the B200 micro-expert layer requires CUDA hidden states")
@@ -585,7 +586,16 @@ class B200MicroExpertChannelMixer(nn.Module):
             stage_events=None if events is None else _lib.ctypes.addressof(events),
         )
         stream = torch.cuda.current_stream(device).cuda_stream
-        _lib.check(lib.spx_layer_forward(dims, pw, x.data_ptr(), outs, ws.data_ptr(), stream), "spx_layer_forward")
+        if block is None:
+            _lib.check(lib.spx_layer_forward(dims, pw, x.data_ptr(), outs, ws.data_ptr(), stream),
+                       "spx_layer_forward")
+        else:
+            norm_weight, eps, hidden_out = block
+            _lib.check(
+                lib.spx_block_channel_forward(dims, pw, norm_weight.data_ptr(), _lib.ctypes.c_float(eps),
+                                              x.data_ptr(), outs, hidden_out.data_ptr(), ws.data_ptr(), stream),
+                "spx_block_channel_forward",
+            )
         controller = self.potentiation_controller
         metrics: dict[str, Any] = {
             "expert_ids": ids,
@@ -773,6 +783,57 @@ class _LayerFunction(torch.autograd.Function):
         return (None, None, None, grads["x"].reshape(ctx.shape), *[grads[n] for n in ctx.names])
 
 
+class RMSNorm(nn.Module):
+    """RMS normalization with float32 variance accumulation (nn/norm.py:9-31)."""
+
+    def __init__(self, d_model: int, eps: float = 1e-6, *, device=None, dtype=None) -> None:
+        super().__init__()
+        if d_model <= 0:
+            raise ValueError("d_model must be positive")
+        if eps <= 0:
+            raise ValueError("eps must be positive")
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(d_model, device=device, dtype=dtype))
+
+    def forward(self, hidden_states: Tensor) -> Tensor:
+        variance = hidden_states.float().square().mean(dim=-1, keepdim=True)
+        normalized = hidden_states * torch.rsqrt(variance + self.eps).to(hidden_states.dtype)
+        return normalized * self.weight.to(hidden_states.dtype)
+
+
+class B200ChannelBlock(nn.Module):
+    """The channel half of ``SPALMERBlock.forward`` (modeling.py:283-302):
+    ``h + channel_mixer(channel_norm(h)).update``, fused into one native call
+    (``spx_block_channel_forward``: the RMSNorm feeds every GEMM, the residual
+    add runs in the combine).  ``forward`` returns ``(h_out, mixer_output)``;
+    ``mixer_output.update`` is the layer update itself.  Forward only: under
+    autograd it runs the unfused modules (norm, mixer with its backward, add).
+    """
+
+    def __init__(self, config, *, channel_norm: RMSNorm | None = None,
+                 channel_mixer: "B200MicroExpertChannelMixer | None" = None, eps: float = 1e-6) -> None:
+        super().__init__()
+        config = coerce_config(config)
+        self.channel_mixer = channel_mixer if channel_mixer is not None else B200MicroExpertChannelMixer(config)
+        self.channel_norm = channel_norm if channel_norm is not None else RMSNorm(config.d_model, eps)
+
+    def forward(self, hidden_states: Tensor) -> tuple[Tensor, ChannelMixerOutput]:
+        mixer = self.channel_mixer
+        if torch.is_grad_enabled() and (
+            hidden_states.requires_grad or any(p.requires_grad for p in self.parameters())
+        ):
+            out = mixer(self.channel_norm(hidden_states))
+            return hidden_states + out.update, out
+        if hidden_states.ndim != 3 or hidden_states.shape[-1] != mixer.config.d_model:
+            raise ValueError(f"hidden_states must be [batch, seq, {mixer.config.d_model}]")
+        if not hidden_states.is_cuda:
+            raise RuntimeError("the B200 micro-expert layer requires CUDA hidden states")
+        weight = self.channel_norm.weight.detach().to(torch.bfloat16).contiguous()
+        hidden_out = torch.empty_like(hidden_states, dtype=torch.bfloat16)
+        out = mixer._forward_native(hidden_states, None, block=(weight, float(self.channel_norm.eps), hidden_out))
+        return hidden_out, out
+
+
 MicroExpertChannelMixer = B200MicroExpertChannelMixer
 
 
@@ -837,7 +898,9 @@ def dispatch(expert_ids: Tensor, num_experts: int) -> tuple[Tensor, Tensor]:
 
 
 __all__ = [
+    "B200ChannelBlock",
     "B200MicroExpertChannelMixer",
+    "RMSNorm",
     "ChannelMixerOutput",
     "ExpertPotentiationController",
     "ExpertResidency",
