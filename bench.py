@@ -47,6 +47,11 @@ CONFIGS = {
     "ep_skew": dict(cfg=dict(d_model=1024, num_experts=200, expert_inter_dim=256, shared_inter_dim=2048,
                              active_experts=8, router_bias=True), batch=128, seq=1024, cpu_sample=256,
                     zipf=True, expert_parallel=True),
+    # The same with token rows sent once per destination GPU and pair rows summed
+    # at the expert's GPU before they return.
+    "ep_skew_dedup": dict(cfg=dict(d_model=1024, num_experts=200, expert_inter_dim=256, shared_inter_dim=2048,
+                                   active_experts=8, router_bias=True), batch=128, seq=1024, cpu_sample=256,
+                          zipf=True, expert_parallel=True, dedup=True),
     # decode-shaped steps through a 16-layer stack (independent seeded weights per
     # layer, 10% of each layer's experts in MXFP8); the forward of the stack is one CUDA graph.
     "decode": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
@@ -151,6 +156,7 @@ def workload_config(name: str, world: int) -> dict:
     extra = {}
     if ep:
         extra = {"total_tokens": spec["batch"] * spec["seq"], "experts_per_gpu": cfg["num_experts"] // world,
+                 "row_dedup": bool(spec.get("dedup", False)),
                  "router_bias": "Zipf(1.1) popularity: b_e = alpha*ln(rank_e), alpha from tests/golden/zipf_ep_skew.json",
                  "exchange": "NCCL all_to_all_single (counts, rows out, rows back); one host read of the counts"}
     return {
@@ -460,7 +466,7 @@ def run_ep(args) -> None:
     tokens = batch * seq
     mixer, _ = build_mixer(spec, device)
     config = mixer.config
-    layer = ExpertParallelMixer(mixer) if world > 1 else None
+    layer = ExpertParallelMixer(mixer, dedup=spec.get("dedup", False)) if world > 1 else None
     x_cpu = torch.randn(spec["batch"], seq, config.d_model, generator=torch.Generator().manual_seed(1))
     x_cpu = x_cpu.to(torch.bfloat16)[rank * batch:(rank + 1) * batch].contiguous()
     x_host = x_cpu.pin_memory()
@@ -494,9 +500,11 @@ def run_ep(args) -> None:
         clocks = sampler.stop()
         total_ms = t0.elapsed_time(t1)
         loads = None
+        exchanged = None
         if layer is not None:
             r = layer(x_bufs[0])
-            loads = r["recv_rows"]
+            loads = r.get("recv_pairs", r["recv_rows"])
+            exchanged = sum(r["send_rows"])
         # e2e: pinned H2D of this rank's tokens, forward, D2H of the update, per step
         out_host = torch.empty(batch, seq, config.d_model, dtype=torch.bfloat16).pin_memory()
         xd = torch.empty_like(x_bufs[0])
@@ -543,6 +551,7 @@ def run_ep(args) -> None:
                          "achieved": flops / (ms_per_step / 1e3) / 1e12, "peak": pk["bf16_tflops_sustained"] or pk["bf16_tflops"],
                          "unit": "TFLOP/s", "traffic": None, "peak_source": f"{pk['source']} bf16 sustained"},
             "expert_rows_per_gpu": recv_loads,
+            "rows_sent_per_gpu_rank0": exchanged,
             "max_over_mean_expert_load": max(recv_loads) / (sum(recv_loads) / len(recv_loads)),
         }
         line["roofline"]["frac"] = line["roofline"]["achieved"] / line["roofline"]["peak"]

@@ -232,7 +232,7 @@ int spx_shared_forward(const spx_layer_dims* dims, const spx_packed_weights* wei
 
 /* update[t] = bf16(shared[t] + sum_j bf16(expert_rows[pair_rank[t*k+j]] * w[t*k+j]))
  * in FP32, slots in order; pair_weights NULL = rows already weighted, shared
- * NULL = no shared path. */
+ * NULL = no shared path, a negative pair_rank = an empty slot. */
 int spx_combine(const uint16_t* expert_rows, const int32_t* pair_rank, const uint16_t* pair_weights,
                 const uint16_t* shared, int64_t tokens, int32_t d, int32_t top_k, uint16_t* update, void* stream);
 

@@ -74,6 +74,7 @@ __global__ void pad_rows_kernel(const uint16_t* __restrict__ src, int64_t rows, 
 // update[t] = bf16(base[t] + sum_j row_j) in FP32 (base first, then slots in
 // order), row_j = Y[rank[t*k + j]] -- or bf16(Y[rank[t*k + j]] * w[t*k + j])
 // when pair weights are given (expert rows computed elsewhere, unweighted).
+// A negative rank marks an empty slot (no row).
 // base is the shared SwiGLU output (BF16) or absent.  8 columns per thread;
 // consecutive threads take consecutive 16-byte chunks of one token, so every
 // slot's row is read in whole 128-byte lines, and a thread issues all k row
@@ -97,10 +98,10 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, const int* __rest
     uint4 v[KMAX];
 #pragma unroll
     for (int j = 0; j < KMAX; ++j)
-      if (j < k) v[j] = __ldg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(r[j]) * d + c));
+      if (j < k && r[j] >= 0) v[j] = __ldg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(r[j]) * d + c));
 #pragma unroll
     for (int j = 0; j < KMAX; ++j) {
-      if (j < k) {
+      if (j < k && r[j] >= 0) {
         const float w = WEIGHTED ? bf16_to_f32(__ldg(weights + t * k + j)) : 1.0f;
         add_row8<WEIGHTED>(acc, v[j], w);
       }
@@ -132,6 +133,7 @@ __global__ void combine_scalar_kernel(const uint16_t* __restrict__ y, const int*
     const int c = static_cast<int>(idx - t * d);
     float acc = base != nullptr ? bf16_to_f32(base[idx]) : 0.0f;
     for (int j = 0; j < k; ++j) {
+      if (rank[t * k + j] < 0) continue;  // empty slot
       float v = bf16_to_f32(y[static_cast<int64_t>(rank[t * k + j]) * d + c]);
       if (weights != nullptr) v = round_bf16(v * bf16_to_f32(weights[t * k + j]));
       acc += v;

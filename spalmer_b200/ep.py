@@ -252,7 +252,7 @@ class CudaOps:
         return out
 
     def shared(self, x: Tensor) -> Tensor | None:
-        if self.shared_w1 is None:
+        if self.mixer.shared is None:
             return None
         lib = _lib.load()
         dims = self._layer_dims(self.config, x.shape[0], self.k)
@@ -264,13 +264,18 @@ class CudaOps:
                    "spx_shared_forward")
         return out
 
-    def combine(self, rows: Tensor, rank: Tensor, weights: Tensor, shared: Tensor | None) -> Tensor:
+    def combine(self, rows: Tensor, rank: Tensor, weights: Tensor | None, shared: Tensor | None,
+                tokens: int | None = None) -> Tensor:
+        """Per token the sum of its slots' rows (weighted when weights are
+        given) on top of `shared`; `rank` is [tokens, slots], -1 = empty."""
+
         lib = _lib.load()
-        T = weights.shape[0]
-        out = torch.empty(T, self.d, dtype=torch.bfloat16, device=rows.device)
-        stream = torch.cuda.current_stream(rows.device).cuda_stream
-        _lib.check(lib.spx_combine(rows.data_ptr(), rank.data_ptr(), weights.data_ptr(), _lib.ptr(shared), T, self.d,
-                                   self.k, out.data_ptr(), stream), "spx_combine")
+        T = weights.shape[0] if tokens is None else tokens
+        k = rank.numel() // max(T, 1)
+        out = torch.empty(T, self.d, dtype=torch.bfloat16, device=rank.device)
+        stream = torch.cuda.current_stream(rank.device).cuda_stream
+        _lib.check(lib.spx_combine(rows.data_ptr(), rank.data_ptr(), _lib.ptr(weights), _lib.ptr(shared), T, self.d,
+                                   k, out.data_ptr(), stream), "spx_combine")
         return out
 
 
@@ -282,8 +287,9 @@ class ExpertParallelMixer:
     update and this rank's routing metrics (statistics over the local tokens).
     """
 
-    def __init__(self, mixer: Any, group: Any = None, ops: Any = None):
+    def __init__(self, mixer: Any, group: Any = None, ops: Any = None, dedup: bool = False):
         self.mixer = mixer
+        self.dedup = dedup
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -316,6 +322,17 @@ class ExpertParallelMixer:
             shared = ops.shared(x)
         logits = None if router_logits is None else router_logits.reshape(T, -1).contiguous()
         r = ops.route(x, logits)
+        if self.dedup:
+            update, stats = self._exchange_dedup(x, r, shared)
+            return {
+                "update": update.reshape(B, S, d),
+                "auxiliary_loss": r["auxiliary_loss"][0],
+                "expert_ids": r["expert_ids"].reshape(B, S, k),
+                "routing_weights": r["routing_weights"].reshape(B, S, k),
+                "router_scores": r["router_scores"].reshape(B, S, -1),
+                "expert_utilization": r["expert_utilization"],
+                **stats,
+            }
         # 2. counts exchange; the only host read of the forward
         recv_counts = torch.empty(self.world * self.e_local, dtype=torch.int32, device=r["counts"].device)
         dist.all_to_all_single(recv_counts, r["counts"], group=self.group)
@@ -348,6 +365,86 @@ class ExpertParallelMixer:
             "send_rows": plan.send_rows,
             "recv_rows": plan.recv_rows,
         }
+
+    def _exchange_dedup(self, x: Tensor, r: dict, shared: Tensor | None) -> tuple[Tensor, dict]:
+        """The exchange with token rows sent once per destination rank.
+
+        A token whose k pairs land on m experts of one rank travels to that
+        rank once instead of m times; with each pair goes a 64-bit word (the
+        token's row within the destination's block << 16 | its BF16 routing
+        weight).  The destination expands the rows to its pairs, runs its
+        experts, and sums each token's weighted pair rows (one BF16 row per
+        token and destination) before sending them back; the source adds those
+        to the shared output.  Per token the pair rows are summed per
+        destination first, so the update matches the single-GPU layer within
+        BF16 tolerance rather than bit for bit.
+        """
+
+        ops, G, el, k = self.ops, self.world, self.e_local, self.mixer.active_experts
+        T, d = x.shape
+        dev = x.device
+        order = r["order"].long()
+        counts = r["counts"].long()
+        # sorted pairs are grouped by expert, hence by destination rank
+        dest_sorted = torch.repeat_interleave(torch.arange(G, device=dev), counts.view(G, el).sum(1))
+        key = dest_sorted * T + order // k
+        uniq, inv = torch.unique(key, sorted=True, return_inverse=True)
+        uniq_dest = uniq // T
+        uniq_tok = uniq % T
+        uniq_counts = torch.bincount(uniq_dest, minlength=G)
+        uniq_off = torch.cumsum(uniq_counts, 0) - uniq_counts
+        rel = inv - uniq_off[dest_sorted]
+        # 2. per destination: pair counts of its experts and the unique rows; one host read
+        send_meta = torch.cat([counts.view(G, el), uniq_counts.view(G, 1)], dim=1).to(torch.int32).contiguous()
+        recv_meta = torch.empty_like(send_meta)
+        dist.all_to_all_single(recv_meta, send_meta, group=self.group)
+        sm, rm = send_meta.cpu().numpy(), recv_meta.cpu().numpy()
+        plan = exchange_plan(sm[:, :el].reshape(-1), rm[:, :el].reshape(-1), G)
+        send_u = [int(v) for v in sm[:, el]]
+        recv_u = [int(v) for v in rm[:, el]]
+        # 3. unique rows out, and the pairs' (row, weight) words
+        send_rows = ops.gather(x, uniq_tok.to(torch.int32), 1)
+        recv_rows = send_rows.new_empty(sum(recv_u), d)
+        dist.all_to_all_single(recv_rows, send_rows, output_split_sizes=recv_u, input_split_sizes=send_u,
+                               group=self.group)
+        w_sorted = r["routing_weights"].reshape(-1)[order].contiguous()
+        words = (rel << 16) | (w_sorted.view(torch.int16).to(torch.int64) & 0xFFFF)
+        recv_words = words.new_empty(sum(plan.recv_rows))
+        dist.all_to_all_single(recv_words, words, output_split_sizes=plan.recv_rows,
+                               input_split_sizes=plan.send_rows, group=self.group)
+        # 4. expand to pair rows, local experts (unweighted)
+        recv_u_t = torch.tensor(recv_u, dtype=torch.int64, device=dev)
+        src_of_pair = torch.repeat_interleave(torch.arange(G, device=dev),
+                                              torch.tensor(plan.recv_rows, dtype=torch.int64, device=dev))
+        row_index = (torch.cumsum(recv_u_t, 0) - recv_u_t)[src_of_pair] + (recv_words >> 16)
+        w_recv = (recv_words & 0xFFFF).to(torch.int16).view(torch.bfloat16)
+        pair_rows = ops.gather(recv_rows, row_index.to(torch.int32).contiguous(), 1)
+        out_rows = ops.experts(pair_rows, receive_expert_ids(plan, dev), self._local_lanes())
+        # 5. per received row, the sum of its pairs' bf16(row * weight): a slot table [U, k]
+        U, P = recv_rows.shape[0], out_rows.shape[0]
+        perm = torch.argsort(row_index, stable=True)
+        cnt = torch.bincount(row_index, minlength=U)
+        u_sorted = row_index[perm]
+        slot = torch.arange(P, device=dev) - (torch.cumsum(cnt, 0) - cnt)[u_sorted]
+        table = torch.full((U * k,), -1, dtype=torch.int32, device=dev)
+        table[u_sorted * k + slot] = perm.to(torch.int32)
+        wtab = torch.zeros(U * k, dtype=torch.bfloat16, device=dev)
+        wtab[u_sorted * k + slot] = w_recv[perm]
+        partial = (ops.combine(out_rows, table, wtab.view(U, k), None, tokens=U) if U > 0
+                   else out_rows.new_empty(0, d))
+        back = partial.new_empty(sum(send_u), d)
+        dist.all_to_all_single(back, partial, output_split_sizes=send_u, input_split_sizes=recv_u,
+                               group=self.group)
+        # 6. update = shared + the partial rows of every destination (slot = destination rank)
+        if self.side is not None:
+            torch.cuda.current_stream(ops.device).wait_stream(self.side)
+            if shared is not None:
+                shared.record_stream(torch.cuda.current_stream(ops.device))
+        tab2 = torch.full((T * G,), -1, dtype=torch.int32, device=dev)
+        tab2[uniq_tok * G + uniq_dest] = torch.arange(uniq.numel(), dtype=torch.int32, device=dev)
+        update = ops.combine(back, tab2, None, shared, tokens=T)
+        return update, {"send_rows": send_u, "recv_rows": recv_u, "send_pairs": plan.send_rows,
+                        "recv_pairs": plan.recv_rows}
 
     __call__ = forward
 

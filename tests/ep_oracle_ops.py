@@ -69,15 +69,18 @@ class OracleOps:
             return None
         return _tensor(R.shared_swiglu(_bits(x), self.p.shared_gate, self.p.shared_up, self.p.shared_down))
 
-    def combine(self, rows: torch.Tensor, rank: torch.Tensor, weights: torch.Tensor, shared) -> torch.Tensor:
+    def combine(self, rows: torch.Tensor, rank: torch.Tensor, weights, shared, tokens: int | None = None):
         y = bf16_bits_to_f32(_bits(rows))
-        w = bf16_bits_to_f32(_bits(weights)).reshape(-1)
-        rk = rank.numpy()
-        T = weights.shape[0]
+        w = np.zeros(0, np.float32) if weights is None else bf16_bits_to_f32(_bits(weights)).reshape(-1)
+        rk = rank.numpy().reshape(-1)
+        T = weights.shape[0] if tokens is None else tokens
         acc = np.zeros((T, self.d), np.float32) if shared is None else bf16_bits_to_f32(_bits(shared)).copy()
-        for j in range(self.k):
-            p = np.arange(T) * self.k + j
-            acc = acc + round_bf16(y[rk[p]] * w[p][:, None])
+        k = rk.size // T
+        for j in range(k):
+            p = np.arange(T) * k + j
+            ok = rk[p] >= 0  # a negative rank is an empty slot
+            add = round_bf16(y[np.where(ok, rk[p], 0)] * w[p][:, None]) if w.size else y[np.where(ok, rk[p], 0)]
+            acc = acc + np.where(ok[:, None], add, np.float32(0))
         return _tensor(f32_to_bf16_bits(acc))
 
 

@@ -54,7 +54,7 @@ def _build():
     return mixer, oracle_params(mixer), x
 
 
-def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
+def _worker(rank: int, world: int, port: int, out_dir: str, dedup: bool = False) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -64,10 +64,10 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
 
         mixer, params, x = _build()
         mine = x.chunk(world, dim=0)[rank].contiguous()
-        ep = ExpertParallelMixer(mixer, ops=OracleOps(params, CFG["active_experts"], rank, world))
+        ep = ExpertParallelMixer(mixer, ops=OracleOps(params, CFG["active_experts"], rank, world), dedup=dedup)
         out = ep(mine)
-        torch.save({"update": out["update"], "send": out["send_rows"], "recv": out["recv_rows"]},
-                   os.path.join(out_dir, f"rank{rank}.pt"))
+        torch.save({"update": out["update"], "send": out["send_rows"], "recv": out["recv_rows"],
+                    "send_pairs": out.get("send_pairs")}, os.path.join(out_dir, f"rank{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
@@ -87,3 +87,27 @@ def test_ep_exchange_matches_single_process_gloo(tmp_path):
     # every row sent was received: rank a's send to b == rank b's receive from a
     assert got[0]["send"][1] == got[1]["recv"][0] and got[1]["send"][0] == got[0]["recv"][1]
     assert sum(got[0]["send"]) == x.shape[1] * x.shape[0] // world * CFG["active_experts"]
+
+
+def test_ep_dedup_exchange_matches_single_process_gloo(tmp_path):
+    """Rows sent once per destination rank, pair rows summed per destination:
+    the update matches the single-process layer within BF16 tolerance, and
+    fewer rows travel than pairs."""
+
+    from tests.ep_oracle_ops import OracleOps, single_process_update
+
+    world = 2
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path), True), nprocs=world, join=True)
+    _, params, x = _build()
+    got = [torch.load(tmp_path / f"rank{r}.pt") for r in range(world)]
+    for r, part in enumerate(x.chunk(world, dim=0)):
+        want = single_process_update(OracleOps(params, CFG["active_experts"], 0, 1),
+                                     part.reshape(-1, 64).contiguous()).float()
+        have = got[r]["update"].reshape(-1, 64).float()
+        assert ((have - want).abs() <= 1e-2 + 2e-2 * want.abs()).all()
+    assert got[0]["send"][1] == got[1]["recv"][0] and got[1]["send"][0] == got[0]["recv"][1]
+    tokens = x.shape[0] * x.shape[1] // world
+    for g in got:
+        assert sum(g["send"]) <= tokens * world  # at most one row per token and destination
+        assert sum(g["send_pairs"]) == tokens * CFG["active_experts"]
+        assert sum(g["send"]) < sum(g["send_pairs"])
