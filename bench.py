@@ -61,6 +61,14 @@ CONFIGS = {
     # (the MXFP8 lane has no backward); loss = sum(update * dU) + aux.
     "m100_train": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
                                 active_experts=8), batch=64, seq=1024, cpu_sample=256, train=True),
+    # Paged expert offload (the reference's inference offload, experts/offload.py): the expert
+    # bank stays in pinned host memory behind a device cache of half the experts; every step
+    # stages the experts it selects through the cache page by page.
+    "m100_paged": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
+                                active_experts=8), batch=64, seq=1024, cpu_sample=256, paged=dict(cache_size=100)),
+    # Decode-shaped paged steps: 64 new tokens per step through one layer, a 64-expert cache.
+    "decode_paged": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
+                                  active_experts=8), batch=1, seq=64, cpu_sample=64, paged=dict(cache_size=64)),
     # 10M-preset shape.
     "m10": dict(cfg=dict(d_model=256, num_experts=200, expert_inter_dim=64, shared_inter_dim=256,
                          active_experts=8), batch=32, seq=512, cpu_sample=4096),
@@ -803,6 +811,122 @@ def cpu_train_baseline(spec: dict, mixer) -> dict:
             "sample": f"{sample} tokens, forward + backward through PyTorch CPU autograd, median of 3"}
 
 
+def run_paged(args) -> None:
+    """The layer with its expert bank offloaded to pinned host memory behind a
+    device cache (spalmer_b200.offload); each step pages the selected experts.
+    Replicas only for N > 1 (no collective)."""
+
+    world, rank, local = init_dist()
+    import torch.distributed as dist
+
+    from spalmer_b200.offload import enable_expert_offload
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    spec = CONFIGS[args.config]
+    batch, seq = spec["batch"], spec["seq"]
+    tokens = batch * seq
+    mixer, _ = build_mixer(spec, device)
+    capacity = spec["paged"]["cache_size"]
+    enable_expert_offload(mixer, device, cache_size=capacity)
+    config = mixer.config
+    bank = mixer.experts
+    cache = bank._offload
+    # Four distinct seeded batches, cycled, so consecutive steps select different experts.
+    gen = torch.Generator().manual_seed(1 + rank)
+    x_cpu = [torch.randn(batch, seq, config.d_model, generator=gen).to(torch.bfloat16) for _ in range(4)]
+    x_host = [x.pin_memory() for x in x_cpu]
+    x_dev = [x.to(device) for x in x_host]
+    K, W = args.steps, args.warmup
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    with torch.inference_mode():
+        for i in range(W):
+            mixer(x_dev[i % 4])
+        torch.cuda.synchronize()
+        barrier()
+        c0, b0, ch = bank.expert_offload_counters, cache.physical_bytes_copied, 0
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        sampler = ClockSampler(local)
+        time.sleep(0.3)
+        t0.record()
+        for i in range(K):
+            mixer(x_dev[i % 4])
+            ch += cache.last_chunks
+        t1.record()
+        torch.cuda.synchronize()
+        clocks = sampler.stop()
+        barrier()
+        c1, b1 = bank.expert_offload_counters, cache.physical_bytes_copied
+        total_ms = t0.elapsed_time(t1)
+        status = mixer.device_status()
+        # e2e: hidden states in from pinned host memory, update and aux loss out, every step
+        out_host = torch.empty(batch, seq, config.d_model, dtype=torch.bfloat16).pin_memory()
+        aux_host = torch.empty((), dtype=torch.bfloat16).pin_memory()
+        x_in = torch.empty_like(x_dev[0])
+        for i in range(W):
+            x_in.copy_(x_host[i % 4], non_blocking=True)
+            o = mixer(x_in)
+            out_host.copy_(o.update, non_blocking=True)
+            aux_host.copy_(o.auxiliary_loss, non_blocking=True)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(K):
+            x_in.copy_(x_host[i % 4], non_blocking=True)
+            o = mixer(x_in)
+            out_host.copy_(o.update, non_blocking=True)
+            aux_host.copy_(o.auxiliary_loss, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = e0.elapsed_time(e1)
+    t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms = float(t[0]), float(t[1])
+    ms_per_step = total_ms / K
+    if rank == 0:
+        rows = (c1[1] - c0[1]) / K
+        phys = (b1 - b0) / K
+        line = {
+            "metric": METRIC, "value": world * tokens / (ms_per_step / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (four seeded N(0,1) hidden-state batches cycled, seeded random-init weights)",
+            "config": {**workload_config(args.config, world),
+                       "expert_offload": f"paged: expert bank in pinned host memory, device cache of {capacity} "
+                                         f"of {config.num_experts} experts, LRU spare slots",
+                       "l2": "expert weights re-staged from the host every step; hidden states cycled over 4 batches",
+                       "parallelism": f"replicas{world}" if world > 1 else "dp1"},
+            "e2e": {"value": world * tokens / (e2e_ms / K / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": tokens * config.d_model * 2 + int(phys),
+                    "d2h_bytes_per_step": tokens * config.d_model * 2 + 2 + 4 * config.num_experts},
+            "gpu_launches": int(K * 9 + 3 * ch),
+            "roofline": None,
+            "paging": {"cache_size": capacity, "transferred_experts_per_step": rows,
+                       "stage_operations_per_step": (c1[0] - c0[0]) / K,
+                       "h2d_packed_bytes_per_step": phys,
+                       "h2d_gbs_over_step": phys / (ms_per_step / 1e3) / 1e9,
+                       "chunks_per_step": ch / K},
+            "device_status": status,
+        }
+        if clocks is not None:
+            line["clocks"] = clocks
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -822,6 +946,8 @@ def main() -> None:
         run_decode(args)
     elif CONFIGS[args.config].get("train"):
         run_train(args)
+    elif CONFIGS[args.config].get("paged"):
+        run_paged(args)
     else:
         run_ours(args)
 

@@ -51,7 +51,7 @@
 extern "C" {
 #endif
 
-#define SPX_ABI_VERSION 5
+#define SPX_ABI_VERSION 6
 
 #define SPX_OK 0
 #define SPX_ERR_INVALID_ARG -1
@@ -261,6 +261,54 @@ int spx_surprise_calibration(const uint16_t* router_scores, const int64_t* exper
 int spx_block_channel_forward(const spx_layer_dims* dims, const spx_packed_weights* weights,
                               const uint16_t* norm_weight, float eps, const uint16_t* hidden,
                               const spx_layer_outputs* outputs, uint16_t* hidden_out, void* workspace, void* stream);
+
+/* ---- paged experts: the layer forward around a bounded device cache of expert weights
+ * Reference: MicroExpertBank._execute_paged_grouped (experts/bank.py:821-899)
+ * with the cache of offload.py / bank.py:241-365: routing over the full pool,
+ * then the selected experts run page by page, each page's weights staged
+ * into the cache first.  Three calls share one workspace (spx_layer_sizes of
+ * `dims`) and run in order on `stream`:
+ *   spx_layer_paged_begin    router, selection, dispatch (outputs as
+ *                            spx_layer_forward; expert_counts required: the
+ *                            host plans the pages from it), the MXFP8
+ *                            quantisation of the hidden rows, shared GEMM1.
+ *                            Expert weights are not read.
+ *   spx_layer_paged_experts  the expert GEMMs of every pair whose expert e has
+ *                            page_slot[e] >= 0 ([E] int32, device), reading
+ *                            that expert's packed weights from slot
+ *                            page_slot[e] of `cache` (expert_w1 / expert_w2 and
+ *                            the MXFP8 copies laid out as spx_pack_weights
+ *                            lays out cache_slots experts; expert_lane_mxfp8
+ *                            as given to begin).  Call once per page; every
+ *                            routed expert must be in exactly one page.
+ *                            sm_limit > 0 caps the GEMMs' persistent grids
+ *                            at that many SMs, leaving the others to a
+ *                            concurrent spx_stage_expert_slots (0 = all).
+ *   spx_layer_paged_finish   shared down projection and combine into
+ *                            outputs->update (same outputs as begin).
+ * The pages write the same rows an unpaged pass writes, so the update is
+ * bit-identical to spx_layer_forward's. */
+int spx_layer_paged_begin(const spx_layer_dims* dims, const spx_packed_weights* weights, const uint16_t* hidden,
+                          const spx_layer_outputs* outputs, void* workspace, void* stream);
+int spx_layer_paged_experts(const spx_layer_dims* dims, const spx_packed_weights* cache, int32_t cache_slots,
+                            const int32_t* page_slot, int32_t sm_limit, const uint16_t* hidden, void* workspace,
+                            void* stream);
+int spx_layer_paged_finish(const spx_layer_dims* dims, const spx_packed_weights* weights, const uint16_t* hidden,
+                           const spx_layer_outputs* outputs, void* workspace, void* stream);
+
+/* Stage whole experts into cache slots (the copy half of _stage_expert_rows,
+ * experts/bank.py:275-306): for each of the n (expert, slot) pairs (device
+ * int32 [n][2]) and each of the `arrays` (<= 8) packed arrays,
+ *   dst[a] + slot * bytes[a]  <-  src[a] + expert * bytes[a].
+ * src, dst and bytes are host arrays of `arrays` entries; src[a] holds
+ * num_experts experts and may be page-locked host memory (the GPU reads it
+ * over the host link: one launch instead of one DMA copy per expert and
+ * array); dst[a] (device) holds `slots` experts; bytes[a] % 16 == 0.
+ * Pairs outside [0, num_experts) x [0, slots) are skipped.  `ctas` CTAs of
+ * 512 threads (0 = 16) walk the blocks, so the copy occupies a few SMs. */
+int spx_stage_expert_slots(const void* const* src, void* const* dst, const int64_t* bytes, int32_t arrays,
+                           const int32_t* pairs, int32_t n, int32_t num_experts, int32_t slots, int32_t ctas,
+                           void* stream);
 
 /* ---- backward of the routed experts and the router scores
  * Reference: autograd through MicroExpertChannelMixer.forward

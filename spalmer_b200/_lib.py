@@ -51,9 +51,13 @@ EXPORTED = (
     "spx_layer_backward_sizes",
     "spx_layer_backward",
     "spx_block_channel_forward",
+    "spx_layer_paged_begin",
+    "spx_layer_paged_experts",
+    "spx_layer_paged_finish",
+    "spx_stage_expert_slots",
 )
 
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 _vp = ctypes.c_void_p
 
@@ -223,6 +227,17 @@ def load() -> ctypes.CDLL:
         "spx_block_channel_forward": (
             ctypes.c_int,
             [P(LayerDims), P(PackedWeights), _vp, ctypes.c_float, _vp, P(LayerOutputs), _vp, _vp, _vp],
+        ),
+        "spx_layer_paged_begin": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, P(LayerOutputs), _vp, _vp]),
+        "spx_layer_paged_experts": (
+            ctypes.c_int,
+            [P(LayerDims), P(PackedWeights), ctypes.c_int32, _vp, ctypes.c_int32, _vp, _vp, _vp],
+        ),
+        "spx_layer_paged_finish": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, P(LayerOutputs), _vp, _vp]),
+        "spx_stage_expert_slots": (
+            ctypes.c_int,
+            [_vp, _vp, _vp, ctypes.c_int32, _vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+             _vp],
         ),
         "spx_mxfp8_mm_nt": (
             ctypes.c_int,

@@ -117,6 +117,7 @@ struct Layout {
   size_t small, tie_rows, lb_partial, lb_sum, chunk_hist, counts, starts, tiles, order, src_row, rank, sorted_w;
   size_t hidden, y, shared_hidden, shared_out, x_pad, x_norm, util, stats, ratios, aux;
   size_t x_q, x_sf, h_q, h_sf, tiles_mx;  // MXFP8 lane (empty otherwise)
+  size_t tiles_page, tiles_mx_page;        // one page of a paged expert pass
   size_t total;
 };
 
@@ -155,6 +156,8 @@ Layout make_layout(const Shape& s) {
   L.h_q = take(s.mx ? static_cast<size_t>(s.P) * s.kh : 0);
   L.h_sf = take(s.mx ? static_cast<size_t>(s.P) * (s.kh / kMxBlock) : 0);
   L.tiles_mx = take(s.mx ? sizeof(int4) * static_cast<size_t>(s.max_tiles) : 0);
+  L.tiles_page = take(sizeof(int4) * static_cast<size_t>(s.max_tiles));
+  L.tiles_mx_page = take(s.mx ? sizeof(int4) * static_cast<size_t>(s.max_tiles) : 0);
   L.total = off;
   return L;
 }
@@ -310,39 +313,59 @@ DispatchArgs layer_dispatch_args(const Ctx& c, const spx_layer_dims* dims, const
   return da;
 }
 
-// K3: expert GEMM1 (+SwiGLU) and GEMM2 over the dispatched rows of `hidden`
-// (`xa` = hidden padded), both lanes; weighted rows land in Y (sorted order).
-int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hidden, const uint16_t* xa,
-                  const DispatchArgs& da, int64_t ld_hidden = 0) {
+// Expert weights and tile tables of one expert pass: the whole bank (groups =
+// E, the dispatch's tables) or one page of a paged pass (groups = cache
+// slots, the page's tables with groups renamed to slots).
+struct ExpertPass {
+  const uint16_t* w1;
+  const uint16_t* w2;
+  const uint8_t* w1_mx;
+  const uint8_t* w1_mx_sf;
+  const uint8_t* w2_mx;
+  const uint8_t* w2_mx_sf;
+  int groups;
+  const int4* tiles;
+  const int* num_tiles;
+  const int4* tiles_mx;  // null: no MXFP8 lane in this pass
+  const int* num_tiles_mx;
+  int max_ctas;  // persistent grid cap of the GEMMs (0 = every SM)
+};
+
+// MXFP8 lane input: E4M3 rows of the hidden states with their block scales
+// (per token, so every expert's gathered rows share them).
+int stage_quantize_x(const Ctx& c, const uint16_t* hidden, int64_t ld_hidden) {
+  const Shape& s = c.s;
+  return launch_mx_quantize_rows(hidden, s.T, s.d, ld_hidden > 0 ? ld_hidden : s.d, s.kx, at<uint8_t>(c.ws, c.L.x_q),
+                                 s.kx, at<uint8_t>(c.ws, c.L.x_sf), s.kx / kMxBlock, c.st);
+}
+
+// K3 GEMMs: expert GEMM1 (+SwiGLU) and GEMM2 over the tiles of `p`, rows
+// gathered from `xa` through src_row; weighted rows land in Y (sorted order).
+int stage_expert_gemms(const Ctx& c, const uint16_t* xa, const int* src_row, const uint16_t* sorted_w,
+                       const ExpertPass& p) {
   const Shape& s = c.s;
   void* ws = c.ws;
   const Layout& L = c.L;
   int rc = SPX_OK;
-  const bool mx = da.lane_mx != nullptr;
+  const bool mx = p.tiles_mx != nullptr;
   uint8_t* xq = at<uint8_t>(ws, L.x_q);
   uint8_t* xsf = at<uint8_t>(ws, L.x_sf);
   uint8_t* hq = at<uint8_t>(ws, L.h_q);
   uint8_t* hsf = at<uint8_t>(ws, L.h_sf);
-  if (mx) {
-    // Hidden states of the MXFP8 lane: E4M3 rows with their block scales
-    // (per token, so every expert's gathered rows share them).
-    if ((rc = launch_mx_quantize_rows(hidden, s.T, s.d, ld_hidden > 0 ? ld_hidden : s.d, s.kx, xq, s.kx, xsf,
-                                      s.kx / kMxBlock, c.st)) != SPX_OK)
-      return rc;
-  }
   uint16_t* hid = at<uint16_t>(ws, L.hidden);
   uint16_t* y = at<uint16_t>(ws, L.y);
   {
     GemmArgs g = base_args(kEpiSwiglu, 2 * s.c, s.kd / 64, c.status);
-    if ((rc = encode_3d(&g.tma_b, w->expert_w1, s.E, static_cast<int64_t>(s.nc) * 2 * s.c, s.kd, 2 * s.c)) != SPX_OK)
+    if ((rc = encode_3d(&g.tma_b, p.w1, p.groups, static_cast<int64_t>(s.nc) * 2 * s.c, s.kd, 2 * s.c)) != SPX_OK)
       return rc;
-    g.groups = s.E;
+    g.groups = p.groups;
+    g.max_ctas = p.max_ctas;
     g.gather = 1;
-    g.gather_idx = da.src_row;
+    g.gather_idx = src_row;
     g.a_base = reinterpret_cast<const uint8_t*>(xa);
     g.lda = 2 * static_cast<int64_t>(s.kd);
-    g.tiles = da.tiles;
-    g.num_tiles = da.num_tiles;
+    g.tiles = p.tiles;
+    g.num_tiles = p.num_tiles;
     g.chunk = s.c;
     g.h_cols = s.kp;
     g.out = hid;
@@ -352,19 +375,20 @@ int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hid
   if (mx) {
     // MXFP8-lane experts: block-scaled GEMM1, hidden written quantised.
     GemmArgs g = base_args(kEpiSwiglu, 2 * s.cm, s.kx / 128, c.status, true);
-    if ((rc = encode_3d(&g.tma_b, w->expert_w1_mx, s.E, static_cast<int64_t>(s.ncm) * 2 * s.cm, s.kx, 2 * s.cm,
+    if ((rc = encode_3d(&g.tma_b, p.w1_mx, p.groups, static_cast<int64_t>(s.ncm) * 2 * s.cm, s.kx, 2 * s.cm,
                         1)) != SPX_OK)
       return rc;
-    g.groups = s.E;
+    g.groups = p.groups;
+    g.max_ctas = p.max_ctas;
     g.gather = 1;
-    g.gather_idx = da.src_row;
+    g.gather_idx = src_row;
     g.a_base = xq;
     g.lda = s.kx;
     g.sfa = xsf;
     g.ld_sfa = s.kx / kMxBlock;
-    g.sfb = w->expert_w1_mx_scales;
-    g.tiles = da.tiles_mx;
-    g.num_tiles = da.num_tiles_mx;
+    g.sfb = p.w1_mx_sf;
+    g.tiles = p.tiles_mx;
+    g.num_tiles = p.num_tiles_mx;
     g.chunk = s.cm;
     g.h_cols = s.kh;
     g.out = hq;
@@ -377,70 +401,92 @@ int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hid
   {
     GemmArgs g = base_args(kEpiScatter, s.bn_d, s.kp / 64, c.status);
     if ((rc = encode_2d(&g.tma_a, hid, s.P, s.kp, s.kp, kTileRows)) != SPX_OK) return rc;
-    if ((rc = encode_3d(&g.tma_b, w->expert_w2, s.E, s.d, s.kp, s.bn_d)) != SPX_OK) return rc;
-    g.groups = s.E;
-    g.tiles = da.tiles;
-    g.num_tiles = da.num_tiles;
+    if ((rc = encode_3d(&g.tma_b, p.w2, p.groups, s.d, s.kp, s.bn_d)) != SPX_OK) return rc;
+    g.groups = p.groups;
+    g.max_ctas = p.max_ctas;
+    g.tiles = p.tiles;
+    g.num_tiles = p.num_tiles;
     g.n_valid = s.d;
     g.out = y;
     g.ldo = s.d;
     g.tma_store = (s.d % 64) == 0;  // whole 64-column boxes; other widths use plain stores
     if (g.tma_store && (rc = encode_2d(&g.tma_out, y, s.P, s.d, s.d, 32)) != SPX_OK) return rc;
-    g.pos_weight = da.sorted_weights;
+    g.pos_weight = sorted_w;
     if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn_d, c.st)) != SPX_OK) return rc;
   }
   if (mx) {
     GemmArgs g = base_args(kEpiScatter, s.bn2m, s.kh / 128, c.status, true);
     if ((rc = encode_2d(&g.tma_a, hq, s.P, s.kh, s.kh, kTileRows, 1)) != SPX_OK) return rc;
-    if ((rc = encode_3d(&g.tma_b, w->expert_w2_mx, s.E, s.d, s.kh, s.bn2m, 1)) != SPX_OK) return rc;
-    g.groups = s.E;
-    g.tiles = da.tiles_mx;
-    g.num_tiles = da.num_tiles_mx;
+    if ((rc = encode_3d(&g.tma_b, p.w2_mx, p.groups, s.d, s.kh, s.bn2m, 1)) != SPX_OK) return rc;
+    g.groups = p.groups;
+    g.max_ctas = p.max_ctas;
+    g.tiles = p.tiles_mx;
+    g.num_tiles = p.num_tiles_mx;
     g.sfa = hsf;
     g.ld_sfa = s.kh / kMxBlock;
-    g.sfb = w->expert_w2_mx_scales;
+    g.sfb = p.w2_mx_sf;
     g.n_valid = s.d;
     g.out = y;
     g.ldo = s.d;
     g.tma_store = (s.d % 64) == 0;
     if (g.tma_store && (rc = encode_2d(&g.tma_out, y, s.P, s.d, s.d, 32)) != SPX_OK) return rc;
-    g.pos_weight = da.sorted_weights;
+    g.pos_weight = sorted_w;
     if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn2m, c.st, true)) != SPX_OK) return rc;
   }
   c.mark(5);
   return SPX_OK;
 }
 
-// K4 (shared half): shared SwiGLU of every token into `shared_out` [T, d].
-// Shared SwiGLU.  With `y` given, the down projection's epilogue also does
-// the combine: out = bf16(shared + the token's k expert rows of y), written
-// to `out` (the layer update); otherwise `out` receives the shared output.
-int stage_shared(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, uint16_t* out,
-                 const uint16_t* y = nullptr, const int* rank = nullptr, const uint16_t* residual = nullptr,
-                 uint16_t* residual_out = nullptr) {
+// K3: expert GEMM1 (+SwiGLU) and GEMM2 over the dispatched rows of `hidden`
+// (`xa` = hidden padded), both lanes; weighted rows land in Y (sorted order).
+int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hidden, const uint16_t* xa,
+                  const DispatchArgs& da, int64_t ld_hidden = 0) {
+  const bool mx = da.lane_mx != nullptr;
+  if (mx) {
+    if (int rc = stage_quantize_x(c, hidden, ld_hidden); rc != SPX_OK) return rc;
+  }
+  const ExpertPass p{w->expert_w1, w->expert_w2, w->expert_w1_mx, w->expert_w1_mx_scales, w->expert_w2_mx,
+                     w->expert_w2_mx_scales, c.s.E, da.tiles, da.num_tiles, mx ? da.tiles_mx : nullptr,
+                     mx ? da.num_tiles_mx : nullptr, 0};
+  return stage_expert_gemms(c, xa, da.src_row, da.sorted_weights, p);
+}
+
+// K4 (shared half), first GEMM: shared gate/up with the SwiGLU into the
+// workspace's shared hidden rows.
+int stage_shared_gemm1(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa) {
   const Shape& s = c.s;
   int rc = SPX_OK;
   uint16_t* hs = at<uint16_t>(c.ws, c.L.shared_hidden);
-  {
-    // Large batches: CTA pairs (256-row tiles; each CTA loads one of the
-    // [gate | up] halves of the B tile).
-    const bool pair = !s.small && (2 * s.cs) % 32 == 0;
-    GemmArgs g = base_args(kEpiSwiglu, 2 * s.cs, s.kd / 64, c.status);
-    if (pair) g.stages = gemm_pair_pick_stages(2 * s.cs);
-    if ((rc = encode_2d(&g.tma_a, xa, s.T, s.kd, s.kd, kTileRows)) != SPX_OK) return rc;
-    if ((rc = encode_3d(&g.tma_b, w->shared_w1, 1, static_cast<int64_t>(s.ncs) * 2 * s.cs, s.kd,
-                        pair ? s.cs : 2 * s.cs)) != SPX_OK)
-      return rc;
-    g.m_rows = static_cast<int>(s.T);
-    g.chunk = s.cs;
-    g.h_cols = s.ksp;
-    g.out = hs;
-    g.ldo = s.ksp;
-    rc = pair ? launch_gemm_pair(kEpiSwiglu, g, ceil_div(s.T, 2 * kTileRows), s.ncs, c.st)
-              : launch_gemm(kEpiSwiglu, g, ceil_div(s.T, kTileRows), s.ncs, c.st);
-    if (rc != SPX_OK) return rc;
-  }
+  // Large batches: CTA pairs (256-row tiles; each CTA loads one of the
+  // [gate | up] halves of the B tile).
+  const bool pair = !s.small && (2 * s.cs) % 32 == 0;
+  GemmArgs g = base_args(kEpiSwiglu, 2 * s.cs, s.kd / 64, c.status);
+  if (pair) g.stages = gemm_pair_pick_stages(2 * s.cs);
+  if ((rc = encode_2d(&g.tma_a, xa, s.T, s.kd, s.kd, kTileRows)) != SPX_OK) return rc;
+  if ((rc = encode_3d(&g.tma_b, w->shared_w1, 1, static_cast<int64_t>(s.ncs) * 2 * s.cs, s.kd,
+                      pair ? s.cs : 2 * s.cs)) != SPX_OK)
+    return rc;
+  g.m_rows = static_cast<int>(s.T);
+  g.chunk = s.cs;
+  g.h_cols = s.ksp;
+  g.out = hs;
+  g.ldo = s.ksp;
+  rc = pair ? launch_gemm_pair(kEpiSwiglu, g, ceil_div(s.T, 2 * kTileRows), s.ncs, c.st)
+            : launch_gemm(kEpiSwiglu, g, ceil_div(s.T, kTileRows), s.ncs, c.st);
+  if (rc != SPX_OK) return rc;
   c.mark(6);
+  return SPX_OK;
+}
+
+// K4 (shared half), down projection.  With `y` given, its epilogue also does
+// the combine: out = bf16(shared + the token's k expert rows of y), written
+// to `out` (the layer update); otherwise `out` receives the shared output.
+int stage_shared_gemm2(const Ctx& c, const spx_packed_weights* w, uint16_t* out, const uint16_t* y = nullptr,
+                       const int* rank = nullptr, const uint16_t* residual = nullptr,
+                       uint16_t* residual_out = nullptr) {
+  const Shape& s = c.s;
+  int rc = SPX_OK;
+  uint16_t* hs = at<uint16_t>(c.ws, c.L.shared_hidden);
   const int epi = y != nullptr ? kEpiCombine : kEpiStore;
   GemmArgs g = base_args(epi, s.bn_sd, s.ksp / 64, c.status);
   if ((rc = encode_2d(&g.tma_a, hs, s.T, s.ksp, s.ksp, kTileRows)) != SPX_OK) return rc;
@@ -456,6 +502,15 @@ int stage_shared(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, 
   g.comb_res = residual;
   g.comb_res_out = residual_out;
   return launch_gemm(epi, g, ceil_div(s.T, kTileRows), s.gn_sd, c.st);
+}
+
+// K4 (shared half): shared SwiGLU of every token, both GEMMs (see
+// stage_shared_gemm2 for `y`).
+int stage_shared(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, uint16_t* out,
+                 const uint16_t* y = nullptr, const int* rank = nullptr, const uint16_t* residual = nullptr,
+                 uint16_t* residual_out = nullptr) {
+  if (int rc = stage_shared_gemm1(c, w, xa); rc != SPX_OK) return rc;
+  return stage_shared_gemm2(c, w, out, y, rank, residual, residual_out);
 }
 
 // The combine can ride on the shared down projection's epilogue.  Not for
@@ -808,6 +863,120 @@ int spx_layer_route(const spx_layer_dims* dims, const spx_packed_weights* w, con
   DispatchArgs da = layer_dispatch_args(c, dims, w, out);
   da.lane_mx = nullptr;  // the experts run elsewhere
   return launch_dispatch(da, c.st);
+}
+
+// ---------------------------------------------------------------- paged experts
+// The layer forward in three calls around a device cache of expert weights
+// (experts/bank.py:821-899 with offload.py): begin (router, dispatch, the
+// MXFP8 quantisation of the hidden rows, shared GEMM1), one experts call per
+// page, finish (shared down projection + combine).
+
+int spx_layer_paged_begin(const spx_layer_dims* dims, const spx_packed_weights* w, const uint16_t* hidden,
+                          const spx_layer_outputs* out, void* workspace, void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (out == nullptr || hidden == nullptr) return SPX_ERR_INVALID_ARG;
+  if (workspace == nullptr) return SPX_ERR_WORKSPACE;
+  if (out->router_scores == nullptr || out->expert_ids == nullptr || out->routing_weights == nullptr ||
+      out->expert_counts == nullptr)
+    return SPX_ERR_INVALID_ARG;
+  if (int rc = check_layer_weights(s, dims, w, true, false, true); rc != SPX_OK) return rc;
+  if (w->expert_lane_mxfp8 != nullptr && !s.mx) return SPX_ERR_INVALID_ARG;
+  if (!aligned16(hidden) || !aligned16(workspace)) return SPX_ERR_ALIGNMENT;
+  const Layout L = make_layout(s);
+  const Ctx c{s, L, workspace, static_cast<cudaStream_t>(stream), at<int>(workspace, L.small), out->stage_events};
+  int rc = SPX_OK;
+  c.mark(0);
+  const uint16_t* xa = nullptr;
+  if ((rc = stage_pad(c, hidden, &xa)) != SPX_OK) return rc;
+  if ((rc = stage_router_route(c, dims, w, xa, out)) != SPX_OK) return rc;
+  c.mark(2);
+  const DispatchArgs da = layer_dispatch_args(c, dims, w, out);
+  if ((rc = launch_dispatch(da, c.st)) != SPX_OK) return rc;
+  c.mark(3);
+  if (da.lane_mx != nullptr && (rc = stage_quantize_x(c, hidden, 0)) != SPX_OK) return rc;
+  if (s.S > 0 && (rc = stage_shared_gemm1(c, w, xa)) != SPX_OK) return rc;
+  return SPX_OK;
+}
+
+int spx_layer_paged_experts(const spx_layer_dims* dims, const spx_packed_weights* cache, int32_t cache_slots,
+                            const int32_t* page_slot, int32_t sm_limit, const uint16_t* hidden, void* workspace,
+                            void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (cache == nullptr || page_slot == nullptr || hidden == nullptr || cache_slots < 1 || sm_limit < 0)
+    return SPX_ERR_INVALID_ARG;
+  if (workspace == nullptr) return SPX_ERR_WORKSPACE;
+  if (int rc = check_layer_weights(s, dims, cache, false, true, false); rc != SPX_OK) return rc;
+  if (!aligned16(hidden) || !aligned16(workspace)) return SPX_ERR_ALIGNMENT;
+  const Layout L = make_layout(s);
+  const Ctx c{s, L, workspace, static_cast<cudaStream_t>(stream), at<int>(workspace, L.small), nullptr};
+  const bool mx = s.mx && cache->expert_lane_mxfp8 != nullptr;
+  int* small = at<int>(workspace, L.small);
+  PageTilesArgs pt{};
+  pt.tiles = at<int4>(workspace, L.tiles);
+  pt.num_tiles = small + 2;
+  pt.tiles_mx = mx ? at<int4>(workspace, L.tiles_mx) : nullptr;
+  pt.num_tiles_mx = mx ? small + 3 : nullptr;
+  pt.page_slot = page_slot;
+  pt.num_experts = s.E;
+  pt.out = at<int4>(workspace, L.tiles_page);
+  pt.out_count = small + 4;
+  pt.out_mx = mx ? at<int4>(workspace, L.tiles_mx_page) : nullptr;
+  pt.out_count_mx = mx ? small + 5 : nullptr;
+  if (int rc = launch_page_tiles(pt, c.st); rc != SPX_OK) return rc;
+  const uint16_t* xa = s.kd != s.d ? at<uint16_t>(workspace, L.x_pad) : hidden;
+  const ExpertPass p{cache->expert_w1, cache->expert_w2, cache->expert_w1_mx, cache->expert_w1_mx_scales,
+                     cache->expert_w2_mx, cache->expert_w2_mx_scales, cache_slots, pt.out, pt.out_count,
+                     pt.out_mx, pt.out_count_mx, sm_limit};
+  return stage_expert_gemms(c, xa, at<int>(workspace, L.src_row), at<uint16_t>(workspace, L.sorted_w), p);
+}
+
+int spx_layer_paged_finish(const spx_layer_dims* dims, const spx_packed_weights* w, const uint16_t* hidden,
+                           const spx_layer_outputs* out, void* workspace, void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (out == nullptr || hidden == nullptr || out->update == nullptr) return SPX_ERR_INVALID_ARG;
+  if (workspace == nullptr) return SPX_ERR_WORKSPACE;
+  if (int rc = check_layer_weights(s, dims, w, false, false, true); rc != SPX_OK) return rc;
+  if (!aligned16(hidden) || !aligned16(out->update) || !aligned16(workspace)) return SPX_ERR_ALIGNMENT;
+  const Layout L = make_layout(s);
+  const Ctx c{s, L, workspace, static_cast<cudaStream_t>(stream), at<int>(workspace, L.small), out->stage_events};
+  int rc = SPX_OK;
+  uint16_t* y = at<uint16_t>(workspace, L.y);
+  const int* rank = out->pair_rank != nullptr ? out->pair_rank : at<int>(workspace, L.rank);
+  if (fused_combine_ok(s)) {
+    if ((rc = stage_shared_gemm2(c, w, out->update, y, rank)) != SPX_OK) return rc;
+  } else {
+    uint16_t* so = nullptr;
+    if (s.S > 0) {
+      so = at<uint16_t>(workspace, L.shared_out);
+      if ((rc = stage_shared_gemm2(c, w, so)) != SPX_OK) return rc;
+    }
+    if ((rc = launch_combine(y, rank, nullptr, so, s.T, s.d, s.k, out->update, c.st)) != SPX_OK) return rc;
+  }
+  c.mark(7);
+  return SPX_OK;
+}
+
+int spx_stage_expert_slots(const void* const* src, void* const* dst, const int64_t* bytes, int32_t arrays,
+                           const int32_t* pairs, int32_t n, int32_t num_experts, int32_t slots, int32_t ctas,
+                           void* stream) {
+  if (src == nullptr || dst == nullptr || bytes == nullptr || arrays < 1 || arrays > kStageMaxArrays || n < 0)
+    return SPX_ERR_INVALID_ARG;
+  StageSlotsArgs a{};
+  for (int i = 0; i < arrays; ++i) {
+    a.src[i] = static_cast<const uint8_t*>(src[i]);
+    a.dst[i] = static_cast<uint8_t*>(dst[i]);
+    a.bytes[i] = bytes[i];
+  }
+  a.arrays = arrays;
+  a.pairs = pairs;
+  a.num_pairs = n;
+  a.num_experts = num_experts;
+  a.slots = slots;
+  a.ctas = ctas;
+  return launch_stage_slots(a, static_cast<cudaStream_t>(stream));
 }
 
 // ---------------------------------------------------------------- backward

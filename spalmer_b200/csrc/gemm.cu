@@ -979,7 +979,7 @@ static int launch_gemm_t(const GemmArgs& a, int grid_m, int grid_n, cudaStream_t
   if (smem > kGemmSmemBudget) return SPX_ERR_INVALID_ARG;
   if (int rc = ensure_max_dynamic_smem(reinterpret_cast<const void*>(gemm_kernel<EPI, MX>)); rc != SPX_OK) return rc;
   // Persistent grid: one CTA per SM, never more CTAs than (upper bound of) tiles.
-  const int sms = device_sm_count();
+  const int sms = a.max_ctas > 0 && a.max_ctas < device_sm_count() ? a.max_ctas : device_sm_count();
   const int64_t tiles = static_cast<int64_t>(grid_m) * grid_n;
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);
   GemmArgs b = a;

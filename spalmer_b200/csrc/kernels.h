@@ -135,6 +135,7 @@ struct GemmArgs {
   const uint16_t* comb_res;  // kEpiCombine: residual stream [rows, ldo] or null; with it
   uint16_t* comb_res_out;    //   comb_res_out = bf16(residual + update) (out may then be null)
   int64_t ldy;
+  int max_ctas;              // persistent grid cap (0 = every SM): leaves SMs to concurrent work
   int* status;
 };
 
@@ -193,6 +194,39 @@ int launch_combine_residual(const uint16_t* y, const int* rank, const uint16_t* 
 // rows of x written with stride ld_out (columns [d, ld_out) zeroed).
 int launch_rmsnorm_rows(const uint16_t* h, const uint16_t* w, float eps, int64_t rows, int d, uint16_t* out,
                         int ld_out, cudaStream_t stream);
+// One page of a paged expert pass: the tiles of the tables whose expert has
+// page_slot[e] >= 0, in order, with the group renamed to that cache slot
+// (MXFP8 table optional: tiles_mx null).
+struct PageTilesArgs {
+  const int4* tiles;
+  const int* num_tiles;
+  const int4* tiles_mx;
+  const int* num_tiles_mx;
+  const int* page_slot;  // [num_experts]
+  int num_experts;
+  int4* out;
+  int* out_count;
+  int4* out_mx;
+  int* out_count_mx;
+};
+int launch_page_tiles(const PageTilesArgs& a, cudaStream_t stream);
+// Whole experts into cache slots: dst[a] + slot * bytes[a] <- src[a] + expert * bytes[a]
+// for each (expert, slot) of `pairs` (device int32 [num_pairs][2]); sources may be
+// mapped page-locked host memory (read by the GPU over the host link).
+constexpr int kStageMaxArrays = 8;
+struct StageSlotsArgs {
+  const uint8_t* src[kStageMaxArrays];
+  uint8_t* dst[kStageMaxArrays];
+  int64_t bytes[kStageMaxArrays];
+  int arrays;
+  const int* pairs;
+  int num_pairs;
+  int num_experts;
+  int slots;
+  int ctas;     // persistent grid (CTAs of 512 threads)
+  int* status;  // device status word | null
+};
+int launch_stage_slots(StageSlotsArgs a, cudaStream_t stream);
 int launch_combine(const uint16_t* y, const int* rank, const uint16_t* weights, const uint16_t* base, int64_t tokens,
                    int d, int k, uint16_t* out, cudaStream_t stream);
 // out[i] = src[index[i] / index_div] (BF16 rows of d elements).

@@ -13,8 +13,11 @@ submodules below create their parameters in the reference's order
 GEMM, exact least-surprise top-k, dispatch, grouped expert SwiGLU, shared
 SwiGLU fused with the combine, routing statistics and the load-balance loss,
 with no host synchronisation.  There is no CPU or PyTorch fallback: inputs
-must be BF16 CUDA tensors and the library must be built.  The backward pass is
-not implemented yet, so ``forward`` refuses to run when autograd would need it.
+must be BF16 CUDA tensors and the library must be built.  Under autograd the
+same native forward runs inside an ``autograd.Function`` whose backward calls
+``spx_layer_backward`` (BF16 experts).  With expert offload enabled
+(``spalmer_b200.offload``) the expert bank stays on the CPU and the forward
+pages the selected experts through a bounded device cache.
 """
 
 from __future__ import annotations
@@ -87,6 +90,8 @@ class MicroExpertBank(nn.Module):
         self.up_proj = nn.Parameter(torch.randn(e, d, i) * std)
         self.down_proj = nn.Parameter(torch.randn(e, i, d) * std)
 
+        object.__setattr__(self, "_offload", None)  # PagedExpertCache while offloaded
+
     @property
     def num_experts(self) -> int:
         return self.config.num_experts
@@ -94,6 +99,120 @@ class MicroExpertBank(nn.Module):
     @property
     def parameters_per_expert(self) -> int:
         return self.gate_proj[0].numel() + self.up_proj[0].numel() + self.down_proj[0].numel()
+
+    # ---- expert offload (bank.py:95-407); the cache itself is spalmer_b200.offload.PagedExpertCache
+    @property
+    def expert_offload_enabled(self) -> bool:
+        return self._offload is not None
+
+    @property
+    def expert_paging_enabled(self) -> bool:
+        return self._offload is not None and self._offload.paging
+
+    @property
+    def expert_cache_capacity(self) -> int | None:
+        return None if self._offload is None else self._offload.capacity
+
+    @property
+    def expert_offload_counters(self) -> tuple[int, int, int, int]:
+        """Stage operations, transferred rows, evicted rows, transferred bytes
+        (bytes of the BF16 masters, as the reference counts them)."""
+
+        return (0, 0, 0, 0) if self._offload is None else tuple(self._offload.policy.counters)
+
+    @property
+    def cached_expert_ids(self) -> tuple[int, ...]:
+        return () if self._offload is None else self._offload.policy.cached_ids
+
+    @property
+    def expert_cache_device(self) -> torch.device | None:
+        return None if self._offload is None else self._offload.target
+
+    @property
+    def expert_master_device(self) -> torch.device:
+        devices = {p.device for p in self.parameters(recurse=False)}
+        if len(devices) != 1:
+            raise RuntimeError(f"expert master projections span devices: {sorted(map(str, devices))}")
+        return next(iter(devices))
+
+    @property
+    def expert_master_bytes(self) -> int:
+        return sum(p.numel() * p.element_size() for p in self.parameters(recurse=False))
+
+    @property
+    def expert_masters_pinned(self) -> bool:
+        params = tuple(self.parameters(recurse=False))
+        return bool(params) and all(p.is_pinned() for p in params)
+
+    @property
+    def expert_cache_bytes(self) -> int:
+        """Physical bytes of the device cache (every slot, packed layouts)."""
+
+        return 0 if self._offload is None else self._offload.cache_bytes
+
+    @property
+    def expert_cache_index_bytes(self) -> int:
+        """Bytes of one expert-to-slot table ([E] int32) handed to the kernels."""
+
+        return 0 if self._offload is None else 4 * self.num_experts
+
+    def _apply(self, fn, recurse: bool = True):
+        # Offloaded masters stay on the CPU when the module around them moves.
+        if self._offload is not None:
+            return self
+        return super()._apply(fn, recurse=recurse)
+
+    @torch.no_grad()
+    def _prepare_expert_offload(self, target_device: torch.device, *, capacity: int, non_blocking: bool,
+                                pin_memory: bool, paging: bool = False) -> None:
+        """Keep the masters on the CPU and prepare an empty device cache (bank.py:195-238)."""
+
+        from spalmer_b200.offload import PagedExpertCache
+
+        if self.training:
+            raise RuntimeError("expert offload is inference-only; put the model in eval mode first")
+        if self._offload is not None:
+            raise RuntimeError("expert offload is already enabled for this bank")
+        if not 1 <= capacity <= self.num_experts:
+            raise ValueError(f"expert cache capacity must lie in [1, {self.num_experts}]; got {capacity}")
+        self.to(device="cpu")
+        if pin_memory:
+            for p in self.parameters(recurse=False):
+                try:
+                    p.data = p.detach().pin_memory()
+                except RuntimeError:
+                    break  # page locking is an optimisation; telemetry reports what happened
+        object.__setattr__(self, "_offload", PagedExpertCache(self, torch.device(target_device), capacity,
+                                                              non_blocking=non_blocking, paging=paging))
+
+    @torch.no_grad()
+    def _stage_expert_rows(self, expert_ids: tuple[int, ...], *, force: bool = False) -> tuple[int, int, int]:
+        """Stage exactly ``expert_ids`` (sorted, unique); returns rows in,
+        rows out, bytes in (bank.py:241-332)."""
+
+        cache = self._offload
+        if cache is None:
+            raise RuntimeError("expert offload has not been prepared for this bank")
+        if any(p.device.type != "cpu" for p in self.parameters(recurse=False)):
+            raise RuntimeError("offloaded expert master parameters must remain on CPU")
+        plan = cache.policy.plan_rows(tuple(expert_ids), force=force)
+        if plan is None:
+            return 0, 0, 0
+        cache.stage_now(plan)
+        return len(plan.incoming), len(plan.evicted), len(plan.incoming) * cache.policy.bytes_per_row
+
+    @torch.no_grad()
+    def _stage_execution_page(self, required_ids: tuple[int, ...]) -> None:
+        """Stage the required ids and keep recent rows in spare slots (bank.py:341-365)."""
+
+        cache = self._offload
+        if cache is None or not cache.paging:
+            raise RuntimeError("layer-local expert paging is not enabled")
+        plan, lru = cache.policy.plan_page(required_ids)
+        cache.stage_now(plan, lru)
+
+    def _clear_expert_offload(self) -> None:
+        object.__setattr__(self, "_offload", None)
 
 
 class SwiGLU(nn.Module):
@@ -391,10 +510,15 @@ class B200MicroExpertChannelMixer(nn.Module):
 
     def _packed(self, device: torch.device, tokens: int, top_k: int) -> dict[str, Tensor | None]:
         """Kernel layouts of the weights, one cache entry per batch class
-        (decode-sized batches of <= 256 tokens use narrower GEMM1 chunks)."""
+        (decode-sized batches of <= 256 tokens use narrower GEMM1 chunks).
+        With expert offload the expert bank is packed by its cache instead."""
 
         tensors = self._weight_tensors()
-        key = (device,) + tuple(
+        offloaded = self.experts.expert_offload_enabled
+        if offloaded:
+            for name in ("gate_proj", "up_proj", "down_proj"):
+                tensors[name] = None
+        key = (device, offloaded) + tuple(
             (None if t is None else (t.data_ptr(), t._version, t.dtype)) for t in tensors.values()
         )
         batch_class = tokens <= SMALL_BATCH_TOKENS
@@ -418,8 +542,8 @@ class B200MicroExpertChannelMixer(nn.Module):
         empty = lambda n: torch.empty(max(1, n), dtype=torch.int16, device=device)  # noqa: E731
         packed = {
             "router_weight": empty(sizes.router_weight),
-            "expert_w1": empty(sizes.expert_w1),
-            "expert_w2": empty(sizes.expert_w2),
+            "expert_w1": None if offloaded else empty(sizes.expert_w1),
+            "expert_w2": None if offloaded else empty(sizes.expert_w2),
             "shared_w1": empty(sizes.shared_w1) if sizes.shared_w1 else None,
             "shared_w2": empty(sizes.shared_w2) if sizes.shared_w2 else None,
             "router_bias": bits["router_bias"],
@@ -436,7 +560,7 @@ class B200MicroExpertChannelMixer(nn.Module):
             ),
             "spx_pack_weights",
         )
-        if dims.mxfp8_lane:
+        if dims.mxfp8_lane and not offloaded:
             mx_bytes = lambda n: torch.empty(max(16, n), dtype=torch.uint8, device=device)  # noqa: E731
             for name in ("expert_w1_mx", "expert_w1_mx_scales", "expert_w2_mx", "expert_w2_mx_scales"):
                 packed[name] = mx_bytes(getattr(sizes, name))
@@ -514,7 +638,8 @@ class B200MicroExpertChannelMixer(nn.Module):
         config = self.config
         if hidden_states.shape[-1] != config.d_model:
             raise ValueError(f"expected trailing dimension {config.d_model}; got {hidden_states.shape[-1]}")
-        if torch.is_grad_enabled() and (
+        # Expert offload is inference-only (offload.py:15-18): its forward records no graph.
+        if torch.is_grad_enabled() and not self.experts.expert_offload_enabled and (
             hidden_states.requires_grad or any(p.requires_grad for p in self.parameters())
         ):
             if router_logits is not None:
@@ -586,7 +711,11 @@ class B200MicroExpertChannelMixer(nn.Module):
             stage_events=None if events is None else _lib.ctypes.addressof(events),
         )
         stream = torch.cuda.current_stream(device).cuda_stream
-        if block is None:
+        if self.experts.expert_offload_enabled:
+            if block is not None:
+                raise RuntimeError("the fused block path needs the expert bank on the device")
+            self._run_paged(dims, pw, x, outs, ws, lanes)
+        elif block is None:
             _lib.check(lib.spx_layer_forward(dims, pw, x.data_ptr(), outs, ws.data_ptr(), stream),
                        "spx_layer_forward")
         else:
@@ -605,7 +734,7 @@ class B200MicroExpertChannelMixer(nn.Module):
             "expert_quantization_error": torch.zeros(E, dtype=torch.float32, device=device),
             "promoted_experts": controller.promoted_mask.detach().clone(),
             "resident_experts": residency.resident_mask.detach().clone(),
-            "expert_paging": False,
+            "expert_paging": self.experts.expert_paging_enabled,
             "routing_full_pool": full_pool,
             "active_experts_per_token": k,
             "num_active_experts": stats[5],
@@ -620,6 +749,49 @@ class B200MicroExpertChannelMixer(nn.Module):
         }
         return ChannelMixerOutput(update=update, state=None, auxiliary_loss=aux[0], metrics=metrics)
 
+
+    def _run_paged(self, dims: _lib.LayerDims, pw: _lib.PackedWeights, x: Tensor, outs: _lib.LayerOutputs,
+                   ws: Tensor, lanes: Tensor | None) -> None:
+        """The layer with the expert bank behind its device cache
+        (bank.py:821-899): route and dispatch, read the per-expert pair counts
+        while shared GEMM1 runs, stage and execute the pages, combine."""
+
+        lib = _lib.load()
+        cache = self.experts._offload
+        device = x.device
+        compute = torch.cuda.current_stream(device)
+        E = self.config.num_experts
+        counts = torch.empty(E, dtype=torch.int32, device=device)
+        outs.expert_counts = counts.data_ptr()
+        if getattr(self, "_paged_sync", None) is None:
+            ev = torch.cuda.Event()
+            ev.record(compute)  # creates the event handle
+            object.__setattr__(self, "_paged_sync", (ev, torch.cuda.Stream(device)))
+        dispatched, side = self._paged_sync
+        events = (_lib.ctypes.c_void_p * _lib.STAGE_EVENTS)()
+        events[3] = dispatched.cuda_event  # recorded by the library once the dispatch is queued
+        outs.stage_events = _lib.ctypes.addressof(events)
+        _lib.check(lib.spx_layer_paged_begin(dims, pw, x.data_ptr(), outs, ws.data_ptr(), compute.cuda_stream),
+                   "spx_layer_paged_begin")
+        outs.stage_events = None
+        host_counts = torch.empty(E, dtype=torch.int32, pin_memory=True)
+        side.wait_event(dispatched)
+        with torch.cuda.stream(side):
+            host_counts.copy_(counts, non_blocking=True)
+            read = torch.cuda.Event()
+            read.record(side)
+        counts.record_stream(side)
+        read.synchronize()
+
+        def run_chunk(page_slot: Tensor, sm_limit: int) -> None:
+            cpw = cache.packed_weights(lanes)
+            _lib.check(lib.spx_layer_paged_experts(dims, cpw, cache.capacity, page_slot.data_ptr(), sm_limit,
+                                                   x.data_ptr(), ws.data_ptr(), compute.cuda_stream),
+                       "spx_layer_paged_experts")
+
+        cache.run_pages(host_counts.numpy(), run_chunk)
+        _lib.check(lib.spx_layer_paged_finish(dims, pw, x.data_ptr(), outs, ws.data_ptr(), compute.cuda_stream),
+                   "spx_layer_paged_finish")
 
     # ---- training: forward through the native kernels, backward through spx_layer_backward
     def _trainable(self) -> list[tuple[str, Tensor]]:
@@ -819,9 +991,9 @@ class B200ChannelBlock(nn.Module):
 
     def forward(self, hidden_states: Tensor) -> tuple[Tensor, ChannelMixerOutput]:
         mixer = self.channel_mixer
-        if torch.is_grad_enabled() and (
+        if mixer.experts.expert_offload_enabled or (torch.is_grad_enabled() and (
             hidden_states.requires_grad or any(p.requires_grad for p in self.parameters())
-        ):
+        )):
             out = mixer(self.channel_norm(hidden_states))
             return hidden_states + out.update, out
         if hidden_states.ndim != 3 or hidden_states.shape[-1] != mixer.config.d_model:
