@@ -262,6 +262,24 @@ int spx_block_channel_forward(const spx_layer_dims* dims, const spx_packed_weigh
                               const uint16_t* norm_weight, float eps, const uint16_t* hidden,
                               const spx_layer_outputs* outputs, uint16_t* hidden_out, void* workspace, void* stream);
 
+/* ---- NVFP4 (experts/native.py:205-302, the ("nvfp4", "nvfp4") pair)
+ * E2M1 values (two per byte, the even element in the low nibble), one UE4M3
+ * scale per 16 elements along K, one FP32 per-tensor scale amax / (448 * 6)
+ * per operand -- NVFP4Tensor.to_nvfp4(v, per_tensor_scale=...), restated.
+ * spx_nvfp4_quantize_rows: _pack_nvfp4 of a BF16 matrix [rows, cols]:
+ *   values [rows, kp/2] bytes, scales [rows, kp/16] bytes (kp = cols rounded
+ *   up to 256, zero beyond cols), *amax = the matrix's largest |v| (float,
+ *   device).
+ * spx_nvfp4_mm_nt: native_nvfp4_linear's forward, out [m, n] =
+ *   bf16(pts_l * pts_r * (deq(left) @ deq(right_rows)^T)) with FP32
+ *   accumulation on tcgen05 kind::mxf4nvf4 MMAs (K = 64, block16 scales);
+ *   workspace from spx_nvfp4_mm_workspace. */
+int spx_nvfp4_quantize_rows(const uint16_t* src, int64_t rows, int32_t cols, uint8_t* values, uint8_t* scales,
+                            float* amax, void* stream);
+size_t spx_nvfp4_mm_workspace(int64_t m, int64_t n, int64_t k);
+int spx_nvfp4_mm_nt(const uint16_t* left, const uint16_t* right_rows, int64_t m, int64_t n, int64_t k,
+                    uint16_t* out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- paged experts: the layer forward around a bounded device cache of expert weights
  * Reference: MicroExpertBank._execute_paged_grouped (experts/bank.py:821-899)
  * with the cache of offload.py / bank.py:241-365: routing over the full pool,

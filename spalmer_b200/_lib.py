@@ -55,6 +55,9 @@ EXPORTED = (
     "spx_layer_paged_experts",
     "spx_layer_paged_finish",
     "spx_stage_expert_slots",
+    "spx_nvfp4_quantize_rows",
+    "spx_nvfp4_mm_workspace",
+    "spx_nvfp4_mm_nt",
 )
 
 ABI_VERSION = 6
@@ -238,6 +241,12 @@ def load() -> ctypes.CDLL:
             ctypes.c_int,
             [_vp, _vp, _vp, ctypes.c_int32, _vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
              _vp],
+        ),
+        "spx_nvfp4_quantize_rows": (ctypes.c_int, [_vp, ctypes.c_int64, ctypes.c_int32, _vp, _vp, _vp, _vp]),
+        "spx_nvfp4_mm_workspace": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]),
+        "spx_nvfp4_mm_nt": (
+            ctypes.c_int,
+            [_vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp, _vp, ctypes.c_size_t, _vp],
         ),
         "spx_mxfp8_mm_nt": (
             ctypes.c_int,

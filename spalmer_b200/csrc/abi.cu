@@ -7,6 +7,7 @@
 #include <algorithm>
 
 #include "kernels.h"
+#include "nv.cuh"
 #include "sm100.cuh"
 
 namespace spx {
@@ -171,11 +172,11 @@ int sm_count() { return device_sm_count(); }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-GemmArgs base_args(int epi, int bn, int k_blocks, int* status, bool mx = false) {
+GemmArgs base_args(int epi, int bn, int k_blocks, int* status, bool mx = false, bool nv = false) {
   GemmArgs g{};
   g.bn = bn;
   g.k_blocks = k_blocks;
-  g.stages = gemm_pick_stages(bn, k_blocks, mx, epi);
+  g.stages = gemm_pick_stages(bn, k_blocks, mx, epi, nv);
   g.tmem_cols = pow2_at_least(static_cast<uint32_t>(bn));
   g.groups = 1;
   g.status = status;
@@ -721,6 +722,97 @@ int spx_mxfp8_mm_nt(const uint16_t* left, const uint16_t* right_rows, int64_t m,
   g.ld_sfa = kp / kMxBlock;
   g.sfb = rsf;
   return launch_gemm(kEpiStore, g, ceil_div(m, kTileRows), ceil_div(n, L.bn), st, true);
+}
+
+namespace {
+struct NvMmLayout {
+  int64_t kp;
+  int bn;
+  size_t status, amax, lq, lsf, rq, rsf, total;
+};
+
+NvMmLayout nv_mm_layout(int64_t m, int64_t n, int64_t k) {
+  NvMmLayout L{};
+  L.kp = static_cast<int64_t>(round_up(static_cast<size_t>(k > 0 ? k : 1), 256));
+  L.bn = static_cast<int>(std::min<int64_t>(kMxDenseBn, static_cast<int64_t>(round_up(static_cast<size_t>(n), 16))));
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = round_up(off + bytes, kAlign);
+    return at;
+  };
+  L.status = take(64);
+  L.amax = take(16);
+  L.lq = take(static_cast<size_t>(m) * (L.kp / 2));
+  L.lsf = take(static_cast<size_t>(m) * (L.kp / kNvBlock));
+  L.rq = take(static_cast<size_t>(n) * (L.kp / 2));
+  L.rsf = take(nv_atoms_bytes(1, static_cast<int>(n), static_cast<int>(L.kp), L.bn));
+  L.total = off;
+  return L;
+}
+}  // namespace
+
+size_t spx_nvfp4_mm_workspace(int64_t m, int64_t n, int64_t k) {
+  if (m < 0 || n < 0 || k < 0) return 0;
+  return nv_mm_layout(m, n, k).total;
+}
+
+int spx_nvfp4_quantize_rows(const uint16_t* src, int64_t rows, int32_t cols, uint8_t* values, uint8_t* scales,
+                            float* amax, void* stream) {
+  if (rows < 0 || cols < 1) return SPX_ERR_INVALID_ARG;
+  if (rows == 0) return SPX_OK;
+  if (src == nullptr || values == nullptr || scales == nullptr || amax == nullptr) return SPX_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(values) & 7u) != 0) return SPX_ERR_ALIGNMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int kp = round_up_i(cols, 256);
+  if (cudaMemsetAsync(amax, 0, sizeof(float), st) != cudaSuccess) return SPX_ERR_CUDA;
+  int rc = launch_nv_amax(src, rows, cols, cols, amax, st);
+  if (rc == SPX_OK) rc = launch_nv_quantize_rows(src, rows, cols, cols, amax, kp, values, scales, st);
+  return rc;
+}
+
+int spx_nvfp4_mm_nt(const uint16_t* left, const uint16_t* right_rows, int64_t m, int64_t n, int64_t k,
+                    uint16_t* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (m < 0 || n < 0 || k < 0) return SPX_ERR_INVALID_ARG;
+  if (m == 0 || n == 0) return SPX_OK;
+  if (out == nullptr) return SPX_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (k == 0)
+    return cudaMemsetAsync(out, 0, static_cast<size_t>(m) * n * 2, st) == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+  if (left == nullptr || right_rows == nullptr) return SPX_ERR_INVALID_ARG;
+  if (m > (int64_t(1) << 31) - 1 || n > (int64_t(1) << 31) - 1 || k > (int64_t(1) << 30)) return SPX_ERR_UNSUPPORTED;
+  const NvMmLayout L = nv_mm_layout(m, n, k);
+  if (workspace == nullptr || workspace_bytes < L.total) return SPX_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return SPX_ERR_ALIGNMENT;
+  float* amax = at<float>(workspace, L.amax);
+  uint8_t* lq = at<uint8_t>(workspace, L.lq);
+  uint8_t* lsf = at<uint8_t>(workspace, L.lsf);
+  uint8_t* rq = at<uint8_t>(workspace, L.rq);
+  uint8_t* rsf = at<uint8_t>(workspace, L.rsf);
+  const int kp = static_cast<int>(L.kp);
+  if (cudaMemsetAsync(amax, 0, 2 * sizeof(float), st) != cudaSuccess) return SPX_ERR_CUDA;
+  int rc = launch_nv_amax(left, m, static_cast<int>(k), k, amax, st);
+  if (rc == SPX_OK) rc = launch_nv_amax(right_rows, n, static_cast<int>(k), k, amax + 1, st);
+  if (rc == SPX_OK) rc = launch_nv_quantize_rows(left, m, static_cast<int>(k), k, amax, kp, lq, lsf, st);
+  if (rc == SPX_OK)
+    rc = launch_nv_quantize_b(kMxSrcRows, right_rows, nullptr, 1, static_cast<int>(n), static_cast<int>(n),
+                              static_cast<int>(k), kp, L.bn, 0, 0, 0, k, amax + 1, rq, rsf, st);
+  if (rc != SPX_OK) return rc;
+  GemmArgs g = base_args(kEpiStore, L.bn, kp / 256, at<int>(workspace, L.status), true, true);
+  if ((rc = encode_2d(&g.tma_a, lq, m, kp / 2, kp / 2, kTileRows, 1)) != SPX_OK) return rc;
+  if ((rc = encode_3d(&g.tma_b, rq, 1, n, kp / 2, L.bn, 1)) != SPX_OK) return rc;
+  g.m_rows = static_cast<int>(m);
+  g.n_valid = static_cast<int>(n);
+  g.out = out;
+  g.ldo = n;
+  g.sfa = lsf;
+  g.ld_sfa = kp / kNvBlock;
+  g.sfb = rsf;
+  g.nv_amax_a = amax;
+  g.nv_amax_b = amax + 1;
+  g.nv_b_stride = 4;
+  g.nv_b_off = 0;
+  return launch_gemm(kEpiStore, g, ceil_div(m, kTileRows), ceil_div(n, L.bn), st, true, true);
 }
 
 int spx_route(const spx_layer_dims* dims, const uint16_t* logits, const uint16_t* softplus_table,

@@ -181,7 +181,8 @@ __device__ __forceinline__ void finish_dispatch(const DispatchArgs& a, int count
     int4* table = mx ? a.tiles_mx : a.tiles;
     for (int t = 0; t < tiles; ++t) {
       const int r0 = t * kTileRows;
-      table[tile_start + t] = make_int4(e, start + r0, min(kTileRows, count - r0), 0);
+      // w repeats the expert: a page of a paged pass renames x to a cache slot
+      table[tile_start + t] = make_int4(e, start + r0, min(kTileRows, count - r0), e);
     }
   }
 

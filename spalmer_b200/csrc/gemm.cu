@@ -40,6 +40,7 @@
 
 #include "kernels.h"
 #include "mx.cuh"
+#include "nv.cuh"
 #include "sm100.cuh"
 
 namespace spx {
@@ -89,9 +90,14 @@ __device__ __forceinline__ void put8(uint16_t* dst, const uint4& v, int n) {
 // One epilogue warp: TMEM lane quadrant `quad` (32 tile rows), output column
 // slices half, half + 2, ... of the tile (two warps share a quadrant).
 // `my_row` is the output row of this thread's tile row.
-template <int EPI>
+// SC (NVFP4 lane): the accumulator is first scaled by alpha0 (alpha1 for the
+// up half of a SwiGLU tile), and a SwiGLU tile raises *amax_out to the
+// largest |hidden| it writes.
+template <int EPI, bool SC = false>
 __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, uint8_t* stage, int quad, int half,
-                                             int lane, int row0, int rows, int n0, int nt, long long my_row) {
+                                             int lane, int row0, int rows, int n0, int nt, long long my_row,
+                                             float alpha0 = 1.0f, float alpha1 = 1.0f, float* amax_out = nullptr) {
+  float hmax = 0.0f;
   constexpr int W = (EPI == kEpiSwiglu) ? 32 : 64;  // output columns per slice
   const int r = quad * 32 + lane;                   // tile row owned by this thread (its TMEM lane)
   const bool live = r < rows;
@@ -110,9 +116,21 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
       tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 32; j += 2) {
-        const float h0 = bfr(silu_fast(bfr(__uint_as_float(g[j])))) * bfr(__uint_as_float(u[j]));
-        const float h1 = bfr(silu_fast(bfr(__uint_as_float(g[j + 1])))) * bfr(__uint_as_float(u[j + 1]));
+        float g0 = __uint_as_float(g[j]), g1 = __uint_as_float(g[j + 1]);
+        float u0 = __uint_as_float(u[j]), u1 = __uint_as_float(u[j + 1]);
+        if constexpr (SC) {
+          g0 *= alpha0;
+          g1 *= alpha0;
+          u0 *= alpha1;
+          u1 *= alpha1;
+        }
+        const float h0 = bfr(silu_fast(bfr(g0))) * bfr(u0);
+        const float h1 = bfr(silu_fast(bfr(g1))) * bfr(u1);
         hw[j / 2] = pack_bf16x2(h0, h1);
+        if constexpr (SC) {
+          if (live && j < w) hmax = fmaxf(hmax, fabsf(bfr(h0)));
+          if (live && j + 1 < w) hmax = fmaxf(hmax, fabsf(bfr(h1)));
+        }
       }
     } else {
       uint32_t v[64];
@@ -124,6 +142,10 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
 #pragma unroll
         for (int j = 0; j < 64; j += 2) {
           float f0 = __uint_as_float(v[j]), f1 = __uint_as_float(v[j + 1]);
+          if constexpr (SC) {
+            f0 *= alpha0;
+            f1 *= alpha0;
+          }
           if (a.bias != nullptr) {
             if (j < w && gcol + j < a.n_valid) f0 += bf16_to_f32(a.bias[gcol + j]);
             if (j + 1 < w && gcol + j + 1 < a.n_valid) f1 += bf16_to_f32(a.bias[gcol + j + 1]);
@@ -157,6 +179,12 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
       uint16_t* dst = out + static_cast<int64_t>(row0 + r) * a.ldo;
       for (int col = a.n_tiles * a.chunk; col < a.h_cols; ++col) dst[col] = 0;
     }
+    if constexpr (SC) {
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) hmax = fmaxf(hmax, __shfl_xor_sync(0xFFFFFFFFu, hmax, off));
+      if (lane == 0 && amax_out != nullptr && hmax > 0.0f)
+        atomicMax(reinterpret_cast<int*>(amax_out), __float_as_int(hmax));
+    }
   }
 }
 
@@ -171,7 +199,7 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
 // bulk group behind.
 __device__ __forceinline__ void run_epilogue_rows(const GemmArgs& a, uint32_t taddr, uint8_t* stage, int quad,
                                                   int half, int lane, int row0, int rows, int n0, float my_w,
-                                                  uint32_t& slices, bool& committed) {
+                                                  uint32_t& slices, bool& committed, float alpha = 1.0f) {
   const int wrows = rows - quad * 32;  // valid rows of this quadrant
   if (wrows <= 0) return;
   uint16_t* out = static_cast<uint16_t*>(a.out);
@@ -194,7 +222,7 @@ __device__ __forceinline__ void run_epilogue_rows(const GemmArgs& a, uint32_t ta
     uint32_t hw[32];
 #pragma unroll
     for (int j = 0; j < 64; j += 2)
-      hw[j / 2] = pack_bf16x2(bfr(__uint_as_float(v[j])) * my_w, bfr(__uint_as_float(v[j + 1])) * my_w);
+      hw[j / 2] = pack_bf16x2(bfr(__uint_as_float(v[j]) * alpha) * my_w, bfr(__uint_as_float(v[j + 1]) * alpha) * my_w);
 #pragma unroll
     for (int c = 0; c < 64; c += 16) stage_put16(buf, lane, c, &hw[c / 2]);
     const int gcol0 = n0 + s0;
@@ -448,7 +476,7 @@ __device__ __forceinline__ bool decode_tile(const GemmArgs& a, int t, int& group
 // every stage of the ring can be in flight at once.
 constexpr uint32_t kCpAsyncArrivals = 32;
 
-template <bool MX>
+template <bool MX, bool NV = false>
 __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa, uint8_t* sb, uint8_t* ssf,
                                                  uint64_t* full, uint64_t* empty, int S, uint32_t a_bytes,
                                                  uint32_t b_bytes, int total, int lane) {
@@ -509,7 +537,22 @@ __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa,
           cp_async16(dst, col + static_cast<int64_t>(src[i]) * a.lda);
         }
       }
-      if constexpr (MX) {
+      if constexpr (MX && NV) {
+        // Four K-64 MMAs per stage: A atom q holds bytes 4q..4q+3 of each
+        // row's 16 scale bytes of the stage; the B atoms of the stage are
+        // contiguous ([q][128-row block]).
+        const uint32_t sf = smem_u32(ssf + s * kNvStageSfBytes);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            cp_async4(sf + q * kMxAtomBytes + lane * 16 + j * 4, a.sfa + sfr[j] * a.ld_sfa + kb * 16 + q * 4);
+        }
+        const int sfb_atoms = 4 * ((bn + 127) / 128);
+        const int64_t atom = ((static_cast<int64_t>(group) * a.n_tiles + nt) * a.k_blocks + kb) * sfb_atoms;
+        for (int q = 0; q < sfb_atoms; ++q)
+          cp_async16(sf + (4 + q) * kMxAtomBytes + lane * 16, a.sfb + (atom + q) * kMxAtomBytes + lane * 16);
+      } else if constexpr (MX) {
         const uint32_t sf = smem_u32(ssf + s * kMxStageSfBytes);
 #pragma unroll
         for (int j = 0; j < 4; ++j) cp_async4(sf + lane * 16 + j * 4, a.sfa + sfr[j] * a.ld_sfa + kb * 4);
@@ -528,8 +571,9 @@ __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa,
 // The TMA producer and the MMA issuer stream k-blocks through the stage ring
 // without stopping at tile boundaries; the accumulator is multi-buffered in
 // TMEM so the epilogue of one tile overlaps the MMAs of the next.
-template <int EPI, bool MX>
+template <int EPI, bool MX, bool NV = false>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ GemmArgs a) {
+  constexpr uint32_t kSfStage = NV ? kNvStageSfBytes : kMxStageSfBytes;
   extern __shared__ uint8_t gemm_smem_raw[];
   uint8_t* smem = align_1024(gemm_smem_raw);
   const int bn = a.bn;
@@ -542,7 +586,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   // Epilogue staging: one 4 KB buffer per epilogue warp, two for the TMA-store epilogue.
   constexpr int kStageBufs = (EPI == kEpiScatter || EPI == kEpiCombine) ? 2 : 1;
   // 1024-byte aligned: the TMA store reads the buffers with the 128B swizzle.
-  uint8_t* stage_all = align_1024(ssf + (MX ? S * kMxStageSfBytes : 0u));
+  uint8_t* stage_all = align_1024(ssf + (MX ? S * kSfStage : 0u));
   uint64_t* full = reinterpret_cast<uint64_t*>(stage_all + kGemmEpilogueWarps * kStageBufs * kStageBytesPerWarp);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;                 // [kMaxAccBufs] accumulator ready
@@ -587,7 +631,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0 && ldst_producer) {
-    produce_cp_async<MX>(a, sa, sb, ssf, full, empty, S, a_bytes, b_bytes, total, lane);
+    produce_cp_async<MX, NV>(a, sa, sb, ssf, full, empty, S, a_bytes, b_bytes, total, lane);
   } else if (warp == 0) {
     // ---------------- TMA producer
     uint32_t it = 0;
@@ -639,7 +683,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
           tc_fence_after();
           const uint32_t a_base = smem_u32(sa + s * a_bytes);
           const uint32_t b_base = smem_u32(sb + s * b_bytes);
-          if constexpr (MX) {
+          if constexpr (MX && NV) {
+            // Per K-64 MMA: its SFA atom and SFB atom(s) -> a rotating
+            // 12-column TMEM slot, then the MMA (scale ids 0).
+            const uint32_t sf_smem = smem_u32(ssf + s * kNvStageSfBytes);
+            const uint32_t nb = bn > 128 ? 2u : 1u;
+            const uint32_t idesc_nv = idesc_nvf4(kTileRows, bn);
+#pragma unroll
+            for (uint32_t q = 0; q < 4; ++q) {
+              const uint32_t slot = (it * 4u + q) % kNvSfSlots;
+              const uint32_t sfa_t = tmem + kMxSfColumn + slot * kNvSfSlotCols;
+              const uint32_t sfb_t = sfa_t + 4u;
+              tmem_cp_32x128b_x4(sfa_t, desc_sf_atom(sf_smem + q * kMxAtomBytes));
+              tmem_cp_32x128b_x4(sfb_t, desc_sf_atom(sf_smem + (4u + q * nb) * kMxAtomBytes));
+              if (nb > 1u) tmem_cp_32x128b_x4(sfb_t + 4u, desc_sf_atom(sf_smem + (5u + q * nb) * kMxAtomBytes));
+              mma_nvf4_ss(acc, desc_kmajor_sw128(a_base + q * 32), desc_kmajor_sw128(b_base + q * 32), idesc_nv,
+                          sfa_t, sfb_t, (kb != 0 || q != 0) ? 1u : 0u);
+            }
+          } else if constexpr (MX) {
             // Scales of this stage -> a rotating TMEM slot (tcgen05.cp and the
             // MMAs that read it are issued in order by this thread).
             const uint32_t sfa_t = tmem + kMxSfColumn + (it % kMxSfSlots) * kMxSfSlotCols;
@@ -694,8 +755,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       if (!go) break;
       tc_fence_after();
       const uint32_t taddr = tmem + b * a.tmem_cols + (static_cast<uint32_t>(quad * 32) << 16);
-      if constexpr (MX && EPI == kEpiSwiglu) {
+      if constexpr (MX && !NV && EPI == kEpiSwiglu) {
         run_epilogue_swiglu_mx(a, taddr, quad, half, lane, row0, rows, nt, &tempty[b]);  // releases early
+      } else if constexpr (NV) {
+        // NVFP4: scale by the per-tensor scales of A (this tile's group) and
+        // of B (gate / up / down of the group) before the BF16 epilogue.
+        const int expert = a.tiles != nullptr ? a.tiles[t / a.n_tiles].w : 0;
+        const float pa = nv_tensor_scale(a.nv_amax_a[expert]);
+        const float* bamax = a.nv_amax_b + static_cast<int64_t>(group) * a.nv_b_stride + a.nv_b_off;
+        const float al0 = pa * nv_tensor_scale(bamax[0]);
+        if constexpr (EPI == kEpiScatter) {
+          run_epilogue_rows(a, taddr, my_stage, quad, half, lane, row0, rows, nt * bn, my_w, slices, committed, al0);
+        } else if constexpr (EPI == kEpiSwiglu) {
+          const float al1 = pa * nv_tensor_scale(bamax[1]);
+          run_epilogue<EPI, true>(a, taddr, my_stage, quad, half, lane, row0, rows, nt * bn, nt, my_row, al0, al1,
+                                  a.nv_amax_out != nullptr ? a.nv_amax_out + expert : nullptr);
+        } else {
+          run_epilogue<EPI, true>(a, taddr, my_stage, quad, half, lane, row0, rows, nt * bn, nt, my_row, al0);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[b]);
       } else if constexpr (EPI == kEpiCombine) {
         run_epilogue_combine(a, taddr, my_stage, quad, half, lane, rows, nt * bn, my_row, &tempty[b]);  // releases early
       } else {
@@ -943,8 +1023,9 @@ int encode_3d(CUtensorMap* map, const void* base, int64_t groups, int64_t rows, 
   return r == CUDA_SUCCESS ? SPX_OK : SPX_ERR_DRIVER;
 }
 
-size_t gemm_smem_bytes(int bn, int stages, bool mx, int epi) {
-  const size_t per_stage = kTileRows * 128 + static_cast<size_t>(bn) * 128 + (mx ? kMxStageSfBytes : 0);
+size_t gemm_smem_bytes(int bn, int stages, bool mx, int epi, bool nv) {
+  const size_t per_stage =
+      kTileRows * 128 + static_cast<size_t>(bn) * 128 + (mx ? (nv ? kNvStageSfBytes : kMxStageSfBytes) : 0);
   const size_t staging =
       static_cast<size_t>(kGemmEpilogueWarps) * kStageBytesPerWarp * (epi == kEpiScatter || epi == kEpiCombine ? 2 : 1);
   return 2048 + static_cast<size_t>(stages) * per_stage + staging + (2 * stages + 2 * kMaxAccBufs) * 8 + 16;
@@ -965,26 +1046,27 @@ int gemm_pair_pick_stages(int bn) {
 
 // As many stages as fit: the persistent producer keeps prefetching the next
 // tile's k-blocks, so stages beyond one tile's K still hide load latency.
-int gemm_pick_stages(int bn, int k_blocks, bool mx, int epi) {
+int gemm_pick_stages(int bn, int k_blocks, bool mx, int epi, bool nv) {
   (void)k_blocks;
   int stages = 2;
   for (int s = 3; s <= 8; ++s)
-    if (gemm_smem_bytes(bn, s, mx, epi) <= kGemmSmemBudget) stages = s;
+    if (gemm_smem_bytes(bn, s, mx, epi, nv) <= kGemmSmemBudget) stages = s;
   return stages;
 }
 
-template <int EPI, bool MX>
+template <int EPI, bool MX, bool NV = false>
 static int launch_gemm_t(const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream) {
-  const size_t smem = gemm_smem_bytes(a.bn, a.stages, MX, EPI);
+  const size_t smem = gemm_smem_bytes(a.bn, a.stages, MX, EPI, NV);
   if (smem > kGemmSmemBudget) return SPX_ERR_INVALID_ARG;
-  if (int rc = ensure_max_dynamic_smem(reinterpret_cast<const void*>(gemm_kernel<EPI, MX>)); rc != SPX_OK) return rc;
+  if (int rc = ensure_max_dynamic_smem(reinterpret_cast<const void*>(gemm_kernel<EPI, MX, NV>)); rc != SPX_OK)
+    return rc;
   // Persistent grid: one CTA per SM, never more CTAs than (upper bound of) tiles.
   const int sms = a.max_ctas > 0 && a.max_ctas < device_sm_count() ? a.max_ctas : device_sm_count();
   const int64_t tiles = static_cast<int64_t>(grid_m) * grid_n;
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);
   GemmArgs b = a;
   b.n_tiles = grid_n;
-  gemm_kernel<EPI, MX><<<grid, kGemmThreads, smem, stream>>>(b);
+  gemm_kernel<EPI, MX, NV><<<grid, kGemmThreads, smem, stream>>>(b);
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 
@@ -1021,9 +1103,25 @@ int launch_gemm_pair(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStr
   }
 }
 
-int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream, bool mx) {
+int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream, bool mx, bool nv) {
   if (grid_m <= 0 || grid_n <= 0) return SPX_OK;
   if (a.bn < 16 || a.bn > 256 || (a.bn % 16) != 0) return SPX_ERR_UNSUPPORTED;
+  if (nv) {
+    // NVFP4: E2M1 operands (128 B = 256 elements per stage), UE4M3 scales per 16.
+    if (a.bn > kMxMaxBn || a.tmem_cols > kMxMaxBn || a.sfa == nullptr || a.sfb == nullptr ||
+        (a.ld_sfa % 16) != 0 || a.nv_amax_a == nullptr || a.nv_amax_b == nullptr || a.gather != 0)
+      return SPX_ERR_INVALID_ARG;
+    switch (epi) {
+      case kEpiStore:
+        return launch_gemm_t<kEpiStore, true, true>(a, grid_m, grid_n, stream);
+      case kEpiSwiglu:
+        return launch_gemm_t<kEpiSwiglu, true, true>(a, grid_m, grid_n, stream);
+      case kEpiScatter:
+        return launch_gemm_t<kEpiScatter, true, true>(a, grid_m, grid_n, stream);
+      default:
+        return SPX_ERR_INVALID_ARG;
+    }
+  }
   if (mx) {
     // Block-scaled lane: one scale atom per 128 B rows of N, accumulators of 128 columns at most.
     if (a.bn > kMxMaxBn || a.tmem_cols > kMxMaxBn || a.sfa == nullptr || a.sfb == nullptr || (a.ld_sfa % 4) != 0)

@@ -47,6 +47,12 @@ constexpr uint32_t kMxSfColumn = 384;
 constexpr int kMxSfSlots = 8;
 constexpr uint32_t kMxSfSlotCols = 16;
 constexpr uint32_t kMxStageSfBytes = 3 * kMxAtomBytes;  // SFA atom + up to two SFB atoms per stage
+// NVFP4 lane: a stage is 128 bytes of K = 256 E2M1 elements = four K-64 MMAs,
+// each with its own SFA atom and up to two SFB atoms; their TMEM copies rotate
+// through ten 12-column slots from column 384.
+constexpr uint32_t kNvStageSfBytes = 12 * kMxAtomBytes;
+constexpr uint32_t kNvSfSlots = 10;
+constexpr uint32_t kNvSfSlotCols = 12;
 
 struct RouteArgs {
   const uint16_t* logits;    // [T, E] bf16
@@ -74,7 +80,7 @@ struct DispatchArgs {
   int* chunk_hist;           // [ceil(P/2048), E]
   int* counts;               // [E]
   int* starts;               // [E]
-  int4* tiles;               // [ceil(P/128) + E] {expert, row0, rows, 0}: BF16-lane experts
+  int4* tiles;               // [ceil(P/128) + E] {expert, row0, rows, expert}: BF16-lane experts
   int* num_tiles;
   const uint8_t* lane_mx;    // [E] 1 = expert runs the MXFP8 lane, or null (all BF16)
   int4* tiles_mx;            // [ceil(P/128) + E] tiles of MXFP8-lane experts (when lane_mx)
@@ -136,6 +142,17 @@ struct GemmArgs {
   uint16_t* comb_res_out;    //   comb_res_out = bf16(residual + update) (out may then be null)
   int64_t ldy;
   int max_ctas;              // persistent grid cap (0 = every SM): leaves SMs to concurrent work
+  // NVFP4 lane (block-scaled kernel with E2M1 operands): the epilogue scales
+  // the accumulator by the two per-tensor scales, amax / 2688 each, of A
+  // (nv_amax_a[expert], the tile's .w; 0 without a tile table) and B
+  // (nv_amax_b[group * nv_b_stride + nv_b_off (+1 for the up half of a SwiGLU
+  // tile)]); kEpiSwiglu also raises nv_amax_out[expert] to the largest
+  // |hidden| it writes.
+  const float* nv_amax_a;
+  const float* nv_amax_b;
+  int nv_b_stride;
+  int nv_b_off;
+  float* nv_amax_out;
   int* status;
 };
 
@@ -159,10 +176,11 @@ int encode_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, in
               int elem_bytes = 2);
 int encode_3d(CUtensorMap* map, const void* base, int64_t groups, int64_t rows, int64_t cols, int box_rows,
               int elem_bytes = 2);
-size_t gemm_smem_bytes(int bn, int stages, bool mx, int epi);
-int gemm_pick_stages(int bn, int k_blocks, bool mx, int epi);
+size_t gemm_smem_bytes(int bn, int stages, bool mx, int epi, bool nv = false);
+int gemm_pick_stages(int bn, int k_blocks, bool mx, int epi, bool nv = false);
 // `mx` selects the block-scaled MXFP8 kernel (bn <= 128, k_blocks of 128 elements).
-int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream, bool mx = false);
+int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream, bool mx = false,
+                bool nv = false);
 // CTA-pair (cluster of 2, cta_group::2) GEMM: 256-row tiles of a TMA-loaded A.
 size_t gemm_pair_smem_bytes(int bn, int stages);
 int gemm_pair_pick_stages(int bn);
@@ -210,6 +228,37 @@ struct PageTilesArgs {
   int* out_count_mx;
 };
 int launch_page_tiles(const PageTilesArgs& a, cudaStream_t stream);
+
+// ---- NVFP4 (nvfp4.cu).  Quantised rows: E2M1 [rows, kp/2] bytes, UE4M3
+// scales [rows, kp/16] bytes (kp a multiple of 256; K beyond `cols` is zero).
+// Largest |v| of a row-major matrix, raised into *amax (zeroed by the caller).
+int launch_nv_amax(const uint16_t* src, int64_t rows, int cols, int64_t ld, float* amax, cudaStream_t stream);
+// Largest |v| of every row into row_amax[rows].
+int launch_nv_row_amax(const uint16_t* src, int64_t rows, int cols, int64_t ld, float* row_amax,
+                       cudaStream_t stream);
+// Per tile of a grouped table: amax[expert] (the tile's .w) raised to the
+// largest row_amax of the tile's rows (row p -> source row gather[p]).
+int launch_nv_tile_amax(const int4* tiles, const int* num_tiles, int max_tiles, const int* gather,
+                        const float* row_amax, float* amax, cudaStream_t stream);
+// Dense rows with one per-tensor amax (amax[0]).
+int launch_nv_quantize_rows(const uint16_t* src, int64_t rows, int cols, int64_t ld, const float* amax, int kp,
+                            uint8_t* q, uint8_t* sf, cudaStream_t stream);
+// Rows of a grouped table (sorted positions): source row gather[p] (or p),
+// per-tensor amax of the tile's expert (.w).
+int launch_nv_quantize_tiles(const int4* tiles, const int* num_tiles, int max_tiles, const uint16_t* src,
+                             int64_t ld, int cols, const int* gather, const float* amax, int kp, uint8_t* q,
+                             uint8_t* sf, cudaStream_t stream);
+// B operands at pack time: E2M1 [groups, rows, kp/2] and the scale atoms
+// [groups][row tiles][kp/256][4][ceil(tile rows/128)][512]; per-tensor amax
+// amax[g * 4 + proj] (W1 rows: proj 0 gate / 1 up; W2: 2; plain rows: 0).
+int launch_nv_quantize_b(int mode, const uint16_t* a, const uint16_t* b, int groups, int rows_per_group,
+                         int rows_real, int k_real, int kp, int tile_rows, int d, int inter, int chunk, int64_t ld,
+                         const float* amax, uint8_t* q, uint8_t* atoms, cudaStream_t stream);
+size_t nv_atoms_bytes(int groups, int rows_per_group, int kp, int tile_rows);
+// Per group g: amax[g * stride + off] raised to the largest |v| of the group's
+// `per_group` consecutive elements of src.
+int launch_nv_group_amax(const uint16_t* src, int groups, int64_t per_group, float* amax, int stride, int off,
+                         cudaStream_t stream);
 // Whole experts into cache slots: dst[a] + slot * bytes[a] <- src[a] + expert * bytes[a]
 // for each (expert, slot) of `pairs` (device int32 [num_pairs][2]); sources may be
 // mapped page-locked host memory (read by the GPU over the host link).

@@ -14,6 +14,7 @@
 #include <stdint.h>
 
 #include "kernels.h"
+#include "sm100.cuh"
 
 namespace spx {
 
@@ -72,5 +73,31 @@ __device__ __forceinline__ uint32_t mx_quantize32(const float (&v)[32], uint32_t
 // quadrants); the block-scaled MMA then reads row r's scale for K sub-block j
 // from column r / 32, byte j.
 __host__ __device__ __forceinline__ int mx_atom_offset(int r, int j) { return (r & 31) * 16 + (r >> 5) * 4 + j; }
+
+// Source element (row `row` of group `g`, K index `k`) of a B operand.
+struct MxBSource {
+  int mode;               // kMxSrcW1 / kMxSrcW2 / kMxSrcRows
+  const uint16_t* a;      // W1: gate [E,d,I]; W2: down [E,I,d]; rows: [rows, ld]
+  const uint16_t* b;      // W1: up [E,d,I]
+  int d, inter, chunk;    // W1 / W2 shapes
+  int64_t ld;             // rows: row stride
+  int k_real;
+  int rows_real;          // rows of one group that exist (beyond: zero)
+};
+
+__device__ __forceinline__ float mx_b_elem(const MxBSource& s, int g, int row, int k) {
+  if (k >= s.k_real || row >= s.rows_real) return 0.0f;
+  if (s.mode == kMxSrcW1) {
+    const int ch = row / (2 * s.chunk);
+    const int within = row - ch * 2 * s.chunk;
+    const int half = within / s.chunk;
+    const int i = ch * s.chunk + (within - half * s.chunk);
+    if (i >= s.inter) return 0.0f;
+    const uint16_t* p = half == 0 ? s.a : s.b;
+    return bf16_to_f32(p[(static_cast<int64_t>(g) * s.d + k) * s.inter + i]);
+  }
+  if (s.mode == kMxSrcW2) return bf16_to_f32(s.a[(static_cast<int64_t>(g) * s.inter + k) * s.d + row]);
+  return bf16_to_f32(s.a[static_cast<int64_t>(row) * s.ld + k]);
+}
 
 }  // namespace spx

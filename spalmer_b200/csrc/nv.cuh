@@ -1,0 +1,73 @@
+// NVFP4 block quantisation on the device: E2M1 elements (two per byte, the
+// even element in the low nibble) with one UE4M3 scale per block of 16
+// consecutive K elements, relative to a per-tensor FP32 scale.
+//
+// Reference: mESmaC/spalmer experts/native.py:205-262 packs both operands of
+// every NVFP4 matmul with torchao's NVFP4Tensor.to_nvfp4(v, per_tensor_scale=
+// per_tensor_amax_to_scale(amax(|v|))).  torchao is not part of this build;
+// its published algorithm, restated:
+//   per_tensor_scale = amax / (448 * 6)                        (FP32)
+//   per block of 16:  s = e4m3_rn(clamp((blk_amax / 6) / per_tensor_scale, 2^-6, 448))
+//   element:          e2m1_rn(clamp(v / (per_tensor_scale * s), -6, 6))
+// and the matmul multiplies the block-scaled product by the two per-tensor
+// scales.  A tensor whose amax is 0 quantises to zeros here (the restated
+// formula would divide by zero).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <stdint.h>
+
+namespace spx {
+
+constexpr int kNvBlock = 16;             // elements per UE4M3 scale
+constexpr float kNvTensorDiv = 2688.0f;  // 448 (E4M3 max) * 6 (E2M1 max)
+constexpr float kNvScaleMin = 0.015625f; // 2^-6, the smallest normal E4M3
+
+// E2M1 code (sign in bit 3) of v, round to nearest even on the grid
+// {0, 0.5, 1, 1.5, 2, 3, 4, 6}; |v| <= 6 expected (clamped by the caller).
+__host__ __device__ __forceinline__ uint32_t nv_e2m1(float v) {
+  const float m = fabsf(v);
+  uint32_t c;
+  if (m <= 0.25f) c = 0;
+  else if (m < 0.75f) c = 1;
+  else if (m <= 1.25f) c = 2;
+  else if (m < 1.75f) c = 3;
+  else if (m <= 2.5f) c = 4;
+  else if (m < 3.5f) c = 5;
+  else if (m <= 5.0f) c = 6;
+  else c = 7;
+  return c | (signbit(v) ? 8u : 0u);
+}
+
+// The per-tensor scale of a tensor whose largest magnitude is amax.
+__host__ __device__ __forceinline__ float nv_tensor_scale(float amax) { return amax / kNvTensorDiv; }
+
+#if defined(__CUDACC__)
+// Quantise 16 values with per-tensor scale `pts` (> 0): two words of E2M1
+// nibbles (element j in bits 4*(j%8) .. of word j/8) and the UE4M3 scale byte.
+__device__ __forceinline__ uint32_t nv_quantize16(const float (&v)[16], float pts, uint32_t& w0, uint32_t& w1) {
+  w0 = w1 = 0u;
+  if (!(pts > 0.0f)) return 0u;
+  float amax = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
+  float s = (amax / 6.0f) / pts;
+  s = fminf(fmaxf(s, kNvScaleMin), 448.0f);
+  const __nv_fp8_storage_t sb = __nv_cvt_float_to_fp8(s, __NV_SATFINITE, __NV_E4M3);
+  const float sf = __half2float(__half(__nv_cvt_fp8_to_halfraw(sb, __NV_E4M3)));
+  const float total = pts * sf;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float x = fminf(fmaxf(v[j] / total, -6.0f), 6.0f);
+    const uint32_t c = nv_e2m1(x);
+    if (j < 8)
+      w0 |= c << (4 * j);
+    else
+      w1 |= c << (4 * (j - 8));
+  }
+  return static_cast<uint32_t>(sb);
+}
+#endif
+
+}  // namespace spx

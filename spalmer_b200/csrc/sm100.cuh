@@ -293,6 +293,20 @@ __device__ __forceinline__ void mma_mxf8_ss(uint32_t d_tmem, uint64_t a_desc, ui
       : "memory");
 }
 
+// Block-scaled NVFP4 MMA: D[tmem] (+)= (A * SFA) * (B * SFB)^T with packed
+// E2M1 operands in shared memory (two per byte) and one UE4M3 scale per 16
+// elements in tensor memory: K = 64 per instruction, whose four scales per
+// row fill one 32-bit TMEM word (scale ids 0).
+__device__ __forceinline__ void mma_nvf4_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
 // Shared memory -> tensor memory: 32 rows x 16 bytes, replicated to the four
 // 32-lane quadrants (the scale-factor layout of the block-scaled MMA).
 __device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t src_desc) {
@@ -370,6 +384,15 @@ __host__ __device__ __forceinline__ uint32_t idesc_mxf8(int m, int n, uint32_t a
          | (1u << 23)                               // scale format: E8M0
          | (static_cast<uint32_t>(m >> 4) << 24)    // M >> 4
          | (a_sf << 29);                            // A scale factor id
+}
+
+// Instruction descriptor, kind::mxf4nvf4 block_scale: E2M1 A and B (K-major,
+// packed), FP32 D, UE4M3 scales, dense K = 64, M x N, scale ids 0.
+__host__ __device__ __forceinline__ uint32_t idesc_nvf4(int m, int n) {
+  return (1u << 7) | (1u << 10)                     // A, B format: E2M1
+         | (static_cast<uint32_t>(n >> 3) << 17)    // N >> 3
+         | (0u << 23)                               // scale format: UE4M3
+         | (static_cast<uint32_t>(m >> 4) << 24);   // M >> 4
 }
 
 // Instruction descriptor, kind::f16: BF16 A and B (K-major), FP32 D, M x N.

@@ -1,0 +1,61 @@
+"""NVFP4 on the GPU: the quantiser (spx_nvfp4_quantize_rows) bit for bit
+against the restatement (oracle/nvfp4.py), and the block-scaled tcgen05
+kind::mxf4nvf4 matmul (spx_nvfp4_mm_nt, the forward of the reference's
+native_nvfp4_linear, experts/native.py:224-302) against the restatement's
+matmul: the same quantised operands, FP32 accumulation in another order."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import nvfp4 as NV
+from oracle.bf16 import bf16_bits_to_f32
+from spalmer_b200 import _lib
+from tests.helpers import bf16_bits, from_bits
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def rand_bf16(shape, scale=1.0, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return (scale * torch.randn(*shape, generator=g)).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("rows,cols", [(300, 200), (64, 768), (1, 16), (129, 1000)])
+def test_quantize_rows_matches_restatement(rows, cols):
+    lib = _lib.load()
+    x = rand_bf16((rows, cols), seed=rows)
+    x[0, :3] = torch.tensor([0.0, -0.0, 1e-3])
+    kp = NV.padded_k(cols)
+    xd = x.to(DEV)
+    q = torch.empty(rows, kp // 2, dtype=torch.uint8, device=DEV)
+    sf = torch.empty(rows, kp // 16, dtype=torch.uint8, device=DEV)
+    amax = torch.empty(1, dtype=torch.float32, device=DEV)
+    st = torch.cuda.current_stream(DEV).cuda_stream
+    assert lib.spx_nvfp4_quantize_rows(xd.data_ptr(), rows, cols, q.data_ptr(), sf.data_ptr(), amax.data_ptr(), st) == 0
+    codes, sb, am = NV.quantize_rows(bf16_bits_to_f32(bf16_bits(x)))
+    assert amax.item() == am
+    np.testing.assert_array_equal(sf.cpu().numpy(), sb)
+    np.testing.assert_array_equal(q.cpu().numpy(), NV.pack_codes(codes))
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 256, 512), (200, 96, 300), (1, 16, 64), (1000, 384, 768), (130, 40, 1024)])
+def test_mm_nt_matches_restatement(m, n, k):
+    lib = _lib.load()
+    a = rand_bf16((m, k), seed=1)
+    b = rand_bf16((n, k), scale=0.02, seed=2)
+    ws = torch.empty(lib.spx_nvfp4_mm_workspace(m, n, k), dtype=torch.uint8, device=DEV)
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=DEV)
+    st = torch.cuda.current_stream(DEV).cuda_stream
+    ad, bd = a.to(DEV), b.to(DEV)
+    assert lib.spx_nvfp4_mm_nt(ad.data_ptr(), bd.data_ptr(), m, n, k, out.data_ptr(), ws.data_ptr(), ws.numel(), st) == 0
+    got = out.float().cpu().numpy()
+    want = bf16_bits_to_f32(NV.nvfp4_matmul_bits(bf16_bits(a), bf16_bits(b)))
+    # identical products, FP32 sums in another order: BF16 results within an ulp or two
+    np.testing.assert_allclose(got, want, rtol=2e-2, atol=1e-3 * np.abs(want).max())
+    assert (got == want).mean() > 0.9
+    exact = a.float().numpy() @ b.float().numpy().T
+    assert np.linalg.norm(got - exact) / np.linalg.norm(exact) < 0.30  # the reference's bound
