@@ -74,8 +74,10 @@ typedef struct spx_layer_dims {
   int32_t top_k;           /* k, active experts per token (1..20, <= E)          */
   int32_t score_transform; /* 0 = softplus, 1 = identity (router_score_transform) */
   int32_t execution_loop;  /* 1 = telemetry of expert_execution="loop"          */
-  int32_t mxfp8_lane;      /* 1 = some experts may run the MXFP8 lane: the workspace
-                              then holds quantised activations (I % 32 == 0)  */
+  int32_t mxfp8_lane;      /* low-precision lane of the layer (I % 32 == 0): 0 none,
+                              1 = some experts may run ("mxfp8", "mxfp8"),
+                              2 = some experts may run ("nvfp4", "nvfp4"); the
+                              workspace then holds quantised activations     */
 } spx_layer_dims;
 
 /* The reference state_dict tensors (BF16), unchanged layouts. */
@@ -105,6 +107,7 @@ typedef struct spx_packed_sizes {
   size_t expert_w1_mx_scales; /* E8M0 scale atoms of expert_w1_mx                */
   size_t expert_w2_mx;        /* E4M3 [E, d, round_up(I, 128)]                   */
   size_t expert_w2_mx_scales; /* E8M0 scale atoms of expert_w2_mx                */
+  size_t expert_nvfp4_amax;   /* bytes of the per-expert weight amax (NVFP4 lane) */
 } spx_packed_sizes;
 
 typedef struct spx_packed_weights {
@@ -124,6 +127,10 @@ typedef struct spx_packed_weights {
   const uint8_t* expert_w1_mx_scales;
   const uint8_t* expert_w2_mx;
   const uint8_t* expert_w2_mx_scales;
+  /* NVFP4 lane (dims->mxfp8_lane == 2): the *_mx fields hold the copies made by
+   * spx_pack_weights_nvfp4 (E2M1 values and UE4M3 scale atoms) and this the
+   * per-expert amax of gate, up, down ([E][4] float, the 4th unused). */
+  const float* expert_nvfp4_amax;
 } spx_packed_weights;
 
 typedef struct spx_layer_outputs {
@@ -276,6 +283,15 @@ int spx_block_channel_forward(const spx_layer_dims* dims, const spx_packed_weigh
  *   workspace from spx_nvfp4_mm_workspace. */
 int spx_nvfp4_quantize_rows(const uint16_t* src, int64_t rows, int32_t cols, uint8_t* values, uint8_t* scales,
                             float* amax, void* stream);
+/* NVFP4 copies of the expert masters for a layer whose dims->mxfp8_lane == 2
+ * (sizes: the *_mx fields of spx_layer_sizes): E2M1 gate|up chunks and down
+ * rows with their scale atoms, each matrix under its own per-tensor scale,
+ * and expert_amax [E][4] (gate, up, down, unused).  The activations get one
+ * per-tensor scale per expert and forward (each expert's input is one call of
+ * the reference's NVFP4 matmul). */
+int spx_pack_weights_nvfp4(const spx_layer_dims* dims, const spx_reference_weights* src, uint8_t* expert_w1_nv,
+                           uint8_t* expert_w1_nv_scales, uint8_t* expert_w2_nv, uint8_t* expert_w2_nv_scales,
+                           float* expert_amax, void* stream);
 size_t spx_nvfp4_mm_workspace(int64_t m, int64_t n, int64_t k);
 int spx_nvfp4_mm_nt(const uint16_t* left, const uint16_t* right_rows, int64_t m, int64_t n, int64_t k,
                     uint16_t* out, void* workspace, size_t workspace_bytes, void* stream);

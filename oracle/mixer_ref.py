@@ -171,6 +171,19 @@ def _swiglu_rows_mxfp8(x_bits, gate_io_bits, up_io_bits, down_io_bits):
     return mxfp8_matmul_bits(h, np.ascontiguousarray(down_io_bits.T))
 
 
+def _swiglu_rows_nvfp4(x_bits, gate_io_bits, up_io_bits, down_io_bits):
+    """``expert_forward`` for the ("nvfp4", "nvfp4") pair: each projection is one
+    ``native_expert_matmul`` call (experts/native.py:324-326 -> 224-262) over all
+    of the expert's rows, so each operand gets one per-tensor scale per call."""
+
+    from oracle.nvfp4 import nvfp4_matmul_bits
+
+    g = nvfp4_matmul_bits(x_bits, np.ascontiguousarray(gate_io_bits.T))
+    u = nvfp4_matmul_bits(x_bits, np.ascontiguousarray(up_io_bits.T))
+    h = f32_to_bf16_bits(bf16_bits_to_f32(_silu_bf16(g)) * bf16_bits_to_f32(u))
+    return nvfp4_matmul_bits(h, np.ascontiguousarray(down_io_bits.T))
+
+
 def _next_pow2(n: np.ndarray) -> np.ndarray:
     out = np.ones_like(n)
     pos = n > 1
@@ -180,7 +193,8 @@ def _next_pow2(n: np.ndarray) -> np.ndarray:
 
 def grouped_experts(x_bits: np.ndarray, expert_ids: np.ndarray, weight_bits: np.ndarray,
                     gate_bits: np.ndarray, up_bits: np.ndarray, down_bits: np.ndarray,
-                    lane_mx: np.ndarray | None = None, execution: str = "grouped"):
+                    lane_mx: np.ndarray | None = None, execution: str = "grouped",
+                    lane_nv: np.ndarray | None = None):
     """``MicroExpertBank._execute_grouped`` (``experts/bank.py:705-779``).
 
     ``x_bits [T,d]``, ``expert_ids [T,k]``, ``weight_bits [T,k]``; expert stacks
@@ -189,7 +203,7 @@ def grouped_experts(x_bits: np.ndarray, expert_ids: np.ndarray, weight_bits: np.
     (buckets by padded capacity, then expert id, then sorted pair order; or
     ascending expert id for ``execution="loop"``, bank.py:674-701) with a BF16
     rounding after every addition.  ``lane_mx[e]`` selects the MXFP8 pair for
-    expert e (``_execution_pair``, bank.py:462-475).
+    expert e (``_execution_pair``, bank.py:462-475); ``lane_nv[e]`` the NVFP4 pair.
     """
 
     T, d = x_bits.shape
@@ -205,7 +219,9 @@ def grouped_experts(x_bits: np.ndarray, expert_ids: np.ndarray, weight_bits: np.
     for e in np.nonzero(counts)[0]:
         rows = order[starts[e]: starts[e] + counts[e]]
         tokens = rows // k
-        if lane_mx is not None and lane_mx[e]:
+        if lane_nv is not None and lane_nv[e]:
+            y = _swiglu_rows_nvfp4(x_bits[tokens], gate_bits[e], up_bits[e], down_bits[e])
+        elif lane_mx is not None and lane_mx[e]:
             y = _swiglu_rows_mxfp8(x_bits[tokens], gate_bits[e], up_bits[e], down_bits[e])
         else:
             y = _swiglu_rows(
@@ -285,7 +301,7 @@ class LayerParams:
 def mixer_forward(params: LayerParams, x_bits: np.ndarray, k: int, *,
                   resident_mask: np.ndarray | None = None, transform: str = "softplus",
                   logit_bits: np.ndarray | None = None, lane_mx: np.ndarray | None = None,
-                  execution: str = "grouped") -> dict:
+                  execution: str = "grouped", lane_nv: np.ndarray | None = None) -> dict:
     """``MicroExpertChannelMixer.forward`` of ``experts/mixer.py:145-241``.
 
     ``x_bits [T,d]``.  ``logit_bits`` injects router logits (the bit-exact
@@ -300,7 +316,7 @@ def mixer_forward(params: LayerParams, x_bits: np.ndarray, k: int, *,
     scores = router_scores(logit_bits, transform)
     ids, weights = select_least_surprised(scores, k, resident_mask)
     routed, order, counts = grouped_experts(x_bits, ids, weights, params.gate, params.up, params.down,
-                                            lane_mx=lane_mx, execution=execution)
+                                            lane_mx=lane_mx, execution=execution, lane_nv=lane_nv)
     if params.shared_gate is not None:
         shared = shared_swiglu(x_bits, params.shared_gate, params.shared_up, params.shared_down)
         update = f32_to_bf16_bits(bf16_bits_to_f32(routed) + bf16_bits_to_f32(shared))

@@ -58,6 +58,7 @@ EXPORTED = (
     "spx_nvfp4_quantize_rows",
     "spx_nvfp4_mm_workspace",
     "spx_nvfp4_mm_nt",
+    "spx_pack_weights_nvfp4",
 )
 
 ABI_VERSION = 6
@@ -103,6 +104,7 @@ class PackedSizes(ctypes.Structure):
         ("expert_w1_mx_scales", ctypes.c_size_t),
         ("expert_w2_mx", ctypes.c_size_t),
         ("expert_w2_mx_scales", ctypes.c_size_t),
+        ("expert_nvfp4_amax", ctypes.c_size_t),
     ]
 
 
@@ -121,6 +123,7 @@ class PackedWeights(ctypes.Structure):
         ("expert_w1_mx_scales", _vp),
         ("expert_w2_mx", _vp),
         ("expert_w2_mx_scales", _vp),
+        ("expert_nvfp4_amax", _vp),
     ]
 
 
@@ -243,6 +246,7 @@ def load() -> ctypes.CDLL:
              _vp],
         ),
         "spx_nvfp4_quantize_rows": (ctypes.c_int, [_vp, ctypes.c_int64, ctypes.c_int32, _vp, _vp, _vp, _vp]),
+        "spx_pack_weights_nvfp4": (ctypes.c_int, [P(LayerDims), P(ReferenceWeights), _vp, _vp, _vp, _vp, _vp, _vp]),
         "spx_nvfp4_mm_workspace": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]),
         "spx_nvfp4_mm_nt": (
             ctypes.c_int,

@@ -42,6 +42,10 @@ struct Shape {
   int cm, ncm;        // GEMM1 chunk (N tile = 2*cm, up to 256) and chunks
   int kh;             // hidden width in bytes (I padded to 128) = GEMM2 K
   int bn2m, gn2m;     // GEMM2 N tile and tiles
+  // NVFP4 lane (dims->mxfp8_lane == 2): the low-precision lane runs the
+  // ("nvfp4", "nvfp4") pair; chunking (cm, ncm, bn2m) as the MXFP8 lane.
+  bool nv;
+  int kxn, khn;       // GEMM1 / GEMM2 K in elements, padded to 256 (128-byte stages of E2M1)
 };
 
 int make_shape(const spx_layer_dims* dm, Shape* s) {
@@ -83,7 +87,11 @@ int make_shape(const spx_layer_dims* dm, Shape* s) {
   s->lb_blocks = route_lb_blocks(s->T);
   s->nchunks = ceil_div(s->P, kDispatchChunk);
   s->max_tiles = ceil_div(s->P, kTileRows) + s->E;
+  if (dm->mxfp8_lane < 0 || dm->mxfp8_lane > 2) return SPX_ERR_INVALID_ARG;
   s->mx = dm->mxfp8_lane != 0;
+  s->nv = dm->mxfp8_lane == 2;
+  s->kxn = round_up_i(s->d, 256);
+  s->khn = round_up_i(s->I, 256);
   if (s->mx) {
     if (s->I % kMxBlock != 0) return SPX_ERR_UNSUPPORTED;
     s->kx = round_up_i(s->d, 128);
@@ -107,6 +115,13 @@ MxPackSizes mx_pack_sizes(const Shape& s) {
   MxPackSizes z{};
   if (!s.mx) return z;
   const int rows1 = s.ncm * 2 * s.cm;
+  if (s.nv) {
+    z.w1 = static_cast<size_t>(s.E) * rows1 * (s.kxn / 2);
+    z.w1_sf = nv_atoms_bytes(s.E, rows1, s.kxn, 2 * s.cm);
+    z.w2 = static_cast<size_t>(s.E) * s.d * (s.khn / 2);
+    z.w2_sf = nv_atoms_bytes(s.E, s.d, s.khn, s.bn2m);
+    return z;
+  }
   z.w1 = static_cast<size_t>(s.E) * rows1 * s.kx;
   z.w1_sf = mx_atoms_bytes(s.E, rows1, s.kx, 2 * s.cm);
   z.w2 = static_cast<size_t>(s.E) * s.d * s.kh;
@@ -119,6 +134,7 @@ struct Layout {
   size_t hidden, y, shared_hidden, shared_out, x_pad, x_norm, util, stats, ratios, aux;
   size_t x_q, x_sf, h_q, h_sf, tiles_mx;  // MXFP8 lane (empty otherwise)
   size_t tiles_page, tiles_mx_page;        // one page of a paged expert pass
+  size_t nv_row_amax, nv_amax;             // NVFP4 lane: per-token amax [T]; per-expert amax of x, h [2][E]
   size_t total;
 };
 
@@ -152,13 +168,22 @@ Layout make_layout(const Shape& s) {
   L.stats = take(sizeof(long long) * 6);
   L.ratios = take(sizeof(float) * 2);
   L.aux = take(sizeof(uint16_t) * 2);
-  L.x_q = take(s.mx ? static_cast<size_t>(s.T) * s.kx : 0);
-  L.x_sf = take(s.mx ? static_cast<size_t>(s.T) * (s.kx / kMxBlock) : 0);
-  L.h_q = take(s.mx ? static_cast<size_t>(s.P) * s.kh : 0);
-  L.h_sf = take(s.mx ? static_cast<size_t>(s.P) * (s.kh / kMxBlock) : 0);
+  if (s.nv) {  // E2M1 rows per routed pair (each expert's input has its own per-tensor scale)
+    L.x_q = take(static_cast<size_t>(s.P) * (s.kxn / 2));
+    L.x_sf = take(static_cast<size_t>(s.P) * (s.kxn / kNvBlock));
+    L.h_q = take(static_cast<size_t>(s.P) * (s.khn / 2));
+    L.h_sf = take(static_cast<size_t>(s.P) * (s.khn / kNvBlock));
+  } else {
+    L.x_q = take(s.mx ? static_cast<size_t>(s.T) * s.kx : 0);
+    L.x_sf = take(s.mx ? static_cast<size_t>(s.T) * (s.kx / kMxBlock) : 0);
+    L.h_q = take(s.mx ? static_cast<size_t>(s.P) * s.kh : 0);
+    L.h_sf = take(s.mx ? static_cast<size_t>(s.P) * (s.kh / kMxBlock) : 0);
+  }
   L.tiles_mx = take(s.mx ? sizeof(int4) * static_cast<size_t>(s.max_tiles) : 0);
   L.tiles_page = take(sizeof(int4) * static_cast<size_t>(s.max_tiles));
   L.tiles_mx_page = take(s.mx ? sizeof(int4) * static_cast<size_t>(s.max_tiles) : 0);
+  L.nv_row_amax = take(s.nv ? sizeof(float) * static_cast<size_t>(s.T) : 0);
+  L.nv_amax = take(s.nv ? sizeof(float) * 2 * static_cast<size_t>(s.E) : 0);
   L.total = off;
   return L;
 }
@@ -327,10 +352,30 @@ struct ExpertPass {
   int groups;
   const int4* tiles;
   const int* num_tiles;
-  const int4* tiles_mx;  // null: no MXFP8 lane in this pass
+  const int4* tiles_mx;  // null: no low-precision lane in this pass
   const int* num_tiles_mx;
   int max_ctas;  // persistent grid cap of the GEMMs (0 = every SM)
+  const float* nv_amax_w;  // NVFP4 lane: weight amax [groups][4] (gate, up, down, unused)
 };
+
+// NVFP4 lane input: each expert's rows in dispatch order as E2M1 with UE4M3
+// block scales under the expert's own per-tensor scale (amax over its rows,
+// experts/native.py:240-256 per expert call); zeroes the per-expert hidden
+// amax that the NVFP4 GEMM1 epilogue raises.
+int stage_quantize_nv_x(const Ctx& c, const uint16_t* hidden, int64_t ld_hidden, const DispatchArgs& da) {
+  const Shape& s = c.s;
+  const int64_t ld = ld_hidden > 0 ? ld_hidden : s.d;
+  float* amax = at<float>(c.ws, c.L.nv_amax);  // [x | h][E]
+  float* row_amax = at<float>(c.ws, c.L.nv_row_amax);
+  if (cudaMemsetAsync(amax, 0, sizeof(float) * 2 * s.E, c.st) != cudaSuccess) return SPX_ERR_CUDA;
+  int rc = launch_nv_row_amax(hidden, s.T, s.d, ld, row_amax, c.st);
+  if (rc == SPX_OK)
+    rc = launch_nv_tile_amax(da.tiles_mx, da.num_tiles_mx, s.max_tiles, da.src_row, row_amax, amax, c.st);
+  if (rc == SPX_OK)
+    rc = launch_nv_quantize_tiles(da.tiles_mx, da.num_tiles_mx, s.max_tiles, hidden, ld, s.d, da.src_row, amax,
+                                  s.kxn, at<uint8_t>(c.ws, c.L.x_q), at<uint8_t>(c.ws, c.L.x_sf), c.st);
+  return rc;
+}
 
 // MXFP8 lane input: E4M3 rows of the hidden states with their block scales
 // (per token, so every expert's gathered rows share them).
@@ -348,7 +393,10 @@ int stage_expert_gemms(const Ctx& c, const uint16_t* xa, const int* src_row, con
   void* ws = c.ws;
   const Layout& L = c.L;
   int rc = SPX_OK;
-  const bool mx = p.tiles_mx != nullptr;
+  const bool mx = p.tiles_mx != nullptr && !s.nv;
+  const bool nv = p.tiles_mx != nullptr && s.nv;
+  float* nv_amax_x = at<float>(ws, L.nv_amax);
+  float* nv_amax_h = nv_amax_x + s.E;
   uint8_t* xq = at<uint8_t>(ws, L.x_q);
   uint8_t* xsf = at<uint8_t>(ws, L.x_sf);
   uint8_t* hq = at<uint8_t>(ws, L.h_q);
@@ -398,6 +446,36 @@ int stage_expert_gemms(const Ctx& c, const uint16_t* xa, const int* src_row, con
     g.ld_out_sf = s.kh / kMxBlock;
     if ((rc = launch_gemm(kEpiSwiglu, g, s.max_tiles, s.ncm, c.st, true)) != SPX_OK) return rc;
   }
+  if (nv) {
+    // NVFP4-lane experts: block-scaled E2M1 GEMM1, BF16 hidden rows (their
+    // per-expert amax raised by the epilogue), then the hidden rows quantised
+    // under each expert's scale.
+    GemmArgs g = base_args(kEpiSwiglu, 2 * s.cm, s.kxn / 256, c.status, true, true);
+    if ((rc = encode_3d(&g.tma_b, p.w1_mx, p.groups, static_cast<int64_t>(s.ncm) * 2 * s.cm, s.kxn / 2, 2 * s.cm,
+                        1)) != SPX_OK)
+      return rc;
+    if ((rc = encode_2d(&g.tma_a, xq, s.P, s.kxn / 2, s.kxn / 2, kTileRows, 1)) != SPX_OK) return rc;
+    g.groups = p.groups;
+    g.max_ctas = p.max_ctas;
+    g.sfa = xsf;
+    g.ld_sfa = s.kxn / kNvBlock;
+    g.sfb = p.w1_mx_sf;
+    g.tiles = p.tiles_mx;
+    g.num_tiles = p.num_tiles_mx;
+    g.chunk = s.cm;
+    g.h_cols = s.kp;
+    g.out = hid;
+    g.ldo = s.kp;
+    g.nv_amax_a = nv_amax_x;
+    g.nv_amax_b = p.nv_amax_w;
+    g.nv_b_stride = 4;
+    g.nv_b_off = 0;
+    g.nv_amax_out = nv_amax_h;
+    if ((rc = launch_gemm(kEpiSwiglu, g, s.max_tiles, s.ncm, c.st, true, true)) != SPX_OK) return rc;
+    if ((rc = launch_nv_quantize_tiles(p.tiles_mx, p.num_tiles_mx, s.max_tiles, hid, s.kp, s.I, nullptr, nv_amax_h,
+                                       s.khn, hq, hsf, c.st)) != SPX_OK)
+      return rc;
+  }
   c.mark(4);
   {
     GemmArgs g = base_args(kEpiScatter, s.bn_d, s.kp / 64, c.status);
@@ -434,6 +512,29 @@ int stage_expert_gemms(const Ctx& c, const uint16_t* xa, const int* src_row, con
     g.pos_weight = sorted_w;
     if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn2m, c.st, true)) != SPX_OK) return rc;
   }
+  if (nv) {
+    GemmArgs g = base_args(kEpiScatter, s.bn2m, s.khn / 256, c.status, true, true);
+    if ((rc = encode_2d(&g.tma_a, hq, s.P, s.khn / 2, s.khn / 2, kTileRows, 1)) != SPX_OK) return rc;
+    if ((rc = encode_3d(&g.tma_b, p.w2_mx, p.groups, s.d, s.khn / 2, s.bn2m, 1)) != SPX_OK) return rc;
+    g.groups = p.groups;
+    g.max_ctas = p.max_ctas;
+    g.tiles = p.tiles_mx;
+    g.num_tiles = p.num_tiles_mx;
+    g.sfa = hsf;
+    g.ld_sfa = s.khn / kNvBlock;
+    g.sfb = p.w2_mx_sf;
+    g.n_valid = s.d;
+    g.out = y;
+    g.ldo = s.d;
+    g.tma_store = (s.d % 64) == 0;
+    if (g.tma_store && (rc = encode_2d(&g.tma_out, y, s.P, s.d, s.d, 32)) != SPX_OK) return rc;
+    g.pos_weight = sorted_w;
+    g.nv_amax_a = nv_amax_h;
+    g.nv_amax_b = p.nv_amax_w;
+    g.nv_b_stride = 4;
+    g.nv_b_off = 2;
+    if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn2m, c.st, true, true)) != SPX_OK) return rc;
+  }
   c.mark(5);
   return SPX_OK;
 }
@@ -444,11 +545,12 @@ int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hid
                   const DispatchArgs& da, int64_t ld_hidden = 0) {
   const bool mx = da.lane_mx != nullptr;
   if (mx) {
-    if (int rc = stage_quantize_x(c, hidden, ld_hidden); rc != SPX_OK) return rc;
+    const int rc = c.s.nv ? stage_quantize_nv_x(c, hidden, ld_hidden, da) : stage_quantize_x(c, hidden, ld_hidden);
+    if (rc != SPX_OK) return rc;
   }
   const ExpertPass p{w->expert_w1, w->expert_w2, w->expert_w1_mx, w->expert_w1_mx_scales, w->expert_w2_mx,
                      w->expert_w2_mx_scales, c.s.E, da.tiles, da.num_tiles, mx ? da.tiles_mx : nullptr,
-                     mx ? da.num_tiles_mx : nullptr, 0};
+                     mx ? da.num_tiles_mx : nullptr, 0, w->expert_nvfp4_amax};
   return stage_expert_gemms(c, xa, da.src_row, da.sorted_weights, p);
 }
 
@@ -530,10 +632,11 @@ int check_layer_weights(const Shape& s, const spx_layer_dims* dims, const spx_pa
   if (experts && (w->expert_w1 == nullptr || w->expert_w2 == nullptr)) return SPX_ERR_INVALID_ARG;
   if (shared && s.S > 0 && (w->shared_w1 == nullptr || w->shared_w2 == nullptr)) return SPX_ERR_INVALID_ARG;
   if (experts && w->expert_lane_mxfp8 != nullptr) {
-    if (!s.mx) return SPX_ERR_INVALID_ARG;  // the workspace has no MXFP8 regions
+    if (!s.mx) return SPX_ERR_INVALID_ARG;  // the workspace has no low-precision regions
     if (w->expert_w1_mx == nullptr || w->expert_w1_mx_scales == nullptr || w->expert_w2_mx == nullptr ||
         w->expert_w2_mx_scales == nullptr)
       return SPX_ERR_INVALID_ARG;
+    if (s.nv && w->expert_nvfp4_amax == nullptr) return SPX_ERR_INVALID_ARG;
   }
   return SPX_OK;
 }
@@ -585,6 +688,7 @@ int spx_layer_sizes(const spx_layer_dims* dims, size_t* workspace_bytes, spx_pac
     packed->expert_w1_mx_scales = z.w1_sf;
     packed->expert_w2_mx = z.w2;
     packed->expert_w2_mx_scales = z.w2_sf;
+    packed->expert_nvfp4_amax = s.nv ? static_cast<size_t>(s.E) * 4 * sizeof(float) : 0;
     packed->router_weight = static_cast<size_t>(s.E) * s.kd;
     packed->expert_w1 = static_cast<size_t>(s.E) * s.nc * 2 * s.c * s.kd;
     packed->expert_w2 = static_cast<size_t>(s.E) * s.d * s.kp;
@@ -629,7 +733,7 @@ int spx_pack_weights_mxfp8(const spx_layer_dims* dims, const spx_reference_weigh
                            void* stream) {
   Shape s;
   if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
-  if (!s.mx) return SPX_ERR_INVALID_ARG;
+  if (!s.mx || s.nv) return SPX_ERR_INVALID_ARG;
   if (src == nullptr || src->gate_proj == nullptr || src->up_proj == nullptr || src->down_proj == nullptr ||
       expert_w1_mx == nullptr || expert_w1_mx_scales == nullptr || expert_w2_mx == nullptr ||
       expert_w2_mx_scales == nullptr)
@@ -644,6 +748,36 @@ int spx_pack_weights_mxfp8(const spx_layer_dims* dims, const spx_reference_weigh
   if (rc == SPX_OK)
     rc = launch_mx_quantize_b(kMxSrcW2, src->down_proj, nullptr, s.E, s.d, s.d, s.I, s.kh, s.bn2m, s.d, s.I, 0, 0,
                               expert_w2_mx, expert_w2_mx_scales, st);
+  return rc;
+}
+
+int spx_pack_weights_nvfp4(const spx_layer_dims* dims, const spx_reference_weights* src, uint8_t* expert_w1_nv,
+                           uint8_t* expert_w1_nv_scales, uint8_t* expert_w2_nv, uint8_t* expert_w2_nv_scales,
+                           float* expert_amax, void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (!s.nv) return SPX_ERR_INVALID_ARG;
+  if (src == nullptr || src->gate_proj == nullptr || src->up_proj == nullptr || src->down_proj == nullptr ||
+      expert_w1_nv == nullptr || expert_w1_nv_scales == nullptr || expert_w2_nv == nullptr ||
+      expert_w2_nv_scales == nullptr || expert_amax == nullptr)
+    return SPX_ERR_INVALID_ARG;
+  if (!aligned16(expert_w1_nv) || !aligned16(expert_w2_nv) || !aligned16(expert_w1_nv_scales) ||
+      !aligned16(expert_w2_nv_scales) || !aligned16(expert_amax))
+    return SPX_ERR_ALIGNMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Per-tensor amax of each expert's gate, up and down matrices ([E][4]).
+  if (cudaMemsetAsync(expert_amax, 0, sizeof(float) * 4 * s.E, st) != cudaSuccess) return SPX_ERR_CUDA;
+  const int64_t per = static_cast<int64_t>(s.d) * s.I;
+  int rc = launch_nv_group_amax(src->gate_proj, s.E, per, expert_amax, 4, 0, st);
+  if (rc == SPX_OK) rc = launch_nv_group_amax(src->up_proj, s.E, per, expert_amax, 4, 1, st);
+  if (rc == SPX_OK) rc = launch_nv_group_amax(src->down_proj, s.E, per, expert_amax, 4, 2, st);
+  const int rows1 = s.ncm * 2 * s.cm;
+  if (rc == SPX_OK)
+    rc = launch_nv_quantize_b(kMxSrcW1, src->gate_proj, src->up_proj, s.E, rows1, rows1, s.d, s.kxn, 2 * s.cm, s.d,
+                              s.I, s.cm, 0, expert_amax, expert_w1_nv, expert_w1_nv_scales, st);
+  if (rc == SPX_OK)
+    rc = launch_nv_quantize_b(kMxSrcW2, src->down_proj, nullptr, s.E, s.d, s.d, s.I, s.khn, s.bn2m, s.d, s.I, 0, 0,
+                              expert_amax, expert_w2_nv, expert_w2_nv_scales, st);
   return rc;
 }
 
@@ -986,7 +1120,9 @@ int spx_layer_paged_begin(const spx_layer_dims* dims, const spx_packed_weights* 
   const DispatchArgs da = layer_dispatch_args(c, dims, w, out);
   if ((rc = launch_dispatch(da, c.st)) != SPX_OK) return rc;
   c.mark(3);
-  if (da.lane_mx != nullptr && (rc = stage_quantize_x(c, hidden, 0)) != SPX_OK) return rc;
+  if (da.lane_mx != nullptr &&
+      (rc = s.nv ? stage_quantize_nv_x(c, hidden, 0, da) : stage_quantize_x(c, hidden, 0)) != SPX_OK)
+    return rc;
   if (s.S > 0 && (rc = stage_shared_gemm1(c, w, xa)) != SPX_OK) return rc;
   return SPX_OK;
 }
@@ -1020,7 +1156,7 @@ int spx_layer_paged_experts(const spx_layer_dims* dims, const spx_packed_weights
   const uint16_t* xa = s.kd != s.d ? at<uint16_t>(workspace, L.x_pad) : hidden;
   const ExpertPass p{cache->expert_w1, cache->expert_w2, cache->expert_w1_mx, cache->expert_w1_mx_scales,
                      cache->expert_w2_mx, cache->expert_w2_mx_scales, cache_slots, pt.out, pt.out_count,
-                     pt.out_mx, pt.out_count_mx, sm_limit};
+                     pt.out_mx, pt.out_count_mx, sm_limit, cache->expert_nvfp4_amax};
   return stage_expert_gemms(c, xa, at<int>(workspace, L.src_row), at<uint16_t>(workspace, L.sorted_w), p);
 }
 

@@ -163,11 +163,10 @@ class CudaOps:
         _lib.check(lib.spx_pack_weights(local, esrc, scratch_router.data_ptr(), pk["w1"].data_ptr(),
                                         pk["w2"].data_ptr(), None, None, stream), "spx_pack_weights (experts)")
         if local.mxfp8_lane:
-            names = ("expert_w1_mx", "expert_w1_mx_scales", "expert_w2_mx", "expert_w2_mx_scales")
-            for name in names:
-                pk["mx"][name] = torch.empty(max(16, getattr(lsizes, name)), dtype=torch.uint8, device=dev)
-            _lib.check(lib.spx_pack_weights_mxfp8(local, esrc, *(pk["mx"][n].data_ptr() for n in names), stream),
-                       "spx_pack_weights_mxfp8")
+            from spalmer_b200.experts import pack_lowp_experts
+
+            pk["mx"] = pack_lowp_experts(local, esrc, lsizes, lambda n: torch.empty(n, dtype=torch.uint8, device=dev),
+                                         stream)
         pk["keep"] = (gate, up, down, dummy_router, scratch_router)
         self._expert_packs[cls] = pk
         return pk
@@ -186,6 +185,7 @@ class CudaOps:
             expert_w1_mx_scales=_lib.ptr(mx.get("expert_w1_mx_scales")),
             expert_w2_mx=_lib.ptr(mx.get("expert_w2_mx")),
             expert_w2_mx_scales=_lib.ptr(mx.get("expert_w2_mx_scales")),
+            expert_nvfp4_amax=_lib.ptr(mx.get("expert_nvfp4_amax")),
         )
 
     def _workspace(self, dims: _lib.LayerDims, tag: str) -> Tensor:

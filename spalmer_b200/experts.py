@@ -365,12 +365,14 @@ def layer_dims(config: MicroExpertsConfig, tokens: int, top_k: int) -> _lib.Laye
         top_k=top_k,
         score_transform=0 if config.router_score_transform == "softplus" else 1,
         execution_loop=1 if config.expert_execution == "loop" else 0,
-        mxfp8_lane=1 if uses_mxfp8_lane(config) else 0,
+        mxfp8_lane=lowp_lane(config),
     )
 
 
-# Precision pairs with a B200 kernel lane: 0 = BF16 grouped GEMM, 1 = MXFP8 block-scaled grouped GEMM.
-_LANES = {("bfloat16", "bfloat16"): 0, ("mxfp8", "mxfp8"): 1}
+# Precision pairs with a B200 kernel lane: 0 = BF16 grouped GEMM, 1 = MXFP8
+# block-scaled grouped GEMM, 2 = NVFP4 block-scaled grouped GEMM.
+_LANES = {("bfloat16", "bfloat16"): 0, ("mxfp8", "mxfp8"): 1, ("nvfp4", "nvfp4"): 2}
+LOWP_ARRAYS = ("expert_w1_mx", "expert_w1_mx_scales", "expert_w2_mx", "expert_w2_mx_scales")
 
 
 def execution_pair(config: MicroExpertsConfig, promoted: bool) -> tuple[str, str]:
@@ -394,10 +396,40 @@ def _lane_of(config: MicroExpertsConfig, promoted: bool) -> int:
     return lane
 
 
-def uses_mxfp8_lane(config: MicroExpertsConfig) -> bool:
-    """True when some expert can execute the ("mxfp8", "mxfp8") pair."""
+def lowp_lane(config: MicroExpertsConfig) -> int:
+    """The layer's low-precision kernel lane: 0 none, 1 MXFP8, 2 NVFP4.  A layer
+    runs at most one of them beside BF16 (NVFP4 experts promoted to MXFP8 have
+    no kernel here)."""
 
-    return 1 in (_lane_of(config, False), _lane_of(config, True))
+    lanes = {_lane_of(config, False), _lane_of(config, True)} - {0}
+    if len(lanes) > 1:
+        raise NativeExpertPrecisionError(
+            "no B200 kernel for NVFP4 experts with an MXFP8 promotion lane; promote to bfloat16"
+        )
+    return lanes.pop() if lanes else 0
+
+
+def uses_mxfp8_lane(config: MicroExpertsConfig) -> bool:
+    """True when some expert can execute a low-precision (MXFP8 or NVFP4) pair."""
+
+    return lowp_lane(config) != 0
+
+
+def pack_lowp_experts(dims: _lib.LayerDims, src: _lib.ReferenceWeights, sizes: _lib.PackedSizes,
+                      alloc, stream: int) -> dict[str, Tensor]:
+    """The low-precision copies of the expert masters for ``dims`` (MXFP8 or
+    NVFP4 by ``dims.mxfp8_lane``); ``alloc(nbytes)`` returns a uint8 device tensor."""
+
+    lib = _lib.load()
+    out = {name: alloc(max(16, getattr(sizes, name))) for name in LOWP_ARRAYS}
+    ptrs = [_lib.ptr(out[name]) for name in LOWP_ARRAYS]
+    if dims.mxfp8_lane == 2:
+        out["expert_nvfp4_amax"] = alloc(max(16, sizes.expert_nvfp4_amax))
+        _lib.check(lib.spx_pack_weights_nvfp4(dims, src, *ptrs, _lib.ptr(out["expert_nvfp4_amax"]), stream),
+                   "spx_pack_weights_nvfp4")
+    else:
+        _lib.check(lib.spx_pack_weights_mxfp8(dims, src, *ptrs, stream), "spx_pack_weights_mxfp8")
+    return out
 
 
 def _bits(t: Tensor) -> Tensor:
@@ -561,22 +593,15 @@ class B200MicroExpertChannelMixer(nn.Module):
             "spx_pack_weights",
         )
         if dims.mxfp8_lane and not offloaded:
-            mx_bytes = lambda n: torch.empty(max(16, n), dtype=torch.uint8, device=device)  # noqa: E731
-            for name in ("expert_w1_mx", "expert_w1_mx_scales", "expert_w2_mx", "expert_w2_mx_scales"):
-                packed[name] = mx_bytes(getattr(sizes, name))
-            _lib.check(
-                lib.spx_pack_weights_mxfp8(
-                    dims, src, _lib.ptr(packed["expert_w1_mx"]), _lib.ptr(packed["expert_w1_mx_scales"]),
-                    _lib.ptr(packed["expert_w2_mx"]), _lib.ptr(packed["expert_w2_mx_scales"]), stream,
-                ),
-                "spx_pack_weights_mxfp8",
-            )
+            packed.update(pack_lowp_experts(
+                dims, src, sizes, lambda n: torch.empty(n, dtype=torch.uint8, device=device), stream))
         packed["_keepalive"] = bits
         self._pack_cache[batch_class] = (key, packed)
         return packed
 
     def _lanes(self, device: torch.device) -> Tensor | None:
-        """Per-expert kernel lane (uint8 [E], 1 = MXFP8) from the promotion mask.
+        """Per-expert kernel lane (uint8 [E], 1 = the layer's low-precision lane,
+        MXFP8 or NVFP4) from the promotion mask.
 
         ``MicroExpertBank._execution_pair`` (experts/bank.py:462-475) decides each
         expert's precision pair from ``promoted_mask``; the lane tensor is built on
@@ -594,7 +619,8 @@ class B200MicroExpertChannelMixer(nn.Module):
         if cached is not None and cached[0] == key:
             return cached[1]
         m = mask.detach().to(device=device, dtype=torch.bool)
-        lanes = torch.where(m, promoted, unpromoted).to(torch.uint8).contiguous()
+        # the kernels take 1 = the layer's low-precision lane (MXFP8 or NVFP4), 0 = BF16
+        lanes = torch.where(m, int(promoted != 0), int(unpromoted != 0)).to(torch.uint8).contiguous()
         object.__setattr__(self, "_lane_cache", (key, lanes))
         return lanes
 
@@ -701,6 +727,7 @@ class B200MicroExpertChannelMixer(nn.Module):
             expert_w1_mx_scales=_lib.ptr(packed.get("expert_w1_mx_scales")),
             expert_w2_mx=_lib.ptr(packed.get("expert_w2_mx")),
             expert_w2_mx_scales=_lib.ptr(packed.get("expert_w2_mx_scales")),
+            expert_nvfp4_amax=_lib.ptr(packed.get("expert_nvfp4_amax")),
         )
         events = self._stage_event_array
         outs = _lib.LayerOutputs(
@@ -807,7 +834,8 @@ class B200MicroExpertChannelMixer(nn.Module):
         lanes = self._lanes(hidden_states.device)
         if lanes is not None and bool(lanes.any()):
             raise NativeExpertPrecisionError(
-                "provider spx_sm100_grouped has no backward for mxfp8 experts; train with BF16 experts"
+                "provider spx_sm100_grouped has no backward for low-precision (mxfp8/nvfp4) experts; "
+                "train with BF16 experts"
             )
         named = self._trainable()
         holder: dict[str, Any] = {}

@@ -221,12 +221,11 @@ class PagedExpertCache:
         return True
 
     def _pack_dims(self, experts: int) -> _lib.LayerDims:
-        from spalmer_b200.experts import layer_dims, uses_mxfp8_lane
+        from spalmer_b200.experts import layer_dims
 
         dims = layer_dims(self.config, 1024, 1)
         dims.num_experts = experts
         dims.shared_dim = 0
-        dims.mxfp8_lane = 1 if uses_mxfp8_lane(self.config) else 0
         return dims
 
     def per_expert_bytes(self) -> dict[str, int]:
@@ -234,9 +233,12 @@ class PagedExpertCache:
         sizes = _lib.PackedSizes()
         _lib.check(lib.spx_layer_sizes(self._pack_dims(1), None, sizes), "spx_layer_sizes")
         out = {"expert_w1": 2 * sizes.expert_w1, "expert_w2": 2 * sizes.expert_w2}
-        if self._pack_dims(1).mxfp8_lane:
+        lane = self._pack_dims(1).mxfp8_lane
+        if lane:
             for name in _PACKED_ARRAYS_MX:
                 out[name] = getattr(sizes, name)
+        if lane == 2:
+            out["expert_nvfp4_amax"] = sizes.expert_nvfp4_amax
         return out
 
     def _pack_host(self) -> None:
@@ -269,8 +271,13 @@ class PagedExpertCache:
                                                 out["expert_w2"].data_ptr(), None, None, stream.cuda_stream),
                            "spx_pack_weights (expert masters)")
                 if dims.mxfp8_lane:
-                    _lib.check(lib.spx_pack_weights_mxfp8(dims, src, *(out[nm].data_ptr() for nm in _PACKED_ARRAYS_MX),
-                                                          stream.cuda_stream), "spx_pack_weights_mxfp8")
+                    from spalmer_b200.experts import pack_lowp_experts
+
+                    lowp = pack_lowp_experts(dims, src, sizes, lambda nb: torch.empty(nb, dtype=torch.uint8, device=dev),
+                                             stream.cuda_stream)
+                    for name in out:
+                        if name in lowp:
+                            out[name].copy_(lowp[name][:out[name].numel()].view(n, -1))
                 for name, t in out.items():
                     host[name][e0:e0 + n].copy_(t)
         stream.synchronize()
@@ -315,6 +322,7 @@ class PagedExpertCache:
             expert_lane_mxfp8=_lib.ptr(lanes),
             expert_w1_mx=_lib.ptr(d.get("expert_w1_mx")), expert_w1_mx_scales=_lib.ptr(d.get("expert_w1_mx_scales")),
             expert_w2_mx=_lib.ptr(d.get("expert_w2_mx")), expert_w2_mx_scales=_lib.ptr(d.get("expert_w2_mx_scales")),
+            expert_nvfp4_amax=_lib.ptr(d.get("expert_nvfp4_amax")),
         )
 
     @property

@@ -59,3 +59,65 @@ def test_mm_nt_matches_restatement(m, n, k):
     assert (got == want).mean() > 0.9
     exact = a.float().numpy() @ b.float().numpy().T
     assert np.linalg.norm(got - exact) / np.linalg.norm(exact) < 0.30  # the reference's bound
+
+
+# ---- the layer with NVFP4 experts (the ("nvfp4", "nvfp4") pair, promoted experts BF16)
+from oracle import mixer_ref as R  # noqa: E402
+from spalmer_b200 import B200MicroExpertChannelMixer, MicroExpertsConfig  # noqa: E402
+from tests.helpers import mxfp8_experts, oracle_params, set_mxfp8_lanes  # noqa: E402
+
+NV_LAYERS = {
+    # decode-sized batch, d below 256 (K padding), loop telemetry
+    "small": (dict(d_model=128, num_experts=32, expert_inter_dim=64, shared_inter_dim=128, active_experts=4,
+                   expert_execution="loop"), (1, 96)),
+    # throughput tiles, fused combine, I = 128 (256-column GEMM1 tiles)
+    "wide": (dict(d_model=256, num_experts=48, expert_inter_dim=128, shared_inter_dim=256, active_experts=8,
+                  expert_execution="loop"), (2, 384)),
+}
+
+
+def nv_config(**kw):
+    kw.setdefault("expert_weight_format", "nvfp4")
+    kw.setdefault("expert_activation_format", "nvfp4")
+    kw.setdefault("expert_promotion_format", "bfloat16")
+    return MicroExpertsConfig(**kw)
+
+
+def relnorm(a, b):
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.mark.parametrize("name", list(NV_LAYERS))
+@pytest.mark.parametrize("fraction", [0.5, 1.0])
+def test_nvfp4_layer_matches_oracle_given_logits(name, fraction):
+    cfg_kw, (batch, seq) = NV_LAYERS[name]
+    config = nv_config(**cfg_kw)
+    torch.manual_seed(0)
+    mixer = B200MicroExpertChannelMixer(config).to(torch.bfloat16).eval().to(DEV)
+    lane = mxfp8_experts(config.num_experts, fraction)
+    set_mxfp8_lanes(mixer, lane)  # the unpromoted experts run the layer's low-precision (NVFP4) lane
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randn(batch, seq, config.d_model, generator=gen).to(torch.bfloat16)
+    x_bits = bf16_bits(x).reshape(-1, config.d_model)
+    params = oracle_params(mixer)
+    k = config.active_experts
+    logits = R.router_logits(x_bits, params.router_w, params.router_b)
+    with torch.no_grad():
+        out = mixer(x.to(DEV), router_logits=from_bits(logits, DEV).reshape(batch, seq, -1))
+    torch.cuda.synchronize()
+    assert mixer.device_status() == 0
+    want = R.mixer_forward(params, x_bits, k, logit_bits=logits, lane_nv=lane, execution="loop")
+    assert np.array_equal(out.metrics["expert_ids"].cpu().numpy().reshape(-1, k), want["expert_ids"])
+    got = bf16_bits_to_f32(bf16_bits(out.update).reshape(want["update"].shape)).astype(np.float64)
+    ref = bf16_bits_to_f32(want["update"]).astype(np.float64)
+    # Same quantiser, same products; a hidden value that rounds one BF16 ulp
+    # apart (accumulation order, the epilogue's SiLU) can land on another E2M1
+    # code, so the bound is on the whole update plus a per-element majority.
+    assert relnorm(got, ref) < 2e-2, relnorm(got, ref)
+    close = np.abs(got - ref) <= 1e-2 + 2e-2 * np.abs(ref)
+    assert close.mean() > 0.97, close.mean()
+    # and the NVFP4 lane is genuinely quantised: the all-BF16 layer differs
+    set_mxfp8_lanes(mixer, np.zeros_like(lane))
+    with torch.no_grad():
+        out_bf16 = mixer(x.to(DEV), router_logits=from_bits(logits, DEV).reshape(batch, seq, -1))
+    assert not torch.equal(out_bf16.update, out.update)
