@@ -39,6 +39,11 @@ CONFIGS = {
     # 100M-preset shape, a seeded 25% of the experts in MXFP8, the rest BF16.
     "m100": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
                           active_experts=8), batch=64, seq=1024, cpu_sample=1024, mxfp8_fraction=0.25),
+    # The same shape with a seeded 25% of the experts in NVFP4 (E2M1, UE4M3 per 1x16, per-tensor
+    # scales; the reference's ("nvfp4", "nvfp4") pair), the rest BF16.
+    "m100_nvfp4": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
+                                active_experts=8, expert_execution="loop"), batch=64, seq=1024, cpu_sample=1024,
+                       mxfp8_fraction=0.25, lowp_format="nvfp4"),
     # The same shape with every expert in BF16.
     "m100_bf16": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
                                active_experts=8), batch=64, seq=1024, cpu_sample=1024),
@@ -121,8 +126,8 @@ def build_mixer(spec: dict, device=None, seed: int = 0):
     zipf = spec.get("zipf", False)
     cfg = dict(spec["cfg"])
     if fraction > 0:
-        cfg.update(expert_weight_format="mxfp8", expert_activation_format="mxfp8",
-                   expert_promotion_format="bfloat16")
+        fmt = spec.get("lowp_format", "mxfp8")
+        cfg.update(expert_weight_format=fmt, expert_activation_format=fmt, expert_promotion_format="bfloat16")
     config = MicroExpertsConfig(**cfg)
     torch.manual_seed(seed)
     mixer = B200MicroExpertChannelMixer(config).to(torch.bfloat16).eval()
@@ -175,9 +180,13 @@ def workload_config(name: str, world: int) -> dict:
         "d_model": cfg["d_model"], "num_experts": cfg["num_experts"],
         "expert_inter_dim": cfg["expert_inter_dim"], "top_k": cfg["active_experts"],
         "shared_inter_dim": cfg["shared_inter_dim"],
-        "expert_precision": (f"MXFP8 (E4M3, E8M0 per 1x32 along K) for a seeded {spec['mxfp8_fraction']:.0%} "
-                             "of the experts (randperm seed 2), BF16 for the rest"
-                             if spec.get("mxfp8_fraction") else "BF16 for all experts"),
+        "expert_precision": (
+            (f"NVFP4 (E2M1, UE4M3 per 1x16 along K, per-tensor FP32 scales) for a seeded "
+             f"{spec['mxfp8_fraction']:.0%} of the experts (randperm seed 2), BF16 for the rest")
+            if spec.get("lowp_format") == "nvfp4" else
+            (f"MXFP8 (E4M3, E8M0 per 1x32 along K) for a seeded {spec['mxfp8_fraction']:.0%} "
+             "of the experts (randperm seed 2), BF16 for the rest")
+            if spec.get("mxfp8_fraction") else "BF16 for all experts"),
         "weights": "random init, torch.manual_seed(0), N(0,0.02)",
         "l2": (f"inputs larger than L2: two {spec['batch'] * spec['seq'] * cfg['d_model'] * 2 / 1e6 / (world if ep else 1):.1f} MB "
                "hidden-state batches alternated, plus the weights; steps timed back to back"),
@@ -422,7 +431,9 @@ def run_ours(args) -> None:
         if lane is not None:
             util = out.metrics["expert_utilization"].float().cpu()
             mx_share = float(util[lane].sum())
-        peak = pk["bf16_tflops"] / ((1.0 - mx_share) + mx_share / 2.0)
+        nvfp4 = spec.get("lowp_format") == "nvfp4"
+        lowp_speed = 4.0 if nvfp4 else 2.0  # dense FP4 / FP8 tensor rate over BF16
+        peak = pk["bf16_tflops"] / ((1.0 - mx_share) + mx_share / lowp_speed)
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -431,14 +442,16 @@ def run_ours(args) -> None:
             "e2e": {"value": e2e_value, "unit": "tokens/s",
                     "h2d_bytes_per_step": tokens * config.d_model * 2,
                     "d2h_bytes_per_step": tokens * config.d_model * 2 + 2},
-            "gpu_launches": K * (14 if lane is not None else 11),
+            "gpu_launches": K * ((17 if nvfp4 else 14) if lane is not None else 11),
             "roofline": {"bound": "tensor",
-                         "kernel": "gemm_kernel<kEpiSwiglu> (expert GEMM1, gathered rows; BF16 and MXFP8 lanes)",
+                         "kernel": ("gemm_kernel<kEpiSwiglu> (expert GEMM1; BF16 lane gathered rows, "
+                                    + ("NVFP4 lane E2M1 rows)" if nvfp4 else "MXFP8 lane)")),
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": STAGE_TRAFFIC_BYTES.get(args.config),
                          "traffic_unit": "bytes per forward (ncu dram read+write of the stage's launches)",
                          "mxfp8_pair_share": mx_share,
-                         "peak_source": f"{pk['source']} bf16 burst; MXFP8 share at 2x"},
+                         "peak_source": f"{pk['source']} bf16 burst; " + ("NVFP4 share at 4x" if nvfp4
+                                                                             else "MXFP8 share at 2x")},
             "layer_tensor_tflops": sum(flops.values()) / (ms_per_step / 1e3) / 1e12,
             "stages_ms": stages,
             "device_status": status,

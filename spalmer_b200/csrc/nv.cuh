@@ -57,10 +57,20 @@ __device__ __forceinline__ uint32_t nv_quantize16(const float (&v)[16], float pt
   const __nv_fp8_storage_t sb = __nv_cvt_float_to_fp8(s, __NV_SATFINITE, __NV_E4M3);
   const float sf = __half2float(__half(__nv_cvt_fp8_to_halfraw(sb, __NV_E4M3)));
   const float total = pts * sf;
+  if (amax == 0.0f) {  // zeros (K padding): only the signs remain
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t c = signbit(v[j]) ? 8u : 0u;
+      if (j < 8)
+        w0 |= c << (4 * j);
+      else
+        w1 |= c << (4 * (j - 8));
+    }
+    return static_cast<uint32_t>(sb);
+  }
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    const float x = fminf(fmaxf(v[j] / total, -6.0f), 6.0f);
-    const uint32_t c = nv_e2m1(x);
+    const uint32_t c = nv_e2m1(fminf(fmaxf(v[j] / total, -6.0f), 6.0f));
     if (j < 8)
       w0 |= c << (4 * j);
     else

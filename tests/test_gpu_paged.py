@@ -190,3 +190,17 @@ def test_stage_expert_slots_copies_whole_experts_from_host():
     nb = (_lib.ctypes.c_int64 * 1)(4096)
     dst1 = (_lib.ctypes.c_void_p * 1)(dev[0].data_ptr())
     assert lib.spx_stage_expert_slots(src_bad, dst1, nb, 1, pairs_dev.data_ptr(), 3, E, C, 0, stream) == -1
+
+
+def test_paged_nvfp4_lane_matches_unpaged():
+    config = MicroExpertsConfig(**M10, expert_weight_format="nvfp4", expert_activation_format="nvfp4",
+                                expert_promotion_format="bfloat16")
+    lanes = mxfp8_experts(config.num_experts, 0.5)
+    ref_mixer, paged = make_pair(config, lanes=lanes)
+    enable_expert_offload(paged, DEV, cache_size=20)
+    x = hidden((2, 512), config.d_model)
+    with torch.no_grad():
+        want = ref_mixer(x)
+        got = paged(x)
+    assert_same(got, want)
+    assert paged.device_status() == 0
