@@ -3,13 +3,15 @@
 * ``native_provider_capabilities``: the capability hook the reference imports
   (precision.py:396-430), with claims shaped like ``ExpertPrecisionCapability``
   (precision.py:68-107).  Claims are verified by running one small layer on the
-  device; the backward pass does not exist yet, so ``backward_available`` is
-  False and the reference will not select this provider for training.
-* ``mx_quantize_rows`` / ``mxfp8_mm_nt`` / ``native_mxfp8_linear`` /
+  device.  The BF16 pair trains (``spx_layer_backward``); the MXFP8 and NVFP4
+  pairs are forward-only, so their ``backward_available`` is False.
+* ``mx_quantize_rows`` / ``mxfp8_mm_nt`` / ``native_mxfp8_linear``,
+  ``nvfp4_quantize_rows`` / ``nvfp4_mm_nt`` / ``native_nvfp4_linear`` and
   ``native_expert_matmul``: forward-only equivalents of ``_mx_quantize_rows``,
-  ``_mxfp8_mm_nt``, ``native_mxfp8_linear`` and ``native_expert_matmul``
-  (experts/native.py:91-202, 305-350) running on libspx's quantiser and
-  block-scaled tcgen05 GEMM.  No emulation: other pairs raise.
+  ``_mxfp8_mm_nt``, ``native_mxfp8_linear``, ``_pack_nvfp4``,
+  ``native_nvfp4_linear`` and ``native_expert_matmul`` (experts/native.py:91-350)
+  running on libspx's quantisers and block-scaled tcgen05 GEMMs
+  (kind::mxf8f6f4 and kind::mxf4nvf4).  No emulation: other pairs raise.
 """
 
 from __future__ import annotations
@@ -39,7 +41,7 @@ def _require_cuda_bf16(left: Tensor, right: Tensor, *, operation: str) -> None:
 
 def _forward_only(*tensors: Tensor) -> None:
     if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tensors):
-        raise NotImplementedError("the B200 MXFP8 provider implements the forward pass only")
+        raise NotImplementedError("the B200 low-precision (MXFP8/NVFP4) provider implements the forward pass only")
 
 
 def mx_quantize_rows(value: Tensor) -> tuple[Tensor, Tensor]:
@@ -97,23 +99,85 @@ def native_mxfp8_linear(input: Tensor, weight: Tensor, bias: Tensor | None = Non
     return out.reshape(*input.shape[:-1], weight.shape[0])
 
 
+def nvfp4_quantize_rows(value: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+    """``_pack_nvfp4`` of BF16 rows (experts/native.py:205-218): E2M1 values
+    ``[rows, kp/2]`` (two per byte), UE4M3 scale bytes ``[rows, kp/16]`` and the
+    per-tensor amax (float32 scalar; the per-tensor scale is amax / 2688), with
+    kp = cols rounded up to 256 (zero columns beyond cols)."""
+
+    if value.ndim != 2 or value.dtype != torch.bfloat16 or not value.is_cuda:
+        raise ValueError("nvfp4_quantize_rows expects a [rows, cols] bfloat16 CUDA tensor")
+    rows, cols = value.shape
+    if cols < 1:
+        raise ValueError("the row length must be positive")
+    kp = -(-cols // 256) * 256
+    src = value.contiguous()
+    values = torch.empty(rows, kp // 2, dtype=torch.uint8, device=value.device)
+    scales = torch.empty(rows, kp // 16, dtype=torch.uint8, device=value.device)
+    amax = torch.zeros((), dtype=torch.float32, device=value.device)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(value.device).cuda_stream
+    _lib.check(lib.spx_nvfp4_quantize_rows(src.data_ptr(), rows, cols, values.data_ptr(), scales.data_ptr(),
+                                           amax.data_ptr(), stream), "spx_nvfp4_quantize_rows")
+    return values, scales, amax
+
+
+def nvfp4_mm_nt(left: Tensor, right_rows: Tensor) -> Tensor:
+    """``left @ right_rows.T`` with both operands NVFP4 (experts/native.py:224-262)."""
+
+    if left.ndim != 2 or right_rows.ndim != 2:
+        raise ValueError("native NVFP4 operands must be rank-2 matrices")
+    if left.shape[1] != right_rows.shape[1]:
+        raise ValueError("native NVFP4 operands must share a contraction dimension")
+    _require_cuda_bf16(left, right_rows, operation="native NVFP4 GEMM")
+    _forward_only(left, right_rows)
+    m, k = left.shape
+    n = right_rows.shape[0]
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=left.device)
+    if m == 0 or n == 0:
+        return out
+    lib = _lib.load()
+    nbytes = lib.spx_nvfp4_mm_workspace(m, n, k)
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=left.device)
+    a = left.detach().contiguous()
+    b = right_rows.detach().contiguous()
+    stream = torch.cuda.current_stream(left.device).cuda_stream
+    _lib.check(lib.spx_nvfp4_mm_nt(a.data_ptr(), b.data_ptr(), m, n, k, out.data_ptr(), ws.data_ptr(), nbytes,
+                                   stream), "spx_nvfp4_mm_nt")
+    return out
+
+
+def native_nvfp4_linear(input: Tensor, weight: Tensor, bias: Tensor | None = None) -> Tensor:
+    """``F.linear`` whose GEMM executes in NVFP4 (experts/native.py:292-302), forward only."""
+
+    if weight.ndim != 2 or input.ndim < 1 or input.shape[-1] != weight.shape[1]:
+        raise ValueError("native NVFP4 linear received incompatible input/weight shapes")
+    _require_cuda_bf16(input, weight, operation="native NVFP4 linear")
+    out = nvfp4_mm_nt(input.reshape(-1, input.shape[-1]), weight)
+    if bias is not None:
+        out = out + bias
+    return out.reshape(*input.shape[:-1], weight.shape[0])
+
+
 def native_expert_matmul(input: Tensor, weight: Tensor, bias: Tensor | None = None, *, weight_format: str,
                          activation_format: str) -> Tensor:
     """``input @ weight`` for an expert's ``[in, out]`` weight (experts/native.py:305-350).
 
-    Only the ("mxfp8", "mxfp8") pair runs here; the BF16 expert lane is the
-    grouped layer kernel, and every other pair raises (no emulation).
+    The ("mxfp8", "mxfp8") and ("nvfp4", "nvfp4") pairs run here; the BF16
+    expert lane is the grouped layer kernel, and every other pair raises (no
+    emulation).
     """
 
     if weight.ndim != 2 or input.ndim < 1 or input.shape[-1] != weight.shape[0]:
         raise ValueError("native expert matmul received incompatible input/weight shapes")
     pair = (str(weight_format), str(activation_format))
-    if pair != ("mxfp8", "mxfp8"):
+    if pair not in {("mxfp8", "mxfp8"), ("nvfp4", "nvfp4")}:
         raise NativeExpertPrecisionError(
             f"no integrated native expert kernel for {weight_format}/{activation_format}; emulation is prohibited"
         )
-    _require_cuda_bf16(input, weight, operation="native MXFP8 expert matmul")
-    out = mxfp8_mm_nt(input.reshape(-1, input.shape[-1]), weight.t())
+    mm = nvfp4_mm_nt if pair[0] == "nvfp4" else mxfp8_mm_nt
+    _require_cuda_bf16(input, weight, operation=f"native {pair[0].upper()} expert matmul")
+    out = mm(input.reshape(-1, input.shape[-1]), weight.t())
     if bias is not None:
         out = out + bias
     return out.reshape(*input.shape[:-1], weight.shape[1])
@@ -149,7 +213,7 @@ def native_provider_capabilities(device: str | torch.device | None = None) -> li
     if resolved.type == "cuda" and resolved.index is None and torch.cuda.is_available():
         resolved = torch.device("cuda", torch.cuda.current_device())
     claims = []
-    for fmt in ("bfloat16", "mxfp8"):
+    for fmt in ("bfloat16", "mxfp8", "nvfp4"):
         if resolved.type != "cuda" or not torch.cuda.is_available():
             available, detail = False, "CUDA is unavailable"
         else:
@@ -160,7 +224,7 @@ def native_provider_capabilities(device: str | torch.device | None = None) -> li
                 "weight_format": fmt,
                 "activation_format": fmt,
                 "forward_available": available,
-                "backward_available": False,
+                "backward_available": available and fmt == "bfloat16",
                 "grouped_available": available,
                 "verified": available,
                 "detail": detail,

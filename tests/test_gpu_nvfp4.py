@@ -121,3 +121,27 @@ def test_nvfp4_layer_matches_oracle_given_logits(name, fraction):
     with torch.no_grad():
         out_bf16 = mixer(x.to(DEV), router_logits=from_bits(logits, DEV).reshape(batch, seq, -1))
     assert not torch.equal(out_bf16.update, out.update)
+
+
+def test_reference_native_nvfp4_bound_and_provider():
+    """test_native_precision.py's ("nvfp4", "nvfp4", 0.30) forward bound through the
+    module-level helpers, the expert layout, and the provider claim."""
+
+    from spalmer_b200.native import (native_expert_matmul, native_nvfp4_linear, native_provider_capabilities,
+                                     nvfp4_quantize_rows)
+
+    gen = torch.Generator(device="cpu").manual_seed(1204)
+    x = torch.randn((7, 37), generator=gen).to(device=DEV, dtype=torch.bfloat16)
+    w = torch.randn((23, 37), generator=gen).to(device=DEV, dtype=torch.bfloat16)
+    out = native_nvfp4_linear(x, w)
+    ref = x.float() @ w.float().t()
+    rel = float((out.float() - ref).norm() / ref.norm().clamp_min(1e-12))
+    assert rel < 0.30, rel
+    out2 = native_expert_matmul(x, w.t().contiguous(), weight_format="nvfp4", activation_format="nvfp4")
+    assert torch.equal(out2, out)
+    values, scales, amax = nvfp4_quantize_rows(x)
+    assert values.shape == (7, 128) and scales.shape == (7, 16)
+    assert float(amax) == float(x.float().abs().max())
+    claims = {c["weight_format"]: c for c in native_provider_capabilities(DEV)}
+    assert claims["nvfp4"]["forward_available"] and not claims["nvfp4"]["backward_available"]
+    assert claims["bfloat16"]["backward_available"]
