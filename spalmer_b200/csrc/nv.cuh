@@ -26,17 +26,21 @@ constexpr float kNvScaleMin = 0.015625f; // 2^-6, the smallest normal E4M3
 
 // E2M1 code (sign in bit 3) of v, round to nearest even on the grid
 // {0, 0.5, 1, 1.5, 2, 3, 4, 6}; |v| <= 6 expected (clamped by the caller).
+// The grid has spacing 0.5 below 2, 1 on [2, 4] and 2 above, and its codes
+// count along it, so one round-to-nearest-even to the spacing of |v|'s range
+// gives the code: below 2 the code is rint(2|v|) (0..4), on [2, 4) it is
+// rint(|v|) + 2 (4..6), from 4 it is rint(|v| / 2) + 4 (6..7).  The ties of
+// the grid (0.25, 0.75, ..., 5) are the ties of these roundings, and the
+// range boundaries 2 and 4 are grid points.
 __host__ __device__ __forceinline__ uint32_t nv_e2m1(float v) {
-  const float m = fabsf(v);
+  const float m = fminf(fabsf(v), 6.0f);
   uint32_t c;
-  if (m <= 0.25f) c = 0;
-  else if (m < 0.75f) c = 1;
-  else if (m <= 1.25f) c = 2;
-  else if (m < 1.75f) c = 3;
-  else if (m <= 2.5f) c = 4;
-  else if (m < 3.5f) c = 5;
-  else if (m <= 5.0f) c = 6;
-  else c = 7;
+  if (m < 2.0f)
+    c = static_cast<uint32_t>(rintf(2.0f * m));
+  else if (m < 4.0f)
+    c = static_cast<uint32_t>(rintf(m)) + 2u;
+  else
+    c = static_cast<uint32_t>(rintf(0.5f * m)) + 4u;
   return c | (signbit(v) ? 8u : 0u);
 }
 

@@ -152,7 +152,7 @@ __global__ void nv_quantize_rows_kernel(const uint16_t* __restrict__ src, int64_
   }
 }
 
-// One CTA (256 threads) per tile: the tile's rows x 16-element blocks.
+// One CTA (256 threads) per tile: a warp per row, a lane per 16-element block.
 __global__ void nv_quantize_tiles_kernel(const int4* __restrict__ tiles, const int* __restrict__ num_tiles,
                                          const uint16_t* __restrict__ src, int64_t ld, int cols,
                                          const int* __restrict__ gather, const float* __restrict__ amax, int kp,
@@ -163,11 +163,13 @@ __global__ void nv_quantize_tiles_kernel(const int4* __restrict__ tiles, const i
   const int nblk = kp / kNvBlock;
   const float pts = nv_tensor_scale(amax[t.w]);
   const bool vec = (cols % 8) == 0 && (ld % 8) == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
-  for (int i = threadIdx.x; i < t.z * nblk; i += blockDim.x) {
-    const int r = i / nblk, blk = i - r * nblk;
+  const int lane = threadIdx.x & 31;
+  for (int r = threadIdx.x >> 5; r < t.z; r += blockDim.x >> 5) {
     const int64_t p = t.y + r;
     const int64_t srow = gather != nullptr ? gather[p] : p;
-    quantize_block(src + srow * ld, cols, vec, blk, pts, q + p * (kp / 2), sf + p * nblk);
+    const uint16_t* row = src + srow * ld;
+    for (int blk = lane; blk < nblk; blk += 32)
+      quantize_block(row, cols, vec, blk, pts, q + p * (kp / 2), sf + p * nblk);
   }
 }
 
