@@ -52,6 +52,10 @@ CONFIGS = {
     "ep_skew": dict(cfg=dict(d_model=1024, num_experts=200, expert_inter_dim=256, shared_inter_dim=2048,
                              active_experts=8, router_bias=True), batch=128, seq=1024, cpu_sample=256,
                     zipf=True, expert_parallel=True),
+    # The same with the rows moved by NCCL all-to-all-v instead of stores into the peers' buffers.
+    "ep_skew_nccl": dict(cfg=dict(d_model=1024, num_experts=200, expert_inter_dim=256, shared_inter_dim=2048,
+                                  active_experts=8, router_bias=True), batch=128, seq=1024, cpu_sample=256,
+                         zipf=True, expert_parallel=True, exchange="nccl"),
     # The same with token rows sent once per destination GPU and pair rows summed
     # at the expert's GPU before they return.
     "ep_skew_dedup": dict(cfg=dict(d_model=1024, num_experts=200, expert_inter_dim=256, shared_inter_dim=2048,
@@ -171,7 +175,10 @@ def workload_config(name: str, world: int) -> dict:
         extra = {"total_tokens": spec["batch"] * spec["seq"], "experts_per_gpu": cfg["num_experts"] // world,
                  "row_dedup": bool(spec.get("dedup", False)),
                  "router_bias": "Zipf(1.1) popularity: b_e = alpha*ln(rank_e), alpha from tests/golden/zipf_ep_skew.json",
-                 "exchange": "NCCL all_to_all_single (counts, rows out, rows back); one host read of the counts"}
+                 "exchange": ("NCCL all_to_all_single (counts, rows out, rows back); one host read of the counts"
+                              if spec.get("exchange") == "nccl" or spec.get("dedup") else
+                              "counts all-gathered (one host read); rows stored straight into the peers' IPC "
+                              "buffers by spx_rows_to_peers, a one-element NCCL all-reduce after each move")}
     return {
         "workload": f"{name}: SPALMER micro-expert layer forward" + (" (expert parallel)" if ep and world > 1 else ""),
         **extra,
@@ -487,7 +494,8 @@ def run_ep(args) -> None:
     tokens = batch * seq
     mixer, _ = build_mixer(spec, device)
     config = mixer.config
-    layer = ExpertParallelMixer(mixer, dedup=spec.get("dedup", False)) if world > 1 else None
+    layer = (ExpertParallelMixer(mixer, dedup=spec.get("dedup", False), exchange=spec.get("exchange"))
+             if world > 1 else None)
     x_cpu = torch.randn(spec["batch"], seq, config.d_model, generator=torch.Generator().manual_seed(1))
     x_cpu = x_cpu.to(torch.bfloat16)[rank * batch:(rank + 1) * batch].contiguous()
     x_host = x_cpu.pin_memory()
@@ -579,6 +587,8 @@ def run_ep(args) -> None:
         if clocks is not None:
             line["clocks"] = clocks
         print(json.dumps(line), flush=True)
+    if layer is not None:
+        layer.close()
     if world > 1:
         dist.destroy_process_group()
 

@@ -344,6 +344,24 @@ int spx_stage_expert_slots(const void* const* src, void* const* dst, const int64
                            const int32_t* pairs, int32_t n, int32_t num_experts, int32_t slots, int32_t ctas,
                            void* stream);
 
+/* ---- expert-parallel exchange over peer memory (NVLink / NVSwitch)
+ * Each rank allocates its exchange buffers here (cudaMalloc) and publishes
+ * the 64-byte CUDA IPC handle; peers open it as a device pointer of theirs.
+ * spx_rows_to_peers stores rows straight into (peer) buffers: row i
+ * (source row index[i] / index_div, or i when index is NULL) of segment g
+ * (seg_offsets[g] <= i < seg_offsets[g+1]) goes to row dst_row_offsets[g] +
+ * i - seg_offsets[g] of dst_ptrs[g] (row stride ld_dst).  seg_offsets
+ * [groups+1], dst_ptrs [groups] and dst_row_offsets [groups] are device
+ * arrays.  The kernel fences its stores at system scope; the caller orders
+ * the peers' reads after it (a stream-ordered collective). */
+int spx_ipc_buffer_alloc(size_t bytes, void** device_ptr, uint8_t* handle);
+int spx_ipc_buffer_open(const uint8_t* handle, void** peer_ptr);
+int spx_ipc_buffer_close(void* peer_ptr);
+int spx_ipc_buffer_free(void* device_ptr);
+int spx_rows_to_peers(const uint16_t* src, int64_t ld_src, const int32_t* index, int32_t index_div, int64_t rows,
+                      int32_t d, const int64_t* seg_offsets, void* const* dst_ptrs, const int64_t* dst_row_offsets,
+                      int64_t ld_dst, int32_t groups, void* stream);
+
 /* ---- backward of the routed experts and the router scores
  * Reference: autograd through MicroExpertChannelMixer.forward
  * (experts/mixer.py:185-241: router.py:51-95, bank.py:705-779, 970-978,

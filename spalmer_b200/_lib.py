@@ -59,6 +59,11 @@ EXPORTED = (
     "spx_nvfp4_mm_workspace",
     "spx_nvfp4_mm_nt",
     "spx_pack_weights_nvfp4",
+    "spx_ipc_buffer_alloc",
+    "spx_ipc_buffer_open",
+    "spx_ipc_buffer_close",
+    "spx_ipc_buffer_free",
+    "spx_rows_to_peers",
 )
 
 ABI_VERSION = 6
@@ -247,6 +252,15 @@ def load() -> ctypes.CDLL:
         ),
         "spx_nvfp4_quantize_rows": (ctypes.c_int, [_vp, ctypes.c_int64, ctypes.c_int32, _vp, _vp, _vp, _vp]),
         "spx_pack_weights_nvfp4": (ctypes.c_int, [P(LayerDims), P(ReferenceWeights), _vp, _vp, _vp, _vp, _vp, _vp]),
+        "spx_ipc_buffer_alloc": (ctypes.c_int, [ctypes.c_size_t, P(_vp), _vp]),
+        "spx_ipc_buffer_open": (ctypes.c_int, [_vp, P(_vp)]),
+        "spx_ipc_buffer_close": (ctypes.c_int, [_vp]),
+        "spx_ipc_buffer_free": (ctypes.c_int, [_vp]),
+        "spx_rows_to_peers": (
+            ctypes.c_int,
+            [_vp, ctypes.c_int64, _vp, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, _vp, _vp, _vp, ctypes.c_int64,
+             ctypes.c_int32, _vp],
+        ),
         "spx_nvfp4_mm_workspace": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]),
         "spx_nvfp4_mm_nt": (
             ctypes.c_int,

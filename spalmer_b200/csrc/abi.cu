@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <cstring>
 
 #include "kernels.h"
 #include "nv.cuh"
@@ -1205,6 +1206,60 @@ int spx_stage_expert_slots(const void* const* src, void* const* dst, const int64
   a.slots = slots;
   a.ctas = ctas;
   return launch_stage_slots(a, static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------- peer exchange
+int spx_ipc_buffer_alloc(size_t bytes, void** device_ptr, uint8_t* handle) {
+  if (bytes == 0 || device_ptr == nullptr || handle == nullptr) return SPX_ERR_INVALID_ARG;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return SPX_ERR_CUDA;
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(p);
+    return SPX_ERR_CUDA;
+  }
+  memcpy(handle, &h, sizeof(h));
+  *device_ptr = p;
+  return SPX_OK;
+}
+
+int spx_ipc_buffer_open(const uint8_t* handle, void** peer_ptr) {
+  if (handle == nullptr || peer_ptr == nullptr) return SPX_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return SPX_ERR_CUDA;
+  }
+  *peer_ptr = p;
+  return SPX_OK;
+}
+
+int spx_ipc_buffer_close(void* peer_ptr) {
+  if (peer_ptr == nullptr) return SPX_ERR_INVALID_ARG;
+  return cudaIpcCloseMemHandle(peer_ptr) == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+int spx_ipc_buffer_free(void* device_ptr) {
+  if (device_ptr == nullptr) return SPX_ERR_INVALID_ARG;
+  return cudaFree(device_ptr) == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+int spx_rows_to_peers(const uint16_t* src, int64_t ld_src, const int32_t* index, int32_t index_div, int64_t rows,
+                      int32_t d, const int64_t* seg_offsets, void* const* dst_ptrs, const int64_t* dst_row_offsets,
+                      int64_t ld_dst, int32_t groups, void* stream) {
+  if (rows < 0 || d < 1 || index_div < 1 || groups < 1 || ld_src < d || ld_dst < d) return SPX_ERR_INVALID_ARG;
+  if (rows == 0) return SPX_OK;
+  if (src == nullptr || seg_offsets == nullptr || dst_ptrs == nullptr || dst_row_offsets == nullptr)
+    return SPX_ERR_INVALID_ARG;
+  return launch_rows_to_peers(src, ld_src, index, index_div, rows, d, seg_offsets,
+                              reinterpret_cast<uint16_t* const*>(dst_ptrs), dst_row_offsets, ld_dst, groups,
+                              static_cast<cudaStream_t>(stream));
 }
 
 // ---------------------------------------------------------------- backward

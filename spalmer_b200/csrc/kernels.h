@@ -229,6 +229,13 @@ struct PageTilesArgs {
 };
 int launch_page_tiles(const PageTilesArgs& a, cudaStream_t stream);
 
+// Rows to (peer) buffers: row i (source row index[i] / index_div, or i) of
+// segment g (seg[g] <= i < seg[g+1]) is stored at row dst_row[g] + i - seg[g]
+// of dst[g]; seg, dst and dst_row are device arrays.  Fences at system scope.
+int launch_rows_to_peers(const uint16_t* src, int64_t ld_src, const int* index, int index_div, int64_t rows, int d,
+                         const int64_t* seg, uint16_t* const* dst, const int64_t* dst_row, int64_t ld_dst,
+                         int groups, cudaStream_t stream);
+
 // ---- NVFP4 (nvfp4.cu).  Quantised rows: E2M1 [rows, kp/2] bytes, UE4M3
 // scales [rows, kp/16] bytes (kp a multiple of 256; K beyond `cols` is zero).
 // Largest |v| of a row-major matrix, raised into *amax (zeroed by the caller).

@@ -279,15 +279,126 @@ class CudaOps:
         return out
 
 
+class _RawRows:
+    """A raw device allocation seen by torch as an int16 matrix (zero copy)."""
+
+    def __init__(self, ptr: int, rows: int, cols: int):
+        self.__cuda_array_interface__ = {"shape": (rows, cols), "typestr": "<i2", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerExchange:
+    """Exchange buffers of every rank of the group, opened as peer pointers.
+
+    Each rank owns a receive buffer (rows of the pairs routed to its experts,
+    from every sender) and a return buffer (the expert outputs of its own
+    pairs, in its dispatch order), allocated by ``spx_ipc_buffer_alloc``;
+    the CUDA IPC handles are all-gathered once and opened by the peers.  Rows
+    move with ``spx_rows_to_peers`` (the sending GPU stores into the peer's
+    buffer over NVLink); a one-element NCCL all-reduce after each move orders
+    the receivers' reads.  Buffers grow together (the sizes are computed from
+    the all-gathered counts, so every rank takes the same decision).
+    """
+
+    def __init__(self, group: Any, device: torch.device, d: int):
+        self.group = group
+        self.device = device
+        self.d = d
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.capacity = {"recv": 0, "back": 0}
+        self.local: dict[str, int] = {}
+        self.peers: dict[str, list[int]] = {}
+        self.ptr_tables: dict[str, Tensor] = {}
+        self.flag = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def _release(self, kind: str) -> None:
+        lib = _lib.load()
+        if kind not in self.local:
+            return
+        torch.cuda.synchronize(self.device)
+        self.barrier()
+        torch.cuda.synchronize(self.device)  # no peer touches the buffers any more
+        for g, ptr in enumerate(self.peers[kind]):
+            if g != self.rank:
+                _lib.check(lib.spx_ipc_buffer_close(_lib.ctypes.c_void_p(ptr)), "spx_ipc_buffer_close")
+        _lib.check(lib.spx_ipc_buffer_free(_lib.ctypes.c_void_p(self.local[kind])), "spx_ipc_buffer_free")
+        del self.local[kind], self.peers[kind], self.ptr_tables[kind]
+        self.capacity[kind] = 0
+
+    def ensure(self, kind: str, rows: int) -> None:
+        """Collective: every rank calls with the same ``rows`` (the largest need)."""
+
+        if rows <= self.capacity[kind]:
+            return
+        lib = _lib.load()
+        self._release(kind)
+        cap = max(int(rows * 1.25), 1024)
+        ptr = _lib.ctypes.c_void_p()
+        handle = (_lib.ctypes.c_uint8 * 64)()
+        with torch.cuda.device(self.device):
+            _lib.check(lib.spx_ipc_buffer_alloc(cap * self.d * 2, _lib.ctypes.byref(ptr), handle),
+                       "spx_ipc_buffer_alloc")
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
+        allh = torch.empty(self.world * 64, dtype=torch.uint8, device=self.device)
+        dist.all_gather_into_tensor(allh, mine, group=self.group)
+        allh = allh.cpu().numpy().reshape(self.world, 64)
+        peers = []
+        for g in range(self.world):
+            if g == self.rank:
+                peers.append(ptr.value)
+                continue
+            pp = _lib.ctypes.c_void_p()
+            h = (_lib.ctypes.c_uint8 * 64)(*allh[g].tolist())
+            with torch.cuda.device(self.device):
+                _lib.check(lib.spx_ipc_buffer_open(h, _lib.ctypes.byref(pp)), "spx_ipc_buffer_open")
+            peers.append(pp.value)
+        self.local[kind] = ptr.value
+        self.peers[kind] = peers
+        self.ptr_tables[kind] = torch.tensor(peers, dtype=torch.int64, device=self.device)
+        self.capacity[kind] = cap
+
+    def view(self, kind: str, rows: int) -> Tensor:
+        """This rank's buffer rows [0, rows) as a BF16 tensor."""
+
+        raw = torch.as_tensor(_RawRows(self.local[kind], max(rows, 0), self.d), device=self.device)
+        return raw.view(torch.bfloat16)
+
+    def send(self, kind: str, src: Tensor, index: Tensor | None, div: int, seg: np.ndarray,
+             dst_rows: np.ndarray) -> None:
+        """Rows of ``src`` (through ``index // div`` when given) in segments
+        ``seg`` [G+1] to every rank's ``kind`` buffer at rows ``dst_rows`` [G]."""
+
+        lib = _lib.load()
+        rows = int(seg[-1])
+        meta = torch.from_numpy(np.concatenate([seg, dst_rows]).astype(np.int64)).pin_memory()
+        meta = meta.to(self.device, non_blocking=True)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(lib.spx_rows_to_peers(src.data_ptr(), src.stride(0), _lib.ptr(index), div, rows, self.d,
+                                         meta.data_ptr(), self.ptr_tables[kind].data_ptr(),
+                                         meta[self.world + 1:].data_ptr(), self.d, self.world, stream),
+                   "spx_rows_to_peers")
+
+    def barrier(self) -> None:
+        dist.all_reduce(self.flag, group=self.group)
+
+    def close(self) -> None:
+        for kind in list(self.local):
+            self._release(kind)
+
+
 class ExpertParallelMixer:
     """Expert-parallel forward of a `B200MicroExpertChannelMixer` (same
     parameters on every rank; rank r executes experts [r*E/G, (r+1)*E/G)).
 
     ``forward(hidden [B, S, d])`` takes this rank's tokens and returns their
     update and this rank's routing metrics (statistics over the local tokens).
+    ``exchange="peer"`` (the default on CUDA) moves the rows with stores into
+    the peers' buffers (``PeerExchange``); ``"nccl"`` with NCCL all-to-all-v.
     """
 
-    def __init__(self, mixer: Any, group: Any = None, ops: Any = None, dedup: bool = False):
+    def __init__(self, mixer: Any, group: Any = None, ops: Any = None, dedup: bool = False,
+                 exchange: str | None = None):
         self.mixer = mixer
         self.dedup = dedup
         self.group = group
@@ -298,7 +409,22 @@ class ExpertParallelMixer:
             device = next(mixer.parameters()).device
             ops = CudaOps(mixer, self.rank, self.world, device)
         self.ops = ops
-        self.side = torch.cuda.Stream(ops.device) if isinstance(ops, CudaOps) else None
+        cuda = isinstance(ops, CudaOps)
+        self.side = torch.cuda.Stream(ops.device) if cuda else None
+        if exchange is None:
+            exchange = "peer" if cuda and not dedup else "nccl"
+        if exchange not in {"peer", "nccl"}:
+            raise ValueError("exchange must be 'peer' or 'nccl'")
+        if exchange == "peer" and (not cuda or dedup):
+            raise ValueError("the peer exchange needs the CUDA backend and runs without row de-dup")
+        self.exchange = exchange
+        self.peer = PeerExchange(group, ops.device, mixer.config.d_model) if exchange == "peer" else None
+
+    def close(self) -> None:
+        """Release the peer exchange buffers (collective)."""
+
+        if self.peer is not None:
+            self.peer.close()
 
     def _local_lanes(self) -> Tensor | None:
         lanes = self.mixer._lanes(self.ops.device) if isinstance(self.ops, CudaOps) else None
@@ -324,6 +450,17 @@ class ExpertParallelMixer:
         r = ops.route(x, logits)
         if self.dedup:
             update, stats = self._exchange_dedup(x, r, shared)
+            return {
+                "update": update.reshape(B, S, d),
+                "auxiliary_loss": r["auxiliary_loss"][0],
+                "expert_ids": r["expert_ids"].reshape(B, S, k),
+                "routing_weights": r["routing_weights"].reshape(B, S, k),
+                "router_scores": r["router_scores"].reshape(B, S, -1),
+                "expert_utilization": r["expert_utilization"],
+                **stats,
+            }
+        if self.peer is not None:
+            update, stats = self._exchange_peer(x, r, shared)
             return {
                 "update": update.reshape(B, S, d),
                 "auxiliary_loss": r["auxiliary_loss"][0],
@@ -365,6 +502,49 @@ class ExpertParallelMixer:
             "send_rows": plan.send_rows,
             "recv_rows": plan.recv_rows,
         }
+
+    def _exchange_peer(self, x: Tensor, r: dict, shared: Tensor | None) -> tuple[Tensor, dict]:
+        """Steps 2-6 with the rows stored straight into the peers' buffers.
+
+        The all-gathered per-expert counts give every rank the full matrix
+        C[s, g] (pairs of rank s on rank g's experts), hence every offset:
+        rank s's pairs for g land at rows sum_{s' < s} C[s', g] of g's receive
+        buffer, and g returns them to rows sum_{g' < g} C[s, g'] of s's return
+        buffer -- s's own dispatch order, which the combine reads.
+        """
+
+        ops, G, el, me, k = self.ops, self.world, self.e_local, self.rank, self.mixer.active_experts
+        T, d = x.shape
+        counts_all = torch.empty(G * self.mixer.config.num_experts, dtype=torch.int32, device=x.device)
+        dist.all_gather_into_tensor(counts_all, r["counts"], group=self.group)
+        ca = counts_all.cpu().numpy().astype(np.int64).reshape(G, G, el)  # [sender, owner, local expert]
+        C = ca.sum(axis=2)  # [sender, owner]
+        peer = self.peer
+        peer.ensure("recv", int(C.sum(axis=0).max()))
+        peer.ensure("back", int(C.sum(axis=1).max()))
+        # 3. rows of this rank's pairs (dispatch order) -> owners' receive buffers
+        send_seg = np.concatenate([[0], np.cumsum(C[me])])
+        recv_at = C[:me].sum(axis=0)  # where this rank's block starts in every owner's buffer
+        peer.send("recv", x, r["order"], k, send_seg, recv_at)
+        peer.barrier()
+        # 4. local experts on the received rows (from each sender: local expert 0, 1, ...)
+        R = int(C[:, me].sum())
+        recv = peer.view("recv", R)
+        plan = ExchangePlan(send_rows=[int(v) for v in C[me]], recv_rows=[int(v) for v in C[:, me]],
+                            recv_expert_counts=ca[:, me, :])
+        out_rows = ops.experts(recv, receive_expert_ids(plan, x.device), self._local_lanes())
+        # 5. outputs -> the senders' return buffers, in their dispatch order
+        recv_seg = np.concatenate([[0], np.cumsum(C[:, me])])
+        back_at = C[:, :me].sum(axis=1)
+        peer.send("back", out_rows, None, 1, recv_seg, back_at)
+        peer.barrier()
+        # 6. combine with the routing weights and the shared output
+        if self.side is not None:
+            torch.cuda.current_stream(ops.device).wait_stream(self.side)
+            if shared is not None:
+                shared.record_stream(torch.cuda.current_stream(ops.device))
+        update = ops.combine(peer.view("back", T * k), r["rank"], r["routing_weights"], shared)
+        return update, {"send_rows": plan.send_rows, "recv_rows": plan.recv_rows}
 
     def _exchange_dedup(self, x: Tensor, r: dict, shared: Tensor | None) -> tuple[Tensor, dict]:
         """The exchange with token rows sent once per destination rank.
@@ -449,5 +629,5 @@ class ExpertParallelMixer:
     __call__ = forward
 
 
-__all__ = ["CudaOps", "ExchangePlan", "ExpertParallelMixer", "exchange_plan", "experts_per_rank",
+__all__ = ["CudaOps", "ExchangePlan", "ExpertParallelMixer", "PeerExchange", "exchange_plan", "experts_per_rank",
            "receive_expert_ids"]

@@ -25,7 +25,8 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank: int, world: int, port: int, mxfp8: bool, out_dir: str, dedup: bool = False) -> None:
+def _worker(rank: int, world: int, port: int, mxfp8: bool, out_dir: str, dedup: bool = False,
+            exchange: str | None = None) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
@@ -44,11 +45,13 @@ def _worker(rank: int, world: int, port: int, mxfp8: bool, out_dir: str, dedup: 
             set_mxfp8_lanes(mixer, mxfp8_experts(config.num_experts, 0.25))
         x = torch.randn(8, 512, CFG["d_model"], generator=torch.Generator().manual_seed(1 + rank))
         x = x.to(torch.bfloat16).to(device)
-        ep = ExpertParallelMixer(mixer, dedup=dedup)
+        ep = ExpertParallelMixer(mixer, dedup=dedup, exchange=exchange)
         with torch.no_grad():
-            got = ep(x)
+            first = ep(x)
+            got = ep(x)  # buffers reused
             want = mixer(x)
         torch.cuda.synchronize()
+        ep.close()
         res = {
             "update_equal": torch.equal(got["update"], want.update),
             "ids_equal": torch.equal(got["expert_ids"], want.metrics["expert_ids"]),
@@ -56,6 +59,7 @@ def _worker(rank: int, world: int, port: int, mxfp8: bool, out_dir: str, dedup: 
             "max_diff": float((got["update"].float() - want.update.float()).abs().max()),
             "within_tol": bool(((got["update"].float() - want.update.float()).abs()
                                 <= 1e-2 + 2e-2 * want.update.float().abs()).all()),
+            "repeat_equal": torch.equal(first["update"], got["update"]),
             "send": got["send_rows"], "recv": got["recv_rows"], "status": mixer.device_status(),
         }
         torch.save(res, os.path.join(out_dir, f"rank{rank}.pt"))
@@ -63,17 +67,19 @@ def _worker(rank: int, world: int, port: int, mxfp8: bool, out_dir: str, dedup: 
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
 @pytest.mark.parametrize("mxfp8", [False, True])
-def test_expert_parallel_matches_single_gpu(tmp_path, mxfp8):
+def test_expert_parallel_matches_single_gpu(tmp_path, mxfp8, exchange):
     world = 2
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    mp.spawn(_worker, args=(world, _free_port(), mxfp8, str(tmp_path)), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), mxfp8, str(tmp_path), False, exchange), nprocs=world, join=True)
     res = [torch.load(tmp_path / f"rank{r}.pt") for r in range(world)]
     for r in res:
         assert r["status"] == 0
         assert r["ids_equal"] and r["weights_equal"]
         assert r["update_equal"], r["max_diff"]
+        assert r["repeat_equal"]
     assert res[0]["send"][1] == res[1]["recv"][0] and res[1]["send"][0] == res[0]["recv"][1]
     assert np.sum(res[0]["send"]) == 8 * 512 * CFG["active_experts"]
 
