@@ -232,6 +232,13 @@ int spx_gather_rows(const uint16_t* src, int64_t ld_src, const int32_t* index, i
  * num_experts = the local experts, shared_dim = 0. */
 int spx_experts_forward(const spx_layer_dims* dims, const spx_packed_weights* weights, const uint16_t* rows,
                         const int64_t* row_expert, uint16_t* out_rows, void* workspace, void* stream);
+/* With out_rows NULL, spx_experts_forward leaves the outputs in dispatch
+ * order inside the workspace: sorted_rows [R, d] and row_rank [R] (the
+ * dispatch position of input row i), until the workspace's next use -- so a
+ * caller can move them elsewhere (spx_rows_to_peers with index = row_rank)
+ * in one pass. */
+int spx_experts_sorted_rows(const spx_layer_dims* dims, void* workspace, const uint16_t** sorted_rows,
+                            const int32_t** row_rank);
 
 /* Shared SwiGLU of `hidden` [T, d] into shared_out [T, d] (dims->shared_dim > 0). */
 int spx_shared_forward(const spx_layer_dims* dims, const spx_packed_weights* weights, const uint16_t* hidden,

@@ -1438,10 +1438,11 @@ int spx_experts_forward(const spx_layer_dims* dims, const spx_packed_weights* w,
   Shape s;
   if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
   if (dims->top_k != 1) return SPX_ERR_INVALID_ARG;  // one expert per row
-  if (rows == nullptr || row_expert == nullptr || out_rows == nullptr) return SPX_ERR_INVALID_ARG;
+  if (rows == nullptr || row_expert == nullptr) return SPX_ERR_INVALID_ARG;
   if (workspace == nullptr) return SPX_ERR_WORKSPACE;
   if (int rc = check_layer_weights(s, dims, w, false, true, false); rc != SPX_OK) return rc;
-  if (!aligned16(rows) || !aligned16(out_rows) || !aligned16(workspace)) return SPX_ERR_ALIGNMENT;
+  if (!aligned16(rows) || (out_rows != nullptr && !aligned16(out_rows)) || !aligned16(workspace))
+    return SPX_ERR_ALIGNMENT;
   const Layout L = make_layout(s);
   const Ctx c{s, L, workspace, static_cast<cudaStream_t>(stream), at<int>(workspace, L.small), nullptr};
   int rc = SPX_OK;
@@ -1461,8 +1462,20 @@ int spx_experts_forward(const spx_layer_dims* dims, const spx_packed_weights* w,
   }
   if ((rc = launch_dispatch(da, c.st)) != SPX_OK) return rc;
   if ((rc = stage_experts(c, w, rows, xa, da)) != SPX_OK) return rc;
+  if (out_rows == nullptr) return SPX_OK;  // rows stay in dispatch order (spx_experts_sorted_rows)
   // back to the input row order (one "slot" per row)
   return launch_combine(at<uint16_t>(workspace, L.y), da.rank, nullptr, nullptr, s.T, s.d, 1, out_rows, c.st);
+}
+
+int spx_experts_sorted_rows(const spx_layer_dims* dims, void* workspace, const uint16_t** sorted_rows,
+                            const int32_t** row_rank) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (workspace == nullptr || sorted_rows == nullptr || row_rank == nullptr) return SPX_ERR_INVALID_ARG;
+  const Layout L = make_layout(s);
+  *sorted_rows = at<uint16_t>(workspace, L.y);
+  *row_rank = at<int32_t>(workspace, L.rank);
+  return SPX_OK;
 }
 
 int spx_shared_forward(const spx_layer_dims* dims, const spx_packed_weights* w, const uint16_t* hidden,

@@ -238,18 +238,31 @@ class CudaOps:
                                        out.data_ptr(), out.stride(0), stream), "spx_gather_rows")
         return out
 
-    def experts(self, rows: Tensor, row_expert: Tensor, lanes: Tensor | None) -> Tensor:
-        out = torch.empty_like(rows)
+    def experts(self, rows: Tensor, row_expert: Tensor, lanes: Tensor | None, *,
+                sorted_out: bool = False) -> Tensor | tuple[Tensor, Tensor]:
+        """Expert outputs of ``rows`` in input order, or (``sorted_out``) the
+        outputs in dispatch order with each input row's dispatch position, views
+        of the workspace valid until its next use."""
+
         R = rows.shape[0]
         if R == 0:
-            return out
+            empty = torch.empty_like(rows)
+            return (empty, torch.empty(0, dtype=torch.int32, device=rows.device)) if sorted_out else empty
+        out = None if sorted_out else torch.empty_like(rows)
         lib = _lib.load()
         dims = self._local_dims(R)
         ws = self._workspace(dims, "experts")
         stream = torch.cuda.current_stream(rows.device).cuda_stream
         _lib.check(lib.spx_experts_forward(dims, self._weights(R, R, lanes), rows.data_ptr(), row_expert.data_ptr(),
-                                           out.data_ptr(), ws.data_ptr(), stream), "spx_experts_forward")
-        return out
+                                           _lib.ptr(out), ws.data_ptr(), stream), "spx_experts_forward")
+        if not sorted_out:
+            return out
+        y, rank = _lib.ctypes.c_void_p(), _lib.ctypes.c_void_p()
+        _lib.check(lib.spx_experts_sorted_rows(dims, ws.data_ptr(), _lib.ctypes.byref(y), _lib.ctypes.byref(rank)),
+                   "spx_experts_sorted_rows")
+        yv = torch.as_tensor(_RawRows(y.value, R, self.d), device=rows.device).view(torch.bfloat16)
+        rv = torch.as_tensor(_RawRows(rank.value, R, 0, "<i4"), device=rows.device)
+        return yv, rv
 
     def shared(self, x: Tensor) -> Tensor | None:
         if self.mixer.shared is None:
@@ -280,10 +293,11 @@ class CudaOps:
 
 
 class _RawRows:
-    """A raw device allocation seen by torch as an int16 matrix (zero copy)."""
+    """A raw device allocation seen by torch as a matrix (zero copy)."""
 
-    def __init__(self, ptr: int, rows: int, cols: int):
-        self.__cuda_array_interface__ = {"shape": (rows, cols), "typestr": "<i2", "data": (ptr, False),
+    def __init__(self, ptr: int, rows: int, cols: int, typestr: str = "<i2"):
+        shape = (rows, cols) if cols else (rows,)
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False),
                                          "version": 3, "strides": None}
 
 
@@ -532,11 +546,12 @@ class ExpertParallelMixer:
         recv = peer.view("recv", R)
         plan = ExchangePlan(send_rows=[int(v) for v in C[me]], recv_rows=[int(v) for v in C[:, me]],
                             recv_expert_counts=ca[:, me, :])
-        out_rows = ops.experts(recv, receive_expert_ids(plan, x.device), self._local_lanes())
-        # 5. outputs -> the senders' return buffers, in their dispatch order
+        y_sorted, y_rank = ops.experts(recv, receive_expert_ids(plan, x.device), self._local_lanes(), sorted_out=True)
+        # 5. outputs -> the senders' return buffers, in their dispatch order: received
+        #    row i is sorted row y_rank[i], read and sent in one pass
         recv_seg = np.concatenate([[0], np.cumsum(C[:, me])])
         back_at = C[:, :me].sum(axis=1)
-        peer.send("back", out_rows, None, 1, recv_seg, back_at)
+        peer.send("back", y_sorted, y_rank if R else None, 1, recv_seg, back_at)
         peer.barrier()
         # 6. combine with the routing weights and the shared output
         if self.side is not None:
