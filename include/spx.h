@@ -239,6 +239,12 @@ int spx_experts_forward(const spx_layer_dims* dims, const spx_packed_weights* we
  * in one pass. */
 int spx_experts_sorted_rows(const spx_layer_dims* dims, void* workspace, const uint16_t** sorted_rows,
                             const int32_t** row_rank);
+/* spx_experts_forward whose down-projection epilogue stores output row i
+ * straight to row_out[i] (device array [R] of row pointers, each possibly in
+ * a peer GPU's memory): the expert GEMM and the return exchange in one
+ * kernel, the stores of a tile leaving as its epilogue runs. */
+int spx_experts_forward_to(const spx_layer_dims* dims, const spx_packed_weights* weights, const uint16_t* rows,
+                           const int64_t* row_expert, uint16_t* const* row_out, void* workspace, void* stream);
 
 /* Shared SwiGLU of `hidden` [T, d] into shared_out [T, d] (dims->shared_dim > 0). */
 int spx_shared_forward(const spx_layer_dims* dims, const spx_packed_weights* weights, const uint16_t* hidden,

@@ -65,6 +65,7 @@ EXPORTED = (
     "spx_ipc_buffer_free",
     "spx_rows_to_peers",
     "spx_experts_sorted_rows",
+    "spx_experts_forward_to",
 )
 
 ABI_VERSION = 6
@@ -258,6 +259,7 @@ def load() -> ctypes.CDLL:
         "spx_ipc_buffer_close": (ctypes.c_int, [_vp]),
         "spx_ipc_buffer_free": (ctypes.c_int, [_vp]),
         "spx_experts_sorted_rows": (ctypes.c_int, [P(LayerDims), _vp, P(_vp), P(_vp)]),
+        "spx_experts_forward_to": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, _vp, _vp, _vp, _vp]),
         "spx_rows_to_peers": (
             ctypes.c_int,
             [_vp, ctypes.c_int64, _vp, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, _vp, _vp, _vp, ctypes.c_int64,

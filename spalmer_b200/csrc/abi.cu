@@ -357,6 +357,8 @@ struct ExpertPass {
   const int* num_tiles_mx;
   int max_ctas;  // persistent grid cap of the GEMMs (0 = every SM)
   const float* nv_amax_w;  // NVFP4 lane: weight amax [groups][4] (gate, up, down, unused)
+  uint16_t* const* row_out = nullptr;  // GEMM2 rows to row_out[row_out_idx[p]] instead of Y
+  const int* row_out_idx = nullptr;
 };
 
 // NVFP4 lane input: each expert's rows in dispatch order as E2M1 with UE4M3
@@ -492,6 +494,9 @@ int stage_expert_gemms(const Ctx& c, const uint16_t* xa, const int* src_row, con
     g.tma_store = (s.d % 64) == 0;  // whole 64-column boxes; other widths use plain stores
     if (g.tma_store && (rc = encode_2d(&g.tma_out, y, s.P, s.d, s.d, 32)) != SPX_OK) return rc;
     g.pos_weight = sorted_w;
+    g.row_out = p.row_out;
+    g.row_out_idx = p.row_out_idx;
+    if (p.row_out != nullptr) g.tma_store = 0;
     if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn_d, c.st)) != SPX_OK) return rc;
   }
   if (mx) {
@@ -511,6 +516,9 @@ int stage_expert_gemms(const Ctx& c, const uint16_t* xa, const int* src_row, con
     g.tma_store = (s.d % 64) == 0;
     if (g.tma_store && (rc = encode_2d(&g.tma_out, y, s.P, s.d, s.d, 32)) != SPX_OK) return rc;
     g.pos_weight = sorted_w;
+    g.row_out = p.row_out;
+    g.row_out_idx = p.row_out_idx;
+    if (p.row_out != nullptr) g.tma_store = 0;
     if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn2m, c.st, true)) != SPX_OK) return rc;
   }
   if (nv) {
@@ -530,6 +538,9 @@ int stage_expert_gemms(const Ctx& c, const uint16_t* xa, const int* src_row, con
     g.tma_store = (s.d % 64) == 0;
     if (g.tma_store && (rc = encode_2d(&g.tma_out, y, s.P, s.d, s.d, 32)) != SPX_OK) return rc;
     g.pos_weight = sorted_w;
+    g.row_out = p.row_out;
+    g.row_out_idx = p.row_out_idx;
+    if (p.row_out != nullptr) g.tma_store = 0;
     g.nv_amax_a = nv_amax_h;
     g.nv_amax_b = p.nv_amax_w;
     g.nv_b_stride = 4;
@@ -1465,6 +1476,46 @@ int spx_experts_forward(const spx_layer_dims* dims, const spx_packed_weights* w,
   if (out_rows == nullptr) return SPX_OK;  // rows stay in dispatch order (spx_experts_sorted_rows)
   // back to the input row order (one "slot" per row)
   return launch_combine(at<uint16_t>(workspace, L.y), da.rank, nullptr, nullptr, s.T, s.d, 1, out_rows, c.st);
+}
+
+int spx_experts_forward_to(const spx_layer_dims* dims, const spx_packed_weights* w, const uint16_t* rows,
+                           const int64_t* row_expert, uint16_t* const* row_out, void* workspace, void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (dims->top_k != 1) return SPX_ERR_INVALID_ARG;
+  if (rows == nullptr || row_expert == nullptr || row_out == nullptr) return SPX_ERR_INVALID_ARG;
+  if (workspace == nullptr) return SPX_ERR_WORKSPACE;
+  if (int rc = check_layer_weights(s, dims, w, false, true, false); rc != SPX_OK) return rc;
+  if (!aligned16(rows) || !aligned16(workspace)) return SPX_ERR_ALIGNMENT;
+  const Layout L = make_layout(s);
+  const Ctx c{s, L, workspace, static_cast<cudaStream_t>(stream), at<int>(workspace, L.small), nullptr};
+  int rc = SPX_OK;
+  const uint16_t* xa = nullptr;
+  if ((rc = stage_pad(c, rows, &xa)) != SPX_OK) return rc;
+  DispatchArgs da = dispatch_args(s, row_expert, nullptr, nullptr, workspace, L);
+  da.lb_blocks = 0;
+  da.utilization = at<float>(workspace, L.util);
+  da.group_stats = at<long long>(workspace, L.stats);
+  da.group_ratios = at<float>(workspace, L.ratios);
+  da.pair_weights = nullptr;
+  da.sorted_weights = nullptr;
+  if (s.mx && w->expert_lane_mxfp8 != nullptr) {
+    da.lane_mx = w->expert_lane_mxfp8;
+    da.tiles_mx = at<int4>(workspace, L.tiles_mx);
+    da.num_tiles_mx = at<int>(workspace, L.small) + 3;
+  }
+  if ((rc = launch_dispatch(da, c.st)) != SPX_OK) return rc;
+  const bool mx = da.lane_mx != nullptr;
+  if (mx) {
+    rc = s.nv ? stage_quantize_nv_x(c, rows, 0, da) : stage_quantize_x(c, rows, 0);
+    if (rc != SPX_OK) return rc;
+  }
+  ExpertPass p{w->expert_w1, w->expert_w2, w->expert_w1_mx, w->expert_w1_mx_scales, w->expert_w2_mx,
+               w->expert_w2_mx_scales, s.E, da.tiles, da.num_tiles, mx ? da.tiles_mx : nullptr,
+               mx ? da.num_tiles_mx : nullptr, 0, w->expert_nvfp4_amax};
+  p.row_out = row_out;
+  p.row_out_idx = da.src_row;
+  return stage_expert_gemms(c, xa, da.src_row, da.sorted_weights, p);
 }
 
 int spx_experts_sorted_rows(const spx_layer_dims* dims, void* workspace, const uint16_t** sorted_rows,

@@ -226,7 +226,7 @@ __device__ __forceinline__ void run_epilogue_rows(const GemmArgs& a, uint32_t ta
 #pragma unroll
     for (int c = 0; c < 64; c += 16) stage_put16(buf, lane, c, &hw[c / 2]);
     const int gcol0 = n0 + s0;
-    if (wrows >= 32 && a.tma_store) {
+    if (wrows >= 32 && a.tma_store && a.row_out == nullptr) {
       fence_proxy_async_smem();  // generic-proxy staging writes -> TMA reads
       __syncwarp();
       if (lane == 0) {
@@ -244,7 +244,9 @@ __device__ __forceinline__ void run_epilogue_rows(const GemmArgs& a, uint32_t ta
         const int n = min(8, valid - j * 8);
         if (ri < wrows && n > 0) {
           const uint4 val = *reinterpret_cast<const uint4*>(buf + stage_off(ri, j));
-          put8(out + static_cast<int64_t>(row0 + quad * 32 + ri) * a.ldo + gcol0 + j * 8, val, n);
+          const int p = row0 + quad * 32 + ri;
+          uint16_t* dst = a.row_out != nullptr ? a.row_out[a.row_out_idx[p]] : out + static_cast<int64_t>(p) * a.ldo;
+          put8(dst + gcol0 + j * 8, val, n);
         }
       }
       committed = false;

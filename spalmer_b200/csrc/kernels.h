@@ -142,6 +142,11 @@ struct GemmArgs {
   uint16_t* comb_res_out;    //   comb_res_out = bf16(residual + update) (out may then be null)
   int64_t ldy;
   int max_ctas;              // persistent grid cap (0 = every SM): leaves SMs to concurrent work
+  // kEpiScatter to other buffers: the row of sorted position p goes to
+  // row_out[row_out_idx[p]] (a row pointer, possibly a peer GPU's) instead of
+  // out + p * ldo; plain stores (no TMA store).
+  uint16_t* const* row_out;
+  const int* row_out_idx;
   // NVFP4 lane (block-scaled kernel with E2M1 operands): the epilogue scales
   // the accumulator by the two per-tensor scales, amax / 2688 each, of A
   // (nv_amax_a[expert], the tile's .w; 0 without a tile table) and B

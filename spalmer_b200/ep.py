@@ -238,6 +238,21 @@ class CudaOps:
                                        out.data_ptr(), out.stride(0), stream), "spx_gather_rows")
         return out
 
+    def experts_to(self, rows: Tensor, row_expert: Tensor, lanes: Tensor | None, row_out: Tensor) -> None:
+        """Expert outputs of ``rows``, output row i stored by the down
+        projection's epilogue at the row pointer ``row_out[i]`` (int64, device;
+        a peer GPU's memory included)."""
+
+        R = rows.shape[0]
+        if R == 0:
+            return
+        lib = _lib.load()
+        dims = self._local_dims(R)
+        ws = self._workspace(dims, "experts")
+        stream = torch.cuda.current_stream(rows.device).cuda_stream
+        _lib.check(lib.spx_experts_forward_to(dims, self._weights(R, R, lanes), rows.data_ptr(), row_expert.data_ptr(),
+                                              row_out.data_ptr(), ws.data_ptr(), stream), "spx_experts_forward_to")
+
     def experts(self, rows: Tensor, row_expert: Tensor, lanes: Tensor | None, *,
                 sorted_out: bool = False) -> Tensor | tuple[Tensor, Tensor]:
         """Expert outputs of ``rows`` in input order, or (``sorted_out``) the
@@ -546,12 +561,17 @@ class ExpertParallelMixer:
         recv = peer.view("recv", R)
         plan = ExchangePlan(send_rows=[int(v) for v in C[me]], recv_rows=[int(v) for v in C[:, me]],
                             recv_expert_counts=ca[:, me, :])
-        y_sorted, y_rank = ops.experts(recv, receive_expert_ids(plan, x.device), self._local_lanes(), sorted_out=True)
-        # 5. outputs -> the senders' return buffers, in their dispatch order: received
-        #    row i is sorted row y_rank[i], read and sent in one pass
+        # 5. the down projection's epilogue stores received row i's output straight
+        #    into its sender's return buffer, at the row of the sender's dispatch order
         recv_seg = np.concatenate([[0], np.cumsum(C[:, me])])
         back_at = C[:, :me].sum(axis=1)
-        peer.send("back", y_sorted, y_rank if R else None, 1, recv_seg, back_at)
+        if R:
+            dev = x.device
+            src = torch.repeat_interleave(torch.arange(G, device=dev),
+                                          torch.from_numpy(np.ascontiguousarray(C[:, me])).to(dev))
+            rows_at = torch.from_numpy(back_at - recv_seg[:-1]).to(dev)[src] + torch.arange(R, device=dev)
+            row_out = peer.ptr_tables["back"][src] + rows_at * (d * 2)
+            ops.experts_to(recv, receive_expert_ids(plan, dev), self._local_lanes(), row_out)
         peer.barrier()
         # 6. combine with the routing weights and the shared output
         if self.side is not None:
