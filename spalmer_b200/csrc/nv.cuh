@@ -32,15 +32,28 @@ constexpr float kNvScaleMin = 0.015625f; // 2^-6, the smallest normal E4M3
 // rint(|v|) + 2 (4..6), from 4 it is rint(|v| / 2) + 4 (6..7).  The ties of
 // the grid (0.25, 0.75, ..., 5) are the ties of these roundings, and the
 // range boundaries 2 and 4 are grid points.
+// Round-to-nearest-even of 0 <= x < 2^22 to an unsigned integer.  On the
+// device: adding 1.5 * 2^23 lands x in a binade whose ulp is 1, so the float
+// add itself rounds x to an integer (to even on ties) and the integer sits in
+// the low mantissa bits -- one add instead of a round and a conversion on the
+// special-function pipe, which the quantisers otherwise saturate.
+__host__ __device__ __forceinline__ uint32_t nv_rne_small(float x) {
+#if defined(__CUDA_ARCH__)
+  return __float_as_uint(x + 12582912.0f) - 0x4B400000u;
+#else
+  return static_cast<uint32_t>(rintf(x));
+#endif
+}
+
 __host__ __device__ __forceinline__ uint32_t nv_e2m1(float v) {
   const float m = fminf(fabsf(v), 6.0f);
   uint32_t c;
   if (m < 2.0f)
-    c = static_cast<uint32_t>(rintf(2.0f * m));
+    c = nv_rne_small(2.0f * m);
   else if (m < 4.0f)
-    c = static_cast<uint32_t>(rintf(m)) + 2u;
+    c = nv_rne_small(m) + 2u;
   else
-    c = static_cast<uint32_t>(rintf(0.5f * m)) + 4u;
+    c = nv_rne_small(0.5f * m) + 4u;
   return c | (signbit(v) ? 8u : 0u);
 }
 
@@ -72,9 +85,25 @@ __device__ __forceinline__ uint32_t nv_quantize16(const float (&v)[16], float pt
     }
     return static_cast<uint32_t>(sb);
   }
+  // The code of v is nv_e2m1(RN(v / total)): it steps up where RN(v / total)
+  // passes a rounding threshold of the E2M1 grid, i.e. where |v| passes that
+  // threshold widened by half an ulp, times total.  Those seven boundaries
+  // are exact in double (a 25-bit widened threshold times a 24-bit float) and
+  // rounded to float toward the side that keeps the comparison exact, once
+  // per block; each element then costs seven float compares instead of a
+  // division.  Steps: above 0.25 (ties down), from 0.75 (ties up), above 1.25,
+  // from 1.75, above 2.5, from 3.5, above 5 -- ties go to the even code.
+  const double t = total;
+  const float b0 = __double2float_rd((0.25 + 0x1p-26) * t), b1 = __double2float_ru((0.75 - 0x1p-25) * t);
+  const float b2 = __double2float_rd((1.25 + 0x1p-24) * t), b3 = __double2float_ru((1.75 - 0x1p-24) * t);
+  const float b4 = __double2float_rd((2.5 + 0x1p-23) * t), b5 = __double2float_ru((3.5 - 0x1p-23) * t);
+  const float b6 = __double2float_rd((5.0 + 0x1p-22) * t);
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    const uint32_t c = nv_e2m1(fminf(fmaxf(v[j] / total, -6.0f), 6.0f));
+    const float a = fabsf(v[j]);
+    uint32_t c = (a > b0 ? 1u : 0u) + (a >= b1 ? 1u : 0u) + (a > b2 ? 1u : 0u) + (a >= b3 ? 1u : 0u) +
+                 (a > b4 ? 1u : 0u) + (a >= b5 ? 1u : 0u) + (a > b6 ? 1u : 0u);
+    c |= signbit(v[j]) ? 8u : 0u;
     if (j < 8)
       w0 |= c << (4 * j);
     else
