@@ -245,6 +245,21 @@ int spx_experts_sorted_rows(const spx_layer_dims* dims, void* workspace, const u
  * kernel, the stores of a tile leaving as its epilogue runs. */
 int spx_experts_forward_to(const spx_layer_dims* dims, const spx_packed_weights* weights, const uint16_t* rows,
                            const int64_t* row_expert, uint16_t* const* row_out, void* workspace, void* stream);
+/* spx_experts_forward_to whose gate/up GEMM reads input row i from
+ * row_ptrs[i] (device array [R] of row pointers, each possibly in a peer
+ * GPU's memory): the dispatch exchange folded into the GEMM's row gather.
+ * BF16 experts only, d_model a multiple of 64 (SPX_ERR_UNSUPPORTED otherwise). */
+int spx_experts_forward_rows(const spx_layer_dims* dims, const spx_packed_weights* weights,
+                             const uint16_t* const* row_ptrs, const int64_t* row_expert, uint16_t* const* row_out,
+                             void* workspace, void* stream);
+/* Row pointers of the rows a rank receives, in its senders' memory: received
+ * row i from sender g (recv_seg[g] <= i < recv_seg[g+1]) is g's pair at
+ * dispatch position send_at[g] + i - recv_seg[g], whose token is
+ * sender_order[g][pos] / top_k; row_ptrs[i] = sender_rows[g] + token * ld_rows.
+ * All arrays are device arrays ([groups], [groups+1], [rows]). */
+int spx_peer_row_pointers(const int32_t* const* sender_order, const int64_t* send_at, const int64_t* recv_seg,
+                          int32_t groups, int32_t top_k, const uint16_t* const* sender_rows, int64_t ld_rows,
+                          int64_t rows, const uint16_t** row_ptrs, void* stream);
 
 /* Shared SwiGLU of `hidden` [T, d] into shared_out [T, d] (dims->shared_dim > 0). */
 int spx_shared_forward(const spx_layer_dims* dims, const spx_packed_weights* weights, const uint16_t* hidden,

@@ -66,6 +66,8 @@ EXPORTED = (
     "spx_rows_to_peers",
     "spx_experts_sorted_rows",
     "spx_experts_forward_to",
+    "spx_experts_forward_rows",
+    "spx_peer_row_pointers",
 )
 
 ABI_VERSION = 6
@@ -260,6 +262,11 @@ def load() -> ctypes.CDLL:
         "spx_ipc_buffer_free": (ctypes.c_int, [_vp]),
         "spx_experts_sorted_rows": (ctypes.c_int, [P(LayerDims), _vp, P(_vp), P(_vp)]),
         "spx_experts_forward_to": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, _vp, _vp, _vp, _vp]),
+        "spx_experts_forward_rows": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, _vp, _vp, _vp, _vp]),
+        "spx_peer_row_pointers": (
+            ctypes.c_int,
+            [_vp, _vp, _vp, ctypes.c_int32, ctypes.c_int32, _vp, ctypes.c_int64, ctypes.c_int64, _vp, _vp],
+        ),
         "spx_rows_to_peers": (
             ctypes.c_int,
             [_vp, ctypes.c_int64, _vp, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, _vp, _vp, _vp, ctypes.c_int64,

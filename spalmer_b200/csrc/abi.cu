@@ -359,6 +359,7 @@ struct ExpertPass {
   const float* nv_amax_w;  // NVFP4 lane: weight amax [groups][4] (gate, up, down, unused)
   uint16_t* const* row_out = nullptr;  // GEMM2 rows to row_out[row_out_idx[p]] instead of Y
   const int* row_out_idx = nullptr;
+  const uint8_t* const* a_rows = nullptr;  // BF16 GEMM1 rows through one pointer per source row
 };
 
 // NVFP4 lane input: each expert's rows in dispatch order as E2M1 with UE4M3
@@ -416,6 +417,7 @@ int stage_expert_gemms(const Ctx& c, const uint16_t* xa, const int* src_row, con
     g.gather_idx = src_row;
     g.a_base = reinterpret_cast<const uint8_t*>(xa);
     g.lda = 2 * static_cast<int64_t>(s.kd);
+    g.a_rows = p.a_rows;
     g.tiles = p.tiles;
     g.num_tiles = p.num_tiles;
     g.chunk = s.c;
@@ -1516,6 +1518,46 @@ int spx_experts_forward_to(const spx_layer_dims* dims, const spx_packed_weights*
   p.row_out = row_out;
   p.row_out_idx = da.src_row;
   return stage_expert_gemms(c, xa, da.src_row, da.sorted_weights, p);
+}
+
+int spx_experts_forward_rows(const spx_layer_dims* dims, const spx_packed_weights* w, const uint16_t* const* row_ptrs,
+                             const int64_t* row_expert, uint16_t* const* row_out, void* workspace, void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (dims->top_k != 1 || s.kd != s.d) return SPX_ERR_UNSUPPORTED;  // rows used as they are: d % 64 == 0
+  if (row_ptrs == nullptr || row_expert == nullptr || row_out == nullptr) return SPX_ERR_INVALID_ARG;
+  if (workspace == nullptr) return SPX_ERR_WORKSPACE;
+  if (w == nullptr || w->expert_lane_mxfp8 != nullptr) return SPX_ERR_UNSUPPORTED;  // BF16 experts only
+  if (int rc = check_layer_weights(s, dims, w, false, true, false); rc != SPX_OK) return rc;
+  if (!aligned16(workspace)) return SPX_ERR_ALIGNMENT;
+  const Layout L = make_layout(s);
+  const Ctx c{s, L, workspace, static_cast<cudaStream_t>(stream), at<int>(workspace, L.small), nullptr};
+  DispatchArgs da = dispatch_args(s, row_expert, nullptr, nullptr, workspace, L);
+  da.lb_blocks = 0;
+  da.utilization = at<float>(workspace, L.util);
+  da.group_stats = at<long long>(workspace, L.stats);
+  da.group_ratios = at<float>(workspace, L.ratios);
+  da.pair_weights = nullptr;
+  da.sorted_weights = nullptr;
+  if (int rc = launch_dispatch(da, c.st); rc != SPX_OK) return rc;
+  ExpertPass p{w->expert_w1, w->expert_w2, nullptr, nullptr, nullptr, nullptr, s.E, da.tiles, da.num_tiles,
+               nullptr, nullptr, 0, nullptr};
+  p.row_out = row_out;
+  p.row_out_idx = da.src_row;
+  p.a_rows = reinterpret_cast<const uint8_t* const*>(row_ptrs);
+  return stage_expert_gemms(c, nullptr, da.src_row, da.sorted_weights, p);
+}
+
+int spx_peer_row_pointers(const int32_t* const* sender_order, const int64_t* send_at, const int64_t* recv_seg,
+                          int32_t groups, int32_t top_k, const uint16_t* const* sender_rows, int64_t ld_rows,
+                          int64_t rows, const uint16_t** row_ptrs, void* stream) {
+  if (groups < 1 || top_k < 1 || rows < 0 || ld_rows < 1) return SPX_ERR_INVALID_ARG;
+  if (rows == 0) return SPX_OK;
+  if (sender_order == nullptr || send_at == nullptr || recv_seg == nullptr || sender_rows == nullptr ||
+      row_ptrs == nullptr)
+    return SPX_ERR_INVALID_ARG;
+  return launch_peer_row_pointers(sender_order, send_at, recv_seg, groups, top_k, sender_rows, ld_rows, rows,
+                                  row_ptrs, static_cast<cudaStream_t>(stream));
 }
 
 int spx_experts_sorted_rows(const spx_layer_dims* dims, void* workspace, const uint16_t** sorted_rows,

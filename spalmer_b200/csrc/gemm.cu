@@ -531,12 +531,23 @@ __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa,
       }
       if (gather) {
         const uint32_t dst0 = smem_u32(sa + s * a_bytes);
-        const uint8_t* col = a.a_base + kb * 128 + chunk * 16;
+        if (a.a_rows != nullptr) {
+          // rows anywhere (a peer GPU's memory included), one pointer per source row
+          const int off = kb * 128 + chunk * 16;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int rr = 4 * i + (lane >> 3);
-          const uint32_t dst = dst0 + (rr >> 3) * 1024 + (rr & 7) * 128 + ((chunk ^ (rr & 7)) << 4);
-          cp_async16(dst, col + static_cast<int64_t>(src[i]) * a.lda);
+          for (int i = 0; i < 32; ++i) {
+            const int rr = 4 * i + (lane >> 3);
+            const uint32_t dst = dst0 + (rr >> 3) * 1024 + (rr & 7) * 128 + ((chunk ^ (rr & 7)) << 4);
+            cp_async16(dst, a.a_rows[src[i]] + off);
+          }
+        } else {
+          const uint8_t* col = a.a_base + kb * 128 + chunk * 16;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int rr = 4 * i + (lane >> 3);
+            const uint32_t dst = dst0 + (rr >> 3) * 1024 + (rr & 7) * 128 + ((chunk ^ (rr & 7)) << 4);
+            cp_async16(dst, col + static_cast<int64_t>(src[i]) * a.lda);
+          }
         }
       }
       if constexpr (MX && NV) {

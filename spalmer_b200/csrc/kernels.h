@@ -118,6 +118,7 @@ struct GemmArgs {
   const int* gather_idx;
   const uint8_t* a_base;     // gather: A rows (row stride lda bytes)
   int64_t lda;
+  const uint8_t* const* a_rows;  // gather: or one pointer per source row (rows of kd BF16), when not null
   // MXFP8 lane (block-scaled kernel only)
   const uint8_t* sfa;        // A scale bytes [A rows, ld_sfa] row-major (row = gathered source row)
   int64_t ld_sfa;            // bytes per row, multiple of 4
@@ -240,6 +241,11 @@ int launch_page_tiles(const PageTilesArgs& a, cudaStream_t stream);
 int launch_rows_to_peers(const uint16_t* src, int64_t ld_src, const int* index, int index_div, int64_t rows, int d,
                          const int64_t* seg, uint16_t* const* dst, const int64_t* dst_row, int64_t ld_dst,
                          int groups, cudaStream_t stream);
+
+// Row pointers of received rows in their senders' buffers (peer.cu).
+int launch_peer_row_pointers(const int* const* order, const int64_t* send_at, const int64_t* recv_seg, int groups,
+                             int top_k, const uint16_t* const* src_rows, int64_t ld, int64_t rows,
+                             const uint16_t** out, cudaStream_t stream);
 
 // ---- NVFP4 (nvfp4.cu).  Quantised rows: E2M1 [rows, kp/2] bytes, UE4M3
 // scales [rows, kp/16] bytes (kp a multiple of 256; K beyond `cols` is zero).

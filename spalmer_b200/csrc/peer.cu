@@ -55,4 +55,33 @@ int launch_rows_to_peers(const uint16_t* src, int64_t ld_src, const int* index, 
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 
+// Row pointers of the rows a rank receives, taken from its senders' own
+// buffers: received row i from sender s (recv_seg[s] <= i < recv_seg[s+1])
+// is s's pair at dispatch position send_at[s] + i - recv_seg[s], whose token
+// is order_s[pos] / top_k and whose row is rows_s + token * ld.
+__global__ void peer_row_pointers_kernel(const int* const* __restrict__ order, const int64_t* __restrict__ send_at,
+                                         const int64_t* __restrict__ recv_seg, int groups, int top_k,
+                                         const uint16_t* const* __restrict__ src_rows, int64_t ld, int64_t rows,
+                                         const uint16_t** __restrict__ out) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < rows;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int g = 0;
+    while (g + 1 < groups && i >= recv_seg[g + 1]) ++g;
+    const int64_t pos = send_at[g] + (i - recv_seg[g]);
+    const int64_t token = order[g][pos] / top_k;
+    out[i] = src_rows[g] + token * ld;
+  }
+}
+
+int launch_peer_row_pointers(const int* const* order, const int64_t* send_at, const int64_t* recv_seg, int groups,
+                             int top_k, const uint16_t* const* src_rows, int64_t ld, int64_t rows,
+                             const uint16_t** out, cudaStream_t stream) {
+  if (rows <= 0) return SPX_OK;
+  int64_t blocks = (rows + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  peer_row_pointers_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(order, send_at, recv_seg, groups, top_k,
+                                                                        src_rows, ld, rows, out);
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
 }  // namespace spx

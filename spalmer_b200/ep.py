@@ -238,6 +238,22 @@ class CudaOps:
                                        out.data_ptr(), out.stride(0), stream), "spx_gather_rows")
         return out
 
+    def experts_rows(self, row_ptrs: Tensor, row_expert: Tensor, row_out: Tensor) -> None:
+        """BF16 experts whose input row i is read at ``row_ptrs[i]`` and whose
+        output row i is stored at ``row_out[i]`` (int64 device tables; peer
+        GPUs' memory included)."""
+
+        R = row_ptrs.shape[0]
+        if R == 0:
+            return
+        lib = _lib.load()
+        dims = self._local_dims(R)
+        ws = self._workspace(dims, "experts")
+        stream = torch.cuda.current_stream(row_ptrs.device).cuda_stream
+        _lib.check(lib.spx_experts_forward_rows(dims, self._weights(R, R, None), row_ptrs.data_ptr(),
+                                                row_expert.data_ptr(), row_out.data_ptr(), ws.data_ptr(), stream),
+                   "spx_experts_forward_rows")
+
     def experts_to(self, rows: Tensor, row_expert: Tensor, lanes: Tensor | None, row_out: Tensor) -> None:
         """Expert outputs of ``rows``, output row i stored by the down
         projection's epilogue at the row pointer ``row_out[i]`` (int64, device;
@@ -355,10 +371,16 @@ class PeerExchange:
         del self.local[kind], self.peers[kind], self.ptr_tables[kind]
         self.capacity[kind] = 0
 
-    def ensure(self, kind: str, rows: int) -> None:
-        """Collective: every rank calls with the same ``rows`` (the largest need)."""
+    def view_int32(self, kind: str, n: int) -> Tensor:
+        """This rank's buffer's first ``n`` int32 values."""
 
-        if rows <= self.capacity[kind]:
+        return torch.as_tensor(_RawRows(self.local[kind], max(n, 0), 0, "<i4"), device=self.device)
+
+    def ensure(self, kind: str, rows: int) -> None:
+        """Collective: every rank calls with the same ``rows`` (the largest need),
+        in rows of d_model BF16 values."""
+
+        if rows <= self.capacity.get(kind, 0):
             return
         lib = _lib.load()
         self._release(kind)
@@ -427,7 +449,7 @@ class ExpertParallelMixer:
     """
 
     def __init__(self, mixer: Any, group: Any = None, ops: Any = None, dedup: bool = False,
-                 exchange: str | None = None):
+                 exchange: str | None = None, peer_rows: str = "store"):
         self.mixer = mixer
         self.dedup = dedup
         self.group = group
@@ -446,7 +468,10 @@ class ExpertParallelMixer:
             raise ValueError("exchange must be 'peer' or 'nccl'")
         if exchange == "peer" and (not cuda or dedup):
             raise ValueError("the peer exchange needs the CUDA backend and runs without row de-dup")
+        if peer_rows not in {"store", "load"}:
+            raise ValueError("peer_rows must be 'store' or 'load'")
         self.exchange = exchange
+        self.peer_rows = peer_rows
         self.peer = PeerExchange(group, ops.device, mixer.config.d_model) if exchange == "peer" else None
 
     def close(self) -> None:
@@ -549,29 +574,56 @@ class ExpertParallelMixer:
         ca = counts_all.cpu().numpy().astype(np.int64).reshape(G, G, el)  # [sender, owner, local expert]
         C = ca.sum(axis=2)  # [sender, owner]
         peer = self.peer
-        peer.ensure("recv", int(C.sum(axis=0).max()))
+        dev = x.device
+        lanes = self._local_lanes()
+        # peer_rows="load": BF16 experts' gate/up GEMM gathers its rows straight
+        # from the senders' memory (an MXFP8/NVFP4 lane quantises rows it holds,
+        # so those rows are always sent first).  "store" (the default) has the
+        # senders store the rows into the owners' receive buffers first: on
+        # ep_skew at 2 GPUs 4.44 ms per step against 5.31 ms for the GEMM's
+        # NVLink gathers, whose latency its producer warp does not hide.
+        rows_in_place = self.peer_rows == "load" and lanes is None and d % 64 == 0
         peer.ensure("back", int(C.sum(axis=1).max()))
-        # 3. rows of this rank's pairs (dispatch order) -> owners' receive buffers
-        send_seg = np.concatenate([[0], np.cumsum(C[me])])
-        recv_at = C[:me].sum(axis=0)  # where this rank's block starts in every owner's buffer
-        peer.send("recv", x, r["order"], k, send_seg, recv_at)
-        peer.barrier()
-        # 4. local experts on the received rows (from each sender: local expert 0, 1, ...)
         R = int(C[:, me].sum())
-        recv = peer.view("recv", R)
         plan = ExchangePlan(send_rows=[int(v) for v in C[me]], recv_rows=[int(v) for v in C[:, me]],
                             recv_expert_counts=ca[:, me, :])
-        # 5. the down projection's epilogue stores received row i's output straight
-        #    into its sender's return buffer, at the row of the sender's dispatch order
         recv_seg = np.concatenate([[0], np.cumsum(C[:, me])])
-        back_at = C[:, :me].sum(axis=1)
+        back_at = C[:, :me].sum(axis=1)  # = where each sender's pairs for this rank start in its dispatch order
+        if rows_in_place:
+            # 3. publish this rank's rows and dispatch order; every owner gathers from them
+            peer.ensure("x", int(C.sum(axis=1).max()) // k + 1)
+            peer.ensure("order", (int(C.sum(axis=1).max()) * 4 + 2 * d - 1) // (2 * d))
+            peer.view("x", T).copy_(x)
+            peer.view_int32("order", T * k).copy_(r["order"])
+            peer.barrier()
+        else:
+            # 3. rows of this rank's pairs (dispatch order) -> owners' receive buffers
+            peer.ensure("recv", int(C.sum(axis=0).max()))
+            send_seg = np.concatenate([[0], np.cumsum(C[me])])
+            recv_at = C[:me].sum(axis=0)  # where this rank's block starts in every owner's buffer
+            peer.send("recv", x, r["order"], k, send_seg, recv_at)
+            peer.barrier()
+        # 4-5. local experts; the down projection's epilogue stores received row i's
+        #      output straight into its sender's return buffer, at the row of the
+        #      sender's dispatch order
         if R:
-            dev = x.device
             src = torch.repeat_interleave(torch.arange(G, device=dev),
                                           torch.from_numpy(np.ascontiguousarray(C[:, me])).to(dev))
             rows_at = torch.from_numpy(back_at - recv_seg[:-1]).to(dev)[src] + torch.arange(R, device=dev)
             row_out = peer.ptr_tables["back"][src] + rows_at * (d * 2)
-            ops.experts_to(recv, receive_expert_ids(plan, dev), self._local_lanes(), row_out)
+            row_expert = receive_expert_ids(plan, dev)
+            if rows_in_place:
+                lib = _lib.load()
+                meta = torch.from_numpy(np.concatenate([back_at, recv_seg]).astype(np.int64)).to(dev)
+                row_ptrs = torch.empty(R, dtype=torch.int64, device=dev)
+                _lib.check(lib.spx_peer_row_pointers(peer.ptr_tables["order"].data_ptr(), meta.data_ptr(),
+                                                     meta[G:].data_ptr(), G, k, peer.ptr_tables["x"].data_ptr(),
+                                                     d, R, row_ptrs.data_ptr(),
+                                                     torch.cuda.current_stream(dev).cuda_stream),
+                           "spx_peer_row_pointers")
+                ops.experts_rows(row_ptrs, row_expert, row_out)
+            else:
+                ops.experts_to(peer.view("recv", R), row_expert, lanes, row_out)
         peer.barrier()
         # 6. combine with the routing weights and the shared output
         if self.side is not None:

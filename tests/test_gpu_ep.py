@@ -26,7 +26,7 @@ def _free_port() -> int:
 
 
 def _worker(rank: int, world: int, port: int, mxfp8: bool, out_dir: str, dedup: bool = False,
-            exchange: str | None = None) -> None:
+            exchange: str | None = None, peer_rows: str = "store") -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
@@ -45,7 +45,7 @@ def _worker(rank: int, world: int, port: int, mxfp8: bool, out_dir: str, dedup: 
             set_mxfp8_lanes(mixer, mxfp8_experts(config.num_experts, 0.25))
         x = torch.randn(8, 512, CFG["d_model"], generator=torch.Generator().manual_seed(1 + rank))
         x = x.to(torch.bfloat16).to(device)
-        ep = ExpertParallelMixer(mixer, dedup=dedup, exchange=exchange)
+        ep = ExpertParallelMixer(mixer, dedup=dedup, exchange=exchange, peer_rows=peer_rows)
         with torch.no_grad():
             first = ep(x)
             got = ep(x)  # buffers reused
@@ -67,13 +67,16 @@ def _worker(rank: int, world: int, port: int, mxfp8: bool, out_dir: str, dedup: 
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+@pytest.mark.parametrize("exchange", ["peer", "peer_load", "nccl"])
 @pytest.mark.parametrize("mxfp8", [False, True])
 def test_expert_parallel_matches_single_gpu(tmp_path, mxfp8, exchange):
     world = 2
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    mp.spawn(_worker, args=(world, _free_port(), mxfp8, str(tmp_path), False, exchange), nprocs=world, join=True)
+    peer_rows = "load" if exchange == "peer_load" else "store"
+    exchange = "peer" if exchange == "peer_load" else exchange
+    mp.spawn(_worker, args=(world, _free_port(), mxfp8, str(tmp_path), False, exchange, peer_rows), nprocs=world,
+             join=True)
     res = [torch.load(tmp_path / f"rank{r}.pt") for r in range(world)]
     for r in res:
         assert r["status"] == 0
