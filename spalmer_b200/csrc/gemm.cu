@@ -8,6 +8,9 @@
 //               x 128 B per instruction -- measured 1.7x faster on this
 //               kernel than TMA tile::gather4; STAGES-deep shared-memory
 //               ring of 128B-swizzled K-major tiles (64 BF16 of K per stage).
+//               In the BF16 instantiations that gather, warp 10 gathers the
+//               second half of each tile's rows (one warp could not keep the
+//               tensor pipe fed: expert GEMM1 246 vs 269 us at the 100M shape).
 //   warp 1      allocates TMEM; one lane issues tcgen05.mma (M=128, N=BN,
 //               K=16 per instruction) and commits stage releases.
 //   warps 2..9  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lane
@@ -478,10 +481,17 @@ __device__ __forceinline__ bool decode_tile(const GemmArgs& a, int t, int& group
 // every stage of the ring can be in flight at once.
 constexpr uint32_t kCpAsyncArrivals = 32;
 
-template <bool MX, bool NV = false>
+// PART 0: one producer warp gathers all 128 rows of a tile; PART 1..N: N
+// producer warps split them into equal row ranges (PART 1 also issues the B
+// TMA and the expect_tx), each lane's copies arriving on full[s] as before.
+template <bool MX, bool NV = false, int PART = 0>
 __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa, uint8_t* sb, uint8_t* ssf,
                                                  uint64_t* full, uint64_t* empty, int S, uint32_t a_bytes,
                                                  uint32_t b_bytes, int total, int lane) {
+  constexpr int kPer = PART == 0 ? 32 : 32 / kGemmGatherProducers;
+  constexpr int kI0 = PART == 0 ? 0 : (PART - 1) * kPer;
+  constexpr int kI1 = kI0 + kPer;
+  constexpr bool kLead = PART <= 1;
   const int bn = a.bn;
   const int chunk = lane & 7;
   const bool gather = a.gather != 0;
@@ -497,7 +507,7 @@ __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa,
     int src[32];  // source row of tile row 4*i + (lane >> 3)
     if (gather) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = kI0; i < kI1; ++i) {
         const int rr = 4 * i + (lane >> 3);
         src[i] = a.gather_idx[row0 + (rr < rows ? rr : 0)];
       }
@@ -518,7 +528,7 @@ __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa,
       int go = 1;
       if (lane == 0) {
         go = mbar_wait(&empty[s], ph ^ 1u, a.status, SPX_DEV_TIMEOUT_PRODUCER) ? 1 : 0;
-        if (go) {
+        if (go && kLead) {
           mbar_arrive_expect_tx(&full[s], tx_bytes);
           tma_load_3d(sb + s * b_bytes, &a.tma_b, &full[s], kb * 64 * (MX ? 2 : 1), n0, group);
           if (!gather) tma_load_2d(sa + s * a_bytes, &a.tma_a, &full[s], kb * 64 * (MX ? 2 : 1), row0);
@@ -535,7 +545,7 @@ __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa,
           // rows anywhere (a peer GPU's memory included), one pointer per source row
           const int off = kb * 128 + chunk * 16;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
+          for (int i = kI0; i < kI1; ++i) {
             const int rr = 4 * i + (lane >> 3);
             const uint32_t dst = dst0 + (rr >> 3) * 1024 + (rr & 7) * 128 + ((chunk ^ (rr & 7)) << 4);
             cp_async16(dst, a.a_rows[src[i]] + off);
@@ -543,7 +553,7 @@ __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa,
         } else {
           const uint8_t* col = a.a_base + kb * 128 + chunk * 16;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
+          for (int i = kI0; i < kI1; ++i) {
             const int rr = 4 * i + (lane >> 3);
             const uint32_t dst = dst0 + (rr >> 3) * 1024 + (rr & 7) * 128 + ((chunk ^ (rr & 7)) << 4);
             cp_async16(dst, col + static_cast<int64_t>(src[i]) * a.lda);
@@ -584,8 +594,15 @@ __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa,
 // The TMA producer and the MMA issuer stream k-blocks through the stage ring
 // without stopping at tile boundaries; the accumulator is multi-buffered in
 // TMEM so the epilogue of one tile overlaps the MMAs of the next.
+// Instantiations that can gather A rows (BF16 kEpiStore / kEpiSwiglu) carry
+// the extra producer warps; the others keep 10 warps (and their registers).
+template <int EPI, bool MX>
+constexpr int gemm_threads() {
+  return (!MX && (EPI == kEpiStore || EPI == kEpiSwiglu)) ? kGemmKernelThreads : kGemmThreads;
+}
+
 template <int EPI, bool MX, bool NV = false>
-__global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ GemmArgs a) {
+__global__ void __launch_bounds__(gemm_threads<EPI, MX>(), 1) gemm_kernel(const __grid_constant__ GemmArgs a) {
   constexpr uint32_t kSfStage = NV ? kNvStageSfBytes : kMxStageSfBytes;
   extern __shared__ uint8_t gemm_smem_raw[];
   uint8_t* smem = align_1024(gemm_smem_raw);
@@ -617,10 +634,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   const int total = m_tiles * a.n_tiles;
   if (static_cast<int>(blockIdx.x) >= total) return;
   const bool ldst_producer = MX || a.gather != 0;
+  const bool gather_producers = gemm_threads<EPI, MX>() == kGemmKernelThreads && a.gather != 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], ldst_producer ? 1 + kCpAsyncArrivals : 1);
+      mbar_init(&full[s], ldst_producer ? 1 + kCpAsyncArrivals * (gather_producers ? kGemmGatherProducers : 1) : 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < kMaxAccBufs; ++b) {
@@ -643,7 +661,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && ldst_producer) {
+  if (warp >= kGemmExtraProducerWarp0) {
+    if (gather_producers) {
+      const int part = 2 + warp - kGemmExtraProducerWarp0;
+      if (part == 2) produce_cp_async<MX, NV, 2>(a, sa, sb, ssf, full, empty, S, a_bytes, b_bytes, total, lane);
+      if constexpr (kGemmGatherProducers > 2) {
+        if (part == 3) produce_cp_async<MX, NV, 3>(a, sa, sb, ssf, full, empty, S, a_bytes, b_bytes, total, lane);
+        if (part == 4) produce_cp_async<MX, NV, 4>(a, sa, sb, ssf, full, empty, S, a_bytes, b_bytes, total, lane);
+      }
+    }
+  } else if (warp == 0 && gather_producers) {
+    produce_cp_async<MX, NV, 1>(a, sa, sb, ssf, full, empty, S, a_bytes, b_bytes, total, lane);
+  } else if (warp == 0 && ldst_producer) {
     produce_cp_async<MX, NV>(a, sa, sb, ssf, full, empty, S, a_bytes, b_bytes, total, lane);
   } else if (warp == 0) {
     // ---------------- TMA producer
@@ -1079,7 +1108,7 @@ static int launch_gemm_t(const GemmArgs& a, int grid_m, int grid_n, cudaStream_t
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);
   GemmArgs b = a;
   b.n_tiles = grid_n;
-  gemm_kernel<EPI, MX, NV><<<grid, kGemmThreads, smem, stream>>>(b);
+  gemm_kernel<EPI, MX, NV><<<grid, gemm_threads<EPI, MX>(), smem, stream>>>(b);
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 

@@ -11,6 +11,11 @@ namespace spx {
 
 constexpr int kTileRows = 128;         // M of every tcgen05 tile (cta_group::1)
 constexpr int kGemmThreads = 320;      // 10 warps: TMA, MMA, 8 x epilogue (2 per TMEM lane quadrant)
+// gemm_kernel adds producer warps for gathered BF16 rows (warp 0 and warps
+// 10.. each gather an equal share of a tile's rows); idle otherwise.
+constexpr int kGemmGatherProducers = 2;
+constexpr int kGemmExtraProducerWarp0 = 10;
+constexpr int kGemmKernelThreads = 32 * (10 + kGemmGatherProducers - 1);
 constexpr int kGemmEpilogueWarps = 8;
 constexpr int kMaxAccBufs = 4;         // TMEM accumulator buffers per CTA (as many as fit in 512 columns)
 constexpr size_t kGemmSmemBudget = 227 * 1024;  // sm_100 opt-in maximum per CTA
