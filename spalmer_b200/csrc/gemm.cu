@@ -560,7 +560,7 @@ __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa,
           }
         }
       }
-      if constexpr (MX && NV) {
+      if constexpr (MX && NV && kLead) {
         // Four K-64 MMAs per stage: A atom q holds bytes 4q..4q+3 of each
         // row's 16 scale bytes of the stage; the B atoms of the stage are
         // contiguous ([q][128-row block]).
@@ -575,7 +575,7 @@ __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa,
         const int64_t atom = ((static_cast<int64_t>(group) * a.n_tiles + nt) * a.k_blocks + kb) * sfb_atoms;
         for (int q = 0; q < sfb_atoms; ++q)
           cp_async16(sf + (4 + q) * kMxAtomBytes + lane * 16, a.sfb + (atom + q) * kMxAtomBytes + lane * 16);
-      } else if constexpr (MX) {
+      } else if constexpr (MX && !NV && kLead) {
         const uint32_t sf = smem_u32(ssf + s * kMxStageSfBytes);
 #pragma unroll
         for (int j = 0; j < 4; ++j) cp_async4(sf + lane * 16 + j * 4, a.sfa + sfr[j] * a.ld_sfa + kb * 4);
@@ -594,15 +594,18 @@ __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa,
 // The TMA producer and the MMA issuer stream k-blocks through the stage ring
 // without stopping at tile boundaries; the accumulator is multi-buffered in
 // TMEM so the epilogue of one tile overlaps the MMAs of the next.
-// Instantiations that can gather A rows (BF16 kEpiStore / kEpiSwiglu) carry
-// the extra producer warps; the others keep 10 warps (and their registers).
-template <int EPI, bool MX>
+// Instantiations that can gather A rows (BF16 kEpiStore / kEpiSwiglu, the
+// MXFP8 kEpiSwiglu; the NVFP4 GEMM1 reads A by TMA) carry the extra producer
+// warps; the others keep 10 warps (and their registers).  Only the lead
+// producer copies scale factors.
+template <int EPI, bool MX, bool NV>
 constexpr int gemm_threads() {
-  return (!MX && (EPI == kEpiStore || EPI == kEpiSwiglu)) ? kGemmKernelThreads : kGemmThreads;
+  return ((!MX && (EPI == kEpiStore || EPI == kEpiSwiglu)) || (MX && !NV && EPI == kEpiSwiglu)) ? kGemmKernelThreads
+                                                                                                  : kGemmThreads;
 }
 
 template <int EPI, bool MX, bool NV = false>
-__global__ void __launch_bounds__(gemm_threads<EPI, MX>(), 1) gemm_kernel(const __grid_constant__ GemmArgs a) {
+__global__ void __launch_bounds__(gemm_threads<EPI, MX, NV>(), 1) gemm_kernel(const __grid_constant__ GemmArgs a) {
   constexpr uint32_t kSfStage = NV ? kNvStageSfBytes : kMxStageSfBytes;
   extern __shared__ uint8_t gemm_smem_raw[];
   uint8_t* smem = align_1024(gemm_smem_raw);
@@ -634,7 +637,7 @@ __global__ void __launch_bounds__(gemm_threads<EPI, MX>(), 1) gemm_kernel(const 
   const int total = m_tiles * a.n_tiles;
   if (static_cast<int>(blockIdx.x) >= total) return;
   const bool ldst_producer = MX || a.gather != 0;
-  const bool gather_producers = gemm_threads<EPI, MX>() == kGemmKernelThreads && a.gather != 0;
+  const bool gather_producers = gemm_threads<EPI, MX, NV>() == kGemmKernelThreads && a.gather != 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -1108,7 +1111,7 @@ static int launch_gemm_t(const GemmArgs& a, int grid_m, int grid_n, cudaStream_t
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);
   GemmArgs b = a;
   b.n_tiles = grid_n;
-  gemm_kernel<EPI, MX, NV><<<grid, gemm_threads<EPI, MX>(), smem, stream>>>(b);
+  gemm_kernel<EPI, MX, NV><<<grid, gemm_threads<EPI, MX, NV>(), smem, stream>>>(b);
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 
