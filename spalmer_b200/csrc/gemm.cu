@@ -60,9 +60,15 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
-__device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 __device__ __forceinline__ float lo_f(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float hi_f(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+// Both values rounded to BF16 (nearest even) and widened back, with one
+// packed conversion instead of two scalar ones.
+__device__ __forceinline__ void bfr2(float& x, float& y) {
+  const uint32_t p = pack_bf16x2(x, y);
+  x = lo_f(p);
+  y = hi_f(p);
+}
 // silu(x) = x / (1 + e^-x); approximate exp/divide, the result is rounded to BF16.
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
@@ -127,12 +133,14 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
           u0 *= alpha1;
           u1 *= alpha1;
         }
-        const float h0 = bfr(silu_fast(bfr(g0))) * bfr(u0);
-        const float h1 = bfr(silu_fast(bfr(g1))) * bfr(u1);
-        hw[j / 2] = pack_bf16x2(h0, h1);
+        bfr2(g0, g1);
+        bfr2(u0, u1);
+        float sg0 = silu_fast(g0), sg1 = silu_fast(g1);
+        bfr2(sg0, sg1);
+        hw[j / 2] = pack_bf16x2(sg0 * u0, sg1 * u1);
         if constexpr (SC) {
-          if (live && j < w) hmax = fmaxf(hmax, fabsf(bfr(h0)));
-          if (live && j + 1 < w) hmax = fmaxf(hmax, fabsf(bfr(h1)));
+          if (live && j < w) hmax = fmaxf(hmax, fabsf(lo_f(hw[j / 2])));
+          if (live && j + 1 < w) hmax = fmaxf(hmax, fabsf(hi_f(hw[j / 2])));
         }
       }
     } else {
@@ -224,8 +232,11 @@ __device__ __forceinline__ void run_epilogue_rows(const GemmArgs& a, uint32_t ta
     tmem_wait_ld();
     uint32_t hw[32];
 #pragma unroll
-    for (int j = 0; j < 64; j += 2)
-      hw[j / 2] = pack_bf16x2(bfr(__uint_as_float(v[j]) * alpha) * my_w, bfr(__uint_as_float(v[j + 1]) * alpha) * my_w);
+    for (int j = 0; j < 64; j += 2) {
+      float f0 = __uint_as_float(v[j]) * alpha, f1 = __uint_as_float(v[j + 1]) * alpha;
+      bfr2(f0, f1);
+      hw[j / 2] = pack_bf16x2(f0 * my_w, f1 * my_w);
+    }
 #pragma unroll
     for (int c = 0; c < 64; c += 16) stage_put16(buf, lane, c, &hw[c / 2]);
     const int gcol0 = n0 + s0;
@@ -427,11 +438,12 @@ __device__ __forceinline__ void run_epilogue_swiglu_mx(const GemmArgs& a, uint32
     float h[32];
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
-      h[2 * c] = bfr(silu_fast(lo_f(gp[j][c]))) * lo_f(up[j][c]);
-      h[2 * c + 1] = bfr(silu_fast(hi_f(gp[j][c]))) * hi_f(up[j][c]);
+      float sg0 = silu_fast(lo_f(gp[j][c])), sg1 = silu_fast(hi_f(gp[j][c]));
+      bfr2(sg0, sg1);
+      h[2 * c] = sg0 * lo_f(up[j][c]);
+      h[2 * c + 1] = sg1 * hi_f(up[j][c]);
+      bfr2(h[2 * c], h[2 * c + 1]);
     }
-#pragma unroll
-    for (int c = 0; c < 32; ++c) h[c] = bfr(h[c]);
     uint32_t q[8];
     const uint32_t sb = mx_quantize32(h, q);
     if (live) {
