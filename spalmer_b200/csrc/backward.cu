@@ -33,6 +33,15 @@ namespace {
 __device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 __device__ __forceinline__ uint16_t bfbits(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+// Two values rounded to BF16 (nearest even) by one packed conversion: the
+// word (lo in the low half) and, widened back in place, the rounded floats.
+__device__ __forceinline__ uint32_t bfr2(float& lo, float& hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  const uint32_t w = *reinterpret_cast<uint32_t*>(&v);
+  lo = __uint_as_float(w << 16);
+  hi = __uint_as_float(w & 0xFFFF0000u);
+  return w;
+}
 
 int grid_for(int64_t items, int per_block) {
   int64_t g = (items + per_block - 1) / per_block;
@@ -63,8 +72,8 @@ __global__ void bwd_gather_kernel(const uint16_t* __restrict__ x, const uint16_t
     uint32_t o[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const float lo = __uint_as_float(in[q] << 16) * w, hi = __uint_as_float(in[q] & 0xFFFF0000u) * w;
-      o[q] = static_cast<uint32_t>(bfbits(lo)) | (static_cast<uint32_t>(bfbits(hi)) << 16);
+      float lo = __uint_as_float(in[q] << 16) * w, hi = __uint_as_float(in[q] & 0xFFFF0000u) * w;
+      o[q] = bfr2(lo, hi);
     }
     *reinterpret_cast<uint4*>(dy_sorted + p * d + c) = make_uint4(o[0], o[1], o[2], o[3]);
   }
@@ -82,27 +91,35 @@ __device__ __forceinline__ void swiglu_bwd8(const uint4& gv, const uint4& uv, co
   uint32_t H[4], DG[4], DU[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    uint32_t hw = 0, dgw = 0, duw = 0;
+    // The word's two columns side by side ([0] low half, [1] high half), each
+    // rounding done for both at once.
+    const float g[2] = {__uint_as_float(G[q] << 16), __uint_as_float(G[q] & 0xFFFF0000u)};
+    const float u[2] = {__uint_as_float(U[q] << 16), __uint_as_float(U[q] & 0xFFFF0000u)};
+    const float dh1[2] = {__uint_as_float(D[q] << 16), __uint_as_float(D[q] & 0xFFFF0000u)};
+    float sgm[2], sg[2], h[2], dh[2], dsg[2], du[2];
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const float g = half ? __uint_as_float(G[q] & 0xFFFF0000u) : __uint_as_float(G[q] << 16);
-      const float u = half ? __uint_as_float(U[q] & 0xFFFF0000u) : __uint_as_float(U[q] << 16);
-      const float dh1 = half ? __uint_as_float(D[q] & 0xFFFF0000u) : __uint_as_float(D[q] << 16);
-      const float sgm = sigmoidf_(g);
-      const float sg = bfr(g / (1.0f + expf(-g)));  // silu as the reference evaluates it
-      const float h = bfr(sg * u);
-      part += dh1 * h;
-      const float dh = bfr(dh1 * w);
-      const float dsg = bfr(dh * u);
-      const float du = bfr(dh * sg);
-      const float dg = bfr(dsg * (sgm * (1.0f + g * (1.0f - sgm))));
-      hw |= static_cast<uint32_t>(bfbits(h)) << (16 * half);
-      dgw |= static_cast<uint32_t>(bfbits(dg)) << (16 * half);
-      duw |= static_cast<uint32_t>(bfbits(du)) << (16 * half);
+    for (int i = 0; i < 2; ++i) {
+      sgm[i] = sigmoidf_(g[i]);
+      sg[i] = g[i] / (1.0f + expf(-g[i]));  // silu as the reference evaluates it
     }
-    H[q] = hw;
-    DG[q] = dgw;
-    DU[q] = duw;
+    bfr2(sg[0], sg[1]);
+    h[0] = sg[0] * u[0];
+    h[1] = sg[1] * u[1];
+    H[q] = bfr2(h[0], h[1]);
+    part += dh1[0] * h[0];
+    part += dh1[1] * h[1];
+    dh[0] = dh1[0] * w;
+    dh[1] = dh1[1] * w;
+    bfr2(dh[0], dh[1]);
+    dsg[0] = dh[0] * u[0];
+    dsg[1] = dh[1] * u[1];
+    bfr2(dsg[0], dsg[1]);
+    du[0] = dh[0] * sg[0];
+    du[1] = dh[1] * sg[1];
+    DU[q] = bfr2(du[0], du[1]);
+    float dg0 = dsg[0] * (sgm[0] * (1.0f + g[0] * (1.0f - sgm[0])));
+    float dg1 = dsg[1] * (sgm[1] * (1.0f + g[1] * (1.0f - sgm[1])));
+    DG[q] = bfr2(dg0, dg1);
   }
   hv = make_uint4(H[0], H[1], H[2], H[3]);
   dgv = make_uint4(DG[0], DG[1], DG[2], DG[3]);
