@@ -39,7 +39,7 @@ def _rows(shape, seed, spread=6.0):
     return f32_to_bf16_bits(x.astype(np.float32))
 
 
-@pytest.mark.parametrize("rows,cols", [(300, 768), (7, 32), (129, 160)])
+@pytest.mark.parametrize("rows,cols", [(300, 768), (7, 32), (129, 160), (30000, 768)])
 def test_quantize_rows_is_bit_exact(rows, cols):
     bits = _rows((rows, cols), seed=rows + cols)
     q, s = mx_quantize_rows(from_bits(bits, DEV))
