@@ -33,6 +33,8 @@
  *   spx_layer_route    router + selection + dispatch     experts/mixer.py:176-199,
  *                                                        bank.py:721-736
  *   spx_gather_rows    hidden_states[token_index] in dispatch order   bank.py:751
+ *   spx_swiglu_backward_rows  SwiGLU backward of rows (shared expert in the
+ *                      layer's training step)            nn/ffn.py:27-30 (autograd)
  *   spx_experts_forward grouped expert SwiGLU of rows with given expert ids
  *                      (unweighted)                      bank.py:740-763
  *   spx_shared_forward SwiGLU.forward                    nn/ffn.py:27-30
@@ -225,6 +227,24 @@ int spx_layer_route(const spx_layer_dims* dims, const spx_packed_weights* weight
 /* out[i, :] = src[index[i] / index_div, :] for BF16 rows of d elements. */
 int spx_gather_rows(const uint16_t* src, int64_t ld_src, const int32_t* index, int32_t index_div, int64_t rows,
                     int32_t d, uint16_t* out, int64_t ld_out, void* stream);
+
+/* SwiGLU backward of rows (the autograd of nn/ffn.py:27-30 and of the
+ * routed experts' silu(x W_g) * (x W_u), experts/bank.py:740-763, with the
+ * routing weight applied to the upstream gradient).  gate_up [rows,
+ * ld_gate_up] holds each row's pre-activations in chunks of `chunk` columns
+ * ([gate chunk | up chunk] per chunk, inter / chunk chunks), d_hidden
+ * [rows, ld_d_hidden] the gradient of the down projection's input before
+ * the weight, weights[rows] BF16 routing weights (1 for unweighted rows).
+ * Writes hidden [rows, inter] = bf16(bf16(silu(gate)) * up), d_gate_up
+ * [rows, 2 * inter_pad] = [d gate | d up] (each half zero-padded to
+ * inter_pad columns) and d_weights[order[r]] = sum over the row of
+ * d_hidden * hidden (FP32).  Every intermediate is rounded to BF16.  Needs
+ * chunk % 8 == 0, inter_pad % 8 == 0 and 16-byte aligned gate_up, d_hidden,
+ * hidden and d_gate_up. */
+int spx_swiglu_backward_rows(const uint16_t* gate_up, int64_t ld_gate_up, int32_t chunk, const uint16_t* d_hidden,
+                             int64_t ld_d_hidden, const uint16_t* weights, const int32_t* order, int64_t rows,
+                             int32_t inter, int32_t inter_pad, uint16_t* hidden, uint16_t* d_gate_up,
+                             float* d_weights, void* stream);
 
 /* Grouped SwiGLU experts of `rows` [R, d], row i through expert row_expert[i]
  * (0..num_experts-1 of `weights`): out_rows[i] = bf16(down(silu(gate x) *

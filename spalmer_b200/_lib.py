@@ -43,6 +43,7 @@ EXPORTED = (
     "spx_mxfp8_mm_nt",
     "spx_layer_route",
     "spx_gather_rows",
+    "spx_swiglu_backward_rows",
     "spx_experts_forward",
     "spx_shared_forward",
     "spx_combine",
@@ -224,6 +225,11 @@ def load() -> ctypes.CDLL:
         "spx_gather_rows": (
             ctypes.c_int,
             [_vp, ctypes.c_int64, _vp, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, _vp, ctypes.c_int64, _vp],
+        ),
+        "spx_swiglu_backward_rows": (
+            ctypes.c_int,
+            [_vp, ctypes.c_int64, ctypes.c_int32, _vp, ctypes.c_int64, _vp, _vp, ctypes.c_int64, ctypes.c_int32,
+             ctypes.c_int32, _vp, _vp, _vp, _vp],
         ),
         "spx_experts_forward": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, _vp, _vp, _vp, _vp]),
         "spx_shared_forward": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, _vp, _vp, _vp]),

@@ -1609,6 +1609,27 @@ int spx_gather_rows(const uint16_t* src, int64_t ld_src, const int32_t* index, i
   return launch_gather_rows(src, ld_src, index, index_div, rows, d, out, ld_out, static_cast<cudaStream_t>(stream));
 }
 
+int spx_swiglu_backward_rows(const uint16_t* gate_up, int64_t ld_gate_up, int32_t chunk, const uint16_t* d_hidden,
+                             int64_t ld_d_hidden, const uint16_t* weights, const int32_t* order, int64_t rows,
+                             int32_t inter, int32_t inter_pad, uint16_t* hidden, uint16_t* d_gate_up,
+                             float* d_weights, void* stream) {
+  if (rows < 0 || chunk < 8 || inter < chunk || inter % chunk != 0 || inter_pad < inter || inter_pad % 8 != 0)
+    return SPX_ERR_INVALID_ARG;
+  if (ld_gate_up < 2 * static_cast<int64_t>(inter) || ld_d_hidden < inter || ld_gate_up > INT32_MAX ||
+      ld_d_hidden > INT32_MAX)
+    return SPX_ERR_INVALID_ARG;
+  if (rows == 0) return SPX_OK;
+  if (gate_up == nullptr || d_hidden == nullptr || weights == nullptr || order == nullptr || hidden == nullptr ||
+      d_gate_up == nullptr || d_weights == nullptr)
+    return SPX_ERR_INVALID_ARG;
+  const uintptr_t any = reinterpret_cast<uintptr_t>(gate_up) | reinterpret_cast<uintptr_t>(d_hidden) |
+                        reinterpret_cast<uintptr_t>(hidden) | reinterpret_cast<uintptr_t>(d_gate_up);
+  if ((any & 15u) != 0) return SPX_ERR_INVALID_ARG;  // 16-byte row loads and stores
+  return launch_bwd_swiglu(gate_up, static_cast<int>(ld_gate_up), chunk, d_hidden, static_cast<int>(ld_d_hidden),
+                           weights, order, rows, inter, inter_pad, hidden, d_gate_up, d_weights,
+                           static_cast<cudaStream_t>(stream));
+}
+
 size_t spx_calibration_workspace(int64_t batch, int64_t seq, int32_t num_experts) {
   if (batch < 1 || seq < 2 || num_experts < 1) return 0;
   return calibration_workspace_bytes(batch, seq, num_experts);

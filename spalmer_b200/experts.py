@@ -913,7 +913,34 @@ class B200MicroExpertChannelMixer(nn.Module):
         grads["experts.gate_proj"] = _grouped_wgrad(x_sorted, dgu[:, :I], counts, offs)
         grads["experts.up_proj"] = _grouped_wgrad(x_sorted, dgu[:, kI:kI + I], counts, offs)
         grads["experts.down_proj"] = _grouped_wgrad(h_sorted, dy_sorted, counts, offs)
-        if self.shared is not None:
+        if self.shared is not None and _shared_bwd_native(self.shared, x):
+            # Shared SwiGLU backward without autograd: [gate | up] in one GEMM,
+            # the elementwise part in one kernel (spx_swiglu_backward_rows,
+            # unit weights), [d gate | d up] against [W_g | W_u] in one GEMM
+            # each for the input and the weight gradients.
+            sh = self.shared
+            wg, wu, wd = (w.detach() for w in (sh.gate_projection.weight, sh.up_projection.weight,
+                                               sh.down_projection.weight))
+            S = wg.shape[0]
+            T = x.shape[0]
+            w1 = torch.cat([wg, wu], 0)
+            gate_up = F.linear(x, w1)
+            d_h = du.mm(wd)
+            h_s = torch.empty(T, S, dtype=torch.bfloat16, device=device)
+            dgu_s = torch.empty(T, 2 * S, dtype=torch.bfloat16, device=device)
+            ones = torch.ones(T, dtype=torch.bfloat16, device=device)
+            order = torch.arange(T, dtype=torch.int32, device=device)
+            d_w = torch.empty(T, dtype=torch.float32, device=device)
+            _lib.check(lib.spx_swiglu_backward_rows(gate_up.data_ptr(), 2 * S, S, d_h.data_ptr(), S,
+                                                    ones.data_ptr(), order.data_ptr(), T, S, S, h_s.data_ptr(),
+                                                    dgu_s.data_ptr(), d_w.data_ptr(), stream),
+                       "spx_swiglu_backward_rows")
+            dx = dx + dgu_s.mm(w1)
+            dw1 = dgu_s.t().mm(x)
+            grads["shared.gate_projection.weight"] = dw1[:S]
+            grads["shared.up_projection.weight"] = dw1[S:]
+            grads["shared.down_projection.weight"] = du.t().mm(h_s)
+        elif self.shared is not None:
             sh = self.shared
             ws_ = [sh.gate_projection.weight, sh.up_projection.weight, sh.down_projection.weight]
             with torch.enable_grad():
@@ -927,6 +954,15 @@ class B200MicroExpertChannelMixer(nn.Module):
             grads["shared.down_projection.weight"] = g[3]
         grads["x"] = dx
         return grads
+
+
+def _shared_bwd_native(shared, x: Tensor) -> bool:
+    """Whether the shared SwiGLU backward fits spx_swiglu_backward_rows (no biases, rows in 16-byte units)."""
+
+    layers = (shared.gate_projection, shared.up_projection, shared.down_projection)
+    S = shared.gate_projection.weight.shape[0]
+    return (all(getattr(m, "bias", None) is None for m in layers) and S % 8 == 0 and x.dim() == 2
+            and x.dtype == torch.bfloat16)
 
 
 def _grouped_wgrad(a_sorted: Tensor, b_sorted: Tensor, counts: Tensor, offs: Tensor) -> Tensor:

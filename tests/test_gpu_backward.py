@@ -101,3 +101,42 @@ def test_training_refuses_mxfp8_experts():
         mixer(x)
     with torch.no_grad():
         mixer(x)  # inference still runs both lanes
+
+
+def test_swiglu_backward_rows_against_torch_fp32():
+    """spx_swiglu_backward_rows (the shared expert's SwiGLU backward in the
+    training step) against a plain PyTorch FP32 statement of the same
+    derivatives, on unit and non-unit row weights."""
+
+    import torch.nn.functional as F
+
+    from spalmer_b200 import _lib
+
+    lib = _lib.load()
+    T, S = 257, 96
+    g = torch.Generator().manual_seed(7)
+    gate, up, dh = (torch.randn(T, S, generator=g).to(torch.bfloat16).to(DEV) for _ in range(3))
+    w = (torch.rand(T, generator=g) + 0.5).to(torch.bfloat16).to(DEV)
+    gate_up = torch.cat([gate, up], 1).contiguous()
+    h = torch.empty(T, S, dtype=torch.bfloat16, device=DEV)
+    dgu = torch.empty(T, 2 * S, dtype=torch.bfloat16, device=DEV)
+    dw = torch.empty(T, dtype=torch.float32, device=DEV)
+    order = torch.arange(T, dtype=torch.int32, device=DEV).flip(0).contiguous()
+    stream = torch.cuda.current_stream(DEV).cuda_stream
+    assert lib.spx_swiglu_backward_rows(gate_up.data_ptr(), 2 * S, S, dh.data_ptr(), S, w.data_ptr(),
+                                        order.data_ptr(), T, S, S, h.data_ptr(), dgu.data_ptr(), dw.data_ptr(),
+                                        stream) == 0
+    torch.cuda.synchronize()
+    gf, uf, dhf, wf = gate.float(), up.float(), dh.float(), w.float()[:, None]
+    sig = torch.sigmoid(gf)
+    hf = F.silu(gf) * uf
+    dhw = dhf * wf
+    want_dgate = dhw * uf * sig * (1 + gf * (1 - sig))
+    want_dup = dhw * F.silu(gf)
+    for got, want in ((h, hf), (dgu[:, :S], want_dgate), (dgu[:, S:], want_dup)):
+        torch.testing.assert_close(got.float(), want, rtol=2e-2, atol=1e-2)
+    torch.testing.assert_close(dw.flip(0), (dhf * hf).sum(1), rtol=2e-2, atol=1e-2 * S)
+    # refused on the host before any launch: chunk not a multiple of 8
+    assert lib.spx_swiglu_backward_rows(gate_up.data_ptr(), 2 * S, 4, dh.data_ptr(), S, w.data_ptr(),
+                                        order.data_ptr(), T, S, S, h.data_ptr(), dgu.data_ptr(), dw.data_ptr(),
+                                        stream) != 0
