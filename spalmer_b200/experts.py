@@ -935,7 +935,7 @@ class B200MicroExpertChannelMixer(nn.Module):
                                                     ones.data_ptr(), order.data_ptr(), T, S, S, h_s.data_ptr(),
                                                     dgu_s.data_ptr(), d_w.data_ptr(), stream),
                        "spx_swiglu_backward_rows")
-            dx = dx + dgu_s.mm(w1)
+            dx = torch.addmm(dx, dgu_s, w1)  # one rounding: dx + [d gate | d up] @ [W_g | W_u]
             dw1 = dgu_s.t().mm(x)
             grads["shared.gate_projection.weight"] = dw1[:S]
             grads["shared.up_projection.weight"] = dw1[S:]
