@@ -36,32 +36,32 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 CONFIGS = {
-    # 100M-preset shape, a seeded 25% of the experts in MXFP8, the rest BF16.
+    # 100M-preset shape, a seeded 25% of the experts in MXFP8, the rest BF16 (the headline workload).
     "m100": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
-                          active_experts=8), batch=64, seq=1024, cpu_sample=1024, mxfp8_fraction=0.25),
+                          active_experts=8), batch=64, seq=1024, cpu_sample=1024, ref_sample=16384, mxfp8_fraction=0.25),
     # The same shape with a seeded 25% of the experts in NVFP4 (E2M1, UE4M3 per 1x16, per-tensor
     # scales; the reference's ("nvfp4", "nvfp4") pair), the rest BF16.
     "m100_nvfp4": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
-                                active_experts=8, expert_execution="loop"), batch=64, seq=1024, cpu_sample=1024,
+                                active_experts=8, expert_execution="loop"), batch=64, seq=1024, cpu_sample=1024, ref_sample=8192,
                        mxfp8_fraction=0.25, lowp_format="nvfp4"),
     # The same shape with every expert in BF16.
     "m100_bf16": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
-                               active_experts=8), batch=64, seq=1024, cpu_sample=1024),
-    # skewed expert parallel (Zipf(1.1) router bias), 131072 tokens in total,
+                               active_experts=8), batch=64, seq=1024, cpu_sample=1024, ref_sample=16384),
+    # Skewed expert parallel (Zipf(1.1) router bias), 131072 tokens in total,
     # experts sharded E/N per GPU with NCCL all-to-all (strong scaling).  S = 2*d (reference default).
     "ep_skew": dict(cfg=dict(d_model=1024, num_experts=200, expert_inter_dim=256, shared_inter_dim=2048,
-                             active_experts=8, router_bias=True), batch=128, seq=1024, cpu_sample=256,
+                             active_experts=8, router_bias=True), batch=128, seq=1024, cpu_sample=256, ref_sample=8192,
                     zipf=True, expert_parallel=True),
     # The same with the rows moved by NCCL all-to-all-v instead of stores into the peers' buffers.
     "ep_skew_nccl": dict(cfg=dict(d_model=1024, num_experts=200, expert_inter_dim=256, shared_inter_dim=2048,
-                                  active_experts=8, router_bias=True), batch=128, seq=1024, cpu_sample=256,
+                                  active_experts=8, router_bias=True), batch=128, seq=1024, cpu_sample=256, ref_sample=8192,
                          zipf=True, expert_parallel=True, exchange="nccl"),
     # The same with token rows sent once per destination GPU and pair rows summed
     # at the expert's GPU before they return.
     "ep_skew_dedup": dict(cfg=dict(d_model=1024, num_experts=200, expert_inter_dim=256, shared_inter_dim=2048,
-                                   active_experts=8, router_bias=True), batch=128, seq=1024, cpu_sample=256,
+                                   active_experts=8, router_bias=True), batch=128, seq=1024, cpu_sample=256, ref_sample=8192,
                           zipf=True, expert_parallel=True, dedup=True),
-    # decode-shaped steps through a 16-layer stack (independent seeded weights per
+    # Decode-shaped steps through a 16-layer stack (independent seeded weights per
     # layer, 10% of each layer's experts in MXFP8); the forward of the stack is one CUDA graph.
     "decode": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
                             active_experts=8), batch=1, seq=64, cpu_sample=64, mxfp8_fraction=0.10,
@@ -69,19 +69,20 @@ CONFIGS = {
     # Training step (forward + backward) of the 100M-shape layer, BF16 experts
     # (the MXFP8 lane has no backward); loss = sum(update * dU) + aux.
     "m100_train": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
-                                active_experts=8), batch=64, seq=1024, cpu_sample=256, train=True),
+                                active_experts=8), batch=64, seq=1024, cpu_sample=256, ref_sample=4096, train=True),
     # Paged expert offload (the reference's inference offload, experts/offload.py): the expert
     # bank stays in pinned host memory behind a device cache of half the experts; every step
     # stages the experts it selects through the cache page by page.
     "m100_paged": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
-                                active_experts=8), batch=64, seq=1024, cpu_sample=256, paged=dict(cache_size=100)),
+                                active_experts=8), batch=64, seq=1024, cpu_sample=256, ref_sample=16384,
+                      paged=dict(cache_size=100)),
     # Decode-shaped paged steps: 64 new tokens per step through one layer, a 64-expert cache.
     "decode_paged": dict(cfg=dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
                                   active_experts=8), batch=1, seq=64, cpu_sample=64, paged=dict(cache_size=64)),
-    # BASELINE config 2: 10M-preset shape.
+    # 10M-preset shape.
     "m10": dict(cfg=dict(d_model=256, num_experts=200, expert_inter_dim=64, shared_inter_dim=256,
-                         active_experts=8), batch=32, seq=512, cpu_sample=4096),
-    # BASELINE config 1: CPU-runnable smoke layer.
+                         active_experts=8), batch=32, seq=512, cpu_sample=4096, ref_sample=16384),
+    # CPU-runnable smoke layer.
     "smoke": dict(cfg=dict(d_model=128, num_experts=200, expert_inter_dim=32, shared_inter_dim=128,
                            active_experts=4), batch=2, seq=256, cpu_sample=512),
 }
@@ -245,51 +246,179 @@ def init_dist():
     return world, rank, local
 
 
+REF_SITE = ROOT / "baseline" / "_ref"
+
+
+def reference_package():
+    """The reference package as installed by ``oracle/install_ref.py`` (unmodified
+    mESmaC/spalmer sources under baseline/_ref), or None when it is absent."""
+
+    if not (REF_SITE / "spalmer" / "experts" / "mixer.py").is_file():
+        return None
+    if str(REF_SITE) not in sys.path:
+        sys.path.insert(0, str(REF_SITE))
+    import spalmer.experts as ref_experts
+
+    return ref_experts
+
+
+def reference_mixer(spec: dict, seed: int = 0):
+    """The reference's own MicroExpertChannelMixer (experts/mixer.py:54-241) for the
+    workload, built under torch.manual_seed(seed) and cast to BF16 on the CPU.
+    Every expert is BF16: the reference has no CPU MXFP8/NVFP4 path and rejects
+    BF16 experts mixed with a low-precision promotion (experts/config.py:140-161)."""
+
+    E = reference_package()
+    config = E.MicroExpertsConfig(**spec["cfg"])
+    torch.manual_seed(seed)
+    mixer = E.MicroExpertChannelMixer(config).to(torch.bfloat16).eval()
+    if spec.get("zipf"):
+        alpha = json.loads((ROOT / "tests" / "golden" / "zipf_ep_skew.json").read_text())["alpha"]
+        perm = torch.randperm(config.num_experts, generator=torch.Generator().manual_seed(3))
+        rank = torch.empty(config.num_experts)
+        rank[perm] = torch.arange(1, config.num_experts + 1, dtype=torch.float32)
+        with torch.no_grad():
+            mixer.router.proj.bias.copy_(alpha * torch.log(rank))
+    return mixer
+
+
+def reference_step(spec: dict, mixer, x: torch.Tensor, du: torch.Tensor | None):
+    """One step of the reference on the CPU: its forward under torch.no_grad(),
+    or for training configs forward + backward through its own autograd graph."""
+
+    if du is None:
+        with torch.no_grad():
+            mixer(x)
+        return
+    mixer.zero_grad(set_to_none=True)
+    xg = x.detach().requires_grad_(True)
+    out = mixer(xg)
+    torch.autograd.backward([out.update, out.auxiliary_loss], [du, torch.ones((), dtype=out.auxiliary_loss.dtype)])
+
+
+def reference_inputs(spec: dict, d_model: int, sample: int):
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randn(1, sample, d_model, generator=gen).to(torch.bfloat16)
+    du = (0.05 * torch.randn(1, sample, d_model, generator=gen)).to(torch.bfloat16) if spec.get("train") else None
+    return x, du
+
+
+def reference_note(spec: dict, name: str, sample: int, runs: str) -> str:
+    what = "forward + backward (autograd)" if spec.get("train") else "forward under torch.no_grad()"
+    return (f"{sample} tokens of the {name} workload through the reference's own "
+            f"MicroExpertChannelMixer {what} (baseline/_ref, torch CPU BF16, "
+            f"expert_execution={spec['cfg'].get('expert_execution', 'grouped')!r}), {runs}"
+            + CPU_ALL_BF16_NOTE * bool(spec.get("mxfp8_fraction")))
+
+
 def run_reference_arm(args) -> None:
+    """The reference's own CPU implementation of the layer, timed on the host
+    cores with every thread torch may use: one step = one forward (training
+    configs: forward + backward) over a bounded token sample of the workload;
+    value = sample tokens / median step time.  Without the reference install,
+    the CPU restatement in oracle/ stands in (kind "port")."""
+
     world, rank, _ = init_dist()
     if rank != 0:
         return
-    import numpy as np
-
-    from oracle import mixer_ref as R
-    from tests.helpers import bf16_bits, oracle_params
-
     spec = CONFIGS[args.config]
-    mixer, _ = build_mixer(spec)
-    config = mixer.config
-    params = oracle_params(mixer)
-    sample = spec["cpu_sample"]
-    x = torch.randn(sample, config.d_model, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
-    x_bits = bf16_bits(x)
-    k = config.active_experts
-    for _ in range(args.warmup):
-        R.mixer_forward(params, x_bits, k)
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        R.mixer_forward(params, x_bits, k)
-        times.append(time.perf_counter() - t0)
-    mean_s = sum(times) / len(times)
-    value = sample / mean_s
-    cores = os.cpu_count()
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    ref_error = None
+    try:
+        ref = reference_package()
+    except Exception as exc:  # noqa: BLE001 - reported in the line
+        ref, ref_error = None, f"{type(exc).__name__}: {exc}"
+    if ref is not None:
+        sample = spec.get("ref_sample", spec["cpu_sample"])
+        mixer = reference_mixer(spec)
+        x, du = reference_inputs(spec, mixer.config.d_model, sample)
+        try:
+            for _ in range(args.warmup):
+                reference_step(spec, mixer, x, du)
+        except RuntimeError as exc:  # e.g. a host without a verified CPU BF16 lane
+            ref, ref_error = None, f"{type(exc).__name__}: {exc}"
+    if ref is not None:
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            reference_step(spec, mixer, x, du)
+            times.append(time.perf_counter() - t0)
+        kind = "reference"
+        note = reference_note(spec, args.config, sample, f"median of {len(times)} steps after {args.warmup} warm-up")
+    else:
+        import numpy as np  # noqa: F401
+
+        from oracle import mixer_ref as R
+        from tests.helpers import bf16_bits, oracle_params
+
+        mixer, _ = build_mixer(spec)
+        config = mixer.config
+        params = oracle_params(mixer)
+        sample = spec["cpu_sample"]
+        xt = torch.randn(sample, config.d_model, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+        x_bits = bf16_bits(xt)
+        k = config.active_experts
+        for _ in range(args.warmup):
+            R.mixer_forward(params, x_bits, k)
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            R.mixer_forward(params, x_bits, k)
+            times.append(time.perf_counter() - t0)
+        kind = "port"
+        note = (f"{sample} tokens of the {args.config} workload through the CPU restatement (oracle/, numpy), "
+                f"median of {len(times)} steps; reference install unavailable ({ref_error or 'baseline/_ref absent'})"
+                + CPU_ALL_BF16_NOTE * bool(spec.get("mxfp8_fraction")))
+    med_s = statistics.median(times)
+    value = sample / med_s
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean_s * 1e3, "higher_is_better": True,
+        "impl": "reference", "metric": METRIC + (" (training step: forward + backward)" if spec.get("train") else ""),
+        "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": med_s * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": workload_config(args.config, world),
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{sample} tokens of the {args.config} workload per step"
-                                   + CPU_ALL_BF16_NOTE * bool(spec.get("mxfp8_fraction"))},
+        "config": {**workload_config(args.config, world),
+                   **({"workload": f"{args.config}: SPALMER micro-expert layer forward + backward"}
+                      if spec.get("train") else {})},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": note},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 def cpu_baseline(args, mixer, x_cpu) -> dict:
+    """The reference's own CPU forward (or, without the reference install, the
+    oracle restatement) on a bounded sample of this workload: median of at
+    least 3 runs after one warm-up, about 15 s of CPU work at most."""
+
+    spec = CONFIGS[args.config]
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    try:
+        ref = reference_package()
+    except Exception:  # noqa: BLE001
+        ref = None
+    if ref is not None:
+        sample = spec.get("ref_sample", spec["cpu_sample"])
+        rmixer = reference_mixer(spec)
+        x, du = reference_inputs(spec, rmixer.config.d_model, sample)
+        try:
+            reference_step(spec, rmixer, x, du)
+        except RuntimeError:
+            ref = None
+    if ref is not None:
+        times = []
+        t_end = time.perf_counter() + 15.0
+        while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 10):
+            t0 = time.perf_counter()
+            reference_step(spec, rmixer, x, du)
+            times.append(time.perf_counter() - t0)
+        med = statistics.median(times)
+        return {"value": sample / med, "unit": "tokens/s", "cores": cores, "kind": "reference",
+                "sample": reference_note(spec, args.config, sample, f"median of {len(times)} runs")}
     from oracle import mixer_ref as R
     from tests.helpers import bf16_bits, oracle_params
 
-    spec = CONFIGS[args.config]
     sample = spec["cpu_sample"]
     params = oracle_params(mixer)
     x_bits = bf16_bits(x_cpu.reshape(-1, x_cpu.shape[-1])[:sample])
@@ -304,7 +433,7 @@ def cpu_baseline(args, mixer, x_cpu) -> dict:
     med = statistics.median(times)
     return {"value": sample / med, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
             "sample": f"{sample} tokens of the {args.config} workload, median of {len(times)} runs "
-                      f"(numpy/OpenBLAS on all host threads)"
+                      f"(CPU restatement, numpy/OpenBLAS on all host threads; reference install absent)"
                       + CPU_ALL_BF16_NOTE * bool(spec.get("mxfp8_fraction"))}
 
 
@@ -530,10 +659,20 @@ def run_ep(args) -> None:
         total_ms = t0.elapsed_time(t1)
         loads = None
         exchanged = None
+        stage_ms = None
         if layer is not None:
             r = layer(x_bufs[0])
             loads = r.get("recv_pairs", r["recv_rows"])
             exchanged = sum(r["send_rows"])
+            # stage split: events at every stage boundary on the compute stream
+            # (outside the timed region; the stages stay stream-ordered)
+            layer.record_stages(True)
+            for i in range(max(K // 2, 3)):
+                layer(x_bufs[i % 2])
+            stage_ms = layer.stage_times()
+            layer.record_stages(False)
+            torch.cuda.synchronize()
+            barrier()
         # e2e: pinned H2D of this rank's tokens, forward, D2H of the update, per step
         out_host = torch.empty(batch, seq, config.d_model, dtype=torch.bfloat16).pin_memory()
         xd = torch.empty_like(x_bufs[0])
@@ -582,6 +721,7 @@ def run_ep(args) -> None:
             "expert_rows_per_gpu": recv_loads,
             "rows_sent_per_gpu_rank0": exchanged,
             "max_over_mean_expert_load": max(recv_loads) / (sum(recv_loads) / len(recv_loads)),
+            "stages_ms_rank0": stage_ms,
         }
         line["roofline"]["frac"] = line["roofline"]["achieved"] / line["roofline"]["peak"]
         if clocks is not None:
@@ -804,7 +944,8 @@ def run_train(args) -> None:
         }
         line["roofline"]["frac"] = line["roofline"]["achieved"] / line["roofline"]["peak"]
         if not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_train_baseline(spec, mixer)
+            line["cpu_baseline"] = (cpu_baseline(args, mixer, None) if reference_package() is not None
+                                    else cpu_train_baseline(spec, mixer))
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

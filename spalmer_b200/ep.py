@@ -473,6 +473,35 @@ class ExpertParallelMixer:
         self.exchange = exchange
         self.peer_rows = peer_rows
         self.peer = PeerExchange(group, ops.device, mixer.config.d_model) if exchange == "peer" else None
+        self._marks: list | None = None
+
+    def record_stages(self, on: bool) -> None:
+        """Record a CUDA event on the compute stream at every stage boundary of
+        the next forwards (route, counts + host read, rows out, experts + rows
+        back, combine); `stage_times()` returns the mean milliseconds per stage."""
+
+        self._marks = [] if on else None
+
+    def _mark(self, name: str) -> None:
+        if self._marks is not None and isinstance(self.ops, CudaOps):
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(torch.cuda.current_stream(self.ops.device))
+            self._marks.append((name, ev))
+
+    def stage_times(self) -> dict[str, float]:
+        if not self._marks:
+            return {}
+        torch.cuda.synchronize(self.ops.device)
+        sums: dict[str, float] = {}
+        calls = 0
+        prev = None
+        for name, ev in self._marks:
+            if name == "start":
+                calls += 1
+            elif prev is not None:
+                sums[name] = sums.get(name, 0.0) + prev.elapsed_time(ev)
+            prev = ev
+        return {name: v / max(calls, 1) for name, v in sums.items()}
 
     def close(self) -> None:
         """Release the peer exchange buffers (collective)."""
@@ -493,6 +522,7 @@ class ExpertParallelMixer:
         ops = self.ops
         k = self.mixer.active_experts
         shared = None
+        self._mark("start")
         if self.side is not None:
             # the shared SwiGLU needs only x: run it while the rows travel
             self.side.wait_stream(torch.cuda.current_stream(ops.device))
@@ -502,6 +532,7 @@ class ExpertParallelMixer:
             shared = ops.shared(x)
         logits = None if router_logits is None else router_logits.reshape(T, -1).contiguous()
         r = ops.route(x, logits)
+        self._mark("route")
         if self.dedup:
             update, stats = self._exchange_dedup(x, r, shared)
             return {
@@ -528,24 +559,29 @@ class ExpertParallelMixer:
         recv_counts = torch.empty(self.world * self.e_local, dtype=torch.int32, device=r["counts"].device)
         dist.all_to_all_single(recv_counts, r["counts"], group=self.group)
         plan = exchange_plan(r["counts"].cpu().numpy(), recv_counts.cpu().numpy(), self.world)
+        self._mark("counts_alltoall_host_read")
         # 3. rows to their experts' ranks
         send = ops.gather(x, r["order"], k)
         recv = send.new_empty(sum(plan.recv_rows), d)
         dist.all_to_all_single(recv, send, output_split_sizes=plan.recv_rows, input_split_sizes=plan.send_rows,
                                group=self.group)
+        self._mark("rows_out")
         # 4. local experts, unweighted
         row_expert = receive_expert_ids(plan, recv.device)
         out_rows = ops.experts(recv, row_expert, self._local_lanes())
+        self._mark("experts")
         # 5. back to the senders (in their dispatch order)
         back = send.new_empty(T * k, d)
         dist.all_to_all_single(back, out_rows, output_split_sizes=plan.send_rows, input_split_sizes=plan.recv_rows,
                                group=self.group)
+        self._mark("rows_back")
         # 6. combine with the routing weights and the shared output
         if self.side is not None:
             torch.cuda.current_stream(ops.device).wait_stream(self.side)
             if shared is not None:
                 shared.record_stream(torch.cuda.current_stream(ops.device))
         update = ops.combine(back, r["rank"], r["routing_weights"], shared)
+        self._mark("shared_wait_combine")
         return {
             "update": update.reshape(B, S, d),
             "auxiliary_loss": r["auxiliary_loss"][0],
@@ -573,6 +609,7 @@ class ExpertParallelMixer:
         dist.all_gather_into_tensor(counts_all, r["counts"], group=self.group)
         ca = counts_all.cpu().numpy().astype(np.int64).reshape(G, G, el)  # [sender, owner, local expert]
         C = ca.sum(axis=2)  # [sender, owner]
+        self._mark("counts_allgather_host_read")
         peer = self.peer
         dev = x.device
         lanes = self._local_lanes()
@@ -603,6 +640,7 @@ class ExpertParallelMixer:
             recv_at = C[:me].sum(axis=0)  # where this rank's block starts in every owner's buffer
             peer.send("recv", x, r["order"], k, send_seg, recv_at)
             peer.barrier()
+        self._mark("rows_out")
         # 4-5. local experts; the down projection's epilogue stores received row i's
         #      output straight into its sender's return buffer, at the row of the
         #      sender's dispatch order
@@ -625,12 +663,14 @@ class ExpertParallelMixer:
             else:
                 ops.experts_to(peer.view("recv", R), row_expert, lanes, row_out)
         peer.barrier()
+        self._mark("experts_rows_back")
         # 6. combine with the routing weights and the shared output
         if self.side is not None:
             torch.cuda.current_stream(ops.device).wait_stream(self.side)
             if shared is not None:
                 shared.record_stream(torch.cuda.current_stream(ops.device))
         update = ops.combine(peer.view("back", T * k), r["rank"], r["routing_weights"], shared)
+        self._mark("shared_wait_combine")
         return update, {"send_rows": plan.send_rows, "recv_rows": plan.recv_rows}
 
     def _exchange_dedup(self, x: Tensor, r: dict, shared: Tensor | None) -> tuple[Tensor, dict]:
