@@ -53,7 +53,7 @@
 extern "C" {
 #endif
 
-#define SPX_ABI_VERSION 6
+#define SPX_ABI_VERSION 7
 
 #define SPX_OK 0
 #define SPX_ERR_INVALID_ARG -1
@@ -205,6 +205,16 @@ int spx_mxfp8_mm_nt(const uint16_t* left, const uint16_t* right_rows, int64_t m,
 int spx_route(const spx_layer_dims* dims, const uint16_t* logits, const uint16_t* softplus_table,
               const uint8_t* resident_mask, uint16_t* router_scores, int64_t* expert_ids,
               uint16_t* routing_weights, void* workspace, void* stream);
+
+/* SurpriseRouter.forward (experts/router.py:40-56): router_scores [T, E] =
+ * softplus(hidden @ W^T + b) in BF16 (the logits themselves for the legacy
+ * identity transform).  Uses weights->router_weight (packed by
+ * spx_pack_weights), ->router_bias and ->softplus_table; the workspace
+ * (spx_router_sizes bytes, zero-filled once) holds the status word and the
+ * K-padded rows when d_model % 64 != 0. */
+int spx_router_sizes(const spx_layer_dims* dims, size_t* workspace_bytes);
+int spx_router_forward(const spx_layer_dims* dims, const spx_packed_weights* weights,
+                       const uint16_t* hidden, uint16_t* router_scores, void* workspace, void* stream);
 
 /* Stable permutation of the T*k pairs by expert id, plus per-expert counts. */
 int spx_dispatch(const spx_layer_dims* dims, const int64_t* expert_ids, int32_t* order,
@@ -458,10 +468,19 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* wei
  * SPX_ERR_SCRATCH_LIMIT.  The first call on a device (with it current) looks
  * up the array's device address; make it before any stream capture.  Calls
  * share the array: calls that overlap on the GPU race, so serialise them.
- * Expert ids outside [0, num_experts) are skipped and their order slots are
- * left unwritten. */
+ * `stream` must belong to the current device (else SPX_ERR_INVALID_ARG); the
+ * looked-up address is kept for the life of the process (not refreshed
+ * after cudaDeviceReset).  Expert ids outside [0, num_experts) are skipped,
+ * their order slots are left unwritten, and the kernels record a non-zero
+ * status word that spx_dispatch_static_status reads. */
 int spx_dispatch_static(const spx_layer_dims* dims, const int64_t* expert_ids, int32_t* order,
                         int32_t* counts, void* stream);
+
+/* Read (and clear when `clear` != 0) the status word that the kernels of the
+ * last spx_dispatch_static call on the current device left in its scratch:
+ * 0 = no error.  Synchronises `stream` (which must belong to the current
+ * device); allocates nothing. */
+int spx_dispatch_static_status(int* device_status, int clear, void* stream);
 
 /* Read (and clear when `clear` != 0) the device status word of a workspace.
  * Synchronises `stream`.  *device_status == 0 means no kernel reported an error. */

@@ -199,10 +199,12 @@ def grouped_experts(x_bits: np.ndarray, expert_ids: np.ndarray, weight_bits: np.
 
     ``x_bits [T,d]``, ``expert_ids [T,k]``, ``weight_bits [T,k]``; expert stacks
     ``gate/up [E,d,I]``, ``down [E,I,d]`` (BF16 bits).  Returns the routed
-    update ``[T,d]`` (BF16 bits), reduced in the reference's ``index_add`` order
-    (buckets by padded capacity, then expert id, then sorted pair order; or
-    ascending expert id for ``execution="loop"``, bank.py:674-701) with a BF16
-    rounding after every addition.  ``lane_mx[e]`` selects the MXFP8 pair for
+    update ``[T,d]`` (BF16 bits), reduced as the reference's ``index_add``
+    calls reduce: grouped (bank.py:779) is one call over every pair in bucket
+    order (buckets by padded capacity, then expert id, then sorted pair order),
+    which torch's CPU index_add on BF16 accumulates in FP32 and rounds once;
+    loop (bank.py:674-701) is one call per expert in ascending id order, a BF16
+    rounding after each.  ``lane_mx[e]`` selects the MXFP8 pair for
     expert e (``_execution_pair``, bank.py:462-475); ``lane_nv[e]`` the NVFP4 pair.
     """
 
@@ -241,8 +243,80 @@ def grouped_experts(x_bits: np.ndarray, expert_ids: np.ndarray, weight_bits: np.
     acc = np.zeros((T, d), dtype=np.float32)
     for j in range(k):
         step = np.take_along_axis(contrib, seq[:, j][:, None, None], axis=1)[:, 0, :]
-        acc = round_bf16(acc + step)
+        acc = acc + step if execution == "grouped" else round_bf16(acc + step)
     return f32_to_bf16_bits(acc), order, counts
+
+
+def execute_routing(x_bits: np.ndarray, token_index: np.ndarray, expert_index: np.ndarray,
+                    weight_bits: np.ndarray, gate_bits: np.ndarray, up_bits: np.ndarray, down_bits: np.ndarray,
+                    *, execution: str = "grouped", resident_ids: np.ndarray | None = None,
+                    lane_mx: np.ndarray | None = None) -> np.ndarray:
+    """``MicroExpertBank.execute_routing`` for arbitrary (token, expert, weight)
+    pairs (``experts/bank.py:593-646``): ``_execute_grouped`` (``bank.py:705-779``)
+    or ``_execute_loop`` (``bank.py:674-703``).
+
+    ``x_bits [N,d]``; ``token_index``, ``expert_index`` int ``[P]``;
+    ``weight_bits [P]`` BF16.  Returns ``[N,d]`` BF16 bits: each pair's
+    ``bf16(bf16(out) * w)`` index_added into BF16 zeros as the reference does
+    -- grouped: one index_add over the pairs in bucket order (ascending
+    power-of-two capacity, within a bucket the candidate experts in order --
+    ``resident_ids`` order or ascending id -- within an expert the stable
+    sorted pair order), pairs whose expert is not a candidate not executed;
+    loop: one index_add per selected expert in ascending id order, pairs in
+    index order.  torch's CPU index_add on BF16 adds a call's sources in FP32
+    onto the FP32 value of the row and rounds once per call.
+    """
+
+    N, d = x_bits.shape
+    E = gate_bits.shape[0]
+    tok = np.asarray(token_index, dtype=np.int64).reshape(-1)
+    ids = np.asarray(expert_index, dtype=np.int64).reshape(-1)
+    w = bf16_bits_to_f32(np.asarray(weight_bits).reshape(-1))
+    P = ids.size
+    acc = np.zeros((N, d), dtype=np.float32)
+    if P == 0:
+        return f32_to_bf16_bits(acc)
+    counts = pair_counts(ids, E)
+    starts = np.cumsum(counts) - counts
+    order = dispatch_order(ids)
+
+    def run(e: int, rows: np.ndarray) -> np.ndarray:
+        xs = x_bits[tok[rows]]
+        if lane_mx is not None and lane_mx[e]:
+            y = _swiglu_rows_mxfp8(xs, gate_bits[e], up_bits[e], down_bits[e])
+        else:
+            y = _swiglu_rows(xs, bf16_bits_to_f32(gate_bits[e]), bf16_bits_to_f32(up_bits[e]),
+                             bf16_bits_to_f32(down_bits[e]))
+        return round_bf16(bf16_bits_to_f32(y) * w[rows][:, None])
+
+    if execution == "loop":
+        seq = []
+        for e in np.unique(ids):
+            rows = np.nonzero(ids == e)[0]
+            seq.append((rows, run(int(e), rows)))
+    elif execution == "grouped":
+        candidates = np.arange(E) if resident_ids is None else np.asarray(resident_ids, dtype=np.int64)
+        groups = [int(e) for e in candidates if counts[e] > 0]
+        cap = {e: int(_next_pow2(np.array([counts[e]]))[0]) for e in groups}
+        seq = []
+        for c in sorted(set(cap.values())):
+            for e in (g for g in groups if cap[g] == c):
+                rows = order[starts[e]: starts[e] + counts[e]]
+                seq.append((rows, run(e, rows)))
+    else:
+        raise ValueError(f"unsupported expert execution mode: {execution!r}")
+    def index_add(calls) -> None:  # each call: FP32 sums onto the rows, one rounding
+        for rows, weighted in calls:
+            touched = np.unique(tok[rows])
+            for i, p in enumerate(rows):
+                acc[tok[p]] = acc[tok[p]] + weighted[i]
+            acc[touched] = round_bf16(acc[touched])
+
+    if execution == "loop":
+        index_add(seq)
+    else:
+        index_add([(np.concatenate([r for r, _ in seq]), np.concatenate([w_ for _, w_ in seq]))])
+    return f32_to_bf16_bits(acc)
 
 
 def shared_swiglu(x_bits, gate_w_bits, up_w_bits, down_w_bits):

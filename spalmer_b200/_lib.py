@@ -69,9 +69,12 @@ EXPORTED = (
     "spx_experts_forward_to",
     "spx_experts_forward_rows",
     "spx_peer_row_pointers",
+    "spx_router_sizes",
+    "spx_router_forward",
+    "spx_dispatch_static_status",
 )
 
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 _vp = ctypes.c_void_p
 
@@ -218,6 +221,9 @@ def load() -> ctypes.CDLL:
         ),
         "spx_workspace_status": (ctypes.c_int, [_vp, P(ctypes.c_int), ctypes.c_int, _vp]),
         "spx_dispatch_static": (ctypes.c_int, [P(LayerDims), _vp, _vp, _vp, _vp]),
+        "spx_dispatch_static_status": (ctypes.c_int, [P(ctypes.c_int), ctypes.c_int, _vp]),
+        "spx_router_sizes": (ctypes.c_int, [P(LayerDims), P(ctypes.c_size_t)]),
+        "spx_router_forward": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, _vp, _vp, _vp]),
         "spx_pack_weights_mxfp8": (ctypes.c_int, [P(LayerDims), P(ReferenceWeights), _vp, _vp, _vp, _vp, _vp]),
         "spx_mxfp8_quantize_rows": (ctypes.c_int, [_vp, ctypes.c_int64, ctypes.c_int32, _vp, _vp, _vp]),
         "spx_mxfp8_mm_workspace": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]),

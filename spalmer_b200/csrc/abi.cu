@@ -982,6 +982,35 @@ int spx_route(const spx_layer_dims* dims, const uint16_t* logits, const uint16_t
                    expert_ids, routing_weights, workspace, L, static_cast<cudaStream_t>(stream));
 }
 
+int spx_router_sizes(const spx_layer_dims* dims, size_t* workspace_bytes) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (workspace_bytes == nullptr) return SPX_ERR_INVALID_ARG;
+  *workspace_bytes = kAlign + (s.kd != s.d ? round_up(2 * static_cast<size_t>(s.T) * s.kd, kAlign) : 0);
+  return SPX_OK;
+}
+
+int spx_router_forward(const spx_layer_dims* dims, const spx_packed_weights* w, const uint16_t* hidden,
+                       uint16_t* router_scores, void* workspace, void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (hidden == nullptr || router_scores == nullptr) return SPX_ERR_INVALID_ARG;
+  if (workspace == nullptr) return SPX_ERR_WORKSPACE;
+  if (int rc = check_layer_weights(s, dims, w, true, false, false); rc != SPX_OK) return rc;
+  if (!aligned16(hidden) || !aligned16(router_scores) || !aligned16(workspace)) return SPX_ERR_ALIGNMENT;
+  // Workspace: the status word, then the K-padded hidden rows when d % 64 != 0.
+  Layout L{};
+  L.small = 0;
+  L.x_pad = kAlign;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const Ctx c{s, L, workspace, st, at<int>(workspace, L.small), nullptr};
+  const uint16_t* xa = nullptr;
+  if (int rc = stage_pad(c, hidden, &xa); rc != SPX_OK) return rc;
+  if (int rc = stage_router(c, w, xa, router_scores); rc != SPX_OK) return rc;
+  if (dims->score_transform != 0) return SPX_OK;  // identity: the logits are the scores
+  return launch_scores_from_logits(router_scores, s.T * s.E, w->softplus_table, st);
+}
+
 int spx_dispatch(const spx_layer_dims* dims, const int64_t* expert_ids, int32_t* order, int32_t* counts,
                  void* workspace, void* stream) {
   Shape s;

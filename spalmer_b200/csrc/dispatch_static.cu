@@ -14,11 +14,14 @@
 // exits.  Host code cannot use the array's name as a device address, so the
 // first call on each device (with that device current) looks the address up
 // with cudaGetSymbolAddress and caches it; make that first call before any
-// stream capture.  All calls share the one array and it keeps the previous
-// call's contents: everything a call reads is rewritten by the same call, and
-// the status word is cleared at the start of every call.  Calls whose kernels
-// overlap on the GPU (different streams, no ordering) race on the array —
-// serialise them.
+// stream capture.  The cached address is kept for the life of the process and
+// is not refreshed after cudaDeviceReset.  The stream must belong to the
+// current device (checked).  All calls share the one array and it keeps the
+// previous call's contents: everything a call reads is rewritten by the same
+// call, and the status word is cleared at the start of every call.  Calls
+// whose kernels overlap on the GPU (different streams, no ordering) race on
+// the array — serialise them.  spx_dispatch_static_status reads the status
+// word the kernels leave (an expert id out of range, a malformed tile).
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -74,8 +77,33 @@ int static_scratch(void** out) {
   return SPX_OK;
 }
 
+// The stream (NULL = the current device's legacy stream) must belong to the current device.
+int check_stream_device(cudaStream_t st) {
+  if (st == nullptr) return SPX_OK;
+  int cur = 0, dev = 0;
+  if (cudaGetDevice(&cur) != cudaSuccess) return SPX_ERR_CUDA;
+  if (cudaStreamGetDevice(st, &dev) != cudaSuccess) return SPX_ERR_CUDA;
+  return dev == cur ? SPX_OK : SPX_ERR_INVALID_ARG;
+}
+
 }  // namespace
 }  // namespace spx
+
+extern "C" int spx_dispatch_static_status(int* device_status, int clear, void* stream) {
+  using namespace spx;
+  if (device_status == nullptr) return SPX_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = check_stream_device(st); rc != SPX_OK) return rc;
+  void* base = nullptr;
+  if (int rc = static_scratch(&base); rc != SPX_OK) return rc;
+  int* word = reinterpret_cast<int*>(static_cast<uint8_t*>(base) + kOffSmall);
+  int v = 0;
+  if (cudaMemcpyAsync(&v, word, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess) return SPX_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return SPX_ERR_CUDA;
+  *device_status = v;
+  if (clear && v != 0 && cudaMemsetAsync(word, 0, sizeof(int), st) != cudaSuccess) return SPX_ERR_CUDA;
+  return SPX_OK;
+}
 
 extern "C" int spx_dispatch_static(const spx_layer_dims* dims, const int64_t* expert_ids, int32_t* order,
                                    int32_t* counts, void* stream) {
@@ -86,10 +114,11 @@ extern "C" int spx_dispatch_static(const spx_layer_dims* dims, const int64_t* ex
   const int experts = dims->num_experts;
   if (tokens < 1 || k < 1 || experts < 1 || k > experts) return SPX_ERR_INVALID_ARG;
   if (tokens * k > kStaticMaxPairs || experts > kStaticMaxExperts) return SPX_ERR_SCRATCH_LIMIT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = check_stream_device(st); rc != SPX_OK) return rc;
   void* base = nullptr;
   if (int rc = static_scratch(&base); rc != SPX_OK) return rc;
   uint8_t* s = static_cast<uint8_t*>(base);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   int* small = reinterpret_cast<int*>(s + kOffSmall);
   if (cudaMemsetAsync(small, 0, 64, st) != cudaSuccess) return SPX_ERR_CUDA;
   DispatchArgs a{};

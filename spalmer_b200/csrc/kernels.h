@@ -176,6 +176,7 @@ int ensure_max_dynamic_smem(const void* func);
 int device_max_pairs(const void* func, size_t smem);
 
 int launch_softplus_table(uint16_t* lut, cudaStream_t stream);
+int launch_scores_from_logits(uint16_t* values, int64_t n, const uint16_t* lut, cudaStream_t stream);
 size_t route_select_smem(int num_experts);
 int launch_route(const RouteArgs& a, cudaStream_t stream);
 int route_lb_blocks(int64_t tokens);  // rows of the route kernel's load-balance partials

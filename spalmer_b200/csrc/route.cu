@@ -27,6 +27,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "kernels.h"
 #include "sm100.cuh"
 #include "topk_exact.cuh"
@@ -666,6 +668,34 @@ __global__ void __launch_bounds__(kTieWarps * 32) route_ties_kernel(const RouteA
 
 int launch_softplus_table(uint16_t* lut, cudaStream_t stream) {
   softplus_table_kernel<<<256, 256, 0, stream>>>(lut);
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+// Router scores from logits in place: v = lut[v] for every BF16 value
+// (F.softplus on BF16, experts/router.py:56), eight values per 16-byte load.
+__global__ void scores_from_logits_kernel(uint16_t* __restrict__ v, int64_t n, const uint16_t* __restrict__ lut) {
+  const int64_t n8 = n / 8;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  uint4* v8 = reinterpret_cast<uint4*>(v);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8; i += stride) {
+    uint4 q = v8[i];
+    uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      w[j] = static_cast<uint32_t>(__ldg(lut + (w[j] & 0xFFFFu))) |
+             (static_cast<uint32_t>(__ldg(lut + (w[j] >> 16))) << 16);
+    v8[i] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  for (int64_t i = n8 * 8 + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n; i += stride)
+    v[i] = __ldg(lut + v[i]);
+}
+
+int launch_scores_from_logits(uint16_t* values, int64_t n, const uint16_t* lut, cudaStream_t stream) {
+  if (n <= 0) return SPX_OK;
+  if ((reinterpret_cast<uintptr_t>(values) & 15u) != 0) return SPX_ERR_ALIGNMENT;
+  int64_t blocks = (n / 8 + 255) / 256;
+  blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, static_cast<int64_t>(device_sm_count()) * 8));
+  scores_from_logits_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(values, n, lut);
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 

@@ -66,15 +66,103 @@ class SurpriseRouter(nn.Module):
         return self.config.d_model
 
     def forward(self, hidden_states: Tensor) -> Tensor:
-        """Predicted surprise ``[..., experts]`` through the B200 router GEMM."""
+        """Predicted surprise ``[..., experts]`` (experts/router.py:40-56):
+        ``softplus(x @ W^T + b)`` in BF16, or the logits for the legacy
+        identity transform, through ``spx_router_forward`` (the layer's
+        tcgen05 router GEMM, then the BF16 softplus table).  Under autograd the
+        gradients of x, W and b follow the reference's autograd steps."""
 
         if hidden_states.shape[-1] != self.config.d_model:
             raise ValueError(
                 f"expected trailing dimension {self.config.d_model}, got {hidden_states.shape[-1]}"
             )
-        raise NotImplementedError(
-            "the standalone router forward runs inside B200MicroExpertChannelMixer.forward"
-        )
+        params = [self.proj.weight] + ([self.proj.bias] if self.proj.bias is not None else [])
+        if torch.is_grad_enabled() and (hidden_states.requires_grad or any(p.requires_grad for p in params)):
+            return _RouterFunction.apply(self, hidden_states, *params)
+        return self._scores(hidden_states, identity=False)
+
+    def _scores(self, hidden_states: Tensor, *, identity: bool) -> Tensor:
+        d, E = self.config.d_model, self.num_experts
+        device = hidden_states.device
+        if device.type != "cuda":
+            raise RuntimeError(f"the B200 router executes CUDA tensors; hidden states are on {device}")
+        w, b = self.proj.weight, self.proj.bias
+        if hidden_states.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+            raise RuntimeError(
+                f"the B200 router executes BF16; hidden states are {hidden_states.dtype}, weight {w.dtype}"
+            )
+        if w.device != device:
+            raise RuntimeError(f"router weight is on {w.device}, hidden states on {device}")
+        lead = hidden_states.shape[:-1]
+        x = hidden_states.reshape(-1, d).contiguous()
+        T = x.shape[0]
+        out = torch.empty(T, E, dtype=torch.bfloat16, device=device)
+        if T == 0:
+            return out.reshape(*lead, E)
+        lib = _lib.load()
+        transform = 1 if identity or self.config.router_score_transform == "identity" else 0
+        dims = _lib.LayerDims(tokens=T, d_model=d, num_experts=E, inter_dim=16, shared_dim=0, top_k=1,
+                              score_transform=transform, execution_loop=0, mxfp8_lane=0)
+        small = T <= SMALL_BATCH_TOKENS
+        key = (device, small, w.data_ptr(), w._version)
+        cache = self.__dict__.setdefault("_router_pack", {})
+        packed = cache.get(small)
+        if packed is None or packed[0] != key:
+            sizes = _lib.PackedSizes()
+            _lib.check(lib.spx_layer_sizes(dims, None, sizes), "spx_layer_sizes")
+            pw = torch.empty(max(1, sizes.router_weight), dtype=torch.int16, device=device)
+            wb = w.detach().contiguous()
+            src = _lib.ReferenceWeights(router_weight=wb.data_ptr())
+            _lib.check(lib.spx_pack_weights(dims, src, pw.data_ptr(), None, None, None, None,
+                                            torch.cuda.current_stream(device).cuda_stream), "spx_pack_weights (router)")
+            packed = (key, pw, wb)
+            cache[small] = packed
+        nbytes = _lib.ctypes.c_size_t()
+        _lib.check(lib.spx_router_sizes(dims, nbytes), "spx_router_sizes")
+        ws = self.__dict__.get("_router_ws")
+        if ws is None or ws.device != device or ws.numel() < nbytes.value:
+            ws = torch.zeros(nbytes.value, dtype=torch.uint8, device=device)
+            self.__dict__["_router_ws"] = ws
+        bias = None if b is None else b.detach().to(torch.bfloat16).contiguous()
+        pwt = _lib.PackedWeights(router_weight=packed[1].data_ptr(), router_bias=_lib.ptr(bias),
+                                 softplus_table=_lib.ptr(softplus_table(device)) if transform == 0 else None)
+        _lib.check(lib.spx_router_forward(dims, pwt, x.data_ptr(), out.data_ptr(), ws.data_ptr(),
+                                          torch.cuda.current_stream(device).cuda_stream), "spx_router_forward")
+        return out.reshape(*lead, E)
+
+
+class _RouterFunction(torch.autograd.Function):
+    """Router scores with gradients: forward through libspx; backward as the
+    reference's autograd computes it for ``softplus(F.linear(x, W, b))`` in
+    BF16 (d logits = bf16(g * sigmoid(logits)) for softplus, then the linear
+    layer's input, weight and bias gradients)."""
+
+    @staticmethod
+    def forward(ctx, router, hidden_states, *params):
+        softplus = router.config.router_score_transform != "identity"
+        logits = router._scores(hidden_states, identity=True) if softplus else None
+        scores = router._scores(hidden_states, identity=False)
+        ctx.save_for_backward(hidden_states, logits, *params)
+        ctx.softplus = softplus
+        ctx.has_bias = len(params) > 1
+        return scores
+
+    @staticmethod
+    def backward(ctx, grad):
+        x, logits, *params = ctx.saved_tensors
+        w = params[0]
+        g = grad
+        if ctx.softplus:  # F.softplus backward (beta 1, threshold 20)
+            z = logits.float()
+            g = torch.where(z > 20.0, grad.float(), grad.float() * torch.sigmoid(z)).to(grad.dtype)
+        g2 = g.reshape(-1, g.shape[-1])
+        x2 = x.reshape(-1, x.shape[-1])
+        dx = (g2 @ w).reshape(x.shape) if ctx.needs_input_grad[1] else None
+        dw = g2.t() @ x2 if ctx.needs_input_grad[2] else None
+        out = [None, dx, dw]
+        if ctx.has_bias:
+            out.append(g2.sum(0) if ctx.needs_input_grad[3] else None)
+        return tuple(out)
 
 
 class MicroExpertBank(nn.Module):
@@ -213,6 +301,155 @@ class MicroExpertBank(nn.Module):
 
     def _clear_expert_offload(self) -> None:
         object.__setattr__(self, "_offload", None)
+
+    # ---- the bank seam: execute given routing pairs (bank.py:593-646)
+    def execute_routing(self, hidden_states: Tensor, token_index: Tensor, expert_index: Tensor,
+                        routing_weights: Tensor, promoted_mask: Tensor | None = None,
+                        resident_ids: Tensor | None = None) -> Tensor:
+        """Execute only the selected (token, expert) pairs and return the
+        ``[num_tokens, d_model]`` weighted combination of their updates
+        (``MicroExpertBank.execute_routing``, experts/bank.py:593-646).
+
+        The pairs' rows are gathered (``spx_gather_rows``), run through the
+        grouped tcgen05 expert GEMMs unweighted in a stable per-expert order
+        (``spx_experts_forward``; experts whose precision pair under
+        ``promoted_mask`` is MXFP8/NVFP4 run in that lane), and each token's
+        pairs are summed as ``bf16(bf16(out) * w)`` in pair order with an FP32
+        accumulator (``spx_combine``), where the reference index_adds in BF16.
+        ``resident_ids`` only restricts which groups the reference's grouped
+        path visits; pairs name their experts, so the result does not depend
+        on it.  One host read (the largest number of pairs of one token) sizes
+        the combine's slot table; the reference's grouped path reads its
+        counts on the host as well.
+        """
+
+        if self._offload is not None:
+            raise RuntimeError("execute_routing on an offloaded bank: run the layer forward, which pages experts")
+        e, d = self.num_experts, self.config.d_model
+        if hidden_states.ndim != 2 or hidden_states.shape[1] != d:
+            raise ValueError(f"hidden_states must be [num_tokens, {d}], got {tuple(hidden_states.shape)}")
+        device = hidden_states.device
+        if device.type != "cuda":
+            raise RuntimeError(f"the B200 expert bank executes CUDA tensors; hidden states are on {device}")
+        weight_fmt = self.config.expert_weight_format
+        if weight_fmt == "float32":
+            raise NativeExpertPrecisionError("no B200 kernel for float32 experts; emulation is prohibited")
+        if hidden_states.dtype != torch.bfloat16:
+            raise RuntimeError(
+                f"{weight_fmt}/{self.config.expert_activation_format} expert execution requires "
+                f"torch.bfloat16 hidden states, got {hidden_states.dtype}"
+            )
+        P = token_index.numel()
+        if token_index.shape != (P,) or expert_index.shape != (P,) or routing_weights.shape != (P,):
+            raise ValueError("token_index, expert_index and routing_weights must be matching 1-D tensors")
+        N = hidden_states.shape[0]
+        out = torch.zeros(N, d, dtype=torch.bfloat16, device=device)
+        if P == 0 or N == 0:
+            return out
+        lib = _lib.load()
+        stream = torch.cuda.current_stream(device).cuda_stream
+        x = hidden_states.contiguous()
+        tok32 = token_index.to(device=device, dtype=torch.int32).contiguous()
+        rows = torch.empty(P, d, dtype=torch.bfloat16, device=device)
+        _lib.check(lib.spx_gather_rows(x.data_ptr(), d, tok32.data_ptr(), 1, P, d, rows.data_ptr(), d, stream),
+                   "spx_gather_rows")
+        dims = self._pair_dims(P)
+        pw = self._packed_experts(device, dims)
+        lanes = self._lanes_of(promoted_mask, device)
+        if lanes is not None:
+            mx = pw["mx"]
+            pw["weights"].expert_lane_mxfp8 = lanes.data_ptr()
+            pw["weights"].expert_w1_mx = _lib.ptr(mx["expert_w1_mx"])
+            pw["weights"].expert_w1_mx_scales = _lib.ptr(mx["expert_w1_mx_scales"])
+            pw["weights"].expert_w2_mx = _lib.ptr(mx["expert_w2_mx"])
+            pw["weights"].expert_w2_mx_scales = _lib.ptr(mx["expert_w2_mx_scales"])
+            pw["weights"].expert_nvfp4_amax = _lib.ptr(mx.get("expert_nvfp4_amax"))
+        else:
+            pw["weights"].expert_lane_mxfp8 = None
+        nbytes = _lib.ctypes.c_size_t()
+        _lib.check(lib.spx_layer_sizes(dims, nbytes, None), "spx_layer_sizes")
+        ws = torch.zeros(nbytes.value, dtype=torch.uint8, device=device)
+        ids = expert_index.to(device=device, dtype=torch.int64).contiguous()
+        y = torch.empty(P, d, dtype=torch.bfloat16, device=device)
+        _lib.check(lib.spx_experts_forward(dims, pw["weights"], rows.data_ptr(), ids.data_ptr(), y.data_ptr(),
+                                           ws.data_ptr(), stream), "spx_experts_forward")
+        status = _lib.ctypes.c_int(0)
+        _lib.check(lib.spx_workspace_status(ws.data_ptr(), status, 1, stream), "spx_workspace_status")
+        if status.value != 0:
+            raise RuntimeError(f"expert kernels reported device status {status.value} (expert id out of range?)")
+        # per token, its pairs in pair order: slot table [N, slots], -1 = empty
+        tok = token_index.to(device=device, dtype=torch.int64)
+        counts = torch.bincount(tok, minlength=N)
+        slots = int(counts.max())
+        perm = torch.argsort(tok, stable=True)
+        starts = torch.cumsum(counts, 0) - counts
+        slot = torch.arange(P, device=device) - starts[tok[perm]]
+        table = torch.full((N * slots,), -1, dtype=torch.int32, device=device)
+        table[tok[perm] * slots + slot] = perm.to(torch.int32)
+        wtab = torch.zeros(N * slots, dtype=torch.bfloat16, device=device)
+        wtab[tok[perm] * slots + slot] = routing_weights.to(device=device, dtype=torch.bfloat16)[perm]
+        table, wtab = table.view(N, slots), wtab.view(N, slots)
+        base = None
+        for j0 in range(0, slots, _MAX_COMBINE_SLOTS):  # the combine adds up to 20 slots per pass
+            j1 = min(slots, j0 + _MAX_COMBINE_SLOTS)
+            t_part, w_part = table[:, j0:j1].contiguous(), wtab[:, j0:j1].contiguous()
+            res = torch.empty(N, d, dtype=torch.bfloat16, device=device)
+            _lib.check(lib.spx_combine(y.data_ptr(), t_part.data_ptr(), w_part.data_ptr(), _lib.ptr(base), N, d,
+                                       j1 - j0, res.data_ptr(), stream), "spx_combine")
+            base = res
+        return base
+
+    def _pair_dims(self, pairs: int) -> _lib.LayerDims:
+        dims = layer_dims(self.config, pairs, 1)
+        dims.shared_dim = 0
+        return dims
+
+    def _lanes_of(self, promoted_mask: Tensor | None, device: torch.device) -> Tensor | None:
+        unpromoted, promoted = _lane_of(self.config, False), _lane_of(self.config, True)
+        if unpromoted == 0 and (promoted == 0 or promoted_mask is None):
+            return None
+        if promoted_mask is None:
+            return torch.ones(self.num_experts, dtype=torch.uint8, device=device)
+        if promoted_mask.shape != (self.num_experts,):
+            raise ValueError(f"promoted_mask must have shape ({self.num_experts},)")
+        m = promoted_mask.to(device=device, dtype=torch.bool)
+        return torch.where(m, int(promoted != 0), int(unpromoted != 0)).to(torch.uint8).contiguous()
+
+    def _packed_experts(self, device: torch.device, dims: _lib.LayerDims) -> dict:
+        """Kernel layouts of the expert masters for the bank seam (one cache
+        entry per batch class, invalidated when a master changes)."""
+
+        small = dims.tokens <= SMALL_BATCH_TOKENS
+        masters = (self.gate_proj, self.up_proj, self.down_proj)
+        key = (device, small, dims.mxfp8_lane) + tuple((t.data_ptr(), t._version) for t in masters)
+        cache = self.__dict__.setdefault("_seam_pack", {})
+        hit = cache.get(small)
+        if hit is not None and hit["key"] == key:
+            return hit
+        for t in masters:
+            if t.device != device or t.dtype != torch.bfloat16:
+                raise RuntimeError(f"expert masters must be BF16 on {device}; got {t.dtype} on {t.device}")
+        lib = _lib.load()
+        sizes = _lib.PackedSizes()
+        _lib.check(lib.spx_layer_sizes(dims, None, sizes), "spx_layer_sizes")
+        stream = torch.cuda.current_stream(device).cuda_stream
+        gate, up, down = (t.detach().contiguous() for t in masters)
+        dummy_router = torch.zeros(self.num_experts, self.config.d_model, dtype=torch.bfloat16, device=device)
+        router_out = torch.empty(max(1, sizes.router_weight), dtype=torch.int16, device=device)
+        w1 = torch.empty(max(1, sizes.expert_w1), dtype=torch.int16, device=device)
+        w2 = torch.empty(max(1, sizes.expert_w2), dtype=torch.int16, device=device)
+        src = _lib.ReferenceWeights(router_weight=dummy_router.data_ptr(), gate_proj=gate.data_ptr(),
+                                    up_proj=up.data_ptr(), down_proj=down.data_ptr())
+        _lib.check(lib.spx_pack_weights(dims, src, router_out.data_ptr(), w1.data_ptr(), w2.data_ptr(), None, None,
+                                        stream), "spx_pack_weights (experts)")
+        mx = {}
+        if dims.mxfp8_lane:
+            mx = pack_lowp_experts(dims, src, sizes, lambda n: torch.empty(n, dtype=torch.uint8, device=device),
+                                   stream)
+        weights = _lib.PackedWeights(expert_w1=w1.data_ptr(), expert_w2=w2.data_ptr())
+        entry = {"key": key, "weights": weights, "mx": mx, "keep": (gate, up, down, dummy_router, router_out, w1, w2)}
+        cache[small] = entry
+        return entry
 
 
 class SwiGLU(nn.Module):
@@ -353,6 +590,8 @@ def softplus_table(device: torch.device) -> Tensor:
 
 # Batches of at most this many tokens use the decode tile shapes (kSmallBatchTokens in libspx).
 SMALL_BATCH_TOKENS = 256
+# Slots one spx_combine pass adds per token (kMaxTopK in libspx).
+_MAX_COMBINE_SLOTS = 20
 
 
 def layer_dims(config: MicroExpertsConfig, tokens: int, top_k: int) -> _lib.LayerDims:

@@ -18,7 +18,8 @@ if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 
 GOLDEN = ROOT / "tests" / "golden"
-LAYER_CASES = ("smoke", "m10_slice", "m100_slice", "k2_routed_only", "bias_resident", "tiny_identity")
+LAYER_CASES = ("smoke", "m10_slice", "m100_slice", "k2_routed_only", "bias_resident", "tiny_identity",
+               "smoke_loop", "m10_loop")
 
 
 def pytest_configure(config):

@@ -2,7 +2,7 @@
 
 Run in the build container, where the reference source is importable::
 
-    python tests/golden/make_golden.py /path/to/reference/src
+    python tests/golden/make_golden.py /path/to/reference/src [--only name,name]
 
 It writes small ``.npz`` fixtures next to this file.  The GPU box never runs
 this script; tests there read only the committed fixtures.
@@ -54,6 +54,14 @@ LAYER_CASES = {
                                    shared_inter_dim=64, active_experts=8, router_bias=True,
                                    max_resident_experts=64),
                           shape=(2, 128), bias_zipf=1.0, resident=40),
+    # The loop executor (experts/bank.py:674-703): per-expert execution, index_add in
+    # ascending expert order, loop telemetry (padded pairs = real pairs).
+    "smoke_loop": dict(cfg=dict(d_model=128, num_experts=200, expert_inter_dim=32,
+                                shared_inter_dim=128, active_experts=4, expert_execution="loop"),
+                       shape=(2, 256)),
+    "m10_loop": dict(cfg=dict(d_model=256, num_experts=200, expert_inter_dim=64,
+                              shared_inter_dim=256, active_experts=8, expert_execution="loop"),
+                     shape=(2, 128)),
     # Tiny bank like the reference's unit tests, legacy identity scores.
     "tiny_identity": dict(cfg=dict(d_model=16, num_experts=6, expert_inter_dim=8,
                                    active_experts=2, router_score_transform="identity"),
@@ -164,12 +172,18 @@ def main() -> None:
     if len(sys.argv) > 1:
         sys.path.insert(0, sys.argv[1])
     torch.set_num_threads(max(1, torch.get_num_threads()))
+    only = None
+    if "--only" in sys.argv:
+        only = set(sys.argv[sys.argv.index("--only") + 1].split(","))
     for name, spec in LAYER_CASES.items():
+        if only is not None and name not in only:
+            continue
         arrays = make_layer(name, spec)
         np.savez_compressed(HERE / f"layer_{name}.npz", **arrays)
         print("wrote", name)
-    np.savez_compressed(HERE / "topk_ties.npz", **make_topk())
-    print("wrote topk_ties")
+    if only is None:
+        np.savez_compressed(HERE / "topk_ties.npz", **make_topk())
+        print("wrote topk_ties")
 
 
 if __name__ == "__main__":

@@ -150,7 +150,8 @@ def test_layer_end_to_end_against_reference(name):
     # Against the oracle given the GPU's own routing: tolerance on every element.
     params = oracle_params(mixer)
     weights = bf16_bits(out.metrics["routing_weights"]).reshape(-1, k)
-    routed, _, _ = R.grouped_experts(arrays["x"], ids, weights, params.gate, params.up, params.down)
+    routed, _, _ = R.grouped_experts(arrays["x"], ids, weights, params.gate, params.up, params.down,
+                                     execution=meta["config"]["expert_execution"])
     want = routed
     if params.shared_gate is not None:
         shared = R.shared_swiglu(arrays["x"], params.shared_gate, params.shared_up, params.shared_down)
