@@ -316,11 +316,11 @@ class MicroExpertBank(nn.Module):
         ``promoted_mask`` is MXFP8/NVFP4 run in that lane), and each token's
         pairs are summed as ``bf16(bf16(out) * w)`` in pair order with an FP32
         accumulator (``spx_combine``), where the reference index_adds in BF16.
-        ``resident_ids`` only restricts which groups the reference's grouped
-        path visits; pairs name their experts, so the result does not depend
-        on it.  One host read (the largest number of pairs of one token) sizes
-        the combine's slot table; the reference's grouped path reads its
-        counts on the host as well.
+        With ``resident_ids`` the grouped executor runs only the groups of
+        those experts (bank.py:725-731): pairs of other experts contribute
+        nothing; the loop executor runs every pair.  One host read (the
+        largest number of pairs of one token) sizes the combine's slot table;
+        the reference's grouped path reads its counts on the host as well.
         """
 
         if self._offload is not None:
@@ -343,6 +343,10 @@ class MicroExpertBank(nn.Module):
         if token_index.shape != (P,) or expert_index.shape != (P,) or routing_weights.shape != (P,):
             raise ValueError("token_index, expert_index and routing_weights must be matching 1-D tensors")
         N = hidden_states.shape[0]
+        if resident_ids is not None and self.config.expert_execution == "grouped" and P > 0:
+            keep = torch.isin(expert_index.to(device), resident_ids.to(device=device, dtype=torch.long))
+            token_index, expert_index, routing_weights = token_index[keep], expert_index[keep], routing_weights[keep]
+            P = token_index.numel()
         out = torch.zeros(N, d, dtype=torch.bfloat16, device=device)
         if P == 0 or N == 0:
             return out
