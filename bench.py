@@ -756,8 +756,9 @@ def run_decode(args) -> None:
     per_t = {}
     clocks = None
     e2e = {}
+    token_counts = [args.tokens] if args.tokens else list(spec["decode_tokens"])
     with torch.inference_mode():
-        for T in spec["decode_tokens"]:
+        for T in token_counts:
             x_host = torch.randn(1, T, config.d_model, generator=torch.Generator().manual_seed(1 + rank))
             x_host = x_host.to(torch.bfloat16).pin_memory()
             x_static = x_host.to(device)
@@ -778,7 +779,7 @@ def run_decode(args) -> None:
             torch.cuda.synchronize()
             if world > 1:
                 dist.barrier()
-            sampler = ClockSampler(local) if T == spec["decode_tokens"][-1] else None
+            sampler = ClockSampler(local) if T == token_counts[-1] else None
             t0 = torch.cuda.Event(enable_timing=True)
             t1 = torch.cuda.Event(enable_timing=True)
             t0.record()
@@ -805,7 +806,7 @@ def run_decode(args) -> None:
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
             per_t[T] = (float(t[0]), float(t[1]))
             del graph
-    T = spec["decode_tokens"][-1]
+    T = token_counts[-1]
     ms, e2e_ms = per_t[T]
     if rank == 0:
         pk = peaks()
@@ -1099,6 +1100,8 @@ def main() -> None:
     ap.add_argument("--config", default="m100", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="decode configs: run this one token count per step instead of the configuration's list")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -558,6 +558,49 @@ int stage_expert_gemms(const Ctx& c, const uint16_t* xa, const int* src_row, con
   return SPX_OK;
 }
 
+// Decode-sized batches: the expert projections as grouped GEMVs (gemv.cu), both
+// lanes in one launch per projection; same outputs as stage_expert_gemms.
+GemvArgs gemv_args(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, const DispatchArgs& da) {
+  const Shape& s = c.s;
+  GemvArgs g{};
+  g.counts = da.counts;
+  g.starts = da.starts;
+  g.src_row = da.src_row;
+  g.sorted_w = da.sorted_weights;
+  g.lane_mx = da.lane_mx;
+  g.num_experts = s.E;
+  g.d = s.d;
+  g.inter = s.I;
+  g.kd = s.kd;
+  g.chunk = s.c;
+  g.nc = s.nc;
+  g.kp = s.kp;
+  g.x = xa;
+  g.ldx = s.kd;
+  g.w1 = w->expert_w1;
+  g.w2 = w->expert_w2;
+  g.hid = at<uint16_t>(c.ws, c.L.hidden);
+  g.y = at<uint16_t>(c.ws, c.L.y);
+  if (da.lane_mx != nullptr) {
+    g.xq = at<uint8_t>(c.ws, c.L.x_q);
+    g.xsf = at<uint8_t>(c.ws, c.L.x_sf);
+    g.kx = s.kx;
+    g.cm = s.cm;
+    g.ncm = s.ncm;
+    g.kh = s.kh;
+    g.bn2m = s.bn2m;
+    g.w1q = w->expert_w1_mx;
+    g.w1sf = w->expert_w1_mx_scales;
+    g.w2q = w->expert_w2_mx;
+    g.w2sf = w->expert_w2_mx_scales;
+    g.hq = at<uint8_t>(c.ws, c.L.h_q);
+    g.hsf = at<uint8_t>(c.ws, c.L.h_sf);
+  }
+  return g;
+}
+
+bool use_gemv(const Ctx& c, const GemvArgs& g) { return c.s.P <= kGemvMaxPairs && !c.s.nv && gemv_supported(g); }
+
 // K3: expert GEMM1 (+SwiGLU) and GEMM2 over the dispatched rows of `hidden`
 // (`xa` = hidden padded), both lanes; weighted rows land in Y (sorted order).
 int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hidden, const uint16_t* xa,
@@ -566,6 +609,13 @@ int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hid
   if (mx) {
     const int rc = c.s.nv ? stage_quantize_nv_x(c, hidden, ld_hidden, da) : stage_quantize_x(c, hidden, ld_hidden);
     if (rc != SPX_OK) return rc;
+  }
+  if (const GemvArgs g = gemv_args(c, w, xa, da); use_gemv(c, g)) {
+    if (int rc = launch_gemv_experts(g, c.st, 1); rc != SPX_OK) return rc;
+    c.mark(4);
+    if (int rc = launch_gemv_experts(g, c.st, 2); rc != SPX_OK) return rc;
+    c.mark(5);
+    return SPX_OK;
   }
   const ExpertPass p{w->expert_w1, w->expert_w2, w->expert_w1_mx, w->expert_w1_mx_scales, w->expert_w2_mx,
                      w->expert_w2_mx_scales, c.s.E, da.tiles, da.num_tiles, mx ? da.tiles_mx : nullptr,

@@ -312,6 +312,38 @@ int launch_pack_w2(const uint16_t* down, int experts, int inter, int d, int kp, 
                    cudaStream_t stream);
 int launch_pad_rows(const uint16_t* src, int64_t rows, int cols, int ld_out, uint16_t* out, cudaStream_t stream);
 
+// Decode-sized expert GEMVs (gemv.cu): both precision lanes in one launch per
+// projection, rows of each expert = its dispatch range.
+constexpr int64_t kGemvMaxPairs = 1024;  // routed pairs up to which the layer uses the GEMVs
+struct GemvArgs {
+  const int* counts;          // [E] rows per expert (dispatch)
+  const int* starts;          // [E] first dispatch position of each expert
+  const int* src_row;         // [P] token row of each dispatch position
+  const uint16_t* sorted_w;   // [P] routing weight per dispatch position, or null (unit weights)
+  const uint8_t* lane_mx;     // [E] 1 = MXFP8 lane, or null (every expert BF16)
+  int num_experts, d, inter;  // E, d_model, I
+  int kd, chunk, nc, kp;      // BF16 packing: d padded, GEMM1 chunk, chunks, hidden width padded
+  const uint16_t* x;          // [T][kd] hidden rows (K-padded)
+  int64_t ldx;
+  const uint16_t* w1;         // [E][nc*2*chunk][kd]
+  const uint16_t* w2;         // [E][d][kp]
+  uint16_t* hid;              // [P][kp] BF16 hidden rows (BF16 lane)
+  uint16_t* y;                // [P][d] weighted expert rows
+  // MXFP8 lane
+  const uint8_t* xq;          // [T][kx] E4M3
+  const uint8_t* xsf;         // [T][kx/32] E8M0
+  int kx, cm, ncm, kh, bn2m;
+  const uint8_t* w1q;         // [E][ncm*2*cm][kx]
+  const uint8_t* w1sf;        // scale atoms
+  const uint8_t* w2q;         // [E][d][kh]
+  const uint8_t* w2sf;
+  uint8_t* hq;                // [P][kh] E4M3 hidden rows
+  uint8_t* hsf;               // [P][kh/32]
+};
+bool gemv_supported(const GemvArgs& a);
+// which = 1: gate/up + SwiGLU into hid / hq; which = 2: down projection + weights into y.
+int launch_gemv_experts(const GemvArgs& a, cudaStream_t stream, int which);
+
 // Backward (backward.cu).
 struct BwdRouterArgs {
   const uint16_t* scores;     // [T, E] router scores (BF16)
