@@ -285,9 +285,31 @@ int stage_pad(const Ctx& c, const uint16_t* hidden, const uint16_t** xa) {
   return SPX_OK;
 }
 
-// K1: router logits (tcgen05 GEMM, bias fused) into `lg`.
+// Dense GEMV pass for decode-sized batches: rows = the batch's tokens.
+GemvPass dense_rows_pass(const Ctx& c, const uint16_t* a, int64_t lda, int k, int k_valid, const uint16_t* w, int n,
+                         const uint16_t* bias, uint16_t* out, int64_t ldo) {
+  GemvPass g{};
+  g.dense_rows = static_cast<int>(c.s.T);
+  g.status = c.status;
+  g.a2 = a;
+  g.lda2 = lda;
+  g.k2 = k;
+  g.k_valid2 = k_valid;
+  g.w2 = w;
+  g.n_out = n;
+  g.bias = bias;
+  g.out = out;
+  g.ldo = ldo;
+  return g;
+}
+
+// K1: router logits (tcgen05 GEMM, bias fused) into `lg`; a GEMV for decode-sized batches.
 int stage_router(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, uint16_t* lg) {
   const Shape& s = c.s;
+  if (s.T <= kGemvMaxTokens) {
+    const GemvPass g = dense_rows_pass(c, xa, s.kd, s.kd, s.kd, w->router_weight, s.E, w->router_bias, lg, s.E);
+    if (gemv_rows_ok(g)) return launch_gemv_rows(g, c.st);
+  }
   GemmArgs g = base_args(kEpiStore, s.bn_router, s.kd / 64, c.status);
   if (int rc = encode_2d(&g.tma_a, xa, s.T, s.kd, s.kd, kTileRows); rc != SPX_OK) return rc;
   if (int rc = encode_3d(&g.tma_b, w->router_weight, 1, s.E, s.kd, s.bn_router); rc != SPX_OK) return rc;
@@ -394,6 +416,65 @@ int stage_quantize_x(const Ctx& c, const uint16_t* hidden, int64_t ld_hidden) {
                                  s.kx, at<uint8_t>(c.ws, c.L.x_sf), s.kx / kMxBlock, c.st);
 }
 
+// Decode-sized batches (<= kGemvMaxPairs routed pairs): the expert projections
+// of a pass as grouped GEMVs (gemv.cu) over the same tile tables, both lanes in
+// one launch per projection; same outputs as the GEMMs below.  Returns 1 when
+// the pass does not qualify (NVFP4 lane, peer row pointers, shapes).
+int expert_gemvs(const Ctx& c, const uint16_t* xa, const int* src_row, const uint16_t* sorted_w,
+                 const ExpertPass& p) {
+  const Shape& s = c.s;
+  if (s.P > kGemvMaxPairs || s.nv || p.row_out != nullptr || p.a_rows != nullptr || xa == nullptr) return 1;
+  GemvPass g{};
+  g.tiles = p.tiles;
+  g.num_tiles = p.num_tiles;
+  g.tiles_mx = p.tiles_mx;
+  g.num_tiles_mx = p.num_tiles_mx;
+  g.max_tiles = s.max_tiles;
+  g.src_row = src_row;
+  g.status = c.status;
+  g.d = s.d;
+  g.inter = s.I;
+  g.kd = s.kd;
+  g.chunk = s.c;
+  g.nc = s.nc;
+  g.x = xa;
+  g.ldx = s.kd;
+  g.w1 = p.w1;
+  g.hid = at<uint16_t>(c.ws, c.L.hidden);
+  g.ldh = s.kp;
+  g.a2 = g.hid;
+  g.lda2 = s.kp;
+  g.k2 = s.kp;
+  g.k_valid2 = s.I;
+  g.w2 = p.w2;
+  g.n_out = s.d;
+  g.row_w = sorted_w;
+  g.out = at<uint16_t>(c.ws, c.L.y);
+  g.ldo = s.d;
+  if (p.tiles_mx != nullptr) {
+    g.xq = at<uint8_t>(c.ws, c.L.x_q);
+    g.xsf = at<uint8_t>(c.ws, c.L.x_sf);
+    g.kx = s.kx;
+    g.cm = s.cm;
+    g.ncm = s.ncm;
+    g.kh = s.kh;
+    g.bn2m = s.bn2m;
+    g.w1q = p.w1_mx;
+    g.w1sf = p.w1_mx_sf;
+    g.w2q = p.w2_mx;
+    g.w2sf = p.w2_mx_sf;
+    g.hq = at<uint8_t>(c.ws, c.L.h_q);
+    g.hsf = at<uint8_t>(c.ws, c.L.h_sf);
+  }
+  if (!gemv_swiglu_ok(g) || !gemv_rows_ok(g)) return 1;
+  if (int rc = launch_gemv_swiglu(g, c.st); rc != SPX_OK) return rc;
+  c.mark(4);
+  g.src_row = nullptr;  // the down projection reads the hidden rows in dispatch order
+  if (int rc = launch_gemv_rows(g, c.st); rc != SPX_OK) return rc;
+  c.mark(5);
+  return SPX_OK;
+}
+
 // K3 GEMMs: expert GEMM1 (+SwiGLU) and GEMM2 over the tiles of `p`, rows
 // gathered from `xa` through src_row; weighted rows land in Y (sorted order).
 int stage_expert_gemms(const Ctx& c, const uint16_t* xa, const int* src_row, const uint16_t* sorted_w,
@@ -402,6 +483,8 @@ int stage_expert_gemms(const Ctx& c, const uint16_t* xa, const int* src_row, con
   void* ws = c.ws;
   const Layout& L = c.L;
   int rc = SPX_OK;
+  if ((rc = expert_gemvs(c, xa, src_row, sorted_w, p)) != 1) return rc;
+  rc = SPX_OK;
   const bool mx = p.tiles_mx != nullptr && !s.nv;
   const bool nv = p.tiles_mx != nullptr && s.nv;
   float* nv_amax_x = at<float>(ws, L.nv_amax);
@@ -558,49 +641,6 @@ int stage_expert_gemms(const Ctx& c, const uint16_t* xa, const int* src_row, con
   return SPX_OK;
 }
 
-// Decode-sized batches: the expert projections as grouped GEMVs (gemv.cu), both
-// lanes in one launch per projection; same outputs as stage_expert_gemms.
-GemvArgs gemv_args(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, const DispatchArgs& da) {
-  const Shape& s = c.s;
-  GemvArgs g{};
-  g.counts = da.counts;
-  g.starts = da.starts;
-  g.src_row = da.src_row;
-  g.sorted_w = da.sorted_weights;
-  g.lane_mx = da.lane_mx;
-  g.num_experts = s.E;
-  g.d = s.d;
-  g.inter = s.I;
-  g.kd = s.kd;
-  g.chunk = s.c;
-  g.nc = s.nc;
-  g.kp = s.kp;
-  g.x = xa;
-  g.ldx = s.kd;
-  g.w1 = w->expert_w1;
-  g.w2 = w->expert_w2;
-  g.hid = at<uint16_t>(c.ws, c.L.hidden);
-  g.y = at<uint16_t>(c.ws, c.L.y);
-  if (da.lane_mx != nullptr) {
-    g.xq = at<uint8_t>(c.ws, c.L.x_q);
-    g.xsf = at<uint8_t>(c.ws, c.L.x_sf);
-    g.kx = s.kx;
-    g.cm = s.cm;
-    g.ncm = s.ncm;
-    g.kh = s.kh;
-    g.bn2m = s.bn2m;
-    g.w1q = w->expert_w1_mx;
-    g.w1sf = w->expert_w1_mx_scales;
-    g.w2q = w->expert_w2_mx;
-    g.w2sf = w->expert_w2_mx_scales;
-    g.hq = at<uint8_t>(c.ws, c.L.h_q);
-    g.hsf = at<uint8_t>(c.ws, c.L.h_sf);
-  }
-  return g;
-}
-
-bool use_gemv(const Ctx& c, const GemvArgs& g) { return c.s.P <= kGemvMaxPairs && !c.s.nv && gemv_supported(g); }
-
 // K3: expert GEMM1 (+SwiGLU) and GEMM2 over the dispatched rows of `hidden`
 // (`xa` = hidden padded), both lanes; weighted rows land in Y (sorted order).
 int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hidden, const uint16_t* xa,
@@ -609,13 +649,6 @@ int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hid
   if (mx) {
     const int rc = c.s.nv ? stage_quantize_nv_x(c, hidden, ld_hidden, da) : stage_quantize_x(c, hidden, ld_hidden);
     if (rc != SPX_OK) return rc;
-  }
-  if (const GemvArgs g = gemv_args(c, w, xa, da); use_gemv(c, g)) {
-    if (int rc = launch_gemv_experts(g, c.st, 1); rc != SPX_OK) return rc;
-    c.mark(4);
-    if (int rc = launch_gemv_experts(g, c.st, 2); rc != SPX_OK) return rc;
-    c.mark(5);
-    return SPX_OK;
   }
   const ExpertPass p{w->expert_w1, w->expert_w2, w->expert_w1_mx, w->expert_w1_mx_scales, w->expert_w2_mx,
                      w->expert_w2_mx_scales, c.s.E, da.tiles, da.num_tiles, mx ? da.tiles_mx : nullptr,
@@ -629,6 +662,26 @@ int stage_shared_gemm1(const Ctx& c, const spx_packed_weights* w, const uint16_t
   const Shape& s = c.s;
   int rc = SPX_OK;
   uint16_t* hs = at<uint16_t>(c.ws, c.L.shared_hidden);
+  if (s.T <= kGemvMaxTokens) {  // decode-sized batch: one dense SwiGLU GEMV
+    GemvPass g{};
+    g.dense_rows = static_cast<int>(s.T);
+    g.status = c.status;
+    g.d = s.d;
+    g.inter = s.S;
+    g.kd = s.kd;
+    g.chunk = s.cs;
+    g.nc = s.ncs;
+    g.x = xa;
+    g.ldx = s.kd;
+    g.w1 = w->shared_w1;
+    g.hid = hs;
+    g.ldh = s.ksp;
+    if (gemv_swiglu_ok(g)) {
+      if ((rc = launch_gemv_swiglu(g, c.st)) != SPX_OK) return rc;
+      c.mark(6);
+      return SPX_OK;
+    }
+  }
   // Large batches: CTA pairs (256-row tiles; each CTA loads one of the
   // [gate | up] halves of the B tile).
   const bool pair = !s.small && (2 * s.cs) % 32 == 0;
@@ -659,6 +712,10 @@ int stage_shared_gemm2(const Ctx& c, const spx_packed_weights* w, uint16_t* out,
   const Shape& s = c.s;
   int rc = SPX_OK;
   uint16_t* hs = at<uint16_t>(c.ws, c.L.shared_hidden);
+  if (y == nullptr && residual == nullptr && s.T <= kGemvMaxTokens) {  // decode-sized batch: dense GEMV
+    const GemvPass g = dense_rows_pass(c, hs, s.ksp, s.ksp, s.S, w->shared_w2, s.d, nullptr, out, s.d);
+    if (gemv_rows_ok(g)) return launch_gemv_rows(g, c.st);
+  }
   const int epi = y != nullptr ? kEpiCombine : kEpiStore;
   GemmArgs g = base_args(epi, s.bn_sd, s.ksp / 64, c.status);
   if ((rc = encode_2d(&g.tma_a, hs, s.T, s.ksp, s.ksp, kTileRows)) != SPX_OK) return rc;

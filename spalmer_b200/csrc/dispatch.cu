@@ -135,7 +135,35 @@ struct ScanShared {
   int count[1024];
 };
 
-__device__ __forceinline__ void finish_dispatch(const DispatchArgs& a, int count, float lb_e, ScanShared& sh) {
+// Inclusive scan over the 1024 threads of the CTA: shuffles within each warp,
+// the 32 warp totals scanned by warp 0 (two CTA barriers).  `tot` receives the
+// sum of all values.  Integer sums, so the order does not matter.
+template <typename T>
+__device__ __forceinline__ T block_inclusive_scan(T v, T* warp_tot, T& tot) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const T u = __shfl_up_sync(0xFFFFFFFFu, v, off);
+    if (lane >= off) v += u;
+  }
+  if (lane == 31) warp_tot[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    T w = warp_tot[lane];
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const T u = __shfl_up_sync(0xFFFFFFFFu, w, off);
+      if (lane >= off) w += u;
+    }
+    warp_tot[lane] = w;  // inclusive warp prefix
+  }
+  __syncthreads();
+  tot = warp_tot[31];
+  return v + (warp > 0 ? warp_tot[warp - 1] : T(0));
+}
+
+// Returns this thread's expert's first dispatch position.
+__device__ __forceinline__ int finish_dispatch(const DispatchArgs& a, int count, float lb_e, ScanShared& sh) {
   int* s_scan = sh.scan;
   unsigned long long* s_scan64 = sh.scan64;
   float* s_red = sh.red;
@@ -146,34 +174,20 @@ __device__ __forceinline__ void finish_dispatch(const DispatchArgs& a, int count
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Block-wide exclusive scans: pair starts and tile starts.
   const int tiles = (count + kTileRows - 1) / kTileRows;
-  s_scan[threadIdx.x] = (e < E) ? count : 0;
-  __syncthreads();
-  for (int off = 1; off < 1024; off <<= 1) {
-    const int v = threadIdx.x >= off ? s_scan[threadIdx.x - off] : 0;
-    __syncthreads();
-    s_scan[threadIdx.x] += v;
-    __syncthreads();
-  }
-  const int start = s_scan[threadIdx.x] - ((e < E) ? count : 0);
-  __syncthreads();
+  int total_pairs = 0;
+  const int mine_count = (e < E) ? count : 0;
+  const int start = block_inclusive_scan<int>(mine_count, s_scan, total_pairs) - mine_count;
   // Tile starts of the two lanes in one scan: BF16-lane tiles in the low
   // 32 bits, MXFP8-lane tiles in the high 32 bits.
   const bool mx = (e < E) && a.lane_mx != nullptr && a.lane_mx[e] != 0;
   const unsigned long long mine =
       (e < E) ? (mx ? (static_cast<unsigned long long>(tiles) << 32) : static_cast<unsigned long long>(tiles)) : 0ull;
-  s_scan64[threadIdx.x] = mine;
-  __syncthreads();
-  for (int off = 1; off < 1024; off <<= 1) {
-    const unsigned long long v = threadIdx.x >= off ? s_scan64[threadIdx.x - off] : 0ull;
-    __syncthreads();
-    s_scan64[threadIdx.x] += v;
-    __syncthreads();
-  }
-  const unsigned long long excl = s_scan64[threadIdx.x] - mine;
+  unsigned long long all_tiles = 0ull;
+  const unsigned long long excl = block_inclusive_scan<unsigned long long>(mine, s_scan64, all_tiles) - mine;
   const int tile_start = mx ? static_cast<int>(excl >> 32) : static_cast<int>(excl & 0xFFFFFFFFull);
   if (threadIdx.x == 1023) {
-    *a.num_tiles = static_cast<int>(s_scan64[1023] & 0xFFFFFFFFull);
-    if (a.num_tiles_mx != nullptr) *a.num_tiles_mx = static_cast<int>(s_scan64[1023] >> 32);
+    *a.num_tiles = static_cast<int>(all_tiles & 0xFFFFFFFFull);
+    if (a.num_tiles_mx != nullptr) *a.num_tiles_mx = static_cast<int>(all_tiles >> 32);
   }
   if (e < E) {
     a.counts[e] = count;
@@ -250,12 +264,19 @@ __device__ __forceinline__ void finish_dispatch(const DispatchArgs& a, int count
       const float mean_p = round_bf16(s / static_cast<float>(a.tokens));
       prod = round_bf16(round_bf16(util) * mean_p);
     }
-    s_red[threadIdx.x] = prod;
+    // sum over experts: butterfly within each warp, then warp 0 over the 32 warp sums
+    float v = prod;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, off);
+    if (lane == 0) s_red[warp] = v;
     __syncthreads();
-    for (int off = 512; off > 0; off >>= 1) {
-      if (threadIdx.x < off) s_red[threadIdx.x] += s_red[threadIdx.x + off];
-      __syncthreads();
+    if (warp == 0) {
+      float w = s_red[lane];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) w += __shfl_xor_sync(0xFFFFFFFFu, w, off);
+      if (lane == 0) s_red[0] = w;
     }
+    __syncthreads();
     if (threadIdx.x == 0) {
       const float total = round_bf16(s_red[0]);
       const long long n_eligible = a.resident != nullptr ? s_i64[3] : a.eligible_experts;
@@ -263,6 +284,7 @@ __device__ __forceinline__ void finish_dispatch(const DispatchArgs& a, int count
       a.aux_loss[0] = f32_to_bf16_rne(eligible * total);
     }
   }
+  return start;
 }
 
 __global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs a) {
@@ -282,16 +304,19 @@ __global__ void __launch_bounds__(1024) dispatch_small_kernel(const DispatchArgs
   __shared__ ScanShared sh;
   __shared__ int s_base[1024];
   __shared__ short s_ids[kDispatchSmallPairs];
+  __shared__ uint16_t s_w[kDispatchSmallPairs];  // pair weights, so the placement loop reads no global memory
   const int E = a.num_experts;
   const int e = threadIdx.x;
   const int P = static_cast<int>(a.pairs);
   if (e < 1024) s_base[e] = 0;
   __syncthreads();
+  const bool weights = a.sorted_weights != nullptr;
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
     const int64_t x = a.ids[p];
     const bool ok = x >= 0 && x < E;
     if (!ok) record_error(a.status, SPX_DEV_BAD_EXPERT);
     s_ids[p] = ok ? static_cast<short>(x) : static_cast<short>(-1);
+    if (weights) s_w[p] = a.pair_weights[p];
     if (ok) atomicAdd(&s_base[x], 1);
   }
   __syncthreads();
@@ -302,9 +327,9 @@ __global__ void __launch_bounds__(1024) dispatch_small_kernel(const DispatchArgs
     for (int b = 0; b < a.lb_blocks; ++b) lb_e += a.lb_partial[static_cast<int64_t>(b) * E + e];
   }
   __syncthreads();
-  finish_dispatch(a, count, lb_e, sh);
+  const int start = finish_dispatch(a, count, lb_e, sh);
   __syncthreads();
-  if (e < E) s_base[e] = a.starts[e];
+  if (e < E) s_base[e] = start;
   __syncthreads();
   if (threadIdx.x >= 32) return;
   const int lane = threadIdx.x;
@@ -322,7 +347,7 @@ __global__ void __launch_bounds__(1024) dispatch_small_kernel(const DispatchArgs
       a.order[pos] = p;
       a.src_row[pos] = p / a.top_k;
       if (a.rank != nullptr) a.rank[p] = pos;
-      if (a.sorted_weights != nullptr) a.sorted_weights[pos] = a.pair_weights[p];
+      if (weights) a.sorted_weights[pos] = s_w[p];
       if ((peers & lt_mask) == 0) s_base[x] = base + __popc(peers);
     }
     __syncwarp();

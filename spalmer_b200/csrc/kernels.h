@@ -312,37 +312,55 @@ int launch_pack_w2(const uint16_t* down, int experts, int inter, int d, int kp, 
                    cudaStream_t stream);
 int launch_pad_rows(const uint16_t* src, int64_t rows, int cols, int ld_out, uint16_t* out, cudaStream_t stream);
 
-// Decode-sized expert GEMVs (gemv.cu): both precision lanes in one launch per
-// projection, rows of each expert = its dispatch range.
-constexpr int64_t kGemvMaxPairs = 1024;  // routed pairs up to which the layer uses the GEMVs
-struct GemvArgs {
-  const int* counts;          // [E] rows per expert (dispatch)
-  const int* starts;          // [E] first dispatch position of each expert
-  const int* src_row;         // [P] token row of each dispatch position
-  const uint16_t* sorted_w;   // [P] routing weight per dispatch position, or null (unit weights)
-  const uint8_t* lane_mx;     // [E] 1 = MXFP8 lane, or null (every expert BF16)
-  int num_experts, d, inter;  // E, d_model, I
-  int kd, chunk, nc, kp;      // BF16 packing: d padded, GEMM1 chunk, chunks, hidden width padded
-  const uint16_t* x;          // [T][kd] hidden rows (K-padded)
+// Decode-sized projections as grouped GEMVs (gemv.cu).  An expert pass is
+// driven by the dispatch's tile tables, like the tcgen05 GEMMs: a tile
+// {group, row0, rows <= 128, expert} covers rows [row0, row0 + rows) of the
+// dispatch order with the weights of `group` (an expert, or a cache slot in a
+// paged pass); the BF16-lane table and the MXFP8-lane table share one launch.
+// A dense pass (tiles == null) is one group of dense_rows rows.
+constexpr int64_t kGemvMaxPairs = 1024;  // routed pairs up to which the expert projections use GEMVs
+constexpr int64_t kGemvMaxTokens = 128;  // tokens up to which router and shared projections use GEMVs
+struct GemvPass {
+  const int4* tiles;          // BF16-lane tiles, or null (dense pass)
+  const int* num_tiles;
+  const int4* tiles_mx;       // MXFP8-lane tiles, or null
+  const int* num_tiles_mx;
+  int max_tiles;              // capacity of each table (grid.x = max_tiles, x2 with tiles_mx)
+  int dense_rows;
+  const int* src_row;         // A row of each row position (gather), or null (identity)
+  int* status;                // device status word
+  // SwiGLU pass: A = x [*, kd] (or E4M3 xq [*, kx] + xsf), B = chunked [gate | up] rows
+  int d, inter, kd, chunk, nc;
+  const uint16_t* x;
   int64_t ldx;
-  const uint16_t* w1;         // [E][nc*2*chunk][kd]
-  const uint16_t* w2;         // [E][d][kp]
-  uint16_t* hid;              // [P][kp] BF16 hidden rows (BF16 lane)
-  uint16_t* y;                // [P][d] weighted expert rows
-  // MXFP8 lane
-  const uint8_t* xq;          // [T][kx] E4M3
-  const uint8_t* xsf;         // [T][kx/32] E8M0
-  int kx, cm, ncm, kh, bn2m;
-  const uint8_t* w1q;         // [E][ncm*2*cm][kx]
-  const uint8_t* w1sf;        // scale atoms
-  const uint8_t* w2q;         // [E][d][kh]
+  const uint16_t* w1;         // [groups][nc*2*chunk][kd]
+  uint16_t* hid;              // [rows][ldh] BF16 hidden rows
+  int ldh;
+  const uint8_t* xq;          // MXFP8 lane: [*, kx] E4M3 rows, [*, kx/32] scales
+  const uint8_t* xsf;
+  int kx, cm, ncm, kh;
+  const uint8_t* w1q;         // [groups][ncm*2*cm][kx] + scale atoms
+  const uint8_t* w1sf;
+  uint8_t* hq;                // [rows][kh] E4M3 hidden rows, [rows][kh/32] scales
+  uint8_t* hsf;
+  // row pass: out[pos, n] = bf16(bf16(<A[pos], W[g][n]> + bias[n]) * row_w[pos])
+  const uint16_t* a2;         // A rows [rows][lda2] (BF16; the MXFP8 lane reads hq / hsf)
+  int64_t lda2;
+  int k2, k_valid2;           // weight row width (BF16 values) and the K that counts
+  const uint16_t* w2;         // [groups][n_out][k2]
+  const uint8_t* w2q;         // MXFP8 lane: [groups][n_out][kh] + scale atoms (bn2m-row tiles)
   const uint8_t* w2sf;
-  uint8_t* hq;                // [P][kh] E4M3 hidden rows
-  uint8_t* hsf;               // [P][kh/32]
+  int bn2m;
+  int n_out, nblk;            // output columns; columns per CTA (set at launch)
+  const uint16_t* bias;       // [n_out] or null
+  const uint16_t* row_w;      // [rows] or null (unit)
+  uint16_t* out;
+  int64_t ldo;
 };
-bool gemv_supported(const GemvArgs& a);
-// which = 1: gate/up + SwiGLU into hid / hq; which = 2: down projection + weights into y.
-int launch_gemv_experts(const GemvArgs& a, cudaStream_t stream, int which);
+bool gemv_swiglu_ok(const GemvPass& a);
+bool gemv_rows_ok(const GemvPass& a);
+int launch_gemv_swiglu(const GemvPass& a, cudaStream_t stream);
+int launch_gemv_rows(GemvPass a, cudaStream_t stream);
 
 // Backward (backward.cu).
 struct BwdRouterArgs {
