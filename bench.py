@@ -546,11 +546,40 @@ def run_ours(args) -> None:
         barrier()
         e2e_ms = e0.elapsed_time(e1)
 
+        # The host link alone: the same pinned copies per step (hidden states in,
+        # update and aux loss out) on the same two copy streams, no forward.
+        # e2e cannot beat this; with N ranks the copies of all ranks share the
+        # host's PCIe / memory bandwidth.
+        def copy_steps(n):
+            for i in range(n):
+                b = i % 2
+                with torch.cuda.stream(s_in):
+                    x_dev[b].copy_(x_host, non_blocking=True)
+                with torch.cuda.stream(s_out):
+                    out_host[b].copy_(x_bufs[b].view(batch, seq, config.d_model), non_blocking=True)
+                    aux_host[b].copy_(out.auxiliary_loss, non_blocking=True)
+
+        copy_steps(W)
+        torch.cuda.synchronize()
+        barrier()
+        c0 = torch.cuda.Event(enable_timing=True)
+        c1 = torch.cuda.Event(enable_timing=True)
+        c0.record(main)
+        s_in.wait_stream(main)
+        s_out.wait_stream(main)
+        copy_steps(K)
+        main.wait_stream(s_in)
+        main.wait_stream(s_out)
+        c1.record(main)
+        torch.cuda.synchronize()
+        barrier()
+        copy_ms = c0.elapsed_time(c1)
+
     # max over ranks
-    t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
+    t = torch.tensor([total_ms, e2e_ms, copy_ms], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms, e2e_ms = float(t[0]), float(t[1])
+    total_ms, e2e_ms, copy_ms = float(t[0]), float(t[1]), float(t[2])
     ms_per_step = total_ms / K
     value = world * tokens / (ms_per_step / 1e3)
     e2e_value = world * tokens / (e2e_ms / K / 1e3)
@@ -577,7 +606,13 @@ def run_ours(args) -> None:
             "config": workload_config(args.config, world),
             "e2e": {"value": e2e_value, "unit": "tokens/s",
                     "h2d_bytes_per_step": tokens * config.d_model * 2,
-                    "d2h_bytes_per_step": tokens * config.d_model * 2 + 2},
+                    "d2h_bytes_per_step": tokens * config.d_model * 2 + 2,
+                    "host_link_bound": {
+                        "value": world * tokens / (copy_ms / K / 1e3), "unit": "tokens/s",
+                        "ms_per_step": copy_ms / K,
+                        "gbs_all_ranks": world * (2 * tokens * config.d_model * 2 + 2) / (copy_ms / K / 1e3) / 1e9,
+                        "what": "the same pinned H2D + D2H copies per step on the same streams, no forward; "
+                                "max over ranks"}},
             "gpu_launches": K * ((17 if nvfp4 else 14) if lane is not None else 11),
             "roofline": {"bound": "tensor",
                          "kernel": ("gemm_kernel<kEpiSwiglu> (expert GEMM1; BF16 lane gathered rows, "

@@ -19,9 +19,10 @@ its data pipeline, not by the expert layer, and is not in the wheelhouse.  The
 Python sources installed are the reference's own, byte for byte (checked
 below against the source tree).
 
-    python oracle/install_ref.py [--reference PATH]
+    python oracle/install_ref.py --reference PATH    (or $SPALMER_REFERENCE)
 
-PATH defaults to ``$SPALMER_REFERENCE`` or ``/root/reference``.
+PATH is the reference project's root (the folder holding ``pyproject.toml``
+and ``src/spalmer``).
 """
 
 from __future__ import annotations
@@ -87,8 +88,10 @@ def install(reference: Path, target: Path = TARGET) -> Path:
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--reference", default=os.environ.get("SPALMER_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("SPALMER_REFERENCE"))
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference PATH or set SPALMER_REFERENCE")
     print(install(Path(args.reference)))
 
 

@@ -140,13 +140,9 @@ struct Layout {
   size_t hidden, y, shared_hidden, shared_out, x_pad, x_norm, util, stats, ratios, aux;
   size_t x_q, x_sf, h_q, h_sf, tiles_mx;  // MXFP8 lane (empty otherwise)
   size_t tiles_page, tiles_mx_page;        // one page of a paged expert pass
-  size_t tiles2;                           // 256-row tiles of the BF16 lane (CTA-pair GEMM1)
   size_t nv_row_amax, nv_amax;             // NVFP4 lane: per-token amax [T]; per-expert amax of x, h [2][E]
   size_t total;
 };
-
-// Capacity of the 256-row tile table (one partial tile per expert at most).
-int max_tiles2(const Shape& s) { return ceil_div(s.P, 2 * kTileRows) + s.E; }
 
 Layout make_layout(const Shape& s) {
   Layout L{};
@@ -191,7 +187,6 @@ Layout make_layout(const Shape& s) {
   }
   L.tiles_mx = take(s.mx ? sizeof(int4) * static_cast<size_t>(s.max_tiles) : 0);
   L.tiles_page = take(sizeof(int4) * static_cast<size_t>(s.max_tiles));
-  L.tiles2 = take(sizeof(int4) * static_cast<size_t>(max_tiles2(s)));
   L.tiles_mx_page = take(s.mx ? sizeof(int4) * static_cast<size_t>(s.max_tiles) : 0);
   L.nv_row_amax = take(s.nv ? sizeof(float) * static_cast<size_t>(s.T) : 0);
   L.nv_amax = take(s.nv ? sizeof(float) * 2 * static_cast<size_t>(s.E) : 0);
@@ -364,10 +359,6 @@ DispatchArgs layer_dispatch_args(const Ctx& c, const spx_layer_dims* dims, const
   da.pair_weights = out->routing_weights;
   da.sorted_weights = at<uint16_t>(ws, L.sorted_w);
   if (out->pair_rank != nullptr) da.rank = out->pair_rank;
-  if (!s.small) {  // 256-row tiles for the CTA-pair expert GEMM1 of large batches
-    da.tiles2 = at<int4>(ws, L.tiles2);
-    da.num_tiles2 = at<int>(ws, L.small) + 4;
-  }
   if (s.mx && w->expert_lane_mxfp8 != nullptr) {
     da.lane_mx = w->expert_lane_mxfp8;
     da.tiles_mx = at<int4>(ws, L.tiles_mx);
@@ -396,8 +387,6 @@ struct ExpertPass {
   uint16_t* const* row_out = nullptr;  // GEMM2 rows to row_out[row_out_idx[p]] instead of Y
   const int* row_out_idx = nullptr;
   const uint8_t* const* a_rows = nullptr;  // BF16 GEMM1 rows through one pointer per source row
-  const int4* tiles2 = nullptr;            // 256-row BF16-lane tiles for the CTA-pair GEMM1, or null
-  const int* num_tiles2 = nullptr;
 };
 
 // NVFP4 lane input: each expert's rows in dispatch order as E2M1 with UE4M3
@@ -506,26 +495,7 @@ int stage_expert_gemms(const Ctx& c, const uint16_t* xa, const int* src_row, con
   uint8_t* hsf = at<uint8_t>(ws, L.h_sf);
   uint16_t* hid = at<uint16_t>(ws, L.hidden);
   uint16_t* y = at<uint16_t>(ws, L.y);
-  if (p.tiles2 != nullptr && p.max_ctas == 0 && p.a_rows == nullptr && (2 * s.c) % 32 == 0 &&
-      gemm_pair_pick_stages(2 * s.c) > kPairGatherDepth) {
-    // CTA pairs over 256-row tiles: each SM loads half of an expert's [gate | up] tile per 128 rows
-    GemmArgs g = base_args(kEpiSwiglu, 2 * s.c, s.kd / 64, c.status);
-    g.stages = gemm_pair_pick_stages(2 * s.c);
-    if ((rc = encode_3d(&g.tma_b, p.w1, p.groups, static_cast<int64_t>(s.nc) * 2 * s.c, s.kd, s.c)) != SPX_OK)
-      return rc;
-    g.groups = p.groups;
-    g.gather = 1;
-    g.gather_idx = src_row;
-    g.a_base = reinterpret_cast<const uint8_t*>(xa);
-    g.lda = 2 * static_cast<int64_t>(s.kd);
-    g.tiles = p.tiles2;
-    g.num_tiles = p.num_tiles2;
-    g.chunk = s.c;
-    g.h_cols = s.kp;
-    g.out = hid;
-    g.ldo = s.kp;
-    if ((rc = launch_gemm_pair_gather(g, max_tiles2(s), s.nc, c.st)) != SPX_OK) return rc;
-  } else {
+  {
     GemmArgs g = base_args(kEpiSwiglu, 2 * s.c, s.kd / 64, c.status);
     if ((rc = encode_3d(&g.tma_b, p.w1, p.groups, static_cast<int64_t>(s.nc) * 2 * s.c, s.kd, 2 * s.c)) != SPX_OK)
       return rc;
@@ -680,11 +650,9 @@ int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hid
     const int rc = c.s.nv ? stage_quantize_nv_x(c, hidden, ld_hidden, da) : stage_quantize_x(c, hidden, ld_hidden);
     if (rc != SPX_OK) return rc;
   }
-  ExpertPass p{w->expert_w1, w->expert_w2, w->expert_w1_mx, w->expert_w1_mx_scales, w->expert_w2_mx,
-               w->expert_w2_mx_scales, c.s.E, da.tiles, da.num_tiles, mx ? da.tiles_mx : nullptr,
-               mx ? da.num_tiles_mx : nullptr, 0, w->expert_nvfp4_amax};
-  p.tiles2 = da.tiles2;
-  p.num_tiles2 = da.num_tiles2;
+  const ExpertPass p{w->expert_w1, w->expert_w2, w->expert_w1_mx, w->expert_w1_mx_scales, w->expert_w2_mx,
+                     w->expert_w2_mx_scales, c.s.E, da.tiles, da.num_tiles, mx ? da.tiles_mx : nullptr,
+                     mx ? da.num_tiles_mx : nullptr, 0, w->expert_nvfp4_amax};
   return stage_expert_gemms(c, xa, da.src_row, da.sorted_weights, p);
 }
 

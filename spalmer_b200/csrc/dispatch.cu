@@ -199,17 +199,6 @@ __device__ __forceinline__ int finish_dispatch(const DispatchArgs& a, int count,
       table[tile_start + t] = make_int4(e, start + r0, min(kTileRows, count - r0), e);
     }
   }
-  // Optional table of 256-row tiles of the BF16-lane experts (CTA-pair GEMMs).
-  if (a.tiles2 != nullptr) {
-    const int t2 = (e < E && !mx) ? (count + 2 * kTileRows - 1) / (2 * kTileRows) : 0;
-    int all2 = 0;
-    const int t2_start = block_inclusive_scan<int>(t2, s_scan + 64, all2) - t2;
-    if (threadIdx.x == 1023) *a.num_tiles2 = all2;
-    for (int t = 0; t < t2; ++t) {
-      const int r0 = t * 2 * kTileRows;
-      a.tiles2[t2_start + t] = make_int4(e, start + r0, min(2 * kTileRows, count - r0), e);
-    }
-  }
 
   // Utilization (losses.py:28-33): count / P in float32.
   const float util = (e < E) ? static_cast<float>(count) / static_cast<float>(a.pairs) : 0.0f;

@@ -1025,224 +1025,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-// Gathered CTA-pair GEMM1 of the BF16 expert lane (kEpiSwiglu): one 256-row
-// tile of one expert (the dispatch's 256-row table) x bn columns per cluster
-// of two CTAs.  Each CTA gathers its 128 rows of A with cp.async (two producer
-// warps, 64 rows each) and TMA-loads its half of the B rows; the leader issues
-// M = 256 tcgen05 MMAs (cta_group::2) that read both CTAs' shared memory, so
-// every SM loads half of the expert's [gate | up] tile per 128 rows.  A
-// producer warp cannot make a cp.async arrive on the other CTA's barrier, so
-// each warp keeps up to kPairGatherDepth stage groups in flight, waits for
-// the oldest (cp.async.wait_group), makes it visible to the tensor cores
-// (fence.proxy.async) and arrives on the leader's full barrier itself with a
-// cluster-scope release -- no forwarding thread on the data path.  The
-// leader's full[s] expects its own expect_tx arrival (the B bytes of both
-// CTAs) plus one arrival per producer warp of both CTAs.  Everything else
-// (stage releases and accumulator-ready multicast commits, the peer's
-// epilogue releases forwarded once per tile, bounded waits, teardown in
-// step) is the TMA-loaded pair kernel's.
-template <int PART>
-__device__ __forceinline__ void produce_pair_gather(const GemmArgs& a, uint8_t* sa, uint8_t* sb, uint64_t* full,
-                                                    uint64_t* empty, int S, uint32_t a_bytes, uint32_t b_bytes,
-                                                    int total, int pair, int npairs, uint32_t rank, int lane) {
-  constexpr int kPer = 32 / kGemmGatherProducers;  // groups of 4 rows per warp
-  constexpr int kI0 = (PART - 1) * kPer;
-  const int bn = a.bn;
-  const int chunk = lane & 7;
-  const uint32_t full_leader = mapa_shared(smem_u32(full), 0);
-  uint32_t it = 0, done = 0;
-  bool ok = true;
-  for (int t = pair; ok && t < total; t += npairs) {
-    const int mt = t / a.n_tiles;
-    const int nt = t - mt * a.n_tiles;
-    const int4 e = a.tiles[mt];
-    if (e.z <= 0 || e.z > 2 * kTileRows || e.x < 0 || e.x >= a.groups) {
-      if (lane == 0) record_error(a.status, SPX_DEV_BAD_TILE);
-      break;
-    }
-    const int group = e.x;
-    const int my0 = e.y + static_cast<int>(rank) * kTileRows;
-    const int my_rows = max(0, min(kTileRows, e.z - static_cast<int>(rank) * kTileRows));
-    int src[kPer];
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int rr = 4 * (kI0 + i) + (lane >> 3);
-      src[i] = my_rows > 0 ? a.gather_idx[my0 + (rr < my_rows ? rr : 0)] : 0;
-    }
-    const int n0 = nt * bn + static_cast<int>(rank) * (bn / 2);
-    const uint8_t* col = a.a_base + chunk * 16;
-    for (int kb = 0; kb < a.k_blocks; ++kb, ++it) {
-      const int s = static_cast<int>(it % S);
-      const uint32_t ph = (it / S) & 1u;
-      int go = 1;
-      if (lane == 0) {
-        go = mbar_wait(&empty[s], ph ^ 1u, a.status, SPX_DEV_TIMEOUT_PRODUCER) ? 1 : 0;
-        if (go && PART == 1) {
-          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * b_bytes);
-          tma_load_3d_pair(sb + s * b_bytes, &a.tma_b, full_leader + s * 8, kb * 64, n0, group);
-        }
-      }
-      go = __shfl_sync(0xFFFFFFFFu, go, 0);
-      if (!go) {
-        ok = false;
-        break;
-      }
-      const uint32_t dst0 = smem_u32(sa + s * a_bytes);
-#pragma unroll
-      for (int i = 0; i < kPer; ++i) {
-        const int rr = 4 * (kI0 + i) + (lane >> 3);
-        const uint32_t dst = dst0 + (rr >> 3) * 1024 + (rr & 7) * 128 + ((chunk ^ (rr & 7)) << 4);
-        cp_async16(dst, col + kb * 128 + static_cast<int64_t>(src[i]) * a.lda);
-      }
-      cp_async_commit();
-      if (it + 1 - done > static_cast<uint32_t>(kPairGatherDepth)) {
-        // the oldest group in flight has landed: hand its stage to the tensor cores
-        cp_async_wait<kPairGatherDepth - 1>();
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(full_leader + (done % S) * 8);
-        ++done;
-      }
-    }
-  }
-  cp_async_wait_all();
-  fence_proxy_async_smem();
-  __syncwarp();
-  for (; done < it; ++done)
-    if (lane == 0) mbar_arrive_cluster(full_leader + (done % S) * 8);
-}
-
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmKernelThreads, 1)
-    gemm_pair_gather_kernel(const __grid_constant__ GemmArgs a) {
-  extern __shared__ uint8_t gemm_smem_raw[];
-  uint8_t* smem = align_1024(gemm_smem_raw);
-  const int bn = a.bn;  // the pair's N; each CTA holds bn / 2 rows of B
-  const int S = a.stages;
-  const uint32_t a_bytes = kTileRows * 128u;
-  const uint32_t b_bytes = static_cast<uint32_t>(bn / 2) * 128u;
-  uint8_t* sa = smem;
-  uint8_t* sb = smem + S * a_bytes;
-  uint8_t* stage_all = align_1024(sb + S * b_bytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(stage_all + kGemmEpilogueWarps * kStageBytesPerWarp);
-  uint64_t* empty = full + S;
-  uint64_t* tfull = empty + S;
-  uint64_t* tempty = tfull + kMaxAccBufs;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + kMaxAccBufs);
-  const uint32_t nacc = min(static_cast<uint32_t>(kMaxAccBufs), 512u / a.tmem_cols);
-  const uint32_t tmem_alloc_cols = nacc * a.tmem_cols;
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_ctarank();
-  const int pair = static_cast<int>(blockIdx.x >> 1);
-  const int npairs = static_cast<int>(gridDim.x >> 1);
-  const int total = *a.num_tiles * a.n_tiles;
-  if (pair >= total) return;  // both CTAs of a pair share `pair`: they leave together
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      // leader: its expect_tx arrival + one arrival per producer warp of both CTAs
-      mbar_init(&full[s], rank == 0 ? 1 + 2 * kGemmGatherProducers : 1);
-      mbar_init(&empty[s], 1);  // one multicast commit
-    }
-    for (int b = 0; b < kMaxAccBufs; ++b) {
-      mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], kGemmEpilogueWarps + (rank == 0 ? 1 : 0));
-    }
-    fence_mbar_init();
-    prefetch_tensormap(&a.tma_b);
-  }
-  if (warp == 1) {
-    tmem_alloc_pair(tmem_slot, tmem_alloc_cols);
-    tmem_relinquish_pair();
-  }
-  tc_fence_before();
-  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0) {
-    produce_pair_gather<1>(a, sa, sb, full, empty, S, a_bytes, b_bytes, total, pair, npairs, rank, lane);
-  } else if (warp == kGemmExtraProducerWarp0) {
-    produce_pair_gather<2>(a, sa, sb, full, empty, S, a_bytes, b_bytes, total, pair, npairs, rank, lane);
-  } else if (warp == 1) {
-    if (rank != 0 && lane == 0) {
-      // ---------------- peer: forward the epilogue's releases to the leader
-      uint32_t lt = 0;
-      for (int t = pair; t < total; t += npairs, ++lt) {
-        const uint32_t b = lt % nacc;
-        if (!mbar_wait(&tempty[b], (lt / nacc) & 1u, a.status, SPX_DEV_TIMEOUT_MMA)) break;
-        tc_fence_after();
-        mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[b]), 0));
-      }
-    } else if (rank == 0 && lane == 0) {
-      // ---------------- leader: MMA issuer
-      const uint32_t idesc = idesc_bf16_f32(2 * kTileRows, bn);
-      uint32_t it = 0, lt = 0;
-      bool ok = true;
-      for (int t = pair; ok && t < total; t += npairs, ++lt) {
-        const uint32_t b = lt % nacc;
-        const uint32_t tph = (lt / nacc) & 1u;
-        if (!mbar_wait(&tempty[b], tph ^ 1u, a.status, SPX_DEV_TIMEOUT_MMA)) break;
-        tc_fence_after();
-        const uint32_t acc = tmem + b * a.tmem_cols;
-        for (int kb = 0; kb < a.k_blocks; ++kb, ++it) {
-          const int s = static_cast<int>(it % S);
-          const uint32_t ph = (it / S) & 1u;
-          if (!mbar_wait_cluster(&full[s], ph, a.status, SPX_DEV_TIMEOUT_MMA)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_base = smem_u32(sa + s * a_bytes);
-          const uint32_t b_base = smem_u32(sb + s * b_bytes);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_bf16_pair(acc, desc_kmajor_sw128(a_base + kk * 32), desc_kmajor_sw128(b_base + kk * 32), idesc,
-                          (kb | kk) != 0 ? 1u : 0u);
-          mma_commit_pair(&empty[s], 0x3);
-        }
-        if (!ok) break;
-        mma_commit_pair(&tfull[b], 0x3);
-      }
-    }
-    __syncwarp();
-  } else if (warp >= 2 && warp < 2 + kGemmEpilogueWarps) {
-    // ---------------- epilogue (both CTAs): this CTA's 128 accumulator rows
-    const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
-    uint8_t* my_stage = stage_all + (warp - 2) * kStageBytesPerWarp;
-    uint32_t lt = 0;
-    for (int t = pair; t < total; t += npairs, ++lt) {
-      const int mt = t / a.n_tiles;
-      const int nt = t - mt * a.n_tiles;
-      const int4 e = a.tiles[mt];
-      const int row0 = e.y + static_cast<int>(rank) * kTileRows;
-      const int rows = max(0, min(kTileRows, e.z - static_cast<int>(rank) * kTileRows));
-      const uint32_t b = lt % nacc;
-      const uint32_t tph = (lt / nacc) & 1u;
-      int go = 1;
-      if (lane == 0) go = mbar_wait(&tfull[b], tph, a.status, SPX_DEV_TIMEOUT_EPILOGUE) ? 1 : 0;
-      go = __shfl_sync(0xFFFFFFFFu, go, 0);
-      if (!go) break;
-      tc_fence_after();
-      const uint32_t taddr = tmem + b * a.tmem_cols + (static_cast<uint32_t>(quad * 32) << 16);
-      const long long my_row = static_cast<long long>(row0) + quad * 32 + lane;
-      run_epilogue<kEpiSwiglu>(a, taddr, my_stage, quad, half, lane, row0, rows, nt * bn, nt, my_row);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[b]);
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();  // no CTA leaves while its pair may still touch its shared or tensor memory
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc_pair(tmem, tmem_alloc_cols);
-  }
-}
-
 // ------------------------------------------------------------------ host side
 
 namespace {
@@ -1376,27 +1158,6 @@ int launch_gemm_pair(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStr
     default:
       return SPX_ERR_UNSUPPORTED;
   }
-}
-
-// Gathered CTA-pair expert GEMM1 (BF16 lane, SwiGLU epilogue) over the
-// dispatch's 256-row tile table a.tiles / *a.num_tiles; max_tiles bounds the
-// table.  bn: 32..256, a multiple of 32; the B tensor map's box holds bn / 2 rows.
-int launch_gemm_pair_gather(const GemmArgs& a, int max_tiles, int grid_n, cudaStream_t stream) {
-  if (max_tiles <= 0 || grid_n <= 0) return SPX_OK;
-  if (a.bn < 32 || a.bn > 256 || (a.bn % 32) != 0 || a.gather == 0 || a.tiles == nullptr || a.a_rows != nullptr)
-    return SPX_ERR_UNSUPPORTED;
-  const size_t smem = gemm_pair_smem_bytes(a.bn, a.stages);
-  // more stages than cp.async groups a producer keeps in flight (stage reuse waits for the arrival)
-  if (smem > kGemmSmemBudget || a.stages < kPairGatherDepth + 1) return SPX_ERR_INVALID_ARG;
-  const void* fn = reinterpret_cast<const void*>(gemm_pair_gather_kernel);
-  if (int rc = ensure_max_dynamic_smem(fn); rc != SPX_OK) return rc;
-  const int pairs_max = device_max_pairs(fn, smem);
-  const int64_t tiles = static_cast<int64_t>(max_tiles) * grid_n;
-  const int pairs = static_cast<int>(tiles < pairs_max ? tiles : pairs_max);
-  GemmArgs b = a;
-  b.n_tiles = grid_n;
-  gemm_pair_gather_kernel<<<2 * pairs, kGemmKernelThreads, smem, stream>>>(b);
-  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 
 int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream, bool mx, bool nv) {

@@ -46,7 +46,7 @@ namespace {
 
 constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
-constexpr int kGemvRows = 16;       // token rows per pass
+constexpr int kGemvRows = 8;        // token rows per pass (one 8-column mma.sync tile)
 constexpr int kSwigluCols = 16;     // hidden columns per swiglu CTA (BF16 lane)
 constexpr int kSwigluColsMx = 32;   // ... MXFP8 lane (one scale block of the hidden row)
 constexpr size_t kSlabBytes = 48 * 1024;  // weight slab budget per CTA
@@ -290,15 +290,13 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-// One warp: D[16 x 8 tokens] for up to two 8-token tiles over k in [k0, k1).
-// a_row(m) gives the shared-memory byte offset of A row m (0..15) of the tile.
+// One warp: D[16 x 8 tokens] over k in [k0, k1).  a_row(m) gives the
+// shared-memory byte offset of A row m (0..15) of the tile.
 template <typename ARow>
-__device__ __forceinline__ void mma_rows(uint32_t slab_u32, ARow a_row, uint32_t xs_u32, int xs_stride, int ntiles,
-                                         int k0, int k1, int lane, float (&d)[2][4]) {
+__device__ __forceinline__ void mma_rows(uint32_t slab_u32, ARow a_row, uint32_t xs_u32, int xs_stride, int k0,
+                                         int k1, int lane, float (&d)[4]) {
 #pragma unroll
-  for (int t = 0; t < 2; ++t)
-#pragma unroll
-    for (int q = 0; q < 4; ++q) d[t][q] = 0.0f;
+  for (int q = 0; q < 4; ++q) d[q] = 0.0f;
   // ldmatrix row addresses: A matrices 0..3 = (rows 0-7 | 8-15) x (k | k+8);
   // B matrices 0, 1 = tokens 0-7 x (k | k+8)
   const int mi = lane >> 3, ri = lane & 7;
@@ -310,16 +308,12 @@ __device__ __forceinline__ void mma_rows(uint32_t slab_u32, ARow a_row, uint32_t
     ldsm_x4(a_base + 2 * k, a);
     uint32_t b[2];
     ldsm_x2(b_base + 2 * k, b);
-    mma_16816(d[0], a, b);
-    if (ntiles > 1) {
-      ldsm_x2(b_base + 8 * xs_stride + 2 * k, b);
-      mma_16816(d[1], a, b);
-    }
+    mma_16816(d, a, b);
   }
 }
 
 // SwiGLU GEMV: gate/up of one block of hidden columns of group g for its rows.
-__global__ void __launch_bounds__(kGemvThreads, 2) gemv_swiglu_kernel(const GemvPass a) {
+__global__ void __launch_bounds__(kGemvThreads, 3) gemv_swiglu_kernel(const GemvPass a) {
   extern __shared__ __align__(128) uint8_t smem[];
   int g, n;
   bool mx;
@@ -344,7 +338,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_swiglu_kernel(const Gemv
   int* abort_flag = reinterpret_cast<int*>(smem + 64);
   uint8_t* slab = smem + 128;
   uint8_t* xsp = slab + 2 * static_cast<size_t>(cols) * ws;
-  float* red = reinterpret_cast<float*>(xsp + static_cast<size_t>(kGemvRows) * xsb);  // [2][8 warps][32][4]
+  float* red = reinterpret_cast<float*>(xsp + static_cast<size_t>(kGemvRows) * xsb);  // [8 warps][32][4]
   uint16_t* hs = reinterpret_cast<uint16_t*>(red);  // MXFP8 lane: [kGemvRows][32] BF16 hidden values
   const uint8_t* wbase = mx ? a.w1q : reinterpret_cast<const uint8_t*>(a.w1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -390,40 +384,34 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_swiglu_kernel(const Gemv
       // K quarter ks = warp >> 1; partial sums reduced in shared memory
       const int mt = warp & 1, ks = warp >> 1;
       const int kq = K / 4;
-      const int ntiles = (R + 7) / 8;
-      float d[2][4];
+      float d[4];
       auto a_row = [&](int m) -> uint32_t {
         const int jl = mt * 8 + (m & 7);
         return static_cast<uint32_t>(((m >> 3) * cols + jl) * ws);  // m < 8: gate row jl, else up row jl
       };
-      mma_rows(smem_u32(slab), a_row, smem_u32(xsp), xsb, ntiles, ks * kq, (ks + 1) * kq, lane, d);
-#pragma unroll
-      for (int t = 0; t < 2; ++t)
-        *reinterpret_cast<float4*>(red + ((t * kGemvWarps + warp) * 32 + lane) * 4) =
-            make_float4(d[t][0], d[t][1], d[t][2], d[t][3]);
+      mma_rows(smem_u32(slab), a_row, smem_u32(xsp), xsb, ks * kq, (ks + 1) * kq, lane, d);
+      *reinterpret_cast<float4*>(red + (warp * 32 + lane) * 4) = make_float4(d[0], d[1], d[2], d[3]);
       __syncthreads();
       if (ks == 0) {
         const int gq = lane >> 2, tq = lane & 3;
         const int jl = mt * 8 + gq;
-        for (int t = 0; t < ntiles; ++t) {
-          float4 sum = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        float4 sum = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
-          for (int s2 = 0; s2 < 4; ++s2) {
-            const float4 v = *reinterpret_cast<const float4*>(red + ((t * kGemvWarps + mt + 2 * s2) * 32 + lane) * 4);
-            sum.x += v.x;
-            sum.y += v.y;
-            sum.z += v.z;
-            sum.w += v.w;
-          }
-          // (x, y): gate of column jl for tokens 2tq, 2tq+1; (z, w): up of the same
+        for (int s2 = 0; s2 < 4; ++s2) {
+          const float4 v = *reinterpret_cast<const float4*>(red + ((mt + 2 * s2) * 32 + lane) * 4);
+          sum.x += v.x;
+          sum.y += v.y;
+          sum.z += v.z;
+          sum.w += v.w;
+        }
+        // (x, y): gate of column jl for tokens 2tq, 2tq+1; (z, w): up of the same
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int i = t * 8 + 2 * tq + u;
-            if (i < R && jl < ncol) {
-              const float gv = u == 0 ? sum.x : sum.y, uv = u == 0 ? sum.z : sum.w;
-              const float h = round_bf16(round_bf16(silu_ref(round_bf16(gv))) * round_bf16(uv));
-              a.hid[(start + r0 + i) * a.ldh + j0 + jl] = f32_to_bf16_rne(h);
-            }
+        for (int u = 0; u < 2; ++u) {
+          const int i = 2 * tq + u;
+          if (i < R && jl < ncol) {
+            const float gv = u == 0 ? sum.x : sum.y, uv = u == 0 ? sum.z : sum.w;
+            const float h = round_bf16(round_bf16(silu_ref(round_bf16(gv))) * round_bf16(uv));
+            a.hid[(start + r0 + i) * a.ldh + j0 + jl] = f32_to_bf16_rne(h);
           }
         }
       }
@@ -469,7 +457,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_swiglu_kernel(const Gemv
 
 // Row GEMV: out[pos, n] = bf16(bf16(<A[pos], W[g][n]> [+ bias[n]]) * w[pos])
 // for a slab of nblk output columns of group g and the group's rows.
-__global__ void __launch_bounds__(kGemvThreads, 2) gemv_rows_kernel(const GemvPass a) {
+__global__ void __launch_bounds__(kGemvThreads, 3) gemv_rows_kernel(const GemvPass a) {
   extern __shared__ __align__(128) uint8_t smem[];
   int g, n;
   bool mx;
@@ -488,7 +476,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_rows_kernel(const GemvPa
   uint8_t* slab = smem + 128;
   uint8_t* xsp = slab + static_cast<size_t>(a.nblk) * ws;
   uint16_t* ys = reinterpret_cast<uint16_t*>(xsp + static_cast<size_t>(kGemvRows) * xsb);  // [kGemvRows][nblk]
-  float* red = reinterpret_cast<float*>(ys + static_cast<size_t>(kGemvRows) * a.nblk);    // [2][8][32][4]
+  float* red = reinterpret_cast<float*>(ys + static_cast<size_t>(kGemvRows) * a.nblk);    // [8][32][4]
   const uint8_t* wbase = mx ? a.w2q : reinterpret_cast<const uint8_t*>(a.w2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool tc = !mx && gemv_rows_tc(a);
@@ -538,51 +526,38 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_rows_kernel(const GemvPa
       const int mtiles = a.nblk / 16, ksplit = kGemvWarps / mtiles;
       const int mt = warp % mtiles, ks = warp / mtiles;
       const int kq = a.k_valid2 / ksplit;
-      const int ntiles = (R + 7) / 8;
-      float d[2][4];
+      float d[4];
       auto a_row = [&](int m) -> uint32_t { return static_cast<uint32_t>((mt * 16 + m) * ws); };
-      mma_rows(smem_u32(slab), a_row, smem_u32(xsp), xsb, ntiles, ks * kq, (ks + 1) * kq, lane, d);
+      mma_rows(smem_u32(slab), a_row, smem_u32(xsp), xsb, ks * kq, (ks + 1) * kq, lane, d);
       if (ksplit > 1) {
-#pragma unroll
-        for (int t = 0; t < 2; ++t)
-          *reinterpret_cast<float4*>(red + ((t * kGemvWarps + warp) * 32 + lane) * 4) =
-              make_float4(d[t][0], d[t][1], d[t][2], d[t][3]);
+        *reinterpret_cast<float4*>(red + (warp * 32 + lane) * 4) = make_float4(d[0], d[1], d[2], d[3]);
         __syncthreads();
         if (ks == 0) {
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            if (t >= ntiles) break;
-            float4 sum = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            for (int s2 = 0; s2 < ksplit; ++s2) {
-              const float4 v =
-                  *reinterpret_cast<const float4*>(red + ((t * kGemvWarps + mt + mtiles * s2) * 32 + lane) * 4);
-              sum.x += v.x;
-              sum.y += v.y;
-              sum.z += v.z;
-              sum.w += v.w;
-            }
-            d[t][0] = sum.x;
-            d[t][1] = sum.y;
-            d[t][2] = sum.z;
-            d[t][3] = sum.w;
+          float4 sum = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          for (int s2 = 0; s2 < ksplit; ++s2) {
+            const float4 v = *reinterpret_cast<const float4*>(red + ((mt + mtiles * s2) * 32 + lane) * 4);
+            sum.x += v.x;
+            sum.y += v.y;
+            sum.z += v.z;
+            sum.w += v.w;
           }
+          d[0] = sum.x;
+          d[1] = sum.y;
+          d[2] = sum.z;
+          d[3] = sum.w;
         }
       }
       if (ks == 0) {
         // (d0, d1): output row mt*16 + gq for tokens 2tq, 2tq+1; (d2, d3): row + 8
         const int gq = lane >> 2, tq = lane & 3;
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (t >= ntiles) break;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int nl = mt * 16 + gq + (q >> 1) * 8;
-            const int i = t * 8 + 2 * tq + (q & 1);
-            if (i < R && nl < ncol) {
-              const float bias = a.bias != nullptr ? bf16_to_f32(a.bias[n0 + nl]) : 0.0f;
-              const float w = a.row_w != nullptr ? bf16_to_f32(a.row_w[start + r0 + i]) : 1.0f;
-              ys[i * a.nblk + nl] = f32_to_bf16_rne(round_bf16(d[t][q] + bias) * w);
-            }
+        for (int q = 0; q < 4; ++q) {
+          const int nl = mt * 16 + gq + (q >> 1) * 8;
+          const int i = 2 * tq + (q & 1);
+          if (i < R && nl < ncol) {
+            const float bias = a.bias != nullptr ? bf16_to_f32(a.bias[n0 + nl]) : 0.0f;
+            const float w = a.row_w != nullptr ? bf16_to_f32(a.row_w[start + r0 + i]) : 1.0f;
+            ys[i * a.nblk + nl] = f32_to_bf16_rne(round_bf16(d[q] + bias) * w);
           }
         }
       }
@@ -662,7 +637,7 @@ int launch_gemv_swiglu(const GemvPass& a, cudaStream_t stream) {
   const int K = std::max(a.kd, mx ? a.kx : 0);
   const size_t slab = std::max<size_t>(2 * kSwigluCols * (2 * static_cast<size_t>(a.kd) + 16),
                                        mx ? 2 * kSwigluColsMx * (static_cast<size_t>(a.kx) + 16) : 0);
-  const size_t red = 2 * kGemvWarps * 32 * 4 * sizeof(float);
+  const size_t red = kGemvWarps * 32 * 4 * sizeof(float);
   const size_t smem = 128 + slab + static_cast<size_t>(kGemvRows) * (2 * static_cast<size_t>(K) + 16) + red;
   if (smem > kGemmSmemBudget) return SPX_ERR_UNSUPPORTED;
   if (int rc = ensure_max_dynamic_smem(reinterpret_cast<const void*>(gemv_swiglu_kernel)); rc != SPX_OK) return rc;
@@ -676,7 +651,7 @@ int launch_gemv_rows(GemvPass a, cudaStream_t stream) {
   const int wbytes = std::max(2 * a.k2, mx ? a.kh : 0);
   a.nblk = pick_nblk(wbytes);
   const int K = std::max(a.k2, mx ? a.kh : 0);
-  const size_t red = 2 * kGemvWarps * 32 * 4 * sizeof(float);
+  const size_t red = kGemvWarps * 32 * 4 * sizeof(float);
   const size_t smem = 128 + static_cast<size_t>(a.nblk) * (wbytes + 16) +
                       static_cast<size_t>(kGemvRows) * (2 * static_cast<size_t>(K) + 16) +
                       static_cast<size_t>(kGemvRows) * a.nblk * 2 + red;

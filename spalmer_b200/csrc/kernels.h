@@ -90,8 +90,6 @@ struct DispatchArgs {
   const uint8_t* lane_mx;    // [E] 1 = expert runs the MXFP8 lane, or null (all BF16)
   int4* tiles_mx;            // [ceil(P/128) + E] tiles of MXFP8-lane experts (when lane_mx)
   int* num_tiles_mx;
-  int4* tiles2;              // [ceil(P/256) + E] 256-row tiles of BF16-lane experts, or null
-  int* num_tiles2;
   int* order;                // [P] argsort(stable) permutation
   int* src_row;              // [P] token row of each sorted position
   int* rank;                 // [P] sorted position of each pair (inverse of order), or null
@@ -198,8 +196,6 @@ int launch_gemm(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t
 // CTA-pair (cluster of 2, cta_group::2) GEMM: 256-row tiles of a TMA-loaded A.
 size_t gemm_pair_smem_bytes(int bn, int stages);
 int gemm_pair_pick_stages(int bn);
-constexpr int kPairGatherDepth = 4;  // cp.async stage groups a pair-gather producer warp keeps in flight
-int launch_gemm_pair_gather(const GemmArgs& a, int max_tiles, int grid_n, cudaStream_t stream);
 int launch_gemm_pair(int epi, const GemmArgs& a, int grid_m, int grid_n, cudaStream_t stream);
 
 // Router calibration loss term and NLL attribution (calibration.cu).

@@ -64,32 +64,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// try_wait with cluster-scope acquire: pairs with arrivals released at
-// cluster scope by the other CTA of a pair.
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* status, int code) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t start = global_ns();
-  while (true) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if (global_ns() - start > SPX_WAIT_NS) {
-      record_error(status, code);
-      return false;
-    }
-  }
-}
-
 // Wait until the phase with the given parity has completed.  Returns false
 // (and records `code`) when the wait exceeds SPX_WAIT_NS.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
