@@ -644,9 +644,9 @@ int stage_expert_gemms(const Ctx& c, const uint16_t* xa, const int* src_row, con
 // K3: expert GEMM1 (+SwiGLU) and GEMM2 over the dispatched rows of `hidden`
 // (`xa` = hidden padded), both lanes; weighted rows land in Y (sorted order).
 int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hidden, const uint16_t* xa,
-                  const DispatchArgs& da, int64_t ld_hidden = 0) {
+                  const DispatchArgs& da, int64_t ld_hidden = 0, bool x_quantized = false) {
   const bool mx = da.lane_mx != nullptr;
-  if (mx) {
+  if (mx && !x_quantized) {
     const int rc = c.s.nv ? stage_quantize_nv_x(c, hidden, ld_hidden, da) : stage_quantize_x(c, hidden, ld_hidden);
     if (rc != SPX_OK) return rc;
   }
@@ -1148,6 +1148,25 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   c.mark(0);
   const uint16_t* xa = nullptr;
   if ((rc = stage_pad(c, hidden, &xa)) != SPX_OK) return rc;
+  // ---- side stream: work that needs only the hidden rows runs beside the
+  // router, selection and dispatch -- the MXFP8 quantisation of the rows
+  // (memory-bound, beside the instruction-bound selection) and, for
+  // decode-sized batches, the shared SwiGLU's gate/up projection.  Large
+  // batches keep the shared GEMM on the main stream: its persistent grid
+  // would hold every SM the selection kernels need.
+  const bool fork_mx = s.mx && !s.nv && w->expert_lane_mxfp8 != nullptr;
+  const bool fork_shared = s.small && s.S > 0;
+  SideStream ss{};
+  const bool forked = (fork_mx || fork_shared) && side_stream(c.st, &ss);
+  if (forked) {
+    if (cudaEventRecord(ss.fork, c.st) != cudaSuccess || cudaStreamWaitEvent(ss.side, ss.fork, 0) != cudaSuccess)
+      return SPX_ERR_CUDA;
+    const Ctx cs{s, L, workspace, ss.side, c.status, nullptr};
+    if (fork_mx && (rc = stage_quantize_x(cs, hidden, 0)) != SPX_OK) return rc;
+    if (cudaEventRecord(ss.join_a, ss.side) != cudaSuccess) return SPX_ERR_CUDA;
+    if (fork_shared && (rc = stage_shared_gemm1(cs, w, xa)) != SPX_OK) return rc;
+    if (cudaEventRecord(ss.join_b, ss.side) != cudaSuccess) return SPX_ERR_CUDA;
+  }
   // ---- K1: router GEMM (unless logits are injected), scores, top-k, weights,
   // load-balance partials
   if ((rc = stage_router_route(c, dims, w, xa, out)) != SPX_OK) return rc;
@@ -1157,16 +1176,22 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   if ((rc = launch_dispatch(da, c.st)) != SPX_OK) return rc;
   c.mark(3);
   // ---- K3: grouped experts (both lanes)
-  if ((rc = stage_experts(c, w, hidden, xa, da)) != SPX_OK) return rc;
+  if (forked && fork_mx && cudaStreamWaitEvent(c.st, ss.join_a, 0) != cudaSuccess) return SPX_ERR_CUDA;
+  if ((rc = stage_experts(c, w, hidden, xa, da, 0, forked && fork_mx)) != SPX_OK) return rc;
   // ---- K4: shared SwiGLU, then update = shared + the token's k weighted expert rows
+  if (forked && cudaStreamWaitEvent(c.st, ss.join_b, 0) != cudaSuccess) return SPX_ERR_CUDA;
+  const bool shared1_done = forked && fork_shared;
+  if (shared1_done) c.mark(6);
   uint16_t* y = at<uint16_t>(workspace, L.y);
   if (fused_combine_ok(s)) {
-    if ((rc = stage_shared(c, w, xa, out->update, y, da.rank)) != SPX_OK) return rc;
+    if (!shared1_done && (rc = stage_shared_gemm1(c, w, xa)) != SPX_OK) return rc;
+    if ((rc = stage_shared_gemm2(c, w, out->update, y, da.rank)) != SPX_OK) return rc;
   } else {
     uint16_t* so = nullptr;
     if (s.S > 0) {
       so = at<uint16_t>(workspace, L.shared_out);
-      if ((rc = stage_shared(c, w, xa, so)) != SPX_OK) return rc;
+      if (!shared1_done && (rc = stage_shared_gemm1(c, w, xa)) != SPX_OK) return rc;
+      if ((rc = stage_shared_gemm2(c, w, so)) != SPX_OK) return rc;
     } else {
       c.mark(6);
     }

@@ -172,6 +172,13 @@ struct GemmArgs {
 int device_sm_count();
 // Raise `func`'s dynamic shared memory limit to the device maximum once per device.
 int ensure_max_dynamic_smem(const void* func);
+// A side stream beside the caller's stream `main` (see launch.cu); false when
+// none can be made (e.g. the first call is inside a stream capture).
+struct SideStream {
+  cudaStream_t side;
+  cudaEvent_t fork, join_a, join_b;
+};
+bool side_stream(cudaStream_t main, SideStream* out);
 // How many 2-CTA clusters of `func` (with `smem` dynamic bytes) fit on the device at once.
 int device_max_pairs(const void* func, size_t smem);
 

@@ -1,7 +1,9 @@
 // Host-side launch helpers shared by the kernels: cached per-device queries.
 #include <cuda_runtime.h>
 
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "kernels.h"
 
@@ -32,6 +34,48 @@ int device_sm_count() {
     g_sm_count[dev] = n;
   }
   return g_sm_count[dev];
+}
+
+// Side streams: one non-blocking stream (same priority) and three events per
+// (device, caller stream), created on the first call that is not being
+// captured and kept for the life of the process.  Work forked onto the side
+// stream joins the caller's stream through the events, so the pair behaves as
+// one stream to the caller (CUDA graph capture included).
+namespace {
+std::map<std::pair<int, cudaStream_t>, SideStream> g_side;
+}  // namespace
+
+bool side_stream(cudaStream_t main, SideStream* out) {
+  const int dev = current_device();
+  if (dev < 0) return false;
+  std::lock_guard<std::mutex> lock(g_mu);
+  const auto key = std::make_pair(dev, main);
+  auto it = g_side.find(key);
+  if (it != g_side.end()) {
+    *out = it->second;
+    return true;
+  }
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(main, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return false;  // create nothing inside a capture: the caller runs unforked
+  }
+  SideStream s{};
+  int prio = 0;
+  if (main != nullptr && cudaStreamGetPriority(main, &prio) != cudaSuccess) prio = 0;
+  if (cudaStreamCreateWithPriority(&s.side, cudaStreamNonBlocking, prio) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&s.join_a, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&s.join_b, cudaEventDisableTiming) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  g_side.emplace(key, s);
+  *out = s;
+  return true;
 }
 
 int ensure_max_dynamic_smem(const void* func) {
