@@ -53,7 +53,7 @@
 extern "C" {
 #endif
 
-#define SPX_ABI_VERSION 7
+#define SPX_ABI_VERSION 9
 
 #define SPX_OK 0
 #define SPX_ERR_INVALID_ARG -1
@@ -133,6 +133,10 @@ typedef struct spx_packed_weights {
    * spx_pack_weights_nvfp4 (E2M1 values and UE4M3 scale atoms) and this the
    * per-expert amax of gate, up, down ([E][4] float, the 4th unused). */
   const float* expert_nvfp4_amax;
+  /* [E] float reconstruction error of each expert's low-precision copies
+   * (spx_expert_quant_error), or NULL: the forward then reports zeros, as the
+   * reference does for bfloat16 / float32 expert weights. */
+  const float* expert_quant_error;
 } spx_packed_weights;
 
 typedef struct spx_layer_outputs {
@@ -154,6 +158,8 @@ typedef struct spx_layer_outputs {
                                       on `stream` at the stage boundaries below            */
   int32_t* pair_rank;              /* [T*k] sorted position of each pair (inverse of
                                       dispatch_order) | NULL; required by spx_layer_route  */
+  float* expert_quantization_error; /* [E] weights->expert_quant_error of the selected
+                                      experts, 0 for the others | NULL (bank.py:526-566)   */
 } spx_layer_outputs;
 
 /* Stage boundaries recorded into spx_layer_outputs.stage_events:
@@ -326,6 +332,27 @@ int spx_surprise_calibration(const uint16_t* router_scores, const int64_t* exper
 int spx_block_channel_forward(const spx_layer_dims* dims, const spx_packed_weights* weights,
                               const uint16_t* norm_weight, float eps, const uint16_t* hidden,
                               const spx_layer_outputs* outputs, uint16_t* hidden_out, void* workspace, void* stream);
+
+/* Reconstruction error of each expert's low-precision copies
+ * (MicroExpertBank.quantization_error with native_weight_reconstruction_error,
+ * mESmaC/spalmer experts/bank.py:568-592 and experts/native.py:391-417): for
+ * gate, up and down of expert e, W^T quantised row-wise along K (weight_format
+ * 1 = MXFP8, 2 = NVFP4 under the matrix's own per-tensor scale) and
+ * sum((W - bf16(deq))^2) / max(sum(W^2), 1e-12); expert_error[e] = the mean of
+ * the three (float).  From the BF16 masters in src; dims gives E, d, I.
+ * Compute it whenever the masters change and pass it as
+ * spx_packed_weights.expert_quant_error. */
+int spx_expert_quant_error(const spx_layer_dims* dims, const spx_reference_weights* src, int32_t weight_format,
+                           float* expert_error, void* stream);
+
+/* RMSNorm.forward (mESmaC/spalmer nn/norm.py:28-31) of BF16 rows: out[r] =
+ * bf16(bf16(h[r] * bf16(rsqrt(mean(float(h[r])^2) + eps))) * weight), the
+ * pass spx_block_channel_forward runs before the layer.  hidden [rows, d],
+ * out [rows, ld_out] with columns d..ld_out zeroed (ld_out >= d); d and
+ * ld_out multiples of 8, pointers 16-byte aligned, eps > 0.  The float sum
+ * of squares runs in the device's own order. */
+int spx_rmsnorm_rows(const uint16_t* hidden, const uint16_t* norm_weight, float eps, int64_t rows, int32_t d,
+                     uint16_t* out, int32_t ld_out, void* stream);
 
 /* ---- NVFP4 (experts/native.py:205-302, the ("nvfp4", "nvfp4") pair)
  * E2M1 values (two per byte, the even element in the low nibble), one UE4M3

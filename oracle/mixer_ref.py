@@ -442,3 +442,75 @@ def block_channel_forward(h_bits: np.ndarray, norm_w_bits: np.ndarray, eps: floa
     """``hidden_states + channel_update`` of ``modeling.py:302`` in BF16 (bits)."""
 
     return f32_to_bf16_bits((bf16_bits_to_f32(h_bits) + bf16_bits_to_f32(update_bits)).astype(np.float32))
+
+
+def reconstruction_error(w_t_bits: np.ndarray, weight_format: str) -> np.float32:
+    """``native_weight_reconstruction_error`` (experts/native.py:391-417) of one
+    expert matrix given as ``W^T`` [rows, K] (BF16 bits): the matrix packed the
+    way its GEMM reads it -- MXFP8 row-wise along K in 32-value blocks, or
+    NVFP4 in 16-value blocks under the matrix's own per-tensor scale -- then
+    dequantised to BF16, and ``sum((W - restored)^2) / max(sum(W^2), 1e-12)``
+    in float32 (the sums taken exactly and rounded once).  Zero padding of K
+    (and of the rows for NVFP4) adds nothing."""
+
+    w = bf16_bits_to_f32(w_t_bits).astype(np.float32)
+    rows, K = w.shape
+    if weight_format == "mxfp8":
+        from oracle.mxfp8 import dequantize_rows, quantize_rows
+
+        kp = -(-K // 32) * 32
+        padded = np.zeros((rows, kp), dtype=np.float32)
+        padded[:, :K] = w
+        q, sb = quantize_rows(padded)
+        restored = dequantize_rows(q, sb)[:, :K]
+    elif weight_format == "nvfp4":
+        from oracle.mxfp8 import E4M3_VALUES
+        from oracle.nvfp4 import BLOCK, TENSOR_DIV, e2m1_values, quantize_rows
+
+        codes, sb, amax = quantize_rows(w)
+        pts = np.float32(np.float32(amax) / TENSOR_DIV)
+        if not pts > 0:
+            restored = np.zeros_like(w)
+        else:
+            total = (pts * E4M3_VALUES[sb]).astype(np.float32)  # the per-block scale torchao applies
+            vals = e2m1_values(codes).reshape(rows, -1, BLOCK)
+            restored = (vals * total[..., None]).astype(np.float32).reshape(rows, -1)[:, :K]
+    elif weight_format in ("bfloat16", "float32"):
+        return np.float32(0.0)
+    else:
+        raise ValueError(f"no packed representation for {weight_format!r}")
+    restored = round_bf16(restored.astype(np.float32))
+    diff = w.astype(np.float64) - restored.astype(np.float64)
+    num = np.float32(np.sum(diff * diff))
+    den = np.float32(max(np.float32(np.sum(w.astype(np.float64) ** 2)), np.float32(1e-12)))
+    return np.float32(num / den)
+
+
+def expert_reconstruction_errors(gate_bits: np.ndarray, up_bits: np.ndarray, down_bits: np.ndarray,
+                                 weight_format: str, experts=None) -> np.ndarray:
+    """``MicroExpertBank._quantization_error_for_rows`` (experts/bank.py:568-592):
+    per expert, the mean of its gate, up and down reconstruction errors
+    (each projection's ``expert_matrix.t()``), in float32.  ``experts``
+    limits the computation to those ids (others stay 0)."""
+
+    E = gate_bits.shape[0]
+    out = np.zeros(E, dtype=np.float32)
+    ids = range(E) if experts is None else experts
+    for e in ids:
+        eg = reconstruction_error(np.ascontiguousarray(gate_bits[e].T), weight_format)
+        eu = reconstruction_error(np.ascontiguousarray(up_bits[e].T), weight_format)
+        ed = reconstruction_error(np.ascontiguousarray(down_bits[e].T), weight_format)
+        out[e] = np.float32(np.float32(np.float32(eg + eu) + ed) / np.float32(3.0))
+    return out
+
+
+def quantization_error(expert_ids: np.ndarray, gate_bits: np.ndarray, up_bits: np.ndarray, down_bits: np.ndarray,
+                       weight_format: str) -> np.ndarray:
+    """``MicroExpertBank.quantization_error`` (experts/bank.py:526-566): the
+    reconstruction error of every expert selected in ``expert_ids``, zero for
+    the others and for bfloat16 / float32 expert weights."""
+
+    if weight_format in ("bfloat16", "float32"):
+        return np.zeros(gate_bits.shape[0], dtype=np.float32)
+    selected = np.unique(np.asarray(expert_ids).reshape(-1))
+    return expert_reconstruction_errors(gate_bits, up_bits, down_bits, weight_format, experts=selected)

@@ -19,6 +19,7 @@ from spalmer_b200.experts import (
     SurpriseRouter,
     SwiGLU,
     dispatch,
+    rms_norm,
     route,
 )
 
@@ -36,5 +37,6 @@ __all__ = [
     "SurpriseRouter",
     "SwiGLU",
     "dispatch",
+    "rms_norm",
     "route",
 ]

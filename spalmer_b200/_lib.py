@@ -52,6 +52,8 @@ EXPORTED = (
     "spx_layer_backward_sizes",
     "spx_layer_backward",
     "spx_block_channel_forward",
+    "spx_rmsnorm_rows",
+    "spx_expert_quant_error",
     "spx_layer_paged_begin",
     "spx_layer_paged_experts",
     "spx_layer_paged_finish",
@@ -74,7 +76,7 @@ EXPORTED = (
     "spx_dispatch_static_status",
 )
 
-ABI_VERSION = 7
+ABI_VERSION = 9
 
 _vp = ctypes.c_void_p
 
@@ -137,6 +139,7 @@ class PackedWeights(ctypes.Structure):
         ("expert_w2_mx", _vp),
         ("expert_w2_mx_scales", _vp),
         ("expert_nvfp4_amax", _vp),
+        ("expert_quant_error", _vp),
     ]
 
 
@@ -156,6 +159,7 @@ class LayerOutputs(ctypes.Structure):
         ("router_logits", _vp),
         ("stage_events", _vp),
         ("pair_rank", _vp),
+        ("expert_quantization_error", _vp),
     ]
 
 
@@ -254,6 +258,11 @@ def load() -> ctypes.CDLL:
         "spx_block_channel_forward": (
             ctypes.c_int,
             [P(LayerDims), P(PackedWeights), _vp, ctypes.c_float, _vp, P(LayerOutputs), _vp, _vp, _vp],
+        ),
+        "spx_expert_quant_error": (ctypes.c_int, [P(LayerDims), P(ReferenceWeights), ctypes.c_int32, _vp, _vp]),
+        "spx_rmsnorm_rows": (
+            ctypes.c_int,
+            [_vp, _vp, ctypes.c_float, ctypes.c_int64, ctypes.c_int32, _vp, ctypes.c_int32, _vp],
         ),
         "spx_layer_paged_begin": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, P(LayerOutputs), _vp, _vp]),
         "spx_layer_paged_experts": (

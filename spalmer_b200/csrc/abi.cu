@@ -356,6 +356,8 @@ DispatchArgs layer_dispatch_args(const Ctx& c, const spx_layer_dims* dims, const
   da.aux_loss = out->auxiliary_loss != nullptr ? out->auxiliary_loss : at<uint16_t>(ws, L.aux);
   da.resident = w->resident_mask;
   da.execution_loop = dims->execution_loop;
+  da.recon_error = w->expert_quant_error;
+  da.quant_error = out->expert_quantization_error;
   da.pair_weights = out->routing_weights;
   da.sorted_weights = at<uint16_t>(ws, L.sorted_w);
   if (out->pair_rank != nullptr) da.rank = out->pair_rank;
@@ -1148,24 +1150,19 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   c.mark(0);
   const uint16_t* xa = nullptr;
   if ((rc = stage_pad(c, hidden, &xa)) != SPX_OK) return rc;
-  // ---- side stream: work that needs only the hidden rows runs beside the
-  // router, selection and dispatch -- the MXFP8 quantisation of the rows
-  // (memory-bound, beside the instruction-bound selection) and, for
-  // decode-sized batches, the shared SwiGLU's gate/up projection.  Large
-  // batches keep the shared GEMM on the main stream: its persistent grid
-  // would hold every SM the selection kernels need.
-  const bool fork_mx = s.mx && !s.nv && w->expert_lane_mxfp8 != nullptr;
-  const bool fork_shared = s.small && s.S > 0;
+  // ---- side stream: the MXFP8 quantisation of the hidden rows (memory-bound)
+  // runs beside the router, selection and dispatch (instruction-bound) for
+  // large batches.  Decode-sized batches keep one stream: there the extra
+  // fork/join edges cost more than the few microseconds they would hide.
+  const bool fork_mx = s.mx && !s.nv && !s.small && w->expert_lane_mxfp8 != nullptr;
   SideStream ss{};
-  const bool forked = (fork_mx || fork_shared) && side_stream(c.st, &ss);
+  const bool forked = fork_mx && side_stream(c.st, &ss);
   if (forked) {
     if (cudaEventRecord(ss.fork, c.st) != cudaSuccess || cudaStreamWaitEvent(ss.side, ss.fork, 0) != cudaSuccess)
       return SPX_ERR_CUDA;
     const Ctx cs{s, L, workspace, ss.side, c.status, nullptr};
-    if (fork_mx && (rc = stage_quantize_x(cs, hidden, 0)) != SPX_OK) return rc;
-    if (cudaEventRecord(ss.join_a, ss.side) != cudaSuccess) return SPX_ERR_CUDA;
-    if (fork_shared && (rc = stage_shared_gemm1(cs, w, xa)) != SPX_OK) return rc;
-    if (cudaEventRecord(ss.join_b, ss.side) != cudaSuccess) return SPX_ERR_CUDA;
+    if ((rc = stage_quantize_x(cs, hidden, 0)) != SPX_OK) return rc;
+    if (cudaEventRecord(ss.join, ss.side) != cudaSuccess) return SPX_ERR_CUDA;
   }
   // ---- K1: router GEMM (unless logits are injected), scores, top-k, weights,
   // load-balance partials
@@ -1176,21 +1173,18 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   if ((rc = launch_dispatch(da, c.st)) != SPX_OK) return rc;
   c.mark(3);
   // ---- K3: grouped experts (both lanes)
-  if (forked && fork_mx && cudaStreamWaitEvent(c.st, ss.join_a, 0) != cudaSuccess) return SPX_ERR_CUDA;
-  if ((rc = stage_experts(c, w, hidden, xa, da, 0, forked && fork_mx)) != SPX_OK) return rc;
+  if (forked && cudaStreamWaitEvent(c.st, ss.join, 0) != cudaSuccess) return SPX_ERR_CUDA;
+  if ((rc = stage_experts(c, w, hidden, xa, da, 0, forked)) != SPX_OK) return rc;
   // ---- K4: shared SwiGLU, then update = shared + the token's k weighted expert rows
-  if (forked && cudaStreamWaitEvent(c.st, ss.join_b, 0) != cudaSuccess) return SPX_ERR_CUDA;
-  const bool shared1_done = forked && fork_shared;
-  if (shared1_done) c.mark(6);
   uint16_t* y = at<uint16_t>(workspace, L.y);
   if (fused_combine_ok(s)) {
-    if (!shared1_done && (rc = stage_shared_gemm1(c, w, xa)) != SPX_OK) return rc;
+    if ((rc = stage_shared_gemm1(c, w, xa)) != SPX_OK) return rc;
     if ((rc = stage_shared_gemm2(c, w, out->update, y, da.rank)) != SPX_OK) return rc;
   } else {
     uint16_t* so = nullptr;
     if (s.S > 0) {
       so = at<uint16_t>(workspace, L.shared_out);
-      if (!shared1_done && (rc = stage_shared_gemm1(c, w, xa)) != SPX_OK) return rc;
+      if ((rc = stage_shared_gemm1(c, w, xa)) != SPX_OK) return rc;
       if ((rc = stage_shared_gemm2(c, w, so)) != SPX_OK) return rc;
     } else {
       c.mark(6);
@@ -1247,6 +1241,25 @@ int spx_block_channel_forward(const spx_layer_dims* dims, const spx_packed_weigh
   }
   c.mark(7);
   return SPX_OK;
+}
+
+int spx_expert_quant_error(const spx_layer_dims* dims, const spx_reference_weights* src, int32_t weight_format,
+                           float* expert_error, void* stream) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (src == nullptr || src->gate_proj == nullptr || src->up_proj == nullptr || src->down_proj == nullptr ||
+      expert_error == nullptr)
+    return SPX_ERR_INVALID_ARG;
+  if (weight_format != 1 && weight_format != 2) return SPX_ERR_INVALID_ARG;
+  return launch_expert_quant_error(src->gate_proj, src->up_proj, src->down_proj, s.E, s.d, s.I, weight_format,
+                                   expert_error, static_cast<cudaStream_t>(stream));
+}
+
+int spx_rmsnorm_rows(const uint16_t* hidden, const uint16_t* norm_weight, float eps, int64_t rows, int32_t d,
+                     uint16_t* out, int32_t ld_out, void* stream) {
+  if (rows < 0 || d <= 0) return SPX_ERR_INVALID_ARG;
+  if (rows > 0 && (hidden == nullptr || norm_weight == nullptr || out == nullptr)) return SPX_ERR_INVALID_ARG;
+  return launch_rmsnorm_rows(hidden, norm_weight, eps, rows, d, out, ld_out, static_cast<cudaStream_t>(stream));
 }
 
 int spx_layer_route(const spx_layer_dims* dims, const spx_packed_weights* w, const uint16_t* hidden,

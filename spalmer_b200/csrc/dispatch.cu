@@ -203,6 +203,9 @@ __device__ __forceinline__ int finish_dispatch(const DispatchArgs& a, int count,
   // Utilization (losses.py:28-33): count / P in float32.
   const float util = (e < E) ? static_cast<float>(count) / static_cast<float>(a.pairs) : 0.0f;
   if (e < E && a.utilization != nullptr) a.utilization[e] = util;
+  // Quantization telemetry (bank.py:526-566): the error of every selected expert, zero elsewhere.
+  if (e < E && a.quant_error != nullptr)
+    a.quant_error[e] = (count > 0 && a.recon_error != nullptr) ? a.recon_error[e] : 0.0f;
 
   // Group statistics (mixer.py:257-297).
   // Warp reductions, then one thread folds the 32 warp results (no contended atomics).
@@ -308,6 +311,8 @@ __global__ void __launch_bounds__(1024) dispatch_small_kernel(const DispatchArgs
   const int E = a.num_experts;
   const int e = threadIdx.x;
   const int P = static_cast<int>(a.pairs);
+  griddep_wait();  // the expert ids, weights and load-balance partials come from the route kernel
+  griddep_launch_dependents();
   if (e < 1024) s_base[e] = 0;
   __syncthreads();
   const bool weights = a.sorted_weights != nullptr;
@@ -407,8 +412,7 @@ int launch_dispatch(const DispatchArgs& a, cudaStream_t stream) {
   if (a.pairs <= 0) return SPX_ERR_INVALID_ARG;
   if (a.num_experts > 1024) return SPX_ERR_UNSUPPORTED;
   if (a.pairs <= kDispatchSmallPairs) {
-    dispatch_small_kernel<<<1, 1024, 0, stream>>>(a);
-    return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+    return launch_pdl(dispatch_small_kernel, dim3(1), dim3(1024), 0, stream, a);
   }
   const int nchunks = static_cast<int>((a.pairs + kDispatchChunk - 1) / kDispatchChunk);
   dispatch_count_kernel<<<nchunks, kDispatchThreads, a.num_experts * sizeof(int), stream>>>(a);

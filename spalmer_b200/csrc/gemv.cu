@@ -1,35 +1,46 @@
-// Decode-sized projections: grouped GEMVs on the CUDA cores.
+// Decode-sized projections: grouped GEMVs.
 //
 // With a few tokens per step every routed expert sees a handful of rows, and
 // the projections are bound by reading their weights once (589,824 bytes per
 // expert in BF16 at the 100M shape).  A 128-row tcgen05 tile would hold those
-// few rows and spend its time filling and draining; here each CTA instead
-// pulls a slab of weight rows into shared memory with bulk asynchronous
-// copies (one or two cp.async.bulk per CTA, all of a slab in flight at once)
-// while its threads stage the token rows, then dots every token row with
-// every weight row from shared memory.
+// few rows and spend its time filling and draining; here every warp streams
+// its weight rows straight from HBM into registers (16-byte non-allocating
+// loads, several K chunks in flight per thread, no shared-memory slab, no
+// barrier inside the K loop) and multiplies them on mma.sync m16n8k16 (BF16
+// in, FP32 accumulate) against up to 16 token rows staged once per pass in
+// shared memory.  The weight rows are the 16-row A operand, the tokens the
+// 8-column B operand: the tensor cores run at a fraction of their rate and
+// still outrun the weight stream.
+//
+// Fragment layout.  The dot product is a sum over k, so A and B may read K in
+// any order as long as both use the same one.  Thread (gq = lane / 4,
+// tq = lane % 4) loads 16 contiguous bytes of its weight row at 8*tq of a
+// 32-value chunk (E4M3: 16 values at 16*tq of a 64-value chunk) and feeds
+// them as the a0/a2 registers of consecutive k16 steps; the B registers come
+// from the same positions of the token rows.  A warp instruction reads 8
+// rows x 64 contiguous bytes.
 //
 // Same rounding points as the tensor-core path (experts/bank.py:755-763 and
 // 970-978, nn/ffn.py:27-30, experts/router.py:51): FP32 accumulation;
 // SwiGLU h = bf16(bf16(silu(bf16(g))) * bf16(u)); projections
 // bf16(bf16(acc [+ bias]) * w).  MXFP8-lane experts (experts/native.py:91-140)
-// dot the E4M3 values with their E8M0 block scales applied: the activations'
-// blocks are dequantised exactly into BF16 (an E4M3 value times a power of two
-// is representable), the weights' into FP32, the products are summed in FP32,
+// multiply the E4M3 values with their E8M0 block scales applied: both
+// operands are dequantised exactly into BF16 (an E4M3 value times a power of
+// two is representable), their products are exact in FP32 and summed there,
 // and the SwiGLU GEMV writes the hidden rows quantised again (32-column
 // blocks, the epilogue rule of the tensor-core path).
 //
-// Two kernels:
-//   gemv_swiglu_kernel  a group's rows x [gate | up] slab of 16 hidden columns
-//                       (32 for the MXFP8 lane, one scale block) -> hidden rows
-//   gemv_rows_kernel    a group's rows x slab of N_blk output rows -> outputs
-//                       (+ bias, x routing weight), rows staged and stored
-//                       as whole row segments
+// Two kernels (128 threads, 4 warps; a warp owns one m-tile, or a K share of
+// one when few tiles would leave SMs idle):
+//   gemv_swiglu_kernel  m-tile = 8 gate + 8 up rows of 8 hidden columns, so a
+//                       thread's accumulators hold the gate and up values of
+//                       one column and the SwiGLU runs in registers
+//   gemv_rows_kernel    m-tile = 16 output columns (+ bias, x routing weight)
 // Expert passes run over the dispatch's tile tables (a tile = up to 128 rows
 // of one expert's dispatch range, token rows gathered through src_row); the
-// dense projections (router, shared SwiGLU) over the whole batch.  Each warp walks 4 weight rows at a time, one group of 8
-// lanes per row (16 bytes per lane per step), accumulators in registers for
-// up to 16 token rows per pass, reduced over the 8 lanes by shuffles.
+// dense projections (router, shared SwiGLU) over the whole batch in 16-row
+// chunks.
+#include <cuda_bf16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -44,12 +55,11 @@ namespace spx {
 
 namespace {
 
-constexpr int kGemvThreads = 256;
+constexpr int kGemvThreads = 128;
 constexpr int kGemvWarps = kGemvThreads / 32;
-constexpr int kGemvRows = 8;        // token rows per pass (one 8-column mma.sync tile)
-constexpr int kSwigluCols = 16;     // hidden columns per swiglu CTA (BF16 lane)
-constexpr int kSwigluColsMx = 32;   // ... MXFP8 lane (one scale block of the hidden row)
-constexpr size_t kSlabBytes = 48 * 1024;  // weight slab budget per CTA
+constexpr int kPassRows = 16;   // token rows per pass: two 8-column mma tiles
+constexpr int kRowPad = 32;     // token row padding in shared memory (values): rows 64 bytes apart mod 128
+constexpr int kRedBytes = kGemvWarps * 32 * 8 * static_cast<int>(sizeof(float));
 
 __device__ __forceinline__ float silu_ref(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
@@ -57,15 +67,6 @@ __device__ __forceinline__ float silu_ref(float x) { return __fdividef(x, 1.0f +
 __device__ __forceinline__ float e8m0_value(uint32_t byte) {
   if (byte == 0u) return __uint_as_float(0x00400000u);  // 2^-127
   return __uint_as_float(byte << 23);
-}
-
-__device__ __forceinline__ void bf16x8(const uint4& v, float* f) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    f[2 * q] = __uint_as_float(w[q] << 16);
-    f[2 * q + 1] = __uint_as_float(w[q] & 0xFFFF0000u);
-  }
 }
 
 // Four E4M3 bytes (one word) to floats, times `s`.
@@ -80,153 +81,92 @@ __device__ __forceinline__ void e4m3x4(uint32_t w, float s, float* f) {
   f[3] = b.y * s;
 }
 
-// Scale byte of (row, K block `blk` of 32) in the atoms of a packed MXFP8 weight:
-// atoms [groups][tiles][K/128][ceil(tile_rows/128)][512] (mx_quantize_b_kernel).
-__device__ __forceinline__ uint32_t w_scale(const uint8_t* atoms, int g, int row, int blk, int rows_per_group,
-                                            int tile_rows, int kp) {
-  const int tiles = (rows_per_group + tile_rows - 1) / tile_rows;
-  const int per_tile = (tile_rows + 127) / 128;
-  const int tile = row / tile_rows, r = row - tile * tile_rows;
-  const int64_t atom = ((static_cast<int64_t>(g) * tiles + tile) * (kp / 128) + (blk >> 2)) * per_tile + (r >> 7);
-  return __ldg(atoms + atom * kMxAtomBytes + mx_atom_offset(r & 127, blk & 3));
+// Two floats that are BF16 values to a BF16 pair (lo in the low half).
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Contiguous global -> shared bulk copy completing on `bar` (16-byte aligned, size % 16 == 0).
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+// 16 bytes of a weight row, read once: no L1 allocation, 256-byte L2 fetches.
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 v;
+  asm("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p));
+  return v;
+}
+
+// 16 bytes of a staged token row.  Volatile, so that the loads stay between
+// the MMAs that use them instead of being hoisted (and held in registers)
+// ahead of a whole step.
+__device__ __forceinline__ uint4 lds128(const uint16_t* p) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(smem_u32(p)));
+  return v;
+}
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
   asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// One thread waits (bounded) for phase `parity` of the CTA's barrier; the
-// others wait at the CTA barrier that follows, so only one thread polls.  On
-// a timeout the status word records it, the thread waits once more (bounded)
-// for the copies still in flight, and every thread of the CTA returns.
-__device__ __forceinline__ bool pass_ready(uint64_t* bar, uint32_t parity, int* status, int* abort_flag) {
-  if (threadIdx.x == 0) {
-    bool ok = mbar_wait(bar, parity, status, SPX_DEV_TIMEOUT_PRODUCER);
-    if (!ok) mbar_wait(bar, parity, nullptr, 0);
-    *abort_flag = ok ? 0 : 1;
-  }
-  __syncthreads();
-  return *abort_flag == 0;
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 // Token rows into shared memory as BF16 [R][K] (row stride xstride values):
-// 16-byte copies, or E4M3 rows dequantised with their block scales (exact).
-// Row i of the pass is token row src[pos0 + i] (gather) or pos0 + i.
+// 16-byte cp.async copies (all in flight at once), or E4M3 rows dequantised
+// with their block scales (exact), loads batched ahead of the conversions.
+// Row i of the pass is token row src[pos0 + i] (gather) or pos0 + i.  The
+// caller waits (cp_async_wait_all) and synchronises.
 __device__ void stage_rows(bool mx, const int* src, int64_t pos0, int R, const uint16_t* rows_bf16, int64_t ld_bf16,
-                           const uint8_t* rows_q, const uint8_t* rows_sf, int64_t ld_q, int K, int xstride,
+                           const uint8_t* rows_q, const uint8_t* rows_sf, int ld_q, int K, int xstride,
                            uint16_t* xs) {
   if (!mx) {
     const int per_row = K / 8;
     for (int i = threadIdx.x; i < R * per_row; i += blockDim.x) {
       const int r = i / per_row, c = i - r * per_row;
       const int64_t row = src != nullptr ? src[pos0 + r] : pos0 + r;
-      reinterpret_cast<uint4*>(xs + static_cast<int64_t>(r) * xstride)[c] =
-          __ldg(reinterpret_cast<const uint4*>(rows_bf16 + row * ld_bf16) + c);
+      cp_async16(smem_u32(xs + static_cast<int64_t>(r) * xstride + 8 * c), rows_bf16 + row * ld_bf16 + 8 * c);
     }
     return;
   }
+  constexpr int kBatch = 2;
   const int per_row = K / 16;
-  for (int i = threadIdx.x; i < R * per_row; i += blockDim.x) {
-    const int r = i / per_row, c = i - r * per_row;
-    const int64_t row = src != nullptr ? src[pos0 + r] : pos0 + r;
-    const uint4 q = __ldg(reinterpret_cast<const uint4*>(rows_q + row * ld_q) + c);
-    const float s = e8m0_value(__ldg(rows_sf + row * (ld_q / kMxBlock) + (c >> 1)));
-    float f[16];
-    e4m3x4(q.x, s, f);
-    e4m3x4(q.y, s, f + 4);
-    e4m3x4(q.z, s, f + 8);
-    e4m3x4(q.w, s, f + 12);
-    uint32_t h[8];
+  for (int i0 = threadIdx.x; i0 < R * per_row; i0 += kBatch * blockDim.x) {
+    uint4 q[kBatch];
+    uint32_t sb[kBatch];
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      h[j] = static_cast<uint32_t>(f32_to_bf16_rne(f[2 * j])) |
-             (static_cast<uint32_t>(f32_to_bf16_rne(f[2 * j + 1])) << 16);
-    uint4* dst = reinterpret_cast<uint4*>(xs + static_cast<int64_t>(r) * xstride + c * 16);
-    dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
-    dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
-  }
-}
-
-// acc[j] += <weight row, token row j> over k < k_valid for the lane's K slots,
-// for NR token rows xs[0..NR) (all valid): lane `seg` of the row's 8-lane
-// group takes 16 bytes per step.  `wrow` is the weight row in shared memory
-// (BF16, or E4M3 with scales from global atoms).
-template <bool MX, int NR>
-__device__ __forceinline__ void dot_chunk(const uint8_t* wrow, const uint8_t* atoms, int g, int wr, int rows_per_group,
-                                          int tile_rows, int Kw, int K, int k_valid, const uint16_t* xs, int seg,
-                                          float (&acc)[NR]) {
-  constexpr int kEl = MX ? 16 : 8;  // values per lane per step
-  constexpr int kStep = 8 * kEl;
-#pragma unroll 2
-  for (int k = seg * kEl; k < k_valid; k += kStep) {
-    float w[kEl];
-    if constexpr (MX) {
-      const uint4 q = *reinterpret_cast<const uint4*>(wrow + k);
-      const float s = e8m0_value(w_scale(atoms, g, wr, k / kMxBlock, rows_per_group, tile_rows, Kw));
-      e4m3x4(q.x, s, w);
-      e4m3x4(q.y, s, w + 4);
-      e4m3x4(q.z, s, w + 8);
-      e4m3x4(q.w, s, w + 12);
-    } else {
-      bf16x8(*reinterpret_cast<const uint4*>(wrow + 2 * k), w);
+    for (int j = 0; j < kBatch; ++j) {
+      const int i = i0 + j * blockDim.x;
+      if (i < R * per_row) {
+        const int r = i / per_row, c = i - r * per_row;
+        const int64_t row = src != nullptr ? src[pos0 + r] : pos0 + r;
+        q[j] = __ldg(reinterpret_cast<const uint4*>(rows_q + row * ld_q) + c);
+        sb[j] = __ldg(rows_sf + row * (ld_q / kMxBlock) + (c >> 1));
+      }
     }
 #pragma unroll
-    for (int i = 0; i < NR; ++i) {
-      const uint4* xp = reinterpret_cast<const uint4*>(xs + static_cast<int64_t>(i) * K + k);
-#pragma unroll
-      for (int h = 0; h < kEl / 8; ++h) {
-        float x[8];
-        bf16x8(xp[h], x);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i] = fmaf(w[8 * h + j], x[j], acc[i]);
+    for (int j = 0; j < kBatch; ++j) {
+      const int i = i0 + j * blockDim.x;
+      if (i < R * per_row) {
+        const int r = i / per_row, c = i - r * per_row;
+        const float s = e8m0_value(sb[j]);
+        float f[16];
+        e4m3x4(q[j].x, s, f);
+        e4m3x4(q[j].y, s, f + 4);
+        e4m3x4(q[j].z, s, f + 8);
+        e4m3x4(q[j].w, s, f + 12);
+        uint4* dst = reinterpret_cast<uint4*>(xs + static_cast<int64_t>(r) * xstride + c * 16);
+        dst[0] = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                            pack_bf16x2(f[6], f[7]));
+        dst[1] = make_uint4(pack_bf16x2(f[8], f[9]), pack_bf16x2(f[10], f[11]), pack_bf16x2(f[12], f[13]),
+                            pack_bf16x2(f[14], f[15]));
       }
     }
   }
-}
-
-// All R token rows of a pass against one weight row, in chunks of 4, 2 and 1
-// rows (no issue slots spent on absent rows); emit(i, partial) receives each
-// row's lane partial sum (every lane of the warp calls it, in the same order).
-template <bool MX, typename Emit>
-__device__ __forceinline__ void dot_rows(const uint8_t* wrow, const uint8_t* atoms, int g, int wr, int rows_per_group,
-                                         int tile_rows, int Kw, int K, int k_valid, const uint16_t* xs, int R,
-                                         int seg, bool live, Emit emit) {
-  int i0 = 0;
-  for (; i0 + 4 <= R; i0 += 4) {
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    if (live)
-      dot_chunk<MX, 4>(wrow, atoms, g, wr, rows_per_group, tile_rows, Kw, K, k_valid,
-                       xs + static_cast<int64_t>(i0) * K, seg, acc);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) emit(i0 + j, acc[j]);
-  }
-  if (i0 + 2 <= R) {
-    float acc[2] = {0.0f, 0.0f};
-    if (live)
-      dot_chunk<MX, 2>(wrow, atoms, g, wr, rows_per_group, tile_rows, Kw, K, k_valid,
-                       xs + static_cast<int64_t>(i0) * K, seg, acc);
-    emit(i0, acc[0]);
-    emit(i0 + 1, acc[1]);
-    i0 += 2;
-  }
-  if (i0 < R) {
-    float acc[1] = {0.0f};
-    if (live)
-      dot_chunk<MX, 1>(wrow, atoms, g, wr, rows_per_group, tile_rows, Kw, K, k_valid,
-                       xs + static_cast<int64_t>(i0) * K, seg, acc);
-    emit(i0, acc[0]);
-  }
-}
-
-__device__ __forceinline__ float group_sum8(float v) {
-  v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
-  v += __shfl_xor_sync(0xFFFFFFFFu, v, 2);
-  v += __shfl_xor_sync(0xFFFFFFFFu, v, 4);
-  return v;
 }
 
 // The rows of this CTA's tile: weight group g, lane, rows [start, start + n)
@@ -257,408 +197,484 @@ __device__ __forceinline__ void tile_rows(const GemvPass& a, int& g, bool& mx, i
   n = tile.z;
 }
 
-// The row GEMV's BF16 tiles run on the tensor cores when the column block
-// splits into 16-row m-tiles that divide the 8 warps and the K range splits
-// evenly over the remaining warp factor in steps of 16.
-__host__ __device__ __forceinline__ bool gemv_rows_tc(const GemvPass& a) {
-  if (a.nblk % 16 != 0 || a.nblk > 16 * kGemvWarps) return false;
-  const int mtiles = a.nblk / 16;
-  if (kGemvWarps % mtiles != 0) return false;
-  return a.k_valid2 % (16 * (kGemvWarps / mtiles)) == 0;
-}
+// ---- A warp's weight stream.  A step is U chunks of 32 values (BF16) or
+// U / 2 chunks of 64 (E4M3) of the thread's two A rows, all its loads issued
+// before the step multiplies.
+template <bool MX, int U>
+struct WBuf;
+template <int U>
+struct WBuf<false, U> {
+  static constexpr int kStep = 32 * U;
+  uint4 l[U], h[U];
+};
+template <int U>
+struct WBuf<true, U> {
+  static constexpr int kN = U / 2;
+  static constexpr int kStep = 64 * kN;
+  uint4 l[kN], h[kN];
+  float sl[kN], sh[kN];
+};
 
-// ---- BF16 tiles on the tensor cores: mma.sync m16n8k16 (BF16 in, FP32
-// accumulate) with the weight rows as the 16-row A operand and up to 8 token
-// rows as the B operand, both read from shared memory by ldmatrix.  Rows in
-// shared memory are padded by 16 bytes so that the 8 row addresses of an
-// 8x8 ldmatrix fall in distinct banks.
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
+// The thread's A rows of one m-tile: rows gq (lo) and gq + 8 (hi).
+struct ARows {
+  const uint8_t* lo;  // row starts (bytes)
+  const uint8_t* hi;
+  const uint8_t* sc_lo;  // MXFP8: the rows' scale bytes of K block 0 (mx_scale_row)
+  const uint8_t* sc_hi;
+};
 
-__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t (&r)[2]) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
-}
+// Scale-atom layout of a packed MXFP8 weight: atoms [groups][tiles][K/128]
+// [ceil(tile_rows/128)][512] (mx_quantize_b_kernel).  The scale byte of
+// (row, K block blk) is row_ptr[(blk / 4) * stride + blk % 4] with
+// row_ptr = mx_scale_row(row) and stride = 512 * ceil(tile_rows / 128).
+struct MxAtoms {
+  const uint8_t* atoms;
+  int g, rows_per_group, tile_rows, kp;
+  __device__ __forceinline__ int stride() const { return kMxAtomBytes * ((tile_rows + 127) / 128); }
+  __device__ __forceinline__ const uint8_t* row(int r) const {
+    const int tiles = (rows_per_group + tile_rows - 1) / tile_rows;
+    const int per_tile = (tile_rows + 127) / 128;
+    const int tile = r / tile_rows, rr = r - tile * tile_rows;
+    const int64_t atom = ((static_cast<int64_t>(g) * tiles + tile) * (kp / 128)) * per_tile + (rr >> 7);
+    return atoms + atom * kMxAtomBytes + mx_atom_offset(rr & 127, 0);
+  }
+};
 
-__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
-}
-
-// One warp: D[16 x 8 tokens] over k in [k0, k1).  a_row(m) gives the
-// shared-memory byte offset of A row m (0..15) of the tile.
-template <typename ARow>
-__device__ __forceinline__ void mma_rows(uint32_t slab_u32, ARow a_row, uint32_t xs_u32, int xs_stride, int k0,
-                                         int k1, int lane, float (&d)[4]) {
+template <int U>
+__device__ __forceinline__ void load_step(const ARows& r, int k0, int ke, int tq, const MxAtoms&, WBuf<false, U>& b) {
 #pragma unroll
-  for (int q = 0; q < 4; ++q) d[q] = 0.0f;
-  // ldmatrix row addresses: A matrices 0..3 = (rows 0-7 | 8-15) x (k | k+8);
-  // B matrices 0, 1 = tokens 0-7 x (k | k+8)
-  const int mi = lane >> 3, ri = lane & 7;
-  const uint32_t a_base = slab_u32 + a_row((mi & 1) * 8 + ri) + static_cast<uint32_t>((mi >> 1) * 16);
-  const uint32_t b_base = xs_u32 + static_cast<uint32_t>(ri * xs_stride + (mi & 1) * 16);
-#pragma unroll 4
-  for (int k = k0; k < k1; k += 16) {
-    uint32_t a[4];
-    ldsm_x4(a_base + 2 * k, a);
-    uint32_t b[2];
-    ldsm_x2(b_base + 2 * k, b);
-    mma_16816(d, a, b);
+  for (int u = 0; u < U; ++u) {
+    const int k = k0 + 32 * u + 8 * tq;
+    b.l[u] = k < ke ? ld_stream(r.lo + 2 * k) : make_uint4(0u, 0u, 0u, 0u);
+    b.h[u] = k < ke ? ld_stream(r.hi + 2 * k) : make_uint4(0u, 0u, 0u, 0u);
   }
 }
 
-// SwiGLU GEMV: gate/up of one block of hidden columns of group g for its rows.
-__global__ void __launch_bounds__(kGemvThreads, 3) gemv_swiglu_kernel(const GemvPass a) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  int g, n;
-  bool mx;
-  int64_t start;
-  tile_rows(a, g, mx, start, n);
-  if (n <= static_cast<int>(blockIdx.z) * kGemvRows) return;
-  const int cols = mx ? kSwigluColsMx : kSwigluCols;
-  const int j0 = blockIdx.y * kSwigluCols;
-  if (mx && (j0 % kSwigluColsMx) != 0) return;  // MXFP8 CTAs take two column blocks
-  if (j0 >= a.inter) return;
-  const int c = mx ? a.cm : a.chunk;
-  const int rows1 = (mx ? a.ncm : a.nc) * 2 * c;
-  const int K = mx ? a.kx : a.kd;                    // token row width (BF16 values) in shared memory
-  const int wbytes = mx ? a.kx : 2 * a.kd;           // weight row bytes
-  const int ws = wbytes + 16;                        // padded row strides in shared memory
-  const int xsb = 2 * K + 16;
-  const int ncol = min(cols, a.inter - j0);
-  // slab rows: gate rows [0, cols) then up rows [cols, 2 cols) of packed rows g0.. and g0 + c..
-  const int ch = j0 / c;
-  const int g0 = ch * 2 * c + (j0 - ch * c);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-  int* abort_flag = reinterpret_cast<int*>(smem + 64);
-  uint8_t* slab = smem + 128;
-  uint8_t* xsp = slab + 2 * static_cast<size_t>(cols) * ws;
-  float* red = reinterpret_cast<float*>(xsp + static_cast<size_t>(kGemvRows) * xsb);  // [8 warps][32][4]
-  uint16_t* hs = reinterpret_cast<uint16_t*>(red);  // MXFP8 lane: [kGemvRows][32] BF16 hidden values
-  const uint8_t* wbase = mx ? a.w1q : reinterpret_cast<const uint8_t*>(a.w1);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint32_t pass = 0;
-  for (int r0 = blockIdx.z * kGemvRows; r0 < n; r0 += gridDim.z * kGemvRows, ++pass) {
-    const int R = min(kGemvRows, n - r0);
-    if (warp == 0) {
-      const uint32_t bytes = (pass == 0 ? 2u * ncol * wbytes : 0u) + (mx ? 0u : static_cast<uint32_t>(R) * 2 * K);
-      if (lane == 0) {
-        if (pass == 0) {
-          mbar_init(bar, 1);
-          fence_mbar_init();
-        } else {
-          fence_proxy_async_smem();  // the previous pass's reads of the rows before the async writes below
-        }
-        if (bytes) mbar_arrive_expect_tx(bar, bytes); else mbar_arrive(bar);
-      }
-      __syncwarp();
-      if (pass == 0) {
-        for (int i = lane; i < 2 * ncol; i += 32) {
-          const int half = i / ncol, jl = i - half * ncol;
-          bulk_load(slab + static_cast<size_t>(half * cols + jl) * ws,
-                    wbase + (static_cast<int64_t>(g) * rows1 + g0 + half * c + jl) * wbytes, wbytes, bar);
-        }
-      }
-      if (!mx) {
-        for (int i = lane; i < R; i += 32) {
-          const int64_t row = a.src_row != nullptr ? a.src_row[start + r0 + i] : start + r0 + i;
-          bulk_load(xsp + static_cast<size_t>(i) * xsb, a.x + row * a.ldx, 2u * K, bar);
-        }
-      }
-    }
-    if (mx) stage_rows(true, a.src_row, start + r0, R, a.x, a.ldx, a.xq, a.xsf, a.kx, a.kx, xsb / 2,
-                       reinterpret_cast<uint16_t*>(xsp));
-    // token rows R..15 of the tiles read by the tensor cores are zero
-    for (int i = threadIdx.x; i < (kGemvRows - R) * (K / 8); i += blockDim.x) {
-      const int r = R + i / (K / 8), q = i % (K / 8);
-      reinterpret_cast<uint4*>(xsp + static_cast<size_t>(r) * xsb)[q] = make_uint4(0u, 0u, 0u, 0u);
-    }
-    if (!pass_ready(bar, pass & 1u, a.status, abort_flag)) return;
-    if (!mx) {
-      // warps: m-tile mt = warp & 1 (8 hidden columns: 8 gate rows + 8 up rows),
-      // K quarter ks = warp >> 1; partial sums reduced in shared memory
-      const int mt = warp & 1, ks = warp >> 1;
-      const int kq = K / 4;
-      float d[4];
-      auto a_row = [&](int m) -> uint32_t {
-        const int jl = mt * 8 + (m & 7);
-        return static_cast<uint32_t>(((m >> 3) * cols + jl) * ws);  // m < 8: gate row jl, else up row jl
-      };
-      mma_rows(smem_u32(slab), a_row, smem_u32(xsp), xsb, ks * kq, (ks + 1) * kq, lane, d);
-      *reinterpret_cast<float4*>(red + (warp * 32 + lane) * 4) = make_float4(d[0], d[1], d[2], d[3]);
-      __syncthreads();
-      if (ks == 0) {
-        const int gq = lane >> 2, tq = lane & 3;
-        const int jl = mt * 8 + gq;
-        float4 sum = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+template <int U>
+__device__ __forceinline__ void load_step(const ARows& r, int k0, int ke, int tq, const MxAtoms& m, WBuf<true, U>& b) {
+  const int stride = m.stride();
 #pragma unroll
-        for (int s2 = 0; s2 < 4; ++s2) {
-          const float4 v = *reinterpret_cast<const float4*>(red + ((mt + 2 * s2) * 32 + lane) * 4);
-          sum.x += v.x;
-          sum.y += v.y;
-          sum.z += v.z;
-          sum.w += v.w;
-        }
-        // (x, y): gate of column jl for tokens 2tq, 2tq+1; (z, w): up of the same
+  for (int u = 0; u < WBuf<true, U>::kN; ++u) {
+    const int k = k0 + 64 * u + 16 * tq;
+    const bool v = k < ke;
+    const int blk = k / kMxBlock, so = (blk >> 2) * stride + (blk & 3);
+    b.l[u] = v ? ld_stream(r.lo + k) : make_uint4(0u, 0u, 0u, 0u);
+    b.h[u] = v ? ld_stream(r.hi + k) : make_uint4(0u, 0u, 0u, 0u);
+    b.sl[u] = v ? e8m0_value(__ldg(r.sc_lo + so)) : 0.0f;
+    b.sh[u] = v ? e8m0_value(__ldg(r.sc_hi + so)) : 0.0f;
+  }
+}
+
+// acc[t] += A[16 rows] . X[8t .. 8t+8)^T for one step (whole thread slots
+// past ke read as zero on both sides).
+template <int U>
+__device__ __forceinline__ void mma_step(const WBuf<false, U>& b, const uint16_t* xs, int xsl, int k0, int ke, int nt,
+                                         int gq, int tq, float (&acc)[2][4]) {
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    if (k0 + 32 * u >= ke) break;  // warp-uniform
+    const int k = k0 + 32 * u + 8 * tq;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      if (t >= nt) break;
+      const uint4 x = k < ke ? lds128(xs + (8 * t + gq) * xsl + k) : make_uint4(0u, 0u, 0u, 0u);
+      mma_16816(acc[t], b.l[u].x, b.h[u].x, b.l[u].y, b.h[u].y, x.x, x.y);
+      mma_16816(acc[t], b.l[u].z, b.h[u].z, b.l[u].w, b.h[u].w, x.z, x.w);
+    }
+  }
+}
+
+template <int U>
+__device__ __forceinline__ void mma_step(const WBuf<true, U>& b, const uint16_t* xs, int xsl, int k0, int ke, int nt,
+                                         int gq, int tq, float (&acc)[2][4]) {
+#pragma unroll
+  for (int u = 0; u < WBuf<true, U>::kN; ++u) {
+    if (k0 + 64 * u >= ke) break;  // warp-uniform
+    const int k = k0 + 64 * u + 16 * tq;
+    uint32_t xw[2][8];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      uint4 x0 = make_uint4(0u, 0u, 0u, 0u), x1 = x0;
+      if (t < nt && k < ke) {
+        x0 = lds128(xs + (8 * t + gq) * xsl + k);
+        x1 = lds128(xs + (8 * t + gq) * xsl + k + 8);
+      }
+      xw[t][0] = x0.x, xw[t][1] = x0.y, xw[t][2] = x0.z, xw[t][3] = x0.w;
+      xw[t][4] = x1.x, xw[t][5] = x1.y, xw[t][6] = x1.z, xw[t][7] = x1.w;
+    }
+    const uint32_t lw[4] = {b.l[u].x, b.l[u].y, b.l[u].z, b.l[u].w};
+    const uint32_t hw[4] = {b.h[u].x, b.h[u].y, b.h[u].z, b.h[u].w};
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      float fl[4], fh[4];
+      e4m3x4(lw[s], b.sl[u], fl);
+      e4m3x4(hw[s], b.sh[u], fh);
+      const uint32_t a0 = pack_bf16x2(fl[0], fl[1]), a2 = pack_bf16x2(fl[2], fl[3]);
+      const uint32_t a1 = pack_bf16x2(fh[0], fh[1]), a3 = pack_bf16x2(fh[2], fh[3]);
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (t >= nt) break;
+        mma_16816(acc[t], a0, a1, a2, a3, xw[t][2 * s], xw[t][2 * s + 1]);
+      }
+    }
+  }
+}
+
+// `steps` steps over m-tiles m = s / G (K group s % G from kb); b holds step
+// 0's loads on entry (issued before the token rows were staged).  end_tile(m)
+// runs after m-tile m's last K group.  One register buffer: the warps of the
+// SM (five CTAs of four) keep the weight stream busy between one warp's
+// steps.
+template <bool MX, int U, typename RowsOf, typename EndTile>
+__device__ __forceinline__ void run_stream(int steps, int G, int kb, int ke, RowsOf rows_of, const MxAtoms& ma,
+                                           const uint16_t* xs, int xsl, int nt, int gq, int tq, WBuf<MX, U>& b,
+                                           float (&acc)[2][4], EndTile end_tile) {
+  constexpr int kStep = WBuf<MX, U>::kStep;
+#pragma unroll 1
+  for (int s = 0; s < steps; ++s) {
+    if (s > 0) load_step(rows_of(s / G), kb + (s % G) * kStep, ke, tq, ma, b);
+    mma_step(b, xs, xsl, kb + (s % G) * kStep, ke, nt, gq, tq, acc);
+    if (s % G == G - 1) end_tile(s / G);
+  }
+}
+
+// Warps sharing an m-tile (ks > 0) add their partial sums into warp ks = 0's
+// accumulators through shared memory.  Every thread of the CTA calls it.
+__device__ __forceinline__ void reduce_ksplit(float* red, int ksplit, int mtiles, int mt, int ks, int lane,
+                                              float (&acc)[2][4]) {
+  if (ksplit == 1) return;
+  if (ks > 0) {
+    float4* dst = reinterpret_cast<float4*>(red + ((threadIdx.x >> 5) * 32 + lane) * 8);
+    dst[0] = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+    dst[1] = make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]);
+  }
+  __syncthreads();
+  if (ks == 0) {
+    for (int s = 1; s < ksplit; ++s) {
+      const float4* src = reinterpret_cast<const float4*>(red + ((s * mtiles + mt) * 32 + lane) * 8);
+      const float4 p0 = src[0], p1 = src[1];
+      acc[0][0] += p0.x;
+      acc[0][1] += p0.y;
+      acc[0][2] += p0.z;
+      acc[0][3] += p0.w;
+      acc[1][0] += p1.x;
+      acc[1][1] += p1.y;
+      acc[1][2] += p1.z;
+      acc[1][3] += p1.w;
+    }
+  }
+}
+
+__device__ __forceinline__ void zero_acc(float (&acc)[2][4]) {
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[t][q] = 0.0f;
+}
+
+// SwiGLU GEMV: hidden[pos, j] for 8 columns per m-tile.  A CTA covers
+// 8 * (4 / ksplit) hidden columns of one tile (the MXFP8 lane: 32 columns,
+// one scale block of the hidden row, ksplit 1) and loops over the tile's
+// 16-row passes.
+template <bool MX>
+__device__ __forceinline__ void swiglu_cta(const GemvPass& a, int g, int64_t start, int n, uint8_t* smem,
+                                           bool pending) {
+  const int ksplit = MX ? 1 : a.ksplit;
+  const int mtiles = kGemvWarps / ksplit;
+  const int j_cta = static_cast<int>(blockIdx.y) * 8 * mtiles;
+  if (j_cta >= a.inter) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int mt = warp % mtiles, ks = warp / mtiles;
+  const int jw = j_cta + 8 * mt;
+  const bool live = jw < a.inter;  // warp-uniform
+  const int c = MX ? a.cm : a.chunk;
+  const int rows1 = (MX ? a.ncm : a.nc) * 2 * c;
+  const int K = MX ? a.kx : a.kd;  // weight row width = token row width (values)
+  const int esz = MX ? 1 : 2;
+  const int xsl = K + kRowPad;
+  uint16_t* xs = reinterpret_cast<uint16_t*>(smem);
+  float* red = reinterpret_cast<float*>(smem + static_cast<size_t>(kPassRows) * xsl * 2);
+  uint16_t* hs = reinterpret_cast<uint16_t*>(red);  // MXFP8 lane: [kPassRows][32] hidden values
+  // A rows of the thread: the gate row of column jw + gq (packed [gate | up]
+  // chunks of c rows) and its up row c rows further
+  const int ch = jw / c;
+  const int grow = ch * 2 * c + (jw - ch * c) + gq;
+  const uint8_t* wbase = MX ? a.w1q : reinterpret_cast<const uint8_t*>(a.w1);
+  const MxAtoms ma{a.w1sf, g, rows1, 2 * c, K};
+  const ARows rows{wbase + (static_cast<int64_t>(g) * rows1 + grow) * K * esz,
+                   wbase + (static_cast<int64_t>(g) * rows1 + grow + c) * K * esz, MX ? ma.row(grow) : nullptr,
+                   MX ? ma.row(grow + c) : nullptr};
+  const int kq = K / ksplit;
+  const int kb = ks * kq, ke = kb + kq;
+  constexpr int U = 4;  // BF16 chunks per step
+  const int G = (kq + WBuf<MX, U>::kStep - 1) / WBuf<MX, U>::kStep;
+  for (int r0 = static_cast<int>(blockIdx.z) * kPassRows; r0 < n; r0 += static_cast<int>(gridDim.z) * kPassRows) {
+    const int R = min(kPassRows, n - r0);
+    const int nt = R > 8 ? 2 : 1;
+    WBuf<MX, U> b0;
+    if (live) load_step(rows, kb, ke, tq, ma, b0);  // under the staging below
+    if (pending) {  // a dense pass: the weights above are static, the token rows are not
+      griddep_wait();
+      griddep_launch_dependents();
+      pending = false;
+    }
+    __syncthreads();  // the previous pass no longer reads xs / hs
+    stage_rows(MX, a.src_row, start + r0, R, a.x, a.ldx, a.xq, a.xsf, a.kx, K, xsl, xs);
+    cp_async_wait_all();
+    __syncthreads();
+    float acc[2][4];
+    zero_acc(acc);
+    if (live) run_stream<MX, U>(G, G, kb, ke, [&](int) { return rows; }, ma, xs, xsl, nt, gq, tq, b0, acc, [](int) {});
+    reduce_ksplit(red, ksplit, mtiles, mt, ks, lane, acc);
+    // (d0, d1): gate of column jw + gq for tokens 2tq, 2tq + 1 of the n-tile; (d2, d3): up
+    if (ks == 0 && live) {
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-          const int i = 2 * tq + u;
-          if (i < R && jl < ncol) {
-            const float gv = u == 0 ? sum.x : sum.y, uv = u == 0 ? sum.z : sum.w;
-            const float h = round_bf16(round_bf16(silu_ref(round_bf16(gv))) * round_bf16(uv));
-            a.hid[(start + r0 + i) * a.ldh + j0 + jl] = f32_to_bf16_rne(h);
+          const int i = 8 * t + 2 * tq + u;
+          if (i < R) {
+            const float h = round_bf16(round_bf16(silu_ref(round_bf16(acc[t][u]))) * round_bf16(acc[t][2 + u]));
+            if (MX)
+              hs[i * 32 + 8 * mt + gq] = f32_to_bf16_rne(h);
+            else
+              a.hid[(start + r0 + i) * a.ldh + jw + gq] = f32_to_bf16_rne(h);
           }
         }
       }
+    }
+    if (MX) {
       __syncthreads();
-      continue;
-    }
-    // MXFP8 tiles on the CUDA cores: warp w: columns jl = w*2 + {0,1} (+16 on
-    // the second pass); lane groups 0: gate(jl), 1: gate(jl+1), 2: up(jl), 3: up(jl+1)
-    const int grp = lane >> 3, seg = lane & 7;
-    for (int p = 0; p < cols / kSwigluCols; ++p) {
-      const int jl = p * kSwigluCols + warp * 2 + (grp & 1);
-      const bool live = jl < ncol;
-      const int half = grp >> 1;
-      const uint8_t* wrow = slab + static_cast<size_t>(half * cols + jl) * ws;
-      const int wr = g0 + half * c + jl;  // packed row (for the MXFP8 scales)
-      auto emit = [&](int i, float part) {
-        const float gv = group_sum8(part);
-        const float uv = __shfl_down_sync(0xFFFFFFFFu, gv, 16);  // up of the same column (groups 2, 3 -> 0, 1)
-        if (grp < 2 && seg == 0 && live) {
-          const float h = round_bf16(round_bf16(silu_ref(round_bf16(gv))) * round_bf16(uv));
-          hs[i * kSwigluColsMx + jl] = f32_to_bf16_rne(h);
-        }
-      };
-      dot_rows<true>(wrow, a.w1sf, g, wr, rows1, 2 * c, a.kx, xsb / 2, a.kx,
-                     reinterpret_cast<const uint16_t*>(xsp), R, seg, live, emit);
-    }
-    __syncthreads();
-    if (static_cast<int>(threadIdx.x) < R) {
-      const int i = threadIdx.x;
-      float v[32];
+      if (static_cast<int>(threadIdx.x) < R) {
+        const int i = threadIdx.x;
+        float v[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = j < ncol ? bf16_to_f32(hs[i * kSwigluColsMx + j]) : 0.0f;
-      uint32_t q[8];
-      const uint32_t sb = mx_quantize32(v, q);
-      uint4* dst = reinterpret_cast<uint4*>(a.hq + (start + r0 + i) * a.kh + j0);
-      dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
-      dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
-      a.hsf[(start + r0 + i) * (a.kh / kMxBlock) + j0 / kMxBlock] = static_cast<uint8_t>(sb);
+        for (int j = 0; j < 32; ++j) v[j] = bf16_to_f32(hs[i * 32 + j]);
+        uint32_t qw[8];
+        const uint32_t sb = mx_quantize32(v, qw);
+        uint4* dst = reinterpret_cast<uint4*>(a.hq + (start + r0 + i) * a.kh + j_cta);
+        dst[0] = make_uint4(qw[0], qw[1], qw[2], qw[3]);
+        dst[1] = make_uint4(qw[4], qw[5], qw[6], qw[7]);
+        a.hsf[(start + r0 + i) * (a.kh / kMxBlock) + j_cta / kMxBlock] = static_cast<uint8_t>(sb);
+      }
     }
-    __syncthreads();
   }
 }
 
-// Row GEMV: out[pos, n] = bf16(bf16(<A[pos], W[g][n]> [+ bias[n]]) * w[pos])
-// for a slab of nblk output columns of group g and the group's rows.
-__global__ void __launch_bounds__(kGemvThreads, 3) gemv_rows_kernel(const GemvPass a) {
-  extern __shared__ __align__(128) uint8_t smem[];
+__global__ void __launch_bounds__(kGemvThreads, 5) gemv_swiglu_kernel(const GemvPass a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  // Expert passes read the dispatch's tile tables: wait first.  Dense passes
+  // issue their first weight loads before waiting.
+  const bool dense = a.tiles == nullptr;
+  if (!dense) {
+    griddep_wait();
+    griddep_launch_dependents();
+  }
   int g, n;
   bool mx;
   int64_t start;
   tile_rows(a, g, mx, start, n);
-  if (n <= static_cast<int>(blockIdx.z) * kGemvRows) return;
-  const int n0 = blockIdx.y * a.nblk;
-  if (n0 >= a.n_out) return;
-  const int K = mx ? a.kh : a.k2;                    // A row width (BF16 values) in shared memory
-  const int wbytes = mx ? a.kh : 2 * a.k2;
-  const int ws = wbytes + 16;
-  const int xsb = 2 * K + 16;
-  const int ncol = min(a.nblk, a.n_out - n0);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-  int* abort_flag = reinterpret_cast<int*>(smem + 64);
-  uint8_t* slab = smem + 128;
-  uint8_t* xsp = slab + static_cast<size_t>(a.nblk) * ws;
-  uint16_t* ys = reinterpret_cast<uint16_t*>(xsp + static_cast<size_t>(kGemvRows) * xsb);  // [kGemvRows][nblk]
-  float* red = reinterpret_cast<float*>(ys + static_cast<size_t>(kGemvRows) * a.nblk);    // [8][32][4]
-  const uint8_t* wbase = mx ? a.w2q : reinterpret_cast<const uint8_t*>(a.w2);
+  if (n <= static_cast<int>(blockIdx.z) * kPassRows) return;
+  if (mx)
+    swiglu_cta<true>(a, g, start, n, smem, dense);
+  else
+    swiglu_cta<false>(a, g, start, n, smem, dense);
+}
+
+// Row GEMV: out[pos, n] = bf16(bf16(<A[pos], W[g][n]> [+ bias[n]]) * w[pos]).
+// A warp walks a.mpw m-tiles of 16 output columns (a.mpw = 1 when warps
+// split K); a CTA covers 16 * mpw * (4 / ksplit) columns of one tile (or of a
+// dense pass's 16-row chunk) and loops over the tile's 16-row passes; K runs
+// to k_valid2 (thread slots past it read as zero).
+template <bool MX>
+__device__ __forceinline__ void rows_cta(const GemvPass& a, int g, int64_t start, int n, uint8_t* smem,
+                                         bool pending) {
+  const int kv = a.k_valid2;
+  const int ksplit = a.ksplit, mpw = a.mpw;
+  const int mtiles = kGemvWarps / ksplit;
+  const int n_cta = static_cast<int>(blockIdx.y) * 16 * mpw * mtiles;
+  if (n_cta >= a.n_out) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool tc = !mx && gemv_rows_tc(a);
-  uint32_t pass = 0;
-  for (int r0 = blockIdx.z * kGemvRows; r0 < n; r0 += gridDim.z * kGemvRows, ++pass) {
-    const int R = min(kGemvRows, n - r0);
-    if (warp == 0) {
-      const uint32_t bytes = (pass == 0 ? static_cast<uint32_t>(ncol) * wbytes : 0u) +
-                             (mx ? 0u : static_cast<uint32_t>(R) * 2 * K);
-      if (lane == 0) {
-        if (pass == 0) {
-          mbar_init(bar, 1);
-          fence_mbar_init();
-        } else {
-          fence_proxy_async_smem();
-        }
-        if (bytes) mbar_arrive_expect_tx(bar, bytes); else mbar_arrive(bar);
-      }
-      __syncwarp();
-      if (pass == 0) {
-        for (int i = lane; i < ncol; i += 32)
-          bulk_load(slab + static_cast<size_t>(i) * ws, wbase + (static_cast<int64_t>(g) * a.n_out + n0 + i) * wbytes,
-                    wbytes, bar);
-      }
-      if (!mx) {
-        for (int i = lane; i < R; i += 32) {
-          const int64_t row = a.src_row != nullptr ? a.src_row[start + r0 + i] : start + r0 + i;
-          bulk_load(xsp + static_cast<size_t>(i) * xsb, a.a2 + row * a.lda2, 2u * K, bar);
-        }
-      }
+  const int gq = lane >> 2, tq = lane & 3;
+  const int mt = warp % mtiles, ks = warp / mtiles;
+  const int n_warp = n_cta + 16 * mpw * mt;  // the warp's first output column
+  const int m_live = min(mpw, (a.n_out - n_warp + 15) / 16);  // m-tiles with columns (<= 0: none)
+  const int K = MX ? a.kh : a.k2;  // weight row width = A row width (values)
+  const int esz = MX ? 1 : 2;
+  const int xsl = K + kRowPad;
+  uint16_t* xs = reinterpret_cast<uint16_t*>(smem);
+  float* red = reinterpret_cast<float*>(smem + static_cast<size_t>(kPassRows) * xsl * 2);
+  const uint8_t* wbase = (MX ? a.w2q : reinterpret_cast<const uint8_t*>(a.w2)) +
+                         static_cast<int64_t>(g) * a.n_out * K * esz;
+  // A rows of m-tile m (clamped inside the weight; the extra rows' sums are not stored)
+  const MxAtoms ma{a.w2sf, g, a.n_out, a.bn2m, K};
+  auto rows_of = [&](int m) {
+    const int nw = n_warp + 16 * m;
+    const int lo = min(nw + gq, a.n_out - 1), hi = min(nw + gq + 8, a.n_out - 1);
+    return ARows{wbase + static_cast<int64_t>(lo) * K * esz, wbase + static_cast<int64_t>(hi) * K * esz,
+                 MX ? ma.row(lo) : nullptr, MX ? ma.row(hi) : nullptr};
+  };
+  constexpr int kSlot = MX ? 16 : 8;
+  const int kq = (kv / kSlot + ksplit - 1) / ksplit * kSlot;  // K share per warp, whole thread slots
+  const int kb = min(ks * kq, kv), ke = min(kb + kq, kv);
+  constexpr int U = 4;  // BF16 chunks per step
+  const int G = (ke - kb + WBuf<MX, U>::kStep - 1) / WBuf<MX, U>::kStep;
+  const int steps = m_live > 0 ? m_live * G : 0;
+  for (int r0 = static_cast<int>(blockIdx.z) * kPassRows; r0 < n; r0 += static_cast<int>(gridDim.z) * kPassRows) {
+    const int R = min(kPassRows, n - r0);
+    const int nt = R > 8 ? 2 : 1;
+    WBuf<MX, U> b0;
+    if (steps > 0) load_step(rows_of(0), kb, ke, tq, ma, b0);  // under the staging below
+    if (pending) {  // a dense pass: the weights above are static, the A rows are not
+      griddep_wait();
+      griddep_launch_dependents();
+      pending = false;
     }
-    if (mx) stage_rows(true, a.src_row, start + r0, R, a.a2, a.lda2, a.hq, a.hsf, a.kh, a.kh, xsb / 2,
-                       reinterpret_cast<uint16_t*>(xsp));
-    for (int i = threadIdx.x; i < (kGemvRows - R) * (K / 8); i += blockDim.x) {
-      const int r = R + i / (K / 8), q = i % (K / 8);
-      reinterpret_cast<uint4*>(xsp + static_cast<size_t>(r) * xsb)[q] = make_uint4(0u, 0u, 0u, 0u);
-    }
-    // slab rows ncol..nblk of a partial column block are not loaded: zero them once
-    if (pass == 0 && tc) {
-      for (int i = threadIdx.x; i < (a.nblk - ncol) * (wbytes / 16); i += blockDim.x) {
-        const int r = ncol + i / (wbytes / 16), q = i % (wbytes / 16);
-        reinterpret_cast<uint4*>(slab + static_cast<size_t>(r) * ws)[q] = make_uint4(0u, 0u, 0u, 0u);
-      }
-    }
-    if (!pass_ready(bar, pass & 1u, a.status, abort_flag)) return;
-    if (tc) {
-      const int mtiles = a.nblk / 16, ksplit = kGemvWarps / mtiles;
-      const int mt = warp % mtiles, ks = warp / mtiles;
-      const int kq = a.k_valid2 / ksplit;
-      float d[4];
-      auto a_row = [&](int m) -> uint32_t { return static_cast<uint32_t>((mt * 16 + m) * ws); };
-      mma_rows(smem_u32(slab), a_row, smem_u32(xsp), xsb, ks * kq, (ks + 1) * kq, lane, d);
-      if (ksplit > 1) {
-        *reinterpret_cast<float4*>(red + (warp * 32 + lane) * 4) = make_float4(d[0], d[1], d[2], d[3]);
-        __syncthreads();
-        if (ks == 0) {
-          float4 sum = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-          for (int s2 = 0; s2 < ksplit; ++s2) {
-            const float4 v = *reinterpret_cast<const float4*>(red + ((mt + mtiles * s2) * 32 + lane) * 4);
-            sum.x += v.x;
-            sum.y += v.y;
-            sum.z += v.z;
-            sum.w += v.w;
-          }
-          d[0] = sum.x;
-          d[1] = sum.y;
-          d[2] = sum.z;
-          d[3] = sum.w;
-        }
-      }
-      if (ks == 0) {
-        // (d0, d1): output row mt*16 + gq for tokens 2tq, 2tq+1; (d2, d3): row + 8
-        const int gq = lane >> 2, tq = lane & 3;
+    __syncthreads();  // the previous pass no longer reads xs / red
+    stage_rows(MX, a.src_row, start + r0, R, a.a2, a.lda2, a.hq, a.hsf, a.kh, K, xsl, xs);
+    // routing weights of the thread's output tokens
+    float w[2][2];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int nl = mt * 16 + gq + (q >> 1) * 8;
-          const int i = 2 * tq + (q & 1);
-          if (i < R && nl < ncol) {
-            const float bias = a.bias != nullptr ? bf16_to_f32(a.bias[n0 + nl]) : 0.0f;
-            const float w = a.row_w != nullptr ? bf16_to_f32(a.row_w[start + r0 + i]) : 1.0f;
-            ys[i * a.nblk + nl] = f32_to_bf16_rne(round_bf16(d[q] + bias) * w);
-          }
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int i = 8 * t + 2 * tq + u;
+        w[t][u] = (a.row_w != nullptr && i < R) ? bf16_to_f32(a.row_w[start + r0 + i]) : 1.0f;
+      }
+    cp_async_wait_all();
+    __syncthreads();
+    float acc[2][4];
+    zero_acc(acc);
+    // (d0, d1): output column nw + gq for tokens 2tq, 2tq + 1 of the n-tile; (d2, d3): column + 8
+    auto store = [&](int m) {
+      const int nw = n_warp + 16 * m;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int col = nw + gq + (q >> 1) * 8;
+        if (col >= a.n_out) continue;
+        const float bias = a.bias != nullptr ? bf16_to_f32(a.bias[col]) : 0.0f;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const int i = 8 * t + 2 * tq + (q & 1);
+          if (i < R)
+            a.out[(start + r0 + i) * a.ldo + col] = f32_to_bf16_rne(round_bf16(acc[t][q] + bias) * w[t][q & 1]);
         }
       }
+    };
+    if (ksplit == 1) {
+      run_stream<MX, U>(steps, G, kb, ke, rows_of, ma, xs, xsl, nt, gq, tq, b0, acc, [&](int m) {
+        store(m);
+        zero_acc(acc);
+      });
     } else {
-      // CUDA cores (MXFP8 tiles, or K not splitting evenly): 4 rows per warp step
-      const int grp = lane >> 3, seg = lane & 7;
-      const int per_warp = a.nblk / kGemvWarps;  // output columns per warp (multiple of 4)
-      for (int p = 0; p < per_warp; p += 4) {
-        const int nl = warp * per_warp + p + grp;
-        const bool live = nl < ncol;
-        const uint8_t* wrow = slab + static_cast<size_t>(nl) * ws;
-        const float bias = (live && a.bias != nullptr) ? bf16_to_f32(a.bias[n0 + nl]) : 0.0f;
-        auto emit = [&](int i, float part) {
-          const float y = group_sum8(part);
-          if (seg == 0 && live) {
-            const float w = a.row_w != nullptr ? bf16_to_f32(a.row_w[start + r0 + i]) : 1.0f;
-            ys[i * a.nblk + nl] = f32_to_bf16_rne(round_bf16(y + bias) * w);
-          }
-        };
-        if (mx)
-          dot_rows<true>(wrow, a.w2sf, g, n0 + nl, a.n_out, a.bn2m, a.kh, xsb / 2, a.k_valid2,
-                         reinterpret_cast<const uint16_t*>(xsp), R, seg, live, emit);
-        else
-          dot_rows<false>(wrow, nullptr, g, n0 + nl, a.n_out, 0, a.k2, xsb / 2, a.k_valid2,
-                          reinterpret_cast<const uint16_t*>(xsp), R, seg, live, emit);
-      }
+      // one m-tile per warp (mpw = 1)
+      run_stream<MX, U>(steps, G, kb, ke, rows_of, ma, xs, xsl, nt, gq, tq, b0, acc, [](int) {});
+      reduce_ksplit(red, ksplit, mtiles, mt, ks, lane, acc);
+      if (ks == 0 && m_live > 0) store(0);
     }
-    __syncthreads();
-    // staged rows out as row segments (16-byte stores when aligned)
-    if ((ncol % 8) == 0 && (a.ldo % 8) == 0) {
-      const int per_row = ncol / 8;
-      for (int t = threadIdx.x; t < R * per_row; t += blockDim.x) {
-        const int i = t / per_row, q = t - i * per_row;
-        reinterpret_cast<uint4*>(a.out + (start + r0 + i) * a.ldo + n0)[q] =
-            reinterpret_cast<const uint4*>(ys + i * a.nblk)[q];
-      }
-    } else {
-      for (int t = threadIdx.x; t < R * ncol; t += blockDim.x) {
-        const int i = t / ncol, q = t - i * ncol;
-        a.out[(start + r0 + i) * a.ldo + n0 + q] = ys[i * a.nblk + q];
-      }
-    }
-    __syncthreads();
   }
 }
 
-int pick_nblk(int row_bytes) {
-  int nb = static_cast<int>(kSlabBytes / static_cast<size_t>(row_bytes));
-  nb = std::max(32, std::min(128, nb));
-  return nb / 32 * 32;
+__global__ void __launch_bounds__(kGemvThreads, 5) gemv_rows_kernel(const GemvPass a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const bool dense = a.tiles == nullptr;
+  if (!dense) {
+    griddep_wait();
+    griddep_launch_dependents();
+  }
+  int g, n;
+  bool mx;
+  int64_t start;
+  tile_rows(a, g, mx, start, n);
+  if (n <= static_cast<int>(blockIdx.z) * kPassRows) return;
+  if (mx)
+    rows_cta<true>(a, g, start, n, smem, dense);
+  else
+    rows_cta<false>(a, g, start, n, smem, dense);
+}
+
+// K split that fills the SMs: the smallest of 1, 2, 4 (up to max_split) that
+// gives at least two CTAs per SM over `units` x column groups.
+int pick_ksplit(int64_t units, int cols, int cols_per_mtile, int max_split) {
+  const int sms = device_sm_count();
+  const int64_t target = 2 * static_cast<int64_t>(sms > 0 ? sms : 148);
+  int ks = 1;
+  while (ks < max_split) {
+    const int per_cta = cols_per_mtile * (kGemvWarps / ks);
+    if (units * ((cols + per_cta - 1) / per_cta) >= target) break;
+    ks *= 2;
+  }
+  return ks;
+}
+
+int64_t gemv_units(const GemvPass& a) {
+  return a.tiles != nullptr ? a.max_tiles : (a.dense_rows + kPassRows - 1) / kPassRows;
+}
+
+// Grid: x = tiles (BF16 table, then the MXFP8 table) or 1 (dense), y = column
+// groups, z = 16-row chunks of a dense pass.
+dim3 gemv_grid(const GemvPass& a, int col_groups) {
+  const unsigned x = a.tiles == nullptr ? 1u : static_cast<unsigned>(a.max_tiles * (a.tiles_mx != nullptr ? 2 : 1));
+  const unsigned z = a.tiles == nullptr ? static_cast<unsigned>((a.dense_rows + kPassRows - 1) / kPassRows) : 1u;
+  return dim3(x, static_cast<unsigned>(col_groups), z);
 }
 
 }  // namespace
 
 bool gemv_swiglu_ok(const GemvPass& a) {
-  return a.kd % 64 == 0 && a.chunk % kSwigluCols == 0 && a.ldh % 8 == 0 &&
-         (a.tiles_mx == nullptr || (a.inter % kMxBlock == 0 && a.cm % kSwigluColsMx == 0 && a.kx % 128 == 0 &&
+  return a.kd % 64 == 0 && a.chunk % 8 == 0 && a.inter > 0 &&
+         (a.tiles_mx == nullptr || (a.inter % kMxBlock == 0 && a.cm % kMxBlock == 0 && a.kx % 128 == 0 &&
                                     a.kh % 128 == 0));
 }
 
 bool gemv_rows_ok(const GemvPass& a) {
-  return a.k2 % 64 == 0 && a.k_valid2 <= a.k2 && a.k_valid2 % (a.tiles_mx != nullptr ? kMxBlock : 8) == 0 &&
+  return a.k2 % 64 == 0 && a.k_valid2 > 0 && a.k_valid2 <= a.k2 && a.n_out > 0 &&
+         a.k_valid2 % (a.tiles_mx != nullptr ? kMxBlock : 8) == 0 &&
          (a.tiles_mx == nullptr || (a.kh % 128 == 0 && a.k_valid2 <= a.kh));
 }
 
-// Grid: x = tiles (BF16 table, then the MXFP8 table) or 1 (dense), y = column
-// blocks, z = 16-row chunks of a dense pass.
-dim3 gemv_grid(const GemvPass& a, int col_blocks) {
-  const unsigned x = a.tiles == nullptr ? 1u : static_cast<unsigned>(a.max_tiles * (a.tiles_mx != nullptr ? 2 : 1));
-  const unsigned z = a.tiles == nullptr ? static_cast<unsigned>((a.dense_rows + kGemvRows - 1) / kGemvRows) : 1u;
-  return dim3(x, static_cast<unsigned>(col_blocks), z);
-}
-
-int launch_gemv_swiglu(const GemvPass& a, cudaStream_t stream) {
+int launch_gemv_swiglu(GemvPass a, cudaStream_t stream) {
   if (!gemv_swiglu_ok(a)) return SPX_ERR_UNSUPPORTED;
   const bool mx = a.tiles_mx != nullptr;
   const int K = std::max(a.kd, mx ? a.kx : 0);
-  const size_t slab = std::max<size_t>(2 * kSwigluCols * (2 * static_cast<size_t>(a.kd) + 16),
-                                       mx ? 2 * kSwigluColsMx * (static_cast<size_t>(a.kx) + 16) : 0);
-  const size_t red = kGemvWarps * 32 * 4 * sizeof(float);
-  const size_t smem = 128 + slab + static_cast<size_t>(kGemvRows) * (2 * static_cast<size_t>(K) + 16) + red;
+  const size_t smem = static_cast<size_t>(kPassRows) * (K + kRowPad) * 2 + kRedBytes;
   if (smem > kGemmSmemBudget) return SPX_ERR_UNSUPPORTED;
-  if (int rc = ensure_max_dynamic_smem(reinterpret_cast<const void*>(gemv_swiglu_kernel)); rc != SPX_OK) return rc;
-  gemv_swiglu_kernel<<<gemv_grid(a, (a.inter + kSwigluCols - 1) / kSwigluCols), kGemvThreads, smem, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+  // the BF16 K share stays a multiple of one 32-value chunk
+  a.ksplit = pick_ksplit(gemv_units(a), a.inter, 8, a.kd % 128 == 0 ? 4 : 2);
+  if (smem > 48 * 1024)
+    if (int rc = ensure_max_dynamic_smem(reinterpret_cast<const void*>(gemv_swiglu_kernel)); rc != SPX_OK) return rc;
+  const int per_cta = 8 * (kGemvWarps / a.ksplit);
+  const int groups = std::max((a.inter + per_cta - 1) / per_cta, mx ? (a.inter + 31) / 32 : 0);
+  return launch_pdl(gemv_swiglu_kernel, gemv_grid(a, groups), dim3(kGemvThreads), smem, stream, a);
 }
 
 int launch_gemv_rows(GemvPass a, cudaStream_t stream) {
   if (!gemv_rows_ok(a)) return SPX_ERR_UNSUPPORTED;
   const bool mx = a.tiles_mx != nullptr;
-  const int wbytes = std::max(2 * a.k2, mx ? a.kh : 0);
-  a.nblk = pick_nblk(wbytes);
   const int K = std::max(a.k2, mx ? a.kh : 0);
-  const size_t red = kGemvWarps * 32 * 4 * sizeof(float);
-  const size_t smem = 128 + static_cast<size_t>(a.nblk) * (wbytes + 16) +
-                      static_cast<size_t>(kGemvRows) * (2 * static_cast<size_t>(K) + 16) +
-                      static_cast<size_t>(kGemvRows) * a.nblk * 2 + red;
+  const size_t smem = static_cast<size_t>(kPassRows) * (K + kRowPad) * 2 + kRedBytes;
   if (smem > kGemmSmemBudget) return SPX_ERR_UNSUPPORTED;
-  if (int rc = ensure_max_dynamic_smem(reinterpret_cast<const void*>(gemv_rows_kernel)); rc != SPX_OK) return rc;
-  gemv_rows_kernel<<<gemv_grid(a, (a.n_out + a.nblk - 1) / a.nblk), kGemvThreads, smem, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+  const int64_t units = gemv_units(a);
+  a.ksplit = pick_ksplit(units, a.n_out, 16, 4);
+  // with whole m-tiles per warp, the most m-tiles per warp that still fill the SMs
+  a.mpw = 1;
+  if (a.ksplit == 1) {
+    const int sms = device_sm_count();
+    const int64_t target = 2 * static_cast<int64_t>(sms > 0 ? sms : 148);
+    for (int m = 4; m > 1; m >>= 1) {
+      const int per = 16 * kGemvWarps * m;
+      if (units * ((a.n_out + per - 1) / per) >= target) {
+        a.mpw = m;
+        break;
+      }
+    }
+  }
+  if (smem > 48 * 1024)
+    if (int rc = ensure_max_dynamic_smem(reinterpret_cast<const void*>(gemv_rows_kernel)); rc != SPX_OK) return rc;
+  const int per_cta = 16 * a.mpw * (kGemvWarps / a.ksplit);
+  return launch_pdl(gemv_rows_kernel, gemv_grid(a, (a.n_out + per_cta - 1) / per_cta), dim3(kGemvThreads), smem,
+                    stream, a);
 }
 
 }  // namespace spx

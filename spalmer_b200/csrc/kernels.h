@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "status.h"
 
 namespace spx {
@@ -106,6 +108,8 @@ struct DispatchArgs {
   int eligible_experts;        // used when resident == null
   const uint8_t* resident;   // [E] resident mask or null
   int execution_loop;        // 1: reference expert_execution == "loop" telemetry
+  const float* recon_error;  // [E] each expert's reconstruction error (spx_expert_quant_error), or null
+  float* quant_error;        // [E] out: recon_error of the selected experts, 0 elsewhere, or null
   int* status;
 };
 
@@ -176,13 +180,38 @@ int ensure_max_dynamic_smem(const void* func);
 // none can be made (e.g. the first call is inside a stream capture).
 struct SideStream {
   cudaStream_t side;
-  cudaEvent_t fork, join_a, join_b;
+  cudaEvent_t fork, join;
 };
 bool side_stream(cudaStream_t main, SideStream* out);
+
+// Launch with programmatic stream serialisation: the kernel may begin while
+// the previous kernel in `stream` runs and must call griddep_wait (sm100.cuh)
+// before touching anything that kernel or an earlier one writes.  Used by
+// the decode-sized layer's kernel chain, where launch latency and kernel
+// prologues are a large part of each step; stream capture keeps the
+// programmatic edges.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
 // How many 2-CTA clusters of `func` (with `smem` dynamic bytes) fit on the device at once.
 int device_max_pairs(const void* func, size_t smem);
 
 int launch_softplus_table(uint16_t* lut, cudaStream_t stream);
+// Per-expert reconstruction error of the low-precision copies (quant_error.cu):
+// format 1 = MXFP8, 2 = NVFP4; masters in the reference layouts.
+int launch_expert_quant_error(const uint16_t* gate, const uint16_t* up, const uint16_t* down, int E, int d, int inter,
+                              int format, float* out, cudaStream_t stream);
 int launch_scores_from_logits(uint16_t* values, int64_t n, const uint16_t* lut, cudaStream_t stream);
 size_t route_select_smem(int num_experts);
 int launch_route(const RouteArgs& a, cudaStream_t stream);
@@ -358,7 +387,9 @@ struct GemvPass {
   const uint8_t* w2q;         // MXFP8 lane: [groups][n_out][kh] + scale atoms (bn2m-row tiles)
   const uint8_t* w2sf;
   int bn2m;
-  int n_out, nblk;            // output columns; columns per CTA (set at launch)
+  int n_out;                  // output columns
+  int ksplit;                 // warps sharing one m-tile's K (set at launch)
+  int mpw;                    // row pass: 16-column m-tiles per warp (set at launch)
   const uint16_t* bias;       // [n_out] or null
   const uint16_t* row_w;      // [rows] or null (unit)
   uint16_t* out;
@@ -366,7 +397,7 @@ struct GemvPass {
 };
 bool gemv_swiglu_ok(const GemvPass& a);
 bool gemv_rows_ok(const GemvPass& a);
-int launch_gemv_swiglu(const GemvPass& a, cudaStream_t stream);
+int launch_gemv_swiglu(GemvPass a, cudaStream_t stream);
 int launch_gemv_rows(GemvPass a, cudaStream_t stream);
 
 // Backward (backward.cu).

@@ -36,7 +36,7 @@ int device_sm_count() {
   return g_sm_count[dev];
 }
 
-// Side streams: one non-blocking stream (same priority) and three events per
+// Side streams: one non-blocking stream (same priority) and two events per
 // (device, caller stream), created on the first call that is not being
 // captured and kept for the life of the process.  Work forked onto the side
 // stream joins the caller's stream through the events, so the pair behaves as
@@ -68,8 +68,7 @@ bool side_stream(cudaStream_t main, SideStream* out) {
     return false;
   }
   if (cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming) != cudaSuccess ||
-      cudaEventCreateWithFlags(&s.join_a, cudaEventDisableTiming) != cudaSuccess ||
-      cudaEventCreateWithFlags(&s.join_b, cudaEventDisableTiming) != cudaSuccess) {
+      cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming) != cudaSuccess) {
     cudaGetLastError();
     return false;
   }

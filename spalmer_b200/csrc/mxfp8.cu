@@ -50,6 +50,8 @@ __global__ void mx_quantize_rows_kernel(const uint16_t* __restrict__ src, int64_
   const int nblk = kp / kMxBlock;
   const int64_t total = rows * nblk;
   const bool vec = (cols % 8) == 0 && (ld_src % 8) == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
+  griddep_wait();
+  griddep_launch_dependents();
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t row = idx / nblk;
@@ -110,8 +112,8 @@ int launch_mx_quantize_rows(const uint16_t* src, int64_t rows, int cols, int64_t
   if (rows <= 0) return SPX_OK;
   if (kp % kMxBlock != 0 || cols > kp || ld_q < kp || ld_sf < kp / kMxBlock) return SPX_ERR_INVALID_ARG;
   const int64_t total = rows * (kp / kMxBlock);
-  mx_quantize_rows_kernel<<<grid_for(total, 256), 256, 0, stream>>>(src, rows, cols, ld_src, kp, q, ld_q, sf, ld_sf);
-  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+  return launch_pdl(mx_quantize_rows_kernel, dim3(grid_for(total, 256)), dim3(256), 0, stream, src, rows, cols, ld_src,
+                    kp, q, ld_q, sf, ld_sf);
 }
 
 size_t mx_atoms_bytes(int groups, int rows_per_group, int kp, int tile_rows) {

@@ -86,6 +86,8 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, const int* __rest
                                const uint16_t* __restrict__ residual, uint16_t* __restrict__ residual_out) {
   const int vec = d / 8;
   const int64_t total = tokens * vec;
+  griddep_wait();
+  griddep_launch_dependents();
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t t = idx / vec;
@@ -200,18 +202,10 @@ int launch_combine_residual(const uint16_t* y, const int* rank, const uint16_t* 
     int64_t g = (total + 255) / 256;
     if (g > 148 * 64) g = 148 * 64;
     const int grid = static_cast<int>(g < 1 ? 1 : g);
-    if (weights == nullptr && k <= 8)
-      combine_kernel<8, false><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out, residual,
-                                                        residual_out);
-    else if (weights == nullptr)
-      combine_kernel<kMaxTopK, false><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out, residual,
-                                                                residual_out);
-    else if (k <= 8)
-      combine_kernel<8, true><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out, residual,
-                                                       residual_out);
-    else
-      combine_kernel<kMaxTopK, true><<<grid, 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out, residual,
-                                                               residual_out);
+    auto fn = weights == nullptr ? (k <= 8 ? combine_kernel<8, false> : combine_kernel<kMaxTopK, false>)
+                                 : (k <= 8 ? combine_kernel<8, true> : combine_kernel<kMaxTopK, true>);
+    return launch_pdl(fn, dim3(grid), dim3(256), 0, stream, y, rank, weights, base, tokens, d, k, out, residual,
+                      residual_out);
   } else {
     combine_scalar_kernel<<<grid_for(tokens * d), 256, 0, stream>>>(y, rank, weights, base, tokens, d, k, out,
                                                                     residual, residual_out);

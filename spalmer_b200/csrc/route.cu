@@ -472,6 +472,8 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_rows_kernel(const Rout
   uint32_t* v = route_smem + kRouteWarps * E + (E + 3) / 4 + warp * (E + 2 * half_words);
   uint16_t* lpos = reinterpret_cast<uint16_t*>(v + E);
   uint16_t* rpos = reinterpret_cast<uint16_t*>(v + E + half_words);
+  griddep_wait();  // the logits (and the mask) come from earlier kernels
+  griddep_launch_dependents();
   for (int c = threadIdx.x; c < E; c += blockDim.x) resident[c] = a.resident ? a.resident[c] : 1;
   __syncthreads();
 
@@ -718,9 +720,8 @@ template <int NCH, int K1MAX>
 static int launch_route_rows_t(const RouteArgs& a, cudaStream_t stream) {
   const void* fn = reinterpret_cast<const void*>(route_rows_kernel<NCH, K1MAX>);
   if (ensure_max_dynamic_smem(fn) != SPX_OK) return SPX_ERR_CUDA;
-  route_rows_kernel<NCH, K1MAX><<<route_lb_blocks(a.tokens), kRouteWarps * 32, route_rows_smem(a.num_experts),
-                                  stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+  return launch_pdl(route_rows_kernel<NCH, K1MAX>, dim3(route_lb_blocks(a.tokens)), dim3(kRouteWarps * 32),
+                    route_rows_smem(a.num_experts), stream, a);
 }
 
 template <int NCH>

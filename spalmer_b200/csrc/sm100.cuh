@@ -237,6 +237,17 @@ __device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
 
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with launch_pdl may start while the kernel before it in
+// the stream is still running.  Before griddep_wait it may only read data no
+// kernel writes (weights) and write nothing; griddep_wait returns once the
+// previous grid has completed and its memory is visible (at once when the
+// launch had no programmatic dependency).  griddep_launch_dependents lets the
+// next kernel launch as soon as every CTA of this grid has issued it (or
+// exited).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 // Make this thread's completed generic-proxy shared-memory writes visible to
 // the async proxy (tcgen05.mma operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -679,6 +679,10 @@ def _bits(t: Tensor) -> Tensor:
     return t.detach().contiguous()
 
 
+# expert_weight_format -> spx_expert_quant_error's weight_format
+_QUANT_ERROR_FORMATS = {"mxfp8": 1, "nvfp4": 2}
+
+
 class B200MicroExpertChannelMixer(nn.Module):
     """Shared SwiGLU plus routed micro-experts on B200 (experts/mixer.py:38-241)."""
 
@@ -714,6 +718,7 @@ class B200MicroExpertChannelMixer(nn.Module):
         object.__setattr__(self, "_potentiation_controller_ref", ref(potentiation_controller))
         object.__setattr__(self, "_residency_ref", ref(residency))
         object.__setattr__(self, "_pack_cache", {})
+        object.__setattr__(self, "_quant_error_cache", None)
         object.__setattr__(self, "_lane_cache", None)
         object.__setattr__(self, "_ws_cache", {})
         object.__setattr__(self, "_stage_event_array", None)
@@ -842,6 +847,39 @@ class B200MicroExpertChannelMixer(nn.Module):
         self._pack_cache[batch_class] = (key, packed)
         return packed
 
+    def _quant_error(self, device: torch.device) -> Tensor | None:
+        """Reconstruction error of every expert's low-precision copies
+        (``MicroExpertBank.quantization_error``, experts/bank.py:526-592), an
+        [E] float tensor computed on the device by ``spx_expert_quant_error``
+        whenever the masters change; each forward's dispatch reports it for
+        the selected experts.  None for bfloat16 / float32 expert weights (the
+        reported errors are zeros).  With expert offload the paged cache
+        computes it while packing its host bank."""
+
+        fmt = _QUANT_ERROR_FORMATS.get(self.config.expert_weight_format)
+        if fmt is None:
+            return None
+        if self.experts.expert_offload_enabled:
+            cache = self.experts._offload
+            cache.ensure_packed()
+            return cache.quant_error
+        ex = self.experts
+        masters = (ex.gate_proj, ex.up_proj, ex.down_proj)
+        key = (device,) + tuple((t.data_ptr(), t._version) for t in masters)
+        cached = self._quant_error_cache
+        if cached is not None and cached[0] == key:
+            return cached[1]
+        out = torch.empty(self.config.num_experts, dtype=torch.float32, device=device)
+        bits = [_bits(t) for t in masters]
+        src = _lib.ReferenceWeights(gate_proj=bits[0].data_ptr(), up_proj=bits[1].data_ptr(),
+                                    down_proj=bits[2].data_ptr())
+        dims = layer_dims(self.config, 1, self.active_experts)
+        _lib.check(_lib.load().spx_expert_quant_error(dims, src, fmt, out.data_ptr(),
+                                                      torch.cuda.current_stream(device).cuda_stream),
+                   "spx_expert_quant_error")
+        object.__setattr__(self, "_quant_error_cache", (key, out))
+        return out
+
     def _lanes(self, device: torch.device) -> Tensor | None:
         """Per-expert kernel lane (uint8 [E], 1 = the layer's low-precision lane,
         MXFP8 or NVFP4) from the promotion mask.
@@ -949,6 +987,7 @@ class B200MicroExpertChannelMixer(nn.Module):
         stats = torch.empty(6, dtype=torch.long, device=device)
         ratios = torch.empty(2, dtype=torch.float32, device=device)
         aux = torch.empty(1, dtype=torch.bfloat16, device=device)
+        quant_error = torch.empty(E, dtype=torch.float32, device=device)
         injected = None
         if router_logits is not None:
             if router_logits.shape != (batch, seq_len, E) or router_logits.dtype != torch.bfloat16:
@@ -971,6 +1010,7 @@ class B200MicroExpertChannelMixer(nn.Module):
             expert_w2_mx=_lib.ptr(packed.get("expert_w2_mx")),
             expert_w2_mx_scales=_lib.ptr(packed.get("expert_w2_mx_scales")),
             expert_nvfp4_amax=_lib.ptr(packed.get("expert_nvfp4_amax")),
+            expert_quant_error=_lib.ptr(self._quant_error(device)),
         )
         events = self._stage_event_array
         outs = _lib.LayerOutputs(
@@ -979,6 +1019,7 @@ class B200MicroExpertChannelMixer(nn.Module):
             group_stats=stats.data_ptr(), group_ratios=ratios.data_ptr(), auxiliary_loss=aux.data_ptr(),
             dispatch_order=None, expert_counts=None, injected_logits=_lib.ptr(injected), router_logits=None,
             stage_events=None if events is None else _lib.ctypes.addressof(events),
+            expert_quantization_error=quant_error.data_ptr(),
         )
         stream = torch.cuda.current_stream(device).cuda_stream
         if self.experts.expert_offload_enabled:
@@ -1001,7 +1042,7 @@ class B200MicroExpertChannelMixer(nn.Module):
             "routing_weights": weights,
             "router_scores": scores,
             "expert_utilization": util,
-            "expert_quantization_error": torch.zeros(E, dtype=torch.float32, device=device),
+            "expert_quantization_error": quant_error,
             "promoted_experts": controller.promoted_mask.detach().clone(),
             "resident_experts": residency.resident_mask.detach().clone(),
             "expert_paging": self.experts.expert_paging_enabled,
@@ -1348,6 +1389,26 @@ def route(logits: Tensor, top_k: int, *, transform: str = "softplus",
     return scores, ids, weights
 
 
+def rms_norm(hidden: Tensor, weight: Tensor, eps: float = 1e-6) -> Tensor:
+    """``RMSNorm.forward`` (nn/norm.py:28-31) of BF16 rows on the device
+    (spx_rmsnorm_rows): the pass ``B200ChannelBlock`` fuses before the layer.
+    ``hidden`` [..., d] BF16 CUDA, ``weight`` [d]; returns BF16 rows [..., d]."""
+
+    if hidden.dtype != torch.bfloat16 or not hidden.is_cuda:
+        raise ValueError("hidden must be a bfloat16 CUDA tensor")
+    d = hidden.shape[-1]
+    if weight.shape != (d,):
+        raise ValueError(f"weight must be [{d}]")
+    rows = hidden.contiguous().view(-1, d)
+    w = weight.detach().to(device=hidden.device, dtype=torch.bfloat16).contiguous()
+    out = torch.empty_like(rows)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(hidden.device).cuda_stream
+    _lib.check(lib.spx_rmsnorm_rows(rows.data_ptr(), w.data_ptr(), float(eps), rows.shape[0], d, out.data_ptr(), d,
+                                    stream), "spx_rmsnorm_rows")
+    return out.view(hidden.shape)
+
+
 def dispatch(expert_ids: Tensor, num_experts: int) -> tuple[Tensor, Tensor]:
     """Stable permutation of pairs by expert and per-expert counts (spx_dispatch).
 
@@ -1390,6 +1451,7 @@ __all__ = [
     "SurpriseRouter",
     "SwiGLU",
     "dispatch",
+    "rms_norm",
     "route",
     "softplus_table",
 ]

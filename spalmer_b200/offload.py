@@ -187,6 +187,7 @@ class PagedExpertCache:
         self._bank_ref = ref(bank)
         self.host: dict[str, Tensor] = {}     # [E, bytes per expert] pinned
         self.device: dict[str, Tensor] = {}   # [capacity, bytes per expert]
+        self.quant_error: Tensor | None = None  # [E] low-precision reconstruction error (device), see _pack_host
         self._master_key: tuple | None = None
         self.copy_stream: torch.cuda.Stream | None = None
         self.physical_bytes_copied = 0  # packed bytes moved host -> device (all arrays, padding included)
@@ -251,6 +252,12 @@ class PagedExpertCache:
         pin = gate.device.type == "cpu"
         host = {name: torch.empty(E, n, dtype=torch.uint8, pin_memory=pin) for name, n in per.items()}
         dev = self.target
+        # reconstruction error of every expert's low-precision copies (bank.py:526-592), from
+        # the same device copies of the masters
+        from spalmer_b200.experts import _QUANT_ERROR_FORMATS
+
+        qfmt = _QUANT_ERROR_FORMATS.get(self.config.expert_weight_format)
+        quant_error = torch.zeros(E, dtype=torch.float32, device=dev) if qfmt is not None else None
         stream = torch.cuda.current_stream(dev)
         step = 32
         with torch.cuda.device(dev):
@@ -270,6 +277,9 @@ class PagedExpertCache:
                 _lib.check(lib.spx_pack_weights(dims, src, scratch.data_ptr(), out["expert_w1"].data_ptr(),
                                                 out["expert_w2"].data_ptr(), None, None, stream.cuda_stream),
                            "spx_pack_weights (expert masters)")
+                if qfmt is not None:
+                    _lib.check(lib.spx_expert_quant_error(dims, src, qfmt, quant_error[e0:].data_ptr(),
+                                                          stream.cuda_stream), "spx_expert_quant_error")
                 if dims.mxfp8_lane:
                     from spalmer_b200.experts import pack_lowp_experts
 
@@ -282,6 +292,7 @@ class PagedExpertCache:
                     host[name][e0:e0 + n].copy_(t)
         stream.synchronize()
         self.host = host
+        self.quant_error = quant_error
         if not self.device:
             self.device = {name: torch.empty(self.capacity, n, dtype=torch.uint8, device=dev)
                            for name, n in per.items()}

@@ -95,3 +95,68 @@ def set_mxfp8_lanes(mixer, lane_mx: np.ndarray) -> None:
     with torch.no_grad():
         mask = mixer.potentiation_controller.promoted_mask
         mask.copy_(torch.from_numpy(~lane_mx).to(mask.device))
+
+
+def torch_layer_update(mixer, x: torch.Tensor, expert_ids: torch.Tensor, weights: torch.Tensor,
+                       lane_mx: np.ndarray | None = None) -> torch.Tensor:
+    """The layer update for every token, restated in FP32 torch ops on the
+    tensors' device with the reference's BF16 rounding points, given the
+    layer's own routing: per routed pair bf16(bf16(SwiGLU_e(x)) * w) with
+    h = bf16(bf16(silu(bf16(x@G))) * bf16(x@U)) (experts/bank.py:755-763,
+    970-978), the token's k pairs summed in FP32 and rounded once (the grouped
+    executor's index_add), plus the shared SwiGLU (nn/ffn.py:27-30), rounded.
+    Experts with lane_mx[e] run the ("mxfp8", "mxfp8") pair: each projection's
+    operands quantised row-wise along K by the oracle's quantiser
+    (experts/native.py:113-140), dequantised and multiplied in FP32.  The
+    full-size tests check every row against it (and a token sample against the
+    oracle); sums run in torch's order, so it is compared within the BF16
+    tolerance."""
+
+    from oracle.mxfp8 import dequantize_rows, quantize_rows
+
+    def mx(t: torch.Tensor) -> torch.Tensor:  # [rows, K] FP32 -> deq(mx(rows)) on the same device
+        q, sb = quantize_rows(t.float().cpu().numpy())
+        return torch.from_numpy(dequantize_rows(q, sb)).to(t.device)
+
+    def mx_mm(a: torch.Tensor, w_io: torch.Tensor) -> torch.Tensor:  # a [n, K] @ w_io [K, N], both quantised along K
+        return mx(a) @ mx(w_io.float().T.contiguous()).T
+
+    def bf(t: torch.Tensor) -> torch.Tensor:
+        return t.to(torch.bfloat16).float()
+
+    prev_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        sd = mixer.state_dict()
+        dev = x.device
+        T, d = x.shape
+        k = expert_ids.shape[1]
+        xf = x.float()
+        flat = expert_ids.reshape(-1).to(dev)
+        order = torch.argsort(flat, stable=True)
+        counts = torch.bincount(flat, minlength=sd["experts.gate_proj"].shape[0]).tolist()
+        wf = weights.reshape(-1).to(dev).float()
+        weighted = torch.zeros(T * k, d, dtype=torch.float32, device=dev)
+        start = 0
+        for e, n in enumerate(counts):
+            if n == 0:
+                continue
+            rows = order[start:start + n]
+            start += n
+            xe = xf[rows // k]
+            gate_e, up_e, down_e = (sd[f"experts.{n}_proj"][e].to(dev).float() for n in ("gate", "up", "down"))
+            mm = mx_mm if lane_mx is not None and lane_mx[e] else torch.matmul
+            g = bf(mm(xe, gate_e))
+            u = bf(mm(xe, up_e))
+            h = bf(bf(torch.nn.functional.silu(g)) * u)
+            y = bf(mm(h, down_e))
+            weighted[rows] = bf(y * wf[rows, None])
+        routed = bf(weighted.view(T, k, d).sum(dim=1))
+        if "shared.gate_projection.weight" in sd:
+            sg = bf(xf @ sd["shared.gate_projection.weight"].to(dev).float().T)
+            su = bf(xf @ sd["shared.up_projection.weight"].to(dev).float().T)
+            sh = bf(bf(torch.nn.functional.silu(sg)) * su)
+            routed = bf(routed + bf(sh @ sd["shared.down_projection.weight"].to(dev).float().T))
+        return routed.to(torch.bfloat16)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev_tf32

@@ -20,7 +20,8 @@ from oracle import mxfp8 as MX
 from oracle.bf16 import bf16_bits_to_f32, f32_to_bf16_bits
 from spalmer_b200 import B200MicroExpertChannelMixer
 from spalmer_b200.native import mx_quantize_rows, mxfp8_mm_nt, native_expert_matmul
-from tests.helpers import bf16_bits, from_bits, mxfp8_config, mxfp8_experts, oracle_params, set_mxfp8_lanes
+from tests.helpers import (bf16_bits, from_bits, mxfp8_config, mxfp8_experts, oracle_params, set_mxfp8_lanes,
+                           torch_layer_update)
 
 pytestmark = pytest.mark.gpu
 
@@ -128,7 +129,8 @@ def test_mxfp8_layer_matches_oracle_given_logits(name, fraction):
 
 
 def test_mxfp8_layer_full_size_sample_and_determinism():
-    """100M shape, 25% of experts MXFP8: sampled rows vs the oracle, bitwise-stable reruns."""
+    """100M shape, 25% of experts MXFP8: sampled rows vs the oracle, every row
+    vs the FP32 torch restatement, bitwise-stable reruns."""
 
     config = mxfp8_config(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768, active_experts=8)
     torch.manual_seed(0)
@@ -159,3 +161,10 @@ def test_mxfp8_layer_full_size_sample_and_determinism():
     ref = bf16_bits_to_f32(want).astype(np.float64)
     bad = np.abs(got - ref) > ATOL + RTOL * np.abs(ref)
     assert not bad.any(), f"{bad.sum()} of {bad.size} outside tolerance"
+    # every update row against the FP32 torch restatement on the device
+    full = torch_layer_update(mixer, xd.reshape(-1, 768), out.metrics["expert_ids"].reshape(-1, k),
+                              out.metrics["routing_weights"].reshape(-1, k), lane_mx=lane)
+    got_all = bf16_bits_to_f32(bf16_bits(out.update).reshape(-1, 768)).astype(np.float64)
+    ref_all = bf16_bits_to_f32(bf16_bits(full)).astype(np.float64)
+    bad = np.abs(got_all - ref_all) > 1e-3 + RTOL * np.abs(ref_all)
+    assert not bad.any(), f"{bad.sum()} of {bad.size} outside tolerance (all rows)"

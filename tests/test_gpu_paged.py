@@ -26,7 +26,7 @@ DEV = torch.device("cuda", 0)
 
 M10 = dict(d_model=256, num_experts=64, expert_inter_dim=64, shared_inter_dim=256, active_experts=8)
 KEYS = ("expert_ids", "routing_weights", "router_scores", "expert_utilization", "expert_group_count",
-        "expert_group_max_load", "expert_group_real_pairs", "expert_group_padded_pairs")
+        "expert_group_max_load", "expert_group_real_pairs", "expert_group_padded_pairs", "expert_quantization_error")
 
 
 def make_pair(config, seed=0, lanes=None):

@@ -19,7 +19,7 @@ from spalmer_b200 import B200MicroExpertChannelMixer, MicroExpertsConfig, dispat
 from spalmer_b200.experts import softplus_table
 from tests.conftest import LAYER_CASES, load_layer_case
 from tests.golden.topk_cases import TOPK_CASES, generate_scores
-from tests.helpers import bf16_bits, build_mixer, from_bits, oracle_params, resident_mask
+from tests.helpers import bf16_bits, build_mixer, from_bits, oracle_params, resident_mask, torch_layer_update
 
 pytestmark = pytest.mark.gpu
 
@@ -216,6 +216,11 @@ def test_full_size_layer_properties(name):
     want = _oracle_update_subset(params, x_bits, ids, weights, sample)
     got = bf16_bits(out.update).reshape(-1, config.d_model)[sample]
     assert_close_bf16(got, want)
+    # (7) every update row against the FP32 torch restatement on the device
+    full = torch_layer_update(mixer, from_bits(x_bits, DEV), m["expert_ids"].reshape(-1, k),
+                              m["routing_weights"].reshape(-1, k))
+    # (the FP32 sums differ in order only: atol 1e-3 holds with room at these widths)
+    assert_close_bf16(bf16_bits(out.update).reshape(-1, config.d_model), bf16_bits(full), atol=1e-3)
 
 
 def test_layer_is_deterministic():
