@@ -881,10 +881,11 @@ def run_decode(args) -> None:
 
 def run_train(args) -> None:
     """One training step of the layer per timed step: forward (native kernels),
-    then backward (spx_layer_backward for the routed experts and router
-    scores; library GEMMs for the weight gradients, the router's input
-    gradient and the shared SwiGLU).  value = tokens / step time; data-parallel
-    replicas for N > 1 (no gradient all-reduce: the layer's own work only)."""
+    then backward (spx_layer_backward for the routed experts -- their weight
+    gradients included -- and the router scores; library GEMMs for the
+    router's weight and input gradients and the shared SwiGLU).  value =
+    tokens / step time; data-parallel replicas for N > 1 (no gradient
+    all-reduce: the layer's own work only)."""
 
     world, rank, local = init_dist()
     import torch.distributed as dist

@@ -53,7 +53,7 @@
 extern "C" {
 #endif
 
-#define SPX_ABI_VERSION 9
+#define SPX_ABI_VERSION 10
 
 #define SPX_OK 0
 #define SPX_ERR_INVALID_ARG -1
@@ -479,6 +479,14 @@ typedef struct spx_layer_grads {
   uint16_t* dy_sorted;              /* [T*k, d]   out                           */
   uint16_t* dgu_sorted;             /* [T*k, 2*kI] out, kI = round_up(I, 64)    */
   int32_t* expert_counts;           /* [E]     out                              */
+  /* The routed experts' weight gradients (optional; NULL = not computed):
+   * d gate | d up [E, d, I] = x_e^T [dg | du]_e and d down [E, I, d] =
+   * h_e^T dy_e over each expert's sorted rows, FP32 accumulation, BF16 out
+   * (tcgen05, both operands MN-major from the sorted buffers above).  Needs
+   * inter_dim % 8 == 0; all three or none. */
+  uint16_t* d_gate_proj;
+  uint16_t* d_up_proj;
+  uint16_t* d_down_proj;
 } spx_layer_grads;
 
 int spx_layer_backward_sizes(const spx_layer_dims* dims, size_t* workspace_bytes);

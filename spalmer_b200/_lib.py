@@ -76,7 +76,7 @@ EXPORTED = (
     "spx_dispatch_static_status",
 )
 
-ABI_VERSION = 9
+ABI_VERSION = 10
 
 _vp = ctypes.c_void_p
 
@@ -181,6 +181,9 @@ class LayerGrads(ctypes.Structure):
         ("dy_sorted", _vp),
         ("dgu_sorted", _vp),
         ("expert_counts", _vp),
+        ("d_gate_proj", _vp),
+        ("d_up_proj", _vp),
+        ("d_down_proj", _vp),
     ]
 
 

@@ -17,7 +17,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 TARGET = HERE / "libspx.so"
-SOURCES = ("abi.cu", "gemm.cu", "route.cu", "dispatch.cu", "pack.cu", "dispatch_static.cu", "launch.cu", "mxfp8.cu", "calibration.cu", "backward.cu", "block.cu", "paged.cu", "nvfp4.cu", "peer.cu", "gemv.cu", "quant_error.cu")
+SOURCES = ("abi.cu", "gemm.cu", "route.cu", "dispatch.cu", "pack.cu", "dispatch_static.cu", "launch.cu", "mxfp8.cu", "calibration.cu", "backward.cu", "block.cu", "paged.cu", "nvfp4.cu", "peer.cu", "gemv.cu", "quant_error.cu", "wgrad.cu")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

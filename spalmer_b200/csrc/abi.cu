@@ -432,6 +432,7 @@ int expert_gemvs(const Ctx& c, const uint16_t* xa, const int* src_row, const uin
   g.tiles_mx = p.tiles_mx;
   g.num_tiles_mx = p.num_tiles_mx;
   g.max_tiles = s.max_tiles;
+  g.tile_grid = static_cast<int>(std::min<int64_t>(s.max_tiles, s.P));  // a tile holds >= 1 pair
   g.src_row = src_row;
   g.status = c.status;
   g.d = s.d;
@@ -1518,6 +1519,13 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
       gr->h_sorted == nullptr || gr->dy_sorted == nullptr || gr->dgu_sorted == nullptr ||
       gr->expert_counts == nullptr)
     return SPX_ERR_INVALID_ARG;
+  const int wgrad_outs = (gr->d_gate_proj != nullptr) + (gr->d_up_proj != nullptr) + (gr->d_down_proj != nullptr);
+  if (wgrad_outs != 0 && wgrad_outs != 3) return SPX_ERR_INVALID_ARG;
+  const bool wgrad = wgrad_outs == 3;
+  if (wgrad && s.I % 8 != 0) return SPX_ERR_UNSUPPORTED;
+  if (wgrad && (!aligned16(gr->h_sorted) || !aligned16(gr->d_gate_proj) || !aligned16(gr->d_up_proj) ||
+                !aligned16(gr->d_down_proj)))
+    return SPX_ERR_ALIGNMENT;
   if (int rc = check_layer_weights(s, dims, w, true, true, false); rc != SPX_OK) return rc;
   if (!aligned16(hidden) || !aligned16(gr->d_update) || !aligned16(workspace) || !aligned16(gr->dgu_sorted) ||
       !aligned16(gr->x_sorted) || !aligned16(gr->dy_sorted) || !aligned16(gr->d_hidden_experts) ||
@@ -1607,6 +1615,15 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
   if ((rc = launch_bwd_gather(hidden, gr->d_update, da.src_row, da.sorted_weights, s.P, s.d, gr->x_sorted,
                               gr->dy_sorted, st)) != SPX_OK)
     return rc;
+  // ---- the experts' weight gradients over the sorted rows (tcgen05, MN-major operands)
+  if (wgrad) {
+    if ((rc = launch_wgrad(gr->x_sorted, s.d, s.d, gr->dgu_sorted, 2 * ki, 2 * ki, s.P, gr->expert_counts, s.E,
+                           gr->d_gate_proj, s.I, s.I, gr->d_up_proj, s.I, ki, s.I, c.status, st)) != SPX_OK)
+      return rc;
+    if ((rc = launch_wgrad(gr->h_sorted, s.I, s.I, gr->dy_sorted, s.d, s.d, s.P, gr->expert_counts, s.E,
+                           gr->d_down_proj, s.d, s.d, nullptr, 0, 0, 0, c.status, st)) != SPX_OK)
+      return rc;
+  }
   // ---- router: selection and load-balance softmaxes, softplus
   BwdRouterArgs ra{};
   ra.scores = gr->router_scores;

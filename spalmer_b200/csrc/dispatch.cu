@@ -123,16 +123,35 @@ __global__ void __launch_bounds__(kPrefixWarps * 32) dispatch_prefix_kernel(cons
   }
 }
 
-// Shared by the scan kernels: from each expert's pair count (thread e holds
-// expert e's), the pair starts, both lanes' tile tables, utilization, group
-// statistics and the auxiliary loss (lb_e = expert e's load-balance sum).
-// One CTA of 1024 threads; E <= 1024.
+// Per-expert inputs of the finishing pass (thread e holds expert e's), loaded
+// by the caller ahead of its first barrier so that their latency overlaps the
+// counting.
+struct ExpertIn {
+  int count;     // pairs routed to the expert
+  float lb;      // its load-balance sum (used with aux_loss)
+  bool mx;       // runs the MXFP8 lane
+  bool resident;
+  float recon;   // reconstruction error of its low-precision copies (quant_error)
+};
+
+__device__ __forceinline__ ExpertIn load_expert_in(const DispatchArgs& a, int e) {
+  ExpertIn in{0, 0.0f, false, false, 0.0f};
+  if (e < a.num_experts) {
+    in.mx = a.lane_mx != nullptr && a.lane_mx[e] != 0;
+    in.resident = a.resident != nullptr && a.resident[e] != 0;
+    in.recon = a.recon_error != nullptr ? a.recon_error[e] : 0.0f;
+  }
+  return in;
+}
+
+// Shared by the scan kernels: from each expert's inputs, the pair starts,
+// both lanes' tile tables, utilization, quantization telemetry, group
+// statistics and the auxiliary loss.  One CTA of 1024 threads; E <= 1024.
 struct ScanShared {
   int scan[1024];
   unsigned long long scan64[1024];
-  float red[1024];
-  long long i64[4];
-  int count[1024];
+  float red[32];
+  long long stat[32][4];
 };
 
 // Inclusive scan over the 1024 threads of the CTA: shuffles within each warp,
@@ -162,129 +181,115 @@ __device__ __forceinline__ T block_inclusive_scan(T v, T* warp_tot, T& tot) {
   return v + (warp > 0 ? warp_tot[warp - 1] : T(0));
 }
 
-// Returns this thread's expert's first dispatch position.
-__device__ __forceinline__ int finish_dispatch(const DispatchArgs& a, int count, float lb_e, ScanShared& sh) {
-  int* s_scan = sh.scan;
-  unsigned long long* s_scan64 = sh.scan64;
-  float* s_red = sh.red;
-  long long* s_i64 = sh.i64;
-  int* s_count = sh.count;
+// Returns this thread's expert's first dispatch position.  Barriers: the
+// scan (two; four when P >= 2^21 needs separate scans of the pair and tile
+// counts) and one for the statistics.
+__device__ __forceinline__ int finish_dispatch(const DispatchArgs& a, const ExpertIn& in, ScanShared& sh) {
   const int E = a.num_experts;
   const int e = threadIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Block-wide exclusive scans: pair starts and tile starts.
+  const bool valid = e < E;
+  const int count = valid ? in.count : 0;
   const int tiles = (count + kTileRows - 1) / kTileRows;
-  int total_pairs = 0;
-  const int mine_count = (e < E) ? count : 0;
-  const int start = block_inclusive_scan<int>(mine_count, s_scan, total_pairs) - mine_count;
-  // Tile starts of the two lanes in one scan: BF16-lane tiles in the low
-  // 32 bits, MXFP8-lane tiles in the high 32 bits.
-  const bool mx = (e < E) && a.lane_mx != nullptr && a.lane_mx[e] != 0;
-  const unsigned long long mine =
-      (e < E) ? (mx ? (static_cast<unsigned long long>(tiles) << 32) : static_cast<unsigned long long>(tiles)) : 0ull;
-  unsigned long long all_tiles = 0ull;
-  const unsigned long long excl = block_inclusive_scan<unsigned long long>(mine, s_scan64, all_tiles) - mine;
-  const int tile_start = mx ? static_cast<int>(excl >> 32) : static_cast<int>(excl & 0xFFFFFFFFull);
-  if (threadIdx.x == 1023) {
-    *a.num_tiles = static_cast<int>(all_tiles & 0xFFFFFFFFull);
-    if (a.num_tiles_mx != nullptr) *a.num_tiles_mx = static_cast<int>(all_tiles >> 32);
+  // Block-wide exclusive scans of the pair counts and of both lanes' tile
+  // counts: one scan of three 21-bit fields while the totals fit.
+  int start, tile_start, tiles_bf, tiles_mx;
+  if (a.pairs < (int64_t(1) << 21)) {
+    const unsigned long long mine =
+        static_cast<unsigned long long>(count) |
+        (static_cast<unsigned long long>(in.mx ? 0 : tiles) << 21) |
+        (static_cast<unsigned long long>(in.mx ? tiles : 0) << 42);
+    unsigned long long all = 0ull;
+    const unsigned long long excl = block_inclusive_scan<unsigned long long>(mine, sh.scan64, all) - mine;
+    constexpr unsigned long long kField = (1ull << 21) - 1ull;
+    start = static_cast<int>(excl & kField);
+    tile_start = static_cast<int>(in.mx ? (excl >> 42) & kField : (excl >> 21) & kField);
+    tiles_bf = static_cast<int>((all >> 21) & kField);
+    tiles_mx = static_cast<int>((all >> 42) & kField);
+  } else {
+    int total_pairs = 0;
+    start = block_inclusive_scan<int>(count, sh.scan, total_pairs) - count;
+    // BF16-lane tiles in the low 32 bits, MXFP8-lane tiles in the high 32 bits
+    const unsigned long long mine =
+        in.mx ? (static_cast<unsigned long long>(tiles) << 32) : static_cast<unsigned long long>(tiles);
+    unsigned long long all = 0ull;
+    const unsigned long long excl = block_inclusive_scan<unsigned long long>(mine, sh.scan64, all) - mine;
+    tile_start = in.mx ? static_cast<int>(excl >> 32) : static_cast<int>(excl & 0xFFFFFFFFull);
+    tiles_bf = static_cast<int>(all & 0xFFFFFFFFull);
+    tiles_mx = static_cast<int>(all >> 32);
   }
-  if (e < E) {
+  if (threadIdx.x == 1023) {
+    *a.num_tiles = tiles_bf;
+    if (a.num_tiles_mx != nullptr) *a.num_tiles_mx = tiles_mx;
+  }
+  // Utilization (losses.py:28-33): count / P in float32.
+  const float util = valid ? static_cast<float>(count) / static_cast<float>(a.pairs) : 0.0f;
+  if (valid) {
     a.counts[e] = count;
     a.starts[e] = start;
-    int4* table = mx ? a.tiles_mx : a.tiles;
+    int4* table = in.mx ? a.tiles_mx : a.tiles;
     for (int t = 0; t < tiles; ++t) {
       const int r0 = t * kTileRows;
       // w repeats the expert: a page of a paged pass renames x to a cache slot
       table[tile_start + t] = make_int4(e, start + r0, min(kTileRows, count - r0), e);
     }
+    if (a.utilization != nullptr) a.utilization[e] = util;
+    // Quantization telemetry (bank.py:526-566): the error of every selected expert, zero elsewhere.
+    if (a.quant_error != nullptr) a.quant_error[e] = count > 0 ? in.recon : 0.0f;
   }
 
-  // Utilization (losses.py:28-33): count / P in float32.
-  const float util = (e < E) ? static_cast<float>(count) / static_cast<float>(a.pairs) : 0.0f;
-  if (e < E && a.utilization != nullptr) a.utilization[e] = util;
-  // Quantization telemetry (bank.py:526-566): the error of every selected expert, zero elsewhere.
-  if (e < E && a.quant_error != nullptr)
-    a.quant_error[e] = (count > 0 && a.recon_error != nullptr) ? a.recon_error[e] : 0.0f;
-
-  // Group statistics (mixer.py:257-297).
-  // Warp reductions, then one thread folds the 32 warp results (no contended atomics).
-  __syncthreads();  // every thread has read its tile_start out of s_scan
-  {
-    const bool act = e < E && count > 0;
-    int groups_w = __popc(__ballot_sync(0xFFFFFFFFu, act));
-    int resid_w = __popc(__ballot_sync(0xFFFFFFFFu, e < E && a.resident != nullptr && a.resident[e] != 0));
-    int max_w = act ? count : 0;
-    long long pad_w = act ? (a.execution_loop ? count : next_pow2_i64(count)) : 0;
+  // Group statistics (mixer.py:257-297) and the load-balance loss
+  // (losses.py:58-70) in one reduction round: warp reductions, then thread 0
+  // folds the 32 warp results in order.
+  const bool act = valid && count > 0;
+  long long groups_w = __popc(__ballot_sync(0xFFFFFFFFu, act));
+  long long resid_w = __popc(__ballot_sync(0xFFFFFFFFu, valid && in.resident));
+  long long max_w = act ? count : 0;
+  long long pad_w = act ? (a.execution_loop ? count : next_pow2_i64(count)) : 0;
+  // mean_p = bf16(sum_t p / T), frac = bf16(util), prod = bf16(frac*mean_p)
+  float prod = 0.0f;
+  const bool lb = a.aux_loss != nullptr && a.lb_blocks > 0;
+  if (valid && lb) prod = round_bf16(round_bf16(util) * round_bf16(in.lb / static_cast<float>(a.tokens)));
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      max_w = max(max_w, __shfl_xor_sync(0xFFFFFFFFu, max_w, off));
-      pad_w += __shfl_xor_sync(0xFFFFFFFFu, pad_w, off);
-    }
-    if (lane == 0) {
-      s_scan[warp] = groups_w;
-      s_scan[32 + warp] = resid_w;
-      s_scan[64 + warp] = max_w;
-      s_count[warp] = static_cast<int>(pad_w);  // s_count is no longer needed: reuse it
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      long long g = 0, rsd = 0, mx = 0, pad = 0;
-      for (int w = 0; w < 32; ++w) {
-        g += s_scan[w];
-        rsd += s_scan[32 + w];
-        mx = max(mx, static_cast<long long>(s_scan[64 + w]));
-        pad += s_count[w];
-      }
-      s_i64[0] = g;
-      s_i64[1] = mx;
-      s_i64[2] = pad;
-      s_i64[3] = rsd;
-    }
-    __syncthreads();
+  for (int off = 16; off > 0; off >>= 1) {
+    max_w = max(max_w, __shfl_xor_sync(0xFFFFFFFFu, max_w, off));
+    pad_w += __shfl_xor_sync(0xFFFFFFFFu, pad_w, off);
+    prod += __shfl_xor_sync(0xFFFFFFFFu, prod, off);
   }
-  if (threadIdx.x == 0 && a.group_stats != nullptr) {
-    const long long groups = s_i64[0], max_load = s_i64[1], padded = s_i64[2];
-    const long long real = a.pairs;
-    a.group_stats[0] = groups;             // expert_group_count
-    a.group_stats[1] = max_load;           // expert_group_max_load
-    a.group_stats[2] = real;               // expert_group_real_pairs
-    a.group_stats[3] = padded;             // expert_group_padded_pairs
-    a.group_stats[4] = max_load * groups;  // ..._global_max_counterfactual_padded_pairs
-    a.group_stats[5] = groups;             // num_active_experts ((utilization > 0).sum())
-    a.group_ratios[0] = static_cast<float>(padded) / static_cast<float>(real);
-    a.group_ratios[1] = static_cast<float>(max_load * groups) / static_cast<float>(real);
+  if (lane == 0) {
+    sh.stat[warp][0] = groups_w;
+    sh.stat[warp][1] = resid_w;
+    sh.stat[warp][2] = max_w;
+    sh.stat[warp][3] = pad_w;
+    sh.red[warp] = prod;
   }
-
-  // Load-balance loss (losses.py:58-70) with its BF16 rounding points:
-  // mean_p = bf16(sum_t p / T), frac = bf16(util), prod = bf16(frac*mean_p),
-  // total = bf16(sum prod), loss = bf16(bf16(eligible) * total).
-  if (a.aux_loss != nullptr && a.lb_blocks > 0) {
-    // Per-expert sums of the route blocks' probability partials (dispatch_prefix_kernel).
-    float prod = 0.0f;
-    if (e < E) {
-      const float s = lb_e;
-      const float mean_p = round_bf16(s / static_cast<float>(a.tokens));
-      prod = round_bf16(round_bf16(util) * mean_p);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    long long g = 0, rsd = 0, mx = 0, pad = 0;
+    float total = 0.0f;
+    for (int w = 0; w < 32; ++w) {
+      g += sh.stat[w][0];
+      rsd += sh.stat[w][1];
+      mx = max(mx, sh.stat[w][2]);
+      pad += sh.stat[w][3];
+      total += sh.red[w];
     }
-    // sum over experts: butterfly within each warp, then warp 0 over the 32 warp sums
-    float v = prod;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, off);
-    if (lane == 0) s_red[warp] = v;
-    __syncthreads();
-    if (warp == 0) {
-      float w = s_red[lane];
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) w += __shfl_xor_sync(0xFFFFFFFFu, w, off);
-      if (lane == 0) s_red[0] = w;
+    if (a.group_stats != nullptr) {
+      const long long real = a.pairs;
+      a.group_stats[0] = g;        // expert_group_count
+      a.group_stats[1] = mx;       // expert_group_max_load
+      a.group_stats[2] = real;     // expert_group_real_pairs
+      a.group_stats[3] = pad;      // expert_group_padded_pairs
+      a.group_stats[4] = mx * g;   // ..._global_max_counterfactual_padded_pairs
+      a.group_stats[5] = g;        // num_active_experts ((utilization > 0).sum())
+      a.group_ratios[0] = static_cast<float>(pad) / static_cast<float>(real);
+      a.group_ratios[1] = static_cast<float>(mx * g) / static_cast<float>(real);
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      const float total = round_bf16(s_red[0]);
-      const long long n_eligible = a.resident != nullptr ? s_i64[3] : a.eligible_experts;
+    if (lb) {
+      // total = bf16(sum prod), loss = bf16(bf16(eligible) * total)
+      const long long n_eligible = a.resident != nullptr ? rsd : a.eligible_experts;
       const float eligible = round_bf16(static_cast<float>(n_eligible));
-      a.aux_loss[0] = f32_to_bf16_rne(eligible * total);
+      a.aux_loss[0] = f32_to_bf16_rne(eligible * round_bf16(total));
     }
   }
   return start;
@@ -292,18 +297,22 @@ __device__ __forceinline__ int finish_dispatch(const DispatchArgs& a, int count,
 
 __global__ void __launch_bounds__(1024) dispatch_scan_kernel(const DispatchArgs a) {
   __shared__ ScanShared sh;
-  const int E = a.num_experts;
   const int e = threadIdx.x;
   // Chunk offsets, per-expert totals and load-balance sums come from dispatch_prefix_kernel.
-  const int count = (e < E) ? a.counts[e] : 0;
-  const float lb_e = (e < E && a.aux_loss != nullptr && a.lb_blocks > 0) ? a.lb_sum[e] : 0.0f;
-  finish_dispatch(a, count, lb_e, sh);
+  ExpertIn in = load_expert_in(a, e);
+  if (e < a.num_experts) {
+    in.count = a.counts[e];
+    if (a.aux_loss != nullptr && a.lb_blocks > 0) in.lb = a.lb_sum[e];
+  }
+  finish_dispatch(a, in, sh);
 }
 
 // Small batches (pairs <= kDispatchSmallPairs): the whole dispatch in one CTA
 // -- counts, the scan work above, then stable placement by warp 0, 32 pairs
-// at a time in pair order (match_any ranks within the 32).
+// at a time in pair order (match_any ranks within the 32).  Every global read
+// is issued before the first barrier.
 __global__ void __launch_bounds__(1024) dispatch_small_kernel(const DispatchArgs a) {
+  constexpr int kPer = kDispatchSmallPairs / 1024;  // pairs per thread
   __shared__ ScanShared sh;
   __shared__ int s_base[1024];
   __shared__ short s_ids[kDispatchSmallPairs];
@@ -311,30 +320,39 @@ __global__ void __launch_bounds__(1024) dispatch_small_kernel(const DispatchArgs
   const int E = a.num_experts;
   const int e = threadIdx.x;
   const int P = static_cast<int>(a.pairs);
+  const bool weights = a.sorted_weights != nullptr;
   griddep_wait();  // the expert ids, weights and load-balance partials come from the route kernel
   griddep_launch_dependents();
-  if (e < 1024) s_base[e] = 0;
+  int64_t xid[kPer];
+  uint16_t wv[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int p = threadIdx.x + j * 1024;
+    xid[j] = p < P ? a.ids[p] : -1;
+    wv[j] = (weights && p < P) ? a.pair_weights[p] : static_cast<uint16_t>(0);
+  }
+  ExpertIn in = load_expert_in(a, e);
+  if (e < E && a.aux_loss != nullptr && a.lb_blocks > 0) {
+#pragma unroll 8
+    for (int b = 0; b < a.lb_blocks; ++b) in.lb += a.lb_partial[static_cast<int64_t>(b) * E + e];
+  }
+  s_base[e] = 0;
   __syncthreads();
-  const bool weights = a.sorted_weights != nullptr;
-  for (int p = threadIdx.x; p < P; p += blockDim.x) {
-    const int64_t x = a.ids[p];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int p = threadIdx.x + j * 1024;
+    if (p >= P) continue;
+    const int64_t x = xid[j];
     const bool ok = x >= 0 && x < E;
     if (!ok) record_error(a.status, SPX_DEV_BAD_EXPERT);
     s_ids[p] = ok ? static_cast<short>(x) : static_cast<short>(-1);
-    if (weights) s_w[p] = a.pair_weights[p];
+    s_w[p] = wv[j];
     if (ok) atomicAdd(&s_base[x], 1);
   }
   __syncthreads();
-  const int count = (e < E) ? s_base[e] : 0;
-  float lb_e = 0.0f;
-  if (e < E && a.aux_loss != nullptr && a.lb_blocks > 0) {
-#pragma unroll 8
-    for (int b = 0; b < a.lb_blocks; ++b) lb_e += a.lb_partial[static_cast<int64_t>(b) * E + e];
-  }
-  __syncthreads();
-  const int start = finish_dispatch(a, count, lb_e, sh);
-  __syncthreads();
-  if (e < E) s_base[e] = start;
+  in.count = e < E ? s_base[e] : 0;
+  const int start = finish_dispatch(a, in, sh);
+  if (e < E) s_base[e] = start;  // nothing reads s_base between the count above and this store
   __syncthreads();
   if (threadIdx.x >= 32) return;
   const int lane = threadIdx.x;

@@ -183,8 +183,9 @@ __device__ __forceinline__ void tile_rows(const GemvPass& a, int& g, bool& mx, i
   }
   int t = blockIdx.x;
   int4 tile;
-  if (t >= a.max_tiles) {
-    t -= a.max_tiles;
+  const int per = a.tile_grid > 0 ? a.tile_grid : a.max_tiles;
+  if (t >= per) {
+    t -= per;
     if (a.tiles_mx == nullptr || t >= *a.num_tiles_mx) return;
     tile = a.tiles_mx[t];
     mx = true;
@@ -608,14 +609,16 @@ int pick_ksplit(int64_t units, int cols, int cols_per_mtile, int max_split) {
   return ks;
 }
 
+int gemv_tile_grid(const GemvPass& a) { return a.tile_grid > 0 ? a.tile_grid : a.max_tiles; }
+
 int64_t gemv_units(const GemvPass& a) {
-  return a.tiles != nullptr ? a.max_tiles : (a.dense_rows + kPassRows - 1) / kPassRows;
+  return a.tiles != nullptr ? gemv_tile_grid(a) : (a.dense_rows + kPassRows - 1) / kPassRows;
 }
 
 // Grid: x = tiles (BF16 table, then the MXFP8 table) or 1 (dense), y = column
 // groups, z = 16-row chunks of a dense pass.
 dim3 gemv_grid(const GemvPass& a, int col_groups) {
-  const unsigned x = a.tiles == nullptr ? 1u : static_cast<unsigned>(a.max_tiles * (a.tiles_mx != nullptr ? 2 : 1));
+  const unsigned x = a.tiles == nullptr ? 1u : static_cast<unsigned>(gemv_tile_grid(a) * (a.tiles_mx != nullptr ? 2 : 1));
   const unsigned z = a.tiles == nullptr ? static_cast<unsigned>((a.dense_rows + kPassRows - 1) / kPassRows) : 1u;
   return dim3(x, static_cast<unsigned>(col_groups), z);
 }

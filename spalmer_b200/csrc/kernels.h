@@ -361,7 +361,9 @@ struct GemvPass {
   const int* num_tiles;
   const int4* tiles_mx;       // MXFP8-lane tiles, or null
   const int* num_tiles_mx;
-  int max_tiles;              // capacity of each table (grid.x = max_tiles, x2 with tiles_mx)
+  int max_tiles;              // capacity of each table
+  int tile_grid;              // CTAs per table along grid.x (x2 with tiles_mx): a bound on the tiles a
+                              // pass can have (<= max_tiles; each tile holds >= 1 pair); 0 = max_tiles
   int dense_rows;
   const int* src_row;         // A row of each row position (gather), or null (identity)
   int* status;                // device status word
@@ -399,6 +401,24 @@ bool gemv_swiglu_ok(const GemvPass& a);
 bool gemv_rows_ok(const GemvPass& a);
 int launch_gemv_swiglu(GemvPass a, cudaStream_t stream);
 int launch_gemv_rows(GemvPass a, cudaStream_t stream);
+
+// Routed experts' weight gradients (wgrad.cu): out[e] = A_e^T B_e over each
+// expert's rows of A [rows, m_total] and B [rows, n_total] (dispatch order,
+// counts[e] rows per expert); output columns [0, n_valid0) of B land in out0
+// [E, m_total, ld0], columns [n_start1, n_start1 + n_valid1) in out1.
+struct WgradArgs {
+  CUtensorMap tma_a, tma_b;  // boxes of 64 rows x 64 columns, 128B swizzle
+  const int* counts;
+  int E, m_total, bn, m_tiles, n_tiles, stages;
+  uint16_t* out0;
+  int ld0, n_valid0;
+  uint16_t* out1;
+  int ld1, n_start1, n_valid1;
+  int* status;
+};
+int launch_wgrad(const uint16_t* a_rows, int64_t ld_a, int m_total, const uint16_t* b_rows, int64_t ld_b,
+                 int n_total, int64_t rows, const int* counts, int E, uint16_t* out0, int ld0, int n_valid0,
+                 uint16_t* out1, int ld1, int n_start1, int n_valid1, int* status, cudaStream_t stream);
 
 // Backward (backward.cu).
 struct BwdRouterArgs {

@@ -1130,10 +1130,14 @@ class B200MicroExpertChannelMixer(nn.Module):
         return ChannelMixerOutput(update=update, state=None, auxiliary_loss=aux, metrics=metrics)
 
     def _backward_native(self, x: Tensor, ids: Tensor, weights: Tensor, scores: Tensor, d_update: Tensor,
-                         d_aux: Tensor | None, d_scores: Tensor | None) -> dict[str, Tensor]:
+                         d_aux: Tensor | None, d_scores: Tensor | None,
+                         expert_wgrad: str = "native") -> dict[str, Tensor]:
         """Gradients of x and of every parameter (``spx_layer_backward`` for the
-        routed experts and the router scores; library GEMMs for the router's
-        and the experts' weight gradients and for the shared SwiGLU)."""
+        routed experts -- their weight gradients included, on tcgen05 grouped
+        GEMMs -- and the router scores; library GEMMs for the router's weight
+        gradient and the shared SwiGLU).  ``expert_wgrad="library"`` computes
+        the experts' weight gradients with ``torch._grouped_mm`` from the same
+        sorted rows instead (a comparison seam for the tests)."""
 
         import torch.nn.functional as F
 
@@ -1157,6 +1161,11 @@ class B200MicroExpertChannelMixer(nn.Module):
         dy_sorted = torch.empty(P, d, dtype=torch.bfloat16, device=device)
         dgu = torch.empty(P, 2 * kI, dtype=torch.bfloat16, device=device)
         counts = torch.empty(E, dtype=torch.int32, device=device)
+        # the experts' weight gradients come out of the same native call (tcgen05 grouped GEMMs over
+        # the sorted rows) when the hidden width allows 16-byte rows
+        native_wgrad = I % 8 == 0 and expert_wgrad == "native"
+        wgrads = {n: torch.empty(E, *shape, dtype=torch.bfloat16, device=device) if native_wgrad else None
+                  for n, shape in (("gate", (d, I)), ("up", (d, I)), ("down", (I, d)))}
         residency = self.residency
         mask = None if residency.is_full else residency.resident_mask.to(device=device).contiguous()
         lut = softplus_table(device) if config.router_score_transform == "softplus" else None
@@ -1182,7 +1191,8 @@ class B200MicroExpertChannelMixer(nn.Module):
             d_update=du.data_ptr(), d_scores=_lib.ptr(dsc), d_aux=_lib.ptr(dax),
             d_hidden_experts=d_hidden.data_ptr(), d_logits=d_logits.data_ptr(), x_sorted=x_sorted.data_ptr(),
             h_sorted=h_sorted.data_ptr(), dy_sorted=dy_sorted.data_ptr(), dgu_sorted=dgu.data_ptr(),
-            expert_counts=counts.data_ptr(),
+            expert_counts=counts.data_ptr(), d_gate_proj=_lib.ptr(wgrads["gate"]),
+            d_up_proj=_lib.ptr(wgrads["up"]), d_down_proj=_lib.ptr(wgrads["down"]),
         )
         stream = torch.cuda.current_stream(device).cuda_stream
         _lib.check(lib.spx_layer_backward(dims, pw, x.data_ptr(), gr, ws.data_ptr(), stream), "spx_layer_backward")
@@ -1193,10 +1203,15 @@ class B200MicroExpertChannelMixer(nn.Module):
         if self.router.proj.bias is not None:
             grads["router.proj.bias"] = d_logits.float().sum(0).to(torch.bfloat16)
         dx = torch.addmm(d_hidden, d_logits, w_router.detach())  # one rounding: d_hidden + d_logits @ W
-        offs = torch.cumsum(counts, 0, dtype=torch.int32)
-        grads["experts.gate_proj"] = _grouped_wgrad(x_sorted, dgu[:, :I], counts, offs)
-        grads["experts.up_proj"] = _grouped_wgrad(x_sorted, dgu[:, kI:kI + I], counts, offs)
-        grads["experts.down_proj"] = _grouped_wgrad(h_sorted, dy_sorted, counts, offs)
+        if native_wgrad:
+            grads["experts.gate_proj"] = wgrads["gate"]
+            grads["experts.up_proj"] = wgrads["up"]
+            grads["experts.down_proj"] = wgrads["down"]
+        else:
+            offs = torch.cumsum(counts, 0, dtype=torch.int32)
+            grads["experts.gate_proj"] = _grouped_wgrad(x_sorted, dgu[:, :I], counts, offs)
+            grads["experts.up_proj"] = _grouped_wgrad(x_sorted, dgu[:, kI:kI + I], counts, offs)
+            grads["experts.down_proj"] = _grouped_wgrad(h_sorted, dy_sorted, counts, offs)
         if self.shared is not None and _shared_bwd_native(self.shared, x):
             # Shared SwiGLU backward without autograd: [gate | up] in one GEMM,
             # the elementwise part in one kernel (spx_swiglu_backward_rows,
