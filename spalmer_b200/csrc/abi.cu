@@ -1151,18 +1151,26 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   c.mark(0);
   const uint16_t* xa = nullptr;
   if ((rc = stage_pad(c, hidden, &xa)) != SPX_OK) return rc;
-  // ---- side stream: the MXFP8 quantisation of the hidden rows (memory-bound)
-  // runs beside the router, selection and dispatch (instruction-bound) for
-  // large batches.  Decode-sized batches keep one stream: there the extra
-  // fork/join edges cost more than the few microseconds they would hide.
+  // ---- side stream: work that needs only the hidden rows runs beside the
+  // router, selection and dispatch.  Large batches: the MXFP8 quantisation of
+  // the rows (memory-bound, beside instruction-bound selection).  Decode-sized
+  // batches: the whole shared SwiGLU (two dense GEMVs) -- route and dispatch
+  // occupy a handful of SMs, and the shared output is needed only by the
+  // combine.
   const bool fork_mx = s.mx && !s.nv && !s.small && w->expert_lane_mxfp8 != nullptr;
+  // (only while the shared projections are dense GEMVs: no tcgen05 kernel,
+  // which would want the tensor memory the main stream's kernels hold)
+  const bool fork_shared = s.small && s.S > 0 && !fused_combine_ok(s) && s.T <= kGemvMaxTokens;
   SideStream ss{};
-  const bool forked = fork_mx && side_stream(c.st, &ss);
+  const bool forked = (fork_mx || fork_shared) && side_stream(c.st, &ss);
+  uint16_t* so = s.S > 0 ? at<uint16_t>(workspace, L.shared_out) : nullptr;
   if (forked) {
     if (cudaEventRecord(ss.fork, c.st) != cudaSuccess || cudaStreamWaitEvent(ss.side, ss.fork, 0) != cudaSuccess)
       return SPX_ERR_CUDA;
     const Ctx cs{s, L, workspace, ss.side, c.status, nullptr};
-    if ((rc = stage_quantize_x(cs, hidden, 0)) != SPX_OK) return rc;
+    if (fork_mx && (rc = stage_quantize_x(cs, hidden, 0)) != SPX_OK) return rc;
+    if (fork_shared && ((rc = stage_shared_gemm1(cs, w, xa)) != SPX_OK || (rc = stage_shared_gemm2(cs, w, so)) != SPX_OK))
+      return rc;
     if (cudaEventRecord(ss.join, ss.side) != cudaSuccess) return SPX_ERR_CUDA;
   }
   // ---- K1: router GEMM (unless logits are injected), scores, top-k, weights,
@@ -1174,17 +1182,18 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   if ((rc = launch_dispatch(da, c.st)) != SPX_OK) return rc;
   c.mark(3);
   // ---- K3: grouped experts (both lanes)
-  if (forked && cudaStreamWaitEvent(c.st, ss.join, 0) != cudaSuccess) return SPX_ERR_CUDA;
-  if ((rc = stage_experts(c, w, hidden, xa, da, 0, forked)) != SPX_OK) return rc;
+  if (fork_mx && forked && cudaStreamWaitEvent(c.st, ss.join, 0) != cudaSuccess) return SPX_ERR_CUDA;
+  if ((rc = stage_experts(c, w, hidden, xa, da, 0, fork_mx && forked)) != SPX_OK) return rc;
   // ---- K4: shared SwiGLU, then update = shared + the token's k weighted expert rows
   uint16_t* y = at<uint16_t>(workspace, L.y);
   if (fused_combine_ok(s)) {
     if ((rc = stage_shared_gemm1(c, w, xa)) != SPX_OK) return rc;
     if ((rc = stage_shared_gemm2(c, w, out->update, y, da.rank)) != SPX_OK) return rc;
   } else {
-    uint16_t* so = nullptr;
-    if (s.S > 0) {
-      so = at<uint16_t>(workspace, L.shared_out);
+    if (fork_shared && forked) {
+      if (cudaStreamWaitEvent(c.st, ss.join, 0) != cudaSuccess) return SPX_ERR_CUDA;
+      c.mark(6);
+    } else if (s.S > 0) {
       if ((rc = stage_shared_gemm1(c, w, xa)) != SPX_OK) return rc;
       if ((rc = stage_shared_gemm2(c, w, so)) != SPX_OK) return rc;
     } else {

@@ -36,44 +36,70 @@ int device_sm_count() {
   return g_sm_count[dev];
 }
 
-// Side streams: one non-blocking stream (same priority) and two events per
-// (device, caller stream), created on the first call that is not being
-// captured and kept for the life of the process.  Work forked onto the side
-// stream joins the caller's stream through the events, so the pair behaves as
-// one stream to the caller (CUDA graph capture included).
+// Side streams: a pool of kSidePool non-blocking streams (two events each)
+// per device, created on the first call on the device that is not being
+// captured and kept for the life of the process.  A caller stream takes the
+// next pool entry the first time it forks, which needs no creation, so a
+// stream first seen inside a capture (torch.cuda.graph captures on a stream
+// of its own) still forks.  Work forked onto the side stream joins the caller's
+// stream through the events, so the pair behaves as one stream to the caller,
+// CUDA graph capture included.  Past kSidePool caller streams, entries are
+// shared: their side work serialises on one stream (still correct, joined by
+// events), and a stream that one thread captures must not also run another
+// thread's eager side work.
 namespace {
-std::map<std::pair<int, cudaStream_t>, SideStream> g_side;
+constexpr int kSidePool = 4;
+struct SidePool {
+  SideStream entry[kSidePool];
+  int next = 0;
+};
+std::map<int, SidePool> g_pool;
+std::map<std::pair<int, cudaStream_t>, int> g_side;
+
+bool make_pool(int dev, SidePool* pool) {
+  int lo = 0, hi = 0;
+  if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess) lo = hi = 0;
+  for (int i = 0; i < kSidePool; ++i) {
+    SideStream& s = pool->entry[i];
+    // the highest priority: side work is short and sits beside the critical path
+    if (cudaStreamCreateWithPriority(&s.side, cudaStreamNonBlocking, hi) != cudaSuccess ||
+        cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+  }
+  (void)dev;
+  return true;
+}
 }  // namespace
 
 bool side_stream(cudaStream_t main, SideStream* out) {
   const int dev = current_device();
   if (dev < 0) return false;
   std::lock_guard<std::mutex> lock(g_mu);
+  auto pool_it = g_pool.find(dev);
+  if (pool_it == g_pool.end()) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(main, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+      cudaGetLastError();
+      return false;  // create nothing inside a capture: the caller runs unforked
+    }
+    SidePool pool;
+    if (!make_pool(dev, &pool)) return false;
+    pool_it = g_pool.emplace(dev, pool).first;
+  }
   const auto key = std::make_pair(dev, main);
   auto it = g_side.find(key);
+  int index;
   if (it != g_side.end()) {
-    *out = it->second;
-    return true;
+    index = it->second;
+  } else {
+    index = pool_it->second.next;
+    pool_it->second.next = (index + 1) % kSidePool;
+    g_side.emplace(key, index);
   }
-  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(main, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
-    cudaGetLastError();
-    return false;  // create nothing inside a capture: the caller runs unforked
-  }
-  SideStream s{};
-  int prio = 0;
-  if (main != nullptr && cudaStreamGetPriority(main, &prio) != cudaSuccess) prio = 0;
-  if (cudaStreamCreateWithPriority(&s.side, cudaStreamNonBlocking, prio) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
-  if (cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming) != cudaSuccess ||
-      cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
-  g_side.emplace(key, s);
-  *out = s;
+  *out = pool_it->second.entry[index];
   return true;
 }
 
