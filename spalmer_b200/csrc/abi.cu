@@ -1153,10 +1153,10 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   if ((rc = stage_pad(c, hidden, &xa)) != SPX_OK) return rc;
   // ---- side stream: work that needs only the hidden rows runs beside the
   // router, selection and dispatch.  Large batches: the MXFP8 quantisation of
-  // the rows (memory-bound, beside instruction-bound selection).  Decode-sized
-  // batches: the whole shared SwiGLU (two dense GEMVs) -- route and dispatch
-  // occupy a handful of SMs, and the shared output is needed only by the
-  // combine.
+  // the rows (joined before the experts).  Decode-sized batches: the whole
+  // shared SwiGLU (two dense GEMVs, joined before the combine) -- route and
+  // dispatch occupy a handful of SMs there; forking their 3 us quantisation as
+  // well measured no faster.
   const bool fork_mx = s.mx && !s.nv && !s.small && w->expert_lane_mxfp8 != nullptr;
   // (only while the shared projections are dense GEMVs: no tcgen05 kernel,
   // which would want the tensor memory the main stream's kernels hold)
@@ -1169,9 +1169,11 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
       return SPX_ERR_CUDA;
     const Ctx cs{s, L, workspace, ss.side, c.status, nullptr};
     if (fork_mx && (rc = stage_quantize_x(cs, hidden, 0)) != SPX_OK) return rc;
-    if (fork_shared && ((rc = stage_shared_gemm1(cs, w, xa)) != SPX_OK || (rc = stage_shared_gemm2(cs, w, so)) != SPX_OK))
-      return rc;
-    if (cudaEventRecord(ss.join, ss.side) != cudaSuccess) return SPX_ERR_CUDA;
+    if (cudaEventRecord(ss.join, ss.side) != cudaSuccess) return SPX_ERR_CUDA;  // before the experts
+    if (fork_shared) {
+      if ((rc = stage_shared_gemm1(cs, w, xa)) != SPX_OK || (rc = stage_shared_gemm2(cs, w, so)) != SPX_OK) return rc;
+      if (cudaEventRecord(ss.join2, ss.side) != cudaSuccess) return SPX_ERR_CUDA;  // before the combine
+    }
   }
   // ---- K1: router GEMM (unless logits are injected), scores, top-k, weights,
   // load-balance partials
@@ -1191,7 +1193,7 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
     if ((rc = stage_shared_gemm2(c, w, out->update, y, da.rank)) != SPX_OK) return rc;
   } else {
     if (fork_shared && forked) {
-      if (cudaStreamWaitEvent(c.st, ss.join, 0) != cudaSuccess) return SPX_ERR_CUDA;
+      if (cudaStreamWaitEvent(c.st, ss.join2, 0) != cudaSuccess) return SPX_ERR_CUDA;
       c.mark(6);
     } else if (s.S > 0) {
       if ((rc = stage_shared_gemm1(c, w, xa)) != SPX_OK) return rc;

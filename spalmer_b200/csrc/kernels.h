@@ -180,7 +180,7 @@ int ensure_max_dynamic_smem(const void* func);
 // none can be made (e.g. the first call is inside a stream capture).
 struct SideStream {
   cudaStream_t side;
-  cudaEvent_t fork, join;
+  cudaEvent_t fork, join, join2;
 };
 bool side_stream(cudaStream_t main, SideStream* out);
 

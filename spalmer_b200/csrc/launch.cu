@@ -36,7 +36,7 @@ int device_sm_count() {
   return g_sm_count[dev];
 }
 
-// Side streams: a pool of kSidePool non-blocking streams (two events each)
+// Side streams: a pool of kSidePool non-blocking streams (three events each)
 // per device, created on the first call on the device that is not being
 // captured and kept for the life of the process.  A caller stream takes the
 // next pool entry the first time it forks, which needs no creation, so a
@@ -64,7 +64,8 @@ bool make_pool(int dev, SidePool* pool) {
     // the highest priority: side work is short and sits beside the critical path
     if (cudaStreamCreateWithPriority(&s.side, cudaStreamNonBlocking, hi) != cudaSuccess ||
         cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming) != cudaSuccess) {
+        cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&s.join2, cudaEventDisableTiming) != cudaSuccess) {
       cudaGetLastError();
       return false;
     }
