@@ -53,7 +53,7 @@
 extern "C" {
 #endif
 
-#define SPX_ABI_VERSION 10
+#define SPX_ABI_VERSION 11
 
 #define SPX_OK 0
 #define SPX_ERR_INVALID_ARG -1
@@ -458,7 +458,11 @@ int spx_rows_to_peers(const uint16_t* src, int64_t ld_src, const int32_t* index,
  * expert weight gradients: with offsets from expert_counts,
  *   d gate_e | d up_e = x_sorted[e]^T @ dgu_sorted[e]   ([d, I] each, the up
  *                                                       half from column kI)
- *   d down_e          = h_sorted[e]^T @ dy_sorted[e]    ([I, d]).
+ *   d down_e          = h_sorted[e]^T @ dy_sorted[e]    ([I, d]),
+ * x_sorted[p] = hidden[token of p] and dy_sorted[p] = bf16(d_update[token of
+ * p] * routing weight of p).  x_sorted and dy_sorted are both given or both
+ * NULL; NULL needs the weight gradients below, whose kernels then gather
+ * those rows by token themselves (no P x d copies are written).
  * BF16 experts only (SPX_ERR_UNSUPPORTED with an MXFP8 lane); d_model must be
  * a multiple of 64.  The dispatch is recomputed from expert_ids, so the
  * forward's workspace need not survive until the backward. */
@@ -474,15 +478,16 @@ typedef struct spx_layer_grads {
   const uint16_t* d_aux;            /* device BF16 scalar dL/d aux | NULL       */
   uint16_t* d_hidden_experts;       /* [T, d]  out                              */
   uint16_t* d_logits;               /* [T, E]  out                              */
-  uint16_t* x_sorted;               /* [T*k, d]   out                           */
+  uint16_t* x_sorted;               /* [T*k, d]   out | NULL (with the wgrads)  */
   uint16_t* h_sorted;               /* [T*k, I]   out                           */
-  uint16_t* dy_sorted;              /* [T*k, d]   out                           */
+  uint16_t* dy_sorted;              /* [T*k, d]   out | NULL (with the wgrads)  */
   uint16_t* dgu_sorted;             /* [T*k, 2*kI] out, kI = round_up(I, 64)    */
   int32_t* expert_counts;           /* [E]     out                              */
   /* The routed experts' weight gradients (optional; NULL = not computed):
    * d gate | d up [E, d, I] = x_e^T [dg | du]_e and d down [E, I, d] =
    * h_e^T dy_e over each expert's sorted rows, FP32 accumulation, BF16 out
-   * (tcgen05, both operands MN-major from the sorted buffers above).  Needs
+   * (tcgen05, both operands MN-major: from the sorted buffers above, or with
+   * x_sorted = dy_sorted = NULL gathered by token inside the kernels).  Needs
    * inter_dim % 8 == 0; all three or none. */
   uint16_t* d_gate_proj;
   uint16_t* d_up_proj;

@@ -76,7 +76,7 @@ EXPORTED = (
     "spx_dispatch_static_status",
 )
 
-ABI_VERSION = 10
+ABI_VERSION = 11
 
 _vp = ctypes.c_void_p
 

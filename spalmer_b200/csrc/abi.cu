@@ -104,7 +104,11 @@ int make_shape(const spx_layer_dims* dm, Shape* s) {
     s->cm = s->nv ? ((s->I % 64 == 0) ? 64 : 32) : (s->I % 128 == 0) ? 128 : (s->I % 64 == 0) ? 64 : 32;
     s->ncm = s->I / s->cm;
     s->kh = round_up_i(s->I, 128);
-    s->bn2m = std::min(kMxDenseBn, round_up_i(s->d, 16));
+    // GEMM2 N tile.  The MXFP8 lane takes 256 columns: with K = I = 128 a tile
+    // is one K block, so its fixed costs (scale copies, accumulator hand-off,
+    // the A tile's load) weigh more than the lost accumulator overlap
+    // (expert GEMM2 stage 207.7 -> 201.9 us on the 100M shape).
+    s->bn2m = s->nv ? std::min(kMxDenseBn, round_up_i(s->d, 16)) : std::min(kMxMaxBn, round_up_i(s->d, 16));
     s->gn2m = ceil_div(s->d, s->bn2m);
   } else {
     s->kx = s->cm = s->ncm = s->kh = s->bn2m = s->gn2m = 0;
@@ -1526,20 +1530,23 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
   if (s.kd != s.d) return SPX_ERR_UNSUPPORTED;                              // d_model % 64 == 0
   if (gr->expert_ids == nullptr || gr->routing_weights == nullptr || gr->router_scores == nullptr ||
       gr->gate_proj == nullptr || gr->up_proj == nullptr || gr->down_proj == nullptr || gr->d_update == nullptr ||
-      gr->d_hidden_experts == nullptr || gr->d_logits == nullptr || gr->x_sorted == nullptr ||
-      gr->h_sorted == nullptr || gr->dy_sorted == nullptr || gr->dgu_sorted == nullptr ||
-      gr->expert_counts == nullptr)
+      gr->d_hidden_experts == nullptr || gr->d_logits == nullptr || gr->h_sorted == nullptr ||
+      gr->dgu_sorted == nullptr || gr->expert_counts == nullptr)
     return SPX_ERR_INVALID_ARG;
   const int wgrad_outs = (gr->d_gate_proj != nullptr) + (gr->d_up_proj != nullptr) + (gr->d_down_proj != nullptr);
   if (wgrad_outs != 0 && wgrad_outs != 3) return SPX_ERR_INVALID_ARG;
   const bool wgrad = wgrad_outs == 3;
+  // x_sorted / dy_sorted: both or neither; neither only with the weight
+  // gradients, which then gather their rows themselves.
+  const bool sorted_rows = gr->x_sorted != nullptr;
+  if (sorted_rows != (gr->dy_sorted != nullptr) || (!sorted_rows && !wgrad)) return SPX_ERR_INVALID_ARG;
   if (wgrad && s.I % 8 != 0) return SPX_ERR_UNSUPPORTED;
   if (wgrad && (!aligned16(gr->h_sorted) || !aligned16(gr->d_gate_proj) || !aligned16(gr->d_up_proj) ||
                 !aligned16(gr->d_down_proj)))
     return SPX_ERR_ALIGNMENT;
   if (int rc = check_layer_weights(s, dims, w, true, true, false); rc != SPX_OK) return rc;
   if (!aligned16(hidden) || !aligned16(gr->d_update) || !aligned16(workspace) || !aligned16(gr->dgu_sorted) ||
-      !aligned16(gr->x_sorted) || !aligned16(gr->dy_sorted) || !aligned16(gr->d_hidden_experts) ||
+      (sorted_rows && (!aligned16(gr->x_sorted) || !aligned16(gr->dy_sorted))) || !aligned16(gr->d_hidden_experts) ||
       !aligned16(gr->gate_proj) || !aligned16(gr->up_proj) || !aligned16(gr->down_proj))
     return SPX_ERR_ALIGNMENT;
   const Layout L = make_layout(s);
@@ -1583,6 +1590,9 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
     g.n_valid = s.nc * 2 * s.c;
     g.out = gu;
     g.ldo = s.nc * 2 * s.c;
+    g.copy_out = gr->x_sorted;  // the gathered x rows, kept in dispatch order (or not at all)
+    g.ld_copy = s.d;
+    if (g.copy_out != nullptr && (rc = encode_2d(&g.tma_copy, g.copy_out, s.P, s.d, s.d, 32)) != SPX_OK) return rc;
     if ((rc = launch_gemm(kEpiStore, g, s.max_tiles, s.nc, st)) != SPX_OK) return rc;
   }
   // ---- dh' = dU_t @ D_e^T (gathered rows of the upstream gradient)
@@ -1622,17 +1632,42 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
   }
   if ((rc = launch_combine(dxs, da.rank, nullptr, nullptr, s.T, s.d, s.k, gr->d_hidden_experts, st)) != SPX_OK)
     return rc;
-  // ---- sorted operands of the expert weight gradients
-  if ((rc = launch_bwd_gather(hidden, gr->d_update, da.src_row, da.sorted_weights, s.P, s.d, gr->x_sorted,
-                              gr->dy_sorted, st)) != SPX_OK)
+  // ---- dy_sorted = bf16(dU row * routing weight) in dispatch order, when the caller wants the sorted rows
+  if (sorted_rows &&
+      (rc = launch_bwd_scaled_rows(gr->d_update, da.src_row, da.sorted_weights, s.P, s.d, gr->dy_sorted, st)) !=
+          SPX_OK)
     return rc;
-  // ---- the experts' weight gradients over the sorted rows (tcgen05, MN-major operands)
+  // ---- the experts' weight gradients over the sorted rows (tcgen05, MN-major
+  // operands); without sorted copies the x rows and the bf16(dU * w) rows are
+  // gathered by token inside the kernels
   if (wgrad) {
-    if ((rc = launch_wgrad(gr->x_sorted, s.d, s.d, gr->dgu_sorted, 2 * ki, 2 * ki, s.P, gr->expert_counts, s.E,
-                           gr->d_gate_proj, s.I, s.I, gr->d_up_proj, s.I, ki, s.I, c.status, st)) != SPX_OK)
+    WgradOperand xo{}, dguo{}, ho{}, dyo{};
+    xo.ld = xo.total = s.d;
+    if (sorted_rows) {
+      xo.rows = gr->x_sorted;
+    } else {
+      xo.src = hidden;
+      xo.index = da.src_row;
+      xo.src_rows = s.T;
+    }
+    dguo.rows = gr->dgu_sorted;
+    dguo.ld = dguo.total = 2 * ki;
+    if ((rc = launch_wgrad(xo, dguo, s.P, gr->expert_counts, s.E, gr->d_gate_proj, s.I, s.I, gr->d_up_proj, s.I, ki,
+                           s.I, c.status, st)) != SPX_OK)
       return rc;
-    if ((rc = launch_wgrad(gr->h_sorted, s.I, s.I, gr->dy_sorted, s.d, s.d, s.P, gr->expert_counts, s.E,
-                           gr->d_down_proj, s.d, s.d, nullptr, 0, 0, 0, c.status, st)) != SPX_OK)
+    ho.rows = gr->h_sorted;
+    ho.ld = ho.total = s.I;
+    dyo.ld = dyo.total = s.d;
+    if (sorted_rows) {
+      dyo.rows = gr->dy_sorted;
+    } else {
+      dyo.src = gr->d_update;
+      dyo.index = da.src_row;
+      dyo.src_rows = s.T;
+      dyo.scale = da.sorted_weights;
+    }
+    if ((rc = launch_wgrad(ho, dyo, s.P, gr->expert_counts, s.E, gr->d_down_proj, s.d, s.d, nullptr, 0, 0, 0,
+                           c.status, st)) != SPX_OK)
       return rc;
   }
   // ---- router: selection and load-balance softmaxes, softplus

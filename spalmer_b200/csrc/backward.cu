@@ -51,12 +51,12 @@ int grid_for(int64_t items, int per_block) {
 
 }  // namespace
 
-// Sorted-order rows for the weight gradients: x_sorted[p] = x[t_p] and
-// dy_sorted[p] = bf16(dU[t_p] * w_p) (the reference's d(outputs) of the
-// weighted update, bank.py:978).  8 columns per thread.
-__global__ void bwd_gather_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ du,
-                                  const int* __restrict__ src_row, const uint16_t* __restrict__ sorted_w, int64_t P,
-                                  int d, uint16_t* __restrict__ x_sorted, uint16_t* __restrict__ dy_sorted) {
+// The weighted upstream gradient in dispatch order for the down projection's
+// weight gradient: dy_sorted[p] = bf16(dU[t_p] * w_p) (the reference's
+// d(outputs) of the weighted update, bank.py:978).  8 columns per thread.
+__global__ void bwd_scaled_rows_kernel(const uint16_t* __restrict__ du, const int* __restrict__ src_row,
+                                       const uint16_t* __restrict__ sorted_w, int64_t P, int d,
+                                       uint16_t* __restrict__ dy_sorted) {
   const int vec = d / 8;
   const int64_t total = P * vec;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
@@ -65,9 +65,7 @@ __global__ void bwd_gather_kernel(const uint16_t* __restrict__ x, const uint16_t
     const int c = static_cast<int>(idx - p * vec) * 8;
     const int64_t t = __ldg(src_row + p);
     const float w = bf16_to_f32(__ldg(sorted_w + p));
-    const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + t * d + c));
     const uint4 dv = __ldg(reinterpret_cast<const uint4*>(du + t * d + c));
-    *reinterpret_cast<uint4*>(x_sorted + p * d + c) = xv;
     const uint32_t in[4] = {dv.x, dv.y, dv.z, dv.w};
     uint32_t o[4];
 #pragma unroll
@@ -286,14 +284,6 @@ __global__ void bwd_router_kernel(const BwdRouterArgs a) {
   }
 }
 
-int launch_bwd_gather(const uint16_t* x, const uint16_t* du, const int* src_row, const uint16_t* sorted_w, int64_t P,
-                      int d, uint16_t* x_sorted, uint16_t* dy_sorted, cudaStream_t stream) {
-  if (d % 8 != 0) return SPX_ERR_UNSUPPORTED;
-  bwd_gather_kernel<<<grid_for(P * (d / 8), 256), 256, 0, stream>>>(x, du, src_row, sorted_w, P, d, x_sorted,
-                                                                    dy_sorted);
-  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
-}
-
 int launch_bwd_swiglu(const uint16_t* gu, int ld_gu, int c, const uint16_t* dhp, int ld_dhp,
                       const uint16_t* sorted_w, const int* order, int64_t P, int I, int kI, uint16_t* h_sorted,
                       uint16_t* dgu, float* dw_pair, cudaStream_t stream) {
@@ -323,6 +313,14 @@ int launch_bwd_router(const BwdRouterArgs& a, cudaStream_t stream) {
     bwd_router_kernel<8><<<grid, 256, 0, stream>>>(a);
   else
     bwd_router_kernel<32><<<grid, 256, 0, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
+}
+
+int launch_bwd_scaled_rows(const uint16_t* du, const int* src_row, const uint16_t* sorted_w, int64_t P, int d,
+                           uint16_t* dy_sorted, cudaStream_t stream) {
+  if (d % 8 != 0) return SPX_ERR_UNSUPPORTED;
+  if (P <= 0) return SPX_OK;
+  bwd_scaled_rows_kernel<<<grid_for(P * (d / 8), 256), 256, 0, stream>>>(du, src_row, sorted_w, P, d, dy_sorted);
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 

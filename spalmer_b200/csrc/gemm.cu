@@ -69,6 +69,16 @@ __device__ __forceinline__ void bfr2(float& x, float& y) {
   x = lo_f(p);
   y = hi_f(p);
 }
+// Product of two BF16 pairs, rounded to nearest even in one instruction.  The
+// FP32 product of two BF16 values is exact (8 x 8 significant bits) above the
+// FP32 normal range's floor, so this is pack_bf16x2(lo_f(a) * lo_f(b), ...)
+// bit for bit -- the reference's BF16 tensor multiply -- for every operand
+// pair whose product is at least 2^-126 in magnitude (or zero, inf, NaN).
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 // silu(x) = x / (1 + e^-x); approximate exp/divide, the result is rounded to BF16.
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
@@ -134,10 +144,8 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, uint32_t taddr, 
           u1 *= alpha1;
         }
         bfr2(g0, g1);
-        bfr2(u0, u1);
-        float sg0 = silu_fast(g0), sg1 = silu_fast(g1);
-        bfr2(sg0, sg1);
-        hw[j / 2] = pack_bf16x2(sg0 * u0, sg1 * u1);
+        const uint32_t u2 = pack_bf16x2(u0, u1);
+        hw[j / 2] = bmul2(pack_bf16x2(silu_fast(g0), silu_fast(g1)), u2);
         if constexpr (SC) {
           if (live && j < w) hmax = fmaxf(hmax, fabsf(lo_f(hw[j / 2])));
           if (live && j + 1 < w) hmax = fmaxf(hmax, fabsf(hi_f(hw[j / 2])));
@@ -214,6 +222,7 @@ __device__ __forceinline__ void run_epilogue_rows(const GemmArgs& a, uint32_t ta
   const int wrows = rows - quad * 32;  // valid rows of this quadrant
   if (wrows <= 0) return;
   uint16_t* out = static_cast<uint16_t*>(a.out);
+  const uint32_t w2 = pack_bf16x2(my_w, my_w);  // my_w is a BF16 routing weight (or 1)
   for (int s0 = half * 64; s0 < a.bn; s0 += 128) {
     uint8_t* buf = stage + (slices & 1u) * kStageBytesPerWarp;
     ++slices;
@@ -232,11 +241,8 @@ __device__ __forceinline__ void run_epilogue_rows(const GemmArgs& a, uint32_t ta
     tmem_wait_ld();
     uint32_t hw[32];
 #pragma unroll
-    for (int j = 0; j < 64; j += 2) {
-      float f0 = __uint_as_float(v[j]) * alpha, f1 = __uint_as_float(v[j + 1]) * alpha;
-      bfr2(f0, f1);
-      hw[j / 2] = pack_bf16x2(f0 * my_w, f1 * my_w);
-    }
+    for (int j = 0; j < 64; j += 2)
+      hw[j / 2] = bmul2(pack_bf16x2(__uint_as_float(v[j]) * alpha, __uint_as_float(v[j + 1]) * alpha), w2);
 #pragma unroll
     for (int c = 0; c < 64; c += 16) stage_put16(buf, lane, c, &hw[c / 2]);
     const int gcol0 = n0 + s0;
@@ -438,11 +444,9 @@ __device__ __forceinline__ void run_epilogue_swiglu_mx(const GemmArgs& a, uint32
     float h[32];
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
-      float sg0 = silu_fast(lo_f(gp[j][c])), sg1 = silu_fast(hi_f(gp[j][c]));
-      bfr2(sg0, sg1);
-      h[2 * c] = sg0 * lo_f(up[j][c]);
-      h[2 * c + 1] = sg1 * hi_f(up[j][c]);
-      bfr2(h[2 * c], h[2 * c + 1]);
+      const uint32_t hp = bmul2(pack_bf16x2(silu_fast(lo_f(gp[j][c])), silu_fast(hi_f(gp[j][c]))), up[j][c]);
+      h[2 * c] = lo_f(hp);
+      h[2 * c + 1] = hi_f(hp);
     }
     uint32_t q[8];
     const uint32_t sb = mx_quantize32(h, q);
@@ -460,6 +464,78 @@ __device__ __forceinline__ void run_epilogue_swiglu_mx(const GemmArgs& a, uint32
     for (int col = c0; col < a.h_cols; col += 16)
       *reinterpret_cast<uint4*>(hq + row * a.ldo + col) = make_uint4(0u, 0u, 0u, 0u);
     for (int b = c0 / kMxBlock; b < a.h_cols / kMxBlock; ++b) a.out_sf[row * a.ld_out_sf + b] = 0;
+  }
+}
+
+// BF16 expert / shared GEMM1 epilogue (kEpiSwiglu, BF16 lane):
+//   hidden = bf16(bf16(silu(bf16(gate))) * bf16(up))
+// The warp reads both of its 32-column slices of gate and up from TMEM,
+// rounding them to BF16 at once (the reference's tensor boundary, two values
+// per register), and releases the accumulator before any arithmetic, so the
+// next tile's MMAs need not wait for the SwiGLU.  Each slice of hidden rows
+// (in tile order) then goes through the warp's 4 KB staging buffer: threads
+// write their own row, and each store instruction moves 8 rows x 64 B.
+// Needs chunk % 8 == 0 and ldo % 8 == 0 (16-byte aligned row segments).
+__device__ __forceinline__ void run_epilogue_swiglu_bf16(const GemmArgs& a, uint32_t taddr, uint8_t* stage,
+                                                         int quad, int half, int lane, int row0, int rows, int nt,
+                                                         uint64_t* release) {
+  const int r = quad * 32 + lane;
+  const bool live = r < rows;
+  uint16_t* out = static_cast<uint16_t*>(a.out);
+  const int64_t row = static_cast<int64_t>(row0) + r;
+  if (rows - quad * 32 <= 0) {  // nothing of this quadrant is stored: release at once
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(release);
+    return;
+  }
+  uint32_t gp[2][16], up[2][16];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int s0 = half * 32 + 64 * j;
+    if (s0 < a.chunk) {
+      uint32_t g[32], u[32];
+      tmem_ld32(taddr + s0, g);
+      tmem_ld32(taddr + a.chunk + s0, u);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        gp[j][c] = pack_bf16x2(__uint_as_float(g[2 * c]), __uint_as_float(g[2 * c + 1]));
+        up[j][c] = pack_bf16x2(__uint_as_float(u[2 * c]), __uint_as_float(u[2 * c + 1]));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(release);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int s0 = half * 32 + 64 * j;
+    if (s0 >= a.chunk) break;
+    uint32_t hw[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      hw[c] = bmul2(pack_bf16x2(silu_fast(lo_f(gp[j][c])), silu_fast(hi_f(gp[j][c]))), up[j][c]);
+    __syncwarp();  // the previous slice's reads of the buffer are done
+    stage_put16(stage, lane, 0, &hw[0]);
+    stage_put16(stage, lane, 16, &hw[8]);
+    __syncwarp();
+    const int nchunk = min(32, a.chunk - s0) >> 3;  // 16-byte chunks per row (the width is a multiple of 8)
+    const int wrows = rows - quad * 32;
+    const int q = lane & 3;
+    uint16_t* col = out + nt * a.chunk + s0 + q * 8;
+#pragma unroll
+    for (int step = 0; step < 4; ++step) {
+      const int ri = step * 8 + (lane >> 2);
+      if (ri < wrows && q < nchunk)
+        *reinterpret_cast<uint4*>(col + static_cast<int64_t>(row0 + quad * 32 + ri) * a.ldo) =
+            *reinterpret_cast<const uint4*>(stage + stage_off(ri, q));
+    }
+  }
+  // Zero the K padding of the hidden matrix (columns [chunks*c, h_cols)).
+  if (half == 0 && live && nt == a.n_tiles - 1) {
+    uint16_t* dst = out + row * a.ldo;
+    for (int col = a.n_tiles * a.chunk; col < a.h_cols; ++col) dst[col] = 0;
   }
 }
 
@@ -610,6 +686,12 @@ __device__ __forceinline__ void produce_cp_async(const GemmArgs& a, uint8_t* sa,
 // MXFP8 kEpiSwiglu; the NVFP4 GEMM1 reads A by TMA) carry the extra producer
 // warps; the others keep 10 warps (and their registers).  Only the lead
 // producer copies scale factors.
+// 4 KB epilogue staging buffers per epilogue warp (the MXFP8 SwiGLU epilogue
+// stores from registers).
+constexpr int gemm_stage_bufs(int epi, bool mx, bool nv) {
+  return (epi == kEpiScatter || epi == kEpiCombine) ? 2 : (mx && !nv && epi == kEpiSwiglu) ? 0 : 1;
+}
+
 template <int EPI, bool MX, bool NV>
 constexpr int gemm_threads() {
   return ((!MX && (EPI == kEpiStore || EPI == kEpiSwiglu)) || (MX && !NV && EPI == kEpiSwiglu)) ? kGemmKernelThreads
@@ -628,8 +710,9 @@ __global__ void __launch_bounds__(gemm_threads<EPI, MX, NV>(), 1) gemm_kernel(co
   uint8_t* sa = smem;
   uint8_t* sb = smem + S * a_bytes;
   uint8_t* ssf = sb + S * b_bytes;                           // MX: [S][SFA atom | SFB atom]
-  // Epilogue staging: one 4 KB buffer per epilogue warp, two for the TMA-store epilogue.
-  constexpr int kStageBufs = (EPI == kEpiScatter || EPI == kEpiCombine) ? 2 : 1;
+  // Epilogue staging: one 4 KB buffer per epilogue warp, two for the TMA-store
+  // epilogue, none for the MXFP8 SwiGLU epilogue.
+  constexpr int kStageBufs = gemm_stage_bufs(EPI, MX, NV);
   // 1024-byte aligned: the TMA store reads the buffers with the 128B swizzle.
   uint8_t* stage_all = align_1024(ssf + (MX ? S * kSfStage : 0u));
   uint64_t* full = reinterpret_cast<uint64_t*>(stage_all + kGemmEpilogueWarps * kStageBufs * kStageBytesPerWarp);
@@ -650,11 +733,12 @@ __global__ void __launch_bounds__(gemm_threads<EPI, MX, NV>(), 1) gemm_kernel(co
   if (static_cast<int>(blockIdx.x) >= total) return;
   const bool ldst_producer = MX || a.gather != 0;
   const bool gather_producers = gemm_threads<EPI, MX, NV>() == kGemmKernelThreads && a.gather != 0;
+  const bool copier = !MX && gather_producers && a.copy_out != nullptr;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], ldst_producer ? 1 + kCpAsyncArrivals * (gather_producers ? kGemmGatherProducers : 1) : 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], copier ? 2 : 1);  // MMA commit (+ copier)
     }
     for (int b = 0; b < kMaxAccBufs; ++b) {
       mbar_init(&tfull[b], 1);
@@ -676,7 +760,53 @@ __global__ void __launch_bounds__(gemm_threads<EPI, MX, NV>(), 1) gemm_kernel(co
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= kGemmExtraProducerWarp0) {
+  if (warp == kGemmCopierWarp) {
+    // ---------------- copier: every gathered A stage (128 rows x 64 columns)
+    // to copy_out in tile-row order -- whole 32-row groups by TMA stores
+    // straight from the staged (swizzled) rows, the rows of a last partial
+    // group by plain copies -- then it releases the stage together with the
+    // MMA once the stores have read it.  Only N tile 0 copies.
+    if (copier) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+        int group, row0, rows, nt;
+        if (!decode_tile(a, t, group, row0, rows, nt)) break;
+        const int groups32 = rows >> 5;  // whole 32-row groups
+        for (int kb = 0; kb < a.k_blocks; ++kb, ++it) {
+          const int s = static_cast<int>(it % S);
+          const uint32_t ph = (it / S) & 1u;
+          int go = 1;
+          if (lane == 0) go = mbar_wait(&full[s], ph, a.status, SPX_DEV_TIMEOUT_PRODUCER) ? 1 : 0;
+          go = __shfl_sync(0xFFFFFFFFu, go, 0);
+          if (!go) {
+            ok = false;
+            break;
+          }
+          if (nt == 0) {
+            const uint8_t* st = sa + s * a_bytes;
+            if (lane == 0 && groups32 > 0) {
+              fence_proxy_async_smem();  // the staged rows (cp.async) -> the bulk stores' reads
+              for (int q = 0; q < groups32; ++q) tma_store_2d(&a.tma_copy, st + q * 4096, kb * 64, row0 + 32 * q);
+              bulk_commit();
+            }
+            const int r = 32 * groups32 + lane;
+            if (r < rows) {
+#pragma unroll
+              for (int c = 0; c < 8; ++c)
+                *reinterpret_cast<uint4*>(a.copy_out + static_cast<int64_t>(row0 + r) * a.ld_copy + kb * 64 + c * 8) =
+                    *reinterpret_cast<const uint4*>(st + r * 128 + ((c ^ (r & 7)) << 4));
+            }
+            if (lane == 0 && groups32 > 0) bulk_wait_read<0>();  // the stores are done reading the stage
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
+        }
+      }
+      if (lane == 0) bulk_wait_all();  // stores complete before the CTA goes away
+      __syncwarp();
+    }
+  } else if (warp >= kGemmExtraProducerWarp0) {
     if (gather_producers) {
       const int part = 2 + warp - kGemmExtraProducerWarp0;
       if (part == 2) produce_cp_async<MX, NV, 2>(a, sa, sb, ssf, full, empty, S, a_bytes, b_bytes, total, lane);
@@ -835,6 +965,8 @@ __global__ void __launch_bounds__(gemm_threads<EPI, MX, NV>(), 1) gemm_kernel(co
         if (lane == 0) mbar_arrive(&tempty[b]);
       } else if constexpr (EPI == kEpiCombine) {
         run_epilogue_combine(a, taddr, my_stage, quad, half, lane, rows, nt * bn, my_row, &tempty[b]);  // releases early
+      } else if constexpr (EPI == kEpiSwiglu) {
+        run_epilogue_swiglu_bf16(a, taddr, my_stage, quad, half, lane, row0, rows, nt, &tempty[b]);  // releases early
       } else {
         if constexpr (EPI == kEpiScatter)
           run_epilogue_rows(a, taddr, my_stage, quad, half, lane, row0, rows, nt * bn, my_w, slices, committed);
@@ -1009,11 +1141,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       if (!go) break;
       tc_fence_after();
       const uint32_t taddr = tmem + b * a.tmem_cols + (static_cast<uint32_t>(quad * 32) << 16);
-      const long long my_row = static_cast<long long>(row0) + quad * 32 + lane;
-      run_epilogue<EPI>(a, taddr, my_stage, quad, half, lane, row0, rows, nt * bn, nt, my_row);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[b]);
+      if constexpr (EPI == kEpiSwiglu) {
+        run_epilogue_swiglu_bf16(a, taddr, my_stage, quad, half, lane, row0, rows, nt, &tempty[b]);  // releases early
+      } else {
+        const long long my_row = static_cast<long long>(row0) + quad * 32 + lane;
+        run_epilogue<EPI>(a, taddr, my_stage, quad, half, lane, row0, rows, nt * bn, nt, my_row);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[b]);
+      }
     }
   }
   tc_fence_before();
@@ -1083,8 +1219,7 @@ int encode_3d(CUtensorMap* map, const void* base, int64_t groups, int64_t rows, 
 size_t gemm_smem_bytes(int bn, int stages, bool mx, int epi, bool nv) {
   const size_t per_stage =
       kTileRows * 128 + static_cast<size_t>(bn) * 128 + (mx ? (nv ? kNvStageSfBytes : kMxStageSfBytes) : 0);
-  const size_t staging =
-      static_cast<size_t>(kGemmEpilogueWarps) * kStageBytesPerWarp * (epi == kEpiScatter || epi == kEpiCombine ? 2 : 1);
+  const size_t staging = static_cast<size_t>(kGemmEpilogueWarps) * kStageBytesPerWarp * gemm_stage_bufs(epi, mx, nv);
   return 2048 + static_cast<size_t>(stages) * per_stage + staging + (2 * stages + 2 * kMaxAccBufs) * 8 + 16;
 }
 

@@ -17,7 +17,8 @@ constexpr int kGemmThreads = 320;      // 10 warps: TMA, MMA, 8 x epilogue (2 pe
 // 10.. each gather an equal share of a tile's rows); idle otherwise.
 constexpr int kGemmGatherProducers = 2;
 constexpr int kGemmExtraProducerWarp0 = 10;
-constexpr int kGemmKernelThreads = 32 * (10 + kGemmGatherProducers - 1);
+constexpr int kGemmCopierWarp = 10 + kGemmGatherProducers - 1;  // copies gathered A stages out (copy_out)
+constexpr int kGemmKernelThreads = 32 * (kGemmCopierWarp + 1);
 constexpr int kGemmEpilogueWarps = 8;
 constexpr int kMaxAccBufs = 4;         // TMEM accumulator buffers per CTA (as many as fit in 512 columns)
 constexpr size_t kGemmSmemBudget = 227 * 1024;  // sm_100 opt-in maximum per CTA
@@ -128,6 +129,13 @@ struct GemmArgs {
   const uint8_t* a_base;     // gather: A rows (row stride lda bytes)
   int64_t lda;
   const uint8_t* const* a_rows;  // gather: or one pointer per source row (rows of kd BF16), when not null
+  // gather (BF16): a copy of the gathered A rows in tile order, copy_out[p] =
+  // A row of tile row p, written by the copier warp from the staged stages
+  // (tma_copy: copy_out as [rows, kd] BF16, box {64, 32}, 128B swizzle).
+  // null = no copy.
+  uint16_t* copy_out;
+  int64_t ld_copy;
+  CUtensorMap tma_copy;
   // MXFP8 lane (block-scaled kernel only)
   const uint8_t* sfa;        // A scale bytes [A rows, ld_sfa] row-major (row = gathered source row)
   int64_t ld_sfa;            // bytes per row, multiple of 4
@@ -406,21 +414,41 @@ int launch_gemv_rows(GemvPass a, cudaStream_t stream);
 // expert's rows of A [rows, m_total] and B [rows, n_total] (dispatch order,
 // counts[e] rows per expert); output columns [0, n_valid0) of B land in out0
 // [E, m_total, ld0], columns [n_start1, n_start1 + n_valid1) in out1.
+// One operand of the weight-gradient GEMM, P rows in dispatch order: either
+// stored (`rows`, row p at rows + p * ld) or gathered (row p is src[index[p]],
+// and with `scale` bf16(src[index[p]] * scale[p]), the product rounded once).
+struct WgradOperand {
+  const uint16_t* rows;   // [P, ld] sorted rows, or null when gathered
+  const uint16_t* src;    // gathered: [*, ld] source rows
+  const int* index;       // gathered: index[p] = source row of sorted row p (< src_rows)
+  const uint16_t* scale;  // gathered, optional: BF16 factor of sorted row p
+  int64_t src_rows;       // gathered: rows of src
+  int64_t ld;
+  int total;              // columns
+};
 struct WgradArgs {
-  CUtensorMap tma_a, tma_b;  // boxes of 64 rows x 64 columns, 128B swizzle
+  CUtensorMap tma_a, tma_b;  // 128B swizzle; boxes of 64 rows x 64 columns (stored), 1 x 64 (gathered)
   const int* counts;
-  int E, m_total, bn, m_tiles, n_tiles, stages;
+  int E, m_total, n_total, bn, m_tiles, n_tiles, stages;
   uint16_t* out0;
   int ld0, n_valid0;
   uint16_t* out1;
   int ld1, n_start1, n_valid1;
+  // The gathered operand (at most one): A when g_is_a, else B; g_src null = none.
+  const uint16_t* g_src;
+  const int* g_index;
+  const uint16_t* g_scale;
+  int64_t g_ld;
+  int g_is_a;
   int* status;
 };
-int launch_wgrad(const uint16_t* a_rows, int64_t ld_a, int m_total, const uint16_t* b_rows, int64_t ld_b,
-                 int n_total, int64_t rows, const int* counts, int E, uint16_t* out0, int ld0, int n_valid0,
-                 uint16_t* out1, int ld1, int n_start1, int n_valid1, int* status, cudaStream_t stream);
+int launch_wgrad(const WgradOperand& a, const WgradOperand& b, int64_t rows, const int* counts, int E,
+                 uint16_t* out0, int ld0, int n_valid0, uint16_t* out1, int ld1, int n_start1, int n_valid1,
+                 int* status, cudaStream_t stream);
 
 // Backward (backward.cu).
+int launch_bwd_scaled_rows(const uint16_t* du, const int* src_row, const uint16_t* sorted_w, int64_t P, int d,
+                           uint16_t* dy_sorted, cudaStream_t stream);
 struct BwdRouterArgs {
   const uint16_t* scores;     // [T, E] router scores (BF16)
   const uint16_t* logits;     // [T, E] router logits, or null (identity score transform)
@@ -436,8 +464,6 @@ struct BwdRouterArgs {
   int num_experts;
   int top_k;
 };
-int launch_bwd_gather(const uint16_t* x, const uint16_t* du, const int* src_row, const uint16_t* sorted_w, int64_t P,
-                      int d, uint16_t* x_sorted, uint16_t* dy_sorted, cudaStream_t stream);
 int launch_bwd_swiglu(const uint16_t* gu, int ld_gu, int c, const uint16_t* dhp, int ld_dhp,
                       const uint16_t* sorted_w, const int* order, int64_t P, int I, int kI, uint16_t* h_sorted,
                       uint16_t* dgu, float* dw_pair, cudaStream_t stream);

@@ -13,15 +13,24 @@
 // canonical MN-major layout (LBO = 8 KB between 64-column boxes, SBO = 1 KB
 // between 8-row groups along K); nothing is transposed in memory.
 //
+// One operand may instead be gathered from unsorted rows: x rows by token for
+// d gate | d up, and bf16(dU[token] * routing weight) rows for d down, so the
+// sorted copies (two P x d matrices) are never written.  The producer loads
+// a gathered operand with TMA gathers (four rows of 64 columns per
+// instruction, the 128-byte swizzle of the box layout the MMA expects); the
+// row scale, when there is one, is applied in shared memory by the fixer
+// warps before the MMA reads the stage.
+//
 // A CTA (persistent, one per SM) walks tiles (expert, 128 output rows, bn
 // output columns) expert-major, so the tiles of one expert run side by side
 // and share its rows through L2.  Warp roles: 0 TMA producer, 1 MMA issuer
-// (and TMEM owner), 2 tail fixer -- an expert's last K block holds rows of
-// the next expert (or TMA zero fill past the end); the fixer zeroes the rows
-// past the segment in shared memory before the MMA reads them --, 4-7
-// epilogue (TMEM lane quadrants 0-3).  Two accumulators of bn columns let the
-// epilogue of one tile overlap the MMAs of the next.  Experts without rows
-// get zero gradients.  Every wait is bounded (status word, then return).
+// (and TMEM owner), 2-3 fixers -- an expert's last K block holds rows of the
+// next expert (or TMA zero fill past the end); the fixers zero the rows past
+// the segment in shared memory, scale a gathered operand's rows, and pass the
+// stage on --, 4-7 epilogue (TMEM lane quadrants 0-3).  Two accumulators of
+// bn columns let the epilogue of one tile overlap the MMAs of the next.
+// Experts without rows get zero gradients.  Every wait is bounded (status
+// word, then return).
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -38,6 +47,21 @@ namespace {
 constexpr int kWgThreads = 256;
 constexpr int kWgBoxBytes = 64 * 128;  // one TMA box: 64 rows x 64 BF16 columns
 constexpr int kWgMaxExperts = 1024;
+constexpr int kWgFixers = 2;           // warps 2 and 3
+
+// Byte offset of 16-byte chunk c (8 columns) of row r in a run of 64-column
+// boxes with the 128-byte swizzle (chunk position c ^ (r & 7) within the row).
+__device__ __forceinline__ uint32_t wg_chunk_off(int r, int c) {
+  return static_cast<uint32_t>((c >> 3) * kWgBoxBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+// BF16 pair product, rounded once (the FP32 product of two BF16 values is
+// exact above the FP32 normal floor, so this is bf16(a * b) of each half).
+__device__ __forceinline__ uint32_t wg_bmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 
 // Shared-memory descriptor of an MN-major operand tile made of 64-column
 // boxes (128-byte rows, 128B swizzle) laid out one after another.
@@ -75,6 +99,9 @@ __global__ void __launch_bounds__(kWgThreads, 1) wgrad_kernel(const __grid_const
   const uint32_t a_bytes = 2 * kWgBoxBytes;
   const uint32_t b_bytes = static_cast<uint32_t>(nbox_b) * kWgBoxBytes;
   const uint32_t stage_bytes = a_bytes + b_bytes;
+  const bool gathered = a.g_src != nullptr;
+  // TMA bytes per stage (the stored operands)
+  const uint32_t tma_bytes = (gathered && a.g_is_a ? 0u : a_bytes) + (gathered && !a.g_is_a ? 0u : b_bytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
   uint64_t* ready = full + S;   // the fixer has passed the stage on
   uint64_t* empty = ready + S;
@@ -108,7 +135,7 @@ __global__ void __launch_bounds__(kWgThreads, 1) wgrad_kernel(const __grid_const
     if (threadIdx.x == 0) {
       for (int s = 0; s < S; ++s) {
         mbar_init(&full[s], 1);
-        mbar_init(&ready[s], 1);
+        mbar_init(&ready[s], kWgFixers);
         mbar_init(&empty[s], 1);
       }
       for (int b = 0; b < 2; ++b) {
@@ -145,27 +172,58 @@ __global__ void __launch_bounds__(kWgThreads, 1) wgrad_kernel(const __grid_const
   auto kblocks = [&](int e) { return (s_count[e] + 63) / 64; };
 
   if (warp == 0) {
-    // ---------------- TMA producer
-    if (lane == 0) {
-      uint32_t it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
-        const WgTile w = wg_tile(a, t);
-        const int nkb = kblocks(w.e);
-        for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int s = static_cast<int>(it % S);
-          const uint32_t ph = (it / S) & 1u;
-          if (!mbar_wait(&empty[s], ph ^ 1u, a.status, SPX_DEV_TIMEOUT_PRODUCER)) {
-            ok = false;
-            break;
+    // ---------------- producer (TMA): stored operands as 64 x 64 boxes, a
+    // gathered one four rows at a time (tile::gather4; lane l of 0..15 takes
+    // block rows 4l .. 4l + 3 of every box).  Rows past the expert's segment
+    // are loaded from the block's first row and zeroed by the fixers.
+    const int gboxes = gathered ? (a.g_is_a ? 2 : nbox_b) : 0;
+    const uint32_t g_bytes = static_cast<uint32_t>(gboxes) * kWgBoxBytes;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+      const WgTile w = wg_tile(a, t);
+      const int nkb = kblocks(w.e);
+      const int start = s_start[w.e], cnt = s_count[w.e];
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = static_cast<int>(it % S);
+        const uint32_t ph = (it / S) & 1u;
+        const int row = start + kb * 64;
+        const int valid = cnt - kb * 64;  // rows of this block inside the segment (> 0)
+        int src[4] = {0, 0, 0, 0};
+        if (gathered && lane < 16) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int rr = 4 * lane + q;
+            src[q] = __ldg(a.g_index + row + (rr < valid ? rr : 0));
           }
-          mbar_arrive_expect_tx(&full[s], stage_bytes);
-          uint8_t* st = smem + s * stage_bytes;
-          const int row = s_start[w.e] + kb * 64;
-          tma_load_2d(st, &a.tma_a, &full[s], w.mt * 128, row);
-          tma_load_2d(st + kWgBoxBytes, &a.tma_a, &full[s], w.mt * 128 + 64, row);
-          for (int j = 0; j < nbox_b; ++j)
-            tma_load_2d(st + a_bytes + j * kWgBoxBytes, &a.tma_b, &full[s], w.nt * a.bn + 64 * j, row);
+        }
+        int go = 1;
+        if (lane == 0) {
+          go = mbar_wait(&empty[s], ph ^ 1u, a.status, SPX_DEV_TIMEOUT_PRODUCER) ? 1 : 0;
+          if (go) {
+            mbar_arrive_expect_tx(&full[s], tma_bytes + g_bytes);
+            uint8_t* st = smem + s * stage_bytes;
+            if (!gathered || !a.g_is_a) {
+              tma_load_2d(st, &a.tma_a, &full[s], w.mt * 128, row);
+              tma_load_2d(st + kWgBoxBytes, &a.tma_a, &full[s], w.mt * 128 + 64, row);
+            }
+            if (!gathered || a.g_is_a) {
+              for (int j = 0; j < nbox_b; ++j)
+                tma_load_2d(st + a_bytes + j * kWgBoxBytes, &a.tma_b, &full[s], w.nt * a.bn + 64 * j, row);
+            }
+          }
+        }
+        go = __shfl_sync(0xFFFFFFFFu, go, 0);
+        if (!go) {
+          ok = false;
+          break;
+        }
+        if (gathered && lane < 16) {  // after lane 0's expect_tx (the shuffle above orders them)
+          const uint32_t base = smem_u32(smem + s * stage_bytes) + (a.g_is_a ? 0u : a_bytes) + lane * 512u;
+          const CUtensorMap* map = a.g_is_a ? &a.tma_a : &a.tma_b;
+          const int col0 = a.g_is_a ? w.mt * 128 : w.nt * a.bn;
+          for (int j = 0; j < gboxes; ++j)
+            tma_gather4_2d(base + j * kWgBoxBytes, map, &full[s], col0 + 64 * j, src[0], src[1], src[2], src[3]);
         }
       }
     }
@@ -205,19 +263,32 @@ __global__ void __launch_bounds__(kWgThreads, 1) wgrad_kernel(const __grid_const
       }
       mma_commit(drained);  // arrives once everything issued above has completed
     }
-  } else if (warp == 2) {
-    // ---------------- fixer: a pipeline stage between the TMA and the MMA.  It
-    // passes every stage on in order (so no barrier phase can be skipped or
-    // overtaken) and first zeroes the rows past the expert's segment in the
-    // segment's last block.
+  } else if (warp == 2 || warp == 3) {
+    // ---------------- fixers: a pipeline stage between the loads and the MMA.
+    // They pass every stage on in order (so no barrier phase can be skipped or
+    // overtaken); first they zero the rows past the expert's segment in the
+    // segment's last block, and scale a gathered operand's rows (fixer f takes
+    // rows 32f .. 32f + 31: one row per lane).
+    const int f = warp - 2;
+    const bool scaled = gathered && a.g_scale != nullptr;
+    const int gchunks = gathered ? 8 * (a.g_is_a ? 2 : nbox_b) : 0;  // 16-byte chunks per gathered row
+    const uint32_t g_base_off = a.g_is_a ? 0u : a_bytes;
     uint32_t it = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
       const WgTile w = wg_tile(a, t);
       const int cnt = s_count[w.e];
+      const int start = s_start[w.e];
       const int nkb = kblocks(w.e);
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = static_cast<int>(it % S);
+        const int valid = cnt - kb * 64;
+        const int r = 32 * f + lane;
+        uint32_t w2 = 0;
+        if (scaled && r < valid) {
+          const uint32_t wb = __ldg(a.g_scale + start + kb * 64 + r);
+          w2 = wb | (wb << 16);
+        }
         int go = 1;
         if (lane == 0) go = mbar_wait(&full[s], (it / S) & 1u, a.status, SPX_DEV_TIMEOUT_PRODUCER) ? 1 : 0;
         go = __shfl_sync(0xFFFFFFFFu, go, 0);
@@ -225,18 +296,35 @@ __global__ void __launch_bounds__(kWgThreads, 1) wgrad_kernel(const __grid_const
           ok = false;
           break;
         }
-        const int valid = cnt - kb * 64;
+        uint8_t* st = smem + s * stage_bytes;
+        bool wrote = false;
         if (valid < 64) {
           // rows [valid, 64) of every box: whole 128-byte rows (the swizzle stays inside a row)
-          uint8_t* st = smem + s * stage_bytes;
           const int nbox = 2 + nbox_b;
           const int chunks = (64 - valid) * 8;  // 16-byte chunks per box
-          for (int i = lane; i < nbox * chunks; i += 32) {
+          for (int i = f * 32 + lane; i < nbox * chunks; i += 32 * kWgFixers) {
             const int box = i / chunks, c = i - box * chunks;
             *reinterpret_cast<uint4*>(st + box * kWgBoxBytes + valid * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
           }
-          fence_proxy_async_smem();  // the MMA reads these rows through the async proxy
+          wrote = true;
         }
+        if (scaled && r < valid) {
+          const uint32_t base = smem_u32(st) + g_base_off;
+#pragma unroll 4
+          for (int c = 0; c < gchunks; ++c) {
+            const uint32_t addr = base + wg_chunk_off(r, c);
+            uint32_t v0, v1, v2, v3;
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(v0), "=r"(v1), "=r"(v2), "=r"(v3)
+                         : "r"(addr)
+                         : "memory");
+            asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(wg_bmul2(v0, w2)),
+                         "r"(wg_bmul2(v1, w2)), "r"(wg_bmul2(v2, w2)), "r"(wg_bmul2(v3, w2))
+                         : "memory");
+          }
+          wrote = true;
+        }
+        if (wrote) fence_proxy_async_smem();  // generic-proxy writes -> the MMA's operand reads
         __syncwarp();
         if (lane == 0) mbar_arrive(&ready[s]);
       }
@@ -319,18 +407,42 @@ size_t wgrad_smem_bytes(int bn, int stages) {
          2 * kWgMaxExperts * sizeof(int);
 }
 
-// out0/out1 as WgradArgs; a [rows, m_total] (ld_a), b [rows, n_total] (ld_b).
-int launch_wgrad(const uint16_t* a_rows, int64_t ld_a, int m_total, const uint16_t* b_rows, int64_t ld_b,
-                 int n_total, int64_t rows, const int* counts, int E, uint16_t* out0, int ld0, int n_valid0,
-                 uint16_t* out1, int ld1, int n_start1, int n_valid1, int* status, cudaStream_t stream) {
+// out0/out1 as WgradArgs; A has m_total columns (a.total), B n_total (b.total),
+// each either stored [rows, total] (ld) or gathered (at most one of them).
+int launch_wgrad(const WgradOperand& A, const WgradOperand& B, int64_t rows, const int* counts, int E,
+                 uint16_t* out0, int ld0, int n_valid0, uint16_t* out1, int ld1, int n_start1, int n_valid1,
+                 int* status, cudaStream_t stream) {
+  const int m_total = A.total, n_total = B.total;
   if (E <= 0 || E > kWgMaxExperts || m_total <= 0 || n_total <= 0 || out0 == nullptr) return SPX_ERR_INVALID_ARG;
-  if (m_total % 8 != 0 || n_total % 8 != 0 || ld0 % 8 != 0 || (out1 != nullptr && ld1 % 8 != 0))
-    return SPX_ERR_UNSUPPORTED;  // 16-byte rows for TMA and the vector stores
+  if (m_total % 8 != 0 || n_total % 8 != 0 || ld0 % 8 != 0 || (out1 != nullptr && ld1 % 8 != 0) || A.ld % 8 != 0 ||
+      B.ld % 8 != 0)
+    return SPX_ERR_UNSUPPORTED;  // 16-byte rows for TMA, cp.async and the vector stores
+  const bool ga = A.rows == nullptr, gb = B.rows == nullptr;
+  if ((ga && gb) || (ga && (A.src == nullptr || A.index == nullptr || A.scale != nullptr)) ||
+      (gb && (B.src == nullptr || B.index == nullptr)))
+    return SPX_ERR_INVALID_ARG;
   WgradArgs w{};
   // empty batches still need the zero gradients: a 1-row view keeps the maps valid
   const int64_t map_rows = rows > 0 ? rows : 1;
-  if (int rc = encode_2d(&w.tma_a, a_rows, map_rows, m_total, ld_a, 64); rc != SPX_OK) return rc;
-  if (int rc = encode_2d(&w.tma_b, b_rows, map_rows, n_total, ld_b, 64); rc != SPX_OK) return rc;
+  // stored operands: 64-row boxes; a gathered one: one-row boxes over its
+  // source rows (tile::gather4)
+  if (int rc = ga ? encode_2d(&w.tma_a, A.src, std::max<int64_t>(A.src_rows, 1), m_total, A.ld, 1)
+                  : encode_2d(&w.tma_a, A.rows, map_rows, m_total, A.ld, 64);
+      rc != SPX_OK)
+    return rc;
+  if (int rc = gb ? encode_2d(&w.tma_b, B.src, std::max<int64_t>(B.src_rows, 1), n_total, B.ld, 1)
+                  : encode_2d(&w.tma_b, B.rows, map_rows, n_total, B.ld, 64);
+      rc != SPX_OK)
+    return rc;
+  if (ga || gb) {
+    const WgradOperand& g = ga ? A : B;
+    w.g_src = g.src;
+    w.g_index = g.index;
+    w.g_scale = g.scale;
+    w.g_ld = g.ld;
+    w.g_is_a = ga ? 1 : 0;
+  }
+  w.n_total = n_total;
   w.counts = counts;
   w.E = E;
   w.m_total = m_total;

@@ -1135,9 +1135,14 @@ class B200MicroExpertChannelMixer(nn.Module):
         """Gradients of x and of every parameter (``spx_layer_backward`` for the
         routed experts -- their weight gradients included, on tcgen05 grouped
         GEMMs -- and the router scores; library GEMMs for the router's weight
-        gradient and the shared SwiGLU).  ``expert_wgrad="library"`` computes
-        the experts' weight gradients with ``torch._grouped_mm`` from the same
-        sorted rows instead (a comparison seam for the tests)."""
+        gradient and the shared SwiGLU).  The recomputed GEMM1 and the dh' GEMM
+        write the x rows and the bf16(dU * w) rows they gather in dispatch
+        order on the side, and the weight-gradient GEMMs read those;
+        ``expert_wgrad="native_gathered"`` skips the two P x d copies (less
+        memory, slower: the weight-gradient kernels then gather the rows
+        themselves), and ``expert_wgrad="library"`` computes the experts' weight
+        gradients with ``torch._grouped_mm`` from the sorted rows instead (a
+        comparison seam for the tests)."""
 
         import torch.nn.functional as F
 
@@ -1156,14 +1161,15 @@ class B200MicroExpertChannelMixer(nn.Module):
         ws = torch.empty(nbytes.value, dtype=torch.uint8, device=device)
         d_hidden = torch.empty(T, d, dtype=torch.bfloat16, device=device)
         d_logits = torch.empty(T, E, dtype=torch.bfloat16, device=device)
-        x_sorted = torch.empty(P, d, dtype=torch.bfloat16, device=device)
         h_sorted = torch.empty(P, I, dtype=torch.bfloat16, device=device)
-        dy_sorted = torch.empty(P, d, dtype=torch.bfloat16, device=device)
         dgu = torch.empty(P, 2 * kI, dtype=torch.bfloat16, device=device)
         counts = torch.empty(E, dtype=torch.int32, device=device)
         # the experts' weight gradients come out of the same native call (tcgen05 grouped GEMMs over
         # the sorted rows) when the hidden width allows 16-byte rows
-        native_wgrad = I % 8 == 0 and expert_wgrad == "native"
+        native_wgrad = I % 8 == 0 and expert_wgrad in ("native", "native_gathered")
+        copies = not (native_wgrad and expert_wgrad == "native_gathered")
+        x_sorted = torch.empty(P, d, dtype=torch.bfloat16, device=device) if copies else None
+        dy_sorted = torch.empty(P, d, dtype=torch.bfloat16, device=device) if copies else None
         wgrads = {n: torch.empty(E, *shape, dtype=torch.bfloat16, device=device) if native_wgrad else None
                   for n, shape in (("gate", (d, I)), ("up", (d, I)), ("down", (I, d)))}
         residency = self.residency
@@ -1189,8 +1195,8 @@ class B200MicroExpertChannelMixer(nn.Module):
             expert_ids=ids.data_ptr(), routing_weights=weights.data_ptr(), router_scores=scores.data_ptr(),
             gate_proj=gate.data_ptr(), up_proj=up.data_ptr(), down_proj=down.data_ptr(),
             d_update=du.data_ptr(), d_scores=_lib.ptr(dsc), d_aux=_lib.ptr(dax),
-            d_hidden_experts=d_hidden.data_ptr(), d_logits=d_logits.data_ptr(), x_sorted=x_sorted.data_ptr(),
-            h_sorted=h_sorted.data_ptr(), dy_sorted=dy_sorted.data_ptr(), dgu_sorted=dgu.data_ptr(),
+            d_hidden_experts=d_hidden.data_ptr(), d_logits=d_logits.data_ptr(), x_sorted=_lib.ptr(x_sorted),
+            h_sorted=h_sorted.data_ptr(), dy_sorted=_lib.ptr(dy_sorted), dgu_sorted=dgu.data_ptr(),
             expert_counts=counts.data_ptr(), d_gate_proj=_lib.ptr(wgrads["gate"]),
             d_up_proj=_lib.ptr(wgrads["up"]), d_down_proj=_lib.ptr(wgrads["down"]),
         )

@@ -1,6 +1,8 @@
 """The routed experts' weight gradients on tcgen05 (wgrad.cu, reached through
-spx_layer_backward): against the library grouped GEMM (torch._grouped_mm)
-on the same sorted rows -- both accumulate in FP32 and round once, so they
+spx_layer_backward): the rows gathered inside the kernels (no sorted copies)
+bit for bit as from the sorted copies the backward GEMMs write on the side,
+and against the library grouped GEMM (torch._grouped_mm) on the same sorted
+rows -- both accumulate in FP32 and round once, so they
 differ only by summation order (relative L2 < 2e-3, every element within
 1e-2 + 2e-2 |want|) -- with ragged per-expert row counts (partial last K
 blocks), experts that receive no rows (zero gradients), both batch classes
@@ -48,8 +50,12 @@ def test_native_expert_wgrad_matches_library(shape, tokens):
         assert (counts == 0).any()  # experts without rows get zero gradients
     assert ((counts % 64) != 0).any()  # partial last K blocks
     native = mixer._backward_native(x, ids, w, scores, du, None, None, expert_wgrad="native")
+    gathered = mixer._backward_native(x, ids, w, scores, du, None, None, expert_wgrad="native_gathered")
     library = mixer._backward_native(x, ids, w, scores, du, None, None, expert_wgrad="library")
     torch.cuda.synchronize()
+    # rows gathered inside the weight-gradient kernels: the same operands in the same order
+    for key in ("experts.gate_proj", "experts.up_proj", "experts.down_proj", "x"):
+        assert torch.equal(gathered[key], native[key]), key
     for key in ("experts.gate_proj", "experts.up_proj", "experts.down_proj"):
         got, want = native[key], library[key]
         assert got.shape == want.shape and got.dtype == torch.bfloat16, key
