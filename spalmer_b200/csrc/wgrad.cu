@@ -13,13 +13,13 @@
 // canonical MN-major layout (LBO = 8 KB between 64-column boxes, SBO = 1 KB
 // between 8-row groups along K); nothing is transposed in memory.
 //
-// One operand may instead be gathered from unsorted rows: x rows by token for
-// d gate | d up, and bf16(dU[token] * routing weight) rows for d down, so the
-// sorted copies (two P x d matrices) are never written.  The producer loads
+// B's rows may carry a BF16 scale per row (the routing weight: d down takes
+// bf16(dU row * w)), applied in shared memory before the MMA reads the stage.
+// One operand may instead be gathered from unsorted rows (x rows by token for
+// d gate | d up, dU rows by token for d down), so no sorted copies (two
+// P x d matrices) are needed.  The producer loads
 // a gathered operand with TMA gathers (four rows of 64 columns per
-// instruction, the 128-byte swizzle of the box layout the MMA expects); the
-// row scale, when there is one, is applied in shared memory by the fixer
-// warps before the MMA reads the stage.
+// instruction, the 128-byte swizzle of the box layout the MMA expects).
 //
 // A CTA (persistent, one per SM) walks tiles (expert, 128 output rows, bn
 // output columns) expert-major, so the tiles of one expert run side by side
@@ -267,12 +267,11 @@ __global__ void __launch_bounds__(kWgThreads, 1) wgrad_kernel(const __grid_const
     // ---------------- fixers: a pipeline stage between the loads and the MMA.
     // They pass every stage on in order (so no barrier phase can be skipped or
     // overtaken); first they zero the rows past the expert's segment in the
-    // segment's last block, and scale a gathered operand's rows (fixer f takes
-    // rows 32f .. 32f + 31: one row per lane).
+    // segment's last block, and scale B's rows when it has a row scale
+    // (fixer f takes rows 32f .. 32f + 31: one row per lane).
     const int f = warp - 2;
-    const bool scaled = gathered && a.g_scale != nullptr;
-    const int gchunks = gathered ? 8 * (a.g_is_a ? 2 : nbox_b) : 0;  // 16-byte chunks per gathered row
-    const uint32_t g_base_off = a.g_is_a ? 0u : a_bytes;
+    const bool scaled = a.b_scale != nullptr;
+    const int bchunks = 8 * nbox_b;  // 16-byte chunks per B row
     uint32_t it = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
@@ -286,7 +285,7 @@ __global__ void __launch_bounds__(kWgThreads, 1) wgrad_kernel(const __grid_const
         const int r = 32 * f + lane;
         uint32_t w2 = 0;
         if (scaled && r < valid) {
-          const uint32_t wb = __ldg(a.g_scale + start + kb * 64 + r);
+          const uint32_t wb = __ldg(a.b_scale + start + kb * 64 + r);
           w2 = wb | (wb << 16);
         }
         int go = 1;
@@ -309,9 +308,9 @@ __global__ void __launch_bounds__(kWgThreads, 1) wgrad_kernel(const __grid_const
           wrote = true;
         }
         if (scaled && r < valid) {
-          const uint32_t base = smem_u32(st) + g_base_off;
+          const uint32_t base = smem_u32(st) + a_bytes;
 #pragma unroll 4
-          for (int c = 0; c < gchunks; ++c) {
+          for (int c = 0; c < bchunks; ++c) {
             const uint32_t addr = base + wg_chunk_off(r, c);
             uint32_t v0, v1, v2, v3;
             asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
@@ -418,7 +417,7 @@ int launch_wgrad(const WgradOperand& A, const WgradOperand& B, int64_t rows, con
       B.ld % 8 != 0)
     return SPX_ERR_UNSUPPORTED;  // 16-byte rows for TMA, cp.async and the vector stores
   const bool ga = A.rows == nullptr, gb = B.rows == nullptr;
-  if ((ga && gb) || (ga && (A.src == nullptr || A.index == nullptr || A.scale != nullptr)) ||
+  if ((ga && gb) || A.scale != nullptr || (ga && (A.src == nullptr || A.index == nullptr)) ||
       (gb && (B.src == nullptr || B.index == nullptr)))
     return SPX_ERR_INVALID_ARG;
   WgradArgs w{};
@@ -438,10 +437,10 @@ int launch_wgrad(const WgradOperand& A, const WgradOperand& B, int64_t rows, con
     const WgradOperand& g = ga ? A : B;
     w.g_src = g.src;
     w.g_index = g.index;
-    w.g_scale = g.scale;
     w.g_ld = g.ld;
     w.g_is_a = ga ? 1 : 0;
   }
+  w.b_scale = B.scale;
   w.n_total = n_total;
   w.counts = counts;
   w.E = E;
