@@ -53,7 +53,7 @@
 extern "C" {
 #endif
 
-#define SPX_ABI_VERSION 11
+#define SPX_ABI_VERSION 12
 
 #define SPX_OK 0
 #define SPX_ERR_INVALID_ARG -1
@@ -160,6 +160,13 @@ typedef struct spx_layer_outputs {
                                       dispatch_order) | NULL; required by spx_layer_route  */
   float* expert_quantization_error; /* [E] weights->expert_quant_error of the selected
                                       experts, 0 for the others | NULL (bank.py:526-566)   */
+  /* Training (BF16 experts): activations for spx_layer_backward, written by
+   * the expert GEMM1 from the rows it stages anyway, so the backward need
+   * not recompute it.  Both or neither; with them the expert projections
+   * always run as tcgen05 GEMMs (no decode GEMVs).                          */
+  uint16_t* saved_x;               /* [T*k, d] hidden rows in dispatch order | NULL  */
+  uint16_t* saved_gu;              /* [T*k, spx_layer_saved_gu_cols] gate | up pre-
+                                      activations (BF16) in dispatch order | NULL   */
 } spx_layer_outputs;
 
 /* Stage boundaries recorded into spx_layer_outputs.stage_events:
@@ -170,6 +177,10 @@ typedef struct spx_layer_outputs {
 
 int spx_abi_version(void);
 const char* spx_status_string(int status);
+
+/* Columns of spx_layer_outputs.saved_gu for `dims` (chunk layout: per chunk
+ * of the hidden width, its gate columns then its up columns). */
+int spx_layer_saved_gu_cols(const spx_layer_dims* dims, int64_t* cols);
 
 /* Workspace bytes and packed weight sizes for `dims`. Host-only, no GPU work. */
 int spx_layer_sizes(const spx_layer_dims* dims, size_t* workspace_bytes, spx_packed_sizes* packed);
@@ -492,6 +503,9 @@ typedef struct spx_layer_grads {
   uint16_t* d_gate_proj;
   uint16_t* d_up_proj;
   uint16_t* d_down_proj;
+  /* The forward's saved_gu | NULL (GEMM1 recomputed).  With it, x_sorted
+   * must hold the forward's saved_x: neither is written again. */
+  const uint16_t* saved_gu;
 } spx_layer_grads;
 
 int spx_layer_backward_sizes(const spx_layer_dims* dims, size_t* workspace_bytes);

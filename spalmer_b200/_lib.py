@@ -50,6 +50,7 @@ EXPORTED = (
     "spx_calibration_workspace",
     "spx_surprise_calibration",
     "spx_layer_backward_sizes",
+    "spx_layer_saved_gu_cols",
     "spx_layer_backward",
     "spx_block_channel_forward",
     "spx_rmsnorm_rows",
@@ -76,7 +77,7 @@ EXPORTED = (
     "spx_dispatch_static_status",
 )
 
-ABI_VERSION = 11
+ABI_VERSION = 12
 
 _vp = ctypes.c_void_p
 
@@ -160,6 +161,8 @@ class LayerOutputs(ctypes.Structure):
         ("stage_events", _vp),
         ("pair_rank", _vp),
         ("expert_quantization_error", _vp),
+        ("saved_x", _vp),
+        ("saved_gu", _vp),
     ]
 
 
@@ -184,6 +187,7 @@ class LayerGrads(ctypes.Structure):
         ("d_gate_proj", _vp),
         ("d_up_proj", _vp),
         ("d_down_proj", _vp),
+        ("saved_gu", _vp),
     ]
 
 
@@ -257,6 +261,7 @@ def load() -> ctypes.CDLL:
             [_vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, _vp, _vp],
         ),
         "spx_layer_backward_sizes": (ctypes.c_int, [P(LayerDims), P(ctypes.c_size_t)]),
+        "spx_layer_saved_gu_cols": (ctypes.c_int, [P(LayerDims), P(ctypes.c_int64)]),
         "spx_layer_backward": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, P(LayerGrads), _vp, _vp]),
         "spx_block_channel_forward": (
             ctypes.c_int,

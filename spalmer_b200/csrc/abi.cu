@@ -393,6 +393,8 @@ struct ExpertPass {
   uint16_t* const* row_out = nullptr;  // GEMM2 rows to row_out[row_out_idx[p]] instead of Y
   const int* row_out_idx = nullptr;
   const uint8_t* const* a_rows = nullptr;  // BF16 GEMM1 rows through one pointer per source row
+  uint16_t* saved_x = nullptr;   // training: BF16 GEMM1's gathered rows in dispatch order [P, d]
+  uint16_t* saved_gu = nullptr;  // training: BF16 GEMM1's gate | up pre-activations [P, nc * 2c]
 };
 
 // NVFP4 lane input: each expert's rows in dispatch order as E2M1 with UE4M3
@@ -429,7 +431,9 @@ int stage_quantize_x(const Ctx& c, const uint16_t* hidden, int64_t ld_hidden) {
 int expert_gemvs(const Ctx& c, const uint16_t* xa, const int* src_row, const uint16_t* sorted_w,
                  const ExpertPass& p) {
   const Shape& s = c.s;
-  if (s.P > kGemvMaxPairs || s.nv || p.row_out != nullptr || p.a_rows != nullptr || xa == nullptr) return 1;
+  if (s.P > kGemvMaxPairs || s.nv || p.row_out != nullptr || p.a_rows != nullptr || xa == nullptr ||
+      p.saved_x != nullptr)
+    return 1;
   GemvPass g{};
   g.tiles = p.tiles;
   g.num_tiles = p.num_tiles;
@@ -519,6 +523,13 @@ int stage_expert_gemms(const Ctx& c, const uint16_t* xa, const int* src_row, con
     g.h_cols = s.kp;
     g.out = hid;
     g.ldo = s.kp;
+    if (p.saved_x != nullptr) {  // training: the rows and the pre-activations, for the backward
+      g.copy_out = p.saved_x;
+      g.ld_copy = s.d;
+      if ((rc = encode_2d(&g.tma_copy, p.saved_x, s.P, s.d, s.d, 32)) != SPX_OK) return rc;
+      g.gu_out = p.saved_gu;
+      g.ld_gu = static_cast<int64_t>(s.nc) * 2 * s.c;
+    }
     if ((rc = launch_gemm(kEpiSwiglu, g, s.max_tiles, s.nc, c.st)) != SPX_OK) return rc;
   }
   if (mx) {
@@ -651,15 +662,18 @@ int stage_expert_gemms(const Ctx& c, const uint16_t* xa, const int* src_row, con
 // K3: expert GEMM1 (+SwiGLU) and GEMM2 over the dispatched rows of `hidden`
 // (`xa` = hidden padded), both lanes; weighted rows land in Y (sorted order).
 int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hidden, const uint16_t* xa,
-                  const DispatchArgs& da, int64_t ld_hidden = 0, bool x_quantized = false) {
+                  const DispatchArgs& da, int64_t ld_hidden = 0, bool x_quantized = false,
+                  uint16_t* saved_x = nullptr, uint16_t* saved_gu = nullptr) {
   const bool mx = da.lane_mx != nullptr;
   if (mx && !x_quantized) {
     const int rc = c.s.nv ? stage_quantize_nv_x(c, hidden, ld_hidden, da) : stage_quantize_x(c, hidden, ld_hidden);
     if (rc != SPX_OK) return rc;
   }
-  const ExpertPass p{w->expert_w1, w->expert_w2, w->expert_w1_mx, w->expert_w1_mx_scales, w->expert_w2_mx,
-                     w->expert_w2_mx_scales, c.s.E, da.tiles, da.num_tiles, mx ? da.tiles_mx : nullptr,
-                     mx ? da.num_tiles_mx : nullptr, 0, w->expert_nvfp4_amax};
+  ExpertPass p{w->expert_w1, w->expert_w2, w->expert_w1_mx, w->expert_w1_mx_scales, w->expert_w2_mx,
+               w->expert_w2_mx_scales, c.s.E, da.tiles, da.num_tiles, mx ? da.tiles_mx : nullptr,
+               mx ? da.num_tiles_mx : nullptr, 0, w->expert_nvfp4_amax};
+  p.saved_x = saved_x;
+  p.saved_gu = saved_gu;
   return stage_expert_gemms(c, xa, da.src_row, da.sorted_weights, p);
 }
 
@@ -782,6 +796,14 @@ using namespace spx;
 extern "C" {
 
 int spx_abi_version(void) { return SPX_ABI_VERSION; }
+
+int spx_layer_saved_gu_cols(const spx_layer_dims* dims, int64_t* cols) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (cols == nullptr) return SPX_ERR_INVALID_ARG;
+  *cols = static_cast<int64_t>(s.nc) * 2 * s.c;
+  return SPX_OK;
+}
 
 const char* spx_status_string(int status) {
   switch (status) {
@@ -1149,6 +1171,11 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
     return SPX_ERR_INVALID_ARG;
   if (int rc = check_layer_weights(s, dims, w, true, true, true); rc != SPX_OK) return rc;
   if (!aligned16(hidden) || !aligned16(out->update) || !aligned16(workspace)) return SPX_ERR_ALIGNMENT;
+  if ((out->saved_x != nullptr) != (out->saved_gu != nullptr)) return SPX_ERR_INVALID_ARG;
+  if (out->saved_x != nullptr) {  // training activations: BF16 experts, d_model % 64 == 0
+    if (s.mx || s.kd != s.d) return SPX_ERR_UNSUPPORTED;
+    if (!aligned16(out->saved_x) || !aligned16(out->saved_gu)) return SPX_ERR_ALIGNMENT;
+  }
   const Layout L = make_layout(s);
   const Ctx c{s, L, workspace, static_cast<cudaStream_t>(stream), at<int>(workspace, L.small), out->stage_events};
   int rc = SPX_OK;
@@ -1189,7 +1216,8 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   c.mark(3);
   // ---- K3: grouped experts (both lanes)
   if (fork_mx && forked && cudaStreamWaitEvent(c.st, ss.join, 0) != cudaSuccess) return SPX_ERR_CUDA;
-  if ((rc = stage_experts(c, w, hidden, xa, da, 0, fork_mx && forked)) != SPX_OK) return rc;
+  if ((rc = stage_experts(c, w, hidden, xa, da, 0, fork_mx && forked, out->saved_x, out->saved_gu)) != SPX_OK)
+    return rc;
   // ---- K4: shared SwiGLU, then update = shared + the token's k weighted expert rows
   uint16_t* y = at<uint16_t>(workspace, L.y);
   if (fused_combine_ok(s)) {
@@ -1540,6 +1568,7 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
   // gradients, which then gather their rows themselves.
   const bool sorted_rows = gr->x_sorted != nullptr;
   if (sorted_rows != (gr->dy_sorted != nullptr) || (!sorted_rows && !wgrad)) return SPX_ERR_INVALID_ARG;
+  if (gr->saved_gu != nullptr && (!sorted_rows || !aligned16(gr->saved_gu))) return SPX_ERR_INVALID_ARG;
   if (wgrad && s.I % 8 != 0) return SPX_ERR_UNSUPPORTED;
   if (wgrad && (!aligned16(gr->h_sorted) || !aligned16(gr->d_gate_proj) || !aligned16(gr->d_up_proj) ||
                 !aligned16(gr->d_down_proj)))
@@ -1555,7 +1584,8 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
   const cudaStream_t st = c.st;
   int rc = SPX_OK;
   const int ki = bwd_ki(s), ldh = bwd_ldh(s);
-  uint16_t* gu = at<uint16_t>(workspace, B.gu);
+  // [P, nc * 2c] gate | up pre-activations: the forward's (saved_gu) or recomputed here
+  const uint16_t* gu = gr->saved_gu != nullptr ? gr->saved_gu : at<uint16_t>(workspace, B.gu);
   uint16_t* dhp = at<uint16_t>(workspace, B.dhp);
   uint16_t* w1cat = at<uint16_t>(workspace, B.w1cat);
   float* dw = at<float>(workspace, B.dw);
@@ -1575,8 +1605,9 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
   da.resident = w->resident_mask;
   if ((rc = launch_dispatch(da, st)) != SPX_OK) return rc;
 
-  // ---- gate | up pre-activations again: GEMM1 (gathered rows) with a plain epilogue
-  {
+  // ---- gate | up pre-activations again: GEMM1 (gathered rows) with a plain
+  // epilogue, unless the forward saved them (and the rows: x_sorted)
+  if (gr->saved_gu == nullptr) {
     GemmArgs g = base_args(kEpiStore, 2 * s.c, s.kd / 64, c.status);
     if ((rc = encode_3d(&g.tma_b, w->expert_w1, s.E, static_cast<int64_t>(s.nc) * 2 * s.c, s.kd, 2 * s.c)) != SPX_OK)
       return rc;
@@ -1588,7 +1619,7 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
     g.tiles = da.tiles;
     g.num_tiles = da.num_tiles;
     g.n_valid = s.nc * 2 * s.c;
-    g.out = gu;
+    g.out = at<uint16_t>(workspace, B.gu);
     g.ldo = s.nc * 2 * s.c;
     g.copy_out = gr->x_sorted;  // the gathered x rows, kept in dispatch order (or not at all)
     g.ld_copy = s.d;

@@ -475,7 +475,9 @@ __device__ __forceinline__ void run_epilogue_swiglu_mx(const GemmArgs& a, uint32
 // next tile's MMAs need not wait for the SwiGLU.  Each slice of hidden rows
 // (in tile order) then goes through the warp's 4 KB staging buffer: threads
 // write their own row, and each store instruction moves 8 rows x 64 B.
-// Needs chunk % 8 == 0 and ldo % 8 == 0 (16-byte aligned row segments).
+// With gu_out (training) the BF16-rounded gate and up values of the slice
+// go out the same way first, for the backward.  Needs chunk % 8 == 0 and
+// ldo % 8 == 0, ld_gu % 8 == 0 (16-byte aligned row segments).
 __device__ __forceinline__ void run_epilogue_swiglu_bf16(const GemmArgs& a, uint32_t taddr, uint8_t* stage,
                                                          int quad, int half, int lane, int row0, int rows, int nt,
                                                          uint64_t* release) {
@@ -508,20 +510,40 @@ __device__ __forceinline__ void run_epilogue_swiglu_bf16(const GemmArgs& a, uint
   tc_fence_before();
   __syncwarp();
   if (lane == 0) mbar_arrive(release);
+  const int wrows = rows - quad * 32;
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
     const int s0 = half * 32 + 64 * j;
     if (s0 >= a.chunk) break;
+    const int nchunk = min(32, a.chunk - s0) >> 3;  // 16-byte chunks per row (the width is a multiple of 8)
+    if (a.gu_out != nullptr) {
+      // the pre-activations (training): gate at columns [0, 32) and up at
+      // [32, 64) of the staged rows, each stored to its own columns
+      __syncwarp();
+      stage_put16(stage, lane, 0, &gp[j][0]);
+      stage_put16(stage, lane, 16, &gp[j][8]);
+      stage_put16(stage, lane, 32, &up[j][0]);
+      stage_put16(stage, lane, 48, &up[j][8]);
+      __syncwarp();
+      const int q = lane & 7;
+      const int part = q >> 2, qc = q & 3;
+      uint16_t* col = a.gu_out + nt * 2 * a.chunk + part * a.chunk + s0 + qc * 8;
+#pragma unroll
+      for (int step = 0; step < 8; ++step) {
+        const int ri = step * 4 + (lane >> 3);
+        if (ri < wrows && qc < nchunk)
+          *reinterpret_cast<uint4*>(col + static_cast<int64_t>(row0 + quad * 32 + ri) * a.ld_gu) =
+              *reinterpret_cast<const uint4*>(stage + stage_off(ri, q));
+      }
+    }
     uint32_t hw[16];
 #pragma unroll
     for (int c = 0; c < 16; ++c)
       hw[c] = bmul2(pack_bf16x2(silu_fast(lo_f(gp[j][c])), silu_fast(hi_f(gp[j][c]))), up[j][c]);
-    __syncwarp();  // the previous slice's reads of the buffer are done
+    __syncwarp();  // the previous reads of the buffer are done
     stage_put16(stage, lane, 0, &hw[0]);
     stage_put16(stage, lane, 16, &hw[8]);
     __syncwarp();
-    const int nchunk = min(32, a.chunk - s0) >> 3;  // 16-byte chunks per row (the width is a multiple of 8)
-    const int wrows = rows - quad * 32;
     const int q = lane & 3;
     uint16_t* col = out + nt * a.chunk + s0 + q * 8;
 #pragma unroll

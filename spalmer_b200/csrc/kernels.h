@@ -136,6 +136,10 @@ struct GemmArgs {
   uint16_t* copy_out;
   int64_t ld_copy;
   CUtensorMap tma_copy;
+  // kEpiSwiglu, BF16 lane: the BF16-rounded gate | up pre-activations of
+  // every tile row, gu_out[p][chunk * 2c + j] (gate j < c, up j >= c).  null = none.
+  uint16_t* gu_out;
+  int64_t ld_gu;
   // MXFP8 lane (block-scaled kernel only)
   const uint8_t* sfa;        // A scale bytes [A rows, ld_sfa] row-major (row = gathered source row)
   int64_t ld_sfa;            // bytes per row, multiple of 4

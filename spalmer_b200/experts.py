@@ -954,8 +954,29 @@ class B200MicroExpertChannelMixer(nn.Module):
             return self._forward_autograd(hidden_states)
         return self._forward_native(hidden_states, router_logits)
 
+    def _training_saves(self, hidden_states: Tensor) -> tuple[Tensor, Tensor] | None:
+        """Buffers for the activations the backward would otherwise recompute
+        (the hidden rows and the gate | up pre-activations of the expert GEMM1,
+        in dispatch order), when this layer's native backward can take them:
+        BF16 experts on the device, d_model % 64 == 0, prefill-sized batches."""
+        config = self.config
+        batch, seq_len, d = hidden_states.shape
+        k = self.active_experts
+        P = batch * seq_len * k
+        if (self._lanes(hidden_states.device) is not None or self.experts.expert_offload_enabled or d % 64
+                or config.resolved_inter_dim % 8 or P <= 1024):
+            return None
+        cols = _lib.ctypes.c_int64()
+        lib = _lib.load()
+        _lib.check(lib.spx_layer_saved_gu_cols(layer_dims(config, batch * seq_len, k), cols),
+                   "spx_layer_saved_gu_cols")
+        device = hidden_states.device
+        return (torch.empty(P, d, dtype=torch.bfloat16, device=device),
+                torch.empty(P, cols.value, dtype=torch.bfloat16, device=device))
+
     def _forward_native(self, hidden_states: Tensor, router_logits: Tensor | None,
-                        block: tuple[Tensor, float, Tensor] | None = None) -> ChannelMixerOutput:
+                        block: tuple[Tensor, float, Tensor] | None = None,
+                        saved: tuple[Tensor, Tensor] | None = None) -> ChannelMixerOutput:
         config = self.config
         if not hidden_states.is_cuda:
             raise RuntimeError("the B200 micro-expert layer requires CUDA hidden states")
@@ -1020,8 +1041,12 @@ class B200MicroExpertChannelMixer(nn.Module):
             dispatch_order=None, expert_counts=None, injected_logits=_lib.ptr(injected), router_logits=None,
             stage_events=None if events is None else _lib.ctypes.addressof(events),
             expert_quantization_error=quant_error.data_ptr(),
+            saved_x=None if saved is None else saved[0].data_ptr(),
+            saved_gu=None if saved is None else saved[1].data_ptr(),
         )
         stream = torch.cuda.current_stream(device).cuda_stream
+        if saved is not None and (self.experts.expert_offload_enabled or block is not None):
+            raise RuntimeError("saved training activations come from spx_layer_forward only")
         if self.experts.expert_offload_enabled:
             if block is not None:
                 raise RuntimeError("the fused block path needs the expert bank on the device")
@@ -1131,7 +1156,8 @@ class B200MicroExpertChannelMixer(nn.Module):
 
     def _backward_native(self, x: Tensor, ids: Tensor, weights: Tensor, scores: Tensor, d_update: Tensor,
                          d_aux: Tensor | None, d_scores: Tensor | None,
-                         expert_wgrad: str = "native") -> dict[str, Tensor]:
+                         expert_wgrad: str = "native",
+                         saved: tuple[Tensor, Tensor] | None = None) -> dict[str, Tensor]:
         """Gradients of x and of every parameter (``spx_layer_backward`` for the
         routed experts -- their weight gradients included, on tcgen05 grouped
         GEMMs -- and the router scores; library GEMMs for the router's weight
@@ -1142,7 +1168,9 @@ class B200MicroExpertChannelMixer(nn.Module):
         memory, slower: the weight-gradient kernels then gather the rows
         themselves), and ``expert_wgrad="library"`` computes the experts' weight
         gradients with ``torch._grouped_mm`` from the sorted rows instead (a
-        comparison seam for the tests)."""
+        comparison seam for the tests).  ``saved``: the activations the
+        forward wrote for this backward (``_training_saves``); GEMM1 is then
+        not recomputed."""
 
         import torch.nn.functional as F
 
@@ -1168,7 +1196,12 @@ class B200MicroExpertChannelMixer(nn.Module):
         # the sorted rows) when the hidden width allows 16-byte rows
         native_wgrad = I % 8 == 0 and expert_wgrad in ("native", "native_gathered")
         copies = not (native_wgrad and expert_wgrad == "native_gathered")
-        x_sorted = torch.empty(P, d, dtype=torch.bfloat16, device=device) if copies else None
+        if not copies:
+            saved = None
+        if saved is not None:
+            x_sorted = saved[0]
+        else:
+            x_sorted = torch.empty(P, d, dtype=torch.bfloat16, device=device) if copies else None
         dy_sorted = torch.empty(P, d, dtype=torch.bfloat16, device=device) if copies else None
         wgrads = {n: torch.empty(E, *shape, dtype=torch.bfloat16, device=device) if native_wgrad else None
                   for n, shape in (("gate", (d, I)), ("up", (d, I)), ("down", (I, d)))}
@@ -1199,6 +1232,7 @@ class B200MicroExpertChannelMixer(nn.Module):
             h_sorted=h_sorted.data_ptr(), dy_sorted=_lib.ptr(dy_sorted), dgu_sorted=dgu.data_ptr(),
             expert_counts=counts.data_ptr(), d_gate_proj=_lib.ptr(wgrads["gate"]),
             d_up_proj=_lib.ptr(wgrads["up"]), d_down_proj=_lib.ptr(wgrads["down"]),
+            saved_gu=None if saved is None else saved[1].data_ptr(),
         )
         stream = torch.cuda.current_stream(device).cuda_stream
         _lib.check(lib.spx_layer_backward(dims, pw, x.data_ptr(), gr, ws.data_ptr(), stream), "spx_layer_backward")
@@ -1302,7 +1336,9 @@ class _LayerFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, mixer, holder, names, hidden_states, *params):
-        out = mixer._forward_native(hidden_states, None)
+        saved = mixer._training_saves(hidden_states)
+        out = mixer._forward_native(hidden_states, None, saved=saved)
+        ctx.saved_activations = saved
         m = out.metrics
         holder["metrics"] = m
         ctx.mixer = mixer
@@ -1320,7 +1356,9 @@ class _LayerFunction(torch.autograd.Function):
         x, ids, weights, scores = ctx.saved_tensors
         if d_update is None:
             d_update = torch.zeros(ctx.shape, dtype=torch.bfloat16, device=x.device)
-        grads = ctx.mixer._backward_native(x, ids, weights, scores, d_update, d_aux, d_scores)
+        grads = ctx.mixer._backward_native(x, ids, weights, scores, d_update, d_aux, d_scores,
+                                           saved=ctx.saved_activations)
+        ctx.saved_activations = None
         return (None, None, None, grads["x"].reshape(ctx.shape), *[grads[n] for n in ctx.names])
 
 

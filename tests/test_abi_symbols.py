@@ -23,7 +23,7 @@ def test_library_builds_and_loads():
     build()
     assert TARGET.exists()
     lib = _lib.load()
-    assert lib.spx_abi_version() == _lib.ABI_VERSION == 11
+    assert lib.spx_abi_version() == _lib.ABI_VERSION == 12
 
 
 def test_every_declared_symbol_is_exported():

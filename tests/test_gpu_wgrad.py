@@ -67,3 +67,34 @@ def test_native_expert_wgrad_matches_library(shape, tokens):
             assert (got[empty] == 0).all(), key
     # the rest of the backward is the same call: bit for bit
     assert torch.equal(native["x"], library["x"])
+
+
+@pytest.mark.parametrize("shape", [dict(d_model=256, num_experts=40, expert_inter_dim=80, shared_inter_dim=64,
+                                        active_experts=4),
+                                   dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=0,
+                                        active_experts=8)], ids=["m10ish_odd_inter", "m100"])
+def test_saved_forward_activations_match_recompute(shape):
+    """The training forward writes the dispatch-order hidden rows and the gate | up
+    pre-activations from its expert GEMM1 (spx_layer_outputs.saved_x / saved_gu);
+    the backward given them skips its GEMM1 and must produce the same gradients,
+    bit for bit, as the backward that recomputes them."""
+    config = MicroExpertsConfig(**shape)
+    tokens = 2048
+    mixer, x, _, _, _, du = _inputs(config, tokens)
+    saved = mixer._training_saves(x.unsqueeze(0))
+    assert saved is not None
+    with torch.no_grad():
+        out = mixer._forward_native(x.unsqueeze(0), None, saved=saved)
+    k = config.active_experts
+    ids = out.metrics["expert_ids"].reshape(tokens, k)
+    w = out.metrics["routing_weights"].reshape(tokens, k)
+    scores = out.metrics["router_scores"].reshape(tokens, -1)
+    # the saved rows are the token rows in dispatch order (stable sort of the expert ids)
+    order = torch.argsort(ids.reshape(-1), stable=True)
+    assert torch.equal(saved[0], x[order // k])
+    recomputed = mixer._backward_native(x, ids, w, scores, du, None, None)
+    from_saved = mixer._backward_native(x, ids, w, scores, du, None, None, saved=saved)
+    torch.cuda.synchronize()
+    assert set(recomputed) == set(from_saved)
+    for key in recomputed:
+        assert torch.equal(from_saved[key], recomputed[key]), key
