@@ -506,6 +506,9 @@ typedef struct spx_layer_grads {
   /* The forward's saved_gu | NULL (GEMM1 recomputed).  With it, x_sorted
    * must hold the forward's saved_x: neither is written again. */
   const uint16_t* saved_gu;
+  /* [T, E] the forward's router logits (spx_layer_outputs.router_logits) |
+   * NULL (the router GEMM runs again; softplus scores only) */
+  const uint16_t* router_logits;
 } spx_layer_grads;
 
 int spx_layer_backward_sizes(const spx_layer_dims* dims, size_t* workspace_bytes);

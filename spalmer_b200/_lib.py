@@ -188,6 +188,7 @@ class LayerGrads(ctypes.Structure):
         ("d_up_proj", _vp),
         ("d_down_proj", _vp),
         ("saved_gu", _vp),
+        ("router_logits", _vp),
     ]
 
 

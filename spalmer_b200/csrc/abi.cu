@@ -1591,10 +1591,18 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
   float* dw = at<float>(workspace, B.dw);
   uint16_t* dxs = at<uint16_t>(workspace, L.y);
 
-  // ---- router logits again (the forward kept only the scores)
+  // ---- router logits: the forward's (router_logits) or again here
   const bool softplus = dims->score_transform == 0;
-  uint16_t* logits = softplus ? at<uint16_t>(workspace, B.logits) : nullptr;
-  if (softplus && (rc = stage_router(c, w, hidden, logits)) != SPX_OK) return rc;
+  const uint16_t* logits = nullptr;
+  if (softplus) {
+    if (gr->router_logits != nullptr) {
+      logits = gr->router_logits;
+    } else {
+      uint16_t* lg = at<uint16_t>(workspace, B.logits);
+      if ((rc = stage_router(c, w, hidden, lg)) != SPX_OK) return rc;
+      logits = lg;
+    }
+  }
 
   // ---- dispatch again, from the forward's expert ids (all experts in the BF16 table)
   DispatchArgs da = dispatch_args(s, gr->expert_ids, nullptr, gr->expert_counts, workspace, L);

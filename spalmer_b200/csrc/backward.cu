@@ -97,8 +97,9 @@ __device__ __forceinline__ void swiglu_bwd8(const uint4& gv, const uint4& uv, co
     float sgm[2], sg[2], h[2], dh[2], dsg[2], du[2];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      sgm[i] = sigmoidf_(g[i]);
-      sg[i] = g[i] / (1.0f + expf(-g[i]));  // silu as the reference evaluates it
+      const float den = 1.0f + expf(-g[i]);  // one exponential for both (sigmoidf_'s and silu's)
+      sgm[i] = 1.0f / den;
+      sg[i] = g[i] / den;  // silu as the reference evaluates it
     }
     bfr2(sg[0], sg[1]);
     h[0] = sg[0] * u[0];
@@ -204,17 +205,26 @@ __global__ void bwd_router_kernel(const BwdRouterArgs a) {
   }
   const float g_aux = a.d_aux != nullptr ? bf16_to_f32(*a.d_aux) : 0.0f;
   const float gs = bfr(g_aux * bfr(static_cast<float>(m)));  // d(sum) = d_aux * eligible
+  // Per column, the same for every row: eligibility and the load-balance
+  // gradient of the mean probability, d_p = bf16(bf16(gs * f_e) / T).
+  bool ok[NQ];
+  float dp[NQ];
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) {
+    const int c = lane + 32 * q;
+    ok[q] = c < E && (a.resident == nullptr || a.resident[c] != 0);
+    const float f = c < E ? bfr(a.fractions[c]) : 0.0f;
+    dp[q] = ok[q] ? bfr(bfr(gs * f) / static_cast<float>(a.tokens)) : 0.0f;
+  }
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); t < a.tokens;
        t += nwarps) {
     const uint16_t* srow = a.scores + t * E;
     float s[NQ], acc[NQ];
-    bool ok[NQ];
     float mx = -INFINITY;
 #pragma unroll
     for (int q = 0; q < NQ; ++q) {
       const int c = lane + 32 * q;
-      ok[q] = c < E && (a.resident == nullptr || a.resident[c] != 0);
       s[q] = c < E ? bf16_to_f32(srow[c]) : 0.0f;
       acc[q] = 0.0f;
       if (ok[q]) mx = fmaxf(mx, -s[q]);
@@ -231,13 +241,10 @@ __global__ void bwd_router_kernel(const BwdRouterArgs a) {
       }
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, off);
-      float p[NQ], dp[NQ], dot = 0.0f;
+      float p[NQ], dot = 0.0f;
 #pragma unroll
       for (int q = 0; q < NQ; ++q) {
-        const int c = lane + 32 * q;
         p[q] = ok[q] ? bfr(e[q] / sum) : 0.0f;
-        const float f = c < E ? bfr(a.fractions[c]) : 0.0f;
-        dp[q] = ok[q] ? bfr(bfr(gs * f) / static_cast<float>(a.tokens)) : 0.0f;
         dot += p[q] * dp[q];
       }
 #pragma unroll

@@ -954,11 +954,12 @@ class B200MicroExpertChannelMixer(nn.Module):
             return self._forward_autograd(hidden_states)
         return self._forward_native(hidden_states, router_logits)
 
-    def _training_saves(self, hidden_states: Tensor) -> tuple[Tensor, Tensor] | None:
+    def _training_saves(self, hidden_states: Tensor) -> tuple[Tensor, Tensor, Tensor | None] | None:
         """Buffers for the activations the backward would otherwise recompute
         (the hidden rows and the gate | up pre-activations of the expert GEMM1,
-        in dispatch order), when this layer's native backward can take them:
-        BF16 experts on the device, d_model % 64 == 0, prefill-sized batches."""
+        in dispatch order, and the router logits of softplus scores), when
+        this layer's native backward can take them: BF16 experts on the
+        device, d_model % 64 == 0, prefill-sized batches."""
         config = self.config
         batch, seq_len, d = hidden_states.shape
         k = self.active_experts
@@ -971,12 +972,15 @@ class B200MicroExpertChannelMixer(nn.Module):
         _lib.check(lib.spx_layer_saved_gu_cols(layer_dims(config, batch * seq_len, k), cols),
                    "spx_layer_saved_gu_cols")
         device = hidden_states.device
+        logits = None
+        if config.router_score_transform == "softplus":
+            logits = torch.empty(batch * seq_len, config.num_experts, dtype=torch.bfloat16, device=device)
         return (torch.empty(P, d, dtype=torch.bfloat16, device=device),
-                torch.empty(P, cols.value, dtype=torch.bfloat16, device=device))
+                torch.empty(P, cols.value, dtype=torch.bfloat16, device=device), logits)
 
     def _forward_native(self, hidden_states: Tensor, router_logits: Tensor | None,
                         block: tuple[Tensor, float, Tensor] | None = None,
-                        saved: tuple[Tensor, Tensor] | None = None) -> ChannelMixerOutput:
+                        saved: tuple[Tensor, Tensor, Tensor | None] | None = None) -> ChannelMixerOutput:
         config = self.config
         if not hidden_states.is_cuda:
             raise RuntimeError("the B200 micro-expert layer requires CUDA hidden states")
@@ -1038,7 +1042,8 @@ class B200MicroExpertChannelMixer(nn.Module):
             update=update.data_ptr(), router_scores=scores.data_ptr(), expert_ids=ids.data_ptr(),
             routing_weights=weights.data_ptr(), expert_utilization=util.data_ptr(),
             group_stats=stats.data_ptr(), group_ratios=ratios.data_ptr(), auxiliary_loss=aux.data_ptr(),
-            dispatch_order=None, expert_counts=None, injected_logits=_lib.ptr(injected), router_logits=None,
+            dispatch_order=None, expert_counts=None, injected_logits=_lib.ptr(injected),
+            router_logits=None if saved is None else _lib.ptr(saved[2]),
             stage_events=None if events is None else _lib.ctypes.addressof(events),
             expert_quantization_error=quant_error.data_ptr(),
             saved_x=None if saved is None else saved[0].data_ptr(),
@@ -1157,7 +1162,7 @@ class B200MicroExpertChannelMixer(nn.Module):
     def _backward_native(self, x: Tensor, ids: Tensor, weights: Tensor, scores: Tensor, d_update: Tensor,
                          d_aux: Tensor | None, d_scores: Tensor | None,
                          expert_wgrad: str = "native",
-                         saved: tuple[Tensor, Tensor] | None = None) -> dict[str, Tensor]:
+                         saved: tuple[Tensor, Tensor, Tensor | None] | None = None) -> dict[str, Tensor]:
         """Gradients of x and of every parameter (``spx_layer_backward`` for the
         routed experts -- their weight gradients included, on tcgen05 grouped
         GEMMs -- and the router scores; library GEMMs for the router's weight
@@ -1233,6 +1238,7 @@ class B200MicroExpertChannelMixer(nn.Module):
             expert_counts=counts.data_ptr(), d_gate_proj=_lib.ptr(wgrads["gate"]),
             d_up_proj=_lib.ptr(wgrads["up"]), d_down_proj=_lib.ptr(wgrads["down"]),
             saved_gu=None if saved is None else saved[1].data_ptr(),
+            router_logits=None if saved is None else _lib.ptr(saved[2]),
         )
         stream = torch.cuda.current_stream(device).cuda_stream
         _lib.check(lib.spx_layer_backward(dims, pw, x.data_ptr(), gr, ws.data_ptr(), stream), "spx_layer_backward")

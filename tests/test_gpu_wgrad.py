@@ -75,9 +75,10 @@ def test_native_expert_wgrad_matches_library(shape, tokens):
                                         active_experts=8)], ids=["m10ish_odd_inter", "m100"])
 def test_saved_forward_activations_match_recompute(shape):
     """The training forward writes the dispatch-order hidden rows and the gate | up
-    pre-activations from its expert GEMM1 (spx_layer_outputs.saved_x / saved_gu);
-    the backward given them skips its GEMM1 and must produce the same gradients,
-    bit for bit, as the backward that recomputes them."""
+    pre-activations from its expert GEMM1 (spx_layer_outputs.saved_x / saved_gu)
+    and keeps the router logits; the backward given them skips its router GEMM and
+    GEMM1 and must produce the same gradients, bit for bit, as the backward that
+    recomputes them."""
     config = MicroExpertsConfig(**shape)
     tokens = 2048
     mixer, x, _, _, _, du = _inputs(config, tokens)
