@@ -167,6 +167,11 @@ typedef struct spx_layer_outputs {
   uint16_t* saved_x;               /* [T*k, d] hidden rows in dispatch order | NULL  */
   uint16_t* saved_gu;              /* [T*k, spx_layer_saved_gu_cols] gate | up pre-
                                       activations (BF16) in dispatch order | NULL   */
+  uint16_t* saved_shared_gu;       /* [T, cols of spx_layer_saved_shared_gu] the shared
+                                      SwiGLU's gate | up pre-activations (BF16), per
+                                      chunk of `chunk` columns its gate then its up
+                                      columns | NULL (the shared SwiGLU's backward
+                                      input, spx_swiglu_backward_rows)             */
 } spx_layer_outputs;
 
 /* Stage boundaries recorded into spx_layer_outputs.stage_events:
@@ -181,6 +186,7 @@ const char* spx_status_string(int status);
 /* Columns of spx_layer_outputs.saved_gu for `dims` (chunk layout: per chunk
  * of the hidden width, its gate columns then its up columns). */
 int spx_layer_saved_gu_cols(const spx_layer_dims* dims, int64_t* cols);
+int spx_layer_saved_shared_gu(const spx_layer_dims* dims, int64_t* cols, int32_t* chunk);
 
 /* Workspace bytes and packed weight sizes for `dims`. Host-only, no GPU work. */
 int spx_layer_sizes(const spx_layer_dims* dims, size_t* workspace_bytes, spx_packed_sizes* packed);

@@ -51,6 +51,7 @@ EXPORTED = (
     "spx_surprise_calibration",
     "spx_layer_backward_sizes",
     "spx_layer_saved_gu_cols",
+    "spx_layer_saved_shared_gu",
     "spx_layer_backward",
     "spx_block_channel_forward",
     "spx_rmsnorm_rows",
@@ -163,6 +164,7 @@ class LayerOutputs(ctypes.Structure):
         ("expert_quantization_error", _vp),
         ("saved_x", _vp),
         ("saved_gu", _vp),
+        ("saved_shared_gu", _vp),
     ]
 
 
@@ -263,6 +265,7 @@ def load() -> ctypes.CDLL:
         ),
         "spx_layer_backward_sizes": (ctypes.c_int, [P(LayerDims), P(ctypes.c_size_t)]),
         "spx_layer_saved_gu_cols": (ctypes.c_int, [P(LayerDims), P(ctypes.c_int64)]),
+        "spx_layer_saved_shared_gu": (ctypes.c_int, [P(LayerDims), P(ctypes.c_int64), P(ctypes.c_int32)]),
         "spx_layer_backward": (ctypes.c_int, [P(LayerDims), P(PackedWeights), _vp, P(LayerGrads), _vp, _vp]),
         "spx_block_channel_forward": (
             ctypes.c_int,

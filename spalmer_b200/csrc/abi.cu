@@ -679,11 +679,13 @@ int stage_experts(const Ctx& c, const spx_packed_weights* w, const uint16_t* hid
 
 // K4 (shared half), first GEMM: shared gate/up with the SwiGLU into the
 // workspace's shared hidden rows.
-int stage_shared_gemm1(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa) {
+// gu_out (training): the BF16 gate | up pre-activations too, [T, ncs * 2cs]
+// in the chunk layout (tcgen05 path at every batch size).
+int stage_shared_gemm1(const Ctx& c, const spx_packed_weights* w, const uint16_t* xa, uint16_t* gu_out = nullptr) {
   const Shape& s = c.s;
   int rc = SPX_OK;
   uint16_t* hs = at<uint16_t>(c.ws, c.L.shared_hidden);
-  if (s.T <= kGemvMaxTokens) {  // decode-sized batch: one dense SwiGLU GEMV
+  if (s.T <= kGemvMaxTokens && gu_out == nullptr) {  // decode-sized batch: one dense SwiGLU GEMV
     GemvPass g{};
     g.dense_rows = static_cast<int>(s.T);
     g.status = c.status;
@@ -712,6 +714,8 @@ int stage_shared_gemm1(const Ctx& c, const spx_packed_weights* w, const uint16_t
   if ((rc = encode_3d(&g.tma_b, w->shared_w1, 1, static_cast<int64_t>(s.ncs) * 2 * s.cs, s.kd,
                       pair ? s.cs : 2 * s.cs)) != SPX_OK)
     return rc;
+  g.gu_out = gu_out;
+  g.ld_gu = static_cast<int64_t>(s.ncs) * 2 * s.cs;
   g.m_rows = static_cast<int>(s.T);
   g.chunk = s.cs;
   g.h_cols = s.ksp;
@@ -802,6 +806,15 @@ int spx_layer_saved_gu_cols(const spx_layer_dims* dims, int64_t* cols) {
   if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
   if (cols == nullptr) return SPX_ERR_INVALID_ARG;
   *cols = static_cast<int64_t>(s.nc) * 2 * s.c;
+  return SPX_OK;
+}
+
+int spx_layer_saved_shared_gu(const spx_layer_dims* dims, int64_t* cols, int32_t* chunk) {
+  Shape s;
+  if (int rc = make_shape(dims, &s); rc != SPX_OK) return rc;
+  if (cols == nullptr || chunk == nullptr) return SPX_ERR_INVALID_ARG;
+  *cols = static_cast<int64_t>(s.ncs) * 2 * s.cs;
+  *chunk = s.cs;
   return SPX_OK;
 }
 
@@ -1176,6 +1189,7 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
     if (s.mx || s.kd != s.d) return SPX_ERR_UNSUPPORTED;
     if (!aligned16(out->saved_x) || !aligned16(out->saved_gu)) return SPX_ERR_ALIGNMENT;
   }
+  if (out->saved_shared_gu != nullptr && (s.S <= 0 || !aligned16(out->saved_shared_gu))) return SPX_ERR_INVALID_ARG;
   const Layout L = make_layout(s);
   const Ctx c{s, L, workspace, static_cast<cudaStream_t>(stream), at<int>(workspace, L.small), out->stage_events};
   int rc = SPX_OK;
@@ -1191,7 +1205,8 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   const bool fork_mx = s.mx && !s.nv && !s.small && w->expert_lane_mxfp8 != nullptr;
   // (only while the shared projections are dense GEMVs: no tcgen05 kernel,
   // which would want the tensor memory the main stream's kernels hold)
-  const bool fork_shared = s.small && s.S > 0 && !fused_combine_ok(s) && s.T <= kGemvMaxTokens;
+  const bool fork_shared = s.small && s.S > 0 && !fused_combine_ok(s) && s.T <= kGemvMaxTokens &&
+                           out->saved_shared_gu == nullptr;
   SideStream ss{};
   const bool forked = (fork_mx || fork_shared) && side_stream(c.st, &ss);
   uint16_t* so = s.S > 0 ? at<uint16_t>(workspace, L.shared_out) : nullptr;
@@ -1221,14 +1236,14 @@ int spx_layer_forward(const spx_layer_dims* dims, const spx_packed_weights* w, c
   // ---- K4: shared SwiGLU, then update = shared + the token's k weighted expert rows
   uint16_t* y = at<uint16_t>(workspace, L.y);
   if (fused_combine_ok(s)) {
-    if ((rc = stage_shared_gemm1(c, w, xa)) != SPX_OK) return rc;
+    if ((rc = stage_shared_gemm1(c, w, xa, out->saved_shared_gu)) != SPX_OK) return rc;
     if ((rc = stage_shared_gemm2(c, w, out->update, y, da.rank)) != SPX_OK) return rc;
   } else {
     if (fork_shared && forked) {
       if (cudaStreamWaitEvent(c.st, ss.join2, 0) != cudaSuccess) return SPX_ERR_CUDA;
       c.mark(6);
     } else if (s.S > 0) {
-      if ((rc = stage_shared_gemm1(c, w, xa)) != SPX_OK) return rc;
+      if ((rc = stage_shared_gemm1(c, w, xa, out->saved_shared_gu)) != SPX_OK) return rc;
       if ((rc = stage_shared_gemm2(c, w, so)) != SPX_OK) return rc;
     } else {
       c.mark(6);

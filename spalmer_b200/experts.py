@@ -954,12 +954,13 @@ class B200MicroExpertChannelMixer(nn.Module):
             return self._forward_autograd(hidden_states)
         return self._forward_native(hidden_states, router_logits)
 
-    def _training_saves(self, hidden_states: Tensor) -> tuple[Tensor, Tensor, Tensor | None] | None:
-        """Buffers for the activations the backward would otherwise recompute
-        (the hidden rows and the gate | up pre-activations of the expert GEMM1,
-        in dispatch order, and the router logits of softplus scores), when
-        this layer's native backward can take them: BF16 experts on the
-        device, d_model % 64 == 0, prefill-sized batches."""
+    def _training_saves(self, hidden_states: Tensor) -> tuple | None:
+        """Buffers for the activations the backward would otherwise recompute,
+        when this layer's native backward can take them (BF16 experts on the
+        device, d_model % 64 == 0, prefill-sized batches): (the hidden rows and
+        the gate | up pre-activations of the expert GEMM1 in dispatch order, the
+        router logits of softplus scores or None, the shared SwiGLU's gate | up
+        pre-activations with their chunk width or None)."""
         config = self.config
         batch, seq_len, d = hidden_states.shape
         k = self.active_experts
@@ -972,15 +973,24 @@ class B200MicroExpertChannelMixer(nn.Module):
         _lib.check(lib.spx_layer_saved_gu_cols(layer_dims(config, batch * seq_len, k), cols),
                    "spx_layer_saved_gu_cols")
         device = hidden_states.device
+        T = batch * seq_len
         logits = None
         if config.router_score_transform == "softplus":
-            logits = torch.empty(batch * seq_len, config.num_experts, dtype=torch.bfloat16, device=device)
+            logits = torch.empty(T, config.num_experts, dtype=torch.bfloat16, device=device)
+        shared_gu = None
+        if self.shared is not None and _shared_bwd_native(self.shared, hidden_states.reshape(T, d)):
+            scols = _lib.ctypes.c_int64()
+            chunk = _lib.ctypes.c_int32()
+            _lib.check(lib.spx_layer_saved_shared_gu(layer_dims(config, T, k), scols, chunk),
+                       "spx_layer_saved_shared_gu")
+            if self.shared.gate_projection.weight.shape[0] % chunk.value == 0:  # whole chunks
+                shared_gu = (torch.empty(T, scols.value, dtype=torch.bfloat16, device=device), chunk.value)
         return (torch.empty(P, d, dtype=torch.bfloat16, device=device),
-                torch.empty(P, cols.value, dtype=torch.bfloat16, device=device), logits)
+                torch.empty(P, cols.value, dtype=torch.bfloat16, device=device), logits, shared_gu)
 
     def _forward_native(self, hidden_states: Tensor, router_logits: Tensor | None,
                         block: tuple[Tensor, float, Tensor] | None = None,
-                        saved: tuple[Tensor, Tensor, Tensor | None] | None = None) -> ChannelMixerOutput:
+                        saved: tuple | None = None) -> ChannelMixerOutput:
         config = self.config
         if not hidden_states.is_cuda:
             raise RuntimeError("the B200 micro-expert layer requires CUDA hidden states")
@@ -1048,6 +1058,7 @@ class B200MicroExpertChannelMixer(nn.Module):
             expert_quantization_error=quant_error.data_ptr(),
             saved_x=None if saved is None else saved[0].data_ptr(),
             saved_gu=None if saved is None else saved[1].data_ptr(),
+            saved_shared_gu=None if saved is None or saved[3] is None else saved[3][0].data_ptr(),
         )
         stream = torch.cuda.current_stream(device).cuda_stream
         if saved is not None and (self.experts.expert_offload_enabled or block is not None):
@@ -1162,7 +1173,7 @@ class B200MicroExpertChannelMixer(nn.Module):
     def _backward_native(self, x: Tensor, ids: Tensor, weights: Tensor, scores: Tensor, d_update: Tensor,
                          d_aux: Tensor | None, d_scores: Tensor | None,
                          expert_wgrad: str = "native",
-                         saved: tuple[Tensor, Tensor, Tensor | None] | None = None) -> dict[str, Tensor]:
+                         saved: tuple | None = None) -> dict[str, Tensor]:
         """Gradients of x and of every parameter (``spx_layer_backward`` for the
         routed experts -- their weight gradients included, on tcgen05 grouped
         GEMMs -- and the router scores; library GEMMs for the router's weight
@@ -1269,14 +1280,18 @@ class B200MicroExpertChannelMixer(nn.Module):
             S = wg.shape[0]
             T = x.shape[0]
             w1 = torch.cat([wg, wu], 0)
-            gate_up = F.linear(x, w1)
+            if saved is not None and saved[3] is not None:
+                # the forward's own gate | up values (chunk layout: per chunk, gate then up)
+                gate_up, chunk = saved[3]
+            else:
+                gate_up, chunk = F.linear(x, w1), S
             d_h = du.mm(wd)
             h_s = torch.empty(T, S, dtype=torch.bfloat16, device=device)
             dgu_s = torch.empty(T, 2 * S, dtype=torch.bfloat16, device=device)
             ones = torch.ones(T, dtype=torch.bfloat16, device=device)
             order = torch.arange(T, dtype=torch.int32, device=device)
             d_w = torch.empty(T, dtype=torch.float32, device=device)
-            _lib.check(lib.spx_swiglu_backward_rows(gate_up.data_ptr(), 2 * S, S, d_h.data_ptr(), S,
+            _lib.check(lib.spx_swiglu_backward_rows(gate_up.data_ptr(), gate_up.shape[1], chunk, d_h.data_ptr(), S,
                                                     ones.data_ptr(), order.data_ptr(), T, S, S, h_s.data_ptr(),
                                                     dgu_s.data_ptr(), d_w.data_ptr(), stream),
                        "spx_swiglu_backward_rows")

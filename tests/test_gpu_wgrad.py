@@ -71,7 +71,7 @@ def test_native_expert_wgrad_matches_library(shape, tokens):
 
 @pytest.mark.parametrize("shape", [dict(d_model=256, num_experts=40, expert_inter_dim=80, shared_inter_dim=64,
                                         active_experts=4),
-                                   dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=0,
+                                   dict(d_model=768, num_experts=200, expert_inter_dim=128, shared_inter_dim=768,
                                         active_experts=8)], ids=["m10ish_odd_inter", "m100"])
 def test_saved_forward_activations_match_recompute(shape):
     """The training forward writes the dispatch-order hidden rows and the gate | up
@@ -97,5 +97,27 @@ def test_saved_forward_activations_match_recompute(shape):
     from_saved = mixer._backward_native(x, ids, w, scores, du, None, None, saved=saved)
     torch.cuda.synchronize()
     assert set(recomputed) == set(from_saved)
+    # The shared SwiGLU's pre-activations come from the forward's tcgen05 GEMM
+    # instead of a library GEMM (another summation order): its weights' and
+    # the input's gradients agree within BF16 GEMM tolerance; the rest is bit
+    # for bit.
+    shared_keys = {"x"} | {key for key in recomputed if key.startswith("shared.")}
+    if saved[3] is None:
+        shared_keys = set()
     for key in recomputed:
-        assert torch.equal(from_saved[key], recomputed[key]), key
+        if key in shared_keys:
+            got, want = from_saved[key].float(), recomputed[key].float()
+            assert ((got - want).norm() / want.norm()).item() < 1e-2, key
+        else:
+            assert torch.equal(from_saved[key], recomputed[key]), key
+    if saved[3] is not None:
+        # the saved shared values are the forward's bf16 gate | up (chunk layout) of x
+        sh = mixer.shared
+        w1 = torch.cat([sh.gate_projection.weight, sh.up_projection.weight], 0).detach()
+        ref = torch.nn.functional.linear(x, w1).float()
+        gu, chunk = saved[3]
+        S = sh.gate_projection.weight.shape[0]
+        cols = torch.cat([torch.arange(n * 2 * chunk + h * chunk, n * 2 * chunk + (h + 1) * chunk)
+                          for h in (0, 1) for n in range(S // chunk)]).to(gu.device)
+        got = gu[:, cols].float()
+        assert ((got - ref).norm() / ref.norm()).item() < 1e-2
