@@ -268,7 +268,7 @@ int spx_gather_rows(const uint16_t* src, int64_t ld_src, const int32_t* index, i
  * ([gate chunk | up chunk] per chunk, inter / chunk chunks), d_hidden
  * [rows, ld_d_hidden] the gradient of the down projection's input before
  * the weight, weights[rows] BF16 routing weights (1 for unweighted rows).
- * Writes hidden [rows, inter] = bf16(bf16(silu(gate)) * up), d_gate_up
+ * Writes hidden [rows, inter] = bf16(bf16(bf16(silu(gate)) * up) * weight), d_gate_up
  * [rows, 2 * inter_pad] = [d gate | d up] (each half zero-padded to
  * inter_pad columns) and d_weights[order[r]] = sum over the row of
  * d_hidden * hidden (FP32).  Every intermediate is rounded to BF16.  Needs
@@ -475,9 +475,11 @@ int spx_rows_to_peers(const uint16_t* src, int64_t ld_src, const int32_t* index,
  * expert weight gradients: with offsets from expert_counts,
  *   d gate_e | d up_e = x_sorted[e]^T @ dgu_sorted[e]   ([d, I] each, the up
  *                                                       half from column kI)
- *   d down_e          = h_sorted[e]^T @ dy_sorted[e]    ([I, d]),
- * x_sorted[p] = hidden[token of p] and dy_sorted[p] = bf16(d_update[token of
- * p] * routing weight of p).  x_sorted and dy_sorted are both given or both
+ *   d down_e          = h_sorted[e]^T @ du_sorted[e]    ([I, d]),
+ * x_sorted[p] = hidden[token of p], du_sorted[p] = d_update[token of p] and
+ * h_sorted[p] = bf16(h_p * w_p), pair p's forward hidden row times its
+ * routing weight (the weight moved from dU to h: the same sum, its BF16
+ * rounding on the narrow side).  x_sorted and du_sorted are both given or both
  * NULL; NULL needs the weight gradients below, whose kernels then gather
  * those rows by token themselves (no P x d copies are written).
  * BF16 experts only (SPX_ERR_UNSUPPORTED with an MXFP8 lane); d_model must be
@@ -496,15 +498,15 @@ typedef struct spx_layer_grads {
   uint16_t* d_hidden_experts;       /* [T, d]  out                              */
   uint16_t* d_logits;               /* [T, E]  out                              */
   uint16_t* x_sorted;               /* [T*k, d]   out | NULL (with the wgrads)  */
-  uint16_t* h_sorted;               /* [T*k, I]   out                           */
-  uint16_t* dy_sorted;              /* [T*k, d]   out | NULL (with the wgrads)  */
+  uint16_t* h_sorted;               /* [T*k, I]   out: bf16(hidden row * w)     */
+  uint16_t* du_sorted;              /* [T*k, d]   out | NULL (with the wgrads)  */
   uint16_t* dgu_sorted;             /* [T*k, 2*kI] out, kI = round_up(I, 64)    */
   int32_t* expert_counts;           /* [E]     out                              */
   /* The routed experts' weight gradients (optional; NULL = not computed):
    * d gate | d up [E, d, I] = x_e^T [dg | du]_e and d down [E, I, d] =
    * h_e^T dy_e over each expert's sorted rows, FP32 accumulation, BF16 out
    * (tcgen05, both operands MN-major: from the sorted buffers above, or with
-   * x_sorted = dy_sorted = NULL gathered by token inside the kernels).  Needs
+   * x_sorted = du_sorted = NULL gathered by token inside the kernels).  Needs
    * inter_dim % 8 == 0; all three or none. */
   uint16_t* d_gate_proj;
   uint16_t* d_up_proj;

@@ -183,7 +183,7 @@ class LayerGrads(ctypes.Structure):
         ("d_logits", _vp),
         ("x_sorted", _vp),
         ("h_sorted", _vp),
-        ("dy_sorted", _vp),
+        ("du_sorted", _vp),
         ("dgu_sorted", _vp),
         ("expert_counts", _vp),
         ("d_gate_proj", _vp),

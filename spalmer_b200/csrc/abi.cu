@@ -1579,10 +1579,10 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
   const int wgrad_outs = (gr->d_gate_proj != nullptr) + (gr->d_up_proj != nullptr) + (gr->d_down_proj != nullptr);
   if (wgrad_outs != 0 && wgrad_outs != 3) return SPX_ERR_INVALID_ARG;
   const bool wgrad = wgrad_outs == 3;
-  // x_sorted / dy_sorted: both or neither; neither only with the weight
+  // x_sorted / du_sorted: both or neither; neither only with the weight
   // gradients, which then gather their rows themselves.
   const bool sorted_rows = gr->x_sorted != nullptr;
-  if (sorted_rows != (gr->dy_sorted != nullptr) || (!sorted_rows && !wgrad)) return SPX_ERR_INVALID_ARG;
+  if (sorted_rows != (gr->du_sorted != nullptr) || (!sorted_rows && !wgrad)) return SPX_ERR_INVALID_ARG;
   if (gr->saved_gu != nullptr && (!sorted_rows || !aligned16(gr->saved_gu))) return SPX_ERR_INVALID_ARG;
   if (wgrad && s.I % 8 != 0) return SPX_ERR_UNSUPPORTED;
   if (wgrad && (!aligned16(gr->h_sorted) || !aligned16(gr->d_gate_proj) || !aligned16(gr->d_up_proj) ||
@@ -1590,7 +1590,7 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
     return SPX_ERR_ALIGNMENT;
   if (int rc = check_layer_weights(s, dims, w, true, true, false); rc != SPX_OK) return rc;
   if (!aligned16(hidden) || !aligned16(gr->d_update) || !aligned16(workspace) || !aligned16(gr->dgu_sorted) ||
-      (sorted_rows && (!aligned16(gr->x_sorted) || !aligned16(gr->dy_sorted))) || !aligned16(gr->d_hidden_experts) ||
+      (sorted_rows && (!aligned16(gr->x_sorted) || !aligned16(gr->du_sorted))) || !aligned16(gr->d_hidden_experts) ||
       !aligned16(gr->gate_proj) || !aligned16(gr->up_proj) || !aligned16(gr->down_proj))
     return SPX_ERR_ALIGNMENT;
   const Layout L = make_layout(s);
@@ -1664,6 +1664,9 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
     g.n_valid = s.I;
     g.out = dhp;
     g.ldo = ldh;
+    g.copy_out = gr->du_sorted;  // the gathered dU rows, kept in dispatch order (or not at all)
+    g.ld_copy = s.d;
+    if (g.copy_out != nullptr && (rc = encode_2d(&g.tma_copy, g.copy_out, s.P, s.d, s.d, 32)) != SPX_OK) return rc;
     if ((rc = launch_gemm(kEpiStore, g, s.max_tiles, ceil_div(s.I, bn), st)) != SPX_OK) return rc;
   }
   // ---- SwiGLU backward: h, [d gate | d up], routing-weight gradients
@@ -1686,14 +1689,9 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
   }
   if ((rc = launch_combine(dxs, da.rank, nullptr, nullptr, s.T, s.d, s.k, gr->d_hidden_experts, st)) != SPX_OK)
     return rc;
-  // ---- dy_sorted = bf16(dU row * routing weight) in dispatch order, when the caller wants the sorted rows
-  if (sorted_rows &&
-      (rc = launch_bwd_scaled_rows(gr->d_update, da.src_row, da.sorted_weights, s.P, s.d, gr->dy_sorted, st)) !=
-          SPX_OK)
-    return rc;
   // ---- the experts' weight gradients over the sorted rows (tcgen05, MN-major
-  // operands); without sorted copies the x rows and the bf16(dU * w) rows are
-  // gathered by token inside the kernels
+  // operands); without sorted copies the x rows and the dU rows are gathered
+  // by token inside the kernels
   if (wgrad) {
     WgradOperand xo{}, dguo{}, ho{}, dyo{};
     xo.ld = xo.total = s.d;
@@ -1713,12 +1711,11 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
     ho.ld = ho.total = s.I;
     dyo.ld = dyo.total = s.d;
     if (sorted_rows) {
-      dyo.rows = gr->dy_sorted;
+      dyo.rows = gr->du_sorted;
     } else {
       dyo.src = gr->d_update;
       dyo.index = da.src_row;
       dyo.src_rows = s.T;
-      dyo.scale = da.sorted_weights;
     }
     if ((rc = launch_wgrad(ho, dyo, s.P, gr->expert_counts, s.E, gr->d_down_proj, s.d, s.d, nullptr, 0, 0, 0,
                            c.status, st)) != SPX_OK)

@@ -51,37 +51,13 @@ int grid_for(int64_t items, int per_block) {
 
 }  // namespace
 
-// The weighted upstream gradient in dispatch order for the down projection's
-// weight gradient: dy_sorted[p] = bf16(dU[t_p] * w_p) (the reference's
-// d(outputs) of the weighted update, bank.py:978).  8 columns per thread.
-__global__ void bwd_scaled_rows_kernel(const uint16_t* __restrict__ du, const int* __restrict__ src_row,
-                                       const uint16_t* __restrict__ sorted_w, int64_t P, int d,
-                                       uint16_t* __restrict__ dy_sorted) {
-  const int vec = d / 8;
-  const int64_t total = P * vec;
-  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t p = idx / vec;
-    const int c = static_cast<int>(idx - p * vec) * 8;
-    const int64_t t = __ldg(src_row + p);
-    const float w = bf16_to_f32(__ldg(sorted_w + p));
-    const uint4 dv = __ldg(reinterpret_cast<const uint4*>(du + t * d + c));
-    const uint32_t in[4] = {dv.x, dv.y, dv.z, dv.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float lo = __uint_as_float(in[q] << 16) * w, hi = __uint_as_float(in[q] & 0xFFFF0000u) * w;
-      o[q] = bfr2(lo, hi);
-    }
-    *reinterpret_cast<uint4*>(dy_sorted + p * d + c) = make_uint4(o[0], o[1], o[2], o[3]);
-  }
-}
-
-// SwiGLU backward.  gu holds the recomputed pre-activations in the forward
-// GEMM1's chunk layout (chunk n: c gate columns, then c up columns), dhp =
-// bf16(dY_t @ D_e^T).  Writes h (forward hidden row), [d_gate | d_up] with
-// the up half at column kI (zero padded to 2 kI), and d_w of the pair in pair
-// order (order[p]).  A row is handled by `lanes` consecutive threads of a
+// SwiGLU backward.  gu holds the pre-activations in the forward GEMM1's
+// chunk layout (chunk n: c gate columns, then c up columns), dhp =
+// bf16(dY_t @ D_e^T).  Writes bf16(h * w) (the forward hidden row times the
+// routing weight: the down projection's weight gradient is
+// sum_p bf16(h_p w_p)^T dU_p; h itself for unit weights), [d_gate | d_up]
+// with the up half at column kI (zero padded to 2 kI), and d_w of the pair in
+// pair order (order[p]).  A row is handled by `lanes` consecutive threads of a
 // warp, 8 hidden columns (16-byte loads and stores) each; needs c % 8 == 0.
 __device__ __forceinline__ void swiglu_bwd8(const uint4& gv, const uint4& uv, const uint4& dv, float w,
                                             uint4& hv, uint4& dgv, uint4& duv, float& part) {
@@ -104,9 +80,11 @@ __device__ __forceinline__ void swiglu_bwd8(const uint4& gv, const uint4& uv, co
     bfr2(sg[0], sg[1]);
     h[0] = sg[0] * u[0];
     h[1] = sg[1] * u[1];
-    H[q] = bfr2(h[0], h[1]);
+    bfr2(h[0], h[1]);
     part += dh1[0] * h[0];
     part += dh1[1] * h[1];
+    float hw[2] = {h[0] * w, h[1] * w};  // the weighted row for the down projection's weight gradient
+    H[q] = bfr2(hw[0], hw[1]);
     dh[0] = dh1[0] * w;
     dh[1] = dh1[1] * w;
     bfr2(dh[0], dh[1]);
@@ -320,14 +298,6 @@ int launch_bwd_router(const BwdRouterArgs& a, cudaStream_t stream) {
     bwd_router_kernel<8><<<grid, 256, 0, stream>>>(a);
   else
     bwd_router_kernel<32><<<grid, 256, 0, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
-}
-
-int launch_bwd_scaled_rows(const uint16_t* du, const int* src_row, const uint16_t* sorted_w, int64_t P, int d,
-                           uint16_t* dy_sorted, cudaStream_t stream) {
-  if (d % 8 != 0) return SPX_ERR_UNSUPPORTED;
-  if (P <= 0) return SPX_OK;
-  bwd_scaled_rows_kernel<<<grid_for(P * (d / 8), 256), 256, 0, stream>>>(du, src_row, sorted_w, P, d, dy_sorted);
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 

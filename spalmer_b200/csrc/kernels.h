@@ -419,13 +419,11 @@ int launch_gemv_rows(GemvPass a, cudaStream_t stream);
 // counts[e] rows per expert); output columns [0, n_valid0) of B land in out0
 // [E, m_total, ld0], columns [n_start1, n_start1 + n_valid1) in out1.
 // One operand of the weight-gradient GEMM, P rows in dispatch order: either
-// stored (`rows`, row p at rows + p * ld) or gathered (row p is src[index[p]]);
-// B may be scaled per row: bf16(row p * scale[p]), the product rounded once.
+// stored (`rows`, row p at rows + p * ld) or gathered (row p is src[index[p]]).
 struct WgradOperand {
   const uint16_t* rows;   // [P, ld] sorted rows, or null when gathered
   const uint16_t* src;    // gathered: [*, ld] source rows
   const int* index;       // gathered: index[p] = source row of sorted row p (< src_rows)
-  const uint16_t* scale;  // B only, optional: BF16 factor of sorted row p
   int64_t src_rows;       // gathered: rows of src
   int64_t ld;
   int total;              // columns
@@ -442,7 +440,6 @@ struct WgradArgs {
   const uint16_t* g_src;
   const int* g_index;
   int64_t g_ld;
-  const uint16_t* b_scale;  // per sorted row BF16 factor of B, or null
   int g_is_a;
   int* status;
 };
@@ -451,8 +448,6 @@ int launch_wgrad(const WgradOperand& a, const WgradOperand& b, int64_t rows, con
                  int* status, cudaStream_t stream);
 
 // Backward (backward.cu).
-int launch_bwd_scaled_rows(const uint16_t* du, const int* src_row, const uint16_t* sorted_w, int64_t P, int d,
-                           uint16_t* dy_sorted, cudaStream_t stream);
 struct BwdRouterArgs {
   const uint16_t* scores;     // [T, E] router scores (BF16)
   const uint16_t* logits;     // [T, E] router logits, or null (identity score transform)

@@ -4,7 +4,8 @@
 //
 // where A_e, B_e are the expert's rows of two matrices kept in dispatch order
 // (rows of one expert contiguous): d gate | d up = x_e^T . [dg | du]_e and
-// d down = h_e^T . dy_e -- the gradients autograd gives the reference's
+// d down = bf16(h w)_e^T . dU_e (the routing weight on the hidden rows) --
+// the gradients autograd gives the reference's
 // expert parameters (experts/bank.py:755-763 differentiated; its grouped
 // executor's torch.bmm / grouped GEMMs).  The reduction runs over an
 // expert's rows, so both operands enter the MMA MN-major: TMA copies
@@ -13,8 +14,6 @@
 // canonical MN-major layout (LBO = 8 KB between 64-column boxes, SBO = 1 KB
 // between 8-row groups along K); nothing is transposed in memory.
 //
-// B's rows may carry a BF16 scale per row (the routing weight: d down takes
-// bf16(dU row * w)), applied in shared memory before the MMA reads the stage.
 // One operand may instead be gathered from unsorted rows (x rows by token for
 // d gate | d up, dU rows by token for d down), so no sorted copies (two
 // P x d matrices) are needed.  The producer loads
@@ -26,7 +25,7 @@
 // and share its rows through L2.  Warp roles: 0 TMA producer, 1 MMA issuer
 // (and TMEM owner), 2-3 fixers -- an expert's last K block holds rows of the
 // next expert (or TMA zero fill past the end); the fixers zero the rows past
-// the segment in shared memory, scale a gathered operand's rows, and pass the
+// the segment in shared memory and pass the
 // stage on --, 4-7 epilogue (TMEM lane quadrants 0-3).  Two accumulators of
 // bn columns let the epilogue of one tile overlap the MMAs of the next.
 // Experts without rows get zero gradients.  Every wait is bounded (status
@@ -48,20 +47,6 @@ constexpr int kWgThreads = 256;
 constexpr int kWgBoxBytes = 64 * 128;  // one TMA box: 64 rows x 64 BF16 columns
 constexpr int kWgMaxExperts = 1024;
 constexpr int kWgFixers = 2;           // warps 2 and 3
-
-// Byte offset of 16-byte chunk c (8 columns) of row r in a run of 64-column
-// boxes with the 128-byte swizzle (chunk position c ^ (r & 7) within the row).
-__device__ __forceinline__ uint32_t wg_chunk_off(int r, int c) {
-  return static_cast<uint32_t>((c >> 3) * kWgBoxBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4));
-}
-
-// BF16 pair product, rounded once (the FP32 product of two BF16 values is
-// exact above the FP32 normal floor, so this is bf16(a * b) of each half).
-__device__ __forceinline__ uint32_t wg_bmul2(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
 
 // Shared-memory descriptor of an MN-major operand tile made of 64-column
 // boxes (128-byte rows, 128B swizzle) laid out one after another.
@@ -267,27 +252,17 @@ __global__ void __launch_bounds__(kWgThreads, 1) wgrad_kernel(const __grid_const
     // ---------------- fixers: a pipeline stage between the loads and the MMA.
     // They pass every stage on in order (so no barrier phase can be skipped or
     // overtaken); first they zero the rows past the expert's segment in the
-    // segment's last block, and scale B's rows when it has a row scale
-    // (fixer f takes rows 32f .. 32f + 31: one row per lane).
+    // segment's last block (split between the two fixers).
     const int f = warp - 2;
-    const bool scaled = a.b_scale != nullptr;
-    const int bchunks = 8 * nbox_b;  // 16-byte chunks per B row
     uint32_t it = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
       const WgTile w = wg_tile(a, t);
       const int cnt = s_count[w.e];
-      const int start = s_start[w.e];
       const int nkb = kblocks(w.e);
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = static_cast<int>(it % S);
         const int valid = cnt - kb * 64;
-        const int r = 32 * f + lane;
-        uint32_t w2 = 0;
-        if (scaled && r < valid) {
-          const uint32_t wb = __ldg(a.b_scale + start + kb * 64 + r);
-          w2 = wb | (wb << 16);
-        }
         int go = 1;
         if (lane == 0) go = mbar_wait(&full[s], (it / S) & 1u, a.status, SPX_DEV_TIMEOUT_PRODUCER) ? 1 : 0;
         go = __shfl_sync(0xFFFFFFFFu, go, 0);
@@ -304,22 +279,6 @@ __global__ void __launch_bounds__(kWgThreads, 1) wgrad_kernel(const __grid_const
           for (int i = f * 32 + lane; i < nbox * chunks; i += 32 * kWgFixers) {
             const int box = i / chunks, c = i - box * chunks;
             *reinterpret_cast<uint4*>(st + box * kWgBoxBytes + valid * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
-          }
-          wrote = true;
-        }
-        if (scaled && r < valid) {
-          const uint32_t base = smem_u32(st) + a_bytes;
-#pragma unroll 4
-          for (int c = 0; c < bchunks; ++c) {
-            const uint32_t addr = base + wg_chunk_off(r, c);
-            uint32_t v0, v1, v2, v3;
-            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                         : "=r"(v0), "=r"(v1), "=r"(v2), "=r"(v3)
-                         : "r"(addr)
-                         : "memory");
-            asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(wg_bmul2(v0, w2)),
-                         "r"(wg_bmul2(v1, w2)), "r"(wg_bmul2(v2, w2)), "r"(wg_bmul2(v3, w2))
-                         : "memory");
           }
           wrote = true;
         }
@@ -417,7 +376,7 @@ int launch_wgrad(const WgradOperand& A, const WgradOperand& B, int64_t rows, con
       B.ld % 8 != 0)
     return SPX_ERR_UNSUPPORTED;  // 16-byte rows for TMA, cp.async and the vector stores
   const bool ga = A.rows == nullptr, gb = B.rows == nullptr;
-  if ((ga && gb) || A.scale != nullptr || (ga && (A.src == nullptr || A.index == nullptr)) ||
+  if ((ga && gb) || (ga && (A.src == nullptr || A.index == nullptr)) ||
       (gb && (B.src == nullptr || B.index == nullptr)))
     return SPX_ERR_INVALID_ARG;
   WgradArgs w{};
@@ -440,7 +399,6 @@ int launch_wgrad(const WgradOperand& A, const WgradOperand& B, int64_t rows, con
     w.g_ld = g.ld;
     w.g_is_a = ga ? 1 : 0;
   }
-  w.b_scale = B.scale;
   w.n_total = n_total;
   w.counts = counts;
   w.E = E;

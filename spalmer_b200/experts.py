@@ -1177,9 +1177,10 @@ class B200MicroExpertChannelMixer(nn.Module):
         """Gradients of x and of every parameter (``spx_layer_backward`` for the
         routed experts -- their weight gradients included, on tcgen05 grouped
         GEMMs -- and the router scores; library GEMMs for the router's weight
-        gradient and the shared SwiGLU).  The recomputed GEMM1 and the dh' GEMM
-        write the x rows and the bf16(dU * w) rows they gather in dispatch
-        order on the side, and the weight-gradient GEMMs read those;
+        gradient and the shared SwiGLU).  The GEMM1 (forward or recomputed) and
+        the dh' GEMM write the x rows and the dU rows they gather in dispatch
+        order on the side, and the weight-gradient GEMMs read those (the down
+        projection's with the routing weights on its hidden rows);
         ``expert_wgrad="native_gathered"`` skips the two P x d copies (less
         memory, slower: the weight-gradient kernels then gather the rows
         themselves), and ``expert_wgrad="library"`` computes the experts' weight
@@ -1218,7 +1219,7 @@ class B200MicroExpertChannelMixer(nn.Module):
             x_sorted = saved[0]
         else:
             x_sorted = torch.empty(P, d, dtype=torch.bfloat16, device=device) if copies else None
-        dy_sorted = torch.empty(P, d, dtype=torch.bfloat16, device=device) if copies else None
+        du_sorted = torch.empty(P, d, dtype=torch.bfloat16, device=device) if copies else None
         wgrads = {n: torch.empty(E, *shape, dtype=torch.bfloat16, device=device) if native_wgrad else None
                   for n, shape in (("gate", (d, I)), ("up", (d, I)), ("down", (I, d)))}
         residency = self.residency
@@ -1245,7 +1246,7 @@ class B200MicroExpertChannelMixer(nn.Module):
             gate_proj=gate.data_ptr(), up_proj=up.data_ptr(), down_proj=down.data_ptr(),
             d_update=du.data_ptr(), d_scores=_lib.ptr(dsc), d_aux=_lib.ptr(dax),
             d_hidden_experts=d_hidden.data_ptr(), d_logits=d_logits.data_ptr(), x_sorted=_lib.ptr(x_sorted),
-            h_sorted=h_sorted.data_ptr(), dy_sorted=_lib.ptr(dy_sorted), dgu_sorted=dgu.data_ptr(),
+            h_sorted=h_sorted.data_ptr(), du_sorted=_lib.ptr(du_sorted), dgu_sorted=dgu.data_ptr(),
             expert_counts=counts.data_ptr(), d_gate_proj=_lib.ptr(wgrads["gate"]),
             d_up_proj=_lib.ptr(wgrads["up"]), d_down_proj=_lib.ptr(wgrads["down"]),
             saved_gu=None if saved is None else saved[1].data_ptr(),
@@ -1268,7 +1269,7 @@ class B200MicroExpertChannelMixer(nn.Module):
             offs = torch.cumsum(counts, 0, dtype=torch.int32)
             grads["experts.gate_proj"] = _grouped_wgrad(x_sorted, dgu[:, :I], counts, offs)
             grads["experts.up_proj"] = _grouped_wgrad(x_sorted, dgu[:, kI:kI + I], counts, offs)
-            grads["experts.down_proj"] = _grouped_wgrad(h_sorted, dy_sorted, counts, offs)
+            grads["experts.down_proj"] = _grouped_wgrad(h_sorted, du_sorted, counts, offs)  # h_sorted: h * w
         if self.shared is not None and _shared_bwd_native(self.shared, x):
             # Shared SwiGLU backward without autograd: [gate | up] in one GEMM,
             # the elementwise part in one kernel (spx_swiglu_backward_rows,

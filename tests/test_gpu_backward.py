@@ -133,7 +133,8 @@ def test_swiglu_backward_rows_against_torch_fp32():
     dhw = dhf * wf
     want_dgate = dhw * uf * sig * (1 + gf * (1 - sig))
     want_dup = dhw * F.silu(gf)
-    for got, want in ((h, hf), (dgu[:, :S], want_dgate), (dgu[:, S:], want_dup)):
+    # the hidden rows come out times their weight (the down projection's weight gradient takes h * w)
+    for got, want in ((h, hf * wf), (dgu[:, :S], want_dgate), (dgu[:, S:], want_dup)):
         torch.testing.assert_close(got.float(), want, rtol=2e-2, atol=1e-2)
     torch.testing.assert_close(dw.flip(0), (dhf * hf).sum(1), rtol=2e-2, atol=1e-2 * S)
     # refused on the host before any launch: chunk not a multiple of 8
