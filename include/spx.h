@@ -517,6 +517,14 @@ typedef struct spx_layer_grads {
   /* [T, E] the forward's router logits (spx_layer_outputs.router_logits) |
    * NULL (the router GEMM runs again; softplus scores only) */
   const uint16_t* router_logits;
+  /* The workspace of the spx_layer_forward call these gradients belong to,
+   * untouched since, with that call's expert_utilization ([E]): the
+   * backward reads the forward's dispatch (sorted rows, tiles, ranks) from it
+   * instead of dispatching again.  Both or neither (NULL: dispatch again from
+   * expert_ids).  That forward must have left dispatch_order, expert_counts
+   * and pair_rank NULL (they then live in its workspace). */
+  const void* forward_workspace;
+  const float* expert_utilization;
 } spx_layer_grads;
 
 int spx_layer_backward_sizes(const spx_layer_dims* dims, size_t* workspace_bytes);

@@ -191,6 +191,8 @@ class LayerGrads(ctypes.Structure):
         ("d_down_proj", _vp),
         ("saved_gu", _vp),
         ("router_logits", _vp),
+        ("forward_workspace", _vp),
+        ("expert_utilization", _vp),
     ]
 
 

@@ -1524,7 +1524,6 @@ namespace {
 struct BwdLayout {
   size_t gu;      // [P, nc * 2c] recomputed gate | up pre-activations (chunk layout)
   size_t dhp;     // [P, ldh]     bf16(dY_t @ D_e^T)
-  size_t w1cat;   // [E, d, 2 kI] [gate_e | up_e] along K
   size_t logits;  // [T, E]       recomputed router logits (softplus scores only)
   size_t dw;      // [P] float    routing-weight gradients in pair order
   size_t total;
@@ -1543,7 +1542,6 @@ BwdLayout make_bwd_layout(const Shape& s, size_t base) {
   };
   B.gu = take(2 * static_cast<size_t>(s.P) * s.nc * 2 * s.c);
   B.dhp = take(2 * static_cast<size_t>(s.P) * bwd_ldh(s));
-  B.w1cat = take(2 * static_cast<size_t>(s.E) * s.d * 2 * bwd_ki(s));
   B.logits = take(2 * static_cast<size_t>(s.T) * s.E);
   B.dw = take(sizeof(float) * static_cast<size_t>(s.P));
   B.total = off;
@@ -1584,6 +1582,9 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
   const bool sorted_rows = gr->x_sorted != nullptr;
   if (sorted_rows != (gr->du_sorted != nullptr) || (!sorted_rows && !wgrad)) return SPX_ERR_INVALID_ARG;
   if (gr->saved_gu != nullptr && (!sorted_rows || !aligned16(gr->saved_gu))) return SPX_ERR_INVALID_ARG;
+  if ((gr->forward_workspace != nullptr) != (gr->expert_utilization != nullptr) ||
+      (gr->forward_workspace != nullptr && !aligned16(gr->forward_workspace)))
+    return SPX_ERR_INVALID_ARG;
   if (wgrad && s.I % 8 != 0) return SPX_ERR_UNSUPPORTED;
   if (wgrad && (!aligned16(gr->h_sorted) || !aligned16(gr->d_gate_proj) || !aligned16(gr->d_up_proj) ||
                 !aligned16(gr->d_down_proj)))
@@ -1602,7 +1603,6 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
   // [P, nc * 2c] gate | up pre-activations: the forward's (saved_gu) or recomputed here
   const uint16_t* gu = gr->saved_gu != nullptr ? gr->saved_gu : at<uint16_t>(workspace, B.gu);
   uint16_t* dhp = at<uint16_t>(workspace, B.dhp);
-  uint16_t* w1cat = at<uint16_t>(workspace, B.w1cat);
   float* dw = at<float>(workspace, B.dw);
   uint16_t* dxs = at<uint16_t>(workspace, L.y);
 
@@ -1619,14 +1619,27 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
     }
   }
 
-  // ---- dispatch again, from the forward's expert ids (all experts in the BF16 table)
-  DispatchArgs da = dispatch_args(s, gr->expert_ids, nullptr, gr->expert_counts, workspace, L);
-  da.lb_blocks = 0;
-  da.pair_weights = gr->routing_weights;
-  da.sorted_weights = at<uint16_t>(workspace, L.sorted_w);
-  da.utilization = at<float>(workspace, L.util);
-  da.resident = w->resident_mask;
-  if ((rc = launch_dispatch(da, st)) != SPX_OK) return rc;
+  // ---- the forward's dispatch, read from its workspace (the same layout L),
+  // or dispatch again from the forward's expert ids (all experts in the BF16 table)
+  DispatchArgs da{};
+  if (gr->forward_workspace != nullptr) {
+    void* fw = const_cast<void*>(gr->forward_workspace);
+    da = dispatch_args(s, gr->expert_ids, nullptr, nullptr, fw, L);
+    da.status = c.status;
+    da.sorted_weights = at<uint16_t>(fw, L.sorted_w);
+    da.utilization = const_cast<float*>(gr->expert_utilization);
+    if (cudaMemcpyAsync(gr->expert_counts, da.counts, static_cast<size_t>(s.E) * 4, cudaMemcpyDeviceToDevice, st) !=
+        cudaSuccess)
+      return SPX_ERR_CUDA;
+  } else {
+    da = dispatch_args(s, gr->expert_ids, nullptr, gr->expert_counts, workspace, L);
+    da.lb_blocks = 0;
+    da.pair_weights = gr->routing_weights;
+    da.sorted_weights = at<uint16_t>(workspace, L.sorted_w);
+    da.utilization = at<float>(workspace, L.util);
+    da.resident = w->resident_mask;
+    if ((rc = launch_dispatch(da, st)) != SPX_OK) return rc;
+  }
 
   // ---- gate | up pre-activations again: GEMM1 (gathered rows) with a plain
   // epilogue, unless the forward saved them (and the rows: x_sorted)
@@ -1674,11 +1687,14 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
                               gr->h_sorted, gr->dgu_sorted, dw, st)) != SPX_OK)
     return rc;
   // ---- input gradient of the experts: dx_p = [d gate | d up] @ [G_e | U_e]^T, then per token
-  if ((rc = launch_bwd_pack_w1cat(gr->gate_proj, gr->up_proj, s.E, s.d, s.I, ki, w1cat, st)) != SPX_OK) return rc;
   {
     GemmArgs g = base_args(kEpiStore, s.bn_d, 2 * ki / 64, c.status);
     if ((rc = encode_2d(&g.tma_a, gr->dgu_sorted, s.P, 2 * ki, 2 * ki, kTileRows)) != SPX_OK) return rc;
-    if ((rc = encode_3d(&g.tma_b, w1cat, s.E, s.d, 2 * ki, s.bn_d)) != SPX_OK) return rc;
+    // B = [G_e | U_e] along K straight from the reference-layout [E, d, I]
+    // matrices: K blocks below kI from gate (zero past I), the rest from up
+    if ((rc = encode_3d(&g.tma_b, gr->gate_proj, s.E, s.d, s.I, s.bn_d)) != SPX_OK) return rc;
+    if ((rc = encode_3d(&g.tma_b2, gr->up_proj, s.E, s.d, s.I, s.bn_d)) != SPX_OK) return rc;
+    g.b_split = ki / 64;
     g.groups = s.E;
     g.tiles = da.tiles;
     g.num_tiles = da.num_tiles;

@@ -145,26 +145,6 @@ __global__ void bwd_swiglu_kernel(const uint16_t* __restrict__ gu, int ld_gu, in
   }
 }
 
-// [gate_e | up_e] concatenated along K for the input-gradient GEMM:
-// out[e][n][k] = gate[e][n][k] (k < I), up[e][n][k - kI] (kI <= k < kI + I),
-// 0 otherwise; gate/up in the reference layout [E, d, I] (I % 8 == 0: 16-byte moves).
-__global__ void bwd_pack_w1cat_kernel(const uint16_t* __restrict__ gate, const uint16_t* __restrict__ up, int E,
-                                      int d, int I, int kI, uint16_t* __restrict__ out) {
-  const int per_row = 2 * kI / 8;
-  const int64_t total = static_cast<int64_t>(E) * d * per_row;
-  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int k = static_cast<int>(idx % per_row) * 8;
-    const int64_t row = idx / per_row;  // e * d + n
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (k < I)
-      v = __ldg(reinterpret_cast<const uint4*>(gate + row * I + k));
-    else if (k >= kI && k < kI + I)
-      v = __ldg(reinterpret_cast<const uint4*>(up + row * I + (k - kI)));
-    *reinterpret_cast<uint4*>(out + row * 2 * kI + k) = v;
-  }
-}
-
 // Router backward, one warp per token row: selection softmax, load-balance
 // softmax, optional upstream score gradient, softplus.  Lanes own columns
 // lane, lane + 32, ...; the row's k selected experts are distinct.
@@ -278,14 +258,6 @@ int launch_bwd_swiglu(const uint16_t* gu, int ld_gu, int c, const uint16_t* dhp,
   const int rows_per_block = 8 * (32 / lanes);
   bwd_swiglu_kernel<<<grid_for(P, rows_per_block), 256, 0, stream>>>(gu, ld_gu, c, dhp, ld_dhp, sorted_w, order, P,
                                                                      I, kI, lanes, h_sorted, dgu, dw_pair);
-  return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
-}
-
-int launch_bwd_pack_w1cat(const uint16_t* gate, const uint16_t* up, int E, int d, int I, int kI, uint16_t* out,
-                          cudaStream_t stream) {
-  if (I % 8 != 0) return SPX_ERR_UNSUPPORTED;
-  const int64_t total = static_cast<int64_t>(E) * d * (2 * kI / 8);
-  bwd_pack_w1cat_kernel<<<grid_for(total, 256), 256, 0, stream>>>(gate, up, E, d, I, kI, out);
   return cudaGetLastError() == cudaSuccess ? SPX_OK : SPX_ERR_CUDA;
 }
 

@@ -866,7 +866,12 @@ __global__ void __launch_bounds__(gemm_threads<EPI, MX, NV>(), 1) gemm_kernel(co
           break;
         }
         if (lane == 0) tma_load_2d(sa + s * a_bytes, &a.tma_a, &full[s], kb * 64, row0);
-        if (lane == 0) tma_load_3d(sb + s * b_bytes, &a.tma_b, &full[s], kb * 64, n0, group);
+        if (lane == 0) {
+          if (a.b_split > 0 && kb >= a.b_split)  // K blocks past the split come from the second operand
+            tma_load_3d(sb + s * b_bytes, &a.tma_b2, &full[s], (kb - a.b_split) * 64, n0, group);
+          else
+            tma_load_3d(sb + s * b_bytes, &a.tma_b, &full[s], kb * 64, n0, group);
+        }
         __syncwarp();
       }
     }

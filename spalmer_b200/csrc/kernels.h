@@ -124,6 +124,11 @@ struct GemmArgs {
   uint32_t tmem_cols;        // per accumulator buffer: power of two >= max(32, bn)
   int n_tiles;               // N tiles per M tile (set by launch_gemm)
   int groups;                // B groups (bounds check of the tile table)
+  // TMA-loaded B (ungathered A, BF16): K blocks from b_split on come from
+  // tma_b2 (K restarting at 0), e.g. [gate | up] along K from two matrices.
+  // 0 = B is tma_b alone.
+  CUtensorMap tma_b2;
+  int b_split;
   int gather;                // 1: A rows gathered through gather_idx with cp.async (a_base/lda)
   const int* gather_idx;
   const uint8_t* a_base;     // gather: A rows (row stride lda bytes)
@@ -466,8 +471,6 @@ struct BwdRouterArgs {
 int launch_bwd_swiglu(const uint16_t* gu, int ld_gu, int c, const uint16_t* dhp, int ld_dhp,
                       const uint16_t* sorted_w, const int* order, int64_t P, int I, int kI, uint16_t* h_sorted,
                       uint16_t* dgu, float* dw_pair, cudaStream_t stream);
-int launch_bwd_pack_w1cat(const uint16_t* gate, const uint16_t* up, int E, int d, int I, int kI, uint16_t* out,
-                          cudaStream_t stream);
 int launch_bwd_router(const BwdRouterArgs& a, cudaStream_t stream);
 
 }  // namespace spx

@@ -1013,6 +1013,8 @@ class B200MicroExpertChannelMixer(nn.Module):
         dims = layer_dims(config, tokens, k)
         packed = self._packed(device, tokens, k)
         ws = self._workspace(device, dims)
+        self._ws_generation = getattr(self, "_ws_generation", 0) + 1  # this call's dispatch now lives in ws
+        self._last_forward = (self._ws_generation, ws)
         x = hidden_states.reshape(tokens, d_model).contiguous()
         update = torch.empty(batch, seq_len, d_model, dtype=torch.bfloat16, device=device)
         scores = torch.empty(batch, seq_len, E, dtype=torch.bfloat16, device=device)
@@ -1173,7 +1175,8 @@ class B200MicroExpertChannelMixer(nn.Module):
     def _backward_native(self, x: Tensor, ids: Tensor, weights: Tensor, scores: Tensor, d_update: Tensor,
                          d_aux: Tensor | None, d_scores: Tensor | None,
                          expert_wgrad: str = "native",
-                         saved: tuple | None = None) -> dict[str, Tensor]:
+                         saved: tuple | None = None,
+                         forward_ws: tuple[Tensor, Tensor] | None = None) -> dict[str, Tensor]:
         """Gradients of x and of every parameter (``spx_layer_backward`` for the
         routed experts -- their weight gradients included, on tcgen05 grouped
         GEMMs -- and the router scores; library GEMMs for the router's weight
@@ -1187,7 +1190,9 @@ class B200MicroExpertChannelMixer(nn.Module):
         gradients with ``torch._grouped_mm`` from the sorted rows instead (a
         comparison seam for the tests).  ``saved``: the activations the
         forward wrote for this backward (``_training_saves``); GEMM1 is then
-        not recomputed."""
+        not recomputed.  ``forward_ws``: (workspace, expert utilization) of that
+        forward when no forward of this layer ran since; its dispatch is read
+        from there instead of being recomputed."""
 
         import torch.nn.functional as F
 
@@ -1251,6 +1256,8 @@ class B200MicroExpertChannelMixer(nn.Module):
             d_up_proj=_lib.ptr(wgrads["up"]), d_down_proj=_lib.ptr(wgrads["down"]),
             saved_gu=None if saved is None else saved[1].data_ptr(),
             router_logits=None if saved is None else _lib.ptr(saved[2]),
+            forward_workspace=None if forward_ws is None else forward_ws[0].data_ptr(),
+            expert_utilization=None if forward_ws is None else forward_ws[1].data_ptr(),
         )
         stream = torch.cuda.current_stream(device).cuda_stream
         _lib.check(lib.spx_layer_backward(dims, pw, x.data_ptr(), gr, ws.data_ptr(), stream), "spx_layer_backward")
@@ -1361,6 +1368,11 @@ class _LayerFunction(torch.autograd.Function):
         saved = mixer._training_saves(hidden_states)
         out = mixer._forward_native(hidden_states, None, saved=saved)
         ctx.saved_activations = saved
+        # the forward's dispatch stays in the layer's workspace until its next forward
+        ctx.forward_ws = (*mixer._last_forward, out.metrics["expert_utilization"]) if saved is not None else None
+        # outputs without a gradient (usually the router scores) reach backward
+        # as None rather than as materialised zeros
+        ctx.set_materialize_grads(False)
         m = out.metrics
         holder["metrics"] = m
         ctx.mixer = mixer
@@ -1378,9 +1390,13 @@ class _LayerFunction(torch.autograd.Function):
         x, ids, weights, scores = ctx.saved_tensors
         if d_update is None:
             d_update = torch.zeros(ctx.shape, dtype=torch.bfloat16, device=x.device)
+        forward_ws = None
+        if ctx.forward_ws is not None and ctx.forward_ws[0] == ctx.mixer._ws_generation:
+            forward_ws = ctx.forward_ws[1:]  # no forward of this layer since: its dispatch is still there
         grads = ctx.mixer._backward_native(x, ids, weights, scores, d_update, d_aux, d_scores,
-                                           saved=ctx.saved_activations)
+                                           saved=ctx.saved_activations, forward_ws=forward_ws)
         ctx.saved_activations = None
+        ctx.forward_ws = None
         return (None, None, None, grads["x"].reshape(ctx.shape), *[grads[n] for n in ctx.names])
 
 

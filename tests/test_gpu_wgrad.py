@@ -93,10 +93,15 @@ def test_saved_forward_activations_match_recompute(shape):
     # the saved rows are the token rows in dispatch order (stable sort of the expert ids)
     order = torch.argsort(ids.reshape(-1), stable=True)
     assert torch.equal(saved[0], x[order // k])
+    # the forward's dispatch read back from its workspace (no forward since): the same gradients
+    forward_ws = (mixer._last_forward[1], out.metrics["expert_utilization"])
+    from_ws = mixer._backward_native(x, ids, w, scores, du, None, None, saved=saved, forward_ws=forward_ws)
     recomputed = mixer._backward_native(x, ids, w, scores, du, None, None)
     from_saved = mixer._backward_native(x, ids, w, scores, du, None, None, saved=saved)
     torch.cuda.synchronize()
-    assert set(recomputed) == set(from_saved)
+    assert set(recomputed) == set(from_saved) == set(from_ws)
+    for key in from_ws:
+        assert torch.equal(from_ws[key], from_saved[key]), key
     # The shared SwiGLU's pre-activations come from the forward's tcgen05 GEMM
     # instead of a library GEMM (another summation order): its weights' and
     # the input's gradients agree within BF16 GEMM tolerance; the rest is bit
