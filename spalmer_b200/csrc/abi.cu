@@ -1686,9 +1686,11 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
   if ((rc = launch_bwd_swiglu(gu, s.nc * 2 * s.c, s.c, dhp, ldh, da.sorted_weights, da.order, s.P, s.I, ki,
                               gr->h_sorted, gr->dgu_sorted, dw, st)) != SPX_OK)
     return rc;
-  // ---- input gradient of the experts: dx_p = [d gate | d up] @ [G_e | U_e]^T, then per token
+  // ---- input gradient of the experts: dx_p = [d gate | d up] @ [G_e | U_e]^T, then per token.
+  // The rows leave through the row epilogue (unweighted: bf16(acc)), which
+  // sends whole 32-row boxes by TMA stores as the forward's GEMM2 does.
   {
-    GemmArgs g = base_args(kEpiStore, s.bn_d, 2 * ki / 64, c.status);
+    GemmArgs g = base_args(kEpiScatter, s.bn_d, 2 * ki / 64, c.status);
     if ((rc = encode_2d(&g.tma_a, gr->dgu_sorted, s.P, 2 * ki, 2 * ki, kTileRows)) != SPX_OK) return rc;
     // B = [G_e | U_e] along K straight from the reference-layout [E, d, I]
     // matrices: K blocks below kI from gate (zero past I), the rest from up
@@ -1701,7 +1703,9 @@ int spx_layer_backward(const spx_layer_dims* dims, const spx_packed_weights* w, 
     g.n_valid = s.d;
     g.out = dxs;
     g.ldo = s.d;
-    if ((rc = launch_gemm(kEpiStore, g, s.max_tiles, s.gn_d, st)) != SPX_OK) return rc;
+    g.tma_store = (s.d % 64) == 0;  // whole 64-column boxes; other widths use plain stores
+    if (g.tma_store && (rc = encode_2d(&g.tma_out, dxs, s.P, s.d, s.d, 32)) != SPX_OK) return rc;
+    if ((rc = launch_gemm(kEpiScatter, g, s.max_tiles, s.gn_d, st)) != SPX_OK) return rc;
   }
   if ((rc = launch_combine(dxs, da.rank, nullptr, nullptr, s.T, s.d, s.k, gr->d_hidden_experts, st)) != SPX_OK)
     return rc;
